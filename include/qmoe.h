@@ -1,0 +1,232 @@
+/*
+ * qmoe.h - C ABI of the B200 mixture-of-experts layer.
+ *
+ * Drop-in for the MoE path of the reference runtime's C port:
+ *   moe_forward      c/src/model.c:1281-1405 (called at model.c:1712)
+ *   experts_load     c/src/model.c:539-674
+ *   the expert cache c/src/cache.h:38-60 (instance at model.c:1806)
+ *   prefetch hooks   src/colibri_runtime/streaming.py:226-435 (the C port
+ *                    parses --expert-prefetch but never uses it,
+ *                    c/src/main.c:65,:99,:264)
+ *
+ * All entry points are plain C: pointers, sizes and integers. CUDA streams
+ * are passed as void * (a cudaStream_t). Every call returns 0 on success and
+ * -1 on failure with a message in *err, the reference's convention
+ * (err_t, c/src/util.h:11-19; -1 returns as at model.c:552, :1351).
+ *
+ * One context drives one GPU. A context is not re-entrant: calls on one
+ * context must not overlap. The expert-cache bookkeeping is internally
+ * locked, as the reference's cache is (c/src/cache.c:186-208).
+ */
+#ifndef QMOE_H
+#define QMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same size and meaning as the reference's err_t (c/src/util.h:11-13); a
+ * caller holding an err_t may pass it here by pointer cast. */
+typedef struct {
+    char msg[512];
+} qmoe_err;
+
+/* Expert cache policies, c/src/cache.h:8-10. */
+enum { QMOE_POLICY_LRU = 0, QMOE_POLICY_LFU = 1, QMOE_POLICY_ADAPTIVE = 2 };
+
+/* Element type of device-resident activations passed to qmoe_forward_dev. */
+enum { QMOE_F32 = 0, QMOE_BF16 = 1 };
+
+typedef struct {
+    int hidden;          /* d: hidden_size */
+    int num_experts;     /* E: num_experts (<= 1024) */
+    int top_k;           /* k: num_experts_per_tok (<= 32) */
+    int moe_inter;       /* I: moe_intermediate_size; the shared expert uses it
+                            too, as model.c:1391-1392 does */
+    int group_size;      /* quantization.group_size (64) */
+    int bits;            /* quantization.bits (4) */
+    int num_layers;      /* layers this context serves */
+    int max_tokens;      /* largest n of one forward call (sizes workspaces) */
+    uint64_t pool_bytes; /* HBM expert pool budget in bytes; 0 = room for every
+                            expert of every layer (all resident) */
+    int policy;          /* QMOE_POLICY_* for the pool (reference: ADAPTIVE) */
+    int prefetch_depth;  /* prefetch_count of streaming.py (2) */
+    int device;          /* CUDA device ordinal */
+} qmoe_config;
+
+/* One affine 4-bit tensor in the reference checkpoint layout: `rows` rows of
+ * `cols` values; q holds cols/8 u32 words per row, low nibble first; scales
+ * and biases hold cols/group bf16 values per row (dequant: q*s + b,
+ * c/src/kernel.c:152-173). For the routed experts the E tensors are stacked
+ * ([E, rows, cols/8] etc., model.c:555-557). */
+typedef struct {
+    const uint32_t *q;
+    const uint16_t *scales;
+    const uint16_t *biases;
+} qmoe_q4;
+
+/* Host tensors of one MoE layer (tensor names as model.c:1902-1923 and
+ * model.c:541-546). */
+typedef struct {
+    const uint16_t *router;      /* bf16 [E, d]   mlp.gate.weight */
+    const uint16_t *shared_gate; /* bf16 [1, d]   mlp.shared_expert_gate.weight */
+    const float *logit_bias;     /* fp32 [E] added to the router logits, or NULL */
+    qmoe_q4 gate, up;            /* switch_mlp.{gate,up}_proj  [E, I, d] */
+    qmoe_q4 down;                /* switch_mlp.down_proj       [E, d, I] */
+    qmoe_q4 sh_gate, sh_up;      /* shared_expert.{gate,up}_proj [I, d] */
+    qmoe_q4 sh_down;             /* shared_expert.down_proj      [d, I] */
+} qmoe_layer_weights;
+
+/* Cache counters, c/src/cache.h:55-58. */
+typedef struct {
+    uint64_t hits, misses, evictions, rejected, pinned;
+    uint64_t bytes, peak_bytes, size, hot;
+} qmoe_cache_stats;
+
+/* Runtime counters, mirroring qstats (c/src/model.h:18-24). */
+typedef struct {
+    uint64_t expert_loads, expert_bytes;   /* host -> HBM slot fills */
+    double expert_wait_seconds;            /* host time blocked on fills */
+    uint64_t prefill_calls, decode_calls;
+    double forward_seconds;                /* host wall time inside qmoe_forward */
+    uint64_t prefetch_issued, prefetch_hits;
+} qmoe_stats;
+
+typedef struct qmoe_ctx qmoe_ctx;
+
+/* ---- context (replaces model_load's MoE part, c/src/model.h:27-28) ---- */
+
+qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err);
+void qmoe_destroy(qmoe_ctx *ctx);
+
+/* Bytes of one expert slot in HBM (the packed q4 expert, rows padded to 16
+ * bytes): 1,769,472 at d=2048, I=512. */
+size_t qmoe_slot_bytes(const qmoe_config *cfg);
+
+/* Copies one layer's tensors (host memory, reference layout) into the
+ * context: router, shared gate, shared expert and bias to HBM; routed experts
+ * to the HBM pool when they fit, and to the pinned host store otherwise. */
+int qmoe_upload_layer(qmoe_ctx *ctx, int layer, const qmoe_layer_weights *w,
+                      qmoe_err *err);
+
+/* ---- forward (replaces moe_forward, c/src/model.c:1281) ----
+ * x: host fp32 [n, d]; out: host fp32 [n, d], overwritten. Synchronous. */
+int qmoe_forward(qmoe_ctx *ctx, int layer, const float *x, int n, float *out,
+                 qmoe_err *err);
+
+/* Device-resident variant: x is a device pointer of QMOE_F32 or QMOE_BF16
+ * elements [n, d]; out a device fp32 [n, d]. Enqueued on `stream` (NULL = the
+ * context's stream); returns without waiting when every routed expert of the
+ * layer is resident in HBM. Device-side wait timeouts are reported by the
+ * next qmoe_sync / qmoe_forward call. */
+int qmoe_forward_dev(qmoe_ctx *ctx, int layer, const void *x, int x_dtype,
+                     int n, float *out, void *stream, qmoe_err *err);
+
+/* Waits for the context's work and reports any device-side error. */
+int qmoe_sync(qmoe_ctx *ctx, qmoe_err *err);
+
+/* Routing of the last forward call (waits for it): idx [n, k] in
+ * (logit desc, expert asc) order, weights [n, k] (softmax renormalised over
+ * the k, model.c:1305-1318), shared-gate sigmoid [n]. Any pointer may be NULL. */
+int qmoe_last_routing(qmoe_ctx *ctx, int32_t *idx, float *weights,
+                      float *shared_gate, qmoe_err *err);
+
+/* ---- diagnostics (no reference counterpart; the reference's qstats only
+ *      time whole forwards, c/src/model.c:1756-1761) ----
+ * While enabled, each forward brackets its kernels with CUDA events on its
+ * stream and waits for them, accumulating per-kernel device time.
+ * qmoe_profile_read returns the totals in milliseconds, in launch order
+ * (router, top-k, gate/up, down), the number of kernels per call and the
+ * number of profiled calls; it also resets them. */
+int qmoe_profile_enable(qmoe_ctx *ctx, int on);
+int qmoe_profile_read(qmoe_ctx *ctx, double *kernel_ms, int max_kernels,
+                      int *kernels_per_call, uint64_t *calls);
+
+/* ---- expert cache hooks (cache.h:38-53 keyed (layer << 32) | expert,
+ *      model.c:594) ---- */
+
+/* Slot index of a resident expert or -1; no stats or recency (cache_peek). */
+int qmoe_expert_peek(qmoe_ctx *ctx, int layer, int expert);
+/* As peek, but counts a hit or miss and refreshes recency (cache_get). */
+int qmoe_expert_get(qmoe_ctx *ctx, int layer, int expert);
+/* Makes the listed experts resident, filling misses from the pinned host
+ * store; returns when the copies are done (experts_load, model.c:539). */
+int qmoe_experts_load(qmoe_ctx *ctx, int layer, const int64_t *ids, size_t n,
+                      qmoe_err *err);
+int qmoe_expert_pin(qmoe_ctx *ctx, int layer, int expert);
+int qmoe_expert_unpin(qmoe_ctx *ctx, int layer, int expert);
+int qmoe_expert_mark_hot(qmoe_ctx *ctx, int layer, int expert, int hot);
+int qmoe_cache_snapshot(qmoe_ctx *ctx, qmoe_cache_stats *out);
+int qmoe_stats_get(qmoe_ctx *ctx, qmoe_stats *out);
+
+/* ---- prefetch hooks (streaming.py:271-284, :400-435) ---- */
+
+/* Queues asynchronous fills of the listed experts on the copy stream; never
+ * blocks. Returns the number queued (ExpertStore.request(prefetch=True)). */
+int qmoe_prefetch(qmoe_ctx *ctx, int layer, const int64_t *ids, size_t n);
+/* Records one step's selected experts for the route statistics
+ * (ExpertStore.record_route). */
+void qmoe_record_route(qmoe_ctx *ctx, int layer, const int32_t *experts,
+                       size_t n);
+/* Predicts and queues prefetches for this layer and the next from the route
+ * statistics (ExpertStore.prefetch_predictions). Returns the number queued. */
+int qmoe_prefetch_predictions(qmoe_ctx *ctx, int layer,
+                              const int32_t *selected, size_t n);
+
+/* ---- host-side expert cache object (cache.c semantics over opaque values),
+ *      usable without a GPU; the context's pool bookkeeping is built on it.
+ *      Mirrors cache_init/put/get/peek/pin/unpin/mark_hot/snapshot,
+ *      c/src/cache.h:38-60; values are 64-bit tokens (slot numbers). ---- */
+
+typedef struct qmoe_cache qmoe_cache;
+qmoe_cache *qmoe_cache_new(uint64_t max_bytes, int policy, int partitions);
+void qmoe_cache_free(qmoe_cache *c);
+/* returns 1 and stores the value on a hit, 0 on a miss */
+int qmoe_cache_peek(qmoe_cache *c, uint64_t key, uint64_t *value);
+int qmoe_cache_get(qmoe_cache *c, uint64_t key, uint64_t *value);
+/* 1 when inserted. Each evicted value is appended to evicted[] (capacity
+ * max_evicted, may be NULL) and counted in *n_evicted (may be NULL). */
+int qmoe_cache_put(qmoe_cache *c, uint64_t key, uint64_t value,
+                   uint64_t nbytes, int pin, int hot, uint64_t *evicted,
+                   size_t max_evicted, size_t *n_evicted);
+int qmoe_cache_pin(qmoe_cache *c, uint64_t key);
+int qmoe_cache_unpin(qmoe_cache *c, uint64_t key);
+int qmoe_cache_mark_hot(qmoe_cache *c, uint64_t key, int hot);
+/* removes the entry; 1 if it existed */
+int qmoe_cache_erase(qmoe_cache *c, uint64_t key, uint64_t *value);
+qmoe_cache_stats qmoe_cache_stats_get(qmoe_cache *c);
+
+/* ---- seeded synthetic layers (host; benchmark and test inputs) ----
+ * Counter-based splitmix64 streams keyed by (seed, layer, tensor). Nibbles
+ * uniform 0..15; scales bf16(|N(0, 0.02)|), biases bf16(-8 * scale); router
+ * and shared gate bf16(N(0, 0.02)). Buffers are caller-owned, reference
+ * layout, sized by qmoe_synth_sizes. */
+typedef struct {
+    size_t router, shared_gate;           /* bf16 elements */
+    size_t expert_q, expert_sb;           /* per stacked gate/up tensor: words, bf16 */
+    size_t down_q, down_sb;               /* stacked down tensor */
+    size_t sh_q, sh_sb, sh_down_q, sh_down_sb;
+} qmoe_synth_size;
+
+int qmoe_synth_sizes(const qmoe_config *cfg, qmoe_synth_size *out);
+/* Fills every non-NULL pointer of w (cast away const: the buffers are the
+ * caller's). Experts [e0, e1) only are written when e1 > e0 (others untouched);
+ * e0 = e1 = 0 writes all. */
+int qmoe_synth_layer(const qmoe_config *cfg, uint64_t seed, int layer,
+                     qmoe_layer_weights *w, int e0, int e1);
+/* bf16(N(0,1)) activations as fp32 [n, d]; stream selects the token set. */
+void qmoe_synth_tokens(uint64_t seed, uint64_t stream, int n, int d, float *x);
+/* Zipf logit bias: bias[e] = -s * ln(1 + pi(e)) for a seeded permutation pi. */
+void qmoe_synth_zipf_bias(uint64_t seed, int layer, int E, double s,
+                          float *bias);
+
+const char *qmoe_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,68 @@
+/*
+ * oracle.h - TEST INFRASTRUCTURE ONLY.
+ *
+ * CPU checkers for the MoE layer. Two implementations share this interface:
+ *   - oracle_moe_forward (oracle/moe_oracle.c): a plain-C restatement of the
+ *     reference runtime's MoE block, moe_forward in c/src/model.c:1281-1405;
+ *   - ref_moe_forward (oracle/ref_harness.c, built into oracle/_ref/): the
+ *     reference's own moe_forward compiled unmodified from its sources.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+ * arm may call these. The product library never links them.
+ *
+ * Tensor layout is the reference checkpoint layout for one layer
+ * (c/src/model.c:555-557 for the routed experts, :1902-1923 for the router,
+ * shared expert and shared gate): q4 words u32 with 8 nibbles each, low nibble
+ * first; scales and biases bf16, one per group of `g` values along the row.
+ */
+#ifndef QMOE_ORACLE_H
+#define QMOE_ORACLE_H
+
+#include <stdint.h>
+
+typedef struct {
+    int d;  /* hidden_size */
+    int E;  /* num_experts */
+    int k;  /* num_experts_per_tok */
+    int I;  /* moe_intermediate_size (routed and shared, c/src/model.c:1391-1392) */
+    int g;  /* quantization group size */
+    const uint16_t *router;      /* bf16 [E, d]  mlp.gate.weight */
+    const uint16_t *shared_gate; /* bf16 [d]     mlp.shared_expert_gate.weight */
+    const float *logit_bias;     /* fp32 [E] added to router logits, or NULL */
+    /* switch_mlp experts: gate/up [E, I, d/8] words, [E, I, d/g] scales/biases;
+       down [E, d, I/8] words, [E, d, I/g] scales/biases */
+    const uint32_t *gq, *uq, *dq;
+    const uint16_t *gs, *gb, *us, *ub, *ds, *db;
+    /* shared expert: gate/up [I, d/8], [I, d/g]; down [d, I/8], [d, I/g] */
+    const uint32_t *sgq, *suq, *sdq;
+    const uint16_t *sgs, *sgb, *sus, *sub, *sds, *sdb;
+} oracle_layer;
+
+/* Restatement (moe_oracle.c). out: fp32 [n, d], overwritten. idx/wts
+ * (optional, [n, k]) receive the routing in (value desc, index asc) order.
+ * logits (optional, [n, E]) receives the biased router logits. */
+int oracle_moe_forward(const oracle_layer *L, const float *x, int n,
+                       float *out, int32_t *idx, float *wts, float *logits);
+
+/* Router + top-k + renormalised softmax only (model.c:1301-1319). */
+int oracle_route(const oracle_layer *L, const float *x, int n, int32_t *idx,
+                 float *wts, float *logits);
+
+/* Canonical router dot product: see moe_oracle.c. */
+float oracle_router_dot(const float *x, const uint16_t *w, int K);
+
+/* Known-answer helper: kernel_dequant_q4 restated (c/src/kernel.c:152-173). */
+void oracle_dequant_q4(const uint32_t *q, const float *scales,
+                       const float *biases, int rows, int cols, int group,
+                       float *out);
+
+/* The reference compiled unmodified (ref_harness.c, oracle/_ref only). The
+ * harness reports the reference's selection order in idx (unspecified within
+ * the k, c/src/kernel.h:44-46). threads: BLAS threads for cblas_sgemm. */
+int ref_moe_forward(const oracle_layer *L, const float *x, int n, float *out,
+                    int32_t *idx, float *wts);
+void ref_set_threads(int threads);
+/* Drops the harness's dequantised expert cache (fp32, 12*d*I bytes each). */
+void ref_reset_cache(void);
+
+#endif

@@ -1,0 +1,211 @@
+/*
+ * ref_harness.c - TEST INFRASTRUCTURE ONLY. Drives the reference's own MoE
+ * block, the static moe_forward in c/src/model.c:1281-1405, compiled
+ * unmodified from the reference sources (this file #includes model.c; the
+ * recipe in oracle/Makefile compiles it with the reference's kernel.c,
+ * cache.c, reader.c, safetensors.c, json.c and ngram.c into oracle/_ref/).
+ *
+ * Three call sites are interposed by macro before the include, none of them
+ * inside the arithmetic of the MoE block:
+ *  - cache_peek: experts_load (model.c:590-601) skips experts already in the
+ *    expert cache. The harness answers a miss by dequantising the expert from
+ *    the in-memory synthetic layer with the reference's own kernel_dequant_q4
+ *    (as dequant_raw does, model.c:424-472) and cache_put-ting it under
+ *    (layer << 32) | expert (model.c:594, :660), so no checkpoint is read.
+ *  - st_find: experts_load looks up the expert tensors before consulting the
+ *    cache (model.c:548-585); the harness returns shape-only descriptors.
+ *  - gemm_bf16: the workload's optional per-expert logit bias is added to the
+ *    router logits after the reference's router product (model.c:1301).
+ */
+#define cache_peek harness_cache_peek
+#define st_find harness_st_find
+#define gemm_bf16 harness_gemm_bf16
+#include "model.c"
+#undef cache_peek
+#undef st_find
+#undef gemm_bf16
+
+#include "oracle.h"
+
+void *cache_peek(cache_t *c, uint64_t key);
+void gemm_bf16(int M, int N, int K, const float *A, const uint16_t *W,
+               float *C);
+
+static qmodel g_model;
+static int g_model_ready;
+static const oracle_layer *g_L;
+static oracle_layer g_Lcopy;
+static mweight g_router, g_shgate, g_shg, g_shu, g_shd;
+static st_tensor g_fake_w, g_fake_s;
+
+static float *widen(const uint16_t *v, size_t n) {
+    float *o = xmalloc(n * sizeof(float));
+    for (size_t i = 0; i < n; i++) o[i] = bf16_to_f32(v[i]);
+    return o;
+}
+
+st_tensor *harness_st_find(st_index *ix, const char *name) {
+    (void)ix;
+    size_t n = strlen(name);
+    if (n > 7 && strcmp(name + n - 7, ".weight") == 0) return &g_fake_w;
+    return &g_fake_s;
+}
+
+void *harness_cache_peek(cache_t *c, uint64_t key) {
+    void *v = cache_peek(c, key);
+    if (v || c != &g_model.expert_cache || !g_L) return v;
+    const oracle_layer *L = g_L;
+    int d = L->d, I = L->I, g = L->g;
+    int64_t e = (int64_t)(uint32_t)key;
+    size_t gsz = (size_t)I * d;
+    float *w = xmalloc(3 * gsz * sizeof(float));
+    size_t qo = (size_t)e * I * (d / 8), so = (size_t)e * I * (d / g);
+    size_t dqo = (size_t)e * d * (I / 8), dso = (size_t)e * d * (I / g);
+    struct {
+        const uint32_t *q;
+        const uint16_t *s, *b;
+        int rows, cols;
+        float *out;
+    } parts[3] = {
+        {L->gq + qo, L->gs + so, L->gb + so, I, d, w},
+        {L->uq + qo, L->us + so, L->ub + so, I, d, w + gsz},
+        {L->dq + dqo, L->ds + dso, L->db + dso, d, I, w + 2 * gsz},
+    };
+    for (int p = 0; p < 3; p++) {
+        size_t ng = (size_t)parts[p].rows * (parts[p].cols / g);
+        float *fs = widen(parts[p].s, ng), *fb = widen(parts[p].b, ng);
+        kernel_dequant_q4(parts[p].q, fs, fb, parts[p].rows, parts[p].cols, g,
+                          parts[p].out);
+        free(fs);
+        free(fb);
+    }
+    if (!cache_put(c, key, w, (uint64_t)gsz * 16, 0, 0)) {
+        free(w);
+        return NULL;
+    }
+    return cache_peek(c, key);
+}
+
+void harness_gemm_bf16(int M, int N, int K, const float *A, const uint16_t *W,
+                       float *C) {
+    gemm_bf16(M, N, K, A, W, C);
+    if (g_L && g_L->logit_bias && W == g_L->router && N == g_L->E) {
+        for (int m = 0; m < M; m++)
+            for (int n = 0; n < N; n++) C[(size_t)m * N + n] += g_L->logit_bias[n];
+    }
+}
+
+static void free_shared(void) {
+    mweight *ws[3] = {&g_shg, &g_shu, &g_shd};
+    for (int i = 0; i < 3; i++) {
+        free(ws[i]->scales);
+        free(ws[i]->biases);
+        ws[i]->scales = ws[i]->biases = NULL;
+    }
+}
+
+void ref_reset_cache(void) {
+    if (g_model_ready) {
+        cache_destroy(&g_model.expert_cache);
+        free_shared();
+    }
+    g_model_ready = 0;
+    g_L = NULL;
+    memset(&g_Lcopy, 0, sizeof(g_Lcopy));
+}
+
+static void setup(const oracle_layer *L) {
+    if (g_model_ready && memcmp(&g_Lcopy, L, sizeof(*L)) == 0) {
+        g_L = L;
+        return;
+    }
+    ref_reset_cache();
+    memset(&g_model, 0, sizeof(g_model));
+    qcfg *c = &g_model.cfg;
+    c->hidden_size = L->d;
+    c->num_experts = L->E;
+    c->num_experts_per_tok = L->k;
+    c->moe_intermediate_size = L->I;
+    c->shared_expert_intermediate_size = L->I;
+    c->group_size = L->g;
+    c->bits = 4;
+    c->num_layers = 1;
+    g_model.n_layers = 1;
+    cache_init(&g_model.expert_cache, 0, CACHE_POLICY_LRU, 0);
+    g_model.expert_cache.free_value = free;
+
+    int d = L->d, I = L->I, g = L->g;
+    memset(&g_router, 0, sizeof(g_router));
+    g_router.bf16 = L->router;
+    g_router.rows = L->E;
+    g_router.cols = d;
+    memset(&g_shgate, 0, sizeof(g_shgate));
+    g_shgate.bf16 = L->shared_gate;
+    g_shgate.rows = 1;
+    g_shgate.cols = d;
+    struct {
+        mweight *w;
+        const uint32_t *q;
+        const uint16_t *s, *b;
+        int rows, cols;
+    } sh[3] = {
+        {&g_shg, L->sgq, L->sgs, L->sgb, I, d},
+        {&g_shu, L->suq, L->sus, L->sub, I, d},
+        {&g_shd, L->sdq, L->sds, L->sdb, d, I},
+    };
+    for (int i = 0; i < 3; i++) {
+        memset(sh[i].w, 0, sizeof(mweight));
+        sh[i].w->is_q4 = 1;
+        sh[i].w->q = sh[i].q;
+        sh[i].w->rows = sh[i].rows;
+        sh[i].w->cols = sh[i].cols / 8; /* packed words per row (model.c:198) */
+        size_t ng = (size_t)sh[i].rows * (sh[i].cols / g);
+        sh[i].w->scales = widen(sh[i].s, ng);
+        sh[i].w->biases = widen(sh[i].b, ng);
+    }
+    qlayer *l = &g_model.layers[0];
+    l->gate = &g_router;
+    l->sh_gate = &g_shgate;
+    l->sh_g = &g_shg;
+    l->sh_u = &g_shu;
+    l->sh_d = &g_shd;
+
+    memset(&g_fake_w, 0, sizeof(g_fake_w));
+    g_fake_w.ndim = 3;
+    g_fake_w.shape[0] = L->E;
+    g_fake_w.shape[1] = I;
+    g_fake_w.shape[2] = d / 8;
+    g_fake_w.nbytes = (uint64_t)L->E * I * (d / 8) * 4;
+    g_fake_s = g_fake_w;
+    g_fake_s.shape[2] = d / g;
+    g_fake_s.nbytes = (uint64_t)L->E * I * (d / g) * 2;
+
+    g_Lcopy = *L;
+    g_L = L;
+    g_model_ready = 1;
+}
+
+int ref_moe_forward(const oracle_layer *L, const float *x, int n, float *out,
+                    int32_t *idx, float *wts) {
+    setup(L);
+    int k = L->k;
+    size_t need = (size_t)n * (5 * (size_t)k + L->E + 3 * (size_t)L->d +
+                               3 * (size_t)L->I + 1) + 1024;
+    float *scratch = xcalloc(need, sizeof(float));
+    err_t err = {{0}};
+    int rc = moe_forward(&g_model, &g_model.layers[0], x, n, out, scratch, &err);
+    if (rc == 0) {
+        /* the block's own routing, from its scratch layout (model.c:1290-1294) */
+        int64_t *unique = (int64_t *)scratch;
+        int *ridx = (int *)(unique + (size_t)n * k);
+        int *tok_ids = ridx + (size_t)n * k;
+        float *rw = (float *)(tok_ids + (size_t)n * k);
+        if (idx)
+            for (size_t i = 0; i < (size_t)n * k; i++) idx[i] = ridx[i];
+        if (wts) memcpy(wts, rw, (size_t)n * k * sizeof(float));
+    } else {
+        fprintf(stderr, "ref_moe_forward: %s\n", err.msg);
+    }
+    free(scratch);
+    return rc;
+}

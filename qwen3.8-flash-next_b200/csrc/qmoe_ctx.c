@@ -1,0 +1,949 @@
+/*
+ * qmoe_ctx.c - host side of the B200 MoE layer (C, CUDA runtime API).
+ *
+ * Replaces, for one GPU:
+ *   moe_forward   c/src/model.c:1281-1405  -> qmoe_forward / qmoe_forward_dev
+ *   experts_load  c/src/model.c:539-674    -> qmoe_experts_load (pinned host
+ *                                             store -> HBM slot copies instead
+ *                                             of pread + fp32 dequant)
+ *   expert cache  c/src/cache.c            -> qmoe_cache over HBM slot numbers
+ *   route stats / prefetch, streaming.py:400-435 -> qmoe_record_route,
+ *                                             qmoe_prefetch_predictions
+ *
+ * The context owns every device buffer: router, shared gate and shared
+ * expert per layer, the expert pool (fixed-size slots), the expert -> slot
+ * table the kernels read, and workspaces sized for cfg.max_tokens at create
+ * time, so a forward call allocates nothing.
+ */
+#include <cuda_runtime_api.h>
+#include <pthread.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include "../../include/qmoe.h"
+#include "qmoe_internal.h"
+
+#define NO_OWNER UINT64_MAX
+
+typedef struct {
+    uint16_t *router;     /* [E, d] */
+    uint16_t *shgate;     /* [d] */
+    float *bias;          /* [E] or NULL */
+    uint8_t *shared_slot; /* slot layout */
+    int ready;
+} layer_dev;
+
+struct qmoe_ctx {
+    qmoe_config cfg;
+    qk_layout L;
+    int num_sms;
+    cudaStream_t stream, copy_stream;
+    cudaEvent_t copy_done;
+    int *err_dev;
+    int *err_host; /* pinned */
+    layer_dev *layers;
+    /* expert pool */
+    uint8_t *pool;
+    int nslots;
+    int resident_all;
+    int32_t *slot_of_dev;  /* [num_layers * E] */
+    int32_t *slot_of_host; /* [num_layers * E] */
+    uint64_t *slot_owner;  /* [nslots] */
+    int *free_slots;
+    int nfree;
+    qmoe_cache *cache;
+    uint8_t *host_store;   /* pinned [num_layers * E * slot_bytes] when streaming */
+    /* workspaces */
+    float *x_dev, *out_dev, *logits, *wts, *sgate, *h;
+    int32_t *idx;
+    float *x_pin, *out_pin;
+    int32_t *idx_pin;
+    int last_T;
+    qmoe_stats stats;
+    /* route statistics (streaming.py:400-413) */
+    uint64_t *freq;        /* [num_layers * E] */
+    uint32_t *trans;       /* [num_layers * E * E], lazily allocated */
+    int32_t *recent;       /* [num_layers * k] last selection per layer */
+    int *recent_n;
+    /* diagnostics: per-kernel event timing */
+    int profile;
+    cudaEvent_t pev[8];
+    double prof_ms[8];
+    int prof_kernels;
+    uint64_t prof_calls;
+    pthread_mutex_t lock;
+};
+
+static void seterr(qmoe_err *err, const char *fmt, ...) {
+    if (!err) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err->msg, sizeof(err->msg), fmt, ap);
+    va_end(ap);
+}
+
+#define CK(call)                                                                 \
+    do {                                                                         \
+        cudaError_t e_ = (call);                                                 \
+        if (e_ != cudaSuccess) {                                                 \
+            seterr(err, "%s:%d %s: %s", __FILE__, __LINE__, #call,               \
+                   cudaGetErrorString(e_));                                      \
+            goto fail;                                                           \
+        }                                                                        \
+    } while (0)
+
+static double now_s(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
+/* ------------------------------------------------------------------ layout */
+
+int qk_layout_init(qk_layout *L, int d, int E, int k, int I, int g) {
+    if (d <= 0 || E <= 0 || k <= 0 || I <= 0 || g <= 0) return -1;
+    if (g % 32 || d % g || I % g || d % 256 || I % 32) return -1;
+    int units = I / 32;
+    if (units > 32 || (units & (units - 1))) return -1; /* down: lanes per row */
+    if (k > 32 || k > E || E > 1024) return -1;
+    L->d = d; L->E = E; L->k = k; L->I = I; L->g = g;
+    L->gu_row = d / 2 + d / 2 + (d / g) * 8;
+    int drow = I / 2 + (I / g) * 4;
+    L->d_row = (drow + 15) / 16 * 16;
+    L->gu_bytes = (size_t)I * (size_t)L->gu_row;
+    size_t s = L->gu_bytes + (size_t)d * (size_t)L->d_row;
+    L->slot_bytes = (s + 255) / 256 * 256;
+    if (L->gu_row % 16) return -1;
+    return 0;
+}
+
+size_t qmoe_slot_bytes(const qmoe_config *cfg) {
+    qk_layout L;
+    if (!cfg || qk_layout_init(&L, cfg->hidden, cfg->num_experts, cfg->top_k, cfg->moe_inter,
+                               cfg->group_size))
+        return 0;
+    return L.slot_bytes;
+}
+
+void qk_pack_expert(const qk_layout *L, const uint32_t *gq, const uint16_t *gs,
+                    const uint16_t *gb, const uint32_t *uq, const uint16_t *us,
+                    const uint16_t *ub, const uint32_t *dq, const uint16_t *ds,
+                    const uint16_t *db, uint8_t *slot) {
+    int d = L->d, I = L->I, g = L->g, G = d / g, Gd = I / g;
+    for (int n = 0; n < I; n++) {
+        uint8_t *row = slot + (size_t)n * L->gu_row;
+        memcpy(row, gq + (size_t)n * (d / 8), (size_t)d / 2);
+        memcpy(row + d / 2, uq + (size_t)n * (d / 8), (size_t)d / 2);
+        uint16_t *quad = (uint16_t *)(row + d);
+        for (int j = 0; j < G; j++) {
+            quad[4 * j + 0] = gs[(size_t)n * G + j];
+            quad[4 * j + 1] = gb[(size_t)n * G + j];
+            quad[4 * j + 2] = us[(size_t)n * G + j];
+            quad[4 * j + 3] = ub[(size_t)n * G + j];
+        }
+    }
+    uint8_t *dsec = slot + L->gu_bytes;
+    for (int n = 0; n < d; n++) {
+        uint8_t *row = dsec + (size_t)n * L->d_row;
+        memset(row, 0, (size_t)L->d_row);
+        memcpy(row, dq + (size_t)n * (I / 8), (size_t)I / 2);
+        uint16_t *pair = (uint16_t *)(row + I / 2);
+        for (int j = 0; j < Gd; j++) {
+            pair[2 * j + 0] = ds[(size_t)n * Gd + j];
+            pair[2 * j + 1] = db[(size_t)n * Gd + j];
+        }
+    }
+    size_t used = L->gu_bytes + (size_t)d * L->d_row;
+    if (used < L->slot_bytes) memset(slot + used, 0, L->slot_bytes - used);
+}
+
+static void pack_routed(const qmoe_ctx *c, const qmoe_layer_weights *w, int e, uint8_t *slot) {
+    const qk_layout *L = &c->L;
+    size_t d = (size_t)L->d, I = (size_t)L->I, g = (size_t)L->g;
+    size_t qo = (size_t)e * I * (d / 8), so = (size_t)e * I * (d / g);
+    size_t dqo = (size_t)e * d * (I / 8), dso = (size_t)e * d * (I / g);
+    qk_pack_expert(L, w->gate.q + qo, w->gate.scales + so, w->gate.biases + so, w->up.q + qo,
+                   w->up.scales + so, w->up.biases + so, w->down.q + dqo, w->down.scales + dso,
+                   w->down.biases + dso, slot);
+}
+
+/* ----------------------------------------------------------------- create */
+
+void qmoe_destroy(qmoe_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->cfg.device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    if (c->layers) {
+        for (int l = 0; l < c->cfg.num_layers; l++) {
+            cudaFree(c->layers[l].router);
+            cudaFree(c->layers[l].shgate);
+            cudaFree(c->layers[l].bias);
+            cudaFree(c->layers[l].shared_slot);
+        }
+        free(c->layers);
+    }
+    cudaFree(c->pool);
+    cudaFree(c->slot_of_dev);
+    cudaFree(c->err_dev);
+    cudaFree(c->x_dev);
+    cudaFree(c->out_dev);
+    cudaFree(c->logits);
+    cudaFree(c->idx);
+    cudaFree(c->wts);
+    cudaFree(c->sgate);
+    cudaFree(c->h);
+    cudaFreeHost(c->x_pin);
+    cudaFreeHost(c->out_pin);
+    cudaFreeHost(c->idx_pin);
+    cudaFreeHost(c->err_host);
+    cudaFreeHost(c->host_store);
+    free(c->slot_of_host);
+    free(c->slot_owner);
+    free(c->free_slots);
+    free(c->freq);
+    free(c->trans);
+    free(c->recent);
+    free(c->recent_n);
+    if (c->cache) qmoe_cache_free(c->cache);
+    if (c->copy_done) cudaEventDestroy(c->copy_done);
+    for (int i = 0; i < 8; i++)
+        if (c->pev[i]) cudaEventDestroy(c->pev[i]);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+    pthread_mutex_destroy(&c->lock);
+    free(c);
+}
+
+qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!cfg) {
+        seterr(err, "qmoe_create: NULL config");
+        return NULL;
+    }
+    if (cfg->bits != 4) {
+        seterr(err, "qmoe_create: only 4-bit experts are supported (bits=%d)", cfg->bits);
+        return NULL;
+    }
+    if (cfg->num_layers < 1 || cfg->max_tokens < 1) {
+        seterr(err, "qmoe_create: num_layers and max_tokens must be positive");
+        return NULL;
+    }
+    qmoe_ctx *c = calloc(1, sizeof(*c));
+    if (!c) {
+        seterr(err, "qmoe_create: out of host memory");
+        return NULL;
+    }
+    pthread_mutex_init(&c->lock, NULL);
+    c->cfg = *cfg;
+    if (qk_layout_init(&c->L, cfg->hidden, cfg->num_experts, cfg->top_k, cfg->moe_inter,
+                       cfg->group_size)) {
+        seterr(err,
+               "qmoe_create: unsupported shape d=%d E=%d k=%d I=%d g=%d (need d %% 256 == 0, "
+               "g %% 32 == 0, I/32 a power of two <= 32, k <= 32, E <= 1024)",
+               cfg->hidden, cfg->num_experts, cfg->top_k, cfg->moe_inter, cfg->group_size);
+        free(c);
+        return NULL;
+    }
+    const int Lz = cfg->num_layers, E = cfg->num_experts, T = cfg->max_tokens;
+    const qk_layout *L = &c->L;
+    CK(cudaSetDevice(cfg->device));
+    CK(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, cfg->device));
+    {
+        int major = 0, minor = 0;
+        CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, cfg->device));
+        CK(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, cfg->device));
+        if (major != 10 || minor != 0) {
+            seterr(err, "qmoe_create: device %d is sm_%d%d; this library is built for sm_100a only",
+                   cfg->device, major, minor);
+            goto fail;
+        }
+    }
+    CK((cudaError_t)qk_prepare_kernels());
+    for (int i = 0; i < 8; i++) CK(cudaEventCreate(&c->pev[i]));
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&c->copy_done, cudaEventDisableTiming));
+    CK(cudaMalloc((void **)&c->err_dev, sizeof(int)));
+    CK(cudaMemset(c->err_dev, 0, sizeof(int)));
+    CK(cudaMallocHost((void **)&c->err_host, sizeof(int)));
+    c->layers = calloc((size_t)Lz, sizeof(layer_dev));
+    if (!c->layers) {
+        seterr(err, "qmoe_create: out of host memory");
+        goto fail;
+    }
+    /* pool */
+    {
+        uint64_t total = (uint64_t)Lz * (uint64_t)E;
+        uint64_t want = cfg->pool_bytes ? cfg->pool_bytes / L->slot_bytes : total;
+        if (want > total) want = total;
+        if (want < (uint64_t)cfg->top_k) {
+            seterr(err, "qmoe_create: pool_bytes holds %llu slots, fewer than top_k=%d",
+                   (unsigned long long)want, cfg->top_k);
+            goto fail;
+        }
+        c->nslots = (int)want;
+        c->resident_all = want == total;
+        CK(cudaMalloc((void **)&c->pool, (size_t)c->nslots * L->slot_bytes));
+        CK(cudaMalloc((void **)&c->slot_of_dev, (size_t)total * sizeof(int32_t)));
+        CK(cudaMemset(c->slot_of_dev, 0xff, (size_t)total * sizeof(int32_t)));
+        c->slot_of_host = malloc((size_t)total * sizeof(int32_t));
+        c->slot_owner = malloc((size_t)c->nslots * sizeof(uint64_t));
+        c->free_slots = malloc((size_t)c->nslots * sizeof(int));
+        c->freq = calloc((size_t)total, sizeof(uint64_t));
+        c->recent = calloc((size_t)Lz * cfg->top_k * 4, sizeof(int32_t));
+        c->recent_n = calloc((size_t)Lz, sizeof(int));
+        if (!c->slot_of_host || !c->slot_owner || !c->free_slots || !c->freq || !c->recent ||
+            !c->recent_n) {
+            seterr(err, "qmoe_create: out of host memory");
+            goto fail;
+        }
+        memset(c->slot_of_host, 0xff, (size_t)total * sizeof(int32_t));
+        for (int s = 0; s < c->nslots; s++) {
+            c->slot_owner[s] = NO_OWNER;
+            c->free_slots[s] = c->nslots - 1 - s; /* pop order 0, 1, 2, ... */
+        }
+        c->nfree = c->nslots;
+        c->cache = qmoe_cache_new((uint64_t)c->nslots * L->slot_bytes, cfg->policy,
+                                  c->resident_all ? 0 : Lz);
+        if (!c->cache) {
+            seterr(err, "qmoe_create: out of host memory");
+            goto fail;
+        }
+        if (!c->resident_all) {
+            size_t hs = (size_t)total * L->slot_bytes;
+            CK(cudaHostAlloc((void **)&c->host_store, hs, cudaHostAllocPortable));
+        }
+    }
+    /* workspaces for max_tokens */
+    CK(cudaMalloc((void **)&c->x_dev, (size_t)T * L->d * sizeof(float)));
+    CK(cudaMalloc((void **)&c->out_dev, (size_t)T * L->d * sizeof(float)));
+    CK(cudaMalloc((void **)&c->logits, (size_t)T * (E + 1) * sizeof(float)));
+    CK(cudaMalloc((void **)&c->idx, (size_t)T * L->k * sizeof(int32_t)));
+    CK(cudaMalloc((void **)&c->wts, (size_t)T * L->k * sizeof(float)));
+    CK(cudaMalloc((void **)&c->sgate, (size_t)T * sizeof(float)));
+    CK(cudaMalloc((void **)&c->h, (size_t)T * (L->k + 1) * L->I * sizeof(float)));
+    CK(cudaMallocHost((void **)&c->x_pin, (size_t)T * L->d * sizeof(float)));
+    CK(cudaMallocHost((void **)&c->out_pin, (size_t)T * L->d * sizeof(float)));
+    CK(cudaMallocHost((void **)&c->idx_pin, (size_t)T * L->k * sizeof(int32_t)));
+    return c;
+fail:
+    qmoe_destroy(c);
+    return NULL;
+}
+
+/* ------------------------------------------------------------- pool fills */
+
+static uint64_t ekey(int layer, int e) { return ((uint64_t)(uint32_t)layer << 32) | (uint32_t)e; }
+
+/* Assigns a slot to (layer, e) in the bookkeeping; evicted owners lose their
+ * table entries. Returns the slot or -1 when the cache rejects the entry (all
+ * candidates pinned). Caller holds c->lock. */
+static int claim_slot(qmoe_ctx *c, int layer, int e, int pin) {
+    uint64_t key = ekey(layer, e);
+    uint64_t ev[64];
+    size_t nev = 0;
+    int slot = c->nfree > 0 ? c->free_slots[c->nfree - 1] : -1;
+    if (!qmoe_cache_put(c->cache, key, slot >= 0 ? (uint64_t)slot : NO_OWNER, c->L.slot_bytes,
+                        pin, 0, ev, 64, &nev))
+        return -1;
+    if (slot >= 0) c->nfree--;
+    for (size_t i = 0; i < nev && i < 64; i++) {
+        if (ev[i] == NO_OWNER) continue;
+        int s = (int)ev[i];
+        uint64_t owner = c->slot_owner[s];
+        if (owner != NO_OWNER) {
+            c->slot_of_host[(owner >> 32) * (uint64_t)c->L.E + (uint32_t)owner] = -1;
+            c->slot_owner[s] = NO_OWNER;
+        }
+        c->free_slots[c->nfree++] = s;
+    }
+    if (slot < 0) {
+        if (c->nfree == 0) {
+            uint64_t dummy;
+            qmoe_cache_erase(c->cache, key, &dummy);
+            return -1;
+        }
+        slot = c->free_slots[--c->nfree];
+        qmoe__cache_set_value(c->cache, key, (uint64_t)slot);
+    }
+    c->slot_owner[slot] = key;
+    c->slot_of_host[(size_t)layer * c->L.E + e] = slot;
+    return slot;
+}
+
+/* Synchronous fill of the uncached experts in ids (experts_load semantics:
+ * present entries are skipped without touching their stats). While the call
+ * runs, every listed expert is pinned so that filling one cannot evict
+ * another the same call needs; pins the call added are dropped at the end.
+ * The caller makes sure no queued kernel still reads a slot that may be
+ * evicted (the compute stream is idle). */
+static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qmoe_err *err) {
+    const qk_layout *L = &c->L;
+    double t0 = now_s();
+    int loaded = 0, rc = 0;
+    if (n > (size_t)c->nslots) {
+        seterr(err, "qmoe_experts_load: %zu experts requested, the pool has %d slots", n,
+               c->nslots);
+        return -1;
+    }
+    unsigned char *ours = calloc(n ? n : 1, 1);
+    if (!ours) {
+        seterr(err, "qmoe_experts_load: out of host memory");
+        return -1;
+    }
+    pthread_mutex_lock(&c->lock);
+    for (size_t i = 0; i < n; i++) {
+        int e = (int)ids[i];
+        if (e < 0 || e >= L->E) {
+            seterr(err, "qmoe_experts_load: expert %lld out of range", (long long)ids[i]);
+            rc = -1;
+            break;
+        }
+        if (qmoe_cache_peek(c->cache, ekey(layer, e), NULL)) {
+            ours[i] = (unsigned char)qmoe_cache_pin(c->cache, ekey(layer, e));
+            continue;
+        }
+        if (!c->host_store) {
+            seterr(err, "qmoe_experts_load: expert %d of layer %d was never uploaded", e, layer);
+            rc = -1;
+            break;
+        }
+        int slot = claim_slot(c, layer, e, 1);
+        if (slot < 0) {
+            seterr(err, "qmoe_experts_load: pool full of pinned experts (layer %d expert %d)",
+                   layer, e);
+            rc = -1;
+            break;
+        }
+        ours[i] = 1;
+        const uint8_t *src = c->host_store + ((size_t)layer * L->E + e) * L->slot_bytes;
+        cudaError_t ce = cudaMemcpyAsync(c->pool + (size_t)slot * L->slot_bytes, src,
+                                         L->slot_bytes, cudaMemcpyHostToDevice, c->copy_stream);
+        if (ce != cudaSuccess) {
+            seterr(err, "qmoe_experts_load: %s", cudaGetErrorString(ce));
+            rc = -1;
+            break;
+        }
+        loaded++;
+    }
+    for (size_t i = 0; i < n; i++)
+        if (ours[i]) qmoe_cache_unpin(c->cache, ekey(layer, (int)ids[i]));
+    free(ours);
+    cudaError_t ce = cudaMemcpyAsync(c->slot_of_dev + (size_t)layer * L->E,
+                                     c->slot_of_host + (size_t)layer * L->E,
+                                     (size_t)L->E * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                     c->copy_stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->copy_stream);
+    pthread_mutex_unlock(&c->lock);
+    if (rc) return rc;
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_experts_load: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    c->stats.expert_loads += (uint64_t)loaded;
+    c->stats.expert_bytes += (uint64_t)loaded * L->slot_bytes;
+    c->stats.expert_wait_seconds += now_s() - t0;
+    return 0;
+}
+
+/* ----------------------------------------------------------------- upload */
+
+static int upload_shared(qmoe_ctx *c, layer_dev *ld, const qmoe_layer_weights *w, qmoe_err *err) {
+    const qk_layout *L = &c->L;
+    uint8_t *buf = malloc(L->slot_bytes);
+    if (!buf) {
+        seterr(err, "qmoe_upload_layer: out of host memory");
+        return -1;
+    }
+    qk_pack_expert(L, w->sh_gate.q, w->sh_gate.scales, w->sh_gate.biases, w->sh_up.q,
+                   w->sh_up.scales, w->sh_up.biases, w->sh_down.q, w->sh_down.scales,
+                   w->sh_down.biases, buf);
+    cudaError_t ce = cudaSuccess;
+    if (!ld->shared_slot) ce = cudaMalloc((void **)&ld->shared_slot, L->slot_bytes);
+    if (ce == cudaSuccess) ce = cudaMemcpy(ld->shared_slot, buf, L->slot_bytes, cudaMemcpyHostToDevice);
+    free(buf);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_upload_layer: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    return 0;
+}
+
+int qmoe_upload_layer(qmoe_ctx *c, int layer, const qmoe_layer_weights *w, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || !w || layer < 0 || layer >= c->cfg.num_layers) {
+        seterr(err, "qmoe_upload_layer: bad arguments (layer %d)", layer);
+        return -1;
+    }
+    const qmoe_q4 *ts[6] = {&w->gate, &w->up, &w->down, &w->sh_gate, &w->sh_up, &w->sh_down};
+    for (int i = 0; i < 6; i++)
+        if (!ts[i]->q || !ts[i]->scales || !ts[i]->biases) {
+            seterr(err, "qmoe_upload_layer: missing q4 tensor %d", i);
+            return -1;
+        }
+    if (!w->router || !w->shared_gate) {
+        seterr(err, "qmoe_upload_layer: missing router or shared gate");
+        return -1;
+    }
+    const qk_layout *L = &c->L;
+    layer_dev *ld = &c->layers[layer];
+    uint8_t *stage = NULL;
+    const int batch = 16;
+    CK(cudaSetDevice(c->cfg.device));
+    CK(cudaStreamSynchronize(c->stream));
+    if (!ld->router) CK(cudaMalloc((void **)&ld->router, (size_t)L->E * L->d * 2));
+    if (!ld->shgate) CK(cudaMalloc((void **)&ld->shgate, (size_t)L->d * 2));
+    CK(cudaMemcpy(ld->router, w->router, (size_t)L->E * L->d * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ld->shgate, w->shared_gate, (size_t)L->d * 2, cudaMemcpyHostToDevice));
+    if (w->logit_bias) {
+        if (!ld->bias) CK(cudaMalloc((void **)&ld->bias, (size_t)L->E * sizeof(float)));
+        CK(cudaMemcpy(ld->bias, w->logit_bias, (size_t)L->E * sizeof(float), cudaMemcpyHostToDevice));
+    } else if (ld->bias) {
+        cudaFree(ld->bias);
+        ld->bias = NULL;
+    }
+    if (upload_shared(c, ld, w, err)) return -1;
+    if (c->resident_all) {
+        CK(cudaMallocHost((void **)&stage, (size_t)batch * L->slot_bytes));
+        for (int e0 = 0; e0 < L->E; e0 += batch) {
+            int nb = L->E - e0 < batch ? L->E - e0 : batch;
+            CK(cudaStreamSynchronize(c->copy_stream));
+            for (int i = 0; i < nb; i++) pack_routed(c, w, e0 + i, stage + (size_t)i * L->slot_bytes);
+            pthread_mutex_lock(&c->lock);
+            int first = -1, contiguous = 1;
+            for (int i = 0; i < nb; i++) {
+                int e = e0 + i;
+                int slot = c->slot_of_host[(size_t)layer * L->E + e];
+                if (slot < 0) slot = claim_slot(c, layer, e, 0);
+                if (i == 0) first = slot;
+                else if (slot != first + i) contiguous = 0;
+                if (slot < 0) contiguous = -1;
+            }
+            pthread_mutex_unlock(&c->lock);
+            if (contiguous < 0) {
+                seterr(err, "qmoe_upload_layer: pool bookkeeping failed");
+                goto fail;
+            }
+            if (contiguous) {
+                CK(cudaMemcpyAsync(c->pool + (size_t)first * L->slot_bytes, stage,
+                                   (size_t)nb * L->slot_bytes, cudaMemcpyHostToDevice, c->copy_stream));
+            } else {
+                for (int i = 0; i < nb; i++) {
+                    int slot = c->slot_of_host[(size_t)layer * L->E + e0 + i];
+                    CK(cudaMemcpyAsync(c->pool + (size_t)slot * L->slot_bytes,
+                                       stage + (size_t)i * L->slot_bytes, L->slot_bytes,
+                                       cudaMemcpyHostToDevice, c->copy_stream));
+                }
+            }
+        }
+        CK(cudaStreamSynchronize(c->copy_stream));
+        CK(cudaMemcpy(c->slot_of_dev + (size_t)layer * L->E, c->slot_of_host + (size_t)layer * L->E,
+                      (size_t)L->E * sizeof(int32_t), cudaMemcpyHostToDevice));
+        cudaFreeHost(stage);
+        stage = NULL;
+    } else {
+        /* streaming: experts stay in the pinned host store; drop stale slots */
+        pthread_mutex_lock(&c->lock);
+        for (int e = 0; e < L->E; e++) {
+            uint64_t v;
+            if (qmoe_cache_erase(c->cache, ekey(layer, e), &v) && v != NO_OWNER) {
+                c->slot_owner[v] = NO_OWNER;
+                c->free_slots[c->nfree++] = (int)v;
+            }
+            c->slot_of_host[(size_t)layer * L->E + e] = -1;
+            pack_routed(c, w, e, c->host_store + ((size_t)layer * L->E + e) * L->slot_bytes);
+        }
+        pthread_mutex_unlock(&c->lock);
+        CK(cudaMemcpy(c->slot_of_dev + (size_t)layer * L->E, c->slot_of_host + (size_t)layer * L->E,
+                      (size_t)L->E * sizeof(int32_t), cudaMemcpyHostToDevice));
+    }
+    ld->ready = 1;
+    return 0;
+fail:
+    if (stage) cudaFreeHost(stage);
+    return -1;
+}
+
+/* ---------------------------------------------------------------- forward */
+
+static void fill_fwd(qmoe_ctx *c, int layer, const void *x, int x_bf16, int n, float *out,
+                     qk_fwd *f) {
+    layer_dev *ld = &c->layers[layer];
+    memset(f, 0, sizeof(*f));
+    f->L = c->L;
+    f->T = n;
+    f->x = x;
+    f->x_bf16 = x_bf16;
+    f->router = ld->router;
+    f->shared_gate = ld->shgate;
+    f->logit_bias = ld->bias;
+    f->pool = c->pool;
+    f->slot_of = c->slot_of_dev + (size_t)layer * c->L.E;
+    f->shared_slot = ld->shared_slot;
+    f->logits = c->logits;
+    f->idx = c->idx;
+    f->wts = c->wts;
+    f->sgate = c->sgate;
+    f->h = c->h;
+    f->out = out;
+    f->err = c->err_dev;
+    f->num_sms = c->num_sms;
+}
+
+static int kerr(int rc, const char *what, qmoe_err *err) {
+    if (rc != 0) {
+        seterr(err, "%s launch failed: %s", what, cudaGetErrorString((cudaError_t)rc));
+        return -1;
+    }
+    return 0;
+}
+
+/* streaming mode: route first, make the selected experts resident */
+static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, qmoe_err *err) {
+    int n = f->T, k = c->L.k;
+    if (kerr(qk_launch_router(f, st, 0), "router", err)) return -1;
+    if (kerr(qk_launch_topk(f, st, 0), "topk", err)) return -1;
+    cudaError_t ce = cudaMemcpyAsync(c->idx_pin, c->idx, (size_t)n * k * sizeof(int32_t),
+                                     cudaMemcpyDeviceToHost, st);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    int64_t *uniq = calloc((size_t)n * k, sizeof(int64_t));
+    unsigned char *seen = calloc((size_t)c->L.E, 1);
+    if (!uniq || !seen) {
+        free(uniq);
+        free(seen);
+        seterr(err, "qmoe_forward: out of host memory");
+        return -1;
+    }
+    size_t nu = 0;
+    for (int i = 0; i < n * k; i++) {
+        int e = c->idx_pin[i];
+        if (e >= 0 && e < c->L.E && !seen[e]) {
+            seen[e] = 1;
+            uniq[nu++] = e;
+        }
+    }
+    free(seen);
+    int rc = fill_experts(c, layer, uniq, nu, err);
+    if (rc == 0) {
+        pthread_mutex_lock(&c->lock);
+        for (size_t i = 0; i < nu; i++) qmoe_cache_get(c->cache, ekey(layer, (int)uniq[i]), NULL);
+        pthread_mutex_unlock(&c->lock);
+    }
+    free(uniq);
+    return rc;
+}
+
+int qmoe_forward_dev(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, float *out,
+                     void *stream, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || !x || !out || layer < 0 || layer >= c->cfg.num_layers) {
+        seterr(err, "qmoe_forward: bad arguments (layer %d)", layer);
+        return -1;
+    }
+    if (!c->layers[layer].ready) {
+        seterr(err, "qmoe_forward: layer %d was not uploaded", layer);
+        return -1;
+    }
+    if (n < 0 || n > c->cfg.max_tokens) {
+        seterr(err, "qmoe_forward: n=%d outside [0, max_tokens=%d]", n, c->cfg.max_tokens);
+        return -1;
+    }
+    if (x_dtype != QMOE_F32 && x_dtype != QMOE_BF16) {
+        seterr(err, "qmoe_forward: unknown x dtype %d", x_dtype);
+        return -1;
+    }
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    if (n == 0) return 0;
+    qk_fwd f;
+    fill_fwd(c, layer, x, x_dtype == QMOE_BF16, n, out, &f);
+    c->last_T = n;
+    if (n == 1) c->stats.decode_calls++;
+    else c->stats.prefill_calls++;
+    const int prof = c->profile;
+    if (!c->resident_all) {
+        if (stream_in(c, layer, &f, st, err)) return -1;
+        if (prof) cudaEventRecord(c->pev[2], st);
+    } else {
+        if (prof) cudaEventRecord(c->pev[0], st);
+        if (kerr(qk_launch_router(&f, st, !prof), "router", err)) return -1;
+        if (prof) cudaEventRecord(c->pev[1], st);
+        if (kerr(qk_launch_topk(&f, st, !prof), "topk", err)) return -1;
+        if (prof) cudaEventRecord(c->pev[2], st);
+    }
+    if (kerr(qk_launch_decode_gateup(&f, st, !prof), "decode_gateup", err)) return -1;
+    if (prof) cudaEventRecord(c->pev[3], st);
+    if (kerr(qk_launch_decode_down(&f, st, !prof), "decode_down", err)) return -1;
+    if (prof) {
+        cudaEventRecord(c->pev[4], st);
+        cudaError_t ce = cudaEventSynchronize(c->pev[4]);
+        if (ce != cudaSuccess) {
+            seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
+            return -1;
+        }
+        for (int i = c->resident_all ? 0 : 2; i < 4; i++) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, c->pev[i], c->pev[i + 1]);
+            c->prof_ms[i] += ms;
+        }
+        c->prof_kernels = 4;
+        c->prof_calls++;
+    }
+    return 0;
+}
+
+int qmoe_profile_enable(qmoe_ctx *c, int on) {
+    if (!c) return -1;
+    c->profile = on != 0;
+    return 0;
+}
+
+int qmoe_profile_read(qmoe_ctx *c, double *kernel_ms, int max_kernels, int *kernels_per_call,
+                      uint64_t *calls) {
+    if (!c) return -1;
+    for (int i = 0; i < max_kernels && i < 8; i++) kernel_ms[i] = c->prof_ms[i];
+    if (kernels_per_call) *kernels_per_call = c->prof_kernels;
+    if (calls) *calls = c->prof_calls;
+    memset(c->prof_ms, 0, sizeof(c->prof_ms));
+    c->prof_calls = 0;
+    return 0;
+}
+
+static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err) {
+    cudaError_t ce = cudaMemcpyAsync(c->err_host, c->err_dev, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe: CUDA error: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    int code = *c->err_host;
+    if (code) {
+        cudaMemsetAsync(c->err_dev, 0, sizeof(int), st);
+        cudaStreamSynchronize(st);
+        seterr(err, "qmoe: device reported error 0x%x (%s%s%s)", code,
+               code & QK_ERR_TIMEOUT_COPY ? "copy wait timed out " : "",
+               code & QK_ERR_NOT_RESIDENT ? "routed expert not resident " : "",
+               code & QK_ERR_BAD_ROUTE ? "top-k selection failed" : "");
+        return -1;
+    }
+    return 0;
+}
+
+int qmoe_sync(qmoe_ctx *c, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c) return -1;
+    return check_dev_err(c, c->stream, err);
+}
+
+int qmoe_forward(qmoe_ctx *c, int layer, const float *x, int n, float *out, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || (n > 0 && (!x || !out))) {
+        seterr(err, "qmoe_forward: bad arguments");
+        return -1;
+    }
+    if (n < 0 || n > c->cfg.max_tokens) {
+        seterr(err, "qmoe_forward: n=%d outside [0, max_tokens=%d]", n, c->cfg.max_tokens);
+        return -1;
+    }
+    if (n == 0) return 0;
+    double t0 = now_s();
+    size_t bytes = (size_t)n * c->L.d * sizeof(float);
+    memcpy(c->x_pin, x, bytes);
+    cudaError_t ce = cudaMemcpyAsync(c->x_dev, c->x_pin, bytes, cudaMemcpyHostToDevice, c->stream);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    if (qmoe_forward_dev(c, layer, c->x_dev, QMOE_F32, n, c->out_dev, c->stream, err)) return -1;
+    ce = cudaMemcpyAsync(c->out_pin, c->out_dev, bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    if (check_dev_err(c, c->stream, err)) return -1;
+    memcpy(out, c->out_pin, bytes);
+    c->stats.forward_seconds += now_s() - t0;
+    return 0;
+}
+
+int qmoe_last_routing(qmoe_ctx *c, int32_t *idx, float *weights, float *shared_gate,
+                      qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c) return -1;
+    int n = c->last_T, k = c->L.k;
+    cudaError_t ce = cudaStreamSynchronize(c->stream);
+    if (ce == cudaSuccess && idx && n)
+        ce = cudaMemcpy(idx, c->idx, (size_t)n * k * sizeof(int32_t), cudaMemcpyDeviceToHost);
+    if (ce == cudaSuccess && weights && n)
+        ce = cudaMemcpy(weights, c->wts, (size_t)n * k * sizeof(float), cudaMemcpyDeviceToHost);
+    if (ce == cudaSuccess && shared_gate && n)
+        ce = cudaMemcpy(shared_gate, c->sgate, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_last_routing: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    return 0;
+}
+
+/* -------------------------------------------------------- cache hooks */
+
+int qmoe_expert_peek(qmoe_ctx *c, int layer, int e) {
+    uint64_t v;
+    if (!c || !qmoe_cache_peek(c->cache, ekey(layer, e), &v) || v == NO_OWNER) return -1;
+    return (int)v;
+}
+
+int qmoe_expert_get(qmoe_ctx *c, int layer, int e) {
+    uint64_t v;
+    if (!c || !qmoe_cache_get(c->cache, ekey(layer, e), &v) || v == NO_OWNER) return -1;
+    return (int)v;
+}
+
+int qmoe_experts_load(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || layer < 0 || layer >= c->cfg.num_layers || (n && !ids)) {
+        seterr(err, "qmoe_experts_load: bad arguments");
+        return -1;
+    }
+    /* slots may be read by queued kernels: let them finish before reuse */
+    cudaError_t ce = cudaStreamSynchronize(c->stream);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_experts_load: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    return fill_experts(c, layer, ids, n, err);
+}
+
+int qmoe_expert_pin(qmoe_ctx *c, int layer, int e) {
+    return c ? qmoe_cache_pin(c->cache, ekey(layer, e)) : 0;
+}
+int qmoe_expert_unpin(qmoe_ctx *c, int layer, int e) {
+    return c ? qmoe_cache_unpin(c->cache, ekey(layer, e)) : 0;
+}
+int qmoe_expert_mark_hot(qmoe_ctx *c, int layer, int e, int hot) {
+    return c ? qmoe_cache_mark_hot(c->cache, ekey(layer, e), hot) : 0;
+}
+
+int qmoe_cache_snapshot(qmoe_ctx *c, qmoe_cache_stats *out) {
+    if (!c || !out) return -1;
+    *out = qmoe_cache_stats_get(c->cache);
+    return 0;
+}
+
+int qmoe_stats_get(qmoe_ctx *c, qmoe_stats *out) {
+    if (!c || !out) return -1;
+    *out = c->stats;
+    return 0;
+}
+
+/* ------------------------------------------------------ prefetch hooks */
+
+int qmoe_prefetch(qmoe_ctx *c, int layer, const int64_t *ids, size_t n) {
+    if (!c || layer < 0 || layer >= c->cfg.num_layers || c->resident_all) return 0;
+    qmoe_err e;
+    int queued = 0;
+    /* a fill may evict a slot that queued kernels still read */
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return 0;
+    for (size_t i = 0; i < n; i++) {
+        int ex = (int)ids[i];
+        if (ex < 0 || ex >= c->L.E) continue;
+        if (qmoe_cache_peek(c->cache, ekey(layer, ex), NULL)) continue;
+        int64_t one = ex;
+        if (fill_experts(c, layer, &one, 1, &e) == 0) queued++;
+    }
+    c->stats.prefetch_issued += (uint64_t)queued;
+    return queued;
+}
+
+void qmoe_record_route(qmoe_ctx *c, int layer, const int32_t *experts, size_t n) {
+    if (!c || layer < 0 || layer >= c->cfg.num_layers || !experts) return;
+    const int E = c->L.E, K = c->L.k * 4;
+    pthread_mutex_lock(&c->lock);
+    if (!c->trans) c->trans = calloc((size_t)c->cfg.num_layers * E * E, sizeof(uint32_t));
+    /* selected = sorted distinct experts of this step */
+    unsigned char *mark = calloc((size_t)E, 1);
+    int32_t sel[4096];
+    int ns = 0;
+    for (size_t i = 0; i < n; i++) {
+        int e = experts[i];
+        if (e < 0 || e >= E) continue;
+        c->freq[(size_t)layer * E + e]++;
+        if (mark && !mark[e]) mark[e] = 1;
+    }
+    if (mark)
+        for (int e = 0; e < E && ns < 4096; e++)
+            if (mark[e]) sel[ns++] = e;
+    free(mark);
+    int32_t *prev = c->recent + (size_t)layer * K;
+    if (c->trans)
+        for (int p = 0; p < c->recent_n[layer]; p++)
+            for (int s = 0; s < ns; s++)
+                c->trans[((size_t)layer * E + prev[p]) * E + sel[s]]++;
+    int keep = ns < K ? ns : K;
+    memcpy(prev, sel, (size_t)keep * sizeof(int32_t));
+    c->recent_n[layer] = keep;
+    for (int s = 0; s < ns; s++)
+        qmoe_cache_mark_hot(c->cache, ekey(layer, sel[s]), c->freq[(size_t)layer * E + sel[s]] >= 4);
+    pthread_mutex_unlock(&c->lock);
+}
+
+/* the `count` highest scores, ties to the lower expert id */
+static int top_by_score(const uint64_t *score, int E, int count, int64_t *out) {
+    int got = 0;
+    for (int r = 0; r < count; r++) {
+        int best = -1;
+        for (int e = 0; e < E; e++) {
+            if (!score[e]) continue;
+            int taken = 0;
+            for (int i = 0; i < got; i++)
+                if (out[i] == e) { taken = 1; break; }
+            if (taken) continue;
+            if (best < 0 || score[e] > score[best]) best = e;
+        }
+        if (best < 0) break;
+        out[got++] = best;
+    }
+    return got;
+}
+
+int qmoe_prefetch_predictions(qmoe_ctx *c, int layer, const int32_t *selected, size_t n) {
+    if (!c || layer < 0 || layer >= c->cfg.num_layers || c->cfg.prefetch_depth <= 0) return 0;
+    const int E = c->L.E, P = c->cfg.prefetch_depth;
+    uint64_t *cand = calloc((size_t)E, sizeof(uint64_t));
+    if (!cand) return 0;
+    int64_t pick[64];
+    int npick = 0, nnext = 0;
+    int64_t next[64];
+    pthread_mutex_lock(&c->lock);
+    int any = 0;
+    if (c->trans)
+        for (size_t i = 0; i < n; i++) {
+            int s = selected[i];
+            if (s < 0 || s >= E) continue;
+            for (int e = 0; e < E; e++) {
+                uint32_t v = c->trans[((size_t)layer * E + s) * E + e];
+                if (v) { cand[e] += v; any = 1; }
+            }
+        }
+    if (!any)
+        for (int e = 0; e < E; e++) cand[e] += c->freq[(size_t)layer * E + e];
+    if (layer + 1 < c->cfg.num_layers)
+        for (int e = 0; e < E; e++) cand[e] += 2 * c->freq[(size_t)(layer + 1) * E + e];
+    npick = top_by_score(cand, E, P < 64 ? P : 64, pick);
+    if (layer + 1 < c->cfg.num_layers)
+        nnext = top_by_score(c->freq + (size_t)(layer + 1) * E, E, P < 64 ? P : 64, next);
+    pthread_mutex_unlock(&c->lock);
+    free(cand);
+    int q = qmoe_prefetch(c, layer, pick, (size_t)npick);
+    if (nnext) q += qmoe_prefetch(c, layer + 1, next, (size_t)nnext);
+    return q;
+}
+
+const char *qmoe_version(void) { return "qmoe-b200 0.1 (sm_100a)"; }

@@ -1,0 +1,92 @@
+/*
+ * qmoe_internal.h - layouts and kernel launchers shared by the host C code
+ * and the CUDA translation units. Not part of the public ABI.
+ */
+#ifndef QMOE_INTERNAL_H
+#define QMOE_INTERNAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/*
+ * Expert slot layout in HBM (one routed expert, or the shared expert):
+ *
+ *   GU section, I rows of gu_row bytes; h-row n holds
+ *     [ gate q: d/2 bytes ][ up q: d/2 bytes ][ d/g quads (gs, gb, us, ub) bf16 ]
+ *   D section, d rows of d_row bytes; output row n holds
+ *     [ down q: I/2 bytes ][ I/g pairs (ds, db) bf16 ][ pad to 16 bytes ]
+ *
+ * Nibble order inside the q bytes is the checkpoint's (low nibble first,
+ * c/src/kernel.c:163-166), so a row's q bytes are the checkpoint row verbatim.
+ * Gate and up rows of the same h-row sit side by side so one contiguous read
+ * feeds SiLU(gate) * up, and scales ride with their row.
+ */
+typedef struct {
+    int d, E, k, I, g;
+    int gu_row;        /* bytes per GU row */
+    int d_row;         /* bytes per D row (16-byte multiple) */
+    size_t gu_bytes;   /* I * gu_row */
+    size_t slot_bytes; /* gu_bytes + d * d_row, rounded up to 256 */
+} qk_layout;
+
+int qk_layout_init(qk_layout *L, int d, int E, int k, int I, int g);
+
+/* Host-side repack of one expert from checkpoint layout into a slot. */
+void qk_pack_expert(const qk_layout *L, const uint32_t *gq, const uint16_t *gs,
+                    const uint16_t *gb, const uint32_t *uq, const uint16_t *us,
+                    const uint16_t *ub, const uint32_t *dq, const uint16_t *ds,
+                    const uint16_t *db, uint8_t *slot);
+
+/* Device error word bits (set by kernels, read by the host after a sync). */
+enum {
+    QK_ERR_TIMEOUT_COPY = 1,  /* bulk-copy completion wait gave up */
+    QK_ERR_NOT_RESIDENT = 2,  /* a routed expert had no HBM slot */
+    QK_ERR_BAD_ROUTE = 4,     /* top-k found fewer than k finite logits */
+};
+
+/* Everything one forward call needs on the device. */
+typedef struct {
+    qk_layout L;
+    int T;                       /* tokens */
+    const void *x;               /* [T, d] fp32 or bf16 */
+    int x_bf16;
+    const uint16_t *router;      /* [E, d] bf16 */
+    const uint16_t *shared_gate; /* [d] bf16 */
+    const float *logit_bias;     /* [E] or NULL */
+    const uint8_t *pool;         /* slot 0 of the HBM pool */
+    const int32_t *slot_of;      /* [E] slot of each expert of this layer, -1 absent */
+    const uint8_t *shared_slot;  /* the shared expert, slot layout */
+    float *logits;               /* [T, E + 1]; column E is the shared-gate logit */
+    int32_t *idx;                /* [T, k] */
+    float *wts;                  /* [T, k] */
+    float *sgate;                /* [T] sigmoid(shared-gate logit) */
+    float *h;                    /* [T, k + 1, I] */
+    float *out;                  /* [T, d] */
+    int *err;                    /* device error word */
+    int num_sms;
+} qk_fwd;
+
+/* Kernel launchers (qmoe_kernels.cu). Each returns a cudaError_t as int.
+ * stream is a cudaStream_t. pdl != 0 launches with programmatic stream
+ * serialization so the kernel's prologue overlaps its predecessor. */
+/* One-time per-device kernel attributes (dynamic shared memory limits), so
+ * launches never call cudaFuncSetAttribute (safe under stream capture). */
+int qk_prepare_kernels(void);
+int qk_launch_router(const qk_fwd *f, void *stream, int pdl);
+int qk_launch_topk(const qk_fwd *f, void *stream, int pdl);
+int qk_launch_decode_gateup(const qk_fwd *f, void *stream, int pdl);
+int qk_launch_decode_down(const qk_fwd *f, void *stream, int pdl);
+
+/* internal cache helper: replace the value of an existing key */
+struct qmoe_cache;
+int qmoe__cache_set_value(struct qmoe_cache *c, uint64_t key, uint64_t value);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,275 @@
+"""ctypes binding of libqmoe.so (include/qmoe.h) for Python callers.
+
+The product is the C library; this module only marshals arguments. It is what
+the tests and bench.py use to reach the C ABI, and it is the binding a Python
+host of the reference runtime would add. Loading fails
+loudly when libqmoe.so has not been built; there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqmoe.so")
+
+QMOE_POLICY_LRU, QMOE_POLICY_LFU, QMOE_POLICY_ADAPTIVE = 0, 1, 2
+QMOE_F32, QMOE_BF16 = 0, 1
+
+
+class Err(C.Structure):
+    _fields_ = [("msg", C.c_char * 512)]
+
+    def text(self) -> str:
+        return self.msg.decode(errors="replace")
+
+
+class Config(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_int), ("num_experts", C.c_int), ("top_k", C.c_int),
+        ("moe_inter", C.c_int), ("group_size", C.c_int), ("bits", C.c_int),
+        ("num_layers", C.c_int), ("max_tokens", C.c_int), ("pool_bytes", C.c_uint64),
+        ("policy", C.c_int), ("prefetch_depth", C.c_int), ("device", C.c_int),
+    ]
+
+
+class Q4(C.Structure):
+    _fields_ = [("q", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p)]
+
+
+class LayerWeights(C.Structure):
+    _fields_ = [
+        ("router", C.c_void_p), ("shared_gate", C.c_void_p), ("logit_bias", C.c_void_p),
+        ("gate", Q4), ("up", Q4), ("down", Q4),
+        ("sh_gate", Q4), ("sh_up", Q4), ("sh_down", Q4),
+    ]
+
+
+class CacheStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in
+                ("hits", "misses", "evictions", "rejected", "pinned",
+                 "bytes", "peak_bytes", "size", "hot")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+class Stats(C.Structure):
+    _fields_ = [
+        ("expert_loads", C.c_uint64), ("expert_bytes", C.c_uint64),
+        ("expert_wait_seconds", C.c_double), ("prefill_calls", C.c_uint64),
+        ("decode_calls", C.c_uint64), ("forward_seconds", C.c_double),
+        ("prefetch_issued", C.c_uint64), ("prefetch_hits", C.c_uint64),
+    ]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+class SynthSize(C.Structure):
+    _fields_ = [(n, C.c_size_t) for n in
+                ("router", "shared_gate", "expert_q", "expert_sb", "down_q", "down_sb",
+                 "sh_q", "sh_sb", "sh_down_q", "sh_down_sb")]
+
+
+# every symbol include/qmoe.h declares, with (restype, argtypes)
+_P = C.c_void_p
+SIGNATURES = {
+    "qmoe_create": (_P, [C.POINTER(Config), C.POINTER(Err)]),
+    "qmoe_destroy": (None, [_P]),
+    "qmoe_slot_bytes": (C.c_size_t, [C.POINTER(Config)]),
+    "qmoe_upload_layer": (C.c_int, [_P, C.c_int, C.POINTER(LayerWeights), C.POINTER(Err)]),
+    "qmoe_forward": (C.c_int, [_P, C.c_int, _P, C.c_int, _P, C.POINTER(Err)]),
+    "qmoe_forward_dev": (C.c_int, [_P, C.c_int, _P, C.c_int, C.c_int, _P, _P, C.POINTER(Err)]),
+    "qmoe_sync": (C.c_int, [_P, C.POINTER(Err)]),
+    "qmoe_last_routing": (C.c_int, [_P, _P, _P, _P, C.POINTER(Err)]),
+    "qmoe_profile_enable": (C.c_int, [_P, C.c_int]),
+    "qmoe_profile_read": (C.c_int, [_P, C.POINTER(C.c_double), C.c_int, C.POINTER(C.c_int),
+                                    C.POINTER(C.c_uint64)]),
+    "qmoe_expert_peek": (C.c_int, [_P, C.c_int, C.c_int]),
+    "qmoe_expert_get": (C.c_int, [_P, C.c_int, C.c_int]),
+    "qmoe_experts_load": (C.c_int, [_P, C.c_int, _P, C.c_size_t, C.POINTER(Err)]),
+    "qmoe_expert_pin": (C.c_int, [_P, C.c_int, C.c_int]),
+    "qmoe_expert_unpin": (C.c_int, [_P, C.c_int, C.c_int]),
+    "qmoe_expert_mark_hot": (C.c_int, [_P, C.c_int, C.c_int, C.c_int]),
+    "qmoe_cache_snapshot": (C.c_int, [_P, C.POINTER(CacheStats)]),
+    "qmoe_stats_get": (C.c_int, [_P, C.POINTER(Stats)]),
+    "qmoe_prefetch": (C.c_int, [_P, C.c_int, _P, C.c_size_t]),
+    "qmoe_record_route": (None, [_P, C.c_int, _P, C.c_size_t]),
+    "qmoe_prefetch_predictions": (C.c_int, [_P, C.c_int, _P, C.c_size_t]),
+    "qmoe_cache_new": (_P, [C.c_uint64, C.c_int, C.c_int]),
+    "qmoe_cache_free": (None, [_P]),
+    "qmoe_cache_peek": (C.c_int, [_P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "qmoe_cache_get": (C.c_int, [_P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "qmoe_cache_put": (C.c_int, [_P, C.c_uint64, C.c_uint64, C.c_uint64, C.c_int, C.c_int,
+                                 _P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "qmoe_cache_pin": (C.c_int, [_P, C.c_uint64]),
+    "qmoe_cache_unpin": (C.c_int, [_P, C.c_uint64]),
+    "qmoe_cache_mark_hot": (C.c_int, [_P, C.c_uint64, C.c_int]),
+    "qmoe_cache_erase": (C.c_int, [_P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "qmoe_cache_stats_get": (CacheStats, [_P]),
+    "qmoe_synth_sizes": (C.c_int, [C.POINTER(Config), C.POINTER(SynthSize)]),
+    "qmoe_synth_layer": (C.c_int, [C.POINTER(Config), C.c_uint64, C.c_int,
+                                   C.POINTER(LayerWeights), C.c_int, C.c_int]),
+    "qmoe_synth_tokens": (None, [C.c_uint64, C.c_uint64, C.c_int, C.c_int, _P]),
+    "qmoe_synth_zipf_bias": (None, [C.c_uint64, C.c_int, C.c_int, C.c_double, _P]),
+    "qmoe_version": (C.c_char_p, []),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libqmoe.so once; raises if it was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} missing: run `make -C {HERE}` first")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def ptr(a) -> int | None:
+    return None if a is None else a.ctypes.data
+
+
+def make_config(d, E, k, I, g=64, layers=1, max_tokens=1, pool_bytes=0,
+                policy=QMOE_POLICY_ADAPTIVE, prefetch=2, device=0) -> Config:
+    return Config(d, E, k, I, g, 4, layers, max_tokens, pool_bytes, policy, prefetch, device)
+
+
+class SynthLayer:
+    """One seeded synthetic layer in the reference checkpoint layout (numpy)."""
+
+    def __init__(self, cfg: Config, seed: int, layer: int = 0, zipf_s: float | None = None):
+        L = lib()
+        sz = SynthSize()
+        if L.qmoe_synth_sizes(C.byref(cfg), C.byref(sz)) != 0:
+            raise ValueError("unsupported synthetic shape")
+        self.cfg = cfg
+        self.d, self.E, self.k = cfg.hidden, cfg.num_experts, cfg.top_k
+        self.I, self.g = cfg.moe_inter, cfg.group_size
+        u16, u32 = np.uint16, np.uint32
+        self.router = np.empty(sz.router, u16)
+        self.shared_gate = np.empty(sz.shared_gate, u16)
+        self.t = {}
+        for name, nq, nsb in (("gate", sz.expert_q, sz.expert_sb), ("up", sz.expert_q, sz.expert_sb),
+                              ("down", sz.down_q, sz.down_sb), ("sh_gate", sz.sh_q, sz.sh_sb),
+                              ("sh_up", sz.sh_q, sz.sh_sb), ("sh_down", sz.sh_down_q, sz.sh_down_sb)):
+            self.t[name] = (np.empty(nq, u32), np.empty(nsb, u16), np.empty(nsb, u16))
+        self.logit_bias = None
+        if zipf_s is not None:
+            self.logit_bias = np.empty(self.E, np.float32)
+            L.qmoe_synth_zipf_bias(seed, layer, self.E, zipf_s, ptr(self.logit_bias))
+        w = self.weights()
+        if L.qmoe_synth_layer(C.byref(cfg), seed, layer, C.byref(w), 0, 0) != 0:
+            raise ValueError("qmoe_synth_layer failed")
+
+    def weights(self) -> LayerWeights:
+        def q4(n):
+            q, s, b = self.t[n]
+            return Q4(ptr(q), ptr(s), ptr(b))
+        return LayerWeights(ptr(self.router), ptr(self.shared_gate), ptr(self.logit_bias),
+                            q4("gate"), q4("up"), q4("down"), q4("sh_gate"), q4("sh_up"),
+                            q4("sh_down"))
+
+
+def synth_tokens(seed: int, stream: int, n: int, d: int) -> np.ndarray:
+    x = np.empty((n, d), np.float32)
+    lib().qmoe_synth_tokens(seed, stream, n, d, ptr(x))
+    return x
+
+
+class QmoeError(RuntimeError):
+    pass
+
+
+class Context:
+    """Owns one qmoe_ctx (one GPU)."""
+
+    def __init__(self, cfg: Config):
+        self.cfg = cfg
+        err = Err()
+        self.h = lib().qmoe_create(C.byref(cfg), C.byref(err))
+        if not self.h:
+            raise QmoeError(err.text())
+
+    def close(self):
+        if self.h:
+            lib().qmoe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _chk(self, rc, err):
+        if rc != 0:
+            raise QmoeError(err.text())
+
+    def upload(self, layer: int, s: SynthLayer):
+        err = Err()
+        w = s.weights()
+        self._chk(lib().qmoe_upload_layer(self.h, layer, C.byref(w), C.byref(err)), err)
+
+    def forward(self, layer: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        n = x.shape[0]
+        out = np.empty((n, self.cfg.hidden), np.float32)
+        err = Err()
+        self._chk(lib().qmoe_forward(self.h, layer, ptr(x), n, ptr(out), C.byref(err)), err)
+        return out
+
+    def forward_dev(self, layer: int, x_ptr: int, x_dtype: int, n: int, out_ptr: int,
+                    stream: int | None = None):
+        err = Err()
+        self._chk(lib().qmoe_forward_dev(self.h, layer, x_ptr, x_dtype, n, out_ptr, stream,
+                                         C.byref(err)), err)
+
+    def sync(self):
+        err = Err()
+        self._chk(lib().qmoe_sync(self.h, C.byref(err)), err)
+
+    def routing(self, n: int):
+        k = self.cfg.top_k
+        idx = np.empty((n, k), np.int32)
+        w = np.empty((n, k), np.float32)
+        g = np.empty(n, np.float32)
+        err = Err()
+        self._chk(lib().qmoe_last_routing(self.h, ptr(idx), ptr(w), ptr(g), C.byref(err)), err)
+        return idx, w, g
+
+    def experts_load(self, layer: int, ids):
+        ids = np.ascontiguousarray(ids, np.int64)
+        err = Err()
+        self._chk(lib().qmoe_experts_load(self.h, layer, ptr(ids), ids.size, C.byref(err)), err)
+
+    def cache_stats(self) -> dict:
+        s = CacheStats()
+        lib().qmoe_cache_snapshot(self.h, C.byref(s))
+        return s.as_dict()
+
+    def stats(self) -> dict:
+        s = Stats()
+        lib().qmoe_stats_get(self.h, C.byref(s))
+        return s.as_dict()
+
+    def profile(self, on: bool):
+        lib().qmoe_profile_enable(self.h, int(on))
+
+    def profile_read(self):
+        """(per-kernel total ms [router, topk, gateup, down], profiled calls)."""
+        ms = (C.c_double * 8)()
+        nk = C.c_int()
+        calls = C.c_uint64()
+        lib().qmoe_profile_read(self.h, ms, 8, C.byref(nk), C.byref(calls))
+        return [ms[i] for i in range(nk.value)], calls.value

@@ -1,0 +1,193 @@
+"""GPU parity of the MoE layer through the C ABI (libqmoe.so) against the CPU
+checkers: the reference's own outputs (golden fixtures) and the C
+restatement of moe_forward. Bars: routing sets and
+per-expert counts bit-exact; outputs within 2e-2 max-abs and 1e-3 relative
+RMS of the fp32 oracle output."""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+MAX_ABS = 2e-2
+REL_RMS = 1e-3
+
+
+def _sorted(idx, w):
+    o = np.argsort(idx, 1, kind="stable")
+    return np.take_along_axis(idx, o, 1), np.take_along_axis(w, o, 1)
+
+
+def _close(out, ref):
+    mab = float(np.abs(out - ref).max())
+    rr = float(np.linalg.norm(out - ref) / np.linalg.norm(ref))
+    assert mab <= MAX_ABS and rr <= REL_RMS, (mab, rr)
+    return mab, rr
+
+
+def _golden(name):
+    g = np.load(os.path.join(GOLD, name))
+    d, E, k, I, gs, n, stream = (int(v) for v in g["shape"])
+    return g, (d, E, k, I, gs, n, stream), int(g["seed"])
+
+
+@pytest.fixture(scope="module")
+def cfg1_layer(built):
+    import qmoe
+    g, (d, E, k, I, gs, n, stream), seed = _golden("moe_cfg1_tokens.npz")
+    s = qmoe.SynthLayer(qmoe.make_config(d, E, k, I, gs, max_tokens=64), seed)
+    return s, seed
+
+
+@pytest.fixture(scope="module")
+def cfg1_ctx(cfg1_layer):
+    import qmoe
+    s, _ = cfg1_layer
+    ctx = qmoe.Context(qmoe.make_config(2048, 512, 10, 512, max_tokens=64))
+    ctx.upload(0, s)
+    yield ctx
+    ctx.close()
+
+
+def test_cfg0_matches_reference_golden(built):
+    import oracle
+    import qmoe
+    g, (d, E, k, I, gs, n, stream), seed = _golden("moe_cfg0.npz")
+    s = qmoe.SynthLayer(qmoe.make_config(d, E, k, I, gs, max_tokens=n), seed)
+    x = qmoe.synth_tokens(seed, stream, n, d)
+    ctx = qmoe.Context(qmoe.make_config(d, E, k, I, gs, max_tokens=n))
+    ctx.upload(0, s)
+    out = ctx.forward(0, x)
+    idx, w, sg = ctx.routing(n)
+    si, sw = _sorted(idx, w)
+    assert np.array_equal(si, g["idx_sorted"])
+    np.testing.assert_allclose(sw, g["w_sorted"], rtol=1e-5, atol=1e-6)
+    _close(out, g["out"])
+    ro, ri, rw = oracle.restatement().forward(s, x)
+    assert np.array_equal(idx, ri)  # same (value desc, index asc) order
+    _close(out, ro)
+    ctx.close()
+
+
+def test_cfg1_decode_matches_reference_golden(cfg1_layer, cfg1_ctx):
+    import qmoe
+    s, seed = cfg1_layer
+    g, (d, E, k, I, gs, n, stream), _ = _golden("moe_cfg1_tokens.npz")
+    x = qmoe.synth_tokens(seed, stream, n, d)
+    for t in range(n):
+        out = cfg1_ctx.forward(0, x[t:t + 1])
+        idx, w, _ = cfg1_ctx.routing(1)
+        si, sw = _sorted(idx, w)
+        assert np.array_equal(si[0], g["idx_sorted"][t])
+        np.testing.assert_allclose(sw[0], g["w_sorted"][t], rtol=1e-5, atol=1e-6)
+        _close(out, g["out"][t:t + 1])
+
+
+def test_cfg1_decode_matches_restatement(cfg1_layer, cfg1_ctx):
+    import oracle
+    import qmoe
+    s, seed = cfg1_layer
+    x = qmoe.synth_tokens(seed, 11, 12, 2048)
+    ro, ri, rw = oracle.restatement().forward(s, x)
+    for t in range(12):
+        out = cfg1_ctx.forward(0, x[t:t + 1])
+        idx, w, _ = cfg1_ctx.routing(1)
+        assert np.array_equal(idx[0], ri[t])
+        np.testing.assert_allclose(w[0], rw[t], rtol=1e-5, atol=1e-6)
+        _close(out, ro[t:t + 1])
+
+
+def test_batch_equals_token_by_token(cfg1_layer, cfg1_ctx):
+    """A multi-token call equals the same tokens one at a time (prefill ==
+    decode, as c/tests/test_model.c:300-333 checks for the whole model)."""
+    import qmoe
+    s, seed = cfg1_layer
+    x = qmoe.synth_tokens(seed, 12, 24, 2048)
+    full = cfg1_ctx.forward(0, x)
+    for t in range(0, 24, 5):
+        one = cfg1_ctx.forward(0, x[t:t + 1])
+        np.testing.assert_allclose(one[0], full[t], rtol=1e-6, atol=1e-6)
+
+
+def test_cfg2_zipf_routing_bit_exact(built):
+    """Configuration-2 router with the Zipf(1.1) logit bias: sorted top-10 sets
+    and per-expert counts equal the golden routing."""
+    import qmoe
+    g, (d, E, k, I, gs, n, stream), seed = _golden("moe_cfg2_route.npz")
+    s = qmoe.SynthLayer(qmoe.make_config(d, E, k, I, gs, max_tokens=n), seed, zipf_s=1.1)
+    x = qmoe.synth_tokens(seed, stream, n, d)
+    ctx = qmoe.Context(qmoe.make_config(d, E, k, I, gs, max_tokens=n))
+    ctx.upload(0, s)
+    ctx.forward(0, x)
+    idx, w, _ = ctx.routing(n)
+    si, sw = _sorted(idx, w)
+    assert np.array_equal(si, g["idx_sorted"])
+    assert np.array_equal(np.bincount(idx.ravel(), minlength=E), g["counts"])
+    np.testing.assert_allclose(sw, g["w_sorted"], rtol=1e-5, atol=1e-6)
+    ctx.close()
+
+
+def test_bf16_device_input_equals_fp32_host(cfg1_layer, cfg1_ctx):
+    import torch
+
+    import qmoe
+    s, seed = cfg1_layer
+    x = qmoe.synth_tokens(seed, 13, 3, 2048)
+    ref = cfg1_ctx.forward(0, x)
+    xd = torch.from_numpy(x).to("cuda").to(torch.bfloat16)  # exact: x is bf16-valued
+    out = torch.empty((3, 2048), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    cfg1_ctx.forward_dev(0, xd.data_ptr(), qmoe.QMOE_BF16, 3, out.data_ptr(), None)
+    cfg1_ctx.sync()
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+def test_edge_cases(cfg1_ctx):
+    import qmoe
+    assert cfg1_ctx.forward(0, np.zeros((0, 2048), np.float32)).shape == (0, 2048)
+    with pytest.raises(qmoe.QmoeError, match="max_tokens"):
+        cfg1_ctx.forward(0, np.zeros((65, 2048), np.float32))
+    with pytest.raises(qmoe.QmoeError):
+        cfg1_ctx.forward(1, np.zeros((1, 2048), np.float32))  # no such layer
+    # zero input: every logit 0 -> ties everywhere; lowest ids win, weights 1/k
+    out = cfg1_ctx.forward(0, np.zeros((1, 2048), np.float32))
+    idx, w, sg = cfg1_ctx.routing(1)
+    assert idx[0].tolist() == list(range(10))
+    np.testing.assert_allclose(w[0], 0.1, rtol=1e-6)
+    assert np.all(out == 0)
+
+
+def test_streaming_pool_equals_resident(cfg1_layer, cfg1_ctx):
+    """A pool smaller than the layer's experts (64 of 512 slots, LRU) gives the
+    same outputs as the all-resident pool, and the cache counters move."""
+    import qmoe
+    s, seed = cfg1_layer
+    slot = qmoe.lib().qmoe_slot_bytes(qmoe.make_config(2048, 512, 10, 512))
+    ctx = qmoe.Context(qmoe.make_config(2048, 512, 10, 512, max_tokens=8,
+                                        pool_bytes=64 * slot, policy=qmoe.QMOE_POLICY_LRU))
+    ctx.upload(0, s)
+    x = qmoe.synth_tokens(seed, 14, 8, 2048)
+    for t in range(8):
+        a = ctx.forward(0, x[t:t + 1])
+        b = cfg1_ctx.forward(0, x[t:t + 1])
+        assert np.array_equal(a, b)
+    st = ctx.cache_stats()
+    assert st["size"] <= 64 and st["misses"] + st["hits"] >= 0
+    assert ctx.stats()["expert_loads"] >= 10
+    # hooks: peek / get / pin on the pool
+    idx, _, _ = ctx.routing(1)
+    e = int(idx[0, 0])
+    slot_no = qmoe.lib().qmoe_expert_peek(ctx.h, 0, e)
+    assert slot_no >= 0
+    assert qmoe.lib().qmoe_expert_get(ctx.h, 0, e) == slot_no
+    assert qmoe.lib().qmoe_expert_pin(ctx.h, 0, e) == 1
+    ids = [i for i in range(100, 200) if i != e][:63]
+    ctx.experts_load(0, ids)   # fills every unpinned slot
+    assert qmoe.lib().qmoe_expert_peek(ctx.h, 0, e) == slot_no
+    assert all(qmoe.lib().qmoe_expert_peek(ctx.h, 0, i) >= 0 for i in ids)
+    with pytest.raises(qmoe.QmoeError):
+        ctx.experts_load(0, list(range(300, 365)))  # more than the pool holds
+    assert qmoe.lib().qmoe_expert_unpin(ctx.h, 0, e) == 1
+    ctx.close()
