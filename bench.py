@@ -63,6 +63,7 @@ def kernel_bytes_per_token():
     """Algorithmic bytes one launch moves at T=1, per kernel."""
     gu_row, d_row = D + (D // G) * 8, I_DIM // 2 + (I_DIM // G) * 4
     return {
+        "decode_fused": layer_bytes_per_token(),
         "router": E * D * 2 + D * 2 + D * 2 + (E + 1) * 4,
         "topk": (E + 1) * 4 + K_TOP * 8 + 4,
         "decode_gateup": (K_TOP + 1) * I_DIM * gu_row + D * 2 + (K_TOP + 1) * I_DIM * 4 + K_TOP * 4,
@@ -227,7 +228,7 @@ def main():
         if world > 1:
             dist.barrier()
 
-    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=1, device=local)
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=4, device=local)
     layer = qmoe.SynthLayer(cfg, SEED)
     ctx = qmoe.Context(cfg)
     ctx.upload(0, layer)
@@ -235,23 +236,25 @@ def main():
     x_dev = torch.from_numpy(x_host).cuda().to(torch.bfloat16).contiguous()
     out_dev = torch.empty((TOKENS, D), dtype=torch.float32, device="cuda")
 
-    # one step = 1000 sequential single-token calls, captured once as a graph
+    # one step = 1000 sequential single-token calls, captured once as a CUDA
+    # graph by the library (qmoe_capture_begin/end) on a torch-owned stream
     stream = torch.cuda.Stream()
+    cs = stream.cuda_stream
     xs, os_ = x_dev.data_ptr(), out_dev.data_ptr()
-    with torch.cuda.stream(stream):
-        for t in range(4):  # eager warm-up outside capture
-            ctx.forward_dev(0, xs + t * D * 2, qmoe.QMOE_BF16, 1, os_ + t * D * 4,
-                            stream.cuda_stream)
+    torch.cuda.synchronize()
+    for t in range(4):  # eager warm-up outside capture
+        ctx.forward_dev(0, xs + t * D * 2, qmoe.QMOE_BF16, 1, os_ + t * D * 4, cs)
     stream.synchronize()
     ctx.sync()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
-        cs = torch.cuda.current_stream().cuda_stream
-        for t in range(TOKENS):
-            ctx.forward_dev(0, xs + t * D * 2, qmoe.QMOE_BF16, 1, os_ + t * D * 4, cs)
-    for _ in range(args.warmup):
-        graph.replay()
+    out_dev.zero_()
     torch.cuda.synchronize()
+    ctx.capture_begin(cs)
+    for t in range(TOKENS):
+        ctx.forward_dev(0, xs + t * D * 2, qmoe.QMOE_BF16, 1, os_ + t * D * 4, cs)
+    graph = ctx.capture_end(cs)
+    for _ in range(args.warmup):
+        graph.launch(cs)
+    stream.synchronize()
     ctx.sync()
 
     clocks = Clocks(local) if rank == 0 else None
@@ -260,7 +263,7 @@ def main():
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):
-        graph.replay()
+        graph.launch(cs)
     ev1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -273,9 +276,10 @@ def main():
         ms = float(tt.item())
     value = world * args.steps * TOKENS / (ms / 1e3)
 
-    # parity spot check of the timed outputs (token 0..3 of the last replay)
-    out_last = out_dev[:4].cpu().numpy()
-    ref4 = ctx.forward(0, x_host[:4])  # host path, token-by-token in one call
+    # parity spot check of the timed outputs (tokens 996..999 of the last
+    # replay; out_dev was zeroed before capture, so these come from the graph)
+    out_last = out_dev[TOKENS - 4:].cpu().numpy()
+    ref4 = ctx.forward(0, x_host[TOKENS - 4:])
     parity_ok = bool(np.allclose(out_last, ref4, rtol=1e-5, atol=1e-5))
 
     # e2e through the host-pointer C ABI: copies in and out on every call
@@ -295,15 +299,21 @@ def main():
         e2e_s = float(tt.item())
     e2e = world * e2e_steps * TOKENS / e2e_s
 
-    # per-kernel event timing (separate pass) -> roofline of the dominant kernel
-    ctx.profile(True)
-    nprof = 200
+    # per-kernel event timing (separate pass, one token replayed as a graph
+    # with events between its kernels) -> roofline of the dominant kernel
+    # distinct tokens, L2 flushed (256 MB write) before each, as in the timed loop
+    acc = None
+    nprof = 48
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
     for t in range(nprof):
-        ctx.forward_dev(0, xs + t * D * 2, qmoe.QMOE_BF16, 1, os_ + t * D * 4, None)
-    kms, calls = ctx.profile_read()
-    ctx.profile(False)
-    names = ["router", "topk", "decode_gateup", "decode_down"]
-    per_launch_ms = {n: kms[i] / calls for i, n in enumerate(names)}
+        flush.fill_(float(t))
+        torch.cuda.synchronize()
+        us = ctx.profile_forward(0, xs + t * D * 2, qmoe.QMOE_BF16, 1, os_ + t * D * 4, 1)
+        acc = np.array(us) if acc is None else acc + np.array(us)
+    del flush
+    names = (["decode_fused"] if len(acc) == 1 else
+             ["router", "topk", "decode_gateup", "decode_down"])
+    per_launch_ms = {n: acc[i] / nprof / 1e3 for i, n in enumerate(names)}
     dom = max(per_launch_ms, key=per_launch_ms.get)
     kb = kernel_bytes_per_token()
     hbm, _, src = peaks()
@@ -339,7 +349,7 @@ def main():
                              "router and shared expert (3.9 MB) stay L2-resident across tokens"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": TOKENS * D * 4,
                     "d2h_bytes_per_step": TOKENS * D * 4},
-            "gpu_launches": 4 * TOKENS * args.steps,
+            "gpu_launches": len(names) * TOKENS * args.steps,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
                          "peak_source": src,

@@ -134,16 +134,29 @@ int qmoe_sync(qmoe_ctx *ctx, qmoe_err *err);
 int qmoe_last_routing(qmoe_ctx *ctx, int32_t *idx, float *weights,
                       float *shared_gate, qmoe_err *err);
 
+/* ---- CUDA graphs of forward calls (no reference counterpart: the
+ *      reference runs eagerly on the CPU) ----
+ * qmoe_capture_begin starts capturing the qmoe_forward_dev calls issued on
+ * `stream` (NULL = the context's stream) into a CUDA graph; qmoe_capture_end
+ * instantiates it. Only contexts whose experts are all resident can be
+ * captured (streaming forwards wait on the host). Replaying the graph with
+ * qmoe_graph_launch reruns the captured calls with the same pointers. */
+typedef struct qmoe_graph qmoe_graph;
+int qmoe_capture_begin(qmoe_ctx *ctx, void *stream, qmoe_err *err);
+qmoe_graph *qmoe_capture_end(qmoe_ctx *ctx, void *stream, qmoe_err *err);
+int qmoe_graph_launch(qmoe_graph *g, void *stream, qmoe_err *err);
+void qmoe_graph_free(qmoe_graph *g);
+
 /* ---- diagnostics (no reference counterpart; the reference's qstats only
  *      time whole forwards, c/src/model.c:1756-1761) ----
- * While enabled, each forward brackets its kernels with CUDA events on its
- * stream and waits for them, accumulating per-kernel device time.
- * qmoe_profile_read returns the totals in milliseconds, in launch order
- * (router, top-k, gate/up, down), the number of kernels per call and the
- * number of profiled calls; it also resets them. */
-int qmoe_profile_enable(qmoe_ctx *ctx, int on);
-int qmoe_profile_read(qmoe_ctx *ctx, double *kernel_ms, int max_kernels,
-                      int *kernels_per_call, uint64_t *calls);
+ * Captures one forward of n tokens with CUDA events between its kernels,
+ * replays it `reps` times and returns the mean device time of each kernel
+ * launch in microseconds, in launch order (router, top-k, gate/up, down);
+ * *kernels receives the count. Kernels run back to back without
+ * programmatic overlap while profiled. Resident contexts only. */
+int qmoe_profile_forward(qmoe_ctx *ctx, int layer, const void *x, int x_dtype,
+                         int n, float *out, int reps, double *kernel_us,
+                         int max_kernels, int *kernels, qmoe_err *err);
 
 /* ---- expert cache hooks (cache.h:38-53 keyed (layer << 32) | expert,
  *      model.c:594) ---- */

@@ -44,6 +44,7 @@ struct qmoe_ctx {
     cudaEvent_t copy_done;
     int *err_dev;
     int *err_host; /* pinned */
+    unsigned *gbar; /* grid-barrier words of the single-launch decode kernel */
     layer_dev *layers;
     /* expert pool */
     uint8_t *pool;
@@ -68,14 +69,14 @@ struct qmoe_ctx {
     uint32_t *trans;       /* [num_layers * E * E], lazily allocated */
     int32_t *recent;       /* [num_layers * k] last selection per layer */
     int *recent_n;
-    /* diagnostics: per-kernel event timing */
+    /* diagnostics: per-kernel event timing (qmoe_profile_forward) */
     int profile;
+    int prof_kernels; /* kernels of the last forward: 1 (single launch) or 4 */
     cudaEvent_t pev[8];
-    double prof_ms[8];
-    int prof_kernels;
-    uint64_t prof_calls;
     pthread_mutex_t lock;
 };
+
+static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err);
 
 static void seterr(qmoe_err *err, const char *fmt, ...) {
     if (!err) return;
@@ -189,6 +190,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     cudaFree(c->pool);
     cudaFree(c->slot_of_dev);
     cudaFree(c->err_dev);
+    cudaFree(c->gbar);
     cudaFree(c->x_dev);
     cudaFree(c->out_dev);
     cudaFree(c->logits);
@@ -270,6 +272,8 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaMalloc((void **)&c->err_dev, sizeof(int)));
     CK(cudaMemset(c->err_dev, 0, sizeof(int)));
     CK(cudaMallocHost((void **)&c->err_host, sizeof(int)));
+    CK(cudaMalloc((void **)&c->gbar, 2 * sizeof(unsigned)));
+    CK(cudaMemset(c->gbar, 0, 2 * sizeof(unsigned)));
     c->layers = calloc((size_t)Lz, sizeof(layer_dev));
     if (!c->layers) {
         seterr(err, "qmoe_create: out of host memory");
@@ -667,53 +671,170 @@ int qmoe_forward_dev(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, 
     c->last_T = n;
     if (n == 1) c->stats.decode_calls++;
     else c->stats.prefill_calls++;
+    /* profiling (inside a capture): external event records between kernels,
+     * so they are real timestamps in the graph; no programmatic overlap */
     const int prof = c->profile;
+#define PEV(i) \
+    if (prof) cudaEventRecordWithFlags(c->pev[i], st, cudaEventRecordExternal)
+    if (c->resident_all && n == 1) {
+        /* one persistent launch for the whole layer */
+        PEV(0);
+        int rc = qk_launch_decode_fused(&f, c->gbar, st, !prof);
+        if (rc == 0) {
+            PEV(1);
+            c->prof_kernels = 1;
+            return 0;
+        }
+        if (rc != QK_FUSED_UNFIT) return kerr(rc, "decode_fused", err);
+    }
+    c->prof_kernels = 4;
     if (!c->resident_all) {
         if (stream_in(c, layer, &f, st, err)) return -1;
-        if (prof) cudaEventRecord(c->pev[2], st);
     } else {
-        if (prof) cudaEventRecord(c->pev[0], st);
+        PEV(0);
         if (kerr(qk_launch_router(&f, st, !prof), "router", err)) return -1;
-        if (prof) cudaEventRecord(c->pev[1], st);
+        PEV(1);
         if (kerr(qk_launch_topk(&f, st, !prof), "topk", err)) return -1;
-        if (prof) cudaEventRecord(c->pev[2], st);
+        PEV(2);
     }
     if (kerr(qk_launch_decode_gateup(&f, st, !prof), "decode_gateup", err)) return -1;
-    if (prof) cudaEventRecord(c->pev[3], st);
+    PEV(3);
     if (kerr(qk_launch_decode_down(&f, st, !prof), "decode_down", err)) return -1;
-    if (prof) {
-        cudaEventRecord(c->pev[4], st);
-        cudaError_t ce = cudaEventSynchronize(c->pev[4]);
-        if (ce != cudaSuccess) {
-            seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
-            return -1;
-        }
-        for (int i = c->resident_all ? 0 : 2; i < 4; i++) {
-            float ms = 0.f;
-            cudaEventElapsedTime(&ms, c->pev[i], c->pev[i + 1]);
-            c->prof_ms[i] += ms;
-        }
-        c->prof_kernels = 4;
-        c->prof_calls++;
+    PEV(4);
+#undef PEV
+    return 0;
+}
+
+/* ------------------------------------------------------------- graphs */
+
+struct qmoe_graph {
+    cudaGraphExec_t exec;
+    cudaStream_t stream;
+};
+
+int qmoe_capture_begin(qmoe_ctx *c, void *stream, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || !c->resident_all) {
+        seterr(err, "qmoe_capture_begin: needs a context with every expert resident");
+        return -1;
+    }
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    cudaError_t ce = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_capture_begin: %s", cudaGetErrorString(ce));
+        return -1;
     }
     return 0;
 }
 
-int qmoe_profile_enable(qmoe_ctx *c, int on) {
-    if (!c) return -1;
-    c->profile = on != 0;
+qmoe_graph *qmoe_capture_end(qmoe_ctx *c, void *stream, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c) return NULL;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    cudaGraph_t g = NULL;
+    cudaError_t ce = cudaStreamEndCapture(st, &g);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_capture_end: %s", cudaGetErrorString(ce));
+        return NULL;
+    }
+    qmoe_graph *q = calloc(1, sizeof(*q));
+    if (!q) {
+        cudaGraphDestroy(g);
+        seterr(err, "qmoe_capture_end: out of host memory");
+        return NULL;
+    }
+    ce = cudaGraphInstantiate(&q->exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) {
+        free(q);
+        seterr(err, "qmoe_capture_end: instantiate: %s", cudaGetErrorString(ce));
+        return NULL;
+    }
+    q->stream = st;
+    return q;
+}
+
+int qmoe_graph_launch(qmoe_graph *g, void *stream, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!g) return -1;
+    cudaError_t ce = cudaGraphLaunch(g->exec, stream ? (cudaStream_t)stream : g->stream);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_graph_launch: %s", cudaGetErrorString(ce));
+        return -1;
+    }
     return 0;
 }
 
-int qmoe_profile_read(qmoe_ctx *c, double *kernel_ms, int max_kernels, int *kernels_per_call,
-                      uint64_t *calls) {
-    if (!c) return -1;
-    for (int i = 0; i < max_kernels && i < 8; i++) kernel_ms[i] = c->prof_ms[i];
-    if (kernels_per_call) *kernels_per_call = c->prof_kernels;
-    if (calls) *calls = c->prof_calls;
-    memset(c->prof_ms, 0, sizeof(c->prof_ms));
-    c->prof_calls = 0;
-    return 0;
+void qmoe_graph_free(qmoe_graph *g) {
+    if (!g) return;
+    cudaGraphExecDestroy(g->exec);
+    free(g);
+}
+
+/* Diagnostics (not in the public header): one single-token forward through the
+ * single-launch kernel with per-CTA phase timestamps; out_ns receives
+ * [grid][16] %globaltimer values. Returns the grid size, or -1. */
+int qmoe__phase_times(qmoe_ctx *c, int layer, const void *x, int x_dtype, float *out,
+                      unsigned long long *out_ns, int max_ctas) {
+    if (!c || !c->resident_all || !c->layers[layer].ready) return -1;
+    unsigned long long *buf = NULL;
+    size_t bytes = (size_t)c->num_sms * 16 * sizeof(unsigned long long);
+    if (cudaMalloc((void **)&buf, bytes) != cudaSuccess) return -1;
+    cudaMemset(buf, 0, bytes);
+    qk_fwd f;
+    fill_fwd(c, layer, x, x_dtype == QMOE_BF16, 1, out, &f);
+    f.ptimes = buf;
+    int rc = qk_launch_decode_fused(&f, c->gbar, c->stream, 0);
+    if (rc == 0) rc = cudaStreamSynchronize(c->stream);
+    if (rc == 0) {
+        int n = max_ctas < c->num_sms ? max_ctas : c->num_sms;
+        rc = cudaMemcpy(out_ns, buf, (size_t)n * 16 * sizeof(unsigned long long),
+                        cudaMemcpyDeviceToHost);
+    }
+    cudaFree(buf);
+    return rc == 0 ? c->num_sms : -1;
+}
+
+int qmoe_profile_forward(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, float *out,
+                         int reps, double *kernel_us, int max_kernels, int *kernels,
+                         qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || reps < 1 || !kernel_us) {
+        seterr(err, "qmoe_profile_forward: bad arguments");
+        return -1;
+    }
+    if (qmoe_capture_begin(c, NULL, err)) return -1;
+    c->profile = 1;
+    int rc = qmoe_forward_dev(c, layer, x, x_dtype, n, out, NULL, err);
+    c->profile = 0;
+    qmoe_graph *g = qmoe_capture_end(c, NULL, rc ? NULL : err);
+    if (rc || !g) {
+        qmoe_graph_free(g);
+        return -1;
+    }
+    const int nk = c->prof_kernels;
+    double acc[4] = {0, 0, 0, 0};
+    for (int r = 0; r < reps; r++) {
+        if (qmoe_graph_launch(g, NULL, err)) {
+            qmoe_graph_free(g);
+            return -1;
+        }
+        cudaError_t ce = cudaStreamSynchronize(c->stream);
+        if (ce != cudaSuccess) {
+            qmoe_graph_free(g);
+            seterr(err, "qmoe_profile_forward: %s", cudaGetErrorString(ce));
+            return -1;
+        }
+        for (int i = 0; i < nk; i++) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, c->pev[i], c->pev[i + 1]);
+            acc[i] += ms;
+        }
+    }
+    qmoe_graph_free(g);
+    for (int i = 0; i < max_kernels && i < nk; i++) kernel_us[i] = 1e3 * acc[i] / reps;
+    if (kernels) *kernels = nk;
+    return check_dev_err(c, c->stream, err);
 }
 
 static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err) {
@@ -725,12 +846,15 @@ static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err) {
     }
     int code = *c->err_host;
     if (code) {
+        /* clear the sticky word and any half-finished grid barrier */
         cudaMemsetAsync(c->err_dev, 0, sizeof(int), st);
+        cudaMemsetAsync(c->gbar, 0, 2 * sizeof(unsigned), st);
         cudaStreamSynchronize(st);
-        seterr(err, "qmoe: device reported error 0x%x (%s%s%s)", code,
-               code & QK_ERR_TIMEOUT_COPY ? "copy wait timed out " : "",
-               code & QK_ERR_NOT_RESIDENT ? "routed expert not resident " : "",
-               code & QK_ERR_BAD_ROUTE ? "top-k selection failed" : "");
+        seterr(err, "qmoe: device reported error 0x%x (%s%s%s%s)", code,
+               code & QK_ERR_TIMEOUT_COPY ? "copy wait timed out; " : "",
+               code & QK_ERR_NOT_RESIDENT ? "routed expert not resident; " : "",
+               code & QK_ERR_BAD_ROUTE ? "top-k selection failed; " : "",
+               code & QK_ERR_TIMEOUT_GRID ? "grid barrier timed out" : "");
         return -1;
     }
     return 0;

@@ -1,0 +1,353 @@
+// qmoe_dev.cuh - device helpers shared by the MoE kernels (sm_100a).
+//
+// mbarrier + cp.async.bulk staging with %globaltimer-bounded waits, the
+// programmatic-dependent-launch controls, a bounded grid barrier, and the
+// arithmetic building blocks that define the layer's results:
+//   router_dot_smem / router_dot_lane  canonical fp64 router dot
+//   dot_unit                           32-nibble q4 dot product
+//   topk_warp                          exact top-k + renormalised softmax
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "qmoe_internal.h"
+
+#define QK_DEV __device__ __forceinline__
+#define QK_FULL 0xffffffffu
+
+namespace qk {
+
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s bound on every device wait
+
+QK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+QK_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+QK_DEV float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
+QK_DEV float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+QK_DEV uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+QK_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+QK_DEV void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+QK_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+QK_DEV uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for phase `parity` of bar; false when it timed out.
+QK_DEV bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = gtimer();
+    for (;;) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (gtimer() - t0 > kWaitNs) return false;
+    }
+}
+
+// Global -> shared bulk copy; dst, src and bytes are 16-byte multiples.
+QK_DEV void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+QK_DEV unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+QK_DEV void st_release(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+QK_DEV unsigned long long atom_add_release(unsigned long long *p, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
+
+QK_DEV unsigned long long ld_acquire64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier for a grid whose CTAs are all resident. `ctr` is a 64-bit
+// counter that only grows: each CTA adds 1 with release semantics and waits
+// (acquire) until the counter reaches the next multiple of the grid size,
+// computed from the value its own add returned. No reset is needed between
+// barriers or launches as long as every launch of the same grid size uses
+// it. The spin is bounded: on timeout it sets QK_ERR_TIMEOUT_GRID and returns
+// false (that call's results are then invalid, but the kernel ends).
+QK_DEV bool grid_sync(unsigned long long *ctr, unsigned nctas, int *err) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const unsigned long long old = atom_add_release(ctr, 1ull);
+        const unsigned long long target = (old / nctas + 1) * nctas;
+        if (ld_acquire64(ctr) < target) {
+            const uint64_t t0 = gtimer();
+            while (ld_acquire64(ctr) < target) {
+                if (gtimer() - t0 > kWaitNs) {
+                    atomicOr(err, QK_ERR_TIMEOUT_GRID);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+// Dot product of 32 nibbles (one 16-byte unit, low nibble first) with x:
+// returns sum_i x_i * (1 + q_i / 16). The caller recovers sum x_i q_i as
+// 16 * (result - sum x_i). Building 1 + q/16 costs one shift and one LOP3
+// (exponent 127 OR'd over the nibble placed at mantissa bits 19..22), so each
+// weight is one FFMA with no int->float conversion.
+QK_DEV float dot_unit(uint4 w, const float *x) {
+    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int sh = 19 - 4 * i;
+            const uint32_t b = sh >= 0 ? (wd[j] << sh) : (wd[j] >> (-sh));
+            const float fq = __uint_as_float((b & 0x00780000u) | 0x3F800000u);
+            if (i & 1)
+                a1 = fmaf(x[8 * j + i], fq, a1);
+            else
+                a0 = fmaf(x[8 * j + i], fq, a0);
+        }
+    }
+    return a0 + a1;
+}
+
+// Lane part of the canonical router dot (see oracle/moe_oracle.c,
+// oracle_router_dot): lane l owns k = 256*i + 8*l + j; eight fp64 sums a[j]
+// over i ascending; exact products; folded ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)).
+// The caller finishes with a butterfly over lanes 16..1 and one rounding.
+QK_DEV double router_lane(const uint16_t *w, const float *x, int d, int lane) {
+    double a[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = 0.0;
+#pragma unroll 4
+    for (int base = 0; base < d; base += 256) {
+        const int k0 = base + 8 * lane;
+        if (k0 < d) {
+            const uint4 wv = *reinterpret_cast<const uint4 *>(w + k0);
+            const float4 x0 = *reinterpret_cast<const float4 *>(x + k0);
+            const float4 x1 = *reinterpret_cast<const float4 *>(x + k0 + 4);
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            const float wf[8] = {bf16lo(wv.x), bf16hi(wv.x), bf16lo(wv.y), bf16hi(wv.y),
+                                 bf16lo(wv.z), bf16hi(wv.z), bf16lo(wv.w), bf16hi(wv.w)};
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                a[j] = fma(static_cast<double>(xv[j]), static_cast<double>(wf[j]), a[j]);
+        }
+    }
+    return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+}
+
+QK_DEV double warp_sum_butterfly(double s) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s = s + __shfl_xor_sync(QK_FULL, s, off);
+    return s;
+}
+
+// Order-preserving u32 key of a logit (-0 folded onto +0).
+QK_DEV uint32_t fkey(float v) {
+    uint32_t b = __float_as_uint(v);
+    if ((b << 1) == 0) b = 0;
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+QK_DEV float key_value(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key ^ 0x80000000u) : ~key);
+}
+
+// Slow path of topk_warp: gathers the canonical top-k into s_key/s_idx
+// (unordered) by finding the k-th largest key MSB-first (one redux.sync count
+// per bit, early exit when exactly k keys qualify); ties at the threshold go
+// to the lower expert ids. keys: nj*32 staged keys (0 = absent). Returns the
+// number gathered (k on success).
+QK_DEV int topk_gather_radix(const uint32_t *keys, int nj, int k, uint32_t *s_key, int *s_idx) {
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0;
+    bool exact = false;
+#pragma unroll 1
+    for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = prefix | (1u << bit);
+        int c = 0;
+#pragma unroll 4
+        for (int j = 0; j < nj; ++j) c += keys[j * 32 + lane] >= cand ? 1 : 0;
+        const int cnt = static_cast<int>(__reduce_add_sync(QK_FULL, static_cast<unsigned>(c)));
+        if (cnt >= k) {
+            prefix = cand;
+            if (cnt == k) {
+                exact = true;
+                break;
+            }
+        }
+    }
+    int base = 0, need_eq = 0;
+    if (!exact) {
+        int c = 0;
+#pragma unroll 4
+        for (int j = 0; j < nj; ++j) c += keys[j * 32 + lane] > prefix ? 1 : 0;
+        need_eq = k - static_cast<int>(__reduce_add_sync(QK_FULL, static_cast<unsigned>(c)));
+    }
+#pragma unroll 1
+    for (int j = 0; j < nj; ++j) {
+        const uint32_t kk = keys[j * 32 + lane];
+        bool sel;
+        if (exact) {
+            sel = kk >= prefix;
+        } else {
+            const bool eq = kk == prefix;
+            const unsigned eqm = __ballot_sync(QK_FULL, eq);
+            const int before = __popc(eqm & ((1u << lane) - 1u));
+            sel = kk > prefix || (eq && before < need_eq);
+            need_eq -= min(__popc(eqm), need_eq);
+        }
+        const unsigned m = __ballot_sync(QK_FULL, sel);
+        if (sel) {
+            const int pos = base + __popc(m & ((1u << lane) - 1u));
+            if (pos < 32) {
+                s_key[pos] = kk;
+                s_idx[pos] = j * 32 + lane;
+            }
+        }
+        base += __popc(m);
+    }
+    __syncwarp();
+    return base;
+}
+
+// Stages the order-preserving keys of E logits into keys[0, nj*32) (zero
+// past E), one slot per thread of the calling group of `nthreads` threads
+// starting at thread index `t0`. Callers synchronise before topk_warp.
+template <bool CG>
+QK_DEV void topk_stage_keys(const float *lg, int E, uint32_t *keys, int t, int nthreads) {
+    const int n = (E + 31) / 32 * 32;
+    for (int e = t; e < n; e += nthreads) keys[e] = e < E ? fkey(CG ? __ldcg(lg + e) : lg[e]) : 0u;
+}
+
+// Exact top-k of E staged keys by one warp (k <= 32), selection by
+// (value desc, index asc), written in that order; w is the softmax over the
+// selected logits (model.c:1305-1318).
+//   1. tau = the k-th largest of the 32 lane maxima. At least k keys are
+//      >= tau, so every member of the top-k (and every key tied with its
+//      k-th value) is >= tau: the keys >= tau are a complete candidate set,
+//      typically 10-20 of them.
+//   2. The candidates are compacted in index order and each is ranked among
+//      the candidates by (key desc, index asc); rank < k is the answer.
+// When more than 32 keys qualify the radix path gathers the set instead.
+// keys: (E+31)/32*32 staged keys; s_key/s_idx/s_ev: 32-entry scratch of this
+// warp. Returns false if fewer than k keys exist.
+QK_DEV bool topk_warp(const uint32_t *keys, int E, int k, uint32_t *s_key, int *s_idx,
+                      float *s_ev, int *idx_out, float *w_out) {
+    const int lane = threadIdx.x & 31;
+    const int nj = (E + 31) / 32;
+    uint32_t mxk = 0;
+#pragma unroll 4
+    for (int j = 0; j < nj; ++j) mxk = max(mxk, keys[j * 32 + lane]);
+    int r = 0;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+        const uint32_t o = __shfl_sync(QK_FULL, mxk, j);
+        r += (o > mxk || (o == mxk && j < lane)) ? 1 : 0;
+    }
+    const unsigned bm = __ballot_sync(QK_FULL, r == k - 1);
+    const uint32_t tau = __shfl_sync(QK_FULL, mxk, __ffs(bm) - 1);
+    int C = 0;
+#pragma unroll 2
+    for (int j = 0; j < nj; ++j) {
+        const int e = j * 32 + lane;
+        const uint32_t kk = keys[e];
+        const bool cand = e < E && kk >= tau && kk != 0u;
+        const unsigned m = __ballot_sync(QK_FULL, cand);
+        if (cand) {
+            const int pos = C + __popc(m & ((1u << lane) - 1u));
+            if (pos < 32) {
+                s_key[pos] = kk;
+                s_idx[pos] = e;
+            }
+        }
+        C += __popc(m);
+    }
+    __syncwarp();
+    if (C > 32) C = topk_gather_radix(keys, nj, k, s_key, s_idx);
+    if (C < k || C > 32) return false;
+    int rank = 0, mi = 0;
+    uint32_t mk = 0;
+    if (lane < C) {
+        mk = s_key[lane];
+        mi = s_idx[lane];
+    }
+    // rank among the candidates: lane m's (key, index) arrive by shuffle
+#pragma unroll 4
+    for (int m = 0; m < C; ++m) {
+        const uint32_t ok = __shfl_sync(QK_FULL, mk, m);
+        const int oi = __shfl_sync(QK_FULL, mi, m);
+        rank += (ok > mk || (ok == mk && oi < mi)) ? 1 : 0;
+    }
+    const bool mine = lane < C && rank < k;
+    float v = 0.f;
+    if (mine) {
+        v = key_value(mk);
+        s_idx[rank] = mi;
+        s_key[rank] = __float_as_uint(v);
+    }
+    __syncwarp();
+    const float mx = __uint_as_float(s_key[0]);
+    float ev = 0.f;
+    if (mine) {
+        ev = expf(v - mx);
+        s_ev[rank] = ev;
+    }
+    __syncwarp();
+    float sum = 0.f;
+    for (int m = 0; m < k; ++m) sum += s_ev[m];
+    if (mine) {
+        idx_out[rank] = mi;
+        w_out[rank] = ev / sum;
+    }
+    __syncwarp();
+    return true;
+}
+
+}  // namespace qk

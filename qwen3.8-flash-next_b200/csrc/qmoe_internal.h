@@ -46,6 +46,7 @@ enum {
     QK_ERR_TIMEOUT_COPY = 1,  /* bulk-copy completion wait gave up */
     QK_ERR_NOT_RESIDENT = 2,  /* a routed expert had no HBM slot */
     QK_ERR_BAD_ROUTE = 4,     /* top-k found fewer than k finite logits */
+    QK_ERR_TIMEOUT_GRID = 8,  /* grid barrier wait gave up */
 };
 
 /* Everything one forward call needs on the device. */
@@ -68,6 +69,8 @@ typedef struct {
     float *out;                  /* [T, d] */
     int *err;                    /* device error word */
     int num_sms;
+    unsigned long long *ptimes;  /* diagnostics: per-CTA phase timestamps
+                                    [grid][16] (%globaltimer ns), or NULL */
 } qk_fwd;
 
 /* Kernel launchers (qmoe_kernels.cu). Each returns a cudaError_t as int.
@@ -80,6 +83,14 @@ int qk_launch_router(const qk_fwd *f, void *stream, int pdl);
 int qk_launch_topk(const qk_fwd *f, void *stream, int pdl);
 int qk_launch_decode_gateup(const qk_fwd *f, void *stream, int pdl);
 int qk_launch_decode_down(const qk_fwd *f, void *stream, int pdl);
+
+/* Single-launch decode (T == 1): router, top-k, gate/up and down+combine in
+ * one persistent kernel with one CTA per SM and grid barriers between the
+ * phases. gbar: two zeroed u32 in device memory owned by the context.
+ * Returns QK_FUSED_UNFIT (no launch) when the shape's per-CTA working set does
+ * not fit in shared memory; the caller then uses the four-kernel path. */
+#define QK_FUSED_UNFIT (-7)
+int qk_launch_decode_fused(const qk_fwd *f, unsigned *gbar, void *stream, int pdl);
 
 /* internal cache helper: replace the value of an existing key */
 struct qmoe_cache;

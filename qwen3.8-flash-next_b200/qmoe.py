@@ -85,9 +85,13 @@ SIGNATURES = {
     "qmoe_forward_dev": (C.c_int, [_P, C.c_int, _P, C.c_int, C.c_int, _P, _P, C.POINTER(Err)]),
     "qmoe_sync": (C.c_int, [_P, C.POINTER(Err)]),
     "qmoe_last_routing": (C.c_int, [_P, _P, _P, _P, C.POINTER(Err)]),
-    "qmoe_profile_enable": (C.c_int, [_P, C.c_int]),
-    "qmoe_profile_read": (C.c_int, [_P, C.POINTER(C.c_double), C.c_int, C.POINTER(C.c_int),
-                                    C.POINTER(C.c_uint64)]),
+    "qmoe_capture_begin": (C.c_int, [_P, _P, C.POINTER(Err)]),
+    "qmoe_capture_end": (_P, [_P, _P, C.POINTER(Err)]),
+    "qmoe_graph_launch": (C.c_int, [_P, _P, C.POINTER(Err)]),
+    "qmoe_graph_free": (None, [_P]),
+    "qmoe_profile_forward": (C.c_int, [_P, C.c_int, _P, C.c_int, C.c_int, _P, C.c_int,
+                                       C.POINTER(C.c_double), C.c_int, C.POINTER(C.c_int),
+                                       C.POINTER(Err)]),
     "qmoe_expert_peek": (C.c_int, [_P, C.c_int, C.c_int]),
     "qmoe_expert_get": (C.c_int, [_P, C.c_int, C.c_int]),
     "qmoe_experts_load": (C.c_int, [_P, C.c_int, _P, C.c_size_t, C.POINTER(Err)]),
@@ -263,13 +267,45 @@ class Context:
         lib().qmoe_stats_get(self.h, C.byref(s))
         return s.as_dict()
 
-    def profile(self, on: bool):
-        lib().qmoe_profile_enable(self.h, int(on))
+    def capture_begin(self, stream=None):
+        err = Err()
+        self._chk(lib().qmoe_capture_begin(self.h, stream, C.byref(err)), err)
 
-    def profile_read(self):
-        """(per-kernel total ms [router, topk, gateup, down], profiled calls)."""
-        ms = (C.c_double * 8)()
+    def capture_end(self, stream=None) -> "Graph":
+        err = Err()
+        g = lib().qmoe_capture_end(self.h, stream, C.byref(err))
+        if not g:
+            raise QmoeError(err.text())
+        return Graph(g)
+
+    def profile_forward(self, layer, x_ptr, x_dtype, n, out_ptr, reps):
+        """Mean device microseconds per kernel launch [router, topk, gateup, down]."""
+        us = (C.c_double * 8)()
         nk = C.c_int()
-        calls = C.c_uint64()
-        lib().qmoe_profile_read(self.h, ms, 8, C.byref(nk), C.byref(calls))
-        return [ms[i] for i in range(nk.value)], calls.value
+        err = Err()
+        self._chk(lib().qmoe_profile_forward(self.h, layer, x_ptr, x_dtype, n, out_ptr, reps,
+                                             us, 8, C.byref(nk), C.byref(err)), err)
+        return [us[i] for i in range(nk.value)]
+
+
+class Graph:
+    """An instantiated CUDA graph of captured forward calls."""
+
+    def __init__(self, h):
+        self.h = h
+
+    def launch(self, stream=None):
+        err = Err()
+        if lib().qmoe_graph_launch(self.h, stream, C.byref(err)) != 0:
+            raise QmoeError(err.text())
+
+    def close(self):
+        if self.h:
+            lib().qmoe_graph_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
