@@ -3,23 +3,29 @@
 // The whole of moe_forward (c/src/model.c:1281-1405) for T == 1 in one
 // persistent kernel: one CTA per SM, three phases split by grid barriers.
 //
-//   prologue  bulk-copy the weights that do not depend on routing into shared
-//             memory: this CTA's router rows (mlp.gate, plus the shared-gate
-//             row) and its rows of the shared expert (gate/up and down).
-//             Issued before griddepcontrol.wait, so they overlap the previous
-//             kernel in the stream.
-//   phase 1   x -> registers / shared memory; router rows -> logits (global);
-//             shared-expert gate/up rows -> h (global).       [grid barrier]
-//   phase 2   every CTA computes the same exact top-k from the 512 logits,
-//             then bulk-copies its share of the routed experts' gate/up rows
-//             AND its share of their down rows (all k experts at once), and
-//             computes its gate/up rows -> h.                 [grid barrier]
-//   phase 3   h -> shared memory; this CTA's output rows for all k+1 experts
-//             (down weights already resident), weighted combine in registers.
+//   prologue  bulk-copy what does not depend on routing into shared memory:
+//             this CTA's router rows (mlp.gate plus the shared-gate row), its
+//             rows of the shared expert (gate/up and down) and the layer's
+//             expert -> slot table. Issued before griddepcontrol.wait.
+//   phase 1   x -> registers and shared memory; router rows -> logits
+//             (global).                                        [grid barrier]
+//   phase 2   the logits are staged as order keys; warp 0 computes the exact
+//             top-k (every CTA computes the same), looks the k experts up in
+//             the staged slot table and issues this CTA's share of their
+//             gate/up rows (in chunks of <= 8 rows, one mbarrier each) and of
+//             their down rows (all k experts at once). Meanwhile warps 1..7
+//             compute the shared expert's gate/up rows. Then all warps compute
+//             the routed gate/up rows chunk by chunk as they land -> h.
+//                                                              [grid barrier]
+//   phase 3   h -> shared memory (swizzled); this CTA's output rows for all
+//             k+1 experts as (expert, row-pair) tasks, so a warp keeps one
+//             expert's h slice in registers across rows; per-expert partials
+//             are combined in a fixed expert order with the routing weights
+//             and the shared gate; each output written once.
 //
 // Per CTA at d=2048, E=512, k=10, I=512 on 148 SMs: 16 KB router, 9 KB shared
-// gate/up, 81 KB routed gate/up, 44 KB down rows: every byte the CTA needs for
-// the token is in flight at once. Dependents are triggered only after the
+// gate/up, 81 KB routed gate/up, 44 KB down rows, so every byte the CTA needs
+// for the token is requested at once. Dependents are triggered only after the
 // second grid barrier, when every CTA of this grid is resident, so a waiting
 // next launch can never take an SM this grid still needs.
 
@@ -32,6 +38,9 @@ cudaError_t qk_launch_raw(const void *fn, dim3 grid, dim3 block, size_t smem, vo
 
 namespace {
 
+constexpr int kChunkRows = 8;   // routed gate/up rows per bulk copy / mbarrier
+constexpr int kMaxChunks = 12;  // chunks per CTA (checked by make_plan)
+
 struct Plan {
     int G;       // CTAs, one per SM
     int rr_max;  // router rows per CTA (of E + 1)
@@ -41,9 +50,7 @@ struct Plan {
     int off_router, off_sgu, off_rgu, off_down, total;
 };
 
-__device__ __forceinline__ int part(int c, int n, int G) {
-    return static_cast<int>((static_cast<long long>(c) * n) / G);
-}
+__device__ __forceinline__ int part(int c, int n, int G) { return (c * n) / G; }
 
 __device__ __forceinline__ void load_x_unit(const qk_fwd &f, int u, float *xr) {
     if (f.x_bf16) {
@@ -99,8 +106,10 @@ template <int UPL, int LPR>
 __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
                                                          unsigned long long *gbar) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bar[3];
+    __shared__ uint64_t bar[2 + kMaxChunks];  // 0: prologue, 1: down rows, 2..: chunks
     __shared__ int s_ok;
+    __shared__ int s_chunk0[kMaxChunks + 1];  // first routed row (CTA-local) of each chunk
+    __shared__ int s_nchunks;
     __shared__ uint32_t s_key[32];
     __shared__ int s_idx[32];
     __shared__ float s_ev[32];
@@ -124,26 +133,21 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
     float *sm_x = reinterpret_cast<float *>(smem + p.total) - d;  // last d floats
 
     // diagnostics: phase timestamps of this CTA (thread 0)
-#define STAMP(i)                                                              \
-    do {                                                                      \
+#define STAMP(i)                                                                         \
+    do {                                                                                 \
         if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 16 + (i)] = gtimer(); \
     } while (0)
     STAMP(0);
-    if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
-        mbar_init(&bar[2], 1);
-    }
+    if (tid < 2 + kMaxChunks) mbar_init(&bar[tid], 1);
     __syncthreads();
 
-    // ---- prologue: weights independent of routing
+    // ---- prologue: what does not depend on routing
     if (tid == 0) {
         const uint32_t b_router = static_cast<uint32_t>((rr1 - rr0) * d * 2);
         const uint32_t b_sgu = static_cast<uint32_t>((sr1 - sr0) * L.gu_row);
         const uint32_t b_sdown = static_cast<uint32_t>((or1 - or0) * L.d_row);
         const uint32_t b_slots = static_cast<uint32_t>(E * 4);
         mbar_expect_tx(&bar[0], b_router + b_sgu + b_sdown + b_slots);
-        bulk_load(s_slots, f.slot_of, b_slots, &bar[0]);
         const int re = min(rr1, E);
         if (re > rr0)
             bulk_load(sm_router, f.router + static_cast<size_t>(rr0) * d,
@@ -151,34 +155,53 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
         if (rr1 > E)
             bulk_load(sm_router + static_cast<size_t>(E - rr0) * d * 2, f.shared_gate,
                       static_cast<uint32_t>(d * 2), &bar[0]);
+        bulk_load(s_slots, f.slot_of, b_slots, &bar[0]);
         if (sr1 > sr0)
             bulk_load(sm_sgu, f.shared_slot + static_cast<size_t>(sr0) * L.gu_row, b_sgu, &bar[0]);
         if (or1 > or0)
             bulk_load(sm_down + static_cast<size_t>(k) * p.or_max * L.d_row,
                       f.shared_slot + L.gu_bytes + static_cast<size_t>(or0) * L.d_row, b_sdown,
                       &bar[0]);
+        // routed gate/up chunk boundaries: runs within one expert, <= 8 rows
+        int n = 0, r = gr0;
+        while (r < gr1 && n < kMaxChunks) {
+            const int end = min(min(gr1, (r / I + 1) * I), r + kChunkRows);
+            s_chunk0[n++] = r - gr0;
+            r = end;
+        }
+        s_chunk0[n] = gr1 - gr0;
+        s_nchunks = n;
     }
     pdl_wait();
     STAMP(1);
 
-    // ---- phase 1: x, router rows, shared gate/up rows
-    for (int i = tid; i < d; i += blockDim.x)
-        sm_x[i] = f.x_bf16
-                      ? __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t *>(f.x)[i]) << 16)
-                      : static_cast<const float *>(f.x)[i];
+    // ---- phase 1: x, router rows. Every warp loads all of x into registers
+    // (lane l owns the 32-element units l, l+32, ...); warp w then writes the
+    // units u with u % 8 == w to shared memory for the router.
     float xr[UPL][32];
     float xs[UPL];
 #pragma unroll
     for (int i = 0; i < UPL; ++i) {
         const int u = lane + 32 * i;
+        if (u < d / 32) load_x_unit(f, u, xr[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < UPL; ++i) {
+        const int u = lane + 32 * i;
         xs[i] = 0.f;
         if (u < d / 32) {
-            load_x_unit(f, u, xr[i]);
 #pragma unroll
             for (int q = 0; q < 32; ++q) xs[i] += xr[i][q];
+            if ((u & 7) == warp) {
+                float4 *dx = reinterpret_cast<float4 *>(sm_x + 32 * u);
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    dx[q] = make_float4(xr[i][4 * q], xr[i][4 * q + 1], xr[i][4 * q + 2], xr[i][4 * q + 3]);
+            }
         }
     }
     __syncthreads();
+    STAMP(13);
     const bool ok0 = mbar_wait(&bar[0], 0);
     STAMP(2);
     if (!ok0 && tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
@@ -198,9 +221,7 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
     grid_sync(gbar, G, f.err);
     STAMP(4);
 
-    // ---- phase 2: top-k, routed copies, routed gate/up rows. Warp 0 does
-    // the top-k, looks the experts up in the staged slot table and issues
-    // every routed copy, one copy per lane.
+    // ---- phase 2
     topk_stage_keys<true>(f.logits, E, s_keys, tid, blockDim.x);
     __syncthreads();
     if (warp == 0) {
@@ -214,37 +235,51 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
         }
         const bool resident = __all_sync(QK_FULL, lane >= k || sp != nullptr);
         const bool good = okk && resident && ok0;  // no copies in flight on error paths
+        const int nch = s_nchunks;
+        const int ndown = or1 > or0 ? k : 0;
+        if (good) {
+            // expect_tx before any copy of that barrier is issued
+            if (lane < nch)
+                mbar_expect_tx(&bar[2 + lane],
+                               static_cast<uint32_t>((s_chunk0[lane + 1] - s_chunk0[lane]) * L.gu_row));
+            if (lane == 31) mbar_expect_tx(&bar[1], static_cast<uint32_t>(ndown * (or1 - or0) * L.d_row));
+        }
+        __syncwarp();
+        // slot pointers by shuffle (all lanes take part), then each lane issues
+        // its copies (at most 64: nch <= 12 chunks plus k <= 32 down copies)
+        const uint8_t *srcs[2];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+            const int q = lane + 32 * h2;
+            int s = 0;
+            if (q < nch) s = (gr0 + s_chunk0[q]) / I;
+            else if (q < nch + ndown) s = q - nch;
+            srcs[h2] = reinterpret_cast<const uint8_t *>(
+                __shfl_sync(QK_FULL, reinterpret_cast<uintptr_t>(sp), s & 31));
+        }
+        if (good) {
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                const int q = lane + 32 * h2;
+                if (q < nch) {
+                    const int lo = gr0 + s_chunk0[q], hi = gr0 + s_chunk0[q + 1];
+                    const int s = lo / I;
+                    bulk_load(sm_rgu + static_cast<size_t>(lo - gr0) * L.gu_row,
+                              srcs[h2] + static_cast<size_t>(lo - s * I) * L.gu_row,
+                              static_cast<uint32_t>((hi - lo) * L.gu_row), &bar[2 + q]);
+                } else if (q < nch + ndown) {
+                    const int s = q - nch;
+                    bulk_load(sm_down + static_cast<size_t>(s) * p.or_max * L.d_row,
+                              srcs[h2] + L.gu_bytes + static_cast<size_t>(or0) * L.d_row,
+                              static_cast<uint32_t>((or1 - or0) * L.d_row), &bar[1]);
+                }
+            }
+        }
         if (lane == 0) {
             r_w[k] = 1.0f / (1.0f + expf(-gl));
             if (!okk) atomicOr(f.err, QK_ERR_BAD_ROUTE);
             else if (!resident) atomicOr(f.err, QK_ERR_NOT_RESIDENT);
             s_ok = good ? 1 : 0;
-            if (good) {
-                mbar_expect_tx(&bar[1], static_cast<uint32_t>((gr1 - gr0) * L.gu_row));
-                mbar_expect_tx(&bar[2], static_cast<uint32_t>(k * (or1 - or0) * L.d_row));
-            }
-        }
-        __syncwarp();
-        if (good) {
-            const int s0 = gr0 / I;
-            const int npieces = gr1 > gr0 ? (gr1 - 1) / I - s0 + 1 : 0;
-            const int ndown = or1 > or0 ? k : 0;
-            for (int q = 0; q < npieces + ndown; q += 32) {
-                const int my = q + lane;
-                const int s = my < npieces ? s0 + my : my - npieces;
-                const uint8_t *src = reinterpret_cast<const uint8_t *>(
-                    __shfl_sync(QK_FULL, reinterpret_cast<uintptr_t>(sp), s & 31));
-                if (my < npieces) {
-                    const int lo = max(gr0, s * I), hi = min(gr1, (s + 1) * I);
-                    bulk_load(sm_rgu + static_cast<size_t>(lo - gr0) * L.gu_row,
-                              src + static_cast<size_t>(lo - s * I) * L.gu_row,
-                              static_cast<uint32_t>((hi - lo) * L.gu_row), &bar[1]);
-                } else if (my < npieces + ndown) {
-                    bulk_load(sm_down + static_cast<size_t>(s) * p.or_max * L.d_row,
-                              src + L.gu_bytes + static_cast<size_t>(or0) * L.d_row,
-                              static_cast<uint32_t>((or1 - or0) * L.d_row), &bar[2]);
-                }
-            }
         }
         if (c == 0 && okk) {
             if (lane < k) {
@@ -253,40 +288,35 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
             }
             if (lane == 0) f.sgate[0] = r_w[k];
         }
+    } else if (ok0) {
+        // warps 1..7: the shared expert's gate/up rows while warp 0 routes
+        for (int i = warp - 1; i < sr1 - sr0; i += 7) {
+            const float hv = gateup_row<UPL>(sm_sgu + static_cast<size_t>(i) * L.gu_row, L, xr, xs, lane);
+            if (lane == 0) f.h[static_cast<size_t>(k) * I + sr0 + i] = hv;
+        }
     }
     __syncthreads();
     STAMP(5);
     const bool live = s_ok != 0;
     bool ok1 = true;
-    STAMP(6);
     if (live) {
-        // The shared expert's rows (staged since the prologue) first, while
-        // the routed copies fly, then the routed rows; one loop, so the
-        // unrolled row code exists once.
-        const int ns = sr1 - sr0, nr = gr1 - gr0;
-        bool waited = false;
-        for (int i = warp; i < ns + nr; i += 8) {
-            const uint8_t *row;
-            size_t hi;
-            if (i < ns) {
-                row = sm_sgu + static_cast<size_t>(i) * L.gu_row;
-                hi = static_cast<size_t>(k) * I + sr0 + i;
-            } else {
-                if (!waited) {
-                    ok1 = mbar_wait(&bar[1], 0);
-                    waited = true;
-                    if (!ok1) break;
-                }
-                row = sm_rgu + static_cast<size_t>(i - ns) * L.gu_row;
-                hi = static_cast<size_t>(gr0 + i - ns);  // slot (gr0+i-ns)/I, row %I
+        // routed rows, each after its chunk has landed
+        const int nr = gr1 - gr0;
+        int ch = 0;
+        for (int i = warp; i < nr; i += 8) {
+            while (ch + 1 < s_nchunks && s_chunk0[ch + 1] <= i) ++ch;
+            if (!mbar_wait(&bar[2 + ch], 0)) {
+                ok1 = false;
+                break;
             }
-            const float hv = gateup_row<UPL>(row, L, xr, xs, lane);
-            if (lane == 0) f.h[hi] = hv;
+            const float hv = gateup_row<UPL>(sm_rgu + static_cast<size_t>(i) * L.gu_row, L, xr, xs, lane);
+            if (lane == 0) f.h[gr0 + i] = hv;  // slot (gr0+i)/I, row (gr0+i)%I
         }
-        if (!waited) ok1 = mbar_wait(&bar[1], 0);
-        STAMP(7);
+        // every chunk has landed before sm_rgu is reused for h
+        for (int q = 0; q < s_nchunks && ok1; ++q) ok1 = mbar_wait(&bar[2 + q], 0);
         if (!ok1 && lane == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
     }
+    ok1 = __syncthreads_and(ok1) != 0;  // CTA-uniform from here on
     STAMP(8);
     grid_sync(gbar, G, f.err);
     STAMP(9);
@@ -295,11 +325,28 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
     // ---- phase 3: h -> shared memory, down rows + weighted combine
     float4 *hs4 = reinterpret_cast<float4 *>(sm_rgu);
     float *hsum = reinterpret_cast<float *>(hs4 + S * (I / 4));
+    float *partial = hsum + S * (I / 32);  // [S][or_max]
     const int q4 = I / 4, units = I / 32;
-    const float4 *hg = reinterpret_cast<const float4 *>(f.h);
-    for (int i = tid; i < S * q4; i += blockDim.x) {
-        const int s = i / q4, cc = i % q4, j = cc >> 3, q = cc & 7;
-        hs4[s * q4 + 8 * j + (q ^ (j & 7))] = __ldcg(hg + i);
+    {
+        // batched: all loads of a thread before its (swizzled) stores
+        const float4 *hg = reinterpret_cast<const float4 *>(f.h);
+        const int n4 = S * q4;
+        for (int base = tid; base < n4; base += 8 * 256) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = base + u * 256;
+                if (i < n4) v[u] = __ldcg(hg + i);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = base + u * 256;
+                if (i < n4) {
+                    const int s = i / q4, cc = i % q4, j = cc >> 3, q = cc & 7;
+                    hs4[s * q4 + 8 * j + (q ^ (j & 7))] = v[u];
+                }
+            }
+        }
     }
     __syncthreads();
     for (int i = tid; i < S * units; i += blockDim.x) {
@@ -316,48 +363,59 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
     __syncthreads();
     STAMP(10);
     if (!live || !ok1) return;
-    if (!mbar_wait(&bar[2], 0)) {
+    if (!mbar_wait(&bar[1], 0)) {
         if (tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
-        mbar_wait(&bar[2], 0);
+        mbar_wait(&bar[1], 0);
         return;
     }
     STAMP(11);
+    // tasks (expert s, row group) in expert-major order; warp w owns a
+    // contiguous task range, so it reloads its h slice only when s changes
     constexpr int RPW = 32 / LPR;
+    const int nrows = or1 - or0;
+    const int ngrp = (nrows + RPW - 1) / RPW;
+    const int ntask = S * ngrp;
+    const int t0 = warp * ntask / 8, t1 = (warp + 1) * ntask / 8;
     const int j = lane % LPR;
-    for (int base = 0; base < or1 - or0; base += 8 * RPW) {
-        const int rl = base + warp * RPW + lane / LPR;
-        const bool on = rl < or1 - or0;
-        const int rlc = on ? rl : 0;
-        float acc = 0.f;
-        for (int s = 0; s < S; ++s) {
-            const uint8_t *row = sm_down + (static_cast<size_t>(s) * p.or_max + rlc) * L.d_row;
-            const uint4 w = *reinterpret_cast<const uint4 *>(row + 16 * j);
-            const int grp = (32 * j) / L.g;
-            const uint32_t sb = *reinterpret_cast<const uint32_t *>(row + I / 2 + 4 * grp);
-            float hv[32];
+    const int grp = (32 * j) / L.g;
+    int cur = -1;
+    float hv[32];
+    float hsu = 0.f;
+    for (int t = t0; t < t1; ++t) {
+        const int s = t / ngrp, rg = t % ngrp;
+        if (s != cur) {
             const float4 *hb = hs4 + s * q4 + 8 * j;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const float4 v = hb[q ^ (j & 7)];
                 hv[4 * q + 0] = v.x; hv[4 * q + 1] = v.y; hv[4 * q + 2] = v.z; hv[4 * q + 3] = v.w;
             }
-            const float hsu = hsum[s * units + j];
-            const float a = dot_unit(w, hv);
-            float part_ = fmaf(bf16lo(sb), 16.f * (a - hsu), bf16hi(sb) * hsu);
-#pragma unroll
-            for (int off = LPR / 2; off >= 1; off >>= 1)
-                part_ += __shfl_xor_sync(QK_FULL, part_, off);
-            acc = fmaf(r_w[s], part_, acc);
+            hsu = hsum[s * units + j];
+            cur = s;
         }
-        if (on && j == 0) f.out[or0 + rl] = acc;
+        const int rl = rg * RPW + lane / LPR;
+        const int rlc = rl < nrows ? rl : 0;
+        const uint8_t *row = sm_down + (static_cast<size_t>(s) * p.or_max + rlc) * L.d_row;
+        const uint4 w = *reinterpret_cast<const uint4 *>(row + 16 * j);
+        const uint32_t sb = *reinterpret_cast<const uint32_t *>(row + I / 2 + 4 * grp);
+        const float a = dot_unit(w, hv);
+        float part_ = fmaf(bf16lo(sb), 16.f * (a - hsu), bf16hi(sb) * hsu);
+#pragma unroll
+        for (int off = LPR / 2; off >= 1; off >>= 1) part_ += __shfl_xor_sync(QK_FULL, part_, off);
+        if (j == 0 && rl < nrows) partial[s * p.or_max + rl] = part_;
     }
-    STAMP(12);  // thread 0's own rows done
+    __syncthreads();
+    // combine in expert order: out = sum_s w_s * partial_s (shared gate last)
+    for (int rl = tid; rl < nrows; rl += blockDim.x) {
+        float acc = 0.f;
+        for (int s = 0; s < S; ++s) acc = fmaf(r_w[s], partial[s * p.or_max + rl], acc);
+        f.out[or0 + rl] = acc;
+    }
+    STAMP(12);
 #undef STAMP
 }
 
-// dynamic shared memory cap; with ~9 KB of static shared memory this stays
-// under the 227 KB a CTA may use
-constexpr int kFusedSmemMax = 200 * 1024;
+constexpr int kFusedSmemMax = 200 * 1024;  // + ~10 KB static stays under 227 KB
 
 int align128(int v) { return (v + 127) / 128 * 128; }
 
@@ -370,13 +428,16 @@ bool make_plan(const qk_fwd *f, Plan *p) {
     p->sr_max = (L.I + G - 1) / G;
     p->gr_max = (L.k * L.I + G - 1) / G;
     p->or_max = (L.d + G - 1) / G;
+    // chunk count bound: every expert boundary inside the range adds one
+    const int chunks = (p->gr_max + kChunkRows - 1) / kChunkRows + (p->gr_max + L.I - 1) / L.I + 1;
+    if (chunks > kMaxChunks) return false;
     int off = 0;
     p->off_router = off;
     off = align128(off + p->rr_max * L.d * 2);
     p->off_sgu = off;
     off = align128(off + p->sr_max * L.gu_row);
     p->off_rgu = off;
-    const int h_bytes = S * L.I * 4 + S * (L.I / 32) * 4;
+    const int h_bytes = S * L.I * 4 + S * (L.I / 32) * 4 + S * p->or_max * 4;
     off = align128(off + (p->gr_max * L.gu_row > h_bytes ? p->gr_max * L.gu_row : h_bytes));
     p->off_down = off;
     off = align128(off + S * p->or_max * L.d_row);

@@ -257,13 +257,48 @@ QK_DEV int topk_gather_radix(const uint32_t *keys, int nj, int k, uint32_t *s_ke
     return base;
 }
 
+// Global (L2) -> shared copy of n float4 by `nthreads` threads, with all of a
+// thread's loads of a batch issued before its stores: a plain load/store
+// loop costs one memory round trip per iteration, since the compiler cannot
+// prove the global source and the shared destination do not alias.
+QK_DEV void copy_f4_l2_to_smem(float4 *dst, const float4 *src, int n, int t, int nthreads) {
+    constexpr int B = 8;
+    for (int base = t; base < n; base += B * nthreads) {
+        float4 v[B];
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            const int i = base + u * nthreads;
+            if (i < n) v[u] = __ldcg(src + i);
+        }
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            const int i = base + u * nthreads;
+            if (i < n) dst[i] = v[u];
+        }
+    }
+}
+
 // Stages the order-preserving keys of E logits into keys[0, nj*32) (zero
-// past E), one slot per thread of the calling group of `nthreads` threads
-// starting at thread index `t0`. Callers synchronise before topk_warp.
+// past E), shared by the calling group of `nthreads` threads (t = index in
+// the group); loads are batched before stores. Callers synchronise before
+// topk_warp.
 template <bool CG>
 QK_DEV void topk_stage_keys(const float *lg, int E, uint32_t *keys, int t, int nthreads) {
+    constexpr int B = 8;
     const int n = (E + 31) / 32 * 32;
-    for (int e = t; e < n; e += nthreads) keys[e] = e < E ? fkey(CG ? __ldcg(lg + e) : lg[e]) : 0u;
+    for (int base = t; base < n; base += B * nthreads) {
+        float v[B];
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            const int e = base + u * nthreads;
+            v[u] = e < E ? (CG ? __ldcg(lg + e) : lg[e]) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            const int e = base + u * nthreads;
+            if (e < n) keys[e] = e < E ? fkey(v[u]) : 0u;
+        }
+    }
 }
 
 // Exact top-k of E staged keys by one warp (k <= 32), selection by
@@ -293,21 +328,34 @@ QK_DEV bool topk_warp(const uint32_t *keys, int E, int k, uint32_t *s_key, int *
     }
     const unsigned bm = __ballot_sync(QK_FULL, r == k - 1);
     const uint32_t tau = __shfl_sync(QK_FULL, mxk, __ffs(bm) - 1);
-    int C = 0;
-#pragma unroll 2
+    // compaction: per-lane count, warp prefix sum, per-lane writes (the
+    // candidate order is irrelevant: ranking compares indices explicitly)
+    int own = 0;
+#pragma unroll 4
     for (int j = 0; j < nj; ++j) {
-        const int e = j * 32 + lane;
-        const uint32_t kk = keys[e];
-        const bool cand = e < E && kk >= tau && kk != 0u;
-        const unsigned m = __ballot_sync(QK_FULL, cand);
-        if (cand) {
-            const int pos = C + __popc(m & ((1u << lane) - 1u));
-            if (pos < 32) {
+        const uint32_t kk = keys[j * 32 + lane];
+        own += (j * 32 + lane < E && kk >= tau && kk != 0u) ? 1 : 0;
+    }
+    int incl = own;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int t = __shfl_up_sync(QK_FULL, incl, off);
+        if (lane >= off) incl += t;
+    }
+    const int C0 = __shfl_sync(QK_FULL, incl, 31);
+    int C = C0;
+    if (C0 <= 32) {
+        int pos = incl - own;
+#pragma unroll 4
+        for (int j = 0; j < nj; ++j) {
+            const int e = j * 32 + lane;
+            const uint32_t kk = keys[e];
+            if (e < E && kk >= tau && kk != 0u) {
                 s_key[pos] = kk;
                 s_idx[pos] = e;
+                ++pos;
             }
         }
-        C += __popc(m);
     }
     __syncwarp();
     if (C > 32) C = topk_gather_radix(keys, nj, k, s_key, s_idx);

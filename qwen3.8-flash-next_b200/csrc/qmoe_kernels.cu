@@ -68,11 +68,23 @@ __global__ void __launch_bounds__(256) k_router(qk_fwd f) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = f.L.d, E = f.L.E;
     const int t = blockIdx.y;
-    for (int i = threadIdx.x; i < d; i += blockDim.x)
-        xs[i] = f.x_bf16 ? __uint_as_float(static_cast<uint32_t>(
-                               static_cast<const uint16_t *>(f.x)[static_cast<size_t>(t) * d + i])
-                           << 16)
-                         : static_cast<const float *>(f.x)[static_cast<size_t>(t) * d + i];
+    // 8 elements per thread per step, loads before stores
+    for (int i0 = 8 * threadIdx.x; i0 < d; i0 += 8 * blockDim.x) {
+        float v[8];
+        if (f.x_bf16) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(f.x) +
+                                                             static_cast<size_t>(t) * d + i0);
+            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
+            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
+        } else {
+            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(f.x) +
+                                                               static_cast<size_t>(t) * d + i0);
+            const float4 a = p[0], b = p[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+        reinterpret_cast<float4 *>(xs + i0)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4 *>(xs + i0)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
     __syncthreads();
     for (int r = blockIdx.x * 8 + warp; r <= E; r += gridDim.x * 8) {
         const uint16_t *w = r < E ? f.router + static_cast<size_t>(r) * d : f.shared_gate;
@@ -254,9 +266,21 @@ __global__ void __launch_bounds__(256, 1) k_decode_down(qk_fwd f) {
     pdl_trigger();
     const float4 *hg = reinterpret_cast<const float4 *>(f.h + static_cast<size_t>(t) * S * L.I);
     const int q4 = L.I / 4;
-    for (int c = threadIdx.x; c < S * q4; c += blockDim.x) {
-        const int s = c / q4, cc = c % q4, j = cc >> 3, q = cc & 7;
-        hs4[s * q4 + 8 * j + (q ^ (j & 7))] = hg[c];
+    for (int base = threadIdx.x; base < S * q4; base += 8 * blockDim.x) {
+        float4 v[8];  // loads before stores
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int c = base + u * blockDim.x;
+            if (c < S * q4) v[u] = hg[c];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int c = base + u * blockDim.x;
+            if (c < S * q4) {
+                const int s = c / q4, cc = c % q4, j = cc >> 3, q = cc & 7;
+                hs4[s * q4 + 8 * j + (q ^ (j & 7))] = v[u];
+            }
+        }
     }
     if (threadIdx.x < S)
         ws[threadIdx.x] = threadIdx.x < L.k ? f.wts[static_cast<size_t>(t) * L.k + threadIdx.x]
