@@ -128,6 +128,50 @@ int qmoe_forward_dev(qmoe_ctx *ctx, int layer, const void *x, int x_dtype,
 /* Waits for the context's work and reports any device-side error. */
 int qmoe_sync(qmoe_ctx *ctx, qmoe_err *err);
 
+/* ---- one decode token without any allocation (no counterpart in the
+ *      reference runtime) ----
+ * For callers that cannot call cudaMalloc: code that must run inside a
+ * device-memory budget or arena owned by someone else, or on a path where an
+ * allocation could block, fail or be forbidden at run time. qmoe_create
+ * allocates its workspaces; this entry point allocates nothing. The caller
+ * passes every input and output in device memory, including the experts
+ * already packed in the slot layout:
+ *   slot = GU section (I rows) then D section (d rows), zero-padded to
+ *   qmoe_slot_bytes(cfg);
+ *   GU row n = gate q row (d/2 bytes) | up q row (d/2 bytes) |
+ *              per group j < d/g: gate scale, gate bias, up scale, up bias
+ *              (4 bf16);
+ *   D row n  = down q row (I/2 bytes) | per group j < I/g: scale, bias
+ *              (2 bf16) | zeros to a multiple of 16 bytes;
+ *   q rows are the checkpoint rows verbatim (u32 words, low nibble first).
+ * The call's intermediates (router logits, routing, gate/up activations, a
+ * grid-barrier counter and an error word) live in one device array of
+ * QMOE_NOALLOC_SCRATCH_BYTES defined inside the library; every GPU that loads
+ * the library holds it until the process exits. A shape needing more than
+ * that (4 * ((E + 1) + 2k + 1 + (k + 1) * I) bytes plus 512) is rejected with
+ * an error, as is a shape the single-launch decode kernel does not cover.
+ * The first call on a device looks up the array's device address and sets
+ * kernel attributes, with that device current; make that first call before
+ * any stream capture. All calls share the array and each call starts by
+ * clearing its error word and barrier counter, so calls that overlap on the
+ * GPU race; serialise them. The call waits for its work on `stream` (NULL =
+ * the legacy default stream) and returns 0, or -1 with a message. */
+#define QMOE_NOALLOC_SCRATCH_BYTES (64u * 1024u)
+typedef struct {
+    int hidden, num_experts, top_k, moe_inter, group_size;
+    const void *x;               /* [1, d] device, QMOE_F32 or QMOE_BF16 */
+    int x_dtype;
+    float *out;                  /* [1, d] device fp32, overwritten */
+    const uint16_t *router;      /* [E, d] bf16 device */
+    const uint16_t *shared_gate; /* [d] bf16 device */
+    const float *logit_bias;     /* [E] device, or NULL */
+    const uint8_t *pool;         /* device base of the packed expert slots */
+    const int32_t *slot_of;      /* [E] device: slot index of each expert */
+    const uint8_t *shared_slot;  /* device: the packed shared expert */
+} qmoe_token_args;
+int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream,
+                               qmoe_err *err);
+
 /* Routing of the last forward call (waits for it): idx [n, k] in
  * (logit desc, expert asc) order, weights [n, k] (softmax renormalised over
  * the k, model.c:1305-1318), shared-gate sigmoid [n]. Any pointer may be NULL. */

@@ -74,6 +74,20 @@ class SynthSize(C.Structure):
                  "sh_q", "sh_sb", "sh_down_q", "sh_down_sb")]
 
 
+class TokenArgs(C.Structure):
+    """qmoe_token_args: one decode token for qmoe_forward_token_noalloc."""
+    _fields_ = [
+        ("hidden", C.c_int), ("num_experts", C.c_int), ("top_k", C.c_int),
+        ("moe_inter", C.c_int), ("group_size", C.c_int),
+        ("x", C.c_void_p), ("x_dtype", C.c_int), ("out", C.c_void_p),
+        ("router", C.c_void_p), ("shared_gate", C.c_void_p), ("logit_bias", C.c_void_p),
+        ("pool", C.c_void_p), ("slot_of", C.c_void_p), ("shared_slot", C.c_void_p),
+    ]
+
+
+NOALLOC_SCRATCH_BYTES = 64 * 1024
+
+
 # every symbol include/qmoe.h declares, with (restype, argtypes)
 _P = C.c_void_p
 SIGNATURES = {
@@ -85,6 +99,7 @@ SIGNATURES = {
     "qmoe_forward_dev": (C.c_int, [_P, C.c_int, _P, C.c_int, C.c_int, _P, _P, C.POINTER(Err)]),
     "qmoe_sync": (C.c_int, [_P, C.POINTER(Err)]),
     "qmoe_last_routing": (C.c_int, [_P, _P, _P, _P, C.POINTER(Err)]),
+    "qmoe_forward_token_noalloc": (C.c_int, [C.POINTER(TokenArgs), _P, C.POINTER(Err)]),
     "qmoe_capture_begin": (C.c_int, [_P, _P, C.POINTER(Err)]),
     "qmoe_capture_end": (_P, [_P, _P, C.POINTER(Err)]),
     "qmoe_graph_launch": (C.c_int, [_P, _P, C.POINTER(Err)]),
