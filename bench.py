@@ -45,6 +45,12 @@ METRIC = "MoE-layer decode tokens/s (batch 1)"
 UNIT = "tokens/s"
 
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
+# one ncu --set full capture of the kernel on this workload
+# (`ncu ... -k regex:k_decode_fused -s 8 -c 1 python bench.py --eager-tokens 20`)
+NCU_TRAFFIC = {"decode_fused": 21660416}
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -118,7 +124,7 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def cpu_reference_rate(x, budget_s=12.0, max_tokens=200, threads=None):
+def cpu_reference_rate(x, budget_s=12.0, max_tokens=1000, threads=None):
     """Times the reference's moe_forward (oracle/_ref) per token on the host
     cores, experts already dequantised in its cache (steady state). Falls back
     to the C restatement when the reference build is absent."""
@@ -198,6 +204,27 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_eager(n):
+    """Small case for ncu captures: n single-token forwards launched eagerly
+    on the config-1 layer (906 MB of experts, larger than L2)."""
+    import torch
+
+    import qmoe
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=1)
+    layer = qmoe.SynthLayer(cfg, SEED)
+    ctx = qmoe.Context(cfg)
+    ctx.upload(0, layer)
+    x = torch.from_numpy(qmoe.synth_tokens(SEED, 0, n, D)).cuda().to(torch.bfloat16)
+    out = torch.empty((n, D), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    for t in range(n):
+        ctx.forward_dev(0, x.data_ptr() + t * D * 2, qmoe.QMOE_BF16, 1, out.data_ptr() + t * D * 4,
+                        None)
+    ctx.sync()
+    ctx.close()
+    print(f"eager case: {n} tokens ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -205,9 +232,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--eager-tokens", type=int, default=0,
+                    help="profiling case: run N single-token forwards eagerly (no graph) and exit")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.eager_tokens:
+        run_eager(args.eager_tokens)
         return
 
     import torch
@@ -318,13 +350,7 @@ def main():
     kb = kernel_bytes_per_token()
     hbm, _, src = peaks()
     achieved = kb[dom] / (per_launch_ms[dom] / 1e3) / 1e9
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
-        try:
-            traffic = json.load(open(tpath)).get(dom)
-        except Exception:
-            traffic = None
+    traffic = NCU_TRAFFIC.get(dom)
     layer_gbs = layer_bytes_per_token() * (value / world) / 1e9
 
     cpu = None
