@@ -57,6 +57,9 @@ struct qmoe_ctx {
     int nfree;
     qmoe_cache *cache;
     uint8_t *host_store;   /* pinned [num_layers * E * slot_bytes] when streaming */
+    /* the pool holds nslots routed slots followed by one shared-expert slot
+       per layer (slot nslots + layer), so TMA descriptors cover both */
+    qk_prefill *prefill;   /* tcgen05 multi-token path, NULL if the shape is not covered */
     /* workspaces */
     float *x_dev, *out_dev, *logits, *wts, *sgate, *h;
     int32_t *idx;
@@ -183,7 +186,6 @@ void qmoe_destroy(qmoe_ctx *c) {
             cudaFree(c->layers[l].router);
             cudaFree(c->layers[l].shgate);
             cudaFree(c->layers[l].bias);
-            cudaFree(c->layers[l].shared_slot);
         }
         free(c->layers);
     }
@@ -211,6 +213,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     free(c->recent);
     free(c->recent_n);
     if (c->cache) qmoe_cache_free(c->cache);
+    qk_prefill_destroy(c->prefill);
     if (c->copy_done) cudaEventDestroy(c->copy_done);
     for (int i = 0; i < 8; i++)
         if (c->pev[i]) cudaEventDestroy(c->pev[i]);
@@ -291,7 +294,9 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
         }
         c->nslots = (int)want;
         c->resident_all = want == total;
-        CK(cudaMalloc((void **)&c->pool, (size_t)c->nslots * L->slot_bytes));
+        CK(cudaMalloc((void **)&c->pool, ((size_t)c->nslots + Lz) * L->slot_bytes));
+        for (int l = 0; l < Lz; l++)
+            c->layers[l].shared_slot = c->pool + ((size_t)c->nslots + l) * L->slot_bytes;
         CK(cudaMalloc((void **)&c->slot_of_dev, (size_t)total * sizeof(int32_t)));
         CK(cudaMemset(c->slot_of_dev, 0xff, (size_t)total * sizeof(int32_t)));
         c->slot_of_host = malloc((size_t)total * sizeof(int32_t));
@@ -333,6 +338,11 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaMallocHost((void **)&c->x_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->out_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->idx_pin, (size_t)T * L->k * sizeof(int32_t)));
+    if (T > 1) {
+        char msg[256] = {0};
+        c->prefill = qk_prefill_create(L, T, c->pool, c->nslots + Lz, c->num_sms, msg, sizeof(msg));
+        /* NULL: shape outside the grouped-GEMM kernels; the per-token path runs */
+    }
     return c;
 fail:
     qmoe_destroy(c);
@@ -466,9 +476,7 @@ static int upload_shared(qmoe_ctx *c, layer_dev *ld, const qmoe_layer_weights *w
     qk_pack_expert(L, w->sh_gate.q, w->sh_gate.scales, w->sh_gate.biases, w->sh_up.q,
                    w->sh_up.scales, w->sh_up.biases, w->sh_down.q, w->sh_down.scales,
                    w->sh_down.biases, buf);
-    cudaError_t ce = cudaSuccess;
-    if (!ld->shared_slot) ce = cudaMalloc((void **)&ld->shared_slot, L->slot_bytes);
-    if (ce == cudaSuccess) ce = cudaMemcpy(ld->shared_slot, buf, L->slot_bytes, cudaMemcpyHostToDevice);
+    cudaError_t ce = cudaMemcpy(ld->shared_slot, buf, L->slot_bytes, cudaMemcpyHostToDevice);
     free(buf);
     if (ce != cudaSuccess) {
         seterr(err, "qmoe_upload_layer: %s", cudaGetErrorString(ce));
@@ -697,6 +705,14 @@ int qmoe_forward_dev(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, 
         if (kerr(qk_launch_topk(&f, st, !prof), "topk", err)) return -1;
         PEV(2);
     }
+    if (c->prefill && n > 1) {
+        /* grouped tcgen05 path: grouping + gather, gate/up, down, combine */
+        void *ev[4] = {c->pev[3], c->pev[4], c->pev[5], c->pev[6]};
+        int rc = qk_launch_prefill(c->prefill, &f, c->nslots + layer, st, prof ? ev : NULL);
+        if (rc) return kerr(rc, "prefill", err);
+        c->prof_kernels = 6;
+        return 0;
+    }
     if (kerr(qk_launch_decode_gateup(&f, st, !prof), "decode_gateup", err)) return -1;
     PEV(3);
     if (kerr(qk_launch_decode_down(&f, st, !prof), "decode_down", err)) return -1;
@@ -813,7 +829,7 @@ int qmoe_profile_forward(qmoe_ctx *c, int layer, const void *x, int x_dtype, int
         return -1;
     }
     const int nk = c->prof_kernels;
-    double acc[4] = {0, 0, 0, 0};
+    double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int r = 0; r < reps; r++) {
         if (qmoe_graph_launch(g, NULL, err)) {
             qmoe_graph_free(g);
@@ -832,7 +848,7 @@ int qmoe_profile_forward(qmoe_ctx *c, int layer, const void *x, int x_dtype, int
         }
     }
     qmoe_graph_free(g);
-    for (int i = 0; i < max_kernels && i < nk; i++) kernel_us[i] = 1e3 * acc[i] / reps;
+    for (int i = 0; i < max_kernels && i < nk && i < 8; i++) kernel_us[i] = 1e3 * acc[i] / reps;
     if (kernels) *kernels = nk;
     return check_dev_err(c, c->stream, err);
 }

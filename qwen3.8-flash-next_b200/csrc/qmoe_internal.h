@@ -92,6 +92,22 @@ int qk_launch_decode_down(const qk_fwd *f, void *stream, int pdl);
 #define QK_FUSED_UNFIT (-7)
 int qk_launch_decode_fused(const qk_fwd *f, unsigned *gbar, void *stream, int pdl);
 
+/* Prefill / multi-token path (qmoe_prefill.cu): tokens grouped by expert, a
+ * tcgen05 grouped GEMM for gate/up (SiLU x up epilogue) and for down, and a
+ * gather-combine. The plan owns its workspaces (sized for max_tokens) and
+ * the TMA descriptors over the pool; created once per context. */
+typedef struct qk_prefill qk_prefill;
+/* pool: base of pool_slots slots (routed slots and one shared slot per layer) */
+qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, const uint8_t *pool,
+                              int pool_slots, int num_sms, char *msg, size_t msg_len);
+void qk_prefill_destroy(qk_prefill *p);
+/* Runs everything after routing (f->idx, f->wts, f->sgate must be ready in
+ * stream order); shared_slot_index: the pool slot of this layer's shared
+ * expert. events: NULL, or 4 cudaEvent_t recorded after grouping+gather,
+ * gate/up GEMM, down GEMM and combine (diagnostics). */
+int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream,
+                      void **events);
+
 /* internal cache helper: replace the value of an existing key */
 struct qmoe_cache;
 int qmoe__cache_set_value(struct qmoe_cache *c, uint64_t key, uint64_t value);

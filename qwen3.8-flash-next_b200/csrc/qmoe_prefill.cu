@@ -1,0 +1,728 @@
+// qmoe_prefill.cu - the multi-token MoE layer on the 5th-generation tensor
+// cores (tcgen05, accumulators in tensor memory).
+//
+// Reference path: moe_forward, c/src/model.c:1281-1405, for n > 1 tokens.
+// After routing (router + top-k kernels in qmoe_kernels.cu):
+//   k_count      per-expert token counts                 (model.c:1321-1332)
+//   k_plan       row offsets of each expert group and the M-tile list
+//   k_positions  stable token -> row permutation per expert, in token order
+//                (model.c:1354-1367 gathers the same rows)
+//   k_gather     x rows -> fp16 A operand, grouped by expert; the shared
+//                expert's group is every token in order
+//   k_gemm<GU>   H = SiLU(X_e Wg_e^T) * (X_e Wu_e^T)           (model.c:1371-1374)
+//   k_gemm<DN>   Y = H_e Wd_e^T                                (model.c:1375)
+//   k_combine    out[t] = sum_s w[t,s] Y[row(t,s)] + sigmoid(g_t) Y_sh[t]
+//                in a fixed order (model.c:1376-1386, :1396-1402)
+//
+// Grouped GEMM (one persistent kernel, one CTA per SM, 10 warps):
+//   warp 0     TMA producer: the A tile (128 rows x 64 fp16, 128-byte swizzle)
+//              and the packed q4 rows + scales of the B tile, per stage
+//   warp 1     allocates 512 TMEM columns; one thread issues tcgen05.mma
+//              (M=128, N=256, K=16 x 4 per stage) and tcgen05.commit
+//   warps 2-5  dequantise q4 -> fp16 into the canonical K-major 128-byte
+//              swizzled layout (w = q*s + b, exact for b = -8s)
+//   warps 6-9  epilogue: tcgen05.ld of the accumulator (double-buffered in
+//              TMEM); gate/up: SiLU(g)*u stored as fp16 (the down GEMM's A
+//              operand); down: fp32 stores (keeps the combine at fp32)
+// Three stages of 60 KB in shared memory; every wait is bounded.
+//
+// Inside each 8-element chunk along K, the fp16 operands use the element
+// order [0,4,1,5,2,6,3,7]: the dequantiser then builds two fp16 values per
+// LOP3 (nibbles i and i+4 of a q4 word). X and H are written in the same
+// order, so the products pair up as in the natural order.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "qmoe_dev.cuh"
+
+using namespace qk;
+
+cudaError_t qk_launch_raw(const void *fn, dim3 grid, dim3 block, size_t smem, void *stream,
+                          int pdl, void **args);
+
+namespace {
+
+constexpr int BM = 128;           // token rows per tile
+constexpr int BK = 64;            // K per stage: one 128-byte swizzle row of fp16
+constexpr int BN = 256;           // accumulator columns (gate|up, or down outputs)
+constexpr int NS = 3;             // pipeline stages
+constexpr int kThreads = 320;     // 10 warps
+constexpr int kA = BM * BK * 2;   // 16 KB
+constexpr int kBf = BN * BK * 2;  // 32 KB
+constexpr int kBq = BN * 32;      // 8 KB packed q4
+constexpr int kBs = BN * 16;      // 4 KB scales
+// Per-mode stage layout. The down GEMM's A operand is H as an fp16 hi/lo pair
+// (H = hi + lo to about 22 significant bits), two A tiles per stage and two
+// MMAs per K step against the same dequantised B tile; it runs 2 stages.
+template <int MODE>
+struct Cfg {
+    static constexpr int NSt = MODE ? 2 : 3;
+    static constexpr int A = MODE ? 2 * kA : kA;
+    static constexpr int Stage = A + kBf + kBq + kBs;
+    static constexpr int Smem = NSt * Stage + 1024;  // + alignment slack
+};
+
+struct MTile {
+    int m0;    // first row in the grouped buffers
+    int rows;  // valid rows (<= 128)
+    int slot;  // pool slot of the expert
+    int pad;
+};
+
+struct GemmArgs {
+    int mode;   // 0: gate/up, 1: down
+    int KB;     // K / 64
+    int NT;     // N-tiles per M-tile
+    int ld_out; // output row length (elements)
+    int d, I;
+    const MTile *tiles;
+    const int *n_mtiles;
+    int rows_max;       // rows of one plane of the grouped buffers
+    size_t lo_plane;    // gate/up: element offset of H's lo plane
+    __half *out;   // gate/up: H (fp16 hi and lo planes, permuted chunks)
+    float *outf;   // down: Y (fp32)
+    int *err;
+};
+
+QK_DEV uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+QK_DEV __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// One q4 word (8 nibbles, k = 8c..8c+7) -> 8 fp16 in the order
+// [0,4,1,5,2,6,3,7], each w = q*s + b (one rounding; exact when b = -8s).
+QK_DEV uint4 dequant_word(uint32_t w, __half2 s2, __half2 b2) {
+    const __half2 k1024 = u2h(0x64006400u);   // {1024, 1024}
+    const __half2 k16th = u2h(0x2C002C00u);   // {1/16, 1/16}
+    const __half2 km64 = u2h(0xD400D400u);    // {-64, -64}
+    const uint32_t w8 = w >> 8;
+    const __half2 q04 = __hsub2(u2h((w & 0x000F000Fu) | 0x64006400u), k1024);
+    const __half2 q15 = __hfma2(u2h((w & 0x00F000F0u) | 0x64006400u), k16th, km64);
+    const __half2 q26 = __hsub2(u2h((w8 & 0x000F000Fu) | 0x64006400u), k1024);
+    const __half2 q37 = __hfma2(u2h((w8 & 0x00F000F0u) | 0x64006400u), k16th, km64);
+    uint4 o;
+    o.x = h2u(__hfma2(q04, s2, b2));
+    o.y = h2u(__hfma2(q15, s2, b2));
+    o.z = h2u(__hfma2(q26, s2, b2));
+    o.w = h2u(__hfma2(q37, s2, b2));
+    return o;
+}
+
+// Row r of a K-major, 128-byte-swizzled tile: 16-byte chunk c lives at
+// (r / 8) * 1024 + (r % 8) * 128 + ((c ^ (r % 8)) * 16).
+QK_DEV uint32_t sw128(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
+
+QK_DEV void dequant_row(const uint8_t *q32, float s, float b, uint8_t *bf, int r) {
+    const uint4 qa = *reinterpret_cast<const uint4 *>(q32);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(q32 + 16);
+    const __half2 s2 = __float2half2_rn(s), b2 = __float2half2_rn(b);
+    const uint32_t wd[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4 *>(bf + sw128(r, c)) = dequant_word(wd[c], s2, b2);
+}
+
+// The 16 values v (natural order, columns j0..j0+15) -> two 16-byte chunks
+// in the order [0,4,1,5,2,6,3,7].
+QK_DEV void pack_perm16(const float *v, uint4 *o) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const float *p = v + 8 * h;
+        o[h].x = h2u(__floats2half2_rn(p[0], p[4]));
+        o[h].y = h2u(__floats2half2_rn(p[1], p[5]));
+        o[h].z = h2u(__floats2half2_rn(p[2], p[6]));
+        o[h].w = h2u(__floats2half2_rn(p[3], p[7]));
+    }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
+           const __grid_constant__ CUtensorMap tmS, GemmArgs g) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t full[NS], ready[NS], empty[NS], acc_full[2], acc_empty[2], drain;
+    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag_;
+    volatile int &abort_flag = abort_flag_;
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&ready[s], 4);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(&drain, 1);
+        abort_flag = 0;
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    const int ntiles = *g.n_mtiles * g.NT;
+    const int KB = g.KB;
+    constexpr int NSm = Cfg<MODE>::NSt;
+    constexpr int kAm = Cfg<MODE>::A;
+    constexpr int kSt = Cfg<MODE>::Stage;
+
+    if (warp == 0) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            int it = 0;
+            int last_it[NS];
+            for (int s = 0; s < NS; ++s) last_it[s] = -1;
+            for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
+                const MTile mt = g.tiles[tile / g.NT];
+                const int nt = tile % g.NT;
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int s = it % NSm;
+                    const uint32_t ph = (it / NSm) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1)) {
+                        atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                        abort_flag = 1;
+                        break;
+                    }
+                    uint8_t *st = smem + s * kSt;
+                    uint8_t *A = st, *Bq = st + kAm + kBf, *Bs = Bq + kBq;
+                    if (MODE == 0) {
+                        mbar_expect_tx(&full[s], kA + 2 * (128 * 32) + 128 * 16);
+                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &full[s]);
+                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 128, mt.slot, &full[s]);
+                        tma_load_3d(Bq + 128 * 32, &tmQ, g.d / 2 + kb * 32, nt * 128, mt.slot,
+                                    &full[s]);
+                        tma_load_3d(Bs, &tmS, g.d + 16 * (kb >> 1), nt * 128, mt.slot, &full[s]);
+                    } else {
+                        mbar_expect_tx(&full[s], 2 * kA + 256 * 32 + 256 * 16);
+                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &full[s]);                   // hi
+                        tma_load_2d(A + kA, &tmA, kb * BK, g.rows_max + mt.m0, &full[s]);  // lo
+                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 256, mt.slot, &full[s]);
+                        tma_load_3d(Bs, &tmS, g.I / 2 + 16 * (kb >> 2), nt * 256, mt.slot, &full[s]);
+                    }
+                    last_it[s] = it;
+                }
+            }
+            // every load this thread issued has landed before the CTA exits
+            for (int s = 0; s < NSm; ++s)
+                if (last_it[s] >= 0) mbar_wait(&full[s], (last_it[s] / NSm) & 1);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        const uint32_t idesc = idesc_f16(BM, BN);
+        int it = 0, lt = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
+            const int buf = lt & 1;
+            const uint32_t aph = (lt >> 1) & 1;
+            if (!mbar_wait(&acc_empty[buf], aph ^ 1)) {
+                if (lane == 0) {
+                    atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const uint32_t dt = tmem + buf * BN;
+            bool ok = true;
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                const int s = it % NSm;
+                const uint32_t ph = (it / NSm) & 1;
+                if (!mbar_wait(&full[s], ph) || !mbar_wait(&ready[s], ph)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a0 = smem_addr(smem + s * kSt);
+                    const uint32_t b0 = a0 + kAm;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        umma_f16(dt, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
+                                 (kb | kk) != 0);
+                        if (MODE == 1)  // lo plane of H, same B
+                            umma_f16(dt, sdesc_sw128(a0 + kA + kk * 32), sdesc_sw128(b0 + kk * 32),
+                                     idesc, 1u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                __syncwarp();
+            }
+            if (!ok) {
+                if (lane == 0) {
+                    atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            if (lane == 0) umma_commit(&acc_full[buf]);
+            __syncwarp();
+        }
+        // every MMA this thread issued has completed before TMEM is freed
+        if (lane == 0) {
+            umma_commit(&drain);
+            mbar_wait(&drain, 0);
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        // ---------------- dequantisers: 128 threads, rows t and t + 128
+        const int t = tid - 64;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
+            bool ok = true;
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                const int s = it % NSm;
+                const uint32_t ph = (it / NSm) & 1;
+                if (!mbar_wait(&full[s], ph)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *st = smem + s * kSt;
+                uint8_t *Bf = st + kAm, *Bq = st + kAm + kBf, *Bs = Bq + kBq;
+                if (MODE == 0) {
+                    // gate row t -> B row t, up row t -> B row 128 + t; the 16
+                    // scale bytes hold the quads of groups 2j and 2j+1
+                    const uint2 quad = *reinterpret_cast<const uint2 *>(Bs + t * 16 + 8 * (kb & 1));
+                    dequant_row(Bq + t * 32, bf16lo(quad.x), bf16hi(quad.x), Bf, t);
+                    dequant_row(Bq + 128 * 32 + t * 32, bf16lo(quad.y), bf16hi(quad.y), Bf, 128 + t);
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int r = t + 128 * h;
+                        const uint32_t pr = *reinterpret_cast<const uint32_t *>(Bs + r * 16 + 4 * (kb & 3));
+                        dequant_row(Bq + r * 32, bf16lo(pr), bf16hi(pr), Bf, r);
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ready[s]);
+            }
+            if (!ok) {
+                if (lane == 0) {
+                    atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                    abort_flag = 1;
+                }
+                break;
+            }
+        }
+    } else {
+        // ---------------- epilogue: 128 threads = 128 accumulator rows
+        const int q = warp & 3;  // TMEM lanes [32q, 32q + 32)
+        const int row = 32 * q + lane;
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
+            const MTile mt = g.tiles[tile / g.NT];
+            const int nt = tile % g.NT;
+            const int buf = lt & 1;
+            const uint32_t aph = (lt >> 1) & 1;
+            if (!mbar_wait(&acc_full[buf], aph)) {
+                if (lane == 0) {
+                    atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tbase = tmem + (static_cast<uint32_t>(32 * q) << 16) + buf * BN;
+            const bool live = row < mt.rows;
+            const size_t orow_i = static_cast<size_t>(mt.m0 + (live ? row : 0)) * g.ld_out;
+            if (MODE == 0) {
+                __half *orow = g.out + orow_i;
+                for (int c = 0; c < 128; c += 16) {
+                    float gv[16], uv[16], hv[16];
+                    tmem_ld16(tbase + c, gv);
+                    tmem_ld16(tbase + 128 + c, uv);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) hv[i] = (gv[i] / (1.0f + expf(-gv[i]))) * uv[i];
+                    // hi = fp16(h), lo = fp16(h - hi): the pair carries h to ~22 bits
+                    float lv[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) lv[i] = hv[i] - __half2float(__float2half_rn(hv[i]));
+                    uint4 o[2], ol[2];
+                    pack_perm16(hv, o);
+                    pack_perm16(lv, ol);
+                    if (live) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(orow + nt * 128 + c);
+                        dst[0] = o[0];
+                        dst[1] = o[1];
+                        uint4 *dl = reinterpret_cast<uint4 *>(orow + g.lo_plane + nt * 128 + c);
+                        dl[0] = ol[0];
+                        dl[1] = ol[1];
+                    }
+                }
+            } else {
+                float *orow = g.outf + orow_i;
+                for (int c = 0; c < 256; c += 16) {
+                    float yv[16];
+                    tmem_ld16(tbase + c, yv);
+                    tmem_wait_ld();
+                    if (live) {
+                        float4 *dst = reinterpret_cast<float4 *>(orow + nt * 256 + c);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            dst[i] = make_float4(yv[4 * i], yv[4 * i + 1], yv[4 * i + 2], yv[4 * i + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+    }
+    // drain: let every issued TMA load and MMA finish before TMEM and shared
+    // memory go away (bounded)
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// routing -> groups
+
+__global__ void k_count(const int32_t *idx, int nk, int *counts) {
+    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < nk; a += gridDim.x * blockDim.x)
+        atomicAdd(counts + idx[a], 1);
+}
+
+// One CTA (1024 threads, E + 1 <= 1024 groups). Group 0 is the shared expert
+// (every token, rows [0, T)); group 1 + e is routed expert e. Writes the
+// first row of each routed expert and the M-tile list.
+__global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int T,
+                                               const int32_t *slot_of, int shared_slot,
+                                               int *row0, MTile *tiles, int *n_mtiles) {
+    __shared__ int s_scan[1024], s_tscan[1024];
+    const int g = threadIdx.x;
+    const int rows = g == 0 ? T : (g <= E ? counts[g - 1] : 0);
+    const int mt = (rows + BM - 1) / BM;
+    s_scan[g] = rows;
+    s_tscan[g] = mt;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+        const int a = g >= off ? s_scan[g - off] : 0;
+        const int b = g >= off ? s_tscan[g - off] : 0;
+        __syncthreads();
+        s_scan[g] += a;
+        s_tscan[g] += b;
+        __syncthreads();
+    }
+    const int r0 = s_scan[g] - rows, t0 = s_tscan[g] - mt;
+    if (g >= 1 && g <= E) row0[g - 1] = r0;
+    const int slot = g == 0 ? shared_slot : (g <= E ? slot_of[g - 1] : -1);
+    for (int i = 0; i < mt; ++i) {
+        MTile m;
+        m.m0 = r0 + BM * i;
+        m.rows = min(BM, rows - BM * i);
+        m.slot = slot;
+        m.pad = 0;
+        tiles[t0 + i] = m;
+    }
+    if (g == 1023) *n_mtiles = s_tscan[1023];
+}
+
+// One CTA per routed expert: its (token, slot) assignments in token order
+// get consecutive rows (a stable, deterministic permutation).
+__global__ void __launch_bounds__(1024) k_positions(const int32_t *idx, int nk, int k,
+                                                    const int *row0, int *inv, int *perm_tok) {
+    __shared__ int s_warp[32];
+    __shared__ int s_base;
+    const int e = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_base = row0[e];
+    __syncthreads();
+    for (int a0 = 0; a0 < nk; a0 += 1024) {
+        const int a = a0 + threadIdx.x;
+        const bool mine = a < nk && idx[a] == e;
+        const unsigned m = __ballot_sync(QK_FULL, mine);
+        if (lane == 0) s_warp[warp] = __popc(m);
+        __syncthreads();
+        if (warp == 0) {
+            int v = s_warp[lane];
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int t = __shfl_up_sync(QK_FULL, v, off);
+                if (lane >= off) v += t;
+            }
+            s_warp[lane] = v;  // inclusive
+        }
+        __syncthreads();
+        const int before = (warp ? s_warp[warp - 1] : 0) + __popc(m & ((1u << lane) - 1u));
+        if (mine) {
+            const int pos = s_base + before;
+            inv[a] = pos;
+            perm_tok[pos] = a / k;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) s_base += s_warp[31];
+        __syncthreads();
+    }
+}
+
+// Grouped fp16 A operand: row r holds token r (r < T, shared group) or
+// perm_tok[r]; each 8-element chunk in the order [0,4,1,5,2,6,3,7].
+__global__ void k_gather(const void *x, int x_bf16, int d, int T, int rows, const int *perm_tok,
+                         __half *xp) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const int tok = warp < T ? warp : perm_tok[warp];
+    __half *dst = xp + static_cast<size_t>(warp) * d;
+    for (int c = lane; c < d / 8; c += 32) {
+        float v[8];
+        if (x_bf16) {
+            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
+                                                            static_cast<size_t>(tok) * d)[c];
+            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
+            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
+        } else {
+            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
+                                                               static_cast<size_t>(tok) * d) + 2 * c;
+            const float4 a = p[0], b = p[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+        uint4 o;
+        o.x = h2u(__floats2half2_rn(v[0], v[4]));
+        o.y = h2u(__floats2half2_rn(v[1], v[5]));
+        o.z = h2u(__floats2half2_rn(v[2], v[6]));
+        o.w = h2u(__floats2half2_rn(v[3], v[7]));
+        reinterpret_cast<uint4 *>(dst)[c] = o;
+    }
+}
+
+// out[t] = sum_s w[t,s] * Y[inv[t,s]] + sigmoid(g_t) * Y[t] (the shared
+// expert's rows come first in Y), fixed order; one CTA per token, 4 columns
+// per thread, all row loads of a thread issued before the sums.
+__global__ void k_combine(const float *Y, const int *inv, const float *wts, const float *sgate,
+                          int k, int d, float *out) {
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x; c < d / 4; c += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 <= k; s0 += 4) {
+            float4 v[4];
+            float w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int s = s0 + u;
+                if (s <= k) {
+                    const int row = s < k ? inv[t * k + s] : t;
+                    w[u] = s < k ? wts[t * k + s] : sgate[t];
+                    v[u] = reinterpret_cast<const float4 *>(Y + static_cast<size_t>(row) * d)[c];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (s0 + u <= k) {
+                    acc.x = fmaf(w[u], v[u].x, acc.x);
+                    acc.y = fmaf(w[u], v[u].y, acc.y);
+                    acc.z = fmaf(w[u], v[u].z, acc.z);
+                    acc.w = fmaf(w[u], v[u].w, acc.w);
+                }
+            }
+        }
+        reinterpret_cast<float4 *>(out + static_cast<size_t>(t) * d)[c] = acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+typedef CUresult (*encode_fn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                              const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                              const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+encode_fn get_encode() {
+    static encode_fn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<encode_fn>(p);
+    }
+    return fn;
+}
+
+bool map_2d_f16(CUtensorMap *m, void *base, uint64_t cols, uint64_t rows) {
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {BK, BM};
+    const cuuint32_t es[2] = {1, 1};
+    return get_encode()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool map_3d_u8(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t rows,
+               uint64_t slots, uint64_t slot_stride, uint32_t box_x, uint32_t box_y) {
+    const cuuint64_t dims[3] = {row_bytes, rows, slots};
+    const cuuint64_t strides[2] = {row_bytes, slot_stride};
+    const cuuint32_t box[3] = {box_x, box_y, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return get_encode()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims,
+                        strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+struct qk_prefill {
+    qk_layout L;
+    int max_tokens, num_sms, pool_slots, rows_max, tiles_max;
+    int *counts, *row0, *inv, *perm_tok, *n_mtiles;
+    MTile *tiles;
+    __half *xp, *H;
+    float *Y;
+    CUtensorMap tmX, tmH, tmQgu, tmSgu, tmQdn, tmSdn;
+};
+
+extern "C" void qk_prefill_destroy(qk_prefill *p) {
+    if (!p) return;
+    cudaFree(p->counts);
+    cudaFree(p->row0);
+    cudaFree(p->inv);
+    cudaFree(p->perm_tok);
+    cudaFree(p->n_mtiles);
+    cudaFree(p->tiles);
+    cudaFree(p->xp);
+    cudaFree(p->H);
+    cudaFree(p->Y);
+    delete p;
+}
+
+extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, const uint8_t *pool,
+                                         int pool_slots, int num_sms, char *msg, size_t msg_len) {
+    // shapes the kernels cover: I a multiple of 128, d a multiple of 256
+    if (L->I % 128 || L->d % 256 || L->g != 64 || L->E + 1 > 1024) {
+        snprintf(msg, msg_len, "prefill path needs I %% 128 == 0, d %% 256 == 0, g == 64, E < 1024");
+        return nullptr;
+    }
+    if (!get_encode()) {
+        snprintf(msg, msg_len, "cuTensorMapEncodeTiled unavailable");
+        return nullptr;
+    }
+    qk_prefill *p = new qk_prefill();
+    memset(p, 0, sizeof(*p));
+    p->L = *L;
+    p->max_tokens = max_tokens;
+    p->num_sms = num_sms;
+    p->pool_slots = pool_slots;
+    p->rows_max = max_tokens * (L->k + 1);
+    p->tiles_max = p->rows_max / BM + L->E + 2;
+    const size_t R = static_cast<size_t>(p->rows_max);
+    cudaError_t e = cudaSuccess;
+    if (e == cudaSuccess) e = cudaMalloc(&p->counts, sizeof(int) * (L->E + 1));
+    if (e == cudaSuccess) e = cudaMalloc(&p->row0, sizeof(int) * (L->E + 1));
+    if (e == cudaSuccess) e = cudaMalloc(&p->inv, sizeof(int) * static_cast<size_t>(max_tokens) * L->k);
+    if (e == cudaSuccess) e = cudaMalloc(&p->perm_tok, sizeof(int) * R);
+    if (e == cudaSuccess) e = cudaMalloc(&p->n_mtiles, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&p->tiles, sizeof(MTile) * p->tiles_max);
+    if (e == cudaSuccess) e = cudaMalloc(&p->xp, R * L->d * sizeof(__half));
+    if (e == cudaSuccess) e = cudaMalloc(&p->H, 2 * R * L->I * sizeof(__half));  // hi, lo planes
+    if (e == cudaSuccess) e = cudaMalloc(&p->Y, R * L->d * sizeof(float));
+    if (e != cudaSuccess) {
+        snprintf(msg, msg_len, "prefill workspace: %s", cudaGetErrorString(e));
+        qk_prefill_destroy(p);
+        return nullptr;
+    }
+    bool ok = map_2d_f16(&p->tmX, p->xp, L->d, R) && map_2d_f16(&p->tmH, p->H, L->I, 2 * R) &&
+              map_3d_u8(&p->tmQgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 32, 128) &&
+              map_3d_u8(&p->tmSgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 16, 128) &&
+              map_3d_u8(&p->tmQdn, pool + L->gu_bytes, L->d_row, L->d, pool_slots, L->slot_bytes, 32,
+                        256) &&
+              map_3d_u8(&p->tmSdn, pool + L->gu_bytes, L->d_row, L->d, pool_slots, L->slot_bytes, 16,
+                        256);
+    if (!ok) {
+        snprintf(msg, msg_len, "prefill: tensor map encoding failed");
+        qk_prefill_destroy(p);
+        return nullptr;
+    }
+    const void *fns[2] = {reinterpret_cast<const void *>(&k_gemm<0>),
+                          reinterpret_cast<const void *>(&k_gemm<1>)};
+    const int smem[2] = {Cfg<0>::Smem, Cfg<1>::Smem};
+    for (int i = 0; i < 2; ++i) {
+        e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem[i]);
+        if (e != cudaSuccess) {
+            snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
+            qk_prefill_destroy(p);
+            return nullptr;
+        }
+    }
+    return p;
+}
+
+extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot_index,
+                                 void *stream, void **events) {
+    const qk_layout &L = p->L;
+    const int T = f->T, k = L.k, E = L.E;
+    if (T > p->max_tokens) return cudaErrorInvalidValue;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // diagnostics: events[0..3] bracket grouping+gather, gate/up, down, combine
+    auto mark = [&](int i) {
+        if (events) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), st,
+                                             cudaEventRecordExternal);
+    };
+    cudaError_t e = cudaMemsetAsync(p->counts, 0, sizeof(int) * (E + 1), st);
+    if (e != cudaSuccess) return e;
+    const int nk = T * k;
+    k_count<<<(nk + 255) / 256, 256, 0, st>>>(f->idx, nk, p->counts);
+    k_plan<<<1, 1024, 0, st>>>(p->counts, E, T, f->slot_of, shared_slot_index, p->row0, p->tiles,
+                               p->n_mtiles);
+    k_positions<<<E, 1024, 0, st>>>(f->idx, nk, k, p->row0, p->inv, p->perm_tok);
+    const int rows = T * (k + 1);
+    k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, rows, p->perm_tok,
+                                                     p->xp);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    mark(0);
+
+    GemmArgs gu;
+    gu.mode = 0;
+    gu.KB = L.d / BK;
+    gu.NT = L.I / 128;
+    gu.ld_out = L.I;
+    gu.d = L.d;
+    gu.I = L.I;
+    gu.tiles = p->tiles;
+    gu.n_mtiles = p->n_mtiles;
+    gu.rows_max = p->rows_max;
+    gu.lo_plane = static_cast<size_t>(p->rows_max) * L.I;
+    gu.out = p->H;
+    gu.outf = nullptr;
+    gu.err = f->err;
+    {
+        void *args[] = {&p->tmX, &p->tmQgu, &p->tmSgu, &gu};
+        e = qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<0>), dim3(p->num_sms),
+                          dim3(kThreads), Cfg<0>::Smem, stream, 0, args);
+        if (e != cudaSuccess) return e;
+    }
+    mark(1);
+    GemmArgs dn = gu;
+    dn.mode = 1;
+    dn.KB = L.I / BK;
+    dn.NT = L.d / 256;
+    dn.ld_out = L.d;
+    dn.out = nullptr;
+    dn.outf = p->Y;
+    {
+        void *args[] = {&p->tmH, &p->tmQdn, &p->tmSdn, &dn};
+        e = qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<1>), dim3(p->num_sms),
+                          dim3(kThreads), Cfg<1>::Smem, stream, 0, args);
+        if (e != cudaSuccess) return e;
+    }
+    mark(2);
+    k_combine<<<T, 256, 0, st>>>(p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
+    mark(3);
+    return cudaGetLastError();
+}

@@ -65,16 +65,17 @@ def case(name, d, E, k, I, n, stream, zipf=None):
     ref.lib.ref_reset_cache()
 
 
-def route_case(name, d, E, k, I, n, stream, zipf):
+def route_case(name, d, E, k, I, n, stream, zipf, weights=True):
     cfg = qmoe.make_config(d, E, k, I, max_tokens=n)
     s = qmoe.SynthLayer(cfg, SEED, 0, zipf_s=zipf)
     x = qmoe.synth_tokens(SEED, stream, n, d)
     idx, w, lg = oracle.restatement().route(s, x)
     si, sw = sorted_routing(idx, w)
     counts = np.bincount(idx.ravel(), minlength=E).astype(np.int32)
-    np.savez_compressed(os.path.join(HERE, name), idx_sorted=si, w_sorted=sw, counts=counts,
+    extra = {"w_sorted": sw} if weights else {}
+    np.savez_compressed(os.path.join(HERE, name), idx_sorted=si.astype(np.int16), counts=counts,
                         x_sha=hashlib.sha256(x.tobytes()).hexdigest(),
-                        shape=np.array([d, E, k, I, 64, n, stream]), seed=SEED)
+                        shape=np.array([d, E, k, I, 64, n, stream]), seed=SEED, **extra)
 
 
 if __name__ == "__main__":
@@ -84,4 +85,6 @@ if __name__ == "__main__":
     case("moe_cfg0.npz", 256, 16, 4, 128, 32, 0)
     case("moe_cfg1_tokens.npz", 2048, 512, 10, 512, 4, 1)
     route_case("moe_cfg2_route.npz", 2048, 512, 10, 512, 64, 2, 1.1)
+    # every token of configuration 2 (4096 tokens): sets and counts
+    route_case("moe_cfg2_full_route.npz", 2048, 512, 10, 512, 4096, 3, 1.1, weights=False)
     print("golden fixtures written to", HERE)

@@ -100,15 +100,57 @@ def test_cfg1_decode_matches_restatement(cfg1_layer, cfg1_ctx):
 
 
 def test_batch_equals_token_by_token(cfg1_layer, cfg1_ctx):
-    """A multi-token call equals the same tokens one at a time (prefill ==
-    decode, as c/tests/test_model.c:300-333 checks for the whole model)."""
+    """A multi-token call (tcgen05 grouped path, fp16 operands) equals the same
+    tokens one at a time (fp32 decode path) within the parity tolerance, with
+    identical routing (prefill == decode, as c/tests/test_model.c:300-333
+    checks for the whole model)."""
     import qmoe
     s, seed = cfg1_layer
     x = qmoe.synth_tokens(seed, 12, 24, 2048)
     full = cfg1_ctx.forward(0, x)
+    idx_full, w_full, _ = cfg1_ctx.routing(24)
     for t in range(0, 24, 5):
         one = cfg1_ctx.forward(0, x[t:t + 1])
-        np.testing.assert_allclose(one[0], full[t], rtol=1e-6, atol=1e-6)
+        idx1, w1, _ = cfg1_ctx.routing(1)
+        assert np.array_equal(idx1[0], idx_full[t])
+        _close(full[t:t + 1], one)
+
+
+def test_prefill_cfg1_shapes_matches_restatement(cfg1_layer, cfg1_ctx):
+    """64 tokens through the grouped tcgen05 path against the C restatement."""
+    import oracle
+    import qmoe
+    s, seed = cfg1_layer
+    x = qmoe.synth_tokens(seed, 15, 64, 2048)
+    out = cfg1_ctx.forward(0, x)
+    idx, w, _ = cfg1_ctx.routing(64)
+    ro, ri, rw = oracle.restatement().forward(s, x)
+    assert np.array_equal(idx, ri)
+    np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-6)
+    _close(out, ro)
+
+
+def test_prefill_cfg2_full_zipf(built):
+    """Config 2: 4096 tokens, Zipf(1.1) router bias. Routing of every token
+    (sorted sets and per-expert counts) equals the golden; a spread sample
+    of token outputs matches the restatement."""
+    import oracle
+    import qmoe
+    g, (d, E, k, I, gs, n, stream), seed = _golden("moe_cfg2_full_route.npz")
+    s = qmoe.SynthLayer(qmoe.make_config(d, E, k, I, gs, max_tokens=n), seed, zipf_s=1.1)
+    x = qmoe.synth_tokens(seed, stream, n, d)
+    ctx = qmoe.Context(qmoe.make_config(d, E, k, I, gs, max_tokens=n))
+    ctx.upload(0, s)
+    out = ctx.forward(0, x)
+    idx, w, _ = ctx.routing(n)
+    si, _ = _sorted(idx, w)
+    assert np.array_equal(np.bincount(idx.ravel(), minlength=E), g["counts"])
+    assert np.array_equal(si.astype(np.int16), g["idx_sorted"])
+    sample = np.linspace(0, n - 1, 24).astype(int)
+    ro, ri, rw = oracle.restatement().forward(s, x[sample])
+    assert np.array_equal(idx[sample], ri)
+    _close(out[sample], ro)
+    ctx.close()
 
 
 def test_cfg2_zipf_routing_bit_exact(built):
