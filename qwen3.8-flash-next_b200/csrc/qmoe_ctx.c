@@ -16,6 +16,7 @@
  * time, so a forward call allocates nothing.
  */
 #include <cuda_runtime_api.h>
+#include <math.h>
 #include <pthread.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -33,6 +34,7 @@ typedef struct {
     uint16_t *shgate;     /* [d] */
     float *bias;          /* [E] or NULL */
     uint8_t *shared_slot; /* slot layout */
+    float router_wmax;    /* max_e |router row e|_2, rounded up */
     int ready;
 } layer_dev;
 
@@ -466,6 +468,24 @@ static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qm
 
 /* ----------------------------------------------------------------- upload */
 
+/* Largest 2-norm of a router row (bf16), in fp64, rounded up to fp32 with a
+ * margin: the error bound of the tensor-core routing scales with it. */
+static float router_wmax(const uint16_t *router, int E, int d) {
+    double best = 0.0;
+    for (int e = 0; e < E; e++) {
+        double ss = 0.0;
+        for (int i = 0; i < d; i++) {
+            uint32_t b = (uint32_t)router[(size_t)e * d + i] << 16;
+            float f;
+            memcpy(&f, &b, 4);
+            ss += (double)f * (double)f;
+        }
+        if (ss > best) best = ss;
+    }
+    float r = (float)(sqrt(best) * (1.0 + 1e-6));
+    return isfinite(r) ? nextafterf(r, INFINITY) : INFINITY;
+}
+
 static int upload_shared(qmoe_ctx *c, layer_dev *ld, const qmoe_layer_weights *w, qmoe_err *err) {
     const qk_layout *L = &c->L;
     uint8_t *buf = malloc(L->slot_bytes);
@@ -519,6 +539,7 @@ int qmoe_upload_layer(qmoe_ctx *c, int layer, const qmoe_layer_weights *w, qmoe_
         ld->bias = NULL;
     }
     if (upload_shared(c, ld, w, err)) return -1;
+    ld->router_wmax = router_wmax(w->router, L->E, L->d);
     if (c->resident_all) {
         CK(cudaMallocHost((void **)&stage, (size_t)batch * L->slot_bytes));
         for (int e0 = 0; e0 < L->E; e0 += batch) {
@@ -614,11 +635,25 @@ static int kerr(int rc, const char *what, qmoe_err *err) {
     return 0;
 }
 
+/* Routing (idx, wts, sgate) of f->T tokens: the tensor-core path with exact
+ * re-ranking for multi-token calls when the plan covers the shape, else the
+ * fp64 router and the one-warp top-k. mid: NULL or an event recorded
+ * between the two kernels of either path. */
+static int route(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, int pdl, cudaEvent_t mid,
+                 qmoe_err *err) {
+    if (c->prefill && f->T > 1) {
+        int rc = qk_launch_route(c->prefill, f, c->layers[layer].router_wmax, st, mid);
+        if (rc != QK_ROUTE_UNFIT) return kerr(rc, "route", err);
+    }
+    if (kerr(qk_launch_router(f, st, pdl), "router", err)) return -1;
+    if (mid) cudaEventRecordWithFlags(mid, st, cudaEventRecordExternal);
+    return kerr(qk_launch_topk(f, st, pdl), "topk", err);
+}
+
 /* streaming mode: route first, make the selected experts resident */
 static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, qmoe_err *err) {
     int n = f->T, k = c->L.k;
-    if (kerr(qk_launch_router(f, st, 0), "router", err)) return -1;
-    if (kerr(qk_launch_topk(f, st, 0), "topk", err)) return -1;
+    if (route(c, layer, f, st, 0, NULL, err)) return -1;
     cudaError_t ce = cudaMemcpyAsync(c->idx_pin, c->idx, (size_t)n * k * sizeof(int32_t),
                                      cudaMemcpyDeviceToHost, st);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
@@ -700,9 +735,7 @@ int qmoe_forward_dev(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, 
         if (stream_in(c, layer, &f, st, err)) return -1;
     } else {
         PEV(0);
-        if (kerr(qk_launch_router(&f, st, !prof), "router", err)) return -1;
-        PEV(1);
-        if (kerr(qk_launch_topk(&f, st, !prof), "topk", err)) return -1;
+        if (route(c, layer, &f, st, !prof, prof ? c->pev[1] : NULL, err)) return -1;
         PEV(2);
     }
     if (c->prefill && n > 1) {

@@ -172,10 +172,12 @@ QK_DEV uint64_t sdesc_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor for kind::f16: fp16 A and B (K-major), fp32 D.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+// Instruction descriptor for kind::f16: fp16 (or bf16) A and B, both
+// K-major, fp32 D. A and B always share one type.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16 = false) {
     return (1u << 4)                                   // D format f32
-           | (0u << 7) | (0u << 10)                    // A, B format f16
+           | ((bf16 ? 1u : 0u) << 7)                   // A format: f16 0, bf16 1
+           | ((bf16 ? 1u : 0u) << 10)                  // B format: same as A
            | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
            | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
@@ -401,6 +403,51 @@ QK_DEV void topk_stage_keys(const float *lg, int E, uint32_t *keys, int t, int n
     }
 }
 
+// Ranks C candidates (keys in s_key, expert ids in s_idx, C <= 32) by
+// (value desc, index asc), writes the first k in that order to idx_out and
+// the softmax over their logits to w_out (model.c:1305-1318). Any candidate
+// set that contains every key ranked above a member of the top-k gives the
+// same result as the full key array.
+QK_DEV void topk_rank_softmax(int C, int k, uint32_t *s_key, int *s_idx, float *s_ev,
+                              int *idx_out, float *w_out) {
+    const int lane = threadIdx.x & 31;
+    int rank = 0, mi = 0;
+    uint32_t mk = 0;
+    if (lane < C) {
+        mk = s_key[lane];
+        mi = s_idx[lane];
+    }
+    // rank among the candidates: lane m's (key, index) arrive by shuffle
+#pragma unroll 4
+    for (int m = 0; m < C; ++m) {
+        const uint32_t ok = __shfl_sync(QK_FULL, mk, m);
+        const int oi = __shfl_sync(QK_FULL, mi, m);
+        rank += (ok > mk || (ok == mk && oi < mi)) ? 1 : 0;
+    }
+    const bool mine = lane < C && rank < k;
+    float v = 0.f;
+    if (mine) {
+        v = key_value(mk);
+        s_idx[rank] = mi;
+        s_key[rank] = __float_as_uint(v);
+    }
+    __syncwarp();
+    const float mx = __uint_as_float(s_key[0]);
+    float ev = 0.f;
+    if (mine) {
+        ev = expf(v - mx);
+        s_ev[rank] = ev;
+    }
+    __syncwarp();
+    float sum = 0.f;
+    for (int m = 0; m < k; ++m) sum += s_ev[m];
+    if (mine) {
+        idx_out[rank] = mi;
+        w_out[rank] = ev / sum;
+    }
+    __syncwarp();
+}
+
 // Exact top-k of E staged keys by one warp (k <= 32), selection by
 // (value desc, index asc), written in that order; w is the softmax over the
 // selected logits (model.c:1305-1318).
@@ -460,41 +507,7 @@ QK_DEV bool topk_warp(const uint32_t *keys, int E, int k, uint32_t *s_key, int *
     __syncwarp();
     if (C > 32) C = topk_gather_radix(keys, nj, k, s_key, s_idx);
     if (C < k || C > 32) return false;
-    int rank = 0, mi = 0;
-    uint32_t mk = 0;
-    if (lane < C) {
-        mk = s_key[lane];
-        mi = s_idx[lane];
-    }
-    // rank among the candidates: lane m's (key, index) arrive by shuffle
-#pragma unroll 4
-    for (int m = 0; m < C; ++m) {
-        const uint32_t ok = __shfl_sync(QK_FULL, mk, m);
-        const int oi = __shfl_sync(QK_FULL, mi, m);
-        rank += (ok > mk || (ok == mk && oi < mi)) ? 1 : 0;
-    }
-    const bool mine = lane < C && rank < k;
-    float v = 0.f;
-    if (mine) {
-        v = key_value(mk);
-        s_idx[rank] = mi;
-        s_key[rank] = __float_as_uint(v);
-    }
-    __syncwarp();
-    const float mx = __uint_as_float(s_key[0]);
-    float ev = 0.f;
-    if (mine) {
-        ev = expf(v - mx);
-        s_ev[rank] = ev;
-    }
-    __syncwarp();
-    float sum = 0.f;
-    for (int m = 0; m < k; ++m) sum += s_ev[m];
-    if (mine) {
-        idx_out[rank] = mi;
-        w_out[rank] = ev / sum;
-    }
-    __syncwarp();
+    topk_rank_softmax(C, k, s_key, s_idx, s_ev, idx_out, w_out);
     return true;
 }
 

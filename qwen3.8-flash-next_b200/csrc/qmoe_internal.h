@@ -107,6 +107,14 @@ void qk_prefill_destroy(qk_prefill *p);
  * gate/up GEMM, down GEMM and combine (diagnostics). */
 int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream,
                       void **events);
+/* Routing of a multi-token call on the tensor cores (approximate logits)
+ * with an exact re-ranking of each token's candidates: writes f->idx, f->wts
+ * and f->sgate, identical to qk_launch_router + qk_launch_topk (f->logits is
+ * not written). wmax: max over experts of the router row's 2-norm, rounded
+ * up. mid_event: NULL, or a cudaEvent_t recorded between the two halves.
+ * Returns QK_ROUTE_UNFIT (no launch) when the plan does not cover the shape. */
+#define QK_ROUTE_UNFIT (-8)
+int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream, void *mid_event);
 
 /* internal cache helper: replace the value of an existing key */
 struct qmoe_cache;

@@ -32,6 +32,7 @@
 // order, so the products pair up as in the natural order.
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdio.h>
 #include <string.h>
@@ -57,11 +58,14 @@ constexpr int kBs = BN * 16;      // 4 KB scales
 // Per-mode stage layout. The down GEMM's A operand is H as an fp16 hi/lo pair
 // (H = hi + lo to about 22 significant bits), two A tiles per stage and two
 // MMAs per K step against the same dequantised B tile; it runs 2 stages.
+// MODE 2 is the router: A = x as a bf16 hi/lo pair, B = the bf16 router rows
+// loaded by TMA straight into the swizzled layout (no dequantisation, no
+// packed-q4 staging); it runs 3 stages.
 template <int MODE>
 struct Cfg {
-    static constexpr int NSt = MODE ? 2 : 3;
+    static constexpr int NSt = MODE == 1 ? 2 : 3;
     static constexpr int A = MODE ? 2 * kA : kA;
-    static constexpr int Stage = A + kBf + kBq + kBs;
+    static constexpr int Stage = A + kBf + (MODE == 2 ? 0 : kBq + kBs);
     static constexpr int Smem = NSt * Stage + 1024;  // + alignment slack
 };
 
@@ -73,10 +77,11 @@ struct MTile {
 };
 
 struct GemmArgs {
-    int mode;   // 0: gate/up, 1: down
+    int mode;   // 0: gate/up, 1: down, 2: router
     int KB;     // K / 64
     int NT;     // N-tiles per M-tile
     int ld_out; // output row length (elements)
+    int n_cols; // fp32 outputs: columns that exist (a multiple of 16)
     int d, I;
     const MTile *tiles;
     const int *n_mtiles;
@@ -201,12 +206,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_3d(Bq + 128 * 32, &tmQ, g.d / 2 + kb * 32, nt * 128, mt.slot,
                                     &full[s]);
                         tma_load_3d(Bs, &tmS, g.d + 16 * (kb >> 1), nt * 128, mt.slot, &full[s]);
-                    } else {
+                    } else if (MODE == 1) {
                         mbar_expect_tx(&full[s], 2 * kA + 256 * 32 + 256 * 16);
                         tma_load_2d(A, &tmA, kb * BK, mt.m0, &full[s]);                   // hi
                         tma_load_2d(A + kA, &tmA, kb * BK, g.rows_max + mt.m0, &full[s]);  // lo
                         tma_load_3d(Bq, &tmQ, kb * 32, nt * 256, mt.slot, &full[s]);
                         tma_load_3d(Bs, &tmS, g.I / 2 + 16 * (kb >> 2), nt * 256, mt.slot, &full[s]);
+                    } else {
+                        mbar_expect_tx(&full[s], 2 * kA + kBf);
+                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &full[s]);                   // hi
+                        tma_load_2d(A + kA, &tmA, kb * BK, g.rows_max + mt.m0, &full[s]);  // lo
+                        tma_load_2d(A + kAm, &tmQ, kb * BK, nt * 256, &full[s]);         // router rows
                     }
                     last_it[s] = it;
                 }
@@ -217,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
-        const uint32_t idesc = idesc_f16(BM, BN);
+        const uint32_t idesc = idesc_f16(BM, BN, MODE == 2);
         int it = 0, lt = 0;
         for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
             const int buf = lt & 1;
@@ -235,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kb = 0; kb < KB; ++kb, ++it) {
                 const int s = it % NSm;
                 const uint32_t ph = (it / NSm) & 1;
-                if (!mbar_wait(&full[s], ph) || !mbar_wait(&ready[s], ph)) {
+                if (!mbar_wait(&full[s], ph) || (MODE != 2 && !mbar_wait(&ready[s], ph))) {
                     ok = false;
                     break;
                 }
@@ -247,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         umma_f16(dt, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
                                  (kb | kk) != 0);
-                        if (MODE == 1)  // lo plane of H, same B
+                        if (MODE != 0)  // lo plane of the A operand, same B
                             umma_f16(dt, sdesc_sw128(a0 + kA + kk * 32), sdesc_sw128(b0 + kk * 32),
                                      idesc, 1u);
                     }
@@ -273,9 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (warp < 6) {
         // ---------------- dequantisers: 128 threads, rows t and t + 128
+        // (the router's B tile arrives ready: no work)
         const int t = tid - 64;
+        const int dq_tiles = MODE == 2 ? 0 : ntiles;
         int it = 0;
-        for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
+        for (int tile = blockIdx.x; tile < dq_tiles && !abort_flag; tile += gridDim.x) {
             bool ok = true;
             for (int kb = 0; kb < KB; ++kb, ++it) {
                 const int s = it % NSm;
@@ -364,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float yv[16];
                     tmem_ld16(tbase + c, yv);
                     tmem_wait_ld();
-                    if (live) {
+                    if (live && nt * 256 + c < g.n_cols) {
                         float4 *dst = reinterpret_cast<float4 *>(orow + nt * 256 + c);
 #pragma unroll
                         for (int i = 0; i < 4; ++i)
@@ -532,6 +544,253 @@ __global__ void k_combine(const float *Y, const int *inv, const float *wts, cons
 }
 
 // ---------------------------------------------------------------------------
+// routing of a multi-token call (model.c:1301-1318, :1396-1398)
+//
+// The canonical router logit of (token t, expert e) is one fp32 rounding of
+// an fp64 sum in a fixed order (router_lane); the top-k and its softmax
+// follow from those values. Computing all T x E of them in fp64 is the cost
+// of the whole layer at prefill sizes, so the call runs in three steps:
+//   k_route_split   x -> bf16 pair (hi = bf16(x), lo = bf16(x - hi)), the
+//                   2-norm of each token
+//   k_gemm<2>       approximate logits a[t, e] = (hi + lo) . w_e on the
+//                   tensor cores (fp32 accumulation)
+//   k_route_exact   per token: with a bound |a - logit| <= beta, every
+//                   member of the exact top-k (and every expert tied with
+//                   one) has a >= a_(k) - 2 beta, a_(k) the k-th largest
+//                   approximate value. The exact logits of that candidate
+//                   set (typically 11-16 experts) are computed in the
+//                   canonical order and ranked exactly, so the selection,
+//                   order and weights are those of the full exact top-k.
+// beta = 2^-10 |x_t| max_e |w_e| + 2^-20 max_e |a[t, e]|: the first term is
+// twice the worst case of 4096 products (hi and lo) summed in fp32 with
+// truncation at every step, |x - hi - lo| <= 2^-18 |x| included, over
+// sum_i |x_i w_i| <= |x| |w| (Cauchy-Schwarz); the second covers the fp32
+// additions of the logit bias. The candidate threshold uses 3 beta. A token
+// whose candidate set exceeds 32, or with a non-finite value, gets every
+// logit exactly instead (the one-warp path of k_topk).
+
+constexpr int kRW = 8;  // tokens (warps) per CTA of k_route_exact
+
+__global__ void k_route_split(const void *x, int x_bf16, int d, int T, int Tpad,
+                              __nv_bfloat16 *xr, float *xnorm, MTile *tiles, int *n_mtiles) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (blockIdx.x == 0) {
+        const int nm = (T + BM - 1) / BM;
+        for (int i = threadIdx.x; i < nm; i += blockDim.x) {
+            MTile m;
+            m.m0 = BM * i;
+            m.rows = min(BM, T - BM * i);
+            m.slot = 0;
+            m.pad = 0;
+            tiles[i] = m;
+        }
+        if (threadIdx.x == 0) *n_mtiles = nm;
+    }
+    if (warp >= T) return;
+    double ss = 0.0;
+    for (int c = lane; c < d / 8; c += 32) {
+        float v[8];
+        if (x_bf16) {
+            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
+                                                            static_cast<size_t>(warp) * d)[c];
+            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
+            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
+        } else {
+            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
+                                                               static_cast<size_t>(warp) * d) + 2 * c;
+            const float4 a = p[0], b = p[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            const float2 hf = __bfloat1622float2(h);
+            const __nv_bfloat162 l = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+            hi[i] = *reinterpret_cast<const uint32_t *>(&h);
+            lo[i] = *reinterpret_cast<const uint32_t *>(&l);
+            ss = fma(static_cast<double>(v[2 * i]), static_cast<double>(v[2 * i]), ss);
+            ss = fma(static_cast<double>(v[2 * i + 1]), static_cast<double>(v[2 * i + 1]), ss);
+        }
+        reinterpret_cast<uint4 *>(xr + static_cast<size_t>(warp) * d)[c] =
+            make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        reinterpret_cast<uint4 *>(xr + static_cast<size_t>(Tpad + warp) * d)[c] =
+            make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    ss = warp_sum_butterfly(ss);
+    if (lane == 0) xnorm[warp] = __double2float_ru(sqrt(ss));
+}
+
+struct RouteArgs {
+    const void *x;
+    int x_bf16, d, E, k, T;
+    const uint16_t *router, *shared_gate;
+    const float *bias;   // [E] or NULL
+    const float *lga;    // [T, E] approximate logits (without the bias)
+    const float *xnorm;  // [T]
+    float wmax;          // max_e |w_e|, rounded up
+    int32_t *idx;
+    float *wts, *sgate;
+    int *err;
+};
+
+// The k-th largest of E staged keys (keys past E are 0; k <= 32, k <= E),
+// or a lower bound of it when more than 32 keys reach the k-th largest of
+// the 32 lane maxima. One warp.
+QK_DEV uint32_t kth_key(const uint32_t *keys, int E, int k, uint32_t *s_key) {
+    const int lane = threadIdx.x & 31;
+    const int nj = (E + 31) / 32;
+    uint32_t mxk = 0;
+    for (int j = 0; j < nj; ++j) mxk = max(mxk, keys[j * 32 + lane]);
+    int r = 0;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+        const uint32_t o = __shfl_sync(QK_FULL, mxk, j);
+        r += (o > mxk || (o == mxk && j < lane)) ? 1 : 0;
+    }
+    const uint32_t tau = __shfl_sync(QK_FULL, mxk, __ffs(__ballot_sync(QK_FULL, r == k - 1)) - 1);
+    int own = 0;
+    for (int j = 0; j < nj; ++j) own += keys[j * 32 + lane] >= tau ? 1 : 0;
+    int incl = own;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int t = __shfl_up_sync(QK_FULL, incl, off);
+        if (lane >= off) incl += t;
+    }
+    const int C = __shfl_sync(QK_FULL, incl, 31);
+    if (C > 32) return tau;
+    int pos = incl - own;
+    for (int j = 0; j < nj; ++j) {
+        const uint32_t kk = keys[j * 32 + lane];
+        if (kk >= tau) s_key[pos++] = kk;
+    }
+    __syncwarp();
+    const uint32_t mk = lane < C ? s_key[lane] : 0u;
+    int rank = 0;
+    for (int m = 0; m < C; ++m) {
+        const uint32_t o = __shfl_sync(QK_FULL, mk, m);
+        rank += (o > mk || (o == mk && m < lane)) ? 1 : 0;
+    }
+    const unsigned hit = __ballot_sync(QK_FULL, lane < C && rank == k - 1);
+    const uint32_t res = __shfl_sync(QK_FULL, mk, __ffs(hit) - 1);
+    __syncwarp();
+    return res;
+}
+
+QK_DEV float exact_logit(const RouteArgs &a, const float *xs, int e, int lane) {
+    const double s = warp_sum_butterfly(router_lane(a.router + static_cast<size_t>(e) * a.d, xs, a.d, lane));
+    float v = static_cast<float>(s);
+    if (a.bias) v = v + a.bias[e];
+    return v;
+}
+
+// One warp per token; dynamic shared memory: kRW x (d floats of x, E keys).
+__global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
+    extern __shared__ __align__(16) float rsm[];
+    __shared__ uint32_t s_key_all[kRW][32];
+    __shared__ int s_idx_all[kRW][32];
+    __shared__ float s_ev_all[kRW][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kRW + warp;
+    if (t >= a.T) return;
+    const int d = a.d, E = a.E, k = a.k, nE = (E + 31) / 32 * 32;
+    float *xs = rsm + static_cast<size_t>(warp) * d;
+    uint32_t *keys = reinterpret_cast<uint32_t *>(rsm + static_cast<size_t>(kRW) * d) + warp * nE;
+    uint32_t *s_key = s_key_all[warp];
+    int *s_idx = s_idx_all[warp];
+    for (int c = lane; c < d / 8; c += 32) {
+        float v[8];
+        if (a.x_bf16) {
+            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.x) +
+                                                            static_cast<size_t>(t) * d)[c];
+            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
+            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
+        } else {
+            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) +
+                                                               static_cast<size_t>(t) * d) + 2 * c;
+            const float4 u = p[0], w = p[1];
+            v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
+        }
+        reinterpret_cast<float4 *>(xs)[2 * c] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4 *>(xs)[2 * c + 1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    // approximate logits (+ bias, as the canonical logit adds it) -> keys
+    const float *lr = a.lga + static_cast<size_t>(t) * E;
+    bool finite = isfinite(a.xnorm[t]);
+    float maxabs = 0.f;
+    for (int e = lane; e < nE; e += 32) {
+        uint32_t key = 0u;
+        if (e < E) {
+            float v = lr[e];
+            if (a.bias) v = v + a.bias[e];
+            finite = finite && isfinite(v);
+            maxabs = fmaxf(maxabs, fabsf(v));
+            key = fkey(v);
+        }
+        keys[e] = key;
+    }
+    finite = __all_sync(QK_FULL, finite);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) maxabs = fmaxf(maxabs, __shfl_xor_sync(QK_FULL, maxabs, off));
+    __syncwarp();
+    bool fast = finite;
+    int C = 0;
+    if (fast) {
+        const float vk = key_value(kth_key(keys, E, k, s_key));
+        const float beta = __fmaf_ru(__fmul_ru(0x1p-10f, a.xnorm[t]), a.wmax, __fmul_ru(0x1p-20f, maxabs));
+        const uint32_t tk = fkey(__fsub_rd(vk, __fmul_ru(3.0f, beta)));
+        int own = 0;
+        for (int e = lane; e < E; e += 32) own += keys[e] >= tk ? 1 : 0;
+        int incl = own;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int u = __shfl_up_sync(QK_FULL, incl, off);
+            if (lane >= off) incl += u;
+        }
+        C = __shfl_sync(QK_FULL, incl, 31);
+        fast = C >= k && C <= 32;
+        if (fast) {
+            int pos = incl - own;
+            for (int e = lane; e < E; e += 32)
+                if (keys[e] >= tk) s_idx[pos++] = e;
+        }
+        __syncwarp();
+    }
+    if (fast) {
+        // exact logits of the candidates, canonical order; lane m keeps m's key
+        uint32_t mykey = 0u;
+        bool fin = true;
+        for (int m = 0; m < C; ++m) {
+            const float v = exact_logit(a, xs, s_idx[m], lane);
+            fin = fin && isfinite(v);
+            if (lane == m) mykey = fkey(v);
+        }
+        fast = fin;
+        if (fast) {
+            if (lane < C) s_key[lane] = mykey;
+            __syncwarp();
+            topk_rank_softmax(C, k, s_key, s_idx, s_ev_all[warp], a.idx + static_cast<size_t>(t) * k,
+                              a.wts + static_cast<size_t>(t) * k);
+        }
+    }
+    if (!fast) {
+        // every logit exactly (rare)
+        for (int e = 0; e < E; ++e) {
+            const float v = exact_logit(a, xs, e, lane);
+            if (lane == 0) keys[e] = fkey(v);
+        }
+        __syncwarp();
+        if (!topk_warp(keys, E, k, s_key, s_idx, s_ev_all[warp], a.idx + static_cast<size_t>(t) * k,
+                       a.wts + static_cast<size_t>(t) * k)) {
+            if (lane == 0) atomicOr(a.err, QK_ERR_BAD_ROUTE);
+            return;
+        }
+    }
+    const double sg = warp_sum_butterfly(router_lane(a.shared_gate, xs, d, lane));
+    if (lane == 0) a.sgate[t] = 1.0f / (1.0f + expf(-static_cast<float>(sg)));
+}
+
+// ---------------------------------------------------------------------------
 // host side
 
 typedef CUresult (*encode_fn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -552,12 +811,16 @@ encode_fn get_encode() {
     return fn;
 }
 
-bool map_2d_f16(CUtensorMap *m, void *base, uint64_t cols, uint64_t rows) {
+// Row-major [rows, cols] of 16-bit elements, boxes of 64 x box_rows with the
+// 128-byte swizzle (the K-major operand layout of the MMA).
+bool map_2d_16(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, bool bf16,
+               uint32_t box_rows = BM) {
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {BK, BM};
+    const cuuint32_t box[2] = {BK, box_rows};
     const cuuint32_t es[2] = {1, 1};
-    return get_encode()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, es,
+    return get_encode()(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void *>(base), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -585,6 +848,15 @@ struct qk_prefill {
     __half *xp, *H;
     float *Y;
     CUtensorMap tmX, tmH, tmQgu, tmSgu, tmQdn, tmSdn;
+    // routing: x as a bf16 pair [2 * Tpad, d], token norms, approximate
+    // logits [max_tokens, E], the router's M-tile list
+    int route_ok, Tpad;
+    size_t route_smem;
+    __nv_bfloat16 *xr;
+    float *xnorm, *lga;
+    MTile *rtiles;
+    int *rn;
+    CUtensorMap tmXr;
 };
 
 extern "C" void qk_prefill_destroy(qk_prefill *p) {
@@ -598,6 +870,11 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->xp);
     cudaFree(p->H);
     cudaFree(p->Y);
+    cudaFree(p->xr);
+    cudaFree(p->xnorm);
+    cudaFree(p->lga);
+    cudaFree(p->rtiles);
+    cudaFree(p->rn);
     delete p;
 }
 
@@ -636,7 +913,8 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
         qk_prefill_destroy(p);
         return nullptr;
     }
-    bool ok = map_2d_f16(&p->tmX, p->xp, L->d, R) && map_2d_f16(&p->tmH, p->H, L->I, 2 * R) &&
+    bool ok = map_2d_16(&p->tmX, p->xp, L->d, R, false) &&
+              map_2d_16(&p->tmH, p->H, L->I, 2 * R, false) &&
               map_3d_u8(&p->tmQgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 32, 128) &&
               map_3d_u8(&p->tmSgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 16, 128) &&
               map_3d_u8(&p->tmQdn, pool + L->gu_bytes, L->d_row, L->d, pool_slots, L->slot_bytes, 32,
@@ -648,10 +926,34 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
         qk_prefill_destroy(p);
         return nullptr;
     }
-    const void *fns[2] = {reinterpret_cast<const void *>(&k_gemm<0>),
-                          reinterpret_cast<const void *>(&k_gemm<1>)};
-    const int smem[2] = {Cfg<0>::Smem, Cfg<1>::Smem};
-    for (int i = 0; i < 2; ++i) {
+    // tensor-core routing: E a multiple of 16 (whole 16-column epilogue
+    // chunks; router rows past E read as zeros), the shapes' workspace
+    const int nE = (L->E + 31) / 32 * 32;
+    p->Tpad = (max_tokens + BM - 1) / BM * BM;
+    p->route_smem = static_cast<size_t>(kRW) * (static_cast<size_t>(L->d) + nE) * 4;
+    p->route_ok = L->E % 16 == 0 && L->k <= 32 && p->route_smem <= 200 * 1024;
+    if (p->route_ok) {
+        const size_t Tp = static_cast<size_t>(p->Tpad);
+        e = cudaMalloc(&p->xr, 2 * Tp * L->d * sizeof(__nv_bfloat16));
+        if (e == cudaSuccess) e = cudaMalloc(&p->xnorm, Tp * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&p->lga, static_cast<size_t>(max_tokens) * L->E * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&p->rtiles, sizeof(MTile) * (Tp / BM));
+        if (e == cudaSuccess) e = cudaMalloc(&p->rn, sizeof(int));
+        if (e != cudaSuccess) {
+            snprintf(msg, msg_len, "prefill routing workspace: %s", cudaGetErrorString(e));
+            qk_prefill_destroy(p);
+            return nullptr;
+        }
+        CUtensorMap probe;  // the per-call router map, encoded once here as a check
+        p->route_ok = map_2d_16(&p->tmXr, p->xr, L->d, 2 * Tp, true) &&
+                      map_2d_16(&probe, p->xr, L->d, L->E, true, 256);
+    }
+    const void *fns[4] = {reinterpret_cast<const void *>(&k_gemm<0>),
+                          reinterpret_cast<const void *>(&k_gemm<1>),
+                          reinterpret_cast<const void *>(&k_gemm<2>),
+                          reinterpret_cast<const void *>(&k_route_exact)};
+    const int smem[4] = {Cfg<0>::Smem, Cfg<1>::Smem, Cfg<2>::Smem, static_cast<int>(p->route_smem)};
+    for (int i = 0; i < (p->route_ok ? 4 : 2); ++i) {
         e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem[i]);
         if (e != cudaSuccess) {
             snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
@@ -692,6 +994,7 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     gu.KB = L.d / BK;
     gu.NT = L.I / 128;
     gu.ld_out = L.I;
+    gu.n_cols = L.I;
     gu.d = L.d;
     gu.I = L.I;
     gu.tiles = p->tiles;
@@ -713,6 +1016,7 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     dn.KB = L.I / BK;
     dn.NT = L.d / 256;
     dn.ld_out = L.d;
+    dn.n_cols = L.d;
     dn.out = nullptr;
     dn.outf = p->Y;
     {
@@ -724,5 +1028,62 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     mark(2);
     k_combine<<<T, 256, 0, st>>>(p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
     mark(3);
+    return cudaGetLastError();
+}
+
+extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream,
+                               void *mid_event) {
+    if (!p->route_ok) return QK_ROUTE_UNFIT;
+    const qk_layout &L = p->L;
+    const int T = f->T, E = L.E;
+    if (T > p->max_tokens) return cudaErrorInvalidValue;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    k_route_split<<<(T * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, p->Tpad, p->xr,
+                                                       p->xnorm, p->rtiles, p->rn);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    CUtensorMap tmR;
+    if (!map_2d_16(&tmR, f->router, L.d, E, true, 256)) return cudaErrorInvalidValue;
+    GemmArgs ra;
+    memset(&ra, 0, sizeof(ra));
+    ra.mode = 2;
+    ra.KB = L.d / BK;
+    ra.NT = (E + BN - 1) / BN;
+    ra.ld_out = E;
+    ra.n_cols = E;
+    ra.d = L.d;
+    ra.I = L.I;
+    ra.tiles = p->rtiles;
+    ra.n_mtiles = p->rn;
+    ra.rows_max = p->Tpad;
+    ra.outf = p->lga;
+    ra.err = f->err;
+    const int ntiles = (T + BM - 1) / BM * ra.NT;
+    {
+        void *args[] = {&p->tmXr, &tmR, &tmR, &ra};
+        e = qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<2>),
+                          dim3(ntiles < p->num_sms ? ntiles : p->num_sms), dim3(kThreads),
+                          Cfg<2>::Smem, stream, 0, args);
+        if (e != cudaSuccess) return e;
+    }
+    if (mid_event) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(mid_event), st, cudaEventRecordExternal);
+    RouteArgs a;
+    a.x = f->x;
+    a.x_bf16 = f->x_bf16;
+    a.d = L.d;
+    a.E = E;
+    a.k = L.k;
+    a.T = T;
+    a.router = f->router;
+    a.shared_gate = f->shared_gate;
+    a.bias = f->logit_bias;
+    a.lga = p->lga;
+    a.xnorm = p->xnorm;
+    a.wmax = wmax;
+    a.idx = f->idx;
+    a.wts = f->wts;
+    a.sgate = f->sgate;
+    a.err = f->err;
+    k_route_exact<<<(T + kRW - 1) / kRW, kRW * 32, p->route_smem, st>>>(a);
     return cudaGetLastError();
 }

@@ -130,6 +130,27 @@ def test_prefill_cfg1_shapes_matches_restatement(cfg1_layer, cfg1_ctx):
     _close(out, ro)
 
 
+def test_prefill_routing_ties_take_exact_path(cfg1_layer, cfg1_ctx):
+    """Multi-token routing re-ranks a candidate set from tensor-core logits.
+    A zero token (every logit 0: a 512-way tie) overflows the candidate set
+    and takes the all-exact path; a token scaled by 1024 stays on the
+    candidate path (its bound scales with |x|). Routing equals the
+    restatement for every token."""
+    import oracle
+    import qmoe
+    s, seed = cfg1_layer
+    x = qmoe.synth_tokens(seed, 16, 8, 2048)
+    x[3] = 0.0
+    x[5] *= 1024.0
+    out = cfg1_ctx.forward(0, x)
+    idx, w, sg = cfg1_ctx.routing(8)
+    ro, ri, rw = oracle.restatement().forward(s, x)
+    assert np.array_equal(idx, ri)
+    np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-6)
+    assert idx[3].tolist() == list(range(10))
+    _close(out[[0, 1, 2, 3, 4, 6, 7]], ro[[0, 1, 2, 3, 4, 6, 7]])
+
+
 def test_prefill_cfg2_full_zipf(built):
     """Config 2: 4096 tokens, Zipf(1.1) router bias. Routing of every token
     (sorted sets and per-expert counts) equals the golden; a spread sample
