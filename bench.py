@@ -311,8 +311,9 @@ def main():
     # parity spot check of the timed outputs (tokens 996..999 of the last
     # replay; out_dev was zeroed before capture, so these come from the graph)
     out_last = out_dev[TOKENS - 4:].cpu().numpy()
-    ref4 = ctx.forward(0, x_host[TOKENS - 4:])
-    parity_ok = bool(np.allclose(out_last, ref4, rtol=1e-5, atol=1e-5))
+    # (one eager single-token call each: the same kernel, so the same bits)
+    ref4 = np.concatenate([ctx.forward(0, x_host[t:t + 1]) for t in range(TOKENS - 4, TOKENS)])
+    parity_ok = bool(np.array_equal(out_last, ref4))
 
     # e2e through the host-pointer C ABI: copies in and out on every call
     e2e_steps = max(1, min(args.steps, 3))

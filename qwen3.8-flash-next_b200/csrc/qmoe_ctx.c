@@ -46,7 +46,7 @@ struct qmoe_ctx {
     cudaEvent_t copy_done;
     int *err_dev;
     int *err_host; /* pinned */
-    unsigned *gbar; /* grid-barrier words of the single-launch decode kernel */
+    void *dsync;     /* launch counter + exchange area of the single-launch decode kernel */
     layer_dev *layers;
     /* expert pool */
     uint8_t *pool;
@@ -194,7 +194,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     cudaFree(c->pool);
     cudaFree(c->slot_of_dev);
     cudaFree(c->err_dev);
-    cudaFree(c->gbar);
+    cudaFree(c->dsync);
     cudaFree(c->x_dev);
     cudaFree(c->out_dev);
     cudaFree(c->logits);
@@ -277,8 +277,8 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaMalloc((void **)&c->err_dev, sizeof(int)));
     CK(cudaMemset(c->err_dev, 0, sizeof(int)));
     CK(cudaMallocHost((void **)&c->err_host, sizeof(int)));
-    CK(cudaMalloc((void **)&c->gbar, 2 * sizeof(unsigned)));
-    CK(cudaMemset(c->gbar, 0, 2 * sizeof(unsigned)));
+    CK(cudaMalloc(&c->dsync, qk_decode_sync_bytes(L)));
+    CK(cudaMemset(c->dsync, 0, qk_decode_sync_bytes(L)));
     c->layers = calloc((size_t)Lz, sizeof(layer_dev));
     if (!c->layers) {
         seterr(err, "qmoe_create: out of host memory");
@@ -722,7 +722,7 @@ int qmoe_forward_dev(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, 
     if (c->resident_all && n == 1) {
         /* one persistent launch for the whole layer */
         PEV(0);
-        int rc = qk_launch_decode_fused(&f, c->gbar, st, !prof);
+        int rc = qk_launch_decode_fused(&f, c->dsync, st, !prof);
         if (rc == 0) {
             PEV(1);
             c->prof_kernels = 1;
@@ -827,17 +827,17 @@ int qmoe__phase_times(qmoe_ctx *c, int layer, const void *x, int x_dtype, float 
                       unsigned long long *out_ns, int max_ctas) {
     if (!c || !c->resident_all || !c->layers[layer].ready) return -1;
     unsigned long long *buf = NULL;
-    size_t bytes = (size_t)c->num_sms * 16 * sizeof(unsigned long long);
+    size_t bytes = (size_t)c->num_sms * 32 * sizeof(unsigned long long);
     if (cudaMalloc((void **)&buf, bytes) != cudaSuccess) return -1;
     cudaMemset(buf, 0, bytes);
     qk_fwd f;
     fill_fwd(c, layer, x, x_dtype == QMOE_BF16, 1, out, &f);
     f.ptimes = buf;
-    int rc = qk_launch_decode_fused(&f, c->gbar, c->stream, 0);
+    int rc = qk_launch_decode_fused(&f, c->dsync, c->stream, 0);
     if (rc == 0) rc = cudaStreamSynchronize(c->stream);
     if (rc == 0) {
         int n = max_ctas < c->num_sms ? max_ctas : c->num_sms;
-        rc = cudaMemcpy(out_ns, buf, (size_t)n * 16 * sizeof(unsigned long long),
+        rc = cudaMemcpy(out_ns, buf, (size_t)n * 32 * sizeof(unsigned long long),
                         cudaMemcpyDeviceToHost);
     }
     cudaFree(buf);
@@ -895,15 +895,16 @@ static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err) {
     }
     int code = *c->err_host;
     if (code) {
-        /* clear the sticky word and any half-finished grid barrier */
+        /* clear the sticky word and the decode kernel's counter and exchange
+         * area (a launch that gave up may have left its epoch unfinished) */
         cudaMemsetAsync(c->err_dev, 0, sizeof(int), st);
-        cudaMemsetAsync(c->gbar, 0, 2 * sizeof(unsigned), st);
+        cudaMemsetAsync(c->dsync, 0, qk_decode_sync_bytes(&c->L), st);
         cudaStreamSynchronize(st);
         seterr(err, "qmoe: device reported error 0x%x (%s%s%s%s)", code,
                code & QK_ERR_TIMEOUT_COPY ? "copy wait timed out; " : "",
                code & QK_ERR_NOT_RESIDENT ? "routed expert not resident; " : "",
                code & QK_ERR_BAD_ROUTE ? "top-k selection failed; " : "",
-               code & QK_ERR_TIMEOUT_GRID ? "grid barrier timed out" : "");
+               code & QK_ERR_TIMEOUT_GRID ? "grid barrier or exchange timed out" : "");
         return -1;
     }
     return 0;

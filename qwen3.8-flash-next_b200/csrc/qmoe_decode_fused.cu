@@ -1,27 +1,32 @@
 // qmoe_decode_fused.cu - one-launch MoE layer for a single decode token.
 //
 // The whole of moe_forward (c/src/model.c:1281-1405) for T == 1 in one
-// persistent kernel: one CTA per SM, three phases split by grid barriers.
+// persistent kernel: one CTA of 16 warps per SM, three phases split by grid
+// barriers (one arrive per CTA, fire-and-forget, and one polling thread).
 //
 //   prologue  bulk-copy what does not depend on routing into shared memory:
 //             this CTA's router rows (mlp.gate plus the shared-gate row), its
 //             rows of the shared expert (gate/up and down) and the layer's
 //             expert -> slot table. Issued before griddepcontrol.wait.
-//   phase 1   x -> registers and shared memory; router rows -> logits
-//             (global).                                        [grid barrier]
-//   phase 2   the logits are staged as order keys; warp 0 computes the exact
-//             top-k (every CTA computes the same), looks the k experts up in
-//             the staged slot table and issues this CTA's share of their
-//             gate/up rows (in chunks of <= 8 rows, one mbarrier each) and of
-//             their down rows (all k experts at once). Meanwhile warps 1..7
-//             compute the shared expert's gate/up rows. Then all warps compute
-//             the routed gate/up rows chunk by chunk as they land -> h.
-//                                                              [grid barrier]
-//   phase 3   h -> shared memory (swizzled); this CTA's output rows for all
-//             k+1 experts as (expert, row-pair) tasks, so a warp keeps one
-//             expert's h slice in registers across rows; per-expert partials
-//             are combined in a fixed expert order with the routing weights
-//             and the shared gate; each output written once.
+//   phase 1   x -> fp64 in shared memory (router) and as 16-bit integers
+//             (quant_word); router rows -> logits.           [grid barrier]
+//   phase 2   every CTA takes all logits as order keys and computes the same
+//             exact top-k (block-wide threshold, then one warp ranks the
+//             candidates), looks the k experts up in the staged slot table
+//             and issues its share of their gate/up rows (in chunks of <= 8
+//             rows, one mbarrier each) and of their down rows (all k experts
+//             at once). Meanwhile warps 1..15 compute the shared expert's
+//             gate/up rows. Then all warps compute the routed gate/up rows
+//             chunk by chunk as they land -> h.              [grid barrier]
+//   phase 3   h -> 24-bit integers in shared memory; this CTA's output rows
+//             for all k+1 experts as (expert, row-pair) tasks, so a warp keeps
+//             one expert's h slice in registers across rows; per-expert
+//             partials are combined in a fixed expert order with the routing
+//             weights and the shared gate; each output written once.
+//
+// The q4 products are the integer dot products of qmoe_dev.cuh (quant_word,
+// dot_unit_q): four dp4a per q4 word for x, six for h. The router dot keeps
+// the canonical fp64 order (router_lane) with x staged once as doubles.
 //
 // Per CTA at d=2048, E=512, k=10, I=512 on 148 SMs: 16 KB router, 9 KB shared
 // gate/up, 81 KB routed gate/up, 44 KB down rows, so every byte the CTA needs
@@ -38,8 +43,13 @@ cudaError_t qk_launch_raw(const void *fn, dim3 grid, dim3 block, size_t smem, vo
 
 namespace {
 
+constexpr int kThreads = 512;   // 16 warps, one CTA per SM
+constexpr int kWarps = kThreads / 32;
 constexpr int kChunkRows = 8;   // routed gate/up rows per bulk copy / mbarrier
 constexpr int kMaxChunks = 12;  // chunks per CTA (checked by make_plan)
+constexpr int kXB = 2;          // byte planes of x
+constexpr int kHB = 3;          // byte planes of h
+constexpr int kSyncWords = 32;  // 64-bit words before the exchange area
 
 struct Plan {
     int G;       // CTAs, one per SM
@@ -47,37 +57,30 @@ struct Plan {
     int sr_max;  // shared gate/up rows per CTA (of I)
     int gr_max;  // routed gate/up rows per CTA (of k * I)
     int or_max;  // output rows per CTA (of d)
-    int off_router, off_sgu, off_rgu, off_down, total;
+    int off_router, off_sgu, off_rgu, off_down, off_xq, off_x, total;
 };
 
 __device__ __forceinline__ int part(int c, int n, int G) { return (c * n) / G; }
 
-__device__ __forceinline__ void load_x_unit(const qk_fwd &f, int u, float *xr) {
+// x (bf16 or fp32) word t: elements 8t .. 8t + 7
+__device__ __forceinline__ void load_x_word(const qk_fwd &f, int t, float (&v)[8]) {
     if (f.x_bf16) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(f.x) + 32 * u);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const uint4 v = p[q];
-            xr[8 * q + 0] = bf16lo(v.x); xr[8 * q + 1] = bf16hi(v.x);
-            xr[8 * q + 2] = bf16lo(v.y); xr[8 * q + 3] = bf16hi(v.y);
-            xr[8 * q + 4] = bf16lo(v.z); xr[8 * q + 5] = bf16hi(v.z);
-            xr[8 * q + 6] = bf16lo(v.w); xr[8 * q + 7] = bf16hi(v.w);
-        }
+        const uint4 w = reinterpret_cast<const uint4 *>(f.x)[t];
+        v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
+        v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
     } else {
-        const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(f.x) + 32 * u);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float4 v = p[q];
-            xr[4 * q + 0] = v.x; xr[4 * q + 1] = v.y; xr[4 * q + 2] = v.z; xr[4 * q + 3] = v.w;
-        }
+        const float4 *p = reinterpret_cast<const float4 *>(f.x) + 2 * t;
+        const float4 a = p[0], b = p[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     }
 }
 
 // One h-row of gate/up from a staged slot row: h = SiLU(gate . x) * (up . x).
+// Lane l owns the 32-element units l, l + 32, ... of x (UPL of them).
 template <int UPL>
 __device__ __forceinline__ float gateup_row(const uint8_t *row, const qk_layout &L,
-                                            const float (&xr)[UPL][32], const float (&xs)[UPL],
-                                            int lane) {
+                                            const uint2 (&xw)[UPL][kXB][4], const float (&xsc)[UPL],
+                                            const float (&xsm)[UPL], int lane) {
     const int nunits = L.d / 32, half = L.d / 2;
     float pg = 0.f, pu = 0.f;
 #pragma unroll
@@ -86,12 +89,11 @@ __device__ __forceinline__ float gateup_row(const uint8_t *row, const qk_layout 
         if (u < nunits) {
             const uint4 gw = *reinterpret_cast<const uint4 *>(row + 16 * u);
             const uint4 uw = *reinterpret_cast<const uint4 *>(row + half + 16 * u);
-            const int grp = (32 * u) / L.g;
-            const uint2 sb = *reinterpret_cast<const uint2 *>(row + L.d + 8 * grp);
-            const float ag = dot_unit(gw, xr[i]);
-            const float au = dot_unit(uw, xr[i]);
-            pg += fmaf(bf16lo(sb.x), 16.f * (ag - xs[i]), bf16hi(sb.x) * xs[i]);
-            pu += fmaf(bf16lo(sb.y), 16.f * (au - xs[i]), bf16hi(sb.y) * xs[i]);
+            const uint2 sb = *reinterpret_cast<const uint2 *>(row + L.d + 8 * ((32 * u) / L.g));
+            const float ag = dot_unit_q<kXB>(gw, xw[i]) * xsc[i];
+            const float au = dot_unit_q<kXB>(uw, xw[i]) * xsc[i];
+            pg += fmaf(bf16lo(sb.x), ag, bf16hi(sb.x) * xsm[i]);
+            pu += fmaf(bf16lo(sb.y), au, bf16hi(sb.y) * xsm[i]);
         }
     }
 #pragma unroll
@@ -103,8 +105,8 @@ __device__ __forceinline__ float gateup_row(const uint8_t *row, const qk_layout 
 }
 
 template <int UPL, int LPR>
-__global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
-                                                         unsigned long long *gbar) {
+__global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
+                                                              unsigned long long *sync) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bar[2 + kMaxChunks];  // 0: prologue, 1: down rows, 2..: chunks
     __shared__ int s_ok;
@@ -115,6 +117,10 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
     __shared__ float s_ev[32];
     __shared__ int r_idx[32];
     __shared__ float r_w[33];
+    __shared__ float s_gl;
+    __shared__ uint32_t s_wmax[kWarps];
+    __shared__ int s_cnt;
+    __shared__ unsigned long long s_base;
     __shared__ __align__(16) int32_t s_slots[1024];  // this layer's expert -> slot table
     __shared__ uint32_t s_keys[1024];                // staged top-k keys
 
@@ -126,16 +132,20 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
     const int sr0 = part(c, I, G), sr1 = part(c + 1, I, G);
     const int gr0 = part(c, k * I, G), gr1 = part(c + 1, k * I, G);
     const int or0 = part(c, d, G), or1 = part(c + 1, d, G);
+    const int xwn = d / 8;  // words of x
     uint8_t *sm_router = smem + p.off_router;
     uint8_t *sm_sgu = smem + p.off_sgu;
     uint8_t *sm_rgu = smem + p.off_rgu;
     uint8_t *sm_down = smem + p.off_down;
-    float *sm_x = reinterpret_cast<float *>(smem + p.total) - d;  // last d floats
+    uint2 *xq = reinterpret_cast<uint2 *>(smem + p.off_xq);   // kXB planes of d / 8 words
+    float *xusc = reinterpret_cast<float *>(xq + kXB * xwn);  // [d / 32] unit scales
+    float *xusm = xusc + d / 32;                              // [d / 32] unit sums
+    double2 *rx = reinterpret_cast<double2 *>(smem + p.off_x);  // x staged for the router
 
     // diagnostics: phase timestamps of this CTA (thread 0)
 #define STAMP(i)                                                                         \
     do {                                                                                 \
-        if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 16 + (i)] = gtimer(); \
+        if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 32 + (i)] = gtimer(); \
     } while (0)
     STAMP(0);
     if (tid < 2 + kMaxChunks) mbar_init(&bar[tid], 1);
@@ -173,60 +183,137 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
         s_nchunks = n;
     }
     pdl_wait();
+    // Grid barriers: every launch adds 2G to the counter (each CTA arrives
+    // twice), so it starts at a multiple of 2G; when this CTA reads it, at
+    // most G - 1 arrivals of this launch can have happened (the first
+    // barrier needs this CTA), so rounding down gives the launch's base.
+    if (tid == 0) s_base = ld_acquire64(sync) / (2ull * G) * (2ull * G);
+    float *lg = reinterpret_cast<float *>(sync + kSyncWords);  // [E + 1] logits
+    float *hf = lg + ((E + 1 + 3) & ~3);                       // [S * I] h
     STAMP(1);
 
-    // ---- phase 1: x, router rows. Every warp loads all of x into registers
-    // (lane l owns the 32-element units l, l+32, ...); warp w then writes the
-    // units u with u % 8 == w to shared memory for the router.
-    float xr[UPL][32];
-    float xs[UPL];
+    // ---- phase 1: x -> fp32 (router) and 16-bit integers; thread t owns
+    // the q4 word position t (elements 8t .. 8t + 7)
+    for (int t0 = 0; t0 < xwn; t0 += kThreads) {
+        const int t = t0 + tid;
+        float v[8];
 #pragma unroll
-    for (int i = 0; i < UPL; ++i) {
-        const int u = lane + 32 * i;
-        if (u < d / 32) load_x_unit(f, u, xr[i]);
-    }
-#pragma unroll
-    for (int i = 0; i < UPL; ++i) {
-        const int u = lane + 32 * i;
-        xs[i] = 0.f;
-        if (u < d / 32) {
-#pragma unroll
-            for (int q = 0; q < 32; ++q) xs[i] += xr[i][q];
-            if ((u & 7) == warp) {
-                float4 *dx = reinterpret_cast<float4 *>(sm_x + 32 * u);
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    dx[q] = make_float4(xr[i][4 * q], xr[i][4 * q + 1], xr[i][4 * q + 2], xr[i][4 * q + 3]);
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        if (t < xwn) load_x_word(f, t, v);
+        uint2 pl[kXB];
+        float usum;
+        const float sc = quant_word<kXB>(v, pl, &usum);
+        if (t < xwn) {
+            rx_store(rx, t, v);
+            store_word<kXB>(xq, xwn, t, pl);
+            if ((t & 3) == 0) {
+                xusc[t >> 2] = sc;
+                xusm[t >> 2] = usum;
             }
         }
     }
     __syncthreads();
+    const unsigned long long base = s_base;
+    // every lane: its x units in registers
+    uint2 xw[UPL][kXB][4];
+    float xsc[UPL], xsm[UPL];
+#pragma unroll
+    for (int i = 0; i < UPL; ++i) {
+        const int u = lane + 32 * i;
+        if (u < d / 32) {
+            load_unit<kXB>(xq, xwn, u, xw[i]);
+            xsc[i] = xusc[u];
+            xsm[i] = xusm[u];
+        } else {
+#pragma unroll
+            for (int pp = 0; pp < kXB; ++pp)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) xw[i][pp][q] = make_uint2(0u, 0u);
+            xsc[i] = 0.f;
+            xsm[i] = 0.f;
+        }
+    }
     STAMP(13);
     const bool ok0 = mbar_wait(&bar[0], 0);
     STAMP(2);
     if (!ok0 && tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
     if (ok0) {
-        for (int r = rr0 + warp; r < rr1; r += 8) {
+        for (int r = rr0 + warp; r < rr1; r += kWarps) {
             const uint16_t *w =
                 reinterpret_cast<const uint16_t *>(sm_router + static_cast<size_t>(r - rr0) * d * 2);
-            const double s = warp_sum_butterfly(router_lane(w, sm_x, d, lane));
+            const double s = warp_sum_butterfly(router_lane(w, rx, d, lane));
+            STAMP(15);
             if (lane == 0) {
                 float v = static_cast<float>(s);
                 if (r < E && f.logit_bias) v = v + f.logit_bias[r];
-                f.logits[r] = v;
+                lg[r] = v;
             }
         }
     }
     STAMP(3);
-    grid_sync(gbar, G, f.err);
+    grid_arrive_wait(sync, base + G, f.err);
     STAMP(4);
 
-    // ---- phase 2
-    topk_stage_keys<true>(f.logits, E, s_keys, tid, blockDim.x);
-    __syncthreads();
+    // ---- phase 2: top-k over the whole CTA. Every warp's largest key goes to
+    // s_wmax; tau = the k-th largest of those maxima, so at least k keys are
+    // >= tau and the keys >= tau hold the top-k and everything tied with or
+    // above its members. They are gathered (in any order: the ranking
+    // compares indices) and ranked by warp 0 (topk_rank_softmax), which
+    // gives the result of topk_warp. When fewer than k warps hold keys, or
+    // more than 32 keys reach tau, warp 0 runs topk_warp on all keys.
+    const int nE = (E + 31) / 32 * 32;
+    const bool block_topk = min(kWarps, nE / 32) >= k;
+    {
+        uint32_t mine[2] = {0u, 0u};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int e = tid + h * kThreads;
+            if (e < nE) {
+                mine[h] = e < E ? fkey(__ldcg(lg + e)) : 0u;
+                s_keys[e] = mine[h];
+            }
+        }
+        if (tid == 0) {
+            s_gl = __ldcg(lg + E);
+            s_cnt = 0;
+        }
+        const uint32_t wm = __reduce_max_sync(QK_FULL, max(mine[0], mine[1]));
+        if (lane == 0) s_wmax[warp] = wm;
+        __syncthreads();
+        if (block_topk) {
+            const uint32_t mv = lane < kWarps ? s_wmax[lane] : 0u;
+            int r = 0;
+#pragma unroll
+            for (int j = 0; j < kWarps; ++j) {
+                const uint32_t o = __shfl_sync(QK_FULL, mv, j);
+                r += (o > mv || (o == mv && j < lane)) ? 1 : 0;
+            }
+            const uint32_t tau = __shfl_sync(QK_FULL, mv, __ffs(__ballot_sync(QK_FULL, r == k - 1)) - 1);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int e = tid + h * kThreads;
+                if (e < E && mine[h] >= tau && mine[h] != 0u) {
+                    const int pos = atomicAdd(&s_cnt, 1);
+                    if (pos < 32) {
+                        s_key[pos] = mine[h];
+                        s_idx[pos] = e;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+    STAMP(6);
     if (warp == 0) {
-        const bool okk = topk_warp(s_keys, E, k, s_key, s_idx, s_ev, r_idx, r_w);
-        const float gl = __ldcg(f.logits + E);
+        const int C = s_cnt;
+        bool okk;
+        if (block_topk && C >= k && C <= 32) {
+            topk_rank_softmax(C, k, s_key, s_idx, s_ev, r_idx, r_w);
+            okk = true;
+        } else {
+            okk = topk_warp(s_keys, E, k, s_key, s_idx, s_ev, r_idx, r_w);
+        }
+        STAMP(7);
         const uint8_t *sp = nullptr;
         if (okk && lane < k) {
             const int e = r_idx[lane];
@@ -275,8 +362,9 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
                 }
             }
         }
+        STAMP(14);
         if (lane == 0) {
-            r_w[k] = 1.0f / (1.0f + expf(-gl));
+            r_w[k] = 1.0f / (1.0f + expf(-s_gl));
             if (!okk) atomicOr(f.err, QK_ERR_BAD_ROUTE);
             else if (!resident) atomicOr(f.err, QK_ERR_NOT_RESIDENT);
             s_ok = good ? 1 : 0;
@@ -289,10 +377,11 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
             if (lane == 0) f.sgate[0] = r_w[k];
         }
     } else if (ok0) {
-        // warps 1..7: the shared expert's gate/up rows while warp 0 routes
-        for (int i = warp - 1; i < sr1 - sr0; i += 7) {
-            const float hv = gateup_row<UPL>(sm_sgu + static_cast<size_t>(i) * L.gu_row, L, xr, xs, lane);
-            if (lane == 0) f.h[static_cast<size_t>(k) * I + sr0 + i] = hv;
+        // warps 1..15: the shared expert's gate/up rows while warp 0 routes
+        for (int i = warp - 1; i < sr1 - sr0; i += kWarps - 1) {
+            const float hv =
+                gateup_row<UPL>(sm_sgu + static_cast<size_t>(i) * L.gu_row, L, xw, xsc, xsm, lane);
+            if (lane == 0) hf[static_cast<size_t>(k) * I + sr0 + i] = hv;
         }
     }
     __syncthreads();
@@ -303,14 +392,16 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
         // routed rows, each after its chunk has landed
         const int nr = gr1 - gr0;
         int ch = 0;
-        for (int i = warp; i < nr; i += 8) {
+        for (int i = warp; i < nr; i += kWarps) {
             while (ch + 1 < s_nchunks && s_chunk0[ch + 1] <= i) ++ch;
             if (!mbar_wait(&bar[2 + ch], 0)) {
                 ok1 = false;
                 break;
             }
-            const float hv = gateup_row<UPL>(sm_rgu + static_cast<size_t>(i) * L.gu_row, L, xr, xs, lane);
-            if (lane == 0) f.h[gr0 + i] = hv;  // slot (gr0+i)/I, row (gr0+i)%I
+            const float hv =
+                gateup_row<UPL>(sm_rgu + static_cast<size_t>(i) * L.gu_row, L, xw, xsc, xsm, lane);
+            // slot (gr0+i)/I, row (gr0+i)%I
+            if (lane == 0) hf[gr0 + i] = hv;
         }
         // every chunk has landed before sm_rgu is reused for h
         for (int q = 0; q < s_nchunks && ok1; ++q) ok1 = mbar_wait(&bar[2 + q], 0);
@@ -318,51 +409,45 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
     }
     ok1 = __syncthreads_and(ok1) != 0;  // CTA-uniform from here on
     STAMP(8);
-    grid_sync(gbar, G, f.err);
+    grid_arrive_wait(sync, base + 2ull * G, f.err);  // every CTA, on every path
     STAMP(9);
+    // every CTA of this grid has arrived, so all of them are resident: a
+    // dependent launch may take SMs as they free up
     pdl_trigger();
+    if (!live) return;
 
-    // ---- phase 3: h -> shared memory, down rows + weighted combine
-    float4 *hs4 = reinterpret_cast<float4 *>(sm_rgu);
-    float *hsum = reinterpret_cast<float *>(hs4 + S * (I / 4));
-    float *partial = hsum + S * (I / 32);  // [S][or_max]
-    const int q4 = I / 4, units = I / 32;
-    {
-        // batched: all loads of a thread before its (swizzled) stores
-        const float4 *hg = reinterpret_cast<const float4 *>(f.h);
-        const int n4 = S * q4;
-        for (int base = tid; base < n4; base += 8 * 256) {
-            float4 v[8];
+    // ---- phase 3: h -> 24-bit integers (kHB planes of S * I / 8 words, one
+    // scale and sum per 32-element unit), down rows + weighted combine
+    const int hwn = S * (I / 8), upe = I / 32;
+    uint2 *hq = reinterpret_cast<uint2 *>(sm_rgu);
+    float *husc = reinterpret_cast<float *>(hq + kHB * hwn);
+    float *husm = husc + S * upe;
+    float *partial = husm + S * upe;  // [S][or_max]
+    for (int w0 = 0; w0 < hwn; w0 += kThreads) {
+        const int w = w0 + tid;
+        float v[8];
+        if (w < hwn) {
+            const float4 *hp = reinterpret_cast<const float4 *>(hf) + 2 * w;
+            const float4 a = __ldcg(hp), b = __ldcg(hp + 1);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int i = base + u * 256;
-                if (i < n4) v[u] = __ldcg(hg + i);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int i = base + u * 256;
-                if (i < n4) {
-                    const int s = i / q4, cc = i % q4, j = cc >> 3, q = cc & 7;
-                    hs4[s * q4 + 8 * j + (q ^ (j & 7))] = v[u];
-                }
+            for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        }
+        uint2 pl[kHB];
+        float usum;
+        const float sc = quant_word<kHB>(v, pl, &usum);
+        if (w < hwn) {
+            store_word<kHB>(hq, hwn, w, pl);
+            if ((w & 3) == 0) {
+                husc[w >> 2] = sc;
+                husm[w >> 2] = usum;
             }
         }
-    }
-    __syncthreads();
-    for (int i = tid; i < S * units; i += blockDim.x) {
-        const int j = i % units;
-        const float4 *pp = hs4 + (i / units) * q4 + 8 * j;
-        float a = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float4 v = pp[q ^ (j & 7)];
-            a += v.x; a += v.y; a += v.z; a += v.w;
-        }
-        hsum[i] = a;
     }
     __syncthreads();
     STAMP(10);
-    if (!live || !ok1) return;
+    if (!ok1) return;
     if (!mbar_wait(&bar[1], 0)) {
         if (tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
         mbar_wait(&bar[1], 0);
@@ -375,22 +460,18 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
     const int nrows = or1 - or0;
     const int ngrp = (nrows + RPW - 1) / RPW;
     const int ntask = S * ngrp;
-    const int t0 = warp * ntask / 8, t1 = (warp + 1) * ntask / 8;
+    const int t0 = warp * ntask / kWarps, t1 = (warp + 1) * ntask / kWarps;
     const int j = lane % LPR;
     const int grp = (32 * j) / L.g;
     int cur = -1;
-    float hv[32];
-    float hsu = 0.f;
+    uint2 hv[kHB][4];
+    float hsc = 0.f, hsm = 0.f;
     for (int t = t0; t < t1; ++t) {
         const int s = t / ngrp, rg = t % ngrp;
         if (s != cur) {
-            const float4 *hb = hs4 + s * q4 + 8 * j;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const float4 v = hb[q ^ (j & 7)];
-                hv[4 * q + 0] = v.x; hv[4 * q + 1] = v.y; hv[4 * q + 2] = v.z; hv[4 * q + 3] = v.w;
-            }
-            hsu = hsum[s * units + j];
+            load_unit<kHB>(hq, hwn, s * upe + j, hv);
+            hsc = husc[s * upe + j];
+            hsm = husm[s * upe + j];
             cur = s;
         }
         const int rl = rg * RPW + lane / LPR;
@@ -398,15 +479,16 @@ __global__ void __launch_bounds__(256, 1) k_decode_fused(qk_fwd f, Plan p,
         const uint8_t *row = sm_down + (static_cast<size_t>(s) * p.or_max + rlc) * L.d_row;
         const uint4 w = *reinterpret_cast<const uint4 *>(row + 16 * j);
         const uint32_t sb = *reinterpret_cast<const uint32_t *>(row + I / 2 + 4 * grp);
-        const float a = dot_unit(w, hv);
-        float part_ = fmaf(bf16lo(sb), 16.f * (a - hsu), bf16hi(sb) * hsu);
+        float part_ = fmaf(bf16lo(sb), dot_unit_q<kHB>(w, hv) * hsc, bf16hi(sb) * hsm);
 #pragma unroll
         for (int off = LPR / 2; off >= 1; off >>= 1) part_ += __shfl_xor_sync(QK_FULL, part_, off);
         if (j == 0 && rl < nrows) partial[s * p.or_max + rl] = part_;
     }
+    STAMP(16);
     __syncthreads();
+    STAMP(17);
     // combine in expert order: out = sum_s w_s * partial_s (shared gate last)
-    for (int rl = tid; rl < nrows; rl += blockDim.x) {
+    for (int rl = tid; rl < nrows; rl += kThreads) {
         float acc = 0.f;
         for (int s = 0; s < S; ++s) acc = fmaf(r_w[s], partial[s * p.or_max + rl], acc);
         f.out[or0 + rl] = acc;
@@ -437,11 +519,16 @@ bool make_plan(const qk_fwd *f, Plan *p) {
     p->off_sgu = off;
     off = align128(off + p->sr_max * L.gu_row);
     p->off_rgu = off;
-    const int h_bytes = S * L.I * 4 + S * (L.I / 32) * 4 + S * p->or_max * 4;
+    // after phase 2 the routed gate/up area holds h (planes, unit scales and
+    // sums) and the per-expert partial outputs
+    const int h_bytes = kHB * S * (L.I / 8) * 8 + 2 * S * (L.I / 32) * 4 + S * p->or_max * 4;
     off = align128(off + (p->gr_max * L.gu_row > h_bytes ? p->gr_max * L.gu_row : h_bytes));
     p->off_down = off;
     off = align128(off + S * p->or_max * L.d_row);
-    off = align128(off + L.d * 4);  // x (fp32) at the end
+    p->off_xq = off;
+    off = align128(off + kXB * (L.d / 8) * 8 + 2 * (L.d / 32) * 4);
+    p->off_x = off;
+    off = align128(off + L.d * 8);
     p->total = off;
     return off <= kFusedSmemMax;
 }
@@ -452,10 +539,10 @@ const void *fused_fn() {
 }
 
 // instantiated shapes: d in (1024, 2048] with I = 512, and d <= 1024 with
-// I = 128 (E <= 1024 for both)
+// I = 128 (E <= 1024, group 64 for both)
 const void *pick(const qk_layout &L) {
     const int nunits = L.d / 32, lpr = L.I / 32;
-    if (L.E > 1024) return nullptr;
+    if (L.E > 1024 || L.g != 64) return nullptr;
     if (nunits <= 64 && nunits > 32 && lpr == 16) return fused_fn<2, 16>();
     if (nunits <= 32 && lpr == 4) return fused_fn<1, 4>();
     return nullptr;
@@ -473,13 +560,19 @@ int qk_prepare_fused() {
     return cudaSuccess;
 }
 
-extern "C" int qk_launch_decode_fused(const qk_fwd *f, unsigned *gbar, void *stream, int pdl) {
+extern "C" size_t qk_decode_sync_bytes(const qk_layout *L) {
+    return 8 * kSyncWords + 4 * static_cast<size_t>((L->E + 1 + 3) & ~3) +
+           4 * static_cast<size_t>(L->k + 1) * L->I;
+}
+
+extern "C" int qk_launch_decode_fused(const qk_fwd *f, void *sync, void *stream, int pdl) {
     if (f->T != 1) return QK_FUSED_UNFIT;
     Plan p;
     const void *fn = pick(f->L);
     if (!fn || !make_plan(f, &p) || (f->L.E & 3)) return QK_FUSED_UNFIT;
     qk_fwd a = *f;
-    unsigned long long *ctr = reinterpret_cast<unsigned long long *>(gbar);
+    unsigned long long *ctr = static_cast<unsigned long long *>(sync);
     void *args[] = {&a, &p, &ctr};
-    return qk_launch_raw(fn, dim3(p.G), dim3(256), static_cast<size_t>(p.total), stream, pdl, args);
+    return qk_launch_raw(fn, dim3(p.G), dim3(kThreads), static_cast<size_t>(p.total), stream, pdl,
+                         args);
 }

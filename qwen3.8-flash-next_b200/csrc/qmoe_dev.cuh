@@ -4,7 +4,7 @@
 // programmatic-dependent-launch controls, a bounded grid barrier, and the
 // arithmetic building blocks that define the layer's results:
 //   router_dot_smem / router_dot_lane  canonical fp64 router dot
-//   dot_unit                           32-nibble q4 dot product
+//   quant_word / dot_unit_q            integer q4 dot products
 //   topk_warp                          exact top-k + renormalised softmax
 #pragma once
 
@@ -204,6 +204,29 @@ QK_DEV unsigned long long ld_acquire64(const unsigned long long *p) {
     return v;
 }
 
+// Arrives at a grid barrier and waits for it: the CTA's writes so far are
+// released (__syncthreads, then one red.release), then one thread polls the
+// counter (acquire) until it reaches `target`. The caller knows the target
+// (its launch's base plus the number of CTAs times the barrier's ordinal),
+// so the arrive needs no reply. Bounded: on timeout QK_ERR_TIMEOUT_GRID is
+// set and the CTA goes on (that launch's results are invalid).
+QK_DEV void grid_arrive_wait(unsigned long long *ctr, unsigned long long target, int *err) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(ctr) : "memory");
+        if (ld_acquire64(ctr) < target) {
+            const uint64_t t0 = gtimer();
+            while (ld_acquire64(ctr) < target) {
+                if (gtimer() - t0 > kWaitNs) {
+                    atomicOr(err, QK_ERR_TIMEOUT_GRID);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
 // Grid-wide barrier for a grid whose CTAs are all resident. `ctr` is a 64-bit
 // counter that only grows: each CTA adds 1 with release semantics and waits
 // (acquire) until the counter reaches the next multiple of the grid size,
@@ -234,51 +257,160 @@ QK_DEV bool grid_sync(unsigned long long *ctr, unsigned nctas, int *err) {
     return s_ok != 0;
 }
 
-// Dot product of 32 nibbles (one 16-byte unit, low nibble first) with x:
-// returns sum_i x_i * (1 + q_i / 16). The caller recovers sum x_i q_i as
-// 16 * (result - sum x_i). Building 1 + q/16 costs one shift and one LOP3
-// (exponent 127 OR'd over the nibble placed at mantissa bits 19..22), so each
-// weight is one FFMA with no int->float conversion.
-QK_DEV float dot_unit(uint4 w, const float *x) {
-    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
-    float a0 = 0.f, a1 = 0.f;
+// Integer q4 dot products. A q4 row times a vector v is, per 64-element
+// group, s * sum(q_i v_i) + b * sum(v_i) (w = q s + b, the dequantised
+// weights of model.c:1371-1375). v is stored once as integers
+// v_i = round(v_i * 2^e), one power-of-two scale per 64 elements, in NB byte
+// planes (plane 0 the signed high byte, the others unsigned): NB = 2 keeps 15
+// significant bits of the group's largest |v| (used for x), NB = 3 keeps 22
+// (used for h, whose groups have a much wider range). A q4 word w (8
+// nibbles, low first) gives its even nibbles as the bytes of w & 0x0F0F0F0F
+// and its odd ones as the bytes of (w >> 4) & 0x0F0F0F0F, so sum(q_i v_i)
+// over the word is 2 NB dp4a (even/odd per plane), exact in int32: 0.9 (NB=2)
+// or 1.1 (NB=3) instructions per weight against about 3 for a float
+// dequantise-and-FMA. Each plane of a word is a uint2 {even bytes, odd
+// bytes}; a vector of n words stores plane p at [p * n, (p + 1) * n).
+
+// 2^e for e in [-126, 127]
+QK_DEV float pow2i(int e) { return __int_as_float((127 + e) << 23); }
+
+// Quantises the 8 values of one q4 word position into NB planes. The calling
+// thread is lane 8a + r (r < 8) of a group of 8 consecutive lanes that
+// together hold one 64-element group; every lane of the warp calls (inactive
+// lanes pass zeros). Returns the group's scale 2^-e; *usum gets the unit's
+// (4 words, 32 elements) sum of the quantised values, scaled back. A group
+// with a non-finite value gets a NaN scale, so its dot products come out NaN
+// as the float ones would.
+template <int NB>
+QK_DEV float quant_word(const float (&v)[8], uint2 (&pl)[NB], float *usum) {
+    constexpr int kBits = NB == 2 ? 15 : 22;  // largest |v| 2^e in [2^(kBits-1), 2^kBits)
+    constexpr int kMax = (1 << (8 * NB - 1)) - 1;
+    float m = 0.f;
+    bool fin = true;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int i = 0; i < 8; ++i) {
+        m = fmaxf(m, fabsf(v[i]));
+        fin = fin && isfinite(v[i]);
+    }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int sh = 19 - 4 * i;
-            const uint32_t b = sh >= 0 ? (wd[j] << sh) : (wd[j] >> (-sh));
-            const float fq = __uint_as_float((b & 0x00780000u) | 0x3F800000u);
-            if (i & 1)
-                a1 = fmaf(x[8 * j + i], fq, a1);
-            else
-                a0 = fmaf(x[8 * j + i], fq, a0);
+    for (int off = 1; off < 8; off <<= 1) m = fmaxf(m, __shfl_xor_sync(QK_FULL, m, off));
+    const unsigned bad = __ballot_sync(QK_FULL, !fin);
+    const int lane = threadIdx.x & 31;
+    const bool gfin = ((bad >> (lane & ~7)) & 0xFFu) == 0u;
+    int ex = 0;
+    frexpf(m, &ex);  // m = f 2^ex, f in [0.5, 1)
+    int e = m > 0.f ? kBits - ex : 0;
+    e = min(max(e, -126), 126);
+    const float up = pow2i(e);
+#pragma unroll
+    for (int p = 0; p < NB; ++p) pl[p] = make_uint2(0u, 0u);
+    int isum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int q = gfin ? min(__float2int_rn(v[i] * up), kMax) : 0;
+        isum += q;
+        const int sh = 8 * (i >> 1);
+#pragma unroll
+        for (int p = 0; p < NB; ++p) {
+            const uint32_t b = (static_cast<uint32_t>(q >> (8 * (NB - 1 - p))) & 0xFFu) << sh;
+            if (i & 1) pl[p].y |= b;
+            else pl[p].x |= b;
         }
     }
-    return a0 + a1;
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) isum += __shfl_xor_sync(QK_FULL, isum, off);
+    const float scale = gfin ? pow2i(-e) : __int_as_float(0x7fc00000);
+    *usum = static_cast<float>(isum) * scale;
+    return scale;
+}
+
+// Stores one quantised word (NB planes) at word w of a vector of n words.
+template <int NB>
+QK_DEV void store_word(uint2 *planes, int n, int w, const uint2 (&pl)[NB]) {
+#pragma unroll
+    for (int p = 0; p < NB; ++p) planes[static_cast<size_t>(p) * n + w] = pl[p];
+}
+
+// The 4 words of unit u (NB planes) of a quantised vector of n words.
+template <int NB>
+QK_DEV void load_unit(const uint2 *planes, int n, int u, uint2 (&v)[NB][4]) {
+#pragma unroll
+    for (int p = 0; p < NB; ++p) {
+        const uint4 *s = reinterpret_cast<const uint4 *>(planes + static_cast<size_t>(p) * n + 4 * u);
+        const uint4 a = s[0], b = s[1];
+        v[p][0] = make_uint2(a.x, a.y);
+        v[p][1] = make_uint2(a.z, a.w);
+        v[p][2] = make_uint2(b.x, b.y);
+        v[p][3] = make_uint2(b.z, b.w);
+    }
+}
+
+// sum(q_i v_i) over one 16-byte unit (32 nibbles), in units of the scale:
+// exact for NB = 2 (below 2^24), one fp32 rounding for NB = 3.
+template <int NB>
+QK_DEV float dot_unit_q(const uint4 &w, const uint2 (&v)[NB][4]) {
+    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+    int hi = 0;
+    unsigned mid = 0, lo = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t ev = wd[i] & 0x0F0F0F0Fu, od = (wd[i] >> 4) & 0x0F0F0F0Fu;
+        hi = __dp4a(static_cast<int>(ev), static_cast<int>(v[0][i].x), hi);
+        hi = __dp4a(static_cast<int>(od), static_cast<int>(v[0][i].y), hi);
+        if (NB == 3) {
+            mid = __dp4a(ev, v[1][i].x, mid);
+            mid = __dp4a(od, v[1][i].y, mid);
+        }
+        lo = __dp4a(ev, v[NB - 1][i].x, lo);
+        lo = __dp4a(od, v[NB - 1][i].y, lo);
+    }
+    if (NB == 2) return static_cast<float>(hi * 256 + static_cast<int>(lo));
+    return fmaf(static_cast<float>(hi), 65536.f, static_cast<float>(mid * 256u + lo));
+}
+
+// bf16 bits (low 16 bits of b) -> double, exactly. Normal numbers are
+// rebuilt with integer operations (sign; exponent + 1023 - 127; the 7
+// mantissa bits on top of the double's); zero, subnormals, infinities and
+// NaN take the conversion instruction, which on this GPU issues at a small
+// fraction of the rate of the integer path.
+QK_DEV double bf16_to_f64(uint32_t b) {
+    const uint32_t e = (b >> 7) & 0xFFu;
+    if (e - 1u >= 254u) return static_cast<double>(__uint_as_float(b << 16));
+    const uint32_t hi = ((b & 0x8000u) << 16) | (((b & 0x7FFFu) << 13) + (896u << 20));
+    return __hiloint2double(static_cast<int>(hi), 0);
+}
+
+// Staged x for the canonical router dot: element k = 256 i + 8 l + j (lane
+// l, j < 8) sits in double2 slot (4 i + j / 2) * 32 + l, so each lane's
+// 128-bit reads are consecutive across the warp. rx_slot gives the slot of
+// the pair (8 t + 2 q, 8 t + 2 q + 1) for word t = 32 i + l.
+QK_DEV int rx_slot(int t, int q) { return ((t >> 5) * 4 + q) * 32 + (t & 31); }
+
+// Stores x word t (8 values) into the staged layout.
+QK_DEV void rx_store(double2 *rx, int t, const float (&v)[8]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        rx[rx_slot(t, q)] = make_double2(static_cast<double>(v[2 * q]), static_cast<double>(v[2 * q + 1]));
 }
 
 // Lane part of the canonical router dot (see oracle/moe_oracle.c,
 // oracle_router_dot): lane l owns k = 256*i + 8*l + j; eight fp64 sums a[j]
 // over i ascending; exact products; folded ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)).
 // The caller finishes with a butterfly over lanes 16..1 and one rounding.
-QK_DEV double router_lane(const uint16_t *w, const float *x, int d, int lane) {
+// w: d bf16 values; rx: x staged by rx_store (d a multiple of 256).
+QK_DEV double router_lane(const uint16_t *w, const double2 *rx, int d, int lane) {
     double a[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) a[j] = 0.0;
 #pragma unroll 4
-    for (int base = 0; base < d; base += 256) {
-        const int k0 = base + 8 * lane;
-        if (k0 < d) {
-            const uint4 wv = *reinterpret_cast<const uint4 *>(w + k0);
-            const float4 x0 = *reinterpret_cast<const float4 *>(x + k0);
-            const float4 x1 = *reinterpret_cast<const float4 *>(x + k0 + 4);
-            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            const float wf[8] = {bf16lo(wv.x), bf16hi(wv.x), bf16lo(wv.y), bf16hi(wv.y),
-                                 bf16lo(wv.z), bf16hi(wv.z), bf16lo(wv.w), bf16hi(wv.w)};
+    for (int i = 0; i < d / 256; ++i) {
+        const uint4 wv = *reinterpret_cast<const uint4 *>(w + 256 * i + 8 * lane);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                a[j] = fma(static_cast<double>(xv[j]), static_cast<double>(wf[j]), a[j]);
+        for (int q = 0; q < 4; ++q) {
+            const double2 xv = rx[(4 * i + q) * 32 + lane];
+            a[2 * q] = fma(xv.x, bf16_to_f64(ww[q] & 0xFFFFu), a[2 * q]);
+            a[2 * q + 1] = fma(xv.y, bf16_to_f64(ww[q] >> 16), a[2 * q + 1]);
         }
     }
     return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
@@ -439,8 +571,10 @@ QK_DEV void topk_rank_softmax(int C, int k, uint32_t *s_key, int *s_idx, float *
         s_ev[rank] = ev;
     }
     __syncwarp();
+    // the sum in rank order (the order of model.c:1311-1316), read by shuffles
+    const float evr = lane < k ? s_ev[lane] : 0.f;
     float sum = 0.f;
-    for (int m = 0; m < k; ++m) sum += s_ev[m];
+    for (int m = 0; m < k; ++m) sum += __shfl_sync(QK_FULL, evr, m);
     if (mine) {
         idx_out[rank] = mi;
         w_out[rank] = ev / sum;

@@ -46,7 +46,7 @@ enum {
     QK_ERR_TIMEOUT_COPY = 1,  /* bulk-copy completion wait gave up */
     QK_ERR_NOT_RESIDENT = 2,  /* a routed expert had no HBM slot */
     QK_ERR_BAD_ROUTE = 4,     /* top-k found fewer than k finite logits */
-    QK_ERR_TIMEOUT_GRID = 8,  /* grid barrier wait gave up */
+    QK_ERR_TIMEOUT_GRID = 8,  /* grid barrier or cross-CTA exchange wait gave up */
 };
 
 /* Everything one forward call needs on the device. */
@@ -70,7 +70,7 @@ typedef struct {
     int *err;                    /* device error word */
     int num_sms;
     unsigned long long *ptimes;  /* diagnostics: per-CTA phase timestamps
-                                    [grid][16] (%globaltimer ns), or NULL */
+                                    [grid][32] (%globaltimer ns), or NULL */
 } qk_fwd;
 
 /* Kernel launchers (qmoe_kernels.cu). Each returns a cudaError_t as int.
@@ -85,12 +85,17 @@ int qk_launch_decode_gateup(const qk_fwd *f, void *stream, int pdl);
 int qk_launch_decode_down(const qk_fwd *f, void *stream, int pdl);
 
 /* Single-launch decode (T == 1): router, top-k, gate/up and down+combine in
- * one persistent kernel with one CTA per SM and grid barriers between the
- * phases. gbar: two zeroed u32 in device memory owned by the context.
+ * one persistent kernel with one CTA per SM; the CTAs exchange the logits
+ * and h through epoch-tagged words. sync: qk_decode_sync_bytes(L) bytes of
+ * device memory owned by the caller (a launch counter, then the exchange
+ * area), zeroed before the first launch and again after a launch that
+ * reported an error; successive launches on it must be stream-ordered.
+ * Only idx, wts, sgate and out of f are written (not logits or h).
  * Returns QK_FUSED_UNFIT (no launch) when the shape's per-CTA working set does
  * not fit in shared memory; the caller then uses the four-kernel path. */
 #define QK_FUSED_UNFIT (-7)
-int qk_launch_decode_fused(const qk_fwd *f, unsigned *gbar, void *stream, int pdl);
+size_t qk_decode_sync_bytes(const qk_layout *L);
+int qk_launch_decode_fused(const qk_fwd *f, void *sync, void *stream, int pdl);
 
 /* Prefill / multi-token path (qmoe_prefill.cu): tokens grouped by expert, a
  * tcgen05 grouped GEMM for gate/up (SiLU x up epilogue) and for down, and a

@@ -33,27 +33,19 @@ __device__ const uint8_t *slot_of_token(const qk_fwd &f, int t, int s) {
     return f.pool + static_cast<size_t>(slot) * f.L.slot_bytes;
 }
 
-__device__ void load_x32(const qk_fwd &f, int t, int u, float *xr) {
+// Elements 8w .. 8w + 7 of token t's x (bf16 or fp32).
+__device__ void load_x8(const qk_fwd &f, int t, int w, float *v) {
     const int d = f.L.d;
     if (f.x_bf16) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(
-            static_cast<const uint16_t *>(f.x) + static_cast<size_t>(t) * d + 32 * u);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const uint4 v = p[q];
-            xr[8 * q + 0] = bf16lo(v.x); xr[8 * q + 1] = bf16hi(v.x);
-            xr[8 * q + 2] = bf16lo(v.y); xr[8 * q + 3] = bf16hi(v.y);
-            xr[8 * q + 4] = bf16lo(v.z); xr[8 * q + 5] = bf16hi(v.z);
-            xr[8 * q + 6] = bf16lo(v.w); xr[8 * q + 7] = bf16hi(v.w);
-        }
+        const uint4 q = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(f.x) +
+                                                        static_cast<size_t>(t) * d)[w];
+        v[0] = bf16lo(q.x); v[1] = bf16hi(q.x); v[2] = bf16lo(q.y); v[3] = bf16hi(q.y);
+        v[4] = bf16lo(q.z); v[5] = bf16hi(q.z); v[6] = bf16lo(q.w); v[7] = bf16hi(q.w);
     } else {
-        const float4 *p = reinterpret_cast<const float4 *>(
-            static_cast<const float *>(f.x) + static_cast<size_t>(t) * d + 32 * u);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float4 v = p[q];
-            xr[4 * q + 0] = v.x; xr[4 * q + 1] = v.y; xr[4 * q + 2] = v.z; xr[4 * q + 3] = v.w;
-        }
+        const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(f.x) +
+                                                           static_cast<size_t>(t) * d) + 2 * w;
+        const float4 a = p[0], b = p[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     }
 }
 
@@ -62,7 +54,7 @@ __device__ void load_x32(const qk_fwd &f, int t, int u, float *xr) {
 // computes one row (rows 0..E-1 are mlp.gate, row E is the shared-expert
 // gate) in the canonical order of router_lane, identical to the CPU oracle.
 __global__ void __launch_bounds__(256) k_router(qk_fwd f) {
-    extern __shared__ __align__(16) float xs[];
+    extern __shared__ __align__(16) double2 rx[];
     pdl_wait();
     pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -82,13 +74,12 @@ __global__ void __launch_bounds__(256) k_router(qk_fwd f) {
             const float4 a = p[0], b = p[1];
             v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
         }
-        reinterpret_cast<float4 *>(xs + i0)[0] = make_float4(v[0], v[1], v[2], v[3]);
-        reinterpret_cast<float4 *>(xs + i0)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        rx_store(rx, i0 / 8, v);
     }
     __syncthreads();
     for (int r = blockIdx.x * 8 + warp; r <= E; r += gridDim.x * 8) {
         const uint16_t *w = r < E ? f.router + static_cast<size_t>(r) * d : f.shared_gate;
-        const double s = warp_sum_butterfly(router_lane(w, xs, d, lane));
+        const double s = warp_sum_butterfly(router_lane(w, rx, d, lane));
         if (lane == 0) {
             float v = static_cast<float>(s);
             if (r < E && f.logit_bias) v = v + f.logit_bias[r];
@@ -127,14 +118,20 @@ __global__ void __launch_bounds__(256) k_topk(qk_fwd f) {
 // Gate/up: rows r in [0, (k+1)*I) enumerate (expert slot s = r / I, h-row
 // n = r % I); slot k is the shared expert. A CTA streams its contiguous row
 // range into shared memory (one bulk copy per expert it touches) while its
-// lanes load their slice of x into registers: lane l owns the 32-element
-// units u = l, l + 32, ... (UPL units). One warp per h-row reduces the gate
-// and up partial dots and writes h = SiLU(g) * u (fp32; model.c:1373-1374).
+// threads put x into 16-bit integers (quant_word) and each lane takes its
+// slice into registers: lane l owns the 32-element units u = l, l + 32, ...
+// (UPL units). One warp per h-row reduces the gate and up partial dots and
+// writes h = SiLU(g) * u (fp32; model.c:1373-1374). The arithmetic is the
+// single-launch decode kernel's, so both give the same bits.
+constexpr int kMaxD = 4096;  // largest hidden size of the per-token kernels
+
 template <int UPL>
 __global__ void __launch_bounds__(256, 1) k_decode_gateup(qk_fwd f, int rows_per_cta) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int ok;
+    __shared__ __align__(16) uint2 xq[2 * (kMaxD / 8)];
+    __shared__ float xusc[kMaxD / 32], xusm[kMaxD / 32];
     const qk_layout &L = f.L;
     const int t = blockIdx.y;
     const int total = (L.k + 1) * L.I;
@@ -168,20 +165,38 @@ __global__ void __launch_bounds__(256, 1) k_decode_gateup(qk_fwd f, int rows_per
             }
         }
     }
-    const int nunits = L.d / 32;
-    float xr[UPL][32];
-    float xsum[UPL];
+    const int nunits = L.d / 32, xwn = L.d / 8;
+    for (int w0 = 0; w0 < xwn; w0 += blockDim.x) {
+        const int w = w0 + threadIdx.x;
+        float v[8];
+        if (w < xwn) {
+            load_x8(f, t, w, v);
+        } else {
 #pragma unroll
-    for (int i = 0; i < UPL; ++i) {
-        const int u = lane + 32 * i;
-        xsum[i] = 0.f;
-        if (u < nunits) {
-            load_x32(f, t, u, xr[i]);
-#pragma unroll
-            for (int q = 0; q < 32; ++q) xsum[i] += xr[i][q];
+            for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        }
+        uint2 pl[2];
+        float usum;
+        const float sc = quant_word<2>(v, pl, &usum);
+        if (w < xwn) {
+            store_word<2>(xq, xwn, w, pl);
+            if ((w & 3) == 0) {
+                xusc[w >> 2] = sc;
+                xusm[w >> 2] = usum;
+            }
         }
     }
     __syncthreads();
+    uint2 xw[UPL][2][4];
+    float xsc[UPL], xsm[UPL];
+#pragma unroll
+    for (int i = 0; i < UPL; ++i) {
+        const int u = lane + 32 * i;
+        const int uc = u < nunits ? u : 0;
+        load_unit<2>(xq, xwn, uc, xw[i]);
+        xsc[i] = u < nunits ? xusc[uc] : 0.f;
+        xsm[i] = u < nunits ? xusm[uc] : 0.f;
+    }
     if (!ok) return;
     if (!mbar_wait(&bar, 0)) {
         if (threadIdx.x == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
@@ -200,10 +215,10 @@ __global__ void __launch_bounds__(256, 1) k_decode_gateup(qk_fwd f, int rows_per
                 const uint4 uw = *reinterpret_cast<const uint4 *>(row + half + 16 * u);
                 const int grp = (32 * u) / L.g;
                 const uint2 sb = *reinterpret_cast<const uint2 *>(row + L.d + 8 * grp);
-                const float ag = dot_unit(gw, xr[i]);
-                const float au = dot_unit(uw, xr[i]);
-                pg += fmaf(bf16lo(sb.x), 16.f * (ag - xsum[i]), bf16hi(sb.x) * xsum[i]);
-                pu += fmaf(bf16lo(sb.y), 16.f * (au - xsum[i]), bf16hi(sb.y) * xsum[i]);
+                const float ag = dot_unit_q<2>(gw, xw[i]) * xsc[i];
+                const float au = dot_unit_q<2>(uw, xw[i]) * xsc[i];
+                pg += fmaf(bf16lo(sb.x), ag, bf16hi(sb.x) * xsm[i]);
+                pu += fmaf(bf16lo(sb.y), au, bf16hi(sb.y) * xsm[i]);
             }
         }
 #pragma unroll
@@ -224,8 +239,8 @@ __global__ void __launch_bounds__(256, 1) k_decode_gateup(qk_fwd f, int rows_per
 // computes them for all k+1 experts, so the weighted combine
 //   out[n] = sum_s w_s * (Wd_s . h_s)[n] + sigmoid(g) * (Wd_sh . h_sh)[n]
 // happens in registers and each output is written once. LPR lanes share one
-// row (one 32-element unit each); h sits in shared memory with its 16-byte
-// chunks XOR-swizzled so the lanes' unit reads are bank-conflict free.
+// row (one 32-element unit each); h sits in shared memory as 24-bit integers
+// (quant_word), as in the single-launch decode kernel.
 template <int LPR>
 __global__ void __launch_bounds__(256, 1) k_decode_down(qk_fwd f) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -239,10 +254,12 @@ __global__ void __launch_bounds__(256, 1) k_decode_down(qk_fwd f) {
     const int nrows = min(R2, L.d - n0);
     const int S = L.k + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hwn = S * (L.I / 8), upe = L.I / 32;  // words of h, units per expert
     uint8_t *wsm = smem;
-    float4 *hs4 = reinterpret_cast<float4 *>(smem + static_cast<size_t>(S) * R2 * L.d_row);
-    float *hsum = reinterpret_cast<float *>(hs4 + S * (L.I / 4));
-    float *ws = hsum + S * (L.I / 32);
+    uint2 *hq = reinterpret_cast<uint2 *>(smem + static_cast<size_t>(S) * R2 * L.d_row);
+    float *husc = reinterpret_cast<float *>(hq + 3 * hwn);
+    float *husm = husc + S * upe;
+    float *ws = husm + S * upe;
     if (threadIdx.x == 0) mbar_init(&bar, 1);
     __syncthreads();
     // Routing is two launches back and complete, so the weight copies start
@@ -265,39 +282,30 @@ __global__ void __launch_bounds__(256, 1) k_decode_down(qk_fwd f) {
     pdl_wait();
     pdl_trigger();
     const float4 *hg = reinterpret_cast<const float4 *>(f.h + static_cast<size_t>(t) * S * L.I);
-    const int q4 = L.I / 4;
-    for (int base = threadIdx.x; base < S * q4; base += 8 * blockDim.x) {
-        float4 v[8];  // loads before stores
+    for (int w0 = 0; w0 < hwn; w0 += blockDim.x) {
+        const int w = w0 + threadIdx.x;
+        float v[8];
+        if (w < hwn) {
+            const float4 a = hg[2 * w], b = hg[2 * w + 1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int c = base + u * blockDim.x;
-            if (c < S * q4) v[u] = hg[c];
+            for (int i = 0; i < 8; ++i) v[i] = 0.f;
         }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int c = base + u * blockDim.x;
-            if (c < S * q4) {
-                const int s = c / q4, cc = c % q4, j = cc >> 3, q = cc & 7;
-                hs4[s * q4 + 8 * j + (q ^ (j & 7))] = v[u];
+        uint2 pl[3];
+        float usum;
+        const float sc = quant_word<3>(v, pl, &usum);
+        if (w < hwn) {
+            store_word<3>(hq, hwn, w, pl);
+            if ((w & 3) == 0) {
+                husc[w >> 2] = sc;
+                husm[w >> 2] = usum;
             }
         }
     }
     if (threadIdx.x < S)
         ws[threadIdx.x] = threadIdx.x < L.k ? f.wts[static_cast<size_t>(t) * L.k + threadIdx.x]
                                             : f.sgate[t];
-    __syncthreads();
-    const int units = L.I / 32;
-    for (int c = threadIdx.x; c < S * units; c += blockDim.x) {
-        const float4 *p = hs4 + (c / units) * q4 + 8 * (c % units);
-        const int j = c % units;
-        float a = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float4 v = p[q ^ (j & 7)];
-            a += v.x; a += v.y; a += v.z; a += v.w;
-        }
-        hsum[c] = a;
-    }
     __syncthreads();
     if (!ok) return;
     if (!mbar_wait(&bar, 0)) {
@@ -315,16 +323,10 @@ __global__ void __launch_bounds__(256, 1) k_decode_down(qk_fwd f) {
         const uint4 w = *reinterpret_cast<const uint4 *>(row + 16 * j);
         const int grp = (32 * j) / L.g;
         const uint32_t sb = *reinterpret_cast<const uint32_t *>(row + L.I / 2 + 4 * grp);
-        float hv[32];
-        const float4 *hb = hs4 + s * q4 + 8 * j;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float4 v = hb[q ^ (j & 7)];
-            hv[4 * q + 0] = v.x; hv[4 * q + 1] = v.y; hv[4 * q + 2] = v.z; hv[4 * q + 3] = v.w;
-        }
-        const float hsu = hsum[s * units + j];
-        const float a = dot_unit(w, hv);
-        float part = fmaf(bf16lo(sb), 16.f * (a - hsu), bf16hi(sb) * hsu);
+        uint2 hv[3][4];
+        load_unit<3>(hq, hwn, s * upe + j, hv);
+        float part = fmaf(bf16lo(sb), dot_unit_q<3>(w, hv) * husc[s * upe + j],
+                          bf16hi(sb) * husm[s * upe + j]);
 #pragma unroll
         for (int off = LPR / 2; off >= 1; off >>= 1) part += __shfl_xor_sync(QK_FULL, part, off);
         acc = fmaf(ws[s], part, acc);
@@ -406,7 +408,7 @@ extern "C" int qk_launch_router(const qk_fwd *f, void *stream, int pdl) {
     const int per_token = (f->L.E + 1 + 7) / 8;
     dim3 grid(per_token < 64 ? per_token : 64, f->T);
     return launch(reinterpret_cast<const void *>(&k_router), grid, dim3(256),
-                  static_cast<size_t>(f->L.d) * sizeof(float), stream, pdl, args);
+                  static_cast<size_t>(f->L.d) * sizeof(double), stream, pdl, args);
 }
 
 extern "C" int qk_launch_topk(const qk_fwd *f, void *stream, int pdl) {
@@ -425,7 +427,7 @@ extern "C" int qk_launch_decode_gateup(const qk_fwd *f, void *stream, int pdl) {
     const int total = (f->L.k + 1) * f->L.I;
     dim3 grid((total + rows - 1) / rows, f->T);
     const size_t smem = static_cast<size_t>(rows) * f->L.gu_row;
-    if (smem > static_cast<size_t>(kMaxDynSmem) || f->L.d / 32 > 128) return cudaErrorInvalidValue;
+    if (smem > static_cast<size_t>(kMaxDynSmem) || f->L.d > kMaxD) return cudaErrorInvalidValue;
     return launch(gateup_fn(f->L.d / 32), grid, dim3(256), smem, stream, pdl, args);
 }
 
@@ -438,8 +440,8 @@ extern "C" int qk_launch_decode_down(const qk_fwd *f, void *stream, int pdl) {
     const int S = f->L.k + 1;
     dim3 grid((f->L.d + R2 - 1) / R2, f->T);
     const size_t smem = static_cast<size_t>(S) * R2 * f->L.d_row +
-                        static_cast<size_t>(S) * f->L.I * 4 + static_cast<size_t>(S) * units * 4 +
-                        static_cast<size_t>(S) * 4;
+                        3 * static_cast<size_t>(S) * (f->L.I / 8) * 8 +
+                        2 * static_cast<size_t>(S) * units * 4 + static_cast<size_t>(S) * 4;
     const void *fn = down_fn(lpr);
     if (!fn || smem > static_cast<size_t>(kMaxDynSmem)) return cudaErrorInvalidValue;
     return launch(fn, grid, dim3(256), smem, stream, pdl, args);

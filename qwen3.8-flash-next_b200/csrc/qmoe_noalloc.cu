@@ -13,8 +13,8 @@
 // device (cudaGetSymbolAddress, with that device current) on the first call
 // for that device, and that address is what the kernel receives. Make that
 // first call before any stream capture. All calls share the array: each call
-// clears the error word and the grid-barrier counter first, and calls that
-// overlap on the GPU race on it.
+// clears the error word and the kernel's launch counter and exchange area
+// first, and calls that overlap on the GPU race on it.
 
 #include <cuda_runtime.h>
 #include <pthread.h>
@@ -84,14 +84,14 @@ extern "C" int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream
         seterr(err, "qmoe_forward_token_noalloc: unsupported shape");
         return -1;
     }
-    // scratch layout: [0,4) error word, [16,24) barrier counter, then from
-    // 256: logits [E+1], idx [k], weights [k], shared gate [1], h [(k+1)*I]
-    const size_t off_logits = 256;
-    const size_t off_idx = off_logits + up16(4 * static_cast<size_t>(L.E + 1));
+    // scratch layout: [0,4) error word; from 256 idx [k], weights [k], shared
+    // gate [1]; then the kernel's counter and exchange area
+    const size_t off_idx = 256;
     const size_t off_wts = off_idx + up16(4 * static_cast<size_t>(L.k));
     const size_t off_sg = off_wts + up16(4 * static_cast<size_t>(L.k));
-    const size_t off_h = off_sg + 16;
-    const size_t need = off_h + 4 * static_cast<size_t>(L.k + 1) * L.I;
+    const size_t off_sync = (off_sg + 16 + 255) / 256 * 256;
+    const size_t sync_bytes = qk_decode_sync_bytes(&L);
+    const size_t need = off_sync + sync_bytes;
     if (need > QMOE_NOALLOC_SCRATCH_BYTES) {
         char m[256];
         snprintf(m, sizeof(m),
@@ -123,22 +123,22 @@ extern "C" int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream
     f.pool = a->pool;
     f.slot_of = a->slot_of;
     f.shared_slot = a->shared_slot;
-    f.logits = reinterpret_cast<float *>(base + off_logits);
     f.idx = reinterpret_cast<int32_t *>(base + off_idx);
     f.wts = reinterpret_cast<float *>(base + off_wts);
     f.sgate = reinterpret_cast<float *>(base + off_sg);
-    f.h = reinterpret_cast<float *>(base + off_h);
     f.out = a->out;
     f.err = reinterpret_cast<int *>(base);
     f.num_sms = g_num_sms[dev];
 
-    // what must start at zero: the error word and the grid-barrier counter
-    e = cudaMemsetAsync(base, 0, 32, st);
+    // what must start at zero: the error word, and the kernel's launch
+    // counter and exchange area (an earlier call may have left them set)
+    e = cudaMemsetAsync(base, 0, 4, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(base + off_sync, 0, sync_bytes, st);
     if (e != cudaSuccess) {
         seterr(err, cudaGetErrorString(e));
         return -1;
     }
-    const int rc = qk_launch_decode_fused(&f, reinterpret_cast<unsigned *>(base + 16), st, 0);
+    const int rc = qk_launch_decode_fused(&f, base + off_sync, st, 0);
     if (rc == QK_FUSED_UNFIT) {
         seterr(err, "qmoe_forward_token_noalloc: shape not covered by the single-launch kernel");
         return -1;

@@ -569,7 +569,7 @@ __global__ void k_combine(const float *Y, const int *inv, const float *wts, cons
 // whose candidate set exceeds 32, or with a non-finite value, gets every
 // logit exactly instead (the one-warp path of k_topk).
 
-constexpr int kRW = 8;  // tokens (warps) per CTA of k_route_exact
+constexpr int kRW = 4;  // tokens (warps) per CTA of k_route_exact
 
 __global__ void k_route_split(const void *x, int x_bf16, int d, int T, int Tpad,
                               __nv_bfloat16 *xr, float *xnorm, MTile *tiles, int *n_mtiles) {
@@ -677,14 +677,15 @@ QK_DEV uint32_t kth_key(const uint32_t *keys, int E, int k, uint32_t *s_key) {
     return res;
 }
 
-QK_DEV float exact_logit(const RouteArgs &a, const float *xs, int e, int lane) {
+QK_DEV float exact_logit(const RouteArgs &a, const double2 *xs, int e, int lane) {
     const double s = warp_sum_butterfly(router_lane(a.router + static_cast<size_t>(e) * a.d, xs, a.d, lane));
     float v = static_cast<float>(s);
     if (a.bias) v = v + a.bias[e];
     return v;
 }
 
-// One warp per token; dynamic shared memory: kRW x (d floats of x, E keys).
+// One warp per token; dynamic shared memory: kRW x (x staged as d doubles,
+// then E keys).
 __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
     extern __shared__ __align__(16) float rsm[];
     __shared__ uint32_t s_key_all[kRW][32];
@@ -694,8 +695,8 @@ __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
     const int t = blockIdx.x * kRW + warp;
     if (t >= a.T) return;
     const int d = a.d, E = a.E, k = a.k, nE = (E + 31) / 32 * 32;
-    float *xs = rsm + static_cast<size_t>(warp) * d;
-    uint32_t *keys = reinterpret_cast<uint32_t *>(rsm + static_cast<size_t>(kRW) * d) + warp * nE;
+    double2 *xs = reinterpret_cast<double2 *>(rsm) + static_cast<size_t>(warp) * (d / 2);
+    uint32_t *keys = reinterpret_cast<uint32_t *>(rsm + static_cast<size_t>(kRW) * d * 2) + warp * nE;
     uint32_t *s_key = s_key_all[warp];
     int *s_idx = s_idx_all[warp];
     for (int c = lane; c < d / 8; c += 32) {
@@ -711,8 +712,7 @@ __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
             const float4 u = p[0], w = p[1];
             v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
         }
-        reinterpret_cast<float4 *>(xs)[2 * c] = make_float4(v[0], v[1], v[2], v[3]);
-        reinterpret_cast<float4 *>(xs)[2 * c + 1] = make_float4(v[4], v[5], v[6], v[7]);
+        rx_store(xs, c, v);
     }
     // approximate logits (+ bias, as the canonical logit adds it) -> keys
     const float *lr = a.lga + static_cast<size_t>(t) * E;
@@ -930,7 +930,7 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     // chunks; router rows past E read as zeros), the shapes' workspace
     const int nE = (L->E + 31) / 32 * 32;
     p->Tpad = (max_tokens + BM - 1) / BM * BM;
-    p->route_smem = static_cast<size_t>(kRW) * (static_cast<size_t>(L->d) + nE) * 4;
+    p->route_smem = static_cast<size_t>(kRW) * (2 * static_cast<size_t>(L->d) + nE) * 4;
     p->route_ok = L->E % 16 == 0 && L->k <= 32 && p->route_smem <= 200 * 1024;
     if (p->route_ok) {
         const size_t Tp = static_cast<size_t>(p->Tpad);
