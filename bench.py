@@ -12,8 +12,14 @@ call. A step is those 1000 sequential calls. Synthetic weights and tokens
              per step), max over ranks, summed over ranks.
   e2e        tokens/s through qmoe_forward with host buffers: every call
              copies its token host->device and its output device->host.
-  roofline   the dominant kernel's algorithmic bytes per launch / its mean
-             event-timed duration, against MEASURED_PEAKS.json hbm_gbs.
+  roofline   the decode kernel's algorithmic bytes per launch / its mean
+             duration in the timed region (the step's graph holds only that
+             kernel, one launch per token), against MEASURED_PEAKS.json
+             hbm_gbs; kernel_us_cold is the same kernel timed alone after an
+             L2 flush.
+  prefill    configs[2] beside it: one 4096-token call on a Zipf(1.1)-biased
+             layer (graph replays, CUDA events), its per-kernel split, and
+             the grouped GEMMs' algorithmic FLOP rate against bf16_tflops.
   cpu_baseline  the reference's own moe_forward (oracle/_ref, built from the
              reference sources) on the host cores, over a bounded sample.
 
@@ -48,7 +54,7 @@ UNIT = "tokens/s"
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
 # one ncu --set full capture of the kernel on this workload
 # (`ncu ... -k regex:k_decode_fused -s 8 -c 1 python bench.py --eager-tokens 20`)
-NCU_TRAFFIC = {"decode_fused": 21660416}
+NCU_TRAFFIC = {"decode_fused": 21659136}
 
 
 def peaks():
@@ -204,6 +210,75 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_T = 4096
+PREFILL_FLOP = 283467841536  # 4096 tokens x 11 experts x 6 d I (gate, up, down)
+
+
+def run_prefill_eager(n):
+    """Small case for ncu captures of the prefill kernels: n eager calls of
+    the config-2 layer (4096 tokens, Zipf(1.1) router bias)."""
+    import torch
+
+    import qmoe
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=PREFILL_T)
+    layer = qmoe.SynthLayer(cfg, SEED, zipf_s=1.1)
+    ctx = qmoe.Context(cfg)
+    ctx.upload(0, layer)
+    x = torch.from_numpy(qmoe.synth_tokens(SEED, 3, PREFILL_T, D)).cuda().to(torch.bfloat16)
+    out = torch.empty((PREFILL_T, D), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    for _ in range(n):
+        ctx.forward_dev(0, x.data_ptr(), qmoe.QMOE_BF16, PREFILL_T, out.data_ptr(), None)
+    ctx.sync()
+    ctx.close()
+    print(f"prefill eager case: {n} calls ok")
+
+
+def measure_prefill(ctx, layer_index, rank, reps=5, warmup=3):
+    """configs[2] on this rank's GPU: whole-call time (graph replays, CUDA
+    events on the launching stream) and the per-kernel split."""
+    import torch
+
+    import qmoe
+    x = torch.from_numpy(qmoe.synth_tokens(SEED, 3 + rank, PREFILL_T, D)).cuda().to(torch.bfloat16)
+    out = torch.empty((PREFILL_T, D), dtype=torch.float32, device="cuda")
+    st = torch.cuda.Stream()
+    cs = st.cuda_stream
+    torch.cuda.synchronize()
+    ctx.forward_dev(layer_index, x.data_ptr(), qmoe.QMOE_BF16, PREFILL_T, out.data_ptr(), cs)
+    st.synchronize()
+    ctx.sync()
+    ctx.capture_begin(cs)
+    ctx.forward_dev(layer_index, x.data_ptr(), qmoe.QMOE_BF16, PREFILL_T, out.data_ptr(), cs)
+    g = ctx.capture_end(cs)
+    for _ in range(warmup):
+        g.launch(cs)
+    st.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        g.launch(cs)
+    e1.record(st)
+    st.synchronize()
+    ctx.sync()
+    ms = e0.elapsed_time(e1) / reps
+    us = ctx.profile_forward(layer_index, x.data_ptr(), qmoe.QMOE_BF16, PREFILL_T, out.data_ptr(), reps)
+    names = ["route_tc", "route_exact", "group_gather", "gemm_gateup", "gemm_down", "combine"]
+    split = {n: float(u) for n, u in zip(names, us)}
+    gemm_us = split.get("gemm_gateup", 0.0) + split.get("gemm_down", 0.0)
+    _, bf16, src = peaks()
+    tf = PREFILL_FLOP / (gemm_us * 1e-6) / 1e12 if gemm_us > 0 else None
+    del g
+    return {"workload": "config2: one MoE layer, prefill 4096 tokens, Zipf(1.1) router bias",
+            "tokens_per_s": PREFILL_T / (ms / 1e3), "ms_per_call": ms, "kernel_us": split,
+            "gpu_launches_per_call": 10,
+            "gemm": {"bound": "tensor", "achieved": tf, "peak": bf16, "unit": "TFLOP/s",
+                     "frac": (tf / bf16) if tf else None, "flop_per_call": PREFILL_FLOP,
+                     "peak_source": src, "note": "algorithmic FLOPs of the two grouped GEMMs "
+                     "over their event-timed durations; the down GEMM issues two fp16 MMAs "
+                     "(h as a hi/lo pair) per algorithmic one"}}
+
+
 def run_eager(n):
     """Small case for ncu captures: n single-token forwards launched eagerly
     on the config-1 layer (906 MB of experts, larger than L2)."""
@@ -234,12 +309,18 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--eager-tokens", type=int, default=0,
                     help="profiling case: run N single-token forwards eagerly (no graph) and exit")
+    ap.add_argument("--prefill-eager", type=int, default=0,
+                    help="profiling case: run N eager 4096-token prefill calls and exit")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] leg")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
         return
     if args.eager_tokens:
         run_eager(args.eager_tokens)
+        return
+    if args.prefill_eager:
+        run_prefill_eager(args.prefill_eager)
         return
 
     import torch
@@ -260,10 +341,15 @@ def main():
         if world > 1:
             dist.barrier()
 
-    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=4, device=local)
+    # layer 0: configs[1] (decode); layer 1: configs[2] (Zipf-biased router)
+    nl = 1 if args.no_prefill else 2
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, layers=nl,
+                           max_tokens=4 if args.no_prefill else PREFILL_T, device=local)
     layer = qmoe.SynthLayer(cfg, SEED)
     ctx = qmoe.Context(cfg)
     ctx.upload(0, layer)
+    if not args.no_prefill:
+        ctx.upload(1, qmoe.SynthLayer(cfg, SEED, 1, zipf_s=1.1))
     x_host = qmoe.synth_tokens(SEED, rank, TOKENS, D)
     x_dev = torch.from_numpy(x_host).cuda().to(torch.bfloat16).contiguous()
     out_dev = torch.empty((TOKENS, D), dtype=torch.float32, device="cuda")
@@ -350,9 +436,15 @@ def main():
     dom = max(per_launch_ms, key=per_launch_ms.get)
     kb = kernel_bytes_per_token()
     hbm, _, src = peaks()
-    achieved = kb[dom] / (per_launch_ms[dom] / 1e3) / 1e9
+    # the timed region holds only the decode kernel, one launch per token
+    timed_launch_ms = ms / (args.steps * TOKENS)
+    achieved = kb[dom] / (timed_launch_ms / 1e3) / 1e9
     traffic = NCU_TRAFFIC.get(dom)
     layer_gbs = layer_bytes_per_token() * (value / world) / 1e9
+
+    prefill = None
+    if not args.no_prefill:
+        prefill = measure_prefill(ctx, 1, rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -381,11 +473,13 @@ def main():
                          "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
                          "peak_source": src,
                          "bytes_per_launch": kb[dom],
-                         "kernel_us": {n: 1e3 * v for n, v in per_launch_ms.items()},
+                         "kernel_us": {dom: 1e3 * timed_launch_ms},
+                         "kernel_us_cold": {n: 1e3 * v for n, v in per_launch_ms.items()},
                          "layer_gbs": layer_gbs, "layer_frac": layer_gbs / hbm},
             "cpu_baseline": cpu,
             "clocks": clk,
             "parity_spot_check": parity_ok,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     ctx.close()

@@ -145,16 +145,16 @@ int qmoe_sync(qmoe_ctx *ctx, qmoe_err *err);
  *              (2 bf16) | zeros to a multiple of 16 bytes;
  *   q rows are the checkpoint rows verbatim (u32 words, low nibble first).
  * The call's intermediates (routing, the router logits and gate/up
- * activations that the kernel's thread blocks exchange, a launch counter and
- * an error word) live in one device array of QMOE_NOALLOC_SCRATCH_BYTES
+ * activations that the kernel's thread blocks exchange, a grid-barrier
+ * counter and an error word) live in one device array of QMOE_NOALLOC_SCRATCH_BYTES
  * defined inside the library; every GPU that loads the library holds it until
- * the process exits. A shape needing more than that (8 * ((E + 1) + (k + 1) *
- * I + 32) bytes plus 512) is rejected with an error, as is a shape the
- * single-launch decode kernel does not cover.
+ * the process exits. A shape needing more than that (at most
+ * 4 * (E + 4 + (k + 1) * I) + 768 bytes) is rejected with an error, as is a
+ * shape the single-launch decode kernel does not cover.
  * The first call on a device looks up the array's device address and sets
  * kernel attributes, with that device current; make that first call before
  * any stream capture. All calls share the array and each call starts by
- * clearing its error word, launch counter and exchange area, so calls that
+ * clearing its error word, barrier counter and exchange area, so calls that
  * overlap on the GPU race; serialise them. The call waits for its work on `stream` (NULL =
  * the legacy default stream) and returns 0, or -1 with a message. */
 #define QMOE_NOALLOC_SCRATCH_BYTES (64u * 1024u)

@@ -896,7 +896,7 @@ static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err) {
     int code = *c->err_host;
     if (code) {
         /* clear the sticky word and the decode kernel's counter and exchange
-         * area (a launch that gave up may have left its epoch unfinished) */
+         * area (a launch that gave up may have left its barrier unfinished) */
         cudaMemsetAsync(c->err_dev, 0, sizeof(int), st);
         cudaMemsetAsync(c->dsync, 0, qk_decode_sync_bytes(&c->L), st);
         cudaStreamSynchronize(st);

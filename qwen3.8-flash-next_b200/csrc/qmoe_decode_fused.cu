@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     __shared__ uint32_t s_wmax[kWarps];
     __shared__ int s_cnt;
     __shared__ unsigned long long s_base;
+    __shared__ double s_rpart[kWarps][32];  // router: per-warp partial sums
     __shared__ __align__(16) int32_t s_slots[1024];  // this layer's expert -> slot table
     __shared__ uint32_t s_keys[1024];                // staged top-k keys
 
@@ -148,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 32 + (i)] = gtimer(); \
     } while (0)
     STAMP(0);
+    if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 32 + 30] = clock64();
     if (tid < 2 + kMaxChunks) mbar_init(&bar[tid], 1);
     __syncthreads();
 
@@ -158,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         const uint32_t b_sdown = static_cast<uint32_t>((or1 - or0) * L.d_row);
         const uint32_t b_slots = static_cast<uint32_t>(E * 4);
         mbar_expect_tx(&bar[0], b_router + b_sgu + b_sdown + b_slots);
+        STAMP(18);
         const int re = min(rr1, E);
         if (re > rr0)
             bulk_load(sm_router, f.router + static_cast<size_t>(rr0) * d,
@@ -172,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
             bulk_load(sm_down + static_cast<size_t>(k) * p.or_max * L.d_row,
                       f.shared_slot + L.gu_bytes + static_cast<size_t>(or0) * L.d_row, b_sdown,
                       &bar[0]);
+        STAMP(19);
         // routed gate/up chunk boundaries: runs within one expert, <= 8 rows
         int n = 0, r = gr0;
         while (r < gr1 && n < kMaxChunks) {
@@ -234,10 +238,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         }
     }
     STAMP(13);
-    const bool ok0 = mbar_wait(&bar[0], 0);
+    const bool ok0 = __syncthreads_and(mbar_wait(&bar[0], 0)) != 0;  // CTA-uniform
     STAMP(2);
     if (!ok0 && tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
-    if (ok0) {
+    const int nrr = rr1 - rr0;
+    const int wpr = nrr * 4 <= kWarps ? 4 : (nrr * 2 <= kWarps ? 2 : 1);  // warps per router row
+    if (ok0 && wpr > 1) {
+        // each row split over wpr warps (2 or 4 of the eight sums per lane),
+        // the parts folded in the canonical order, then one butterfly
+        const int rl = warp / wpr, q = warp % wpr;
+        if (rl < nrr) {
+            const uint16_t *w =
+                reinterpret_cast<const uint16_t *>(sm_router + static_cast<size_t>(rl) * d * 2);
+            s_rpart[warp][lane] = wpr == 4 ? router_lane_part<2>(w, rx, d, lane, 2 * q)
+                                           : router_lane_part<4>(w, rx, d, lane, 4 * q);
+        }
+        __syncthreads();
+        if (warp < nrr) {
+            const double *pp = &s_rpart[warp * wpr][lane];
+            const double a = wpr == 4 ? (pp[0] + pp[32]) + (pp[64] + pp[96]) : pp[0] + pp[32];
+            const double s = warp_sum_butterfly(a);
+            STAMP(15);
+            if (lane == 0) {
+                const int r = rr0 + warp;
+                float v = static_cast<float>(s);
+                if (r < E && f.logit_bias) v = v + f.logit_bias[r];
+                lg[r] = v;
+            }
+        }
+    } else if (ok0) {
         for (int r = rr0 + warp; r < rr1; r += kWarps) {
             const uint16_t *w =
                 reinterpret_cast<const uint16_t *>(sm_router + static_cast<size_t>(r - rr0) * d * 2);
@@ -305,6 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     }
     STAMP(6);
     if (warp == 0) {
+        STAMP(20);
         const int C = s_cnt;
         bool okk;
         if (block_topk && C >= k && C <= 32) {
@@ -494,6 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         f.out[or0 + rl] = acc;
     }
     STAMP(12);
+    if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 32 + 31] = clock64();
 #undef STAMP
 }
 

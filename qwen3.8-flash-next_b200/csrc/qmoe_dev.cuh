@@ -416,6 +416,31 @@ QK_DEV double router_lane(const uint16_t *w, const double2 *rx, int d, int lane)
     return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
 }
 
+// The same dot split across warps: this lane's sums a[j] for the NJ values
+// j0 .. j0 + NJ - 1 (NJ = 2 or 4, j0 a multiple of NJ), folded as the
+// canonical fold folds them, so combining the warps' parts as
+//   NJ = 2: (p0 + p1) + (p2 + p3),  NJ = 4: P0 + P1
+// gives router_lane's value bit for bit.
+template <int NJ>
+QK_DEV double router_lane_part(const uint16_t *w, const double2 *rx, int d, int lane, int j0) {
+    double a[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) a[j] = 0.0;
+#pragma unroll 4
+    for (int i = 0; i < d / 256; ++i) {
+#pragma unroll
+        for (int q2 = 0; q2 < NJ / 2; ++q2) {
+            const int q = j0 / 2 + q2;
+            const uint32_t wv = *reinterpret_cast<const uint32_t *>(w + 256 * i + 8 * lane + 2 * q);
+            const double2 xv = rx[(4 * i + q) * 32 + lane];
+            a[2 * q2] = fma(xv.x, bf16_to_f64(wv & 0xFFFFu), a[2 * q2]);
+            a[2 * q2 + 1] = fma(xv.y, bf16_to_f64(wv >> 16), a[2 * q2 + 1]);
+        }
+    }
+    if (NJ == 2) return a[0] + a[1];
+    return (a[0] + a[1]) + (a[2 % NJ] + a[3 % NJ]);
+}
+
 QK_DEV double warp_sum_butterfly(double s) {
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) s = s + __shfl_xor_sync(QK_FULL, s, off);

@@ -85,10 +85,10 @@ int qk_launch_decode_gateup(const qk_fwd *f, void *stream, int pdl);
 int qk_launch_decode_down(const qk_fwd *f, void *stream, int pdl);
 
 /* Single-launch decode (T == 1): router, top-k, gate/up and down+combine in
- * one persistent kernel with one CTA per SM; the CTAs exchange the logits
- * and h through epoch-tagged words. sync: qk_decode_sync_bytes(L) bytes of
- * device memory owned by the caller (a launch counter, then the exchange
- * area), zeroed before the first launch and again after a launch that
+ * one persistent kernel with one CTA per SM and grid barriers between the
+ * phases. sync: qk_decode_sync_bytes(L) bytes of device memory owned by the
+ * caller (the grid-barrier counter, then the logits and h the CTAs
+ * exchange), zeroed before the first launch and again after a launch that
  * reported an error; successive launches on it must be stream-ordered.
  * Only idx, wts, sgate and out of f are written (not logits or h).
  * Returns QK_FUSED_UNFIT (no launch) when the shape's per-CTA working set does

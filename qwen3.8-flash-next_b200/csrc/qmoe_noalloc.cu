@@ -13,7 +13,7 @@
 // device (cudaGetSymbolAddress, with that device current) on the first call
 // for that device, and that address is what the kernel receives. Make that
 // first call before any stream capture. All calls share the array: each call
-// clears the error word and the kernel's launch counter and exchange area
+// clears the error word and the kernel's barrier counter and exchange area
 // first, and calls that overlap on the GPU race on it.
 
 #include <cuda_runtime.h>
@@ -130,7 +130,7 @@ extern "C" int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream
     f.err = reinterpret_cast<int *>(base);
     f.num_sms = g_num_sms[dev];
 
-    // what must start at zero: the error word, and the kernel's launch
+    // what must start at zero: the error word, and the kernel's barrier
     // counter and exchange area (an earlier call may have left them set)
     e = cudaMemsetAsync(base, 0, 4, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(base + off_sync, 0, sync_bytes, st);
