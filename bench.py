@@ -279,6 +279,53 @@ def measure_prefill(ctx, layer_index, rank, reps=5, warmup=3):
                      "(h as a hi/lo pair) per algorithmic one"}}
 
 
+def measure_prefill_ep(rank, world, local, reps=5, warmup=2):
+    """configs[2] expert-parallel over the torchrun ranks: the 4096 tokens
+    split evenly, rank g owning experts [g E/W, (g+1) E/W), qmoe_forward_ep
+    on each rank (NCCL through the library). Whole-call time = max over
+    ranks of the CUDA-event time per call."""
+    import torch
+    import torch.distributed as dist
+
+    import qmoe
+    T_per = PREFILL_T // world
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=T_per, device=local,
+                           ep_rank=rank, ep_world=world)
+    ctx = qmoe.Context(cfg)
+    ctx.upload(0, qmoe.SynthLayer(cfg, SEED, 1, zipf_s=1.1))
+    uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(qmoe.ep_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    ctx.ep_connect(bytes(uid.cpu().numpy().tobytes()))
+    x_all = qmoe.synth_tokens(SEED, 3, PREFILL_T, D)
+    x = torch.from_numpy(x_all[rank * T_per:(rank + 1) * T_per]).cuda().to(torch.bfloat16)
+    out = torch.empty((T_per, D), dtype=torch.float32, device="cuda")
+    st = torch.cuda.Stream()
+    cs = st.cuda_stream
+    torch.cuda.synchronize()
+    for _ in range(warmup):
+        ctx.forward_ep(0, x.data_ptr(), qmoe.QMOE_BF16, T_per, out.data_ptr(), cs)
+    st.synchronize()
+    ctx.sync()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        ctx.forward_ep(0, x.data_ptr(), qmoe.QMOE_BF16, T_per, out.data_ptr(), cs)
+    e1.record(st)
+    st.synchronize()
+    ctx.sync()
+    tt = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda")
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    ctx.close()
+    return {"workload": "config2 expert-parallel: 4096 tokens split over the ranks, Zipf(1.1)",
+            "ranks": world, "tokens_per_s": PREFILL_T / (ms / 1e3), "ms_per_call": ms,
+            "scaling": "strong", "timing": "CUDA events per rank, max over ranks",
+            "exchange": "NCCL send/recv all-to-all of fp16 rows and fp32 outputs"}
+
+
 def run_eager(n):
     """Small case for ncu captures: n single-token forwards launched eagerly
     on the config-1 layer (906 MB of experts, larger than L2)."""
@@ -445,6 +492,8 @@ def main():
     prefill = None
     if not args.no_prefill:
         prefill = measure_prefill(ctx, 1, rank)
+        if world > 1:
+            prefill["expert_parallel"] = measure_prefill_ep(rank, world, local)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -55,6 +55,12 @@ typedef struct {
     int policy;          /* QMOE_POLICY_* for the pool (reference: ADAPTIVE) */
     int prefetch_depth;  /* prefetch_count of streaming.py (2) */
     int device;          /* CUDA device ordinal */
+    int ep_rank;         /* expert parallelism: this context's rank ... */
+    int ep_world;        /* ... of ep_world (0 or 1: no expert parallelism). Rank
+                            g holds experts [g E/W, (g+1) E/W) of every layer
+                            (E % W == 0, every expert resident) and serves
+                            qmoe_forward_ep; max_tokens is the per-rank token
+                            count of one call */
 } qmoe_config;
 
 /* One affine 4-bit tensor in the reference checkpoint layout: `rows` rows of
@@ -172,6 +178,32 @@ typedef struct {
 } qmoe_token_args;
 int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream,
                                qmoe_err *err);
+
+/* Expert parallelism over ep_world GPUs, one context (and one process or
+ * thread) per GPU, created with qmoe_config.ep_rank / ep_world. Experts are
+ * partitioned as in a config-2/3 expert-parallel run: rank g owns experts
+ * [g E/W, (g+1) E/W) of every layer; the router and the shared expert are on
+ * every rank. Rank 0 makes an id (qmoe_ep_unique_id), the caller hands it to
+ * every rank, and each rank calls qmoe_ep_connect (collective; NCCL is
+ * loaded at run time from libnccl.so.2).
+ * qmoe_forward_ep is a collective replacement of qmoe_forward_dev for the
+ * rank's own n tokens (device pointers, n may differ between ranks and may
+ * be 0): local routing, an all-to-all of (token, slot) rows to the owners of
+ * their experts, the owners' grouped GEMMs, an all-to-all of the down outputs
+ * back, then the shared expert and the weighted combine on the token's rank.
+ * It waits for the row counts on the host once per call. No reference
+ * counterpart: the C port runs on one device. */
+#define QMOE_EP_ID_BYTES 128
+int qmoe_ep_unique_id(unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err);
+int qmoe_ep_connect(qmoe_ctx *ctx, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err);
+int qmoe_forward_ep(qmoe_ctx *ctx, int layer, const void *x_dev, int x_dtype, int n,
+                    float *out_dev, void *stream, qmoe_err *err);
+/* Host form of qmoe_forward_ep's dispatch plan, the same arithmetic as its
+ * device kernels: for the routing idx [n, k] of one rank, counts[g] = rows
+ * bound for rank g (of W, E % W == 0) and, if pos is not NULL, the send
+ * position of each (token, slot): grouped by destination rank, in (token,
+ * slot) order within a rank. Returns 0, or -1 on bad arguments. */
+int qmoe_ep_plan_host(const int32_t *idx, int n, int k, int E, int W, int *counts, int *pos);
 
 /* Routing of the last forward call (waits for it): idx [n, k] in
  * (logit desc, expert asc) order, weights [n, k] (softmax renormalised over

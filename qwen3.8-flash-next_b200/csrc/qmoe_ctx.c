@@ -16,7 +16,9 @@
  * time, so a forward call allocates nothing.
  */
 #include <cuda_runtime_api.h>
+#include <dlfcn.h>
 #include <math.h>
+#include <nccl.h>
 #include <pthread.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -79,6 +81,11 @@ struct qmoe_ctx {
     int prof_kernels; /* kernels of the last forward: 1 (single launch) or 4 */
     cudaEvent_t pev[8];
     pthread_mutex_t lock;
+    /* expert parallelism */
+    int ep_world, ep_rank, ep_lo, ep_hi; /* experts [ep_lo, ep_hi) are local */
+    ncclComm_t ep_comm;
+    int *ep_counts_dev;  /* [2 * W]: rows to each rank, rows from each rank */
+    int *ep_counts_pin;  /* pinned copy */
 };
 
 static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err);
@@ -176,6 +183,48 @@ static void pack_routed(const qmoe_ctx *c, const qmoe_layer_weights *w, int e, u
                    w->down.biases + dso, slot);
 }
 
+/* ---------------------------------------------------------------- NCCL */
+
+/* NCCL is resolved at run time (dlopen of libnccl.so.2): a process that
+ * already loaded it (PyTorch does) shares that copy, and contexts that never
+ * use expert parallelism need no NCCL at all. */
+typedef struct {
+    int ok;
+    ncclResult_t (*get_unique_id)(ncclUniqueId *);
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*comm_destroy)(ncclComm_t);
+    ncclResult_t (*group_start)(void);
+    ncclResult_t (*group_end)(void);
+    ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    const char *(*error_string)(ncclResult_t);
+} nccl_fns;
+
+static nccl_fns g_nccl;
+static pthread_once_t g_nccl_once = PTHREAD_ONCE_INIT;
+
+static void nccl_load(void) {
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+    if (!h) return;
+    *(void **)&g_nccl.get_unique_id = dlsym(h, "ncclGetUniqueId");
+    *(void **)&g_nccl.comm_init_rank = dlsym(h, "ncclCommInitRank");
+    *(void **)&g_nccl.comm_destroy = dlsym(h, "ncclCommDestroy");
+    *(void **)&g_nccl.group_start = dlsym(h, "ncclGroupStart");
+    *(void **)&g_nccl.group_end = dlsym(h, "ncclGroupEnd");
+    *(void **)&g_nccl.send = dlsym(h, "ncclSend");
+    *(void **)&g_nccl.recv = dlsym(h, "ncclRecv");
+    *(void **)&g_nccl.error_string = dlsym(h, "ncclGetErrorString");
+    g_nccl.ok = g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.comm_destroy &&
+                g_nccl.group_start && g_nccl.group_end && g_nccl.send && g_nccl.recv &&
+                g_nccl.error_string;
+}
+
+static const nccl_fns *nccl_api(void) {
+    pthread_once(&g_nccl_once, nccl_load);
+    return &g_nccl;
+}
+
 /* ----------------------------------------------------------------- create */
 
 void qmoe_destroy(qmoe_ctx *c) {
@@ -216,6 +265,9 @@ void qmoe_destroy(qmoe_ctx *c) {
     free(c->recent_n);
     if (c->cache) qmoe_cache_free(c->cache);
     qk_prefill_destroy(c->prefill);
+    if (c->ep_comm) nccl_api()->comm_destroy(c->ep_comm);
+    cudaFree(c->ep_counts_dev);
+    cudaFreeHost(c->ep_counts_pin);
     if (c->copy_done) cudaEventDestroy(c->copy_done);
     for (int i = 0; i < 8; i++)
         if (c->pev[i]) cudaEventDestroy(c->pev[i]);
@@ -257,6 +309,17 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     }
     const int Lz = cfg->num_layers, E = cfg->num_experts, T = cfg->max_tokens;
     const qk_layout *L = &c->L;
+    c->ep_world = cfg->ep_world > 1 ? cfg->ep_world : 1;
+    c->ep_rank = c->ep_world > 1 ? cfg->ep_rank : 0;
+    if (c->ep_world > 1 && (E % c->ep_world || c->ep_rank < 0 || c->ep_rank >= c->ep_world ||
+                            cfg->pool_bytes != 0 || c->ep_world > 64)) {
+        seterr(err, "qmoe_create: expert parallelism needs E %% ep_world == 0, 0 <= ep_rank < "
+                    "ep_world <= 64 and every local expert resident (pool_bytes = 0)");
+        free(c);
+        return NULL;
+    }
+    c->ep_lo = c->ep_rank * (E / c->ep_world);
+    c->ep_hi = c->ep_lo + E / c->ep_world;
     CK(cudaSetDevice(cfg->device));
     CK(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, cfg->device));
     {
@@ -287,15 +350,16 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     /* pool */
     {
         uint64_t total = (uint64_t)Lz * (uint64_t)E;
-        uint64_t want = cfg->pool_bytes ? cfg->pool_bytes / L->slot_bytes : total;
-        if (want > total) want = total;
+        uint64_t local = (uint64_t)Lz * (uint64_t)(c->ep_hi - c->ep_lo);
+        uint64_t want = cfg->pool_bytes ? cfg->pool_bytes / L->slot_bytes : local;
+        if (want > local) want = local;
         if (want < (uint64_t)cfg->top_k) {
             seterr(err, "qmoe_create: pool_bytes holds %llu slots, fewer than top_k=%d",
                    (unsigned long long)want, cfg->top_k);
             goto fail;
         }
         c->nslots = (int)want;
-        c->resident_all = want == total;
+        c->resident_all = want == local;
         CK(cudaMalloc((void **)&c->pool, ((size_t)c->nslots + Lz) * L->slot_bytes));
         for (int l = 0; l < Lz; l++)
             c->layers[l].shared_slot = c->pool + ((size_t)c->nslots + l) * L->slot_bytes;
@@ -340,7 +404,19 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaMallocHost((void **)&c->x_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->out_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->idx_pin, (size_t)T * L->k * sizeof(int32_t)));
-    if (T > 1) {
+    if (c->ep_world > 1) {
+        /* a rank receives at most every rank's T tokens x k slots */
+        char msg[256] = {0};
+        c->prefill = qk_prefill_create(L, T * c->ep_world, c->pool, c->nslots + Lz, c->num_sms,
+                                       msg, sizeof(msg));
+        if (!c->prefill) {
+            seterr(err, "qmoe_create: expert parallelism needs the grouped path: %s", msg);
+            goto fail;
+        }
+        CK((cudaError_t)qk_ep_alloc(c->prefill, T * L->k, T * c->ep_world * L->k));
+        CK(cudaMalloc((void **)&c->ep_counts_dev, 2 * sizeof(int) * c->ep_world));
+        CK(cudaMallocHost((void **)&c->ep_counts_pin, 2 * sizeof(int) * c->ep_world));
+    } else if (T > 1) {
         char msg[256] = {0};
         c->prefill = qk_prefill_create(L, T, c->pool, c->nslots + Lz, c->num_sms, msg, sizeof(msg));
         /* NULL: shape outside the grouped-GEMM kernels; the per-token path runs */
@@ -542,8 +618,8 @@ int qmoe_upload_layer(qmoe_ctx *c, int layer, const qmoe_layer_weights *w, qmoe_
     ld->router_wmax = router_wmax(w->router, L->E, L->d);
     if (c->resident_all) {
         CK(cudaMallocHost((void **)&stage, (size_t)batch * L->slot_bytes));
-        for (int e0 = 0; e0 < L->E; e0 += batch) {
-            int nb = L->E - e0 < batch ? L->E - e0 : batch;
+        for (int e0 = c->ep_lo; e0 < c->ep_hi; e0 += batch) {
+            int nb = c->ep_hi - e0 < batch ? c->ep_hi - e0 : batch;
             CK(cudaStreamSynchronize(c->copy_stream));
             for (int i = 0; i < nb; i++) pack_routed(c, w, e0 + i, stage + (size_t)i * L->slot_bytes);
             pthread_mutex_lock(&c->lock);
@@ -1121,3 +1197,179 @@ int qmoe_prefetch_predictions(qmoe_ctx *c, int layer, const int32_t *selected, s
 }
 
 const char *qmoe_version(void) { return "qmoe-b200 0.1 (sm_100a)"; }
+
+/* ------------------------------------------------- expert parallelism */
+
+#define NCK(call, what)                                                                   \
+    do {                                                                                  \
+        ncclResult_t r_ = (call);                                                         \
+        if (r_ != ncclSuccess) {                                                          \
+            seterr(err, "%s: NCCL %s", what, nccl_api()->error_string(r_));               \
+            return -1;                                                                    \
+        }                                                                                 \
+    } while (0)
+
+int qmoe_ep_unique_id(unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    const nccl_fns *n = nccl_api();
+    if (!n->ok) {
+        seterr(err, "qmoe_ep_unique_id: libnccl.so.2 could not be loaded");
+        return -1;
+    }
+    ncclUniqueId u;
+    NCK(n->get_unique_id(&u), "qmoe_ep_unique_id");
+    memcpy(id, u.internal, QMOE_EP_ID_BYTES);
+    return 0;
+}
+
+int qmoe_ep_connect(qmoe_ctx *c, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || c->ep_world < 2) {
+        seterr(err, "qmoe_ep_connect: the context was created without ep_world > 1");
+        return -1;
+    }
+    const nccl_fns *n = nccl_api();
+    if (!n->ok) {
+        seterr(err, "qmoe_ep_connect: libnccl.so.2 could not be loaded");
+        return -1;
+    }
+    if (c->ep_comm) return 0;
+    ncclUniqueId u;
+    memcpy(u.internal, id, QMOE_EP_ID_BYTES);
+    if (cudaSetDevice(c->cfg.device) != cudaSuccess) {
+        seterr(err, "qmoe_ep_connect: cudaSetDevice failed");
+        return -1;
+    }
+    NCK(n->comm_init_rank(&c->ep_comm, c->ep_world, u, c->ep_rank), "qmoe_ep_connect");
+    return 0;
+}
+
+/* One collective forward: every rank calls it for the same layer with its
+ * own n tokens. Route locally; send each (token, slot) row to the rank that
+ * owns its expert (counts first, then fp16 rows and expert ids); run the
+ * grouped GEMMs on the rows received; send the down outputs back; add the
+ * shared expert of the local tokens and combine. */
+int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, float *out,
+                    void *stream, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || !c->ep_comm) {
+        seterr(err, "qmoe_forward_ep: no expert-parallel communicator (qmoe_ep_connect)");
+        return -1;
+    }
+    if (layer < 0 || layer >= c->cfg.num_layers || !c->layers[layer].ready) {
+        seterr(err, "qmoe_forward_ep: layer %d is not uploaded", layer);
+        return -1;
+    }
+    if (n < 0 || n > c->cfg.max_tokens || (n > 0 && (!x || !out))) {
+        seterr(err, "qmoe_forward_ep: n=%d outside [0, max_tokens=%d] or missing buffers", n,
+               c->cfg.max_tokens);
+        return -1;
+    }
+    if (x_dtype != QMOE_F32 && x_dtype != QMOE_BF16) {
+        seterr(err, "qmoe_forward_ep: unknown x dtype %d", x_dtype);
+        return -1;
+    }
+    const nccl_fns *nc = nccl_api();
+    const int W = c->ep_world, d = c->L.d;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    if (cudaSetDevice(c->cfg.device) != cudaSuccess) {
+        seterr(err, "qmoe_forward_ep: cudaSetDevice failed");
+        return -1;
+    }
+    qk_fwd f;
+    fill_fwd(c, layer, x, x_dtype == QMOE_BF16, n, out, &f);
+    c->last_T = n;
+    c->stats.prefill_calls++;
+    int *cnt = c->ep_counts_dev, *rcnt = c->ep_counts_dev + W;
+    void *send_x, *recv_x;
+    int32_t *send_e, *recv_e;
+    float *ret, *back;
+    qk_ep_buffers(c->prefill, &send_x, &send_e, &recv_x, &recv_e, &ret, &back);
+    if (n > 0) {
+        if (route(c, layer, &f, st, 0, NULL, err)) return -1;
+        if (kerr(qk_ep_dispatch(c->prefill, &f, W, cnt, st), "ep dispatch", err)) return -1;
+    } else if (cudaMemsetAsync(cnt, 0, sizeof(int) * W, st) != cudaSuccess) {
+        seterr(err, "qmoe_forward_ep: memset failed");
+        return -1;
+    }
+    /* row counts: to every rank, from every rank */
+    NCK(nc->group_start(), "qmoe_forward_ep");
+    for (int p = 0; p < W; p++) {
+        NCK(nc->send(cnt + p, 1, ncclInt32, p, c->ep_comm, st), "qmoe_forward_ep counts");
+        NCK(nc->recv(rcnt + p, 1, ncclInt32, p, c->ep_comm, st), "qmoe_forward_ep counts");
+    }
+    NCK(nc->group_end(), "qmoe_forward_ep");
+    cudaError_t ce = cudaMemcpyAsync(c->ep_counts_pin, c->ep_counts_dev, 2 * sizeof(int) * W,
+                                     cudaMemcpyDeviceToHost, st);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_forward_ep: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    const int *hc = c->ep_counts_pin, *hr = c->ep_counts_pin + W;
+    size_t so[64], ro[64];
+    size_t ns = 0, nr = 0;
+    for (int p = 0; p < W; p++) {
+        so[p] = ns;
+        ro[p] = nr;
+        ns += (size_t)hc[p];
+        nr += (size_t)hr[p];
+    }
+    if (nr > (size_t)c->cfg.max_tokens * W * c->L.k) {
+        seterr(err, "qmoe_forward_ep: %zu rows received, more than the plan holds", nr);
+        return -1;
+    }
+    /* rows and expert ids out, rows and expert ids in */
+    NCK(nc->group_start(), "qmoe_forward_ep");
+    for (int p = 0; p < W; p++) {
+        if (hc[p]) {
+            NCK(nc->send((const uint16_t *)send_x + so[p] * d, (size_t)hc[p] * d, ncclFloat16, p,
+                         c->ep_comm, st), "qmoe_forward_ep dispatch");
+            NCK(nc->send(send_e + so[p], (size_t)hc[p], ncclInt32, p, c->ep_comm, st),
+                "qmoe_forward_ep dispatch");
+        }
+        if (hr[p]) {
+            NCK(nc->recv((uint16_t *)recv_x + ro[p] * d, (size_t)hr[p] * d, ncclFloat16, p,
+                         c->ep_comm, st), "qmoe_forward_ep dispatch");
+            NCK(nc->recv(recv_e + ro[p], (size_t)hr[p], ncclInt32, p, c->ep_comm, st),
+                "qmoe_forward_ep dispatch");
+        }
+    }
+    NCK(nc->group_end(), "qmoe_forward_ep");
+    /* this rank's experts over the rows it received */
+    if (kerr(qk_ep_experts(c->prefill, &f, (int)nr, st), "ep experts", err)) return -1;
+    /* down outputs back to the ranks that own the tokens */
+    NCK(nc->group_start(), "qmoe_forward_ep");
+    for (int p = 0; p < W; p++) {
+        if (hr[p])
+            NCK(nc->send(ret + ro[p] * d, (size_t)hr[p] * d, ncclFloat32, p, c->ep_comm, st),
+                "qmoe_forward_ep combine");
+        if (hc[p])
+            NCK(nc->recv(back + so[p] * d, (size_t)hc[p] * d, ncclFloat32, p, c->ep_comm, st),
+                "qmoe_forward_ep combine");
+    }
+    NCK(nc->group_end(), "qmoe_forward_ep");
+    if (n > 0 && kerr(qk_ep_finish(c->prefill, &f, c->nslots + layer, st), "ep finish", err))
+        return -1;
+    return 0;
+}
+
+int qmoe_ep_plan_host(const int32_t *idx, int n, int k, int E, int W, int *counts, int *pos) {
+    if (!idx || !counts || n < 0 || k < 1 || W < 1 || E % W) return -1;
+    const int e_per = E / W;
+    for (int g = 0; g < W; g++) counts[g] = 0;
+    for (int a = 0; a < n * k; a++) {
+        if (idx[a] < 0 || idx[a] >= E) return -1;
+        counts[idx[a] / e_per]++;
+    }
+    if (pos) {
+        int base[64];
+        if (W > 64) return -1;
+        for (int g = 0, b = 0; g < W; g++) {
+            base[g] = b;
+            b += counts[g];
+        }
+        for (int a = 0; a < n * k; a++) pos[a] = base[idx[a] / e_per]++;
+    }
+    return 0;
+}

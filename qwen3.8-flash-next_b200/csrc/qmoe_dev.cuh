@@ -80,7 +80,7 @@ QK_DEV void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
         : "memory");
 }
 
-// ---- tensor-memory accelerator (TMA) tiled loads, no multicast ----
+// ---- tensor-memory accelerator (TMA) tiled loads, each to this CTA only ----
 QK_DEV void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -121,6 +121,25 @@ int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot_index, voi
 #define QK_ROUTE_UNFIT (-8)
 int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream, void *mid_event);
 
+/* Expert parallelism (qmoe_prefill.cu). Rank g of G owns experts
+ * [g E/G, (g+1) E/G). The plan holds the send / receive rows:
+ *   qk_ep_alloc     buffers for send_max (token, slot) rows out and recv_max in
+ *   qk_ep_dispatch  after routing: counts[G] rows per destination (device),
+ *                   send rows (fp16 x, natural order) and expert ids grouped
+ *                   by destination, stable in (token, slot) order
+ *   qk_ep_experts   grouped GEMMs over `rows` received rows (k = 1 each, no
+ *                   shared expert); their down outputs in received order
+ *   qk_ep_finish    the shared expert over this rank's tokens and the
+ *                   combine of the returned outputs (send order) into out
+ * The transfers between them are the caller's (NCCL send/recv on the
+ * buffers of qk_ep_buffers). */
+int qk_ep_alloc(qk_prefill *p, int send_max, int recv_max);
+void qk_ep_buffers(qk_prefill *p, void **send_x, int32_t **send_e, void **recv_x, int32_t **recv_e,
+                   float **ret, float **back);
+int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int G, int *counts, void *stream);
+int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, void *stream);
+int qk_ep_finish(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream);
+
 /* internal cache helper: replace the value of an existing key */
 struct qmoe_cache;
 int qmoe__cache_set_value(struct qmoe_cache *c, uint64_t key, uint64_t value);

@@ -407,14 +407,14 @@ __global__ void k_count(const int32_t *idx, int nk, int *counts) {
 }
 
 // One CTA (1024 threads, E + 1 <= 1024 groups). Group 0 is the shared expert
-// (every token, rows [0, T)); group 1 + e is routed expert e. Writes the
-// first row of each routed expert and the M-tile list.
-__global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int T,
+// (rows [0, nsh): every token, or none); group 1 + e is routed expert e.
+// Writes the first row of each routed expert and the M-tile list.
+__global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh,
                                                const int32_t *slot_of, int shared_slot,
                                                int *row0, MTile *tiles, int *n_mtiles) {
     __shared__ int s_scan[1024], s_tscan[1024];
     const int g = threadIdx.x;
-    const int rows = g == 0 ? T : (g <= E ? counts[g - 1] : 0);
+    const int rows = g == 0 ? nsh : (g <= E ? counts[g - 1] : 0);
     const int mt = (rows + BM - 1) / BM;
     s_scan[g] = rows;
     s_tscan[g] = mt;
@@ -479,17 +479,30 @@ __global__ void __launch_bounds__(1024) k_positions(const int32_t *idx, int nk, 
     }
 }
 
-// Grouped fp16 A operand: row r holds token r (r < T, shared group) or
+// x element types of the grouped path
+enum { XK_F32 = 0, XK_BF16 = 1, XK_F16 = 2 };
+
+// Grouped fp16 A operand: row r holds token r (r < nsh, the shared group) or
 // perm_tok[r]; each 8-element chunk in the order [0,4,1,5,2,6,3,7].
-__global__ void k_gather(const void *x, int x_bf16, int d, int T, int rows, const int *perm_tok,
+__global__ void k_gather(const void *x, int x_kind, int d, int nsh, int rows, const int *perm_tok,
                          __half *xp) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
-    const int tok = warp < T ? warp : perm_tok[warp];
+    const int tok = warp < nsh ? warp : perm_tok[warp];
     __half *dst = xp + static_cast<size_t>(warp) * d;
     for (int c = lane; c < d / 8; c += 32) {
         float v[8];
-        if (x_bf16) {
+        if (x_kind == XK_F16) {
+            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) +
+                                                            static_cast<size_t>(tok) * d)[c];
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 p = __half22float2(u2h(ww[i]));
+                v[2 * i] = p.x;
+                v[2 * i + 1] = p.y;
+            }
+        } else if (x_kind == XK_BF16) {
             const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
                                                             static_cast<size_t>(tok) * d)[c];
             v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
@@ -509,11 +522,11 @@ __global__ void k_gather(const void *x, int x_bf16, int d, int T, int rows, cons
     }
 }
 
-// out[t] = sum_s w[t,s] * Y[inv[t,s]] + sigmoid(g_t) * Y[t] (the shared
-// expert's rows come first in Y), fixed order; one CTA per token, 4 columns
-// per thread, all row loads of a thread issued before the sums.
-__global__ void k_combine(const float *Y, const int *inv, const float *wts, const float *sgate,
-                          int k, int d, float *out) {
+// out[t] = sum_s w[t,s] * Yr[inv[t,s]] + sigmoid(g_t) * Ysh[t], fixed
+// order; one CTA per token, 4 columns per thread, all row loads of a thread
+// issued before the sums.
+__global__ void k_combine(const float *Yr, const float *Ysh, const int *inv, const float *wts,
+                          const float *sgate, int k, int d, float *out) {
     const int t = blockIdx.x;
     for (int c = threadIdx.x; c < d / 4; c += blockDim.x) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -524,9 +537,10 @@ __global__ void k_combine(const float *Y, const int *inv, const float *wts, cons
             for (int u = 0; u < 4; ++u) {
                 const int s = s0 + u;
                 if (s <= k) {
-                    const int row = s < k ? inv[t * k + s] : t;
+                    const float *Y = s < k ? Yr + static_cast<size_t>(inv[t * k + s]) * d
+                                           : Ysh + static_cast<size_t>(t) * d;
                     w[u] = s < k ? wts[t * k + s] : sgate[t];
-                    v[u] = reinterpret_cast<const float4 *>(Y + static_cast<size_t>(row) * d)[c];
+                    v[u] = reinterpret_cast<const float4 *>(Y)[c];
                 }
             }
 #pragma unroll
@@ -541,6 +555,105 @@ __global__ void k_combine(const float *Y, const int *inv, const float *wts, cons
         }
         reinterpret_cast<float4 *>(out + static_cast<size_t>(t) * d)[c] = acc;
     }
+}
+
+// ---------------------------------------------------------------------------
+// expert-parallel dispatch and return (one rank per GPU; rank g owns experts
+// [g * E_per, (g + 1) * E_per))
+
+// Rows per destination rank: counts[g] (block-aggregated).
+__global__ void k_ep_count(const int32_t *idx, int nk, int e_per, int G, int *counts) {
+    __shared__ int s_c[64];
+    for (int g = threadIdx.x; g < G; g += blockDim.x) s_c[g] = 0;
+    __syncthreads();
+    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < nk; a += gridDim.x * blockDim.x)
+        atomicAdd(&s_c[idx[a] / e_per], 1);
+    __syncthreads();
+    for (int g = threadIdx.x; g < G; g += blockDim.x)
+        if (s_c[g]) atomicAdd(counts + g, s_c[g]);
+}
+
+// One CTA per destination rank g: the (token, slot) assignments bound for g
+// get consecutive send positions after the rows of ranks < g, in
+// assignment order (stable); the expert id travels with the row.
+__global__ void __launch_bounds__(1024) k_ep_positions(const int32_t *idx, int nk, int e_per,
+                                                       const int *counts, int *pos, int32_t *send_e) {
+    __shared__ int s_warp[32];
+    __shared__ int s_base;
+    const int g = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        int b = 0;
+        for (int q = 0; q < g; ++q) b += counts[q];
+        s_base = b;
+    }
+    __syncthreads();
+    for (int a0 = 0; a0 < nk; a0 += 1024) {
+        const int a = a0 + threadIdx.x;
+        const int e = a < nk ? idx[a] : -1;
+        const bool mine = a < nk && e / e_per == g;
+        const unsigned m = __ballot_sync(QK_FULL, mine);
+        if (lane == 0) s_warp[warp] = __popc(m);
+        __syncthreads();
+        if (warp == 0) {
+            int v = s_warp[lane];
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int t = __shfl_up_sync(QK_FULL, v, off);
+                if (lane >= off) v += t;
+            }
+            s_warp[lane] = v;
+        }
+        __syncthreads();
+        const int before = (warp ? s_warp[warp - 1] : 0) + __popc(m & ((1u << lane) - 1u));
+        if (mine) {
+            const int p = s_base + before;
+            pos[a] = p;
+            send_e[p] = e;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) s_base += s_warp[31];
+        __syncthreads();
+    }
+}
+
+// send_x[pos[a]] = fp16(x[a / k]), natural element order; one warp per row.
+__global__ void k_ep_pack_x(const void *x, int x_bf16, int d, int nk, int k, const int *pos,
+                            __half *send_x) {
+    const int a = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (a >= nk) return;
+    const int t = a / k;
+    __half *dst = send_x + static_cast<size_t>(pos[a]) * d;
+    for (int c = lane; c < d / 8; c += 32) {
+        float v[8];
+        if (x_bf16) {
+            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
+                                                            static_cast<size_t>(t) * d)[c];
+            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
+            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
+        } else {
+            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
+                                                               static_cast<size_t>(t) * d) + 2 * c;
+            const float4 u = p[0], w = p[1];
+            v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
+        }
+        uint4 o;
+        o.x = h2u(__floats2half2_rn(v[0], v[1]));
+        o.y = h2u(__floats2half2_rn(v[2], v[3]));
+        o.z = h2u(__floats2half2_rn(v[4], v[5]));
+        o.w = h2u(__floats2half2_rn(v[6], v[7]));
+        reinterpret_cast<uint4 *>(dst)[c] = o;
+    }
+}
+
+// ret[r] = Y[inv[r]]: the down outputs of the received rows, back in the
+// order they arrived (so each source rank's block is contiguous).
+__global__ void k_ep_ret(const float *Y, const int *inv, int rows, int d, float *ret) {
+    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const float4 *src = reinterpret_cast<const float4 *>(Y + static_cast<size_t>(inv[r]) * d);
+    float4 *dst = reinterpret_cast<float4 *>(ret + static_cast<size_t>(r) * d);
+    for (int c = lane; c < d / 4; c += 32) dst[c] = src[c];
 }
 
 // ---------------------------------------------------------------------------
@@ -857,6 +970,12 @@ struct qk_prefill {
     MTile *rtiles;
     int *rn;
     CUtensorMap tmXr;
+    // expert parallelism: send and receive rows, positions, returned outputs
+    int ep_send_max, ep_recv_max;
+    int *ep_pos;                  // [max_tokens * k] send position of each (token, slot)
+    int32_t *ep_send_e, *ep_recv_e;
+    __half *ep_send_x, *ep_recv_x;  // fp16 rows
+    float *ep_ret, *ep_back;        // fp32 down outputs: received order / send order
 };
 
 extern "C" void qk_prefill_destroy(qk_prefill *p) {
@@ -875,6 +994,13 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->lga);
     cudaFree(p->rtiles);
     cudaFree(p->rn);
+    cudaFree(p->ep_pos);
+    cudaFree(p->ep_send_e);
+    cudaFree(p->ep_recv_e);
+    cudaFree(p->ep_send_x);
+    cudaFree(p->ep_recv_x);
+    cudaFree(p->ep_ret);
+    cudaFree(p->ep_back);
     delete p;
 }
 
@@ -964,32 +1090,42 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     return p;
 }
 
-extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot_index,
-                                 void *stream, void **events) {
+namespace {
+
+// Grouping, gather and the two grouped GEMMs for T "tokens" (rows of x) with
+// k routed slots each (idx [T, k], global expert ids with a slot in
+// slot_of), plus the shared expert over all T rows when with_shared. Leaves
+// the down outputs in p->Y (shared rows first) and the row of each
+// (token, slot) in p->inv. events: NULL or 3 events (after grouping+gather,
+// gate/up, down).
+cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32_t *idx, int k,
+                    int with_shared, const int32_t *slot_of, int shared_slot_index, int *err,
+                    cudaStream_t st, void **events) {
     const qk_layout &L = p->L;
-    const int T = f->T, k = L.k, E = L.E;
-    if (T > p->max_tokens) return cudaErrorInvalidValue;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // diagnostics: events[0..3] bracket grouping+gather, gate/up, down, combine
+    const int E = L.E;
+    const int nsh = with_shared ? T : 0;
+    const int nk = T * k;
+    const int rows = nsh + nk;
+    if (rows > p->rows_max || nk > p->max_tokens * L.k) return cudaErrorInvalidValue;
     auto mark = [&](int i) {
         if (events) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), st,
                                              cudaEventRecordExternal);
     };
     cudaError_t e = cudaMemsetAsync(p->counts, 0, sizeof(int) * (E + 1), st);
     if (e != cudaSuccess) return e;
-    const int nk = T * k;
-    k_count<<<(nk + 255) / 256, 256, 0, st>>>(f->idx, nk, p->counts);
-    k_plan<<<1, 1024, 0, st>>>(p->counts, E, T, f->slot_of, shared_slot_index, p->row0, p->tiles,
+    if (nk > 0) k_count<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, p->counts);
+    k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index, p->row0, p->tiles,
                                p->n_mtiles);
-    k_positions<<<E, 1024, 0, st>>>(f->idx, nk, k, p->row0, p->inv, p->perm_tok);
-    const int rows = T * (k + 1);
-    k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, rows, p->perm_tok,
-                                                     p->xp);
+    if (nk > 0) k_positions<<<E, 1024, 0, st>>>(idx, nk, k, p->row0, p->inv, p->perm_tok);
+    if (rows > 0)
+        k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->perm_tok,
+                                                         p->xp);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     mark(0);
 
     GemmArgs gu;
+    memset(&gu, 0, sizeof(gu));
     gu.mode = 0;
     gu.KB = L.d / BK;
     gu.NT = L.I / 128;
@@ -1003,11 +1139,11 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     gu.lo_plane = static_cast<size_t>(p->rows_max) * L.I;
     gu.out = p->H;
     gu.outf = nullptr;
-    gu.err = f->err;
+    gu.err = err;
     {
         void *args[] = {&p->tmX, &p->tmQgu, &p->tmSgu, &gu};
         e = qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<0>), dim3(p->num_sms),
-                          dim3(kThreads), Cfg<0>::Smem, stream, 0, args);
+                          dim3(kThreads), Cfg<0>::Smem, st, 0, args);
         if (e != cudaSuccess) return e;
     }
     mark(1);
@@ -1022,12 +1158,93 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     {
         void *args[] = {&p->tmH, &p->tmQdn, &p->tmSdn, &dn};
         e = qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<1>), dim3(p->num_sms),
-                          dim3(kThreads), Cfg<1>::Smem, stream, 0, args);
+                          dim3(kThreads), Cfg<1>::Smem, st, 0, args);
         if (e != cudaSuccess) return e;
     }
     mark(2);
-    k_combine<<<T, 256, 0, st>>>(p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
-    mark(3);
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot_index,
+                                 void *stream, void **events) {
+    const qk_layout &L = p->L;
+    const int T = f->T, k = L.k;
+    if (T > p->max_tokens) return cudaErrorInvalidValue;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // diagnostics: events[0..3] bracket grouping+gather, gate/up, down, combine
+    cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, k, 1, f->slot_of,
+                            shared_slot_index, f->err, st, events);
+    if (e != cudaSuccess) return e;
+    k_combine<<<T, 256, 0, st>>>(p->Y, p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
+    if (events) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[3]), st, cudaEventRecordExternal);
+    return cudaGetLastError();
+}
+
+extern "C" int qk_ep_alloc(qk_prefill *p, int send_max, int recv_max) {
+    const qk_layout &L = p->L;
+    if (send_max > p->max_tokens * L.k || recv_max > p->max_tokens * L.k) return cudaErrorInvalidValue;
+    p->ep_send_max = send_max;
+    p->ep_recv_max = recv_max;
+    const size_t d = static_cast<size_t>(L.d);
+    cudaError_t e = cudaMalloc(&p->ep_pos, sizeof(int) * send_max);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_e, sizeof(int32_t) * send_max);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_e, sizeof(int32_t) * recv_max);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_x, sizeof(__half) * send_max * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_x, sizeof(__half) * recv_max * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_ret, sizeof(float) * recv_max * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_back, sizeof(float) * send_max * d);
+    return e;
+}
+
+extern "C" void qk_ep_buffers(qk_prefill *p, void **send_x, int32_t **send_e, void **recv_x,
+                              int32_t **recv_e, float **ret, float **back) {
+    *send_x = p->ep_send_x;
+    *send_e = p->ep_send_e;
+    *recv_x = p->ep_recv_x;
+    *recv_e = p->ep_recv_e;
+    *ret = p->ep_ret;
+    *back = p->ep_back;
+}
+
+extern "C" int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int G, int *counts, void *stream) {
+    const qk_layout &L = p->L;
+    const int nk = f->T * L.k;
+    if (nk > p->ep_send_max || G > 64 || L.E % G) return cudaErrorInvalidValue;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int e_per = L.E / G;
+    cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * G, st);
+    if (e != cudaSuccess) return e;
+    if (nk > 0) {
+        k_ep_count<<<(nk + 1023) / 1024, 1024, 0, st>>>(f->idx, nk, e_per, G, counts);
+        k_ep_positions<<<G, 1024, 0, st>>>(f->idx, nk, e_per, counts, p->ep_pos, p->ep_send_e);
+        k_ep_pack_x<<<(nk * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, nk, L.k, p->ep_pos,
+                                                          p->ep_send_x);
+    }
+    return cudaGetLastError();
+}
+
+extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, void *stream) {
+    if (rows > p->ep_recv_max) return cudaErrorInvalidValue;
+    if (rows == 0) return cudaSuccess;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = grouped(p, p->ep_recv_x, XK_F16, rows, p->ep_recv_e, 1, 0, f->slot_of, 0, f->err,
+                            st, nullptr);
+    if (e != cudaSuccess) return e;
+    k_ep_ret<<<(rows * 32 + 255) / 256, 256, 0, st>>>(p->Y, p->inv, rows, p->L.d, p->ep_ret);
+    return cudaGetLastError();
+}
+
+extern "C" int qk_ep_finish(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream) {
+    const qk_layout &L = p->L;
+    const int T = f->T;
+    if (T == 0) return cudaSuccess;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, nullptr, 0, 1, f->slot_of,
+                            shared_slot_index, f->err, st, nullptr);
+    if (e != cudaSuccess) return e;
+    k_combine<<<T, 256, 0, st>>>(p->ep_back, p->Y, p->ep_pos, f->wts, f->sgate, L.k, L.d, f->out);
     return cudaGetLastError();
 }
 

@@ -32,6 +32,7 @@ class Config(C.Structure):
         ("moe_inter", C.c_int), ("group_size", C.c_int), ("bits", C.c_int),
         ("num_layers", C.c_int), ("max_tokens", C.c_int), ("pool_bytes", C.c_uint64),
         ("policy", C.c_int), ("prefetch_depth", C.c_int), ("device", C.c_int),
+        ("ep_rank", C.c_int), ("ep_world", C.c_int),
     ]
 
 
@@ -97,6 +98,10 @@ SIGNATURES = {
     "qmoe_upload_layer": (C.c_int, [_P, C.c_int, C.POINTER(LayerWeights), C.POINTER(Err)]),
     "qmoe_forward": (C.c_int, [_P, C.c_int, _P, C.c_int, _P, C.POINTER(Err)]),
     "qmoe_forward_dev": (C.c_int, [_P, C.c_int, _P, C.c_int, C.c_int, _P, _P, C.POINTER(Err)]),
+    "qmoe_ep_unique_id": (C.c_int, [_P, C.POINTER(Err)]),
+    "qmoe_ep_plan_host": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),
+    "qmoe_ep_connect": (C.c_int, [_P, _P, C.POINTER(Err)]),
+    "qmoe_forward_ep": (C.c_int, [_P, C.c_int, _P, C.c_int, C.c_int, _P, _P, C.POINTER(Err)]),
     "qmoe_sync": (C.c_int, [_P, C.POINTER(Err)]),
     "qmoe_last_routing": (C.c_int, [_P, _P, _P, _P, C.POINTER(Err)]),
     "qmoe_forward_token_noalloc": (C.c_int, [C.POINTER(TokenArgs), _P, C.POINTER(Err)]),
@@ -159,9 +164,20 @@ def ptr(a) -> int | None:
     return None if a is None else a.ctypes.data
 
 
+def ep_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for qmoe_ep_connect; made on one rank
+    and handed to the others by the caller."""
+    buf = C.create_string_buffer(128)
+    err = Err()
+    if lib().qmoe_ep_unique_id(buf, C.byref(err)) != 0:
+        raise QmoeError(err.text())
+    return buf.raw
+
+
 def make_config(d, E, k, I, g=64, layers=1, max_tokens=1, pool_bytes=0,
-                policy=QMOE_POLICY_ADAPTIVE, prefetch=2, device=0) -> Config:
-    return Config(d, E, k, I, g, 4, layers, max_tokens, pool_bytes, policy, prefetch, device)
+                policy=QMOE_POLICY_ADAPTIVE, prefetch=2, device=0, ep_rank=0, ep_world=0) -> Config:
+    return Config(d, E, k, I, g, 4, layers, max_tokens, pool_bytes, policy, prefetch, device,
+                  ep_rank, ep_world)
 
 
 class SynthLayer:
@@ -253,6 +269,19 @@ class Context:
         err = Err()
         self._chk(lib().qmoe_forward_dev(self.h, layer, x_ptr, x_dtype, n, out_ptr, stream,
                                          C.byref(err)), err)
+
+    def ep_connect(self, uid: bytes):
+        """Joins the expert-parallel group (collective over the ep_world ranks)."""
+        err = Err()
+        buf = C.create_string_buffer(bytes(uid), 128)
+        self._chk(lib().qmoe_ep_connect(self.h, buf, C.byref(err)), err)
+
+    def forward_ep(self, layer: int, x_ptr: int, x_dtype: int, n: int, out_ptr: int,
+                   stream: int | None = None):
+        """Collective forward of this rank's n tokens (device pointers)."""
+        err = Err()
+        self._chk(lib().qmoe_forward_ep(self.h, layer, x_ptr, x_dtype, n, out_ptr, stream,
+                                        C.byref(err)), err)
 
     def sync(self):
         err = Err()

@@ -1,0 +1,198 @@
+"""Expert parallelism: the dispatch plan (host form of the device kernels of
+qmoe_forward_ep), a two-rank exchange of that plan over gloo on the CPU, and
+on two GPUs the collective forward itself against the C restatement.
+
+Rank g of W owns experts [g E/W, (g+1) E/W); each rank routes its own
+tokens, sends every (token, slot) row to the owner of its expert, and gets
+the down outputs back: the expert-parallel layout of the workload's
+prefill and batched-decode configurations."""
+import ctypes as C
+import os
+import socket
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _plan(idx, E, W):
+    import qmoe
+    idx = np.ascontiguousarray(idx, np.int32)
+    n, k = idx.shape
+    counts = np.zeros(W, np.int32)
+    pos = np.zeros(n * k, np.int32)
+    rc = qmoe.lib().qmoe_ep_plan_host(idx.ctypes.data, n, k, E, W, counts.ctypes.data,
+                                      pos.ctypes.data)
+    assert rc == 0
+    return counts, pos.reshape(n, k)
+
+
+def test_plan_groups_rows_by_owner_stably(built):
+    rng = np.random.default_rng(7)
+    E, W, n, k = 64, 4, 50, 6
+    idx = np.stack([rng.choice(E, k, replace=False) for _ in range(n)]).astype(np.int32)
+    counts, pos = _plan(idx, E, W)
+    owner = idx // (E // W)
+    assert counts.tolist() == np.bincount(owner.ravel(), minlength=W).tolist()
+    flat = pos.ravel()
+    assert sorted(flat.tolist()) == list(range(n * k))           # a permutation
+    starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    for g in range(W):
+        mine = flat[owner.ravel() == g]                            # (token, slot) order
+        assert mine.tolist() == list(range(starts[g], starts[g] + counts[g]))
+
+
+def test_plan_rejects_bad_arguments(built):
+    import qmoe
+    idx = np.zeros((2, 2), np.int32)
+    counts = np.zeros(4, np.int32)
+    f = qmoe.lib().qmoe_ep_plan_host
+    assert f(idx.ctypes.data, 2, 2, 10, 4, counts.ctypes.data, None) == -1   # E % W
+    bad = np.array([[0, 99]], np.int32)
+    assert f(bad.ctypes.data, 1, 2, 16, 4, counts.ctypes.data, None) == -1   # expert id
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _gloo_rank(rank, world, port, result):
+    import sys
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "qwen3.8-flash-next_b200"))
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    import qmoe
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        d, E, k, I = 256, 16, 4, 128
+        cfg = qmoe.make_config(d, E, k, I, max_tokens=32)
+        s = qmoe.SynthLayer(cfg, 20261201)
+        x = qmoe.synth_tokens(20261201, 40 + rank, 12 + 5 * rank, d)   # ranks differ in n
+        idx, w, _ = oracle.restatement().route(s, x)
+        counts, pos = _plan(idx, E, world)
+        # counts out, counts in
+        rcounts = torch.zeros(world, dtype=torch.int32)
+        dist.all_to_all_single(rcounts, torch.from_numpy(counts))
+        # expert ids in send order, then the exchange itself
+        send_e = np.empty(idx.size, np.int32)
+        send_e[pos.ravel()] = idx.ravel()
+        recv_e = torch.zeros(int(rcounts.sum()), dtype=torch.int32)
+        dist.all_to_all_single(recv_e, torch.from_numpy(send_e),
+                               output_split_sizes=rcounts.tolist(),
+                               input_split_sizes=counts.tolist())
+        # every row received is for one of this rank's experts, and the rows
+        # received are exactly every rank's assignments to those experts
+        all_idx = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(all_idx, torch.tensor([idx.size]))
+        mx = max(int(t) for t in all_idx)   # gloo gathers equal sizes: pad with -1
+        padded = np.full(mx, -1, np.int32)
+        padded[:idx.size] = idx.ravel()
+        gathered = [torch.zeros(mx, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(gathered, torch.from_numpy(padded))
+        every = np.concatenate([g.numpy() for g in gathered])
+        every = every[every >= 0]
+        lo, hi = rank * E // world, (rank + 1) * E // world
+        got = recv_e.numpy()
+        ok = bool(np.all((got >= lo) & (got < hi)))
+        ok = ok and np.bincount(got, minlength=E)[lo:hi].tolist() == \
+            np.bincount(every, minlength=E)[lo:hi].tolist()
+        result[rank] = ok
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_dispatch_over_gloo(built):
+    """World size 2 on the CPU (gloo): each rank routes its own tokens with
+    the C restatement, plans its dispatch with the library's host plan, and
+    the exchanged rows land exactly on the owners of their experts."""
+    import torch.multiprocessing as mp
+    world = 2
+    with mp.Manager() as m:
+        result = m.dict()
+        mp.spawn(_gloo_rank, args=(world, _free_port(), result), nprocs=world, join=True)
+        assert dict(result) == {0: True, 1: True}
+
+
+def _ep_rank(rank, world, uid_q, out_q, T_per):
+    import sys
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "qwen3.8-flash-next_b200"))
+    import torch
+
+    import qmoe
+    torch.cuda.set_device(rank)
+    d, E, k, I = 2048, 512, 10, 512
+    cfg = qmoe.make_config(d, E, k, I, max_tokens=T_per, device=rank, ep_rank=rank,
+                           ep_world=world)
+    s = qmoe.SynthLayer(cfg, 20261201, zipf_s=1.1)
+    ctx = qmoe.Context(cfg)
+    ctx.upload(0, s)
+    if rank == 0:
+        uid = qmoe.ep_unique_id()
+        for _ in range(world - 1):
+            uid_q.put(uid)
+    else:
+        uid = uid_q.get(timeout=120)
+    ctx.ep_connect(uid)
+    x = qmoe.synth_tokens(20261201, 60 + rank, T_per, d)
+    xd = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    out = torch.empty((T_per, d), dtype=torch.float32, device="cuda")
+    for _ in range(2):   # twice: the second call reuses every buffer
+        ctx.forward_ep(0, xd.data_ptr(), qmoe.QMOE_BF16, T_per, out.data_ptr(), None)
+        ctx.sync()
+    idx, _, _ = ctx.routing(T_per)
+    out_q.put((rank, out.cpu().numpy(), idx))
+    ctx.close()
+
+
+@pytest.mark.gpu
+def test_expert_parallel_forward_two_gpus(built):
+    """Two GPUs, one process each, NCCL through the library: every token's
+    routing equals the restatement's and a spread sample of outputs is within
+    the parity tolerance (the same bars as the one-GPU path)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    import oracle
+    import qmoe
+    world, T_per = 2, 256
+    ctx = mp.get_context("spawn")
+    uid_q, out_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_ep_rank, args=(r, world, uid_q, out_q, T_per))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            r, out, idx = out_q.get(timeout=600)
+            results[r] = (out, idx)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    cfg = qmoe.make_config(2048, 512, 10, 512, max_tokens=T_per)
+    s = qmoe.SynthLayer(cfg, 20261201, zipf_s=1.1)
+    for r in range(world):
+        out, idx = results[r]
+        x = qmoe.synth_tokens(20261201, 60 + r, T_per, 2048)
+        sample = np.linspace(0, T_per - 1, 12).astype(int)
+        ro, ri, _ = oracle.restatement().forward(s, x[sample])
+        assert np.array_equal(idx[sample], ri)
+        mab = float(np.abs(out[sample] - ro).max())
+        rr = float(np.linalg.norm(out[sample] - ro) / np.linalg.norm(ro))
+        assert mab <= 2e-2 and rr <= 1e-3, (r, mab, rr)
