@@ -49,24 +49,29 @@ namespace {
 constexpr int BM = 128;           // token rows per tile
 constexpr int BK = 64;            // K per stage: one 128-byte swizzle row of fp16
 constexpr int BN = 256;           // accumulator columns (gate|up, or down outputs)
-constexpr int NS = 3;             // pipeline stages
 constexpr int kThreads = 320;     // 10 warps
 constexpr int kA = BM * BK * 2;   // 16 KB
 constexpr int kBf = BN * BK * 2;  // 32 KB
 constexpr int kBq = BN * 32;      // 8 KB packed q4
 constexpr int kBs = BN * 16;      // 4 KB scales
-// Per-mode stage layout. The down GEMM's A operand is H as an fp16 hi/lo pair
-// (H = hi + lo to about 22 significant bits), two A tiles per stage and two
-// MMAs per K step against the same dequantised B tile; it runs 2 stages.
+// Two rings in shared memory. The raw ring takes the TMA loads of one K step
+// (A tile, packed q4 rows, scales) and is released by the MMA; the Bf ring
+// holds two dequantised B tiles, written by the dequantisers and released by
+// the MMA too, so dequantisation runs ahead of the MMA while the raw ring
+// prefetches further. The down GEMM's A operand is H as an fp16 hi/lo pair
+// (H = hi + lo to about 22 significant bits): two A tiles per raw stage and
+// two MMAs per K step against the same dequantised B tile.
 // MODE 2 is the router: A = x as a bf16 hi/lo pair, B = the bf16 router rows
-// loaded by TMA straight into the swizzled layout (no dequantisation, no
-// packed-q4 staging); it runs 3 stages.
+// loaded by TMA straight into the swizzled layout (no dequantisation): its
+// raw stage holds A and B, and there is no Bf ring.
+constexpr int kMaxNR = 5;
 template <int MODE>
 struct Cfg {
-    static constexpr int NSt = MODE == 1 ? 2 : 3;
     static constexpr int A = MODE ? 2 * kA : kA;
-    static constexpr int Stage = A + kBf + (MODE == 2 ? 0 : kBq + kBs);
-    static constexpr int Smem = NSt * Stage + 1024;  // + alignment slack
+    static constexpr int Raw = MODE == 2 ? A + kBf : A + kBq + kBs;
+    static constexpr int NR = MODE == 0 ? 5 : 3;
+    static constexpr int Smem = NR * Raw + (MODE == 2 ? 0 : 2 * kBf) + (MODE ? 4 * 4096 : 0) +
+                                1024;  // + alignment slack
 };
 
 struct MTile {
@@ -145,21 +150,31 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
            const __grid_constant__ CUtensorMap tmS, GemmArgs g) {
+    constexpr int NR = Cfg<MODE>::NR;
+    constexpr int kAm = Cfg<MODE>::A;
+    constexpr int kRaw = Cfg<MODE>::Raw;
+    constexpr bool kDeq = MODE != 2;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full[NS], ready[NS], empty[NS], acc_full[2], acc_empty[2], drain;
+    // raw ring: TMA in, released by the MMA; Bf ring: dequantised B tiles
+    __shared__ uint64_t raw_full[kMaxNR], raw_empty[kMaxNR], bf_full[2], bf_empty[2];
+    __shared__ uint64_t acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag_;
     volatile int &abort_flag = abort_flag_;
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t *bf_base = smem + NR * kRaw;  // two dequantised B tiles (MODE 0, 1)
+    // fp32 epilogue staging (MODE 1, 2): 4 KB per epilogue warp
+    uint8_t *stg_base = bf_base + (MODE == 2 ? 0 : 2 * kBf);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&ready[s], 4);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < NR; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
+            mbar_init(&bf_full[b], 4);
+            mbar_init(&bf_empty[b], 1);
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 4);
         }
@@ -176,54 +191,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = tmem_base;
     const int ntiles = *g.n_mtiles * g.NT;
     const int KB = g.KB;
-    constexpr int NSm = Cfg<MODE>::NSt;
-    constexpr int kAm = Cfg<MODE>::A;
-    constexpr int kSt = Cfg<MODE>::Stage;
 
     if (warp == 0) {
-        // ---------------- TMA producer
+        // ---------------- TMA producer: the raw ring
         if (lane == 0) {
             int it = 0;
-            int last_it[NS];
-            for (int s = 0; s < NS; ++s) last_it[s] = -1;
+            int last_it[kMaxNR];
+            for (int s = 0; s < NR; ++s) last_it[s] = -1;
             for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
                 const MTile mt = g.tiles[tile / g.NT];
                 const int nt = tile % g.NT;
                 for (int kb = 0; kb < KB; ++kb, ++it) {
-                    const int s = it % NSm;
-                    const uint32_t ph = (it / NSm) & 1;
-                    if (!mbar_wait(&empty[s], ph ^ 1)) {
+                    const int s = it % NR;
+                    const uint32_t ph = (it / NR) & 1;
+                    if (!mbar_wait(&raw_empty[s], ph ^ 1)) {
                         atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
                         abort_flag = 1;
                         break;
                     }
-                    uint8_t *st = smem + s * kSt;
-                    uint8_t *A = st, *Bq = st + kAm + kBf, *Bs = Bq + kBq;
+                    uint8_t *A = smem + s * kRaw;
+                    uint8_t *Bq = A + kAm, *Bs = Bq + kBq;
                     if (MODE == 0) {
-                        mbar_expect_tx(&full[s], kA + 2 * (128 * 32) + 128 * 16);
-                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &full[s]);
-                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 128, mt.slot, &full[s]);
+                        mbar_expect_tx(&raw_full[s], kA + 2 * (128 * 32) + 128 * 16);
+                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &raw_full[s]);
+                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 128, mt.slot, &raw_full[s]);
                         tma_load_3d(Bq + 128 * 32, &tmQ, g.d / 2 + kb * 32, nt * 128, mt.slot,
-                                    &full[s]);
-                        tma_load_3d(Bs, &tmS, g.d + 16 * (kb >> 1), nt * 128, mt.slot, &full[s]);
+                                    &raw_full[s]);
+                        tma_load_3d(Bs, &tmS, g.d + 16 * (kb >> 1), nt * 128, mt.slot, &raw_full[s]);
                     } else if (MODE == 1) {
-                        mbar_expect_tx(&full[s], 2 * kA + 256 * 32 + 256 * 16);
-                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &full[s]);                   // hi
-                        tma_load_2d(A + kA, &tmA, kb * BK, g.rows_max + mt.m0, &full[s]);  // lo
-                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 256, mt.slot, &full[s]);
-                        tma_load_3d(Bs, &tmS, g.I / 2 + 16 * (kb >> 2), nt * 256, mt.slot, &full[s]);
+                        mbar_expect_tx(&raw_full[s], 2 * kA + 256 * 32 + 256 * 16);
+                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &raw_full[s]);                   // hi
+                        tma_load_2d(A + kA, &tmA, kb * BK, g.rows_max + mt.m0, &raw_full[s]);  // lo
+                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 256, mt.slot, &raw_full[s]);
+                        tma_load_3d(Bs, &tmS, g.I / 2 + 16 * (kb >> 2), nt * 256, mt.slot,
+                                    &raw_full[s]);
                     } else {
-                        mbar_expect_tx(&full[s], 2 * kA + kBf);
-                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &full[s]);                   // hi
-                        tma_load_2d(A + kA, &tmA, kb * BK, g.rows_max + mt.m0, &full[s]);  // lo
-                        tma_load_2d(A + kAm, &tmQ, kb * BK, nt * 256, &full[s]);         // router rows
+                        mbar_expect_tx(&raw_full[s], 2 * kA + kBf);
+                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &raw_full[s]);                   // hi
+                        tma_load_2d(A + kA, &tmA, kb * BK, g.rows_max + mt.m0, &raw_full[s]);  // lo
+                        tma_load_2d(A + kAm, &tmQ, kb * BK, nt * 256, &raw_full[s]);         // router rows
                     }
                     last_it[s] = it;
                 }
             }
             // every load this thread issued has landed before the CTA exits
-            for (int s = 0; s < NSm; ++s)
-                if (last_it[s] >= 0) mbar_wait(&full[s], (last_it[s] / NSm) & 1);
+            for (int s = 0; s < NR; ++s)
+                if (last_it[s] >= 0) mbar_wait(&raw_full[s], (last_it[s] / NR) & 1);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
@@ -243,16 +256,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t dt = tmem + buf * BN;
             bool ok = true;
             for (int kb = 0; kb < KB; ++kb, ++it) {
-                const int s = it % NSm;
-                const uint32_t ph = (it / NSm) & 1;
-                if (!mbar_wait(&full[s], ph) || (MODE != 2 && !mbar_wait(&ready[s], ph))) {
+                const int s = it % NR, b = it & 1;
+                const uint32_t ph = (it / NR) & 1, bph = (it >> 1) & 1;
+                if (!mbar_wait(&raw_full[s], ph) || (kDeq && !mbar_wait(&bf_full[b], bph))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint32_t a0 = smem_addr(smem + s * kSt);
-                    const uint32_t b0 = a0 + kAm;
+                    const uint32_t a0 = smem_addr(smem + s * kRaw);
+                    const uint32_t b0 = kDeq ? smem_addr(bf_base + b * kBf) : a0 + kAm;
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         umma_f16(dt, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
@@ -261,7 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             umma_f16(dt, sdesc_sw128(a0 + kA + kk * 32), sdesc_sw128(b0 + kk * 32),
                                      idesc, 1u);
                     }
-                    umma_commit(&empty[s]);
+                    umma_commit(&raw_empty[s]);
+                    if (kDeq) umma_commit(&bf_empty[b]);
                 }
                 __syncwarp();
             }
@@ -282,22 +296,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp < 6) {
-        // ---------------- dequantisers: 128 threads, rows t and t + 128
-        // (the router's B tile arrives ready: no work)
+        // ---------------- dequantisers: 128 threads, rows t and t + 128, from
+        // raw stage s into Bf tile b (the router's B tile arrives ready)
         const int t = tid - 64;
-        const int dq_tiles = MODE == 2 ? 0 : ntiles;
+        const int dq_tiles = kDeq ? ntiles : 0;
         int it = 0;
         for (int tile = blockIdx.x; tile < dq_tiles && !abort_flag; tile += gridDim.x) {
             bool ok = true;
             for (int kb = 0; kb < KB; ++kb, ++it) {
-                const int s = it % NSm;
-                const uint32_t ph = (it / NSm) & 1;
-                if (!mbar_wait(&full[s], ph)) {
+                const int s = it % NR, b = it & 1;
+                const uint32_t ph = (it / NR) & 1, bph = (it >> 1) & 1;
+                if (!mbar_wait(&raw_full[s], ph) || !mbar_wait(&bf_empty[b], bph ^ 1)) {
                     ok = false;
                     break;
                 }
-                uint8_t *st = smem + s * kSt;
-                uint8_t *Bf = st + kAm, *Bq = st + kAm + kBf, *Bs = Bq + kBq;
+                uint8_t *Bq = smem + s * kRaw + kAm, *Bs = Bq + kBq;
+                uint8_t *Bf = bf_base + b * kBf;
                 if (MODE == 0) {
                     // gate row t -> B row t, up row t -> B row 128 + t; the 16
                     // scale bytes hold the quads of groups 2j and 2j+1
@@ -314,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&ready[s]);
+                if (lane == 0) mbar_arrive(&bf_full[b]);
             }
             if (!ok) {
                 if (lane == 0) {
@@ -371,17 +385,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else {
-                float *orow = g.outf + orow_i;
-                for (int c = 0; c < 256; c += 16) {
-                    float yv[16];
+                // fp32 out, 32 columns at a time through this warp's 4 KB of
+                // shared memory (float4 index XOR row % 8: no bank conflicts),
+                // so each store instruction writes 4 full 128-byte row pieces
+                float4 *stg = reinterpret_cast<float4 *>(stg_base + q * 4096);
+                for (int c = 0; c < 256; c += 32) {
+                    float yv[32];
                     tmem_ld16(tbase + c, yv);
+                    tmem_ld16(tbase + c + 16, yv + 16);
                     tmem_wait_ld();
-                    if (live && nt * 256 + c < g.n_cols) {
-                        float4 *dst = reinterpret_cast<float4 *>(orow + nt * 256 + c);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            dst[i] = make_float4(yv[4 * i], yv[4 * i + 1], yv[4 * i + 2], yv[4 * i + 3]);
+                    for (int j = 0; j < 8; ++j)
+                        stg[lane * 8 + (j ^ (lane & 7))] =
+                            make_float4(yv[4 * j], yv[4 * j + 1], yv[4 * j + 2], yv[4 * j + 3]);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = 4 * i + (lane >> 3), j = lane & 7;
+                        const int col = nt * 256 + c + 4 * j;
+                        const float4 v = stg[r * 8 + (j ^ (r & 7))];
+                        if (32 * q + r < mt.rows && col < g.n_cols)
+                            *reinterpret_cast<float4 *>(
+                                g.outf + static_cast<size_t>(mt.m0 + 32 * q + r) * g.ld_out + col) = v;
                     }
+                    __syncwarp();
                 }
             }
             tc_fence_before();
