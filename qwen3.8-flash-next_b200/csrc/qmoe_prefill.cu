@@ -14,17 +14,20 @@
 //   k_combine    out[t] = sum_s w[t,s] Y[row(t,s)] + sigmoid(g_t) Y_sh[t]
 //                in a fixed order (model.c:1376-1386, :1396-1402)
 //
-// Grouped GEMM (one persistent kernel, one CTA per SM, 10 warps):
-//   warp 0     TMA producer: the A tile (128 rows x 64 fp16, 128-byte swizzle)
-//              and the packed q4 rows + scales of the B tile, per stage
-//   warp 1     allocates 512 TMEM columns; one thread issues tcgen05.mma
-//              (M=128, N=256, K=16 x 4 per stage) and tcgen05.commit
-//   warps 2-5  dequantise q4 -> fp16 into the canonical K-major 128-byte
-//              swizzled layout (w = q*s + b, exact for b = -8s)
-//   warps 6-9  epilogue: tcgen05.ld of the accumulator (double-buffered in
-//              TMEM); gate/up: SiLU(g)*u stored as fp16 (the down GEMM's A
-//              operand); down: fp32 stores (keeps the combine at fp32)
-// Three stages of 60 KB in shared memory; every wait is bounded.
+// Grouped GEMM (one persistent kernel, one CTA per SM, 14 warps):
+//   warp 0       TMA producer: the A tile (128 rows x 64 fp16, 128-byte
+//                swizzle) and the packed q4 rows + scales of the B tile
+//   warp 1       allocates 512 TMEM columns; one thread issues tcgen05.mma
+//                (M=128, N=256, K=16 x 4 per K step) and tcgen05.commit
+//   warps 2-9    dequantise q4 -> fp16 into the canonical K-major 128-byte
+//                swizzled layout (w = q*s + b, exact for b = -8s), one B row
+//                per thread; two warps per scheduler hide each other's latency
+//   warps 10-13  epilogue: tcgen05.ld of the accumulator (double-buffered in
+//                TMEM); gate/up: SiLU(g)*u stored as fp16 (the down GEMM's A
+//                operand); down: fp32 stores (keeps the combine at fp32)
+// Measured per K step on config 2 before the dequantisers were doubled: the
+// MMA issue ran at the tensor pipe's full rate and waited 31% of the time for
+// dequantised B tiles and 17% for TMA data. Every wait is bounded.
 //
 // Inside each 8-element chunk along K, the fp16 operands use the element
 // order [0,4,1,5,2,6,3,7]: the dequantiser then builds two fp16 values per
@@ -49,7 +52,8 @@ namespace {
 constexpr int BM = 128;           // token rows per tile
 constexpr int BK = 64;            // K per stage: one 128-byte swizzle row of fp16
 constexpr int BN = 256;           // accumulator columns (gate|up, or down outputs)
-constexpr int kThreads = 320;     // 10 warps
+constexpr int kThreads = 448;     // 14 warps
+constexpr int kDeqWarps = 8;      // warps 2 .. 9
 constexpr int kA = BM * BK * 2;   // 16 KB
 constexpr int kBf = BN * BK * 2;  // 32 KB
 constexpr int kBq = BN * 32;      // 8 KB packed q4
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&raw_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&bf_full[b], 4);
+            mbar_init(&bf_full[b], kDeqWarps);
             mbar_init(&bf_empty[b], 1);
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 4);
@@ -295,9 +299,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait(&drain, 0);
         }
         __syncwarp();
-    } else if (warp < 6) {
-        // ---------------- dequantisers: 128 threads, rows t and t + 128, from
-        // raw stage s into Bf tile b (the router's B tile arrives ready)
+    } else if (warp < 2 + kDeqWarps) {
+        // ---------------- dequantisers: 256 threads, B row t each, from raw
+        // stage s into Bf tile b (the router's B tile arrives ready)
         const int t = tid - 64;
         const int dq_tiles = kDeq ? ntiles : 0;
         int it = 0;
@@ -313,18 +317,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint8_t *Bq = smem + s * kRaw + kAm, *Bs = Bq + kBq;
                 uint8_t *Bf = bf_base + b * kBf;
                 if (MODE == 0) {
-                    // gate row t -> B row t, up row t -> B row 128 + t; the 16
-                    // scale bytes hold the quads of groups 2j and 2j+1
-                    const uint2 quad = *reinterpret_cast<const uint2 *>(Bs + t * 16 + 8 * (kb & 1));
-                    dequant_row(Bq + t * 32, bf16lo(quad.x), bf16hi(quad.x), Bf, t);
-                    dequant_row(Bq + 128 * 32 + t * 32, bf16lo(quad.y), bf16hi(quad.y), Bf, 128 + t);
+                    // gate row r -> B row r, up row r -> B row 128 + r; the 16
+                    // scale bytes of row r hold the quads of groups 2j and 2j+1
+                    const int r = t & 127;
+                    const uint2 quad = *reinterpret_cast<const uint2 *>(Bs + r * 16 + 8 * (kb & 1));
+                    const uint32_t sb = t < 128 ? quad.x : quad.y;
+                    dequant_row(Bq + t * 32, bf16lo(sb), bf16hi(sb), Bf, t);
                 } else {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int r = t + 128 * h;
-                        const uint32_t pr = *reinterpret_cast<const uint32_t *>(Bs + r * 16 + 4 * (kb & 3));
-                        dequant_row(Bq + r * 32, bf16lo(pr), bf16hi(pr), Bf, r);
-                    }
+                    const uint32_t pr = *reinterpret_cast<const uint32_t *>(Bs + t * 16 + 4 * (kb & 3));
+                    dequant_row(Bq + t * 32, bf16lo(pr), bf16hi(pr), Bf, t);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
