@@ -516,7 +516,7 @@ def main():
                        "l2": "inputs larger than L2: 906 MB of experts per layer vs 126 MB L2; "
                              "router and shared expert (3.9 MB) stay L2-resident across tokens"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": TOKENS * D * 4,
-                    "d2h_bytes_per_step": TOKENS * D * 4},
+                    "d2h_bytes_per_step": TOKENS * (D * 4 + 4)},
             "gpu_launches": len(names) * TOKENS * args.steps,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,

@@ -32,6 +32,7 @@
 #define NO_OWNER UINT64_MAX
 
 typedef struct {
+    cudaGraphExec_t tok_graph; /* host-pointer single-token call, captured once */
     uint16_t *router;     /* [E, d] */
     uint16_t *shgate;     /* [d] */
     float *bias;          /* [E] or NULL */
@@ -46,8 +47,12 @@ struct qmoe_ctx {
     int num_sms;
     cudaStream_t stream, copy_stream;
     cudaEvent_t copy_done;
+    /* device error word and output share one allocation (err at 0, out at
+       256) so a host-pointer forward reads both back with one copy; the
+       pinned mirror has the same layout */
+    uint8_t *io_dev, *io_pin;
     int *err_dev;
-    int *err_host; /* pinned */
+    int *err_host;
     void *dsync;     /* launch counter + exchange area of the single-launch decode kernel */
     layer_dev *layers;
     /* expert pool */
@@ -89,6 +94,7 @@ struct qmoe_ctx {
 };
 
 static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err);
+static int report_dev_err(qmoe_ctx *c, int code, cudaStream_t st, qmoe_err *err);
 
 static void seterr(qmoe_err *err, const char *fmt, ...) {
     if (!err) return;
@@ -234,6 +240,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
     if (c->layers) {
         for (int l = 0; l < c->cfg.num_layers; l++) {
+            if (c->layers[l].tok_graph) cudaGraphExecDestroy(c->layers[l].tok_graph);
             cudaFree(c->layers[l].router);
             cudaFree(c->layers[l].shgate);
             cudaFree(c->layers[l].bias);
@@ -242,19 +249,17 @@ void qmoe_destroy(qmoe_ctx *c) {
     }
     cudaFree(c->pool);
     cudaFree(c->slot_of_dev);
-    cudaFree(c->err_dev);
+    cudaFree(c->io_dev);
     cudaFree(c->dsync);
     cudaFree(c->x_dev);
-    cudaFree(c->out_dev);
     cudaFree(c->logits);
     cudaFree(c->idx);
     cudaFree(c->wts);
     cudaFree(c->sgate);
     cudaFree(c->h);
     cudaFreeHost(c->x_pin);
-    cudaFreeHost(c->out_pin);
     cudaFreeHost(c->idx_pin);
-    cudaFreeHost(c->err_host);
+    cudaFreeHost(c->io_pin);
     cudaFreeHost(c->host_store);
     free(c->slot_of_host);
     free(c->slot_owner);
@@ -337,9 +342,16 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&c->copy_done, cudaEventDisableTiming));
-    CK(cudaMalloc((void **)&c->err_dev, sizeof(int)));
-    CK(cudaMemset(c->err_dev, 0, sizeof(int)));
-    CK(cudaMallocHost((void **)&c->err_host, sizeof(int)));
+    {
+        const size_t io = 256 + (size_t)T * L->d * sizeof(float);
+        CK(cudaMalloc((void **)&c->io_dev, io));
+        CK(cudaMemset(c->io_dev, 0, 256));
+        CK(cudaMallocHost((void **)&c->io_pin, io));
+        c->err_dev = (int *)c->io_dev;
+        c->err_host = (int *)c->io_pin;
+        c->out_dev = (float *)(c->io_dev + 256);
+        c->out_pin = (float *)(c->io_pin + 256);
+    }
     CK(cudaMalloc(&c->dsync, qk_decode_sync_bytes(L)));
     CK(cudaMemset(c->dsync, 0, qk_decode_sync_bytes(L)));
     c->layers = calloc((size_t)Lz, sizeof(layer_dev));
@@ -395,14 +407,12 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     }
     /* workspaces for max_tokens */
     CK(cudaMalloc((void **)&c->x_dev, (size_t)T * L->d * sizeof(float)));
-    CK(cudaMalloc((void **)&c->out_dev, (size_t)T * L->d * sizeof(float)));
     CK(cudaMalloc((void **)&c->logits, (size_t)T * (E + 1) * sizeof(float)));
     CK(cudaMalloc((void **)&c->idx, (size_t)T * L->k * sizeof(int32_t)));
     CK(cudaMalloc((void **)&c->wts, (size_t)T * L->k * sizeof(float)));
     CK(cudaMalloc((void **)&c->sgate, (size_t)T * sizeof(float)));
     CK(cudaMalloc((void **)&c->h, (size_t)T * (L->k + 1) * L->I * sizeof(float)));
     CK(cudaMallocHost((void **)&c->x_pin, (size_t)T * L->d * sizeof(float)));
-    CK(cudaMallocHost((void **)&c->out_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->idx_pin, (size_t)T * L->k * sizeof(int32_t)));
     if (c->ep_world > 1) {
         /* a rank receives at most every rank's T tokens x k slots */
@@ -600,6 +610,10 @@ int qmoe_upload_layer(qmoe_ctx *c, int layer, const qmoe_layer_weights *w, qmoe_
     const qk_layout *L = &c->L;
     layer_dev *ld = &c->layers[layer];
     uint8_t *stage = NULL;
+    if (ld->tok_graph) { /* it holds this layer's old pointers */
+        cudaGraphExecDestroy(ld->tok_graph);
+        ld->tok_graph = NULL;
+    }
     const int batch = 16;
     CK(cudaSetDevice(c->cfg.device));
     CK(cudaStreamSynchronize(c->stream));
@@ -969,7 +983,12 @@ static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err) {
         seterr(err, "qmoe: CUDA error: %s", cudaGetErrorString(ce));
         return -1;
     }
-    int code = *c->err_host;
+    return report_dev_err(c, *c->err_host, st, err);
+}
+
+/* code: the error word as read back (0: no error). On an error, clears the
+ * word and the decode kernel's barrier and exchange area. */
+static int report_dev_err(qmoe_ctx *c, int code, cudaStream_t st, qmoe_err *err) {
     if (code) {
         /* clear the sticky word and the decode kernel's counter and exchange
          * area (a launch that gave up may have left its barrier unfinished) */
@@ -1006,18 +1025,65 @@ int qmoe_forward(qmoe_ctx *c, int layer, const float *x, int n, float *out, qmoe
     double t0 = now_s();
     size_t bytes = (size_t)n * c->L.d * sizeof(float);
     memcpy(c->x_pin, x, bytes);
+    if (n == 1 && c->resident_all && layer >= 0 && layer < c->cfg.num_layers &&
+        c->layers[layer].ready) {
+        /* one token: x read by a small kernel from pinned memory (the decode
+         * kernel's prologue overlaps it), the output written straight into
+         * pinned memory, the error word copied back by a dependent launch;
+         * no copy-engine transfers. The three launches are captured once per
+         * layer as a graph (fixed buffers) and replayed. */
+        layer_dev *ld = &c->layers[layer];
+        if (!ld->tok_graph) {
+            cudaGraph_t g = NULL;
+            int ok = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+            if (ok) {
+                int rc = qk_launch_copy_in(c->x_pin, c->x_dev, bytes, c->stream) ||
+                         qmoe_forward_dev(c, layer, c->x_dev, QMOE_F32, n, c->out_pin, c->stream,
+                                          err) ||
+                         qk_launch_report(c->err_dev, c->err_host, c->stream);
+                cudaError_t ee = cudaStreamEndCapture(c->stream, &g);
+                ok = rc == 0 && ee == cudaSuccess && g &&
+                     cudaGraphInstantiate(&ld->tok_graph, g, 0) == cudaSuccess;
+                if (g) cudaGraphDestroy(g);
+            }
+            if (!ok) {
+                cudaGetLastError();
+                ld->tok_graph = NULL;
+                seterr(err, "qmoe_forward: could not capture the single-token call");
+                return -1;
+            }
+            c->stats.decode_calls--; /* counted below, once per call */
+        }
+        c->stats.decode_calls++;
+        c->last_T = 1;
+        if (cudaGraphLaunch(ld->tok_graph, c->stream) != cudaSuccess) {
+            seterr(err, "qmoe_forward: graph launch failed");
+            return -1;
+        }
+        cudaError_t se = cudaStreamSynchronize(c->stream);
+        if (se != cudaSuccess) {
+            seterr(err, "qmoe_forward: %s", cudaGetErrorString(se));
+            return -1;
+        }
+        if (report_dev_err(c, *(volatile int *)c->err_host, c->stream, err)) return -1;
+        memcpy(out, c->out_pin, bytes);
+        c->stats.forward_seconds += now_s() - t0;
+        return 0;
+    }
     cudaError_t ce = cudaMemcpyAsync(c->x_dev, c->x_pin, bytes, cudaMemcpyHostToDevice, c->stream);
     if (ce != cudaSuccess) {
         seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
         return -1;
     }
     if (qmoe_forward_dev(c, layer, c->x_dev, QMOE_F32, n, c->out_dev, c->stream, err)) return -1;
-    ce = cudaMemcpyAsync(c->out_pin, c->out_dev, bytes, cudaMemcpyDeviceToHost, c->stream);
+    /* the error word and the output in one copy */
+    ce = cudaMemcpyAsync(c->io_pin, c->io_dev, 256 + bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->stream);
     if (ce != cudaSuccess) {
         seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
         return -1;
     }
-    if (check_dev_err(c, c->stream, err)) return -1;
+    if (report_dev_err(c, *c->err_host, c->stream, err)) return -1;
     memcpy(out, c->out_pin, bytes);
     c->stats.forward_seconds += now_s() - t0;
     return 0;

@@ -84,6 +84,13 @@ int qk_launch_topk(const qk_fwd *f, void *stream, int pdl);
 int qk_launch_decode_gateup(const qk_fwd *f, void *stream, int pdl);
 int qk_launch_decode_down(const qk_fwd *f, void *stream, int pdl);
 
+/* Host-pointer single-token calls: copy `bytes` (a multiple of 16) of x from
+ * pinned host memory to the device with one CTA that lets its dependents
+ * launch at once; after the layer, a dependent launch copies the error word
+ * to pinned host memory. */
+int qk_launch_copy_in(const void *src_host, void *dst, size_t bytes, void *stream);
+int qk_launch_report(const int *err, int *err_host, void *stream);
+
 /* Single-launch decode (T == 1): router, top-k, gate/up and down+combine in
  * one persistent kernel with one CTA per SM and grid barriers between the
  * phases. sync: qk_decode_sync_bytes(L) bytes of device memory owned by the

@@ -335,6 +335,20 @@ __global__ void __launch_bounds__(256, 1) k_decode_down(qk_fwd f) {
 }
 
 // ---------------------------------------------------------------------------
+// Host-pointer single-token calls: x is read from pinned host memory by one
+// CTA (its dependents may launch at once, so the decode kernel's weight
+// prologue overlaps the PCIe read), and after the layer the error word is
+// copied to pinned host memory by a dependent launch (the output itself is
+// written to pinned host memory by the decode kernel).
+__global__ void k_copy_in(const float4 *src, float4 *dst, int n4) {
+    pdl_trigger();
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = src[i];
+}
+
+__global__ void k_report(const int *err, volatile int *err_host) {
+    pdl_wait();
+    if (threadIdx.x == 0) *err_host = *err;
+}
 
 cudaError_t launch(const void *fn, dim3 grid, dim3 block, size_t smem, void *stream, int pdl,
                    void **args) {
@@ -409,6 +423,22 @@ extern "C" int qk_launch_router(const qk_fwd *f, void *stream, int pdl) {
     dim3 grid(per_token < 64 ? per_token : 64, f->T);
     return launch(reinterpret_cast<const void *>(&k_router), grid, dim3(256),
                   static_cast<size_t>(f->L.d) * sizeof(double), stream, pdl, args);
+}
+
+extern "C" int qk_launch_copy_in(const void *src_host, void *dst, size_t bytes, void *stream) {
+    if (bytes % 16) return cudaErrorInvalidValue;
+    const float4 *s = static_cast<const float4 *>(src_host);
+    float4 *d = static_cast<float4 *>(dst);
+    int n4 = static_cast<int>(bytes / 16);
+    void *args[] = {&s, &d, &n4};
+    return launch(reinterpret_cast<const void *>(&k_copy_in), dim3(1), dim3(512), 0, stream, 0,
+                  args);
+}
+
+extern "C" int qk_launch_report(const int *err, int *err_host, void *stream) {
+    volatile int *h = err_host;
+    void *args[] = {&err, &h};
+    return launch(reinterpret_cast<const void *>(&k_report), dim3(1), dim3(32), 0, stream, 1, args);
 }
 
 extern "C" int qk_launch_topk(const qk_fwd *f, void *stream, int pdl) {
