@@ -188,21 +188,23 @@ int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream,
  * loaded at run time from libnccl.so.2).
  * qmoe_forward_ep is a collective replacement of qmoe_forward_dev for the
  * rank's own n tokens (device pointers, n may differ between ranks and may
- * be 0): local routing, an all-to-all of (token, slot) rows to the owners of
- * their experts, the owners' grouped GEMMs, an all-to-all of the down outputs
- * back, then the shared expert and the weighted combine on the token's rank.
- * It waits for the row counts on the host once per call. No reference
- * counterpart: the C port runs on one device. */
+ * be 0): local routing; each token sent once (fp16, with its k slots) to
+ * every rank that owns one of its experts; the owners' grouped GEMMs and a
+ * weighted combine of each token's local slots; one fp32 partial row per
+ * (token, rank) sent back; on the token's rank the partials (in rank order)
+ * plus the shared expert. It waits for the row counts on the host once per
+ * call. No reference counterpart: the C port runs on one device. */
 #define QMOE_EP_ID_BYTES 128
 int qmoe_ep_unique_id(unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err);
 int qmoe_ep_connect(qmoe_ctx *ctx, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err);
 int qmoe_forward_ep(qmoe_ctx *ctx, int layer, const void *x_dev, int x_dtype, int n,
                     float *out_dev, void *stream, qmoe_err *err);
 /* Host form of qmoe_forward_ep's dispatch plan, the same arithmetic as its
- * device kernels: for the routing idx [n, k] of one rank, counts[g] = rows
- * bound for rank g (of W, E % W == 0) and, if pos is not NULL, the send
- * position of each (token, slot): grouped by destination rank, in (token,
- * slot) order within a rank. Returns 0, or -1 on bad arguments. */
+ * device kernels: for the routing idx [n, k] of one rank, counts[g] = tokens
+ * sent to rank g (of W <= 64, E % W == 0: those with at least one expert in
+ * [g E/W, (g+1) E/W)) and, if pos is not NULL, pos[g * n + t] = the send
+ * row of token t for rank g, or -1: rows grouped by destination rank, in
+ * token order within a rank. Returns 0, or -1 on bad arguments. */
 int qmoe_ep_plan_host(const int32_t *idx, int n, int k, int E, int W, int *counts, int *pos);
 
 /* Routing of the last forward call (waits for it): idx [n, k] in

@@ -415,7 +415,7 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaMallocHost((void **)&c->x_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->idx_pin, (size_t)T * L->k * sizeof(int32_t)));
     if (c->ep_world > 1) {
-        /* a rank receives at most every rank's T tokens x k slots */
+        /* a rank receives at most every rank's T tokens, once each */
         char msg[256] = {0};
         c->prefill = qk_prefill_create(L, T * c->ep_world, c->pool, c->nslots + Lz, c->num_sms,
                                        msg, sizeof(msg));
@@ -423,7 +423,7 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
             seterr(err, "qmoe_create: expert parallelism needs the grouped path: %s", msg);
             goto fail;
         }
-        CK((cudaError_t)qk_ep_alloc(c->prefill, T * L->k, T * c->ep_world * L->k));
+        CK((cudaError_t)qk_ep_alloc(c->prefill, T, c->ep_world));
         CK(cudaMalloc((void **)&c->ep_counts_dev, 2 * sizeof(int) * c->ep_world));
         CK(cudaMallocHost((void **)&c->ep_counts_pin, 2 * sizeof(int) * c->ep_world));
     } else if (T > 1) {
@@ -1311,10 +1311,11 @@ int qmoe_ep_connect(qmoe_ctx *c, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_
 }
 
 /* One collective forward: every rank calls it for the same layer with its
- * own n tokens. Route locally; send each (token, slot) row to the rank that
- * owns its expert (counts first, then fp16 rows and expert ids); run the
- * grouped GEMMs on the rows received; send the down outputs back; add the
- * shared expert of the local tokens and combine. */
+ * own n tokens. Route locally; send each token once to every rank that owns
+ * one of its experts (counts first, then fp16 rows, slot expert ids and
+ * weights); run the grouped GEMMs on the rows received and combine each
+ * row's local slots; send those partial rows back; add them (rank order)
+ * and the shared expert of the local tokens. */
 int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, float *out,
                     void *stream, qmoe_err *err) {
     if (err) err->msg[0] = 0;
@@ -1336,7 +1337,7 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
         return -1;
     }
     const nccl_fns *nc = nccl_api();
-    const int W = c->ep_world, d = c->L.d;
+    const int W = c->ep_world, d = c->L.d, k = c->L.k;
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
     if (cudaSetDevice(c->cfg.device) != cudaSuccess) {
         seterr(err, "qmoe_forward_ep: cudaSetDevice failed");
@@ -1347,13 +1348,11 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
     c->last_T = n;
     c->stats.prefill_calls++;
     int *cnt = c->ep_counts_dev, *rcnt = c->ep_counts_dev + W;
-    void *send_x, *recv_x;
-    int32_t *send_e, *recv_e;
-    float *ret, *back;
-    qk_ep_buffers(c->prefill, &send_x, &send_e, &recv_x, &recv_e, &ret, &back);
+    qk_ep_bufs b;
+    qk_ep_buffers(c->prefill, &b);
     if (n > 0) {
         if (route(c, layer, &f, st, 0, NULL, err)) return -1;
-        if (kerr(qk_ep_dispatch(c->prefill, &f, W, cnt, st), "ep dispatch", err)) return -1;
+        if (kerr(qk_ep_dispatch(c->prefill, &f, cnt, st), "ep dispatch", err)) return -1;
     } else if (cudaMemsetAsync(cnt, 0, sizeof(int) * W, st) != cudaSuccess) {
         seterr(err, "qmoe_forward_ep: memset failed");
         return -1;
@@ -1381,37 +1380,42 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
         ns += (size_t)hc[p];
         nr += (size_t)hr[p];
     }
-    if (nr > (size_t)c->cfg.max_tokens * W * c->L.k) {
+    if (nr > (size_t)c->cfg.max_tokens * W) {
         seterr(err, "qmoe_forward_ep: %zu rows received, more than the plan holds", nr);
         return -1;
     }
-    /* rows and expert ids out, rows and expert ids in */
+    /* token rows with their slots out, and in */
     NCK(nc->group_start(), "qmoe_forward_ep");
     for (int p = 0; p < W; p++) {
-        if (hc[p]) {
-            NCK(nc->send((const uint16_t *)send_x + so[p] * d, (size_t)hc[p] * d, ncclFloat16, p,
-                         c->ep_comm, st), "qmoe_forward_ep dispatch");
-            NCK(nc->send(send_e + so[p], (size_t)hc[p], ncclInt32, p, c->ep_comm, st),
+        const size_t sc = (size_t)hc[p], rc = (size_t)hr[p];
+        if (sc) {
+            NCK(nc->send((const uint16_t *)b.send_x + so[p] * d, sc * d, ncclFloat16, p, c->ep_comm,
+                         st), "qmoe_forward_ep dispatch");
+            NCK(nc->send(b.send_e + so[p] * k, sc * k, ncclInt32, p, c->ep_comm, st),
+                "qmoe_forward_ep dispatch");
+            NCK(nc->send(b.send_w + so[p] * k, sc * k, ncclFloat32, p, c->ep_comm, st),
                 "qmoe_forward_ep dispatch");
         }
-        if (hr[p]) {
-            NCK(nc->recv((uint16_t *)recv_x + ro[p] * d, (size_t)hr[p] * d, ncclFloat16, p,
-                         c->ep_comm, st), "qmoe_forward_ep dispatch");
-            NCK(nc->recv(recv_e + ro[p], (size_t)hr[p], ncclInt32, p, c->ep_comm, st),
+        if (rc) {
+            NCK(nc->recv((uint16_t *)b.recv_x + ro[p] * d, rc * d, ncclFloat16, p, c->ep_comm, st),
+                "qmoe_forward_ep dispatch");
+            NCK(nc->recv(b.recv_e + ro[p] * k, rc * k, ncclInt32, p, c->ep_comm, st),
+                "qmoe_forward_ep dispatch");
+            NCK(nc->recv(b.recv_w + ro[p] * k, rc * k, ncclFloat32, p, c->ep_comm, st),
                 "qmoe_forward_ep dispatch");
         }
     }
     NCK(nc->group_end(), "qmoe_forward_ep");
-    /* this rank's experts over the rows it received */
+    /* this rank's experts over the rows it received, combined per row */
     if (kerr(qk_ep_experts(c->prefill, &f, (int)nr, st), "ep experts", err)) return -1;
-    /* down outputs back to the ranks that own the tokens */
+    /* partial rows back to the ranks that own the tokens */
     NCK(nc->group_start(), "qmoe_forward_ep");
     for (int p = 0; p < W; p++) {
         if (hr[p])
-            NCK(nc->send(ret + ro[p] * d, (size_t)hr[p] * d, ncclFloat32, p, c->ep_comm, st),
+            NCK(nc->send(b.ret + ro[p] * d, (size_t)hr[p] * d, ncclFloat32, p, c->ep_comm, st),
                 "qmoe_forward_ep combine");
         if (hc[p])
-            NCK(nc->recv(back + so[p] * d, (size_t)hc[p] * d, ncclFloat32, p, c->ep_comm, st),
+            NCK(nc->recv(b.back + so[p] * d, (size_t)hc[p] * d, ncclFloat32, p, c->ep_comm, st),
                 "qmoe_forward_ep combine");
     }
     NCK(nc->group_end(), "qmoe_forward_ep");
@@ -1421,21 +1425,32 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
 }
 
 int qmoe_ep_plan_host(const int32_t *idx, int n, int k, int E, int W, int *counts, int *pos) {
-    if (!idx || !counts || n < 0 || k < 1 || W < 1 || E % W) return -1;
+    if (!idx || !counts || n < 0 || k < 1 || W < 1 || W > 64 || E % W) return -1;
     const int e_per = E / W;
+    unsigned long long *mask = malloc(sizeof(unsigned long long) * (n > 0 ? n : 1));
+    if (!mask) return -1;
     for (int g = 0; g < W; g++) counts[g] = 0;
-    for (int a = 0; a < n * k; a++) {
-        if (idx[a] < 0 || idx[a] >= E) return -1;
-        counts[idx[a] / e_per]++;
+    for (int t = 0; t < n; t++) {
+        unsigned long long m = 0;
+        for (int s = 0; s < k; s++) {
+            int e = idx[(size_t)t * k + s];
+            if (e < 0 || e >= E) {
+                free(mask);
+                return -1;
+            }
+            m |= 1ull << (e / e_per);
+        }
+        mask[t] = m;
+        for (int g = 0; g < W; g++) counts[g] += (int)((m >> g) & 1ull);
     }
     if (pos) {
-        int base[64];
-        if (W > 64) return -1;
-        for (int g = 0, b = 0; g < W; g++) {
-            base[g] = b;
-            b += counts[g];
+        int base = 0;
+        for (int g = 0; g < W; g++) {
+            int p = base;
+            for (int t = 0; t < n; t++) pos[(size_t)g * n + t] = ((mask[t] >> g) & 1ull) ? p++ : -1;
+            base += counts[g];
         }
-        for (int a = 0; a < n * k; a++) pos[a] = base[idx[a] / e_per]++;
     }
+    free(mask);
     return 0;
 }

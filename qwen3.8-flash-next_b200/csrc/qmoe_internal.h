@@ -129,21 +129,28 @@ int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot_index, voi
 int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream, void *mid_event);
 
 /* Expert parallelism (qmoe_prefill.cu). Rank g of G owns experts
- * [g E/G, (g+1) E/G). The plan holds the send / receive rows:
- *   qk_ep_alloc     buffers for send_max (token, slot) rows out and recv_max in
- *   qk_ep_dispatch  after routing: counts[G] rows per destination (device),
- *                   send rows (fp16 x, natural order) and expert ids grouped
- *                   by destination, stable in (token, slot) order
- *   qk_ep_experts   grouped GEMMs over `rows` received rows (k = 1 each, no
- *                   shared expert); their down outputs in received order
- *   qk_ep_finish    the shared expert over this rank's tokens and the
- *                   combine of the returned outputs (send order) into out
+ * [g E/G, (g+1) E/G). A token travels once to every rank that owns one of
+ * its experts (fp16 x plus its k slots, other ranks' slots as expert id -1),
+ * that rank combines its slots' outputs with the routing weights, and one
+ * fp32 partial row per (token, rank) comes back:
+ *   qk_ep_alloc     buffers for T tokens per rank and G ranks
+ *   qk_ep_dispatch  after routing: counts[G] rows per destination (device)
+ *                   and the send rows grouped by destination, token order
+ *   qk_ep_experts   grouped GEMMs over `rows` received rows and the
+ *                   expert-side combine into one partial row each
+ *   qk_ep_finish    the shared expert over this rank's tokens and the sum
+ *                   of the returned partials (rank order) into out
  * The transfers between them are the caller's (NCCL send/recv on the
  * buffers of qk_ep_buffers). */
-int qk_ep_alloc(qk_prefill *p, int send_max, int recv_max);
-void qk_ep_buffers(qk_prefill *p, void **send_x, int32_t **send_e, void **recv_x, int32_t **recv_e,
-                   float **ret, float **back);
-int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int G, int *counts, void *stream);
+typedef struct {
+    void *send_x, *recv_x;       /* fp16 [rows, d] */
+    int32_t *send_e, *recv_e;    /* [rows, k] */
+    float *send_w, *recv_w;      /* [rows, k] */
+    float *ret, *back;           /* fp32 [rows, d]: partials received order / send order */
+} qk_ep_bufs;
+int qk_ep_alloc(qk_prefill *p, int T, int G);
+void qk_ep_buffers(qk_prefill *p, qk_ep_bufs *b);
+int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int *counts, void *stream);
 int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, void *stream);
 int qk_ep_finish(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream);
 

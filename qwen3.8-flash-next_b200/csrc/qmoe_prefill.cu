@@ -429,9 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // routing -> groups
 
+// Slots with a negative expert id (owned by another rank) are skipped.
 __global__ void k_count(const int32_t *idx, int nk, int *counts) {
     for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < nk; a += gridDim.x * blockDim.x)
-        atomicAdd(counts + idx[a], 1);
+        if (idx[a] >= 0) atomicAdd(counts + idx[a], 1);
 }
 
 // One CTA (1024 threads, E + 1 <= 1024 groups). Group 0 is the shared expert
@@ -439,7 +440,8 @@ __global__ void k_count(const int32_t *idx, int nk, int *counts) {
 // Writes the first row of each routed expert and the M-tile list.
 __global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh,
                                                const int32_t *slot_of, int shared_slot,
-                                               int *row0, MTile *tiles, int *n_mtiles) {
+                                               int *row0, MTile *tiles, int *n_mtiles,
+                                               int *n_rows) {
     __shared__ int s_scan[1024], s_tscan[1024];
     const int g = threadIdx.x;
     const int rows = g == 0 ? nsh : (g <= E ? counts[g - 1] : 0);
@@ -466,7 +468,10 @@ __global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh
         m.pad = 0;
         tiles[t0 + i] = m;
     }
-    if (g == 1023) *n_mtiles = s_tscan[1023];
+    if (g == 1023) {
+        *n_mtiles = s_tscan[1023];
+        *n_rows = s_scan[1023];
+    }
 }
 
 // One CTA per routed expert: its (token, slot) assignments in token order
@@ -512,10 +517,10 @@ enum { XK_F32 = 0, XK_BF16 = 1, XK_F16 = 2 };
 
 // Grouped fp16 A operand: row r holds token r (r < nsh, the shared group) or
 // perm_tok[r]; each 8-element chunk in the order [0,4,1,5,2,6,3,7].
-__global__ void k_gather(const void *x, int x_kind, int d, int nsh, int rows, const int *perm_tok,
-                         __half *xp) {
+__global__ void k_gather(const void *x, int x_kind, int d, int nsh, int rows, const int *n_rows,
+                         const int *perm_tok, __half *xp) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= rows) return;
+    if (warp >= rows || warp >= *n_rows) return;
     const int tok = warp < nsh ? warp : perm_tok[warp];
     __half *dst = xp + static_cast<size_t>(warp) * d;
     for (int c = lane; c < d / 8; c += 32) {
@@ -589,23 +594,30 @@ __global__ void k_combine(const float *Yr, const float *Ysh, const int *inv, con
 // expert-parallel dispatch and return (one rank per GPU; rank g owns experts
 // [g * E_per, (g + 1) * E_per))
 
-// Rows per destination rank: counts[g] (block-aggregated).
-__global__ void k_ep_count(const int32_t *idx, int nk, int e_per, int G, int *counts) {
+// Each token goes once to every rank that owns one of its experts; its
+// other slots travel with it as expert id -1. The bit mask of destinations
+// of token t: mask[t]; rows per destination: counts[g] (block-aggregated).
+__global__ void k_ep_count(const int32_t *idx, int T, int k, int e_per, int G,
+                           unsigned long long *mask, int *counts) {
     __shared__ int s_c[64];
     for (int g = threadIdx.x; g < G; g += blockDim.x) s_c[g] = 0;
     __syncthreads();
-    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < nk; a += gridDim.x * blockDim.x)
-        atomicAdd(&s_c[idx[a] / e_per], 1);
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+        unsigned long long m = 0;
+        for (int s = 0; s < k; ++s) m |= 1ull << (idx[t * k + s] / e_per);
+        mask[t] = m;
+        for (unsigned long long r = m; r; r &= r - 1) atomicAdd(&s_c[__ffsll(r) - 1], 1);
+    }
     __syncthreads();
     for (int g = threadIdx.x; g < G; g += blockDim.x)
         if (s_c[g]) atomicAdd(counts + g, s_c[g]);
 }
 
-// One CTA per destination rank g: the (token, slot) assignments bound for g
-// get consecutive send positions after the rows of ranks < g, in
-// assignment order (stable); the expert id travels with the row.
-__global__ void __launch_bounds__(1024) k_ep_positions(const int32_t *idx, int nk, int e_per,
-                                                       const int *counts, int *pos, int32_t *send_e) {
+// One CTA per destination rank g: the tokens bound for g get consecutive
+// send positions after the rows of ranks < g, in token order; pos[g * T + t]
+// (-1 when t does not go to g).
+__global__ void __launch_bounds__(1024) k_ep_positions(const unsigned long long *mask, int T,
+                                                       const int *counts, int *pos) {
     __shared__ int s_warp[32];
     __shared__ int s_base;
     const int g = blockIdx.x;
@@ -616,10 +628,9 @@ __global__ void __launch_bounds__(1024) k_ep_positions(const int32_t *idx, int n
         s_base = b;
     }
     __syncthreads();
-    for (int a0 = 0; a0 < nk; a0 += 1024) {
-        const int a = a0 + threadIdx.x;
-        const int e = a < nk ? idx[a] : -1;
-        const bool mine = a < nk && e / e_per == g;
+    for (int t0 = 0; t0 < T; t0 += 1024) {
+        const int t = t0 + threadIdx.x;
+        const bool mine = t < T && ((mask[t] >> g) & 1ull);
         const unsigned m = __ballot_sync(QK_FULL, mine);
         if (lane == 0) s_warp[warp] = __popc(m);
         __syncthreads();
@@ -627,31 +638,39 @@ __global__ void __launch_bounds__(1024) k_ep_positions(const int32_t *idx, int n
             int v = s_warp[lane];
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
-                const int t = __shfl_up_sync(QK_FULL, v, off);
-                if (lane >= off) v += t;
+                const int u = __shfl_up_sync(QK_FULL, v, off);
+                if (lane >= off) v += u;
             }
             s_warp[lane] = v;
         }
         __syncthreads();
-        const int before = (warp ? s_warp[warp - 1] : 0) + __popc(m & ((1u << lane) - 1u));
-        if (mine) {
-            const int p = s_base + before;
-            pos[a] = p;
-            send_e[p] = e;
-        }
+        if (t < T)
+            pos[static_cast<size_t>(g) * T + t] =
+                mine ? s_base + (warp ? s_warp[warp - 1] : 0) + __popc(m & ((1u << lane) - 1u)) : -1;
         __syncthreads();
         if (threadIdx.x == 0) s_base += s_warp[31];
         __syncthreads();
     }
 }
 
-// send_x[pos[a]] = fp16(x[a / k]), natural element order; one warp per row.
-__global__ void k_ep_pack_x(const void *x, int x_bf16, int d, int nk, int k, const int *pos,
-                            __half *send_x) {
-    const int a = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (a >= nk) return;
-    const int t = a / k;
-    __half *dst = send_x + static_cast<size_t>(pos[a]) * d;
+// Send row p = pos[g, t]: fp16 x[t] (natural element order) and the token's
+// k slots, expert ids of other ranks replaced by -1 (weights 0). One warp
+// per (rank, token).
+__global__ void k_ep_pack(const void *x, int x_bf16, int d, int T, int k, int e_per, int G,
+                          const int32_t *idx, const float *wts, const int *pos, __half *send_x,
+                          int32_t *send_e, float *send_w) {
+    const int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (wi >= G * T) return;
+    const int g = wi / T, t = wi % T;
+    const int p = pos[wi];
+    if (p < 0) return;
+    if (lane < k) {
+        const int e = idx[t * k + lane];
+        const bool own = e / e_per == g;
+        send_e[static_cast<size_t>(p) * k + lane] = own ? e : -1;
+        send_w[static_cast<size_t>(p) * k + lane] = own ? wts[t * k + lane] : 0.f;
+    }
+    __half *dst = send_x + static_cast<size_t>(p) * d;
     for (int c = lane; c < d / 8; c += 32) {
         float v[8];
         if (x_bf16) {
@@ -660,9 +679,9 @@ __global__ void k_ep_pack_x(const void *x, int x_bf16, int d, int nk, int k, con
             v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
             v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
         } else {
-            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
+            const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
                                                                static_cast<size_t>(t) * d) + 2 * c;
-            const float4 u = p[0], w = p[1];
+            const float4 u = q[0], w = q[1];
             v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
         }
         uint4 o;
@@ -674,14 +693,51 @@ __global__ void k_ep_pack_x(const void *x, int x_bf16, int d, int nk, int k, con
     }
 }
 
-// ret[r] = Y[inv[r]]: the down outputs of the received rows, back in the
-// order they arrived (so each source rank's block is contiguous).
-__global__ void k_ep_ret(const float *Y, const int *inv, int rows, int d, float *ret) {
-    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (r >= rows) return;
-    const float4 *src = reinterpret_cast<const float4 *>(Y + static_cast<size_t>(inv[r]) * d);
-    float4 *dst = reinterpret_cast<float4 *>(ret + static_cast<size_t>(r) * d);
-    for (int c = lane; c < d / 4; c += 32) dst[c] = src[c];
+// Expert-side combine of the received rows: part[r] = sum over the row's
+// local slots (expert id >= 0) of w * Y[inv[r, s]], in slot order.
+__global__ void k_ep_partial(const float *Y, const int *inv, const int32_t *e_of, const float *w,
+                             int k, int d, float *part) {
+    const int r = blockIdx.x;
+    for (int c = threadIdx.x; c < d / 4; c += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < k; ++s) {
+            const size_t a = static_cast<size_t>(r) * k + s;
+            if (e_of[a] < 0) continue;
+            const float4 v = reinterpret_cast<const float4 *>(Y + static_cast<size_t>(inv[a]) * d)[c];
+            const float ws = w[a];
+            acc.x = fmaf(ws, v.x, acc.x);
+            acc.y = fmaf(ws, v.y, acc.y);
+            acc.z = fmaf(ws, v.z, acc.z);
+            acc.w = fmaf(ws, v.w, acc.w);
+        }
+        reinterpret_cast<float4 *>(part + static_cast<size_t>(r) * d)[c] = acc;
+    }
+}
+
+// Token side: out[t] = sum over the destination ranks in rank order of the
+// returned partial rows + sigmoid(g_t) * Ysh[t].
+__global__ void k_ep_final(const float *back, const int *pos, int T, int G, const float *Ysh,
+                           const float *sgate, int d, float *out) {
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x; c < d / 4; c += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int g = 0; g < G; ++g) {
+            const int p = pos[static_cast<size_t>(g) * T + t];
+            if (p < 0) continue;
+            const float4 v = reinterpret_cast<const float4 *>(back + static_cast<size_t>(p) * d)[c];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const float sg = sgate[t];
+        const float4 v = reinterpret_cast<const float4 *>(Ysh + static_cast<size_t>(t) * d)[c];
+        acc.x = fmaf(sg, v.x, acc.x);
+        acc.y = fmaf(sg, v.y, acc.y);
+        acc.z = fmaf(sg, v.z, acc.z);
+        acc.w = fmaf(sg, v.w, acc.w);
+        reinterpret_cast<float4 *>(out + static_cast<size_t>(t) * d)[c] = acc;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -984,7 +1040,7 @@ bool map_3d_u8(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t ro
 struct qk_prefill {
     qk_layout L;
     int max_tokens, num_sms, pool_slots, rows_max, tiles_max;
-    int *counts, *row0, *inv, *perm_tok, *n_mtiles;
+    int *counts, *row0, *inv, *perm_tok, *n_mtiles, *n_rows;
     MTile *tiles;
     __half *xp, *H;
     float *Y;
@@ -998,12 +1054,14 @@ struct qk_prefill {
     MTile *rtiles;
     int *rn;
     CUtensorMap tmXr;
-    // expert parallelism: send and receive rows, positions, returned outputs
-    int ep_send_max, ep_recv_max;
-    int *ep_pos;                  // [max_tokens * k] send position of each (token, slot)
-    int32_t *ep_send_e, *ep_recv_e;
-    __half *ep_send_x, *ep_recv_x;  // fp16 rows
-    float *ep_ret, *ep_back;        // fp32 down outputs: received order / send order
+    // expert parallelism: one row per (token, destination rank)
+    int ep_T, ep_G;                 // tokens per rank, ranks
+    unsigned long long *ep_mask;    // [ep_T] destination ranks of each token
+    int *ep_pos;                    // [ep_G * ep_T] send row of (rank, token), -1 if none
+    int32_t *ep_send_e, *ep_recv_e; // [rows * k] slot expert ids (-1: another rank's)
+    float *ep_send_w, *ep_recv_w;   // [rows * k] slot weights
+    __half *ep_send_x, *ep_recv_x;  // [rows, d] fp16
+    float *ep_ret, *ep_back;        // [rows, d] fp32 partial outputs: received / send order
 };
 
 extern "C" void qk_prefill_destroy(qk_prefill *p) {
@@ -1013,6 +1071,7 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->inv);
     cudaFree(p->perm_tok);
     cudaFree(p->n_mtiles);
+    cudaFree(p->n_rows);
     cudaFree(p->tiles);
     cudaFree(p->xp);
     cudaFree(p->H);
@@ -1022,9 +1081,12 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->lga);
     cudaFree(p->rtiles);
     cudaFree(p->rn);
+    cudaFree(p->ep_mask);
     cudaFree(p->ep_pos);
     cudaFree(p->ep_send_e);
     cudaFree(p->ep_recv_e);
+    cudaFree(p->ep_send_w);
+    cudaFree(p->ep_recv_w);
     cudaFree(p->ep_send_x);
     cudaFree(p->ep_recv_x);
     cudaFree(p->ep_ret);
@@ -1058,6 +1120,7 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     if (e == cudaSuccess) e = cudaMalloc(&p->inv, sizeof(int) * static_cast<size_t>(max_tokens) * L->k);
     if (e == cudaSuccess) e = cudaMalloc(&p->perm_tok, sizeof(int) * R);
     if (e == cudaSuccess) e = cudaMalloc(&p->n_mtiles, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&p->n_rows, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&p->tiles, sizeof(MTile) * p->tiles_max);
     if (e == cudaSuccess) e = cudaMalloc(&p->xp, R * L->d * sizeof(__half));
     if (e == cudaSuccess) e = cudaMalloc(&p->H, 2 * R * L->I * sizeof(__half));  // hi, lo planes
@@ -1143,11 +1206,11 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     if (e != cudaSuccess) return e;
     if (nk > 0) k_count<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, p->counts);
     k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index, p->row0, p->tiles,
-                               p->n_mtiles);
+                               p->n_mtiles, p->n_rows);
     if (nk > 0) k_positions<<<E, 1024, 0, st>>>(idx, nk, k, p->row0, p->inv, p->perm_tok);
     if (rows > 0)
-        k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->perm_tok,
-                                                         p->xp);
+        k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->n_rows,
+                                                         p->perm_tok, p->xp);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     mark(0);
@@ -1210,57 +1273,65 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     return cudaGetLastError();
 }
 
-extern "C" int qk_ep_alloc(qk_prefill *p, int send_max, int recv_max) {
+extern "C" int qk_ep_alloc(qk_prefill *p, int T, int G) {
     const qk_layout &L = p->L;
-    if (send_max > p->max_tokens * L.k || recv_max > p->max_tokens * L.k) return cudaErrorInvalidValue;
-    p->ep_send_max = send_max;
-    p->ep_recv_max = recv_max;
-    const size_t d = static_cast<size_t>(L.d);
-    cudaError_t e = cudaMalloc(&p->ep_pos, sizeof(int) * send_max);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_e, sizeof(int32_t) * send_max);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_e, sizeof(int32_t) * recv_max);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_x, sizeof(__half) * send_max * d);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_x, sizeof(__half) * recv_max * d);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_ret, sizeof(float) * recv_max * d);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_back, sizeof(float) * send_max * d);
+    const size_t rows = static_cast<size_t>(T) * G;  // both directions: at most T per pair
+    if (G > 64 || rows > static_cast<size_t>(p->max_tokens)) return cudaErrorInvalidValue;
+    p->ep_T = T;
+    p->ep_G = G;
+    const size_t d = static_cast<size_t>(L.d), k = static_cast<size_t>(L.k);
+    cudaError_t e = cudaMalloc(&p->ep_mask, sizeof(unsigned long long) * T);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_pos, sizeof(int) * rows);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_e, sizeof(int32_t) * rows * k);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_e, sizeof(int32_t) * rows * k);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_w, sizeof(float) * rows * k);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_w, sizeof(float) * rows * k);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_x, sizeof(__half) * rows * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_x, sizeof(__half) * rows * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_ret, sizeof(float) * rows * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_back, sizeof(float) * rows * d);
     return e;
 }
 
-extern "C" void qk_ep_buffers(qk_prefill *p, void **send_x, int32_t **send_e, void **recv_x,
-                              int32_t **recv_e, float **ret, float **back) {
-    *send_x = p->ep_send_x;
-    *send_e = p->ep_send_e;
-    *recv_x = p->ep_recv_x;
-    *recv_e = p->ep_recv_e;
-    *ret = p->ep_ret;
-    *back = p->ep_back;
+extern "C" void qk_ep_buffers(qk_prefill *p, qk_ep_bufs *b) {
+    b->send_x = p->ep_send_x;
+    b->send_e = p->ep_send_e;
+    b->send_w = p->ep_send_w;
+    b->recv_x = p->ep_recv_x;
+    b->recv_e = p->ep_recv_e;
+    b->recv_w = p->ep_recv_w;
+    b->ret = p->ep_ret;
+    b->back = p->ep_back;
 }
 
-extern "C" int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int G, int *counts, void *stream) {
+extern "C" int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int *counts, void *stream) {
     const qk_layout &L = p->L;
-    const int nk = f->T * L.k;
-    if (nk > p->ep_send_max || G > 64 || L.E % G) return cudaErrorInvalidValue;
+    const int T = f->T, G = p->ep_G;
+    if (T > p->ep_T || L.E % G) return cudaErrorInvalidValue;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int e_per = L.E / G;
     cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * G, st);
     if (e != cudaSuccess) return e;
-    if (nk > 0) {
-        k_ep_count<<<(nk + 1023) / 1024, 1024, 0, st>>>(f->idx, nk, e_per, G, counts);
-        k_ep_positions<<<G, 1024, 0, st>>>(f->idx, nk, e_per, counts, p->ep_pos, p->ep_send_e);
-        k_ep_pack_x<<<(nk * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, nk, L.k, p->ep_pos,
-                                                          p->ep_send_x);
+    if (T > 0) {
+        k_ep_count<<<(T + 255) / 256, 256, 0, st>>>(f->idx, T, L.k, e_per, G, p->ep_mask, counts);
+        k_ep_positions<<<G, 1024, 0, st>>>(p->ep_mask, T, counts, p->ep_pos);
+        k_ep_pack<<<(G * T * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, L.k, e_per, G,
+                                                           f->idx, f->wts, p->ep_pos, p->ep_send_x,
+                                                           p->ep_send_e, p->ep_send_w);
     }
     return cudaGetLastError();
 }
 
 extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, void *stream) {
-    if (rows > p->ep_recv_max) return cudaErrorInvalidValue;
+    const qk_layout &L = p->L;
+    if (rows > p->ep_T * p->ep_G) return cudaErrorInvalidValue;
     if (rows == 0) return cudaSuccess;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = grouped(p, p->ep_recv_x, XK_F16, rows, p->ep_recv_e, 1, 0, f->slot_of, 0, f->err,
-                            st, nullptr);
+    cudaError_t e = grouped(p, p->ep_recv_x, XK_F16, rows, p->ep_recv_e, L.k, 0, f->slot_of, 0,
+                            f->err, st, nullptr);
     if (e != cudaSuccess) return e;
-    k_ep_ret<<<(rows * 32 + 255) / 256, 256, 0, st>>>(p->Y, p->inv, rows, p->L.d, p->ep_ret);
+    k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv, p->ep_recv_e, p->ep_recv_w, L.k, L.d,
+                                       p->ep_ret);
     return cudaGetLastError();
 }
 
@@ -1272,7 +1343,7 @@ extern "C" int qk_ep_finish(qk_prefill *p, const qk_fwd *f, int shared_slot_inde
     cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, nullptr, 0, 1, f->slot_of,
                             shared_slot_index, f->err, st, nullptr);
     if (e != cudaSuccess) return e;
-    k_combine<<<T, 256, 0, st>>>(p->ep_back, p->Y, p->ep_pos, f->wts, f->sgate, L.k, L.d, f->out);
+    k_ep_final<<<T, 256, 0, st>>>(p->ep_back, p->ep_pos, T, p->ep_G, p->Y, f->sgate, L.d, f->out);
     return cudaGetLastError();
 }
 

@@ -3,9 +3,10 @@ qmoe_forward_ep), a two-rank exchange of that plan over gloo on the CPU, and
 on two GPUs the collective forward itself against the C restatement.
 
 Rank g of W owns experts [g E/W, (g+1) E/W); each rank routes its own
-tokens, sends every (token, slot) row to the owner of its expert, and gets
-the down outputs back: the expert-parallel layout of the workload's
-prefill and batched-decode configurations."""
+tokens, sends each token once to every rank that owns one of its experts,
+and gets one combined partial row per (token, rank) back: the
+expert-parallel layout of the workload's prefill and batched-decode
+configurations."""
 import ctypes as C
 import os
 import socket
@@ -21,25 +22,27 @@ def _plan(idx, E, W):
     idx = np.ascontiguousarray(idx, np.int32)
     n, k = idx.shape
     counts = np.zeros(W, np.int32)
-    pos = np.zeros(n * k, np.int32)
+    pos = np.zeros(W * n, np.int32)
     rc = qmoe.lib().qmoe_ep_plan_host(idx.ctypes.data, n, k, E, W, counts.ctypes.data,
                                       pos.ctypes.data)
     assert rc == 0
-    return counts, pos.reshape(n, k)
+    return counts, pos.reshape(W, n)
 
 
-def test_plan_groups_rows_by_owner_stably(built):
+def test_plan_sends_each_token_once_per_owner_rank(built):
     rng = np.random.default_rng(7)
     E, W, n, k = 64, 4, 50, 6
     idx = np.stack([rng.choice(E, k, replace=False) for _ in range(n)]).astype(np.int32)
     counts, pos = _plan(idx, E, W)
     owner = idx // (E // W)
-    assert counts.tolist() == np.bincount(owner.ravel(), minlength=W).tolist()
-    flat = pos.ravel()
-    assert sorted(flat.tolist()) == list(range(n * k))           # a permutation
+    goes = np.stack([(owner == g).any(1) for g in range(W)])      # [W, n]
+    assert counts.tolist() == goes.sum(1).tolist()
+    sent = pos[pos >= 0]
+    assert sorted(sent.tolist()) == list(range(int(counts.sum())))  # rows 0..total-1 once
+    assert np.array_equal(pos >= 0, goes)
     starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
     for g in range(W):
-        mine = flat[owner.ravel() == g]                            # (token, slot) order
+        mine = pos[g][goes[g]]                                     # token order
         assert mine.tolist() == list(range(starts[g], starts[g] + counts[g]))
 
 
@@ -83,10 +86,16 @@ def _gloo_rank(rank, world, port, result):
         # counts out, counts in
         rcounts = torch.zeros(world, dtype=torch.int32)
         dist.all_to_all_single(rcounts, torch.from_numpy(counts))
-        # expert ids in send order, then the exchange itself
-        send_e = np.empty(idx.size, np.int32)
-        send_e[pos.ravel()] = idx.ravel()
-        recv_e = torch.zeros(int(rcounts.sum()), dtype=torch.int32)
+        # the slots of each sent row (other ranks' experts as -1), then the
+        # exchange itself
+        n, k = idx.shape
+        send_e = np.full((int(counts.sum()), k), -1, np.int32)
+        for g in range(world):
+            for t in range(n):
+                if pos[g, t] >= 0:
+                    own = idx[t] // (E // world) == g
+                    send_e[pos[g, t]] = np.where(own, idx[t], -1)
+        recv_e = torch.zeros((int(rcounts.sum()), k), dtype=torch.int32)
         dist.all_to_all_single(recv_e, torch.from_numpy(send_e),
                                output_split_sizes=rcounts.tolist(),
                                input_split_sizes=counts.tolist())
@@ -102,7 +111,8 @@ def _gloo_rank(rank, world, port, result):
         every = np.concatenate([g.numpy() for g in gathered])
         every = every[every >= 0]
         lo, hi = rank * E // world, (rank + 1) * E // world
-        got = recv_e.numpy()
+        got = recv_e.numpy().ravel()
+        got = got[got >= 0]
         ok = bool(np.all((got >= lo) & (got < hi)))
         ok = ok and np.bincount(got, minlength=E)[lo:hi].tolist() == \
             np.bincount(every, minlength=E)[lo:hi].tolist()
