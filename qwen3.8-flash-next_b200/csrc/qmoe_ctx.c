@@ -415,10 +415,11 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaMallocHost((void **)&c->x_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->idx_pin, (size_t)T * L->k * sizeof(int32_t)));
     if (c->ep_world > 1) {
-        /* a rank receives at most every rank's T tokens, once each */
+        /* the experts pass holds the own T tokens and at most T tokens from
+         * every rank */
         char msg[256] = {0};
-        c->prefill = qk_prefill_create(L, T * c->ep_world, c->pool, c->nslots + Lz, c->num_sms,
-                                       msg, sizeof(msg));
+        c->prefill = qk_prefill_create(L, T * (c->ep_world + 1), c->pool, c->nslots + Lz,
+                                       c->num_sms, msg, sizeof(msg));
         if (!c->prefill) {
             seterr(err, "qmoe_create: expert parallelism needs the grouped path: %s", msg);
             goto fail;
@@ -1313,9 +1314,10 @@ int qmoe_ep_connect(qmoe_ctx *c, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_
 /* One collective forward: every rank calls it for the same layer with its
  * own n tokens. Route locally; send each token once to every rank that owns
  * one of its experts (counts first, then fp16 rows, slot expert ids and
- * weights); run the grouped GEMMs on the rows received and combine each
- * row's local slots; send those partial rows back; add them (rank order)
- * and the shared expert of the local tokens. */
+ * weights); one grouped pass runs the shared expert on the own tokens and
+ * this rank's experts on the rows received, combining each received row's
+ * local slots; those partial rows go back; add them (rank order) and the
+ * shared expert's rows. */
 int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, float *out,
                     void *stream, qmoe_err *err) {
     if (err) err->msg[0] = 0;
@@ -1374,6 +1376,7 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
     const int *hc = c->ep_counts_pin, *hr = c->ep_counts_pin + W;
     size_t so[64], ro[64];
     size_t ns = 0, nr = 0;
+    const size_t own = (size_t)n; /* received rows follow the own tokens */
     for (int p = 0; p < W; p++) {
         so[p] = ns;
         ro[p] = nr;
@@ -1397,17 +1400,18 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
                 "qmoe_forward_ep dispatch");
         }
         if (rc) {
-            NCK(nc->recv((uint16_t *)b.recv_x + ro[p] * d, rc * d, ncclFloat16, p, c->ep_comm, st),
+            NCK(nc->recv((uint16_t *)b.recv_x + (own + ro[p]) * d, rc * d, ncclFloat16, p,
+                         c->ep_comm, st), "qmoe_forward_ep dispatch");
+            NCK(nc->recv(b.recv_e + (own + ro[p]) * k, rc * k, ncclInt32, p, c->ep_comm, st),
                 "qmoe_forward_ep dispatch");
-            NCK(nc->recv(b.recv_e + ro[p] * k, rc * k, ncclInt32, p, c->ep_comm, st),
-                "qmoe_forward_ep dispatch");
-            NCK(nc->recv(b.recv_w + ro[p] * k, rc * k, ncclFloat32, p, c->ep_comm, st),
+            NCK(nc->recv(b.recv_w + (own + ro[p]) * k, rc * k, ncclFloat32, p, c->ep_comm, st),
                 "qmoe_forward_ep dispatch");
         }
     }
     NCK(nc->group_end(), "qmoe_forward_ep");
     /* this rank's experts over the rows it received, combined per row */
-    if (kerr(qk_ep_experts(c->prefill, &f, (int)nr, st), "ep experts", err)) return -1;
+    if (kerr(qk_ep_experts(c->prefill, &f, (int)nr, c->nslots + layer, st), "ep experts", err))
+        return -1;
     /* partial rows back to the ranks that own the tokens */
     NCK(nc->group_start(), "qmoe_forward_ep");
     for (int p = 0; p < W; p++) {
@@ -1419,8 +1423,7 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
                 "qmoe_forward_ep combine");
     }
     NCK(nc->group_end(), "qmoe_forward_ep");
-    if (n > 0 && kerr(qk_ep_finish(c->prefill, &f, c->nslots + layer, st), "ep finish", err))
-        return -1;
+    if (n > 0 && kerr(qk_ep_finish(c->prefill, &f, st), "ep finish", err)) return -1;
     return 0;
 }
 

@@ -134,12 +134,15 @@ int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream, vo
  * that rank combines its slots' outputs with the routing weights, and one
  * fp32 partial row per (token, rank) comes back:
  *   qk_ep_alloc     buffers for T tokens per rank and G ranks
- *   qk_ep_dispatch  after routing: counts[G] rows per destination (device)
- *                   and the send rows grouped by destination, token order
- *   qk_ep_experts   grouped GEMMs over `rows` received rows and the
- *                   expert-side combine into one partial row each
- *   qk_ep_finish    the shared expert over this rank's tokens and the sum
- *                   of the returned partials (rank order) into out
+ *   qk_ep_dispatch  after routing: counts[G] rows per destination (device),
+ *                   the send rows grouped by destination (token order), and
+ *                   the own tokens as the leading rows of the receive buffer
+ *   qk_ep_experts   one grouped pass: the own tokens through the shared
+ *                   expert, the `rows` received rows through this rank's
+ *                   experts, then the expert-side combine into one partial
+ *                   row each
+ *   qk_ep_finish    the sum of the returned partials (rank order) and the
+ *                   shared expert into out
  * The transfers between them are the caller's (NCCL send/recv on the
  * buffers of qk_ep_buffers). */
 typedef struct {
@@ -151,8 +154,8 @@ typedef struct {
 int qk_ep_alloc(qk_prefill *p, int T, int G);
 void qk_ep_buffers(qk_prefill *p, qk_ep_bufs *b);
 int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int *counts, void *stream);
-int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, void *stream);
-int qk_ep_finish(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream);
+int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, int shared_slot_index, void *stream);
+int qk_ep_finish(qk_prefill *p, const qk_fwd *f, void *stream);
 
 /* internal cache helper: replace the value of an existing key */
 struct qmoe_cache;

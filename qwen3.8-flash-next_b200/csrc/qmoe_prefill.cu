@@ -693,6 +693,37 @@ __global__ void k_ep_pack(const void *x, int x_bf16, int d, int T, int k, int e_
     }
 }
 
+// The rank's own tokens as the leading rows of the receive buffer: fp16 x
+// (natural order), no routed slots (the experts pass gives them only the
+// shared expert).
+__global__ void k_ep_own(const void *x, int x_bf16, int d, int T, int k, __half *recv_x,
+                         int32_t *recv_e) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= T) return;
+    if (lane < k) recv_e[static_cast<size_t>(t) * k + lane] = -1;
+    __half *dst = recv_x + static_cast<size_t>(t) * d;
+    for (int c = lane; c < d / 8; c += 32) {
+        float v[8];
+        if (x_bf16) {
+            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
+                                                            static_cast<size_t>(t) * d)[c];
+            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
+            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
+        } else {
+            const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
+                                                               static_cast<size_t>(t) * d) + 2 * c;
+            const float4 u = q[0], w = q[1];
+            v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
+        }
+        uint4 o;
+        o.x = h2u(__floats2half2_rn(v[0], v[1]));
+        o.y = h2u(__floats2half2_rn(v[2], v[3]));
+        o.z = h2u(__floats2half2_rn(v[4], v[5]));
+        o.w = h2u(__floats2half2_rn(v[6], v[7]));
+        reinterpret_cast<uint4 *>(dst)[c] = o;
+    }
+}
+
 // Expert-side combine of the received rows: part[r] = sum over the row's
 // local slots (expert id >= 0) of w * Y[inv[r, s]], in slot order.
 __global__ void k_ep_partial(const float *Y, const int *inv, const int32_t *e_of, const float *w,
@@ -1185,16 +1216,15 @@ namespace {
 
 // Grouping, gather and the two grouped GEMMs for T "tokens" (rows of x) with
 // k routed slots each (idx [T, k], global expert ids with a slot in
-// slot_of), plus the shared expert over all T rows when with_shared. Leaves
-// the down outputs in p->Y (shared rows first) and the row of each
+// slot_of; -1 for none), plus the shared expert over the first nsh rows.
+// Leaves the down outputs in p->Y (shared rows first) and the row of each
 // (token, slot) in p->inv. events: NULL or 3 events (after grouping+gather,
 // gate/up, down).
 cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32_t *idx, int k,
-                    int with_shared, const int32_t *slot_of, int shared_slot_index, int *err,
+                    int nsh, const int32_t *slot_of, int shared_slot_index, int *err,
                     cudaStream_t st, void **events) {
     const qk_layout &L = p->L;
     const int E = L.E;
-    const int nsh = with_shared ? T : 0;
     const int nk = T * k;
     const int rows = nsh + nk;
     if (rows > p->rows_max || nk > p->max_tokens * L.k) return cudaErrorInvalidValue;
@@ -1265,7 +1295,7 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     if (T > p->max_tokens) return cudaErrorInvalidValue;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // diagnostics: events[0..3] bracket grouping+gather, gate/up, down, combine
-    cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, k, 1, f->slot_of,
+    cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, k, T, f->slot_of,
                             shared_slot_index, f->err, st, events);
     if (e != cudaSuccess) return e;
     k_combine<<<T, 256, 0, st>>>(p->Y, p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
@@ -1276,18 +1306,19 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
 extern "C" int qk_ep_alloc(qk_prefill *p, int T, int G) {
     const qk_layout &L = p->L;
     const size_t rows = static_cast<size_t>(T) * G;  // both directions: at most T per pair
-    if (G > 64 || rows > static_cast<size_t>(p->max_tokens)) return cudaErrorInvalidValue;
+    // the receive side holds the own T tokens first, then up to T per rank
+    if (G > 64 || rows + T > static_cast<size_t>(p->max_tokens)) return cudaErrorInvalidValue;
     p->ep_T = T;
     p->ep_G = G;
     const size_t d = static_cast<size_t>(L.d), k = static_cast<size_t>(L.k);
     cudaError_t e = cudaMalloc(&p->ep_mask, sizeof(unsigned long long) * T);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_pos, sizeof(int) * rows);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_e, sizeof(int32_t) * rows * k);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_e, sizeof(int32_t) * rows * k);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_e, sizeof(int32_t) * (rows + T) * k);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_w, sizeof(float) * rows * k);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_w, sizeof(float) * rows * k);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_w, sizeof(float) * (rows + T) * k);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_x, sizeof(__half) * rows * d);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_x, sizeof(__half) * rows * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_x, sizeof(__half) * (rows + T) * d);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_ret, sizeof(float) * rows * d);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_back, sizeof(float) * rows * d);
     return e;
@@ -1318,31 +1349,39 @@ extern "C" int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int *counts, void 
         k_ep_pack<<<(G * T * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, L.k, e_per, G,
                                                            f->idx, f->wts, p->ep_pos, p->ep_send_x,
                                                            p->ep_send_e, p->ep_send_w);
+        // this rank's own tokens lead the receive buffer (shared expert only)
+        k_ep_own<<<(T * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, L.k, p->ep_recv_x,
+                                                       p->ep_recv_e);
     }
     return cudaGetLastError();
 }
 
-extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, void *stream) {
+extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, int shared_slot_index,
+                             void *stream) {
     const qk_layout &L = p->L;
+    const int T = f->T;
     if (rows > p->ep_T * p->ep_G) return cudaErrorInvalidValue;
-    if (rows == 0) return cudaSuccess;
+    if (rows + T == 0) return cudaSuccess;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = grouped(p, p->ep_recv_x, XK_F16, rows, p->ep_recv_e, L.k, 0, f->slot_of, 0,
-                            f->err, st, nullptr);
+    // one grouped pass: the own tokens through the shared expert (rows
+    // [0, T)), the received rows through this rank's experts
+    cudaError_t e = grouped(p, p->ep_recv_x, XK_F16, T + rows, p->ep_recv_e, L.k, T, f->slot_of,
+                            shared_slot_index, f->err, st, nullptr);
     if (e != cudaSuccess) return e;
-    k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv, p->ep_recv_e, p->ep_recv_w, L.k, L.d,
-                                       p->ep_ret);
+    if (rows > 0)
+        k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv + static_cast<size_t>(T) * L.k,
+                                           p->ep_recv_e + static_cast<size_t>(T) * L.k,
+                                           p->ep_recv_w + static_cast<size_t>(T) * L.k, L.k, L.d,
+                                           p->ep_ret);
     return cudaGetLastError();
 }
 
-extern "C" int qk_ep_finish(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream) {
+extern "C" int qk_ep_finish(qk_prefill *p, const qk_fwd *f, void *stream) {
     const qk_layout &L = p->L;
     const int T = f->T;
     if (T == 0) return cudaSuccess;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, nullptr, 0, 1, f->slot_of,
-                            shared_slot_index, f->err, st, nullptr);
-    if (e != cudaSuccess) return e;
+    // the shared rows are Y[0, T) of the experts pass
     k_ep_final<<<T, 256, 0, st>>>(p->ep_back, p->ep_pos, T, p->ep_G, p->Y, f->sgate, L.d, f->out);
     return cudaGetLastError();
 }
