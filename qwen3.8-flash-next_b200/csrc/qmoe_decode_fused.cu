@@ -122,6 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     __shared__ int s_cnt;
     __shared__ unsigned long long s_base;
     __shared__ double s_rpart[kWarps][32];  // router: per-warp partial sums
+    __shared__ const uint8_t *s_slotp[32];  // slot of each routed expert
     __shared__ __align__(16) int32_t s_slots[1024];  // this layer's expert -> slot table
     __shared__ uint32_t s_keys[1024];                // staged top-k keys
 
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         s_chunk0[n] = gr1 - gr0;
         s_nchunks = n;
     }
+    STAMP(24);
     pdl_wait();
     // Grid barriers: every launch adds 2G to the counter (each CTA arrives
     // twice), so it starts at a multiple of 2G; when this CTA reads it, at
@@ -351,46 +353,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
             if (slot >= 0) sp = f.pool + static_cast<size_t>(slot) * L.slot_bytes;
         }
         const bool resident = __all_sync(QK_FULL, lane >= k || sp != nullptr);
+        STAMP(25);
         const bool good = okk && resident && ok0;  // no copies in flight on error paths
         const int nch = s_nchunks;
-        const int ndown = or1 > or0 ? k : 0;
-        if (good) {
-            // expect_tx before any copy of that barrier is issued
-            if (lane < nch)
-                mbar_expect_tx(&bar[2 + lane],
-                               static_cast<uint32_t>((s_chunk0[lane + 1] - s_chunk0[lane]) * L.gu_row));
-            if (lane == 31) mbar_expect_tx(&bar[1], static_cast<uint32_t>(ndown * (or1 - or0) * L.d_row));
-        }
+        if (good && lane < nch)  // expect_tx before any copy of that barrier is issued
+            mbar_expect_tx(&bar[2 + lane],
+                           static_cast<uint32_t>((s_chunk0[lane + 1] - s_chunk0[lane]) * L.gu_row));
+        if (lane < k) s_slotp[lane] = sp;
         __syncwarp();
-        // slot pointers by shuffle (all lanes take part), then each lane issues
-        // its copies (at most 64: nch <= 12 chunks plus k <= 32 down copies)
-        const uint8_t *srcs[2];
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-            const int q = lane + 32 * h2;
-            int s = 0;
-            if (q < nch) s = (gr0 + s_chunk0[q]) / I;
-            else if (q < nch + ndown) s = q - nch;
-            srcs[h2] = reinterpret_cast<const uint8_t *>(
-                __shfl_sync(QK_FULL, reinterpret_cast<uintptr_t>(sp), s & 31));
-        }
-        if (good) {
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-                const int q = lane + 32 * h2;
-                if (q < nch) {
-                    const int lo = gr0 + s_chunk0[q], hi = gr0 + s_chunk0[q + 1];
-                    const int s = lo / I;
-                    bulk_load(sm_rgu + static_cast<size_t>(lo - gr0) * L.gu_row,
-                              srcs[h2] + static_cast<size_t>(lo - s * I) * L.gu_row,
-                              static_cast<uint32_t>((hi - lo) * L.gu_row), &bar[2 + q]);
-                } else if (q < nch + ndown) {
-                    const int s = q - nch;
-                    bulk_load(sm_down + static_cast<size_t>(s) * p.or_max * L.d_row,
-                              srcs[h2] + L.gu_bytes + static_cast<size_t>(or0) * L.d_row,
-                              static_cast<uint32_t>((or1 - or0) * L.d_row), &bar[1]);
-                }
-            }
+        STAMP(26);
+        // the routed gate/up rows: one bulk copy per chunk (nch <= 12); the
+        // down rows follow below as 16-byte asynchronous copies by every
+        // thread (a bulk copy costs tens of ns to issue)
+        const int s = lane < nch ? (gr0 + s_chunk0[lane]) / I : 0;
+        const uint8_t *src =
+            reinterpret_cast<const uint8_t *>(__shfl_sync(QK_FULL, reinterpret_cast<uintptr_t>(sp), s & 31));
+        if (good && lane < nch) {
+            const int lo = gr0 + s_chunk0[lane], hi = gr0 + s_chunk0[lane + 1];
+            bulk_load(sm_rgu + static_cast<size_t>(lo - gr0) * L.gu_row,
+                      src + static_cast<size_t>(lo - s * I) * L.gu_row,
+                      static_cast<uint32_t>((hi - lo) * L.gu_row), &bar[2 + lane]);
         }
         STAMP(14);
         if (lane == 0) {
@@ -417,6 +399,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     __syncthreads();
     STAMP(5);
     const bool live = s_ok != 0;
+    if (live) {
+        // this CTA's down rows of the k routed experts -> sm_down (expert s
+        // at s * or_max rows), 16 bytes per copy, spread over every thread
+        const int per = (or1 - or0) * (L.d_row / 16);
+        for (int i = tid; i < k * per; i += kThreads) {
+            const int s = i / per, rem = i - s * per;
+            cp_async16(sm_down + static_cast<size_t>(s) * p.or_max * L.d_row + 16 * static_cast<size_t>(rem),
+                       s_slotp[s] + L.gu_bytes + static_cast<size_t>(or0) * L.d_row + 16 * static_cast<size_t>(rem));
+        }
+        cp_async_commit();
+    }
     bool ok1 = true;
     if (live) {
         // routed rows, each after its chunk has landed
@@ -475,14 +468,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
             }
         }
     }
+    cp_async_wait_all();  // this thread's down-row copies (none when !live)
     __syncthreads();
     STAMP(10);
     if (!ok1) return;
-    if (!mbar_wait(&bar[1], 0)) {
-        if (tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
-        mbar_wait(&bar[1], 0);
-        return;
-    }
     STAMP(11);
     // tasks (expert s, row group) in expert-major order; warp w owns a
     // contiguous task range, so it reloads its h slice only when s changes

@@ -97,6 +97,15 @@ QK_DEV void tma_load_3d(void *dst, const void *tmap, int x, int y, int z, uint64
         : "memory");
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only); completion per
+// thread with cp_async_wait_all.
+QK_DEV void cp_async16(void *dst_smem, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst_smem)), "l"(src)
+                 : "memory");
+}
+QK_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+QK_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 QK_DEV void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
