@@ -5,8 +5,8 @@
 // After routing (router + top-k kernels in qmoe_kernels.cu):
 //   k_count      per-expert token counts                 (model.c:1321-1332)
 //   k_plan       row offsets of each expert group and the M-tile list
-//   k_positions  stable token -> row permutation per expert, in token order
-//                (model.c:1354-1367 gathers the same rows)
+//   k_place      token -> row permutation per expert (warp-aggregated
+//                atomics; model.c:1354-1367 gathers the same rows)
 //   k_gather     x rows -> fp16 A operand, grouped by expert; the shared
 //                expert's group is every token in order
 //   k_gemm<GU>   H = SiLU(X_e Wg_e^T) * (X_e Wu_e^T)           (model.c:1371-1374)
@@ -429,10 +429,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // routing -> groups
 
-// Slots with a negative expert id (owned by another rank) are skipped.
+// Slots with a negative expert id (owned by another rank) are skipped. Lanes
+// of a warp with the same expert add together (one atomic per expert per
+// warp: hot experts would otherwise serialise on one counter).
 __global__ void k_count(const int32_t *idx, int nk, int *counts) {
-    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < nk; a += gridDim.x * blockDim.x)
-        if (idx[a] >= 0) atomicAdd(counts + idx[a], 1);
+    const int lane = threadIdx.x & 31;
+    for (int a0 = blockIdx.x * blockDim.x; a0 < nk; a0 += gridDim.x * blockDim.x) {
+        const int a = a0 + threadIdx.x;
+        const int e = a < nk ? idx[a] : -1;
+        const unsigned same = __match_any_sync(QK_FULL, e);
+        if (e >= 0 && lane == __ffs(same) - 1) atomicAdd(counts + e, __popc(same));
+    }
 }
 
 // One CTA (1024 threads, E + 1 <= 1024 groups). Group 0 is the shared expert
@@ -474,41 +481,26 @@ __global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh
     }
 }
 
-// One CTA per routed expert: its (token, slot) assignments in token order
-// get consecutive rows (a stable, deterministic permutation).
-__global__ void __launch_bounds__(1024) k_positions(const int32_t *idx, int nk, int k,
-                                                    const int *row0, int *inv, int *perm_tok) {
-    __shared__ int s_warp[32];
-    __shared__ int s_base;
-    const int e = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) s_base = row0[e];
-    __syncthreads();
-    for (int a0 = 0; a0 < nk; a0 += 1024) {
+// Row of each (token, slot) within its expert's group: row0[e] plus a place
+// taken from the expert's cursor (warp-aggregated atomics). The order of the
+// rows inside a group varies from call to call, the results do not: every
+// row's products and sums are the same wherever the row sits in a tile.
+__global__ void k_place(const int32_t *idx, int nk, int k, const int *row0, int *cursor, int *inv,
+                        int *perm_tok) {
+    const int lane = threadIdx.x & 31;
+    for (int a0 = blockIdx.x * blockDim.x; a0 < nk; a0 += gridDim.x * blockDim.x) {
         const int a = a0 + threadIdx.x;
-        const bool mine = a < nk && idx[a] == e;
-        const unsigned m = __ballot_sync(QK_FULL, mine);
-        if (lane == 0) s_warp[warp] = __popc(m);
-        __syncthreads();
-        if (warp == 0) {
-            int v = s_warp[lane];
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const int t = __shfl_up_sync(QK_FULL, v, off);
-                if (lane >= off) v += t;
-            }
-            s_warp[lane] = v;  // inclusive
-        }
-        __syncthreads();
-        const int before = (warp ? s_warp[warp - 1] : 0) + __popc(m & ((1u << lane) - 1u));
-        if (mine) {
-            const int pos = s_base + before;
+        const int e = a < nk ? idx[a] : -1;
+        const unsigned same = __match_any_sync(QK_FULL, e);
+        const int leader = __ffs(same) - 1;
+        int base = 0;
+        if (e >= 0 && lane == leader) base = atomicAdd(cursor + e, __popc(same));
+        base = __shfl_sync(QK_FULL, base, leader);
+        if (e >= 0) {
+            const int pos = row0[e] + base + __popc(same & ((1u << lane) - 1u));
             inv[a] = pos;
             perm_tok[pos] = a / k;
         }
-        __syncthreads();
-        if (threadIdx.x == 0) s_base += s_warp[31];
-        __syncthreads();
     }
 }
 
@@ -797,7 +789,7 @@ __global__ void k_ep_final(const float *back, const int *pos, int T, int G, cons
 // whose candidate set exceeds 32, or with a non-finite value, gets every
 // logit exactly instead (the one-warp path of k_topk).
 
-constexpr int kRW = 4;  // tokens (warps) per CTA of k_route_exact
+constexpr int kRW = 4;  // warps per token (CTA) of k_route_exact
 
 __global__ void k_route_split(const void *x, int x_bf16, int d, int T, int Tpad,
                               __nv_bfloat16 *xr, float *xnorm, MTile *tiles, int *n_mtiles) {
@@ -912,22 +904,24 @@ QK_DEV float exact_logit(const RouteArgs &a, const double2 *xs, int e, int lane)
     return v;
 }
 
-// One warp per token; dynamic shared memory: kRW x (x staged as d doubles,
-// then E keys).
+// One CTA of kRW warps per token; dynamic shared memory: x staged as d
+// doubles, then E keys. Warp 0 finds the candidate set; the candidates'
+// canonical logits are spread over the warps (each dot is a chain of L2
+// loads, so several in flight per token matter); warp 0 ranks them.
 __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
     extern __shared__ __align__(16) float rsm[];
-    __shared__ uint32_t s_key_all[kRW][32];
-    __shared__ int s_idx_all[kRW][32];
-    __shared__ float s_ev_all[kRW][32];
+    __shared__ uint32_t s_key[32];
+    __shared__ int s_idx[32];
+    __shared__ float s_ev[32];
+    __shared__ float s_wmax[kRW];
+    __shared__ int s_C, s_fast, s_fin;
+    __shared__ float s_sg;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * kRW + warp;
-    if (t >= a.T) return;
+    const int t = blockIdx.x;
     const int d = a.d, E = a.E, k = a.k, nE = (E + 31) / 32 * 32;
-    double2 *xs = reinterpret_cast<double2 *>(rsm) + static_cast<size_t>(warp) * (d / 2);
-    uint32_t *keys = reinterpret_cast<uint32_t *>(rsm + static_cast<size_t>(kRW) * d * 2) + warp * nE;
-    uint32_t *s_key = s_key_all[warp];
-    int *s_idx = s_idx_all[warp];
-    for (int c = lane; c < d / 8; c += 32) {
+    double2 *xs = reinterpret_cast<double2 *>(rsm);
+    uint32_t *keys = reinterpret_cast<uint32_t *>(rsm + static_cast<size_t>(d) * 2);
+    for (int c = threadIdx.x; c < d / 8; c += kRW * 32) {
         float v[8];
         if (a.x_bf16) {
             const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.x) +
@@ -946,7 +940,7 @@ __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
     const float *lr = a.lga + static_cast<size_t>(t) * E;
     bool finite = isfinite(a.xnorm[t]);
     float maxabs = 0.f;
-    for (int e = lane; e < nE; e += 32) {
+    for (int e = threadIdx.x; e < nE; e += kRW * 32) {
         uint32_t key = 0u;
         if (e < E) {
             float v = lr[e];
@@ -957,65 +951,78 @@ __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
         }
         keys[e] = key;
     }
-    finite = __all_sync(QK_FULL, finite);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) maxabs = fmaxf(maxabs, __shfl_xor_sync(QK_FULL, maxabs, off));
-    __syncwarp();
-    bool fast = finite;
-    int C = 0;
-    if (fast) {
-        const float vk = key_value(kth_key(keys, E, k, s_key));
-        const float beta = __fmaf_ru(__fmul_ru(0x1p-10f, a.xnorm[t]), a.wmax, __fmul_ru(0x1p-20f, maxabs));
-        const uint32_t tk = fkey(__fsub_rd(vk, __fmul_ru(3.0f, beta)));
-        int own = 0;
-        for (int e = lane; e < E; e += 32) own += keys[e] >= tk ? 1 : 0;
-        int incl = own;
+    if (lane == 0) s_wmax[warp] = maxabs;
+    finite = __syncthreads_and(finite) != 0;
+    if (warp == 0) {
+        float m = lane < kRW ? s_wmax[lane] : 0.f;
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int u = __shfl_up_sync(QK_FULL, incl, off);
-            if (lane >= off) incl += u;
-        }
-        C = __shfl_sync(QK_FULL, incl, 31);
-        fast = C >= k && C <= 32;
+        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(QK_FULL, m, off));
+        bool fast = finite;
+        int C = 0;
         if (fast) {
-            int pos = incl - own;
-            for (int e = lane; e < E; e += 32)
-                if (keys[e] >= tk) s_idx[pos++] = e;
+            const float vk = key_value(kth_key(keys, E, k, s_key));
+            const float beta = __fmaf_ru(__fmul_ru(0x1p-10f, a.xnorm[t]), a.wmax, __fmul_ru(0x1p-20f, m));
+            const uint32_t tk = fkey(__fsub_rd(vk, __fmul_ru(3.0f, beta)));
+            int own = 0;
+            for (int e = lane; e < E; e += 32) own += keys[e] >= tk ? 1 : 0;
+            int incl = own;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int u = __shfl_up_sync(QK_FULL, incl, off);
+                if (lane >= off) incl += u;
+            }
+            C = __shfl_sync(QK_FULL, incl, 31);
+            fast = C >= k && C <= 32;
+            if (fast) {
+                int pos = incl - own;
+                for (int e = lane; e < E; e += 32)
+                    if (keys[e] >= tk) s_idx[pos++] = e;
+            }
         }
-        __syncwarp();
+        if (lane == 0) {
+            s_C = C;
+            s_fast = fast ? 1 : 0;
+            s_fin = 1;
+        }
     }
+    __syncthreads();
+    const bool fast = s_fast != 0;
+    const int C = s_C;
     if (fast) {
-        // exact logits of the candidates, canonical order; lane m keeps m's key
-        uint32_t mykey = 0u;
-        bool fin = true;
-        for (int m = 0; m < C; ++m) {
+        // exact logits of the candidates, canonical order, spread over warps
+        for (int m = warp; m < C; m += kRW) {
             const float v = exact_logit(a, xs, s_idx[m], lane);
-            fin = fin && isfinite(v);
-            if (lane == m) mykey = fkey(v);
-        }
-        fast = fin;
-        if (fast) {
-            if (lane < C) s_key[lane] = mykey;
-            __syncwarp();
-            topk_rank_softmax(C, k, s_key, s_idx, s_ev_all[warp], a.idx + static_cast<size_t>(t) * k,
-                              a.wts + static_cast<size_t>(t) * k);
+            if (lane == 0) {
+                s_key[m] = fkey(v);
+                if (!isfinite(v)) s_fin = 0;
+            }
         }
     }
-    if (!fast) {
+    if (warp == kRW - 1) {  // the shared gate, canonical order
+        const double sg = warp_sum_butterfly(router_lane(a.shared_gate, xs, d, lane));
+        if (lane == 0) s_sg = 1.0f / (1.0f + expf(-static_cast<float>(sg)));
+    }
+    __syncthreads();
+    if (fast && s_fin) {
+        if (warp == 0)
+            topk_rank_softmax(C, k, s_key, s_idx, s_ev, a.idx + static_cast<size_t>(t) * k,
+                              a.wts + static_cast<size_t>(t) * k);
+    } else {
         // every logit exactly (rare)
-        for (int e = 0; e < E; ++e) {
+        for (int e = warp; e < E; e += kRW) {
             const float v = exact_logit(a, xs, e, lane);
             if (lane == 0) keys[e] = fkey(v);
         }
-        __syncwarp();
-        if (!topk_warp(keys, E, k, s_key, s_idx, s_ev_all[warp], a.idx + static_cast<size_t>(t) * k,
-                       a.wts + static_cast<size_t>(t) * k)) {
+        __syncthreads();
+        if (warp == 0 && !topk_warp(keys, E, k, s_key, s_idx, s_ev, a.idx + static_cast<size_t>(t) * k,
+                                    a.wts + static_cast<size_t>(t) * k)) {
             if (lane == 0) atomicOr(a.err, QK_ERR_BAD_ROUTE);
             return;
         }
     }
-    const double sg = warp_sum_butterfly(router_lane(a.shared_gate, xs, d, lane));
-    if (lane == 0) a.sgate[t] = 1.0f / (1.0f + expf(-static_cast<float>(sg)));
+    if (threadIdx.x == 0) a.sgate[t] = s_sg;
 }
 
 // ---------------------------------------------------------------------------
@@ -1071,7 +1078,7 @@ bool map_3d_u8(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t ro
 struct qk_prefill {
     qk_layout L;
     int max_tokens, num_sms, pool_slots, rows_max, tiles_max;
-    int *counts, *row0, *inv, *perm_tok, *n_mtiles, *n_rows;
+    int *counts, *cursor, *row0, *inv, *perm_tok, *n_mtiles, *n_rows;
     MTile *tiles;
     __half *xp, *H;
     float *Y;
@@ -1097,7 +1104,7 @@ struct qk_prefill {
 
 extern "C" void qk_prefill_destroy(qk_prefill *p) {
     if (!p) return;
-    cudaFree(p->counts);
+    cudaFree(p->counts);  // cursor lives in the same allocation
     cudaFree(p->row0);
     cudaFree(p->inv);
     cudaFree(p->perm_tok);
@@ -1146,7 +1153,8 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     p->tiles_max = p->rows_max / BM + L->E + 2;
     const size_t R = static_cast<size_t>(p->rows_max);
     cudaError_t e = cudaSuccess;
-    if (e == cudaSuccess) e = cudaMalloc(&p->counts, sizeof(int) * (L->E + 1));
+    if (e == cudaSuccess) e = cudaMalloc(&p->counts, sizeof(int) * 2 * (L->E + 1));
+    if (e == cudaSuccess) p->cursor = p->counts + (L->E + 1);
     if (e == cudaSuccess) e = cudaMalloc(&p->row0, sizeof(int) * (L->E + 1));
     if (e == cudaSuccess) e = cudaMalloc(&p->inv, sizeof(int) * static_cast<size_t>(max_tokens) * L->k);
     if (e == cudaSuccess) e = cudaMalloc(&p->perm_tok, sizeof(int) * R);
@@ -1178,7 +1186,7 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     // chunks; router rows past E read as zeros), the shapes' workspace
     const int nE = (L->E + 31) / 32 * 32;
     p->Tpad = (max_tokens + BM - 1) / BM * BM;
-    p->route_smem = static_cast<size_t>(kRW) * (2 * static_cast<size_t>(L->d) + nE) * 4;
+    p->route_smem = (2 * static_cast<size_t>(L->d) + nE) * 4;
     p->route_ok = L->E % 16 == 0 && L->k <= 32 && p->route_smem <= 200 * 1024;
     if (p->route_ok) {
         const size_t Tp = static_cast<size_t>(p->Tpad);
@@ -1232,12 +1240,15 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         if (events) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), st,
                                              cudaEventRecordExternal);
     };
-    cudaError_t e = cudaMemsetAsync(p->counts, 0, sizeof(int) * (E + 1), st);
+    // counts and cursors in one allocation, cleared together
+    cudaError_t e = cudaMemsetAsync(p->counts, 0, sizeof(int) * 2 * (E + 1), st);
     if (e != cudaSuccess) return e;
     if (nk > 0) k_count<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, p->counts);
     k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index, p->row0, p->tiles,
                                p->n_mtiles, p->n_rows);
-    if (nk > 0) k_positions<<<E, 1024, 0, st>>>(idx, nk, k, p->row0, p->inv, p->perm_tok);
+    if (nk > 0)
+        k_place<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, k, p->row0, p->cursor, p->inv,
+                                                 p->perm_tok);
     if (rows > 0)
         k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->n_rows,
                                                          p->perm_tok, p->xp);
@@ -1439,6 +1450,6 @@ extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void 
     a.wts = f->wts;
     a.sgate = f->sgate;
     a.err = f->err;
-    k_route_exact<<<(T + kRW - 1) / kRW, kRW * 32, p->route_smem, st>>>(a);
+    k_route_exact<<<T, kRW * 32, p->route_smem, st>>>(a);
     return cudaGetLastError();
 }
