@@ -326,6 +326,113 @@ def measure_prefill_ep(rank, world, local, reps=5, warmup=2):
             "exchange": "NCCL send/recv all-to-all of fp16 rows and fp32 outputs"}
 
 
+STACK_L, STACK_T, STACK_SEED = 76, 64, 20261203
+SLOT = 1769472
+
+
+def measure_stack(rank, world, local, layers=STACK_L, reps=3, warmup=2):
+    """the 76-layer MoE-only stack (h <- h + MoE_l(RMSNorm(h)),
+    eps 1e-6), decode at batch 64, every layer with its own seeded router and
+    experts (generated on the device: 68.9 GB of experts at one GPU). With
+    world > 1 the ranks are expert-parallel (rank g owns experts
+    [g E/W, (g+1) E/W) of every layer, 64/W tokens each, NCCL exchange inside
+    the library). One step = the whole stack for the 64 tokens, captured as
+    one CUDA graph per rank (inputs reset from a resident copy inside the
+    graph); time = CUDA events per rank, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import qmoe
+    T_per = STACK_T // world
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, layers=layers, max_tokens=T_per, device=local,
+                           ep_rank=rank if world > 1 else 0, ep_world=world if world > 1 else 0)
+    ctx = qmoe.Context(cfg)
+    t0 = time.perf_counter()
+    for l in range(layers):
+        ctx.synth_layer_dev(l, STACK_SEED)
+    ctx.sync()
+    synth_s = time.perf_counter() - t0
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(qmoe.ep_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        ctx.ep_connect(bytes(uid.cpu().numpy().tobytes()))
+    h0 = torch.from_numpy(qmoe.synth_tokens(STACK_SEED, 100 + rank, T_per, D)).cuda()
+    h = h0.clone()
+    st = torch.cuda.Stream()
+    cs = st.cuda_stream
+    torch.cuda.synchronize()
+    # census pass, layer by layer: the distinct experts each layer touches
+    # (over all ranks' tokens), for the algorithmic bytes of a step
+    lo, hi = rank * E // world, (rank + 1) * E // world
+    touched = []
+    for l in range(layers):
+        ctx.forward_stack(l, l + 1, h.data_ptr(), T_per, 1e-6, cs)
+        st.synchronize()
+        idx = torch.from_numpy(ctx.routing(T_per)[0]).cuda()
+        if world > 1:
+            parts = [torch.empty_like(idx) for _ in range(world)]
+            dist.all_gather(parts, idx)
+            idx = torch.cat(parts)
+        u = torch.unique(idx)
+        touched.append(int(((u >= lo) & (u < hi)).sum()))
+    h_eager = h.clone()
+    # one graph per rank for the whole step
+    ctx.capture_begin(cs)
+    with torch.cuda.stream(st):
+        h.copy_(h0)
+    ctx.forward_stack(0, layers, h.data_ptr(), T_per, 1e-6, cs)
+    g = ctx.capture_end(cs)
+    for _ in range(warmup):
+        g.launch(cs)
+    st.synchronize()
+    ctx.sync()
+    same = bool(torch.equal(h, h_eager))
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        g.launch(cs)
+    e1.record(st)
+    st.synchronize()
+    ctx.sync()
+    ms = e0.elapsed_time(e1) / reps
+    stats = torch.tensor([ms, float(sum(touched)), 0.0 if same else 1.0], device="cuda")
+    if world > 1:
+        mx = stats.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stats.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms, all_touched, bad = float(mx[0]), float(sm[1]), float(mx[2])
+    else:
+        all_touched, bad = float(stats[1]), float(stats[2])
+    g.close()
+    ctx.close()
+    # algorithmic bytes of one step, all ranks: every rank reads the router,
+    # shared gate and shared expert of every layer, and its own touched experts
+    per_layer_fixed = E * D * 2 + D * 2 + SLOT
+    step_bytes = world * layers * per_layer_fixed + all_touched * SLOT
+    hbm, _, src = peaks()
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    return {"workload": f"config3: {layers}-layer MoE-only stack, decode batch {STACK_T}, "
+                        "RMSNorm eps 1e-6 + residual",
+            "ranks": world, "parallelism": f"ep{world}" if world > 1 else "single GPU",
+            "tokens_per_s": STACK_T / (ms / 1e3), "ms_per_step": ms,
+            "tokens_per_step": STACK_T, "layers": layers,
+            "experts_touched_per_layer": all_touched / layers,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm * world, "unit": "GB/s",
+                         "frac": gbs / (hbm * world), "bytes_per_step": step_bytes,
+                         "peak_source": f"{src}, x{world} GPUs",
+                         "note": "router + shared expert + shared gate per layer per rank, "
+                                 "plus the distinct routed experts the step touches"},
+            "graph_equals_eager": bad == 0.0, "weights_generated_s": synth_s,
+            "timing": "one CUDA graph per rank per step, CUDA events, max over ranks",
+            "exchange": "NCCL send/recv, fixed-size blocks of fp16 rows and fp32 partials"
+                        if world > 1 else None}
+
+
 def run_eager(n):
     """Small case for ncu captures: n single-token forwards launched eagerly
     on the config-1 layer (906 MB of experts, larger than L2)."""
@@ -359,6 +466,9 @@ def main():
     ap.add_argument("--prefill-eager", type=int, default=0,
                     help="profiling case: run N eager 4096-token prefill calls and exit")
     ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] leg")
+    ap.add_argument("--no-stack", action="store_true", help="skip the configs[3] leg")
+    ap.add_argument("--stack-only", type=int, default=0,
+                    help="run only the configs[3] leg with this many layers and print it")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -368,6 +478,23 @@ def main():
         return
     if args.prefill_eager:
         run_prefill_eager(args.prefill_eager)
+        return
+    if args.stack_only:
+        import torch
+        import torch.distributed as dist
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        if world > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        r = measure_stack(rank, world, local, layers=args.stack_only)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return
 
     import torch
@@ -495,6 +622,10 @@ def main():
         if world > 1:
             prefill["expert_parallel"] = measure_prefill_ep(rank, world, local)
 
+    stack = None
+    if not args.no_stack:
+        stack = measure_stack(rank, world, local)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
@@ -529,6 +660,7 @@ def main():
             "clocks": clk,
             "parity_spot_check": parity_ok,
             "prefill": prefill,
+            "stack": stack,
         }
         print(json.dumps(line), flush=True)
     ctx.close()

@@ -134,6 +134,19 @@ int qmoe_forward_dev(qmoe_ctx *ctx, int layer, const void *x, int x_dtype,
 /* Waits for the context's work and reports any device-side error. */
 int qmoe_sync(qmoe_ctx *ctx, qmoe_err *err);
 
+/* MoE-only layer stack (the workload's 76-layer configuration; attention
+ * replaced by the identity): for l in [l0, l1)
+ *   h <- h + MoE_l(RMSNorm(h)),  RMSNorm unit weight, eps (1e-6 there),
+ * RMSNorm as kernel_rmsnorm (c/src/kernel.c:10-20). h: device fp32 [n, d],
+ * updated in place. Each layer is qmoe_forward_dev, or qmoe_forward_ep on an
+ * expert-parallel context (then collective: every rank calls it for the same
+ * layers). Enqueued on `stream` without any host synchronisation, so the
+ * whole stack can be captured in one CUDA graph. No reference counterpart:
+ * the reference calls moe_forward once per layer from model_forward
+ * (c/src/model.c:1712). */
+int qmoe_forward_stack(qmoe_ctx *ctx, int l0, int l1, float *h, int n, float eps,
+                       void *stream, qmoe_err *err);
+
 /* ---- one decode token without any allocation (no counterpart in the
  *      reference runtime) ----
  * For callers that cannot call cudaMalloc: code that must run inside a
@@ -192,8 +205,12 @@ int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream,
  * every rank that owns one of its experts; the owners' grouped GEMMs and a
  * weighted combine of each token's local slots; one fp32 partial row per
  * (token, rank) sent back; on the token's rank the partials (in rank order)
- * plus the shared expert. It waits for the row counts on the host once per
- * call. No reference counterpart: the C port runs on one device. */
+ * plus the shared expert. Transfers have a fixed size, max_tokens rows
+ * between every pair of ranks (token t in row t, rows of tokens not bound
+ * for a rank carrying expert ids -1), so the call never waits on the host
+ * and can be captured in a CUDA graph; size max_tokens to the tokens per
+ * rank actually used. No reference counterpart: the C port runs on one
+ * device. */
 #define QMOE_EP_ID_BYTES 128
 int qmoe_ep_unique_id(unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err);
 int qmoe_ep_connect(qmoe_ctx *ctx, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err);
@@ -203,9 +220,11 @@ int qmoe_forward_ep(qmoe_ctx *ctx, int layer, const void *x_dev, int x_dtype, in
  * device kernels: for the routing idx [n, k] of one rank, counts[g] = tokens
  * sent to rank g (of W <= 64, E % W == 0: those with at least one expert in
  * [g E/W, (g+1) E/W)) and, if pos is not NULL, pos[g * n + t] = the send
- * row of token t for rank g, or -1: rows grouped by destination rank, in
- * token order within a rank. Returns 0, or -1 on bad arguments. */
-int qmoe_ep_plan_host(const int32_t *idx, int n, int k, int E, int W, int *counts, int *pos);
+ * row of token t for rank g, g * cap + t, or -1 when t is not sent there
+ * (cap >= n: the rows per rank, max_tokens in qmoe_forward_ep). Returns 0,
+ * or -1 on bad arguments. */
+int qmoe_ep_plan_host(const int32_t *idx, int n, int k, int E, int W, int cap, int *counts,
+                      int *pos);
 
 /* Routing of the last forward call (waits for it): idx [n, k] in
  * (logit desc, expert asc) order, weights [n, k] (softmax renormalised over
@@ -314,6 +333,16 @@ void qmoe_synth_tokens(uint64_t seed, uint64_t stream, int n, int d, float *x);
 /* Zipf logit bias: bias[e] = -s * ln(1 + pi(e)) for a seeded permutation pi. */
 void qmoe_synth_zipf_bias(uint64_t seed, int layer, int E, double s,
                           float *bias);
+/* The same layer generated on the device straight into a context with every
+ * local expert resident: its experts (the rank's share on an
+ * expert-parallel context), shared expert, router, shared gate, and the Zipf
+ * bias when zipf_s > 0. For stacks too large to build on the host (76 layers
+ * of 512 experts: 68.9 GB). Nibble words equal the host streams bit for
+ * bit; the normals use the device's log and cos, which may differ from the
+ * host's in the last place, so a scale or router weight may differ from
+ * qmoe_synth_layer's by one bf16 unit in rare elements. */
+int qmoe_synth_layer_dev(qmoe_ctx *ctx, int layer, uint64_t seed, double zipf_s,
+                         qmoe_err *err);
 
 const char *qmoe_version(void);
 

@@ -89,8 +89,8 @@ struct qmoe_ctx {
     /* expert parallelism */
     int ep_world, ep_rank, ep_lo, ep_hi; /* experts [ep_lo, ep_hi) are local */
     ncclComm_t ep_comm;
-    int *ep_counts_dev;  /* [2 * W]: rows to each rank, rows from each rank */
-    int *ep_counts_pin;  /* pinned copy */
+    /* MoE-only stack: the normalised layer input and the layer output */
+    float *stk_xn, *stk_y; /* fp32 [max_tokens, d] each */
 };
 
 static int check_dev_err(qmoe_ctx *c, cudaStream_t st, qmoe_err *err);
@@ -257,6 +257,8 @@ void qmoe_destroy(qmoe_ctx *c) {
     cudaFree(c->wts);
     cudaFree(c->sgate);
     cudaFree(c->h);
+    cudaFree(c->stk_xn);
+    cudaFree(c->stk_y);
     cudaFreeHost(c->x_pin);
     cudaFreeHost(c->idx_pin);
     cudaFreeHost(c->io_pin);
@@ -271,8 +273,6 @@ void qmoe_destroy(qmoe_ctx *c) {
     if (c->cache) qmoe_cache_free(c->cache);
     qk_prefill_destroy(c->prefill);
     if (c->ep_comm) nccl_api()->comm_destroy(c->ep_comm);
-    cudaFree(c->ep_counts_dev);
-    cudaFreeHost(c->ep_counts_pin);
     if (c->copy_done) cudaEventDestroy(c->copy_done);
     for (int i = 0; i < 8; i++)
         if (c->pev[i]) cudaEventDestroy(c->pev[i]);
@@ -412,6 +412,8 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaMalloc((void **)&c->wts, (size_t)T * L->k * sizeof(float)));
     CK(cudaMalloc((void **)&c->sgate, (size_t)T * sizeof(float)));
     CK(cudaMalloc((void **)&c->h, (size_t)T * (L->k + 1) * L->I * sizeof(float)));
+    CK(cudaMalloc((void **)&c->stk_xn, (size_t)T * L->d * sizeof(float)));
+    CK(cudaMalloc((void **)&c->stk_y, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->x_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->idx_pin, (size_t)T * L->k * sizeof(int32_t)));
     if (c->ep_world > 1) {
@@ -425,8 +427,6 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
             goto fail;
         }
         CK((cudaError_t)qk_ep_alloc(c->prefill, T, c->ep_world));
-        CK(cudaMalloc((void **)&c->ep_counts_dev, 2 * sizeof(int) * c->ep_world));
-        CK(cudaMallocHost((void **)&c->ep_counts_pin, 2 * sizeof(int) * c->ep_world));
     } else if (T > 1) {
         char msg[256] = {0};
         c->prefill = qk_prefill_create(L, T, c->pool, c->nslots + Lz, c->num_sms, msg, sizeof(msg));
@@ -689,6 +689,90 @@ int qmoe_upload_layer(qmoe_ctx *c, int layer, const qmoe_layer_weights *w, qmoe_
     return 0;
 fail:
     if (stage) cudaFreeHost(stage);
+    return -1;
+}
+
+/* The seeded synthetic layer of qmoe_synth_layer, generated on the device
+ * straight into the pool (the local experts), the shared slot, the router
+ * and the shared gate; the Zipf bias (zipf_s > 0) is made on the host. */
+int qmoe_synth_layer_dev(qmoe_ctx *c, int layer, uint64_t seed, double zipf_s, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || layer < 0 || layer >= c->cfg.num_layers) {
+        seterr(err, "qmoe_synth_layer_dev: bad arguments (layer %d)", layer);
+        return -1;
+    }
+    if (!c->resident_all) {
+        seterr(err, "qmoe_synth_layer_dev: needs every local expert resident (pool_bytes = 0); "
+                    "streaming contexts take host layers (qmoe_upload_layer)");
+        return -1;
+    }
+    const qk_layout *L = &c->L;
+    layer_dev *ld = &c->layers[layer];
+    cudaStream_t st = c->copy_stream;
+    uint16_t *router_host = NULL;
+    float *bias_host = NULL;
+    const uint64_t Ly = (uint64_t)layer;
+    const uint64_t rk[6] = {qk_stream_key(seed, Ly, QK_T_GQ), qk_stream_key(seed, Ly, QK_T_GS),
+                            qk_stream_key(seed, Ly, QK_T_UQ), qk_stream_key(seed, Ly, QK_T_US),
+                            qk_stream_key(seed, Ly, QK_T_DQ), qk_stream_key(seed, Ly, QK_T_DS)};
+    const uint64_t sk[6] = {qk_stream_key(seed, Ly, QK_T_SGQ), qk_stream_key(seed, Ly, QK_T_SGS),
+                            qk_stream_key(seed, Ly, QK_T_SUQ), qk_stream_key(seed, Ly, QK_T_SUS),
+                            qk_stream_key(seed, Ly, QK_T_SDQ), qk_stream_key(seed, Ly, QK_T_SDS)};
+    if (ld->tok_graph) { /* it holds this layer's old pointers */
+        cudaGraphExecDestroy(ld->tok_graph);
+        ld->tok_graph = NULL;
+    }
+    ld->ready = 0;
+    CK(cudaSetDevice(c->cfg.device));
+    CK(cudaStreamSynchronize(c->stream));
+    if (!ld->router) CK(cudaMalloc((void **)&ld->router, (size_t)L->E * L->d * 2));
+    if (!ld->shgate) CK(cudaMalloc((void **)&ld->shgate, (size_t)L->d * 2));
+    CK((cudaError_t)qk_synth_bf16_normal(ld->router, (size_t)L->E * L->d,
+                                         qk_stream_key(seed, Ly, QK_T_ROUTER), st));
+    CK((cudaError_t)qk_synth_bf16_normal(ld->shgate, (size_t)L->d,
+                                         qk_stream_key(seed, Ly, QK_T_SHGATE), st));
+    CK((cudaError_t)qk_synth_slot(L, ld->shared_slot, 0, sk, st));
+    for (int e = c->ep_lo; e < c->ep_hi; e++) {
+        pthread_mutex_lock(&c->lock);
+        int slot = c->slot_of_host[(size_t)layer * L->E + e];
+        if (slot < 0) slot = claim_slot(c, layer, e, 0);
+        pthread_mutex_unlock(&c->lock);
+        if (slot < 0) {
+            seterr(err, "qmoe_synth_layer_dev: pool bookkeeping failed");
+            goto fail;
+        }
+        CK((cudaError_t)qk_synth_slot(L, c->pool + (size_t)slot * L->slot_bytes, e, rk, st));
+    }
+    if (zipf_s > 0) {
+        bias_host = malloc((size_t)L->E * sizeof(float));
+        if (!bias_host) {
+            seterr(err, "qmoe_synth_layer_dev: out of host memory");
+            goto fail;
+        }
+        qmoe_synth_zipf_bias(seed, layer, L->E, zipf_s, bias_host);
+        if (!ld->bias) CK(cudaMalloc((void **)&ld->bias, (size_t)L->E * sizeof(float)));
+        CK(cudaMemcpy(ld->bias, bias_host, (size_t)L->E * sizeof(float), cudaMemcpyHostToDevice));
+    } else if (ld->bias) {
+        cudaFree(ld->bias);
+        ld->bias = NULL;
+    }
+    router_host = malloc((size_t)L->E * L->d * 2);
+    if (!router_host) {
+        seterr(err, "qmoe_synth_layer_dev: out of host memory");
+        goto fail;
+    }
+    CK(cudaMemcpyAsync(router_host, ld->router, (size_t)L->E * L->d * 2, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    ld->router_wmax = router_wmax(router_host, L->E, L->d);
+    CK(cudaMemcpy(c->slot_of_dev + (size_t)layer * L->E, c->slot_of_host + (size_t)layer * L->E,
+                  (size_t)L->E * sizeof(int32_t), cudaMemcpyHostToDevice));
+    free(router_host);
+    free(bias_host);
+    ld->ready = 1;
+    return 0;
+fail:
+    free(router_host);
+    free(bias_host);
     return -1;
 }
 
@@ -1312,12 +1396,13 @@ int qmoe_ep_connect(qmoe_ctx *c, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_
 }
 
 /* One collective forward: every rank calls it for the same layer with its
- * own n tokens. Route locally; send each token once to every rank that owns
- * one of its experts (counts first, then fp16 rows, slot expert ids and
- * weights); one grouped pass runs the shared expert on the own tokens and
- * this rank's experts on the rows received, combining each received row's
- * local slots; those partial rows go back; add them (rank order) and the
- * shared expert's rows. */
+ * own n tokens. Route locally; send every rank a block of max_tokens rows in
+ * which row t is token t when that rank owns one of its experts (fp16 x,
+ * slot expert ids and weights) and a row of expert ids -1 otherwise; one
+ * grouped pass runs the shared expert on the own tokens and this rank's
+ * experts on the rows received, combining each received row's local slots;
+ * those partial rows go back; add them (rank order) and the shared expert's
+ * rows. No host synchronisation: the call can be captured in a graph. */
 int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, float *out,
                     void *stream, qmoe_err *err) {
     if (err) err->msg[0] = 0;
@@ -1340,6 +1425,7 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
     }
     const nccl_fns *nc = nccl_api();
     const int W = c->ep_world, d = c->L.d, k = c->L.k;
+    const size_t cap = (size_t)c->cfg.max_tokens;
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
     if (cudaSetDevice(c->cfg.device) != cudaSuccess) {
         seterr(err, "qmoe_forward_ep: cudaSetDevice failed");
@@ -1349,111 +1435,93 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
     fill_fwd(c, layer, x, x_dtype == QMOE_BF16, n, out, &f);
     c->last_T = n;
     c->stats.prefill_calls++;
-    int *cnt = c->ep_counts_dev, *rcnt = c->ep_counts_dev + W;
     qk_ep_bufs b;
     qk_ep_buffers(c->prefill, &b);
-    if (n > 0) {
-        if (route(c, layer, &f, st, 0, NULL, err)) return -1;
-        if (kerr(qk_ep_dispatch(c->prefill, &f, cnt, st), "ep dispatch", err)) return -1;
-    } else if (cudaMemsetAsync(cnt, 0, sizeof(int) * W, st) != cudaSuccess) {
-        seterr(err, "qmoe_forward_ep: memset failed");
-        return -1;
-    }
-    /* row counts: to every rank, from every rank */
+    if (n > 0 && route(c, layer, &f, st, 0, NULL, err)) return -1;
+    if (kerr(qk_ep_dispatch(c->prefill, &f, st), "ep dispatch", err)) return -1;
+    /* token rows with their slots out, and in (after the own n tokens) */
+    const size_t own = (size_t)n;
     NCK(nc->group_start(), "qmoe_forward_ep");
     for (int p = 0; p < W; p++) {
-        NCK(nc->send(cnt + p, 1, ncclInt32, p, c->ep_comm, st), "qmoe_forward_ep counts");
-        NCK(nc->recv(rcnt + p, 1, ncclInt32, p, c->ep_comm, st), "qmoe_forward_ep counts");
-    }
-    NCK(nc->group_end(), "qmoe_forward_ep");
-    cudaError_t ce = cudaMemcpyAsync(c->ep_counts_pin, c->ep_counts_dev, 2 * sizeof(int) * W,
-                                     cudaMemcpyDeviceToHost, st);
-    if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
-    if (ce != cudaSuccess) {
-        seterr(err, "qmoe_forward_ep: %s", cudaGetErrorString(ce));
-        return -1;
-    }
-    const int *hc = c->ep_counts_pin, *hr = c->ep_counts_pin + W;
-    size_t so[64], ro[64];
-    size_t ns = 0, nr = 0;
-    const size_t own = (size_t)n; /* received rows follow the own tokens */
-    for (int p = 0; p < W; p++) {
-        so[p] = ns;
-        ro[p] = nr;
-        ns += (size_t)hc[p];
-        nr += (size_t)hr[p];
-    }
-    if (nr > (size_t)c->cfg.max_tokens * W) {
-        seterr(err, "qmoe_forward_ep: %zu rows received, more than the plan holds", nr);
-        return -1;
-    }
-    /* token rows with their slots out, and in */
-    NCK(nc->group_start(), "qmoe_forward_ep");
-    for (int p = 0; p < W; p++) {
-        const size_t sc = (size_t)hc[p], rc = (size_t)hr[p];
-        if (sc) {
-            NCK(nc->send((const uint16_t *)b.send_x + so[p] * d, sc * d, ncclFloat16, p, c->ep_comm,
-                         st), "qmoe_forward_ep dispatch");
-            NCK(nc->send(b.send_e + so[p] * k, sc * k, ncclInt32, p, c->ep_comm, st),
-                "qmoe_forward_ep dispatch");
-            NCK(nc->send(b.send_w + so[p] * k, sc * k, ncclFloat32, p, c->ep_comm, st),
-                "qmoe_forward_ep dispatch");
-        }
-        if (rc) {
-            NCK(nc->recv((uint16_t *)b.recv_x + (own + ro[p]) * d, rc * d, ncclFloat16, p,
-                         c->ep_comm, st), "qmoe_forward_ep dispatch");
-            NCK(nc->recv(b.recv_e + (own + ro[p]) * k, rc * k, ncclInt32, p, c->ep_comm, st),
-                "qmoe_forward_ep dispatch");
-            NCK(nc->recv(b.recv_w + (own + ro[p]) * k, rc * k, ncclFloat32, p, c->ep_comm, st),
-                "qmoe_forward_ep dispatch");
-        }
+        const size_t so = (size_t)p * cap, ro = own + (size_t)p * cap;
+        NCK(nc->send((const uint16_t *)b.send_x + so * d, cap * d, ncclFloat16, p, c->ep_comm, st),
+            "qmoe_forward_ep dispatch");
+        NCK(nc->send(b.send_e + so * k, cap * k, ncclInt32, p, c->ep_comm, st),
+            "qmoe_forward_ep dispatch");
+        NCK(nc->send(b.send_w + so * k, cap * k, ncclFloat32, p, c->ep_comm, st),
+            "qmoe_forward_ep dispatch");
+        NCK(nc->recv((uint16_t *)b.recv_x + ro * d, cap * d, ncclFloat16, p, c->ep_comm, st),
+            "qmoe_forward_ep dispatch");
+        NCK(nc->recv(b.recv_e + ro * k, cap * k, ncclInt32, p, c->ep_comm, st),
+            "qmoe_forward_ep dispatch");
+        NCK(nc->recv(b.recv_w + ro * k, cap * k, ncclFloat32, p, c->ep_comm, st),
+            "qmoe_forward_ep dispatch");
     }
     NCK(nc->group_end(), "qmoe_forward_ep");
     /* this rank's experts over the rows it received, combined per row */
-    if (kerr(qk_ep_experts(c->prefill, &f, (int)nr, c->nslots + layer, st), "ep experts", err))
-        return -1;
+    if (kerr(qk_ep_experts(c->prefill, &f, c->nslots + layer, st), "ep experts", err)) return -1;
     /* partial rows back to the ranks that own the tokens */
     NCK(nc->group_start(), "qmoe_forward_ep");
     for (int p = 0; p < W; p++) {
-        if (hr[p])
-            NCK(nc->send(b.ret + ro[p] * d, (size_t)hr[p] * d, ncclFloat32, p, c->ep_comm, st),
-                "qmoe_forward_ep combine");
-        if (hc[p])
-            NCK(nc->recv(b.back + so[p] * d, (size_t)hc[p] * d, ncclFloat32, p, c->ep_comm, st),
-                "qmoe_forward_ep combine");
+        const size_t o = (size_t)p * cap;
+        NCK(nc->send(b.ret + o * d, cap * d, ncclFloat32, p, c->ep_comm, st),
+            "qmoe_forward_ep combine");
+        NCK(nc->recv(b.back + o * d, cap * d, ncclFloat32, p, c->ep_comm, st),
+            "qmoe_forward_ep combine");
     }
     NCK(nc->group_end(), "qmoe_forward_ep");
     if (n > 0 && kerr(qk_ep_finish(c->prefill, &f, st), "ep finish", err)) return -1;
     return 0;
 }
 
-int qmoe_ep_plan_host(const int32_t *idx, int n, int k, int E, int W, int *counts, int *pos) {
-    if (!idx || !counts || n < 0 || k < 1 || W < 1 || W > 64 || E % W) return -1;
+/* MoE-only stack over layers [l0, l1): h_{l+1} = h_l + MoE_l(RMSNorm(h_l)),
+ * RMSNorm with unit weight and eps; each layer through qmoe_forward_ep on an
+ * expert-parallel context, else qmoe_forward_dev. h: fp32 [n, d] device
+ * rows, updated in place. Stream-ordered only (no host synchronisation),
+ * so a whole stack can be captured in a graph. */
+int qmoe_forward_stack(qmoe_ctx *c, int l0, int l1, float *h, int n, float eps, void *stream,
+                       qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || !h || l0 < 0 || l1 > c->cfg.num_layers || l0 > l1 || n < 0 ||
+        n > c->cfg.max_tokens) {
+        seterr(err, "qmoe_forward_stack: bad arguments (layers [%d, %d), n=%d)", l0, l1, n);
+        return -1;
+    }
+    if (c->ep_world > 1 && !c->ep_comm) {
+        seterr(err, "qmoe_forward_stack: no expert-parallel communicator (qmoe_ep_connect)");
+        return -1;
+    }
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    const int d = c->L.d;
+    for (int l = l0; l < l1; l++) {
+        int rc = qk_launch_residual_norm(h, l > l0 ? c->stk_y : NULL, c->stk_xn, n, d, eps, st);
+        if (kerr(rc, "residual_norm", err)) return -1;
+        if (c->ep_world > 1) rc = qmoe_forward_ep(c, l, c->stk_xn, QMOE_F32, n, c->stk_y, st, err);
+        else rc = n > 0 ? qmoe_forward_dev(c, l, c->stk_xn, QMOE_F32, n, c->stk_y, st, err) : 0;
+        if (rc) return -1;
+    }
+    if (l1 > l0 && kerr(qk_launch_residual_norm(h, c->stk_y, NULL, n, d, eps, st), "residual_norm", err))
+        return -1;
+    return 0;
+}
+
+int qmoe_ep_plan_host(const int32_t *idx, int n, int k, int E, int W, int cap, int *counts,
+                      int *pos) {
+    if (!idx || !counts || n < 0 || cap < n || k < 1 || W < 1 || W > 64 || E % W) return -1;
     const int e_per = E / W;
-    unsigned long long *mask = malloc(sizeof(unsigned long long) * (n > 0 ? n : 1));
-    if (!mask) return -1;
     for (int g = 0; g < W; g++) counts[g] = 0;
     for (int t = 0; t < n; t++) {
         unsigned long long m = 0;
         for (int s = 0; s < k; s++) {
             int e = idx[(size_t)t * k + s];
-            if (e < 0 || e >= E) {
-                free(mask);
-                return -1;
-            }
+            if (e < 0 || e >= E) return -1;
             m |= 1ull << (e / e_per);
         }
-        mask[t] = m;
-        for (int g = 0; g < W; g++) counts[g] += (int)((m >> g) & 1ull);
-    }
-    if (pos) {
-        int base = 0;
         for (int g = 0; g < W; g++) {
-            int p = base;
-            for (int t = 0; t < n; t++) pos[(size_t)g * n + t] = ((mask[t] >> g) & 1ull) ? p++ : -1;
-            base += counts[g];
+            const int live = (int)((m >> g) & 1ull);
+            counts[g] += live;
+            if (pos) pos[(size_t)g * n + t] = live ? g * cap + t : -1;
         }
     }
-    free(mask);
     return 0;
 }

@@ -132,15 +132,18 @@ int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream, vo
  * [g E/G, (g+1) E/G). A token travels once to every rank that owns one of
  * its experts (fp16 x plus its k slots, other ranks' slots as expert id -1),
  * that rank combines its slots' outputs with the routing weights, and one
- * fp32 partial row per (token, rank) comes back:
- *   qk_ep_alloc     buffers for T tokens per rank and G ranks
- *   qk_ep_dispatch  after routing: counts[G] rows per destination (device),
- *                   the send rows grouped by destination (token order), and
- *                   the own tokens as the leading rows of the receive buffer
- *   qk_ep_experts   one grouped pass: the own tokens through the shared
- *                   expert, the `rows` received rows through this rank's
- *                   experts, then the expert-side combine into one partial
- *                   row each
+ * fp32 partial row per (token, rank) comes back. Transfers have a fixed
+ * size: cap rows (the plan's tokens per rank) between every pair of ranks,
+ * token t in row t of its destination's block, so nothing waits for counts
+ * on the host and a whole call can be captured in a graph; rows of tokens
+ * not bound for a rank carry only expert ids -1.
+ *   qk_ep_alloc     buffers for cap tokens per rank and G ranks
+ *   qk_ep_dispatch  after routing: the G cap send rows (rank-major) and the
+ *                   own tokens as the leading rows of the receive buffer
+ *   qk_ep_experts   one grouped pass: the own T tokens through the shared
+ *                   expert, the G cap received rows (after the own tokens)
+ *                   through this rank's experts, then the expert-side combine
+ *                   into one partial row each
  *   qk_ep_finish    the sum of the returned partials (rank order) and the
  *                   shared expert into out
  * The transfers between them are the caller's (NCCL send/recv on the
@@ -149,13 +152,33 @@ typedef struct {
     void *send_x, *recv_x;       /* fp16 [rows, d] */
     int32_t *send_e, *recv_e;    /* [rows, k] */
     float *send_w, *recv_w;      /* [rows, k] */
-    float *ret, *back;           /* fp32 [rows, d]: partials received order / send order */
+    float *ret, *back;           /* fp32 [G cap, d]: partials in received order / send order */
 } qk_ep_bufs;
-int qk_ep_alloc(qk_prefill *p, int T, int G);
+int qk_ep_alloc(qk_prefill *p, int cap, int G);
 void qk_ep_buffers(qk_prefill *p, qk_ep_bufs *b);
-int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int *counts, void *stream);
-int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, int shared_slot_index, void *stream);
+int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, void *stream);
+int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream);
 int qk_ep_finish(qk_prefill *p, const qk_fwd *f, void *stream);
+
+/* Seeded synthetic weights (qmoe_synth.c on the host, qmoe_synth_dev.cu on
+ * the device). Stream of tensor `tensor` of layer `layer`: a splitmix64
+ * counter sequence keyed by qk_stream_key. */
+enum {
+    QK_T_ROUTER = 0, QK_T_SHGATE, QK_T_GQ, QK_T_GS, QK_T_UQ, QK_T_US, QK_T_DQ, QK_T_DS,
+    QK_T_SGQ, QK_T_SGS, QK_T_SUQ, QK_T_SUS, QK_T_SDQ, QK_T_SDS, QK_T_PERM = 20
+};
+uint64_t qk_stream_key(uint64_t seed, uint64_t layer, uint64_t tensor);
+/* One expert straight into its slot: keys = the streams of gate q, gate
+ * scales, up q, up scales, down q, down scales; e = the expert's index in
+ * those (stacked) streams, 0 for the shared expert. */
+int qk_synth_slot(const qk_layout *L, uint8_t *slot, int e, const uint64_t keys[6], void *stream);
+/* bf16(N(0, 1) * 0.02) for elements [0, n) of a stream */
+int qk_synth_bf16_normal(uint16_t *out, size_t n, uint64_t key, void *stream);
+
+/* Residual stream of the MoE-only stack (qmoe_stack.cu), h fp32 [n, d]:
+ * y != NULL: h += y; xn != NULL: xn = RMSNorm(h) (unit weight, eps). */
+int qk_launch_residual_norm(float *h, const float *y, float *xn, int n, int d, float eps,
+                            void *stream);
 
 /* internal cache helper: replace the value of an existing key */
 struct qmoe_cache;

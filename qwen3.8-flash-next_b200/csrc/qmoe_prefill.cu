@@ -588,81 +588,37 @@ __global__ void k_combine(const float *Yr, const float *Ysh, const int *inv, con
 
 // Each token goes once to every rank that owns one of its experts; its
 // other slots travel with it as expert id -1. The bit mask of destinations
-// of token t: mask[t]; rows per destination: counts[g] (block-aggregated).
-__global__ void k_ep_count(const int32_t *idx, int T, int k, int e_per, int G,
-                           unsigned long long *mask, int *counts) {
-    __shared__ int s_c[64];
-    for (int g = threadIdx.x; g < G; g += blockDim.x) s_c[g] = 0;
-    __syncthreads();
+// of token t: mask[t].
+__global__ void k_ep_mask(const int32_t *idx, int T, int k, int e_per, unsigned long long *mask) {
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
         unsigned long long m = 0;
         for (int s = 0; s < k; ++s) m |= 1ull << (idx[t * k + s] / e_per);
         mask[t] = m;
-        for (unsigned long long r = m; r; r &= r - 1) atomicAdd(&s_c[__ffsll(r) - 1], 1);
-    }
-    __syncthreads();
-    for (int g = threadIdx.x; g < G; g += blockDim.x)
-        if (s_c[g]) atomicAdd(counts + g, s_c[g]);
-}
-
-// One CTA per destination rank g: the tokens bound for g get consecutive
-// send positions after the rows of ranks < g, in token order; pos[g * T + t]
-// (-1 when t does not go to g).
-__global__ void __launch_bounds__(1024) k_ep_positions(const unsigned long long *mask, int T,
-                                                       const int *counts, int *pos) {
-    __shared__ int s_warp[32];
-    __shared__ int s_base;
-    const int g = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) {
-        int b = 0;
-        for (int q = 0; q < g; ++q) b += counts[q];
-        s_base = b;
-    }
-    __syncthreads();
-    for (int t0 = 0; t0 < T; t0 += 1024) {
-        const int t = t0 + threadIdx.x;
-        const bool mine = t < T && ((mask[t] >> g) & 1ull);
-        const unsigned m = __ballot_sync(QK_FULL, mine);
-        if (lane == 0) s_warp[warp] = __popc(m);
-        __syncthreads();
-        if (warp == 0) {
-            int v = s_warp[lane];
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const int u = __shfl_up_sync(QK_FULL, v, off);
-                if (lane >= off) v += u;
-            }
-            s_warp[lane] = v;
-        }
-        __syncthreads();
-        if (t < T)
-            pos[static_cast<size_t>(g) * T + t] =
-                mine ? s_base + (warp ? s_warp[warp - 1] : 0) + __popc(m & ((1u << lane) - 1u)) : -1;
-        __syncthreads();
-        if (threadIdx.x == 0) s_base += s_warp[31];
-        __syncthreads();
     }
 }
 
-// Send row p = pos[g, t]: fp16 x[t] (natural element order) and the token's
-// k slots, expert ids of other ranks replaced by -1 (weights 0). One warp
-// per (rank, token).
-__global__ void k_ep_pack(const void *x, int x_bf16, int d, int T, int k, int e_per, int G,
-                          const int32_t *idx, const float *wts, const int *pos, __half *send_x,
-                          int32_t *send_e, float *send_w) {
+// Fixed-capacity send rows: rank g's rows are [g cap, (g + 1) cap), token t
+// in row g cap + t. A row carries fp16 x[t] (natural element order) and the
+// token's k slots, expert ids of other ranks replaced by -1 (weights 0);
+// rows of tokens not bound for g, and rows t >= T, carry only k ids -1 (x
+// is not written). One warp per row.
+__global__ void k_ep_pack(const void *x, int x_bf16, int d, int T, int cap, int k, int e_per,
+                          int G, const int32_t *idx, const float *wts,
+                          const unsigned long long *mask, __half *send_x, int32_t *send_e,
+                          float *send_w) {
     const int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (wi >= G * T) return;
-    const int g = wi / T, t = wi % T;
-    const int p = pos[wi];
-    if (p < 0) return;
+    if (wi >= G * cap) return;
+    const int g = wi / cap, t = wi % cap;
+    const size_t p = static_cast<size_t>(wi);
+    const bool live = t < T && ((mask[t] >> g) & 1ull);
     if (lane < k) {
-        const int e = idx[t * k + lane];
-        const bool own = e / e_per == g;
-        send_e[static_cast<size_t>(p) * k + lane] = own ? e : -1;
-        send_w[static_cast<size_t>(p) * k + lane] = own ? wts[t * k + lane] : 0.f;
+        const int e = live ? idx[t * k + lane] : -1;
+        const bool own = live && e / e_per == g;
+        send_e[p * k + lane] = own ? e : -1;
+        send_w[p * k + lane] = own ? wts[t * k + lane] : 0.f;
     }
-    __half *dst = send_x + static_cast<size_t>(p) * d;
+    if (!live) return;
+    __half *dst = send_x + p * d;
     for (int c = lane; c < d / 8; c += 32) {
         float v[8];
         if (x_bf16) {
@@ -738,16 +694,17 @@ __global__ void k_ep_partial(const float *Y, const int *inv, const int32_t *e_of
 }
 
 // Token side: out[t] = sum over the destination ranks in rank order of the
-// returned partial rows + sigmoid(g_t) * Ysh[t].
-__global__ void k_ep_final(const float *back, const int *pos, int T, int G, const float *Ysh,
-                           const float *sgate, int d, float *out) {
+// returned partial rows (row g cap + t from rank g) + sigmoid(g_t) * Ysh[t].
+__global__ void k_ep_final(const float *back, const unsigned long long *mask, int T, int cap,
+                           int G, const float *Ysh, const float *sgate, int d, float *out) {
     const int t = blockIdx.x;
+    const unsigned long long m = mask[t];
     for (int c = threadIdx.x; c < d / 4; c += blockDim.x) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int g = 0; g < G; ++g) {
-            const int p = pos[static_cast<size_t>(g) * T + t];
-            if (p < 0) continue;
-            const float4 v = reinterpret_cast<const float4 *>(back + static_cast<size_t>(p) * d)[c];
+            if (!((m >> g) & 1ull)) continue;
+            const size_t p = static_cast<size_t>(g) * cap + t;
+            const float4 v = reinterpret_cast<const float4 *>(back + p * d)[c];
             acc.x += v.x;
             acc.y += v.y;
             acc.z += v.z;
@@ -1093,9 +1050,8 @@ struct qk_prefill {
     int *rn;
     CUtensorMap tmXr;
     // expert parallelism: one row per (token, destination rank)
-    int ep_T, ep_G;                 // tokens per rank, ranks
+    int ep_T, ep_G;                 // rows per rank pair (capacity), ranks
     unsigned long long *ep_mask;    // [ep_T] destination ranks of each token
-    int *ep_pos;                    // [ep_G * ep_T] send row of (rank, token), -1 if none
     int32_t *ep_send_e, *ep_recv_e; // [rows * k] slot expert ids (-1: another rank's)
     float *ep_send_w, *ep_recv_w;   // [rows * k] slot weights
     __half *ep_send_x, *ep_recv_x;  // [rows, d] fp16
@@ -1120,7 +1076,6 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->rtiles);
     cudaFree(p->rn);
     cudaFree(p->ep_mask);
-    cudaFree(p->ep_pos);
     cudaFree(p->ep_send_e);
     cudaFree(p->ep_recv_e);
     cudaFree(p->ep_send_w);
@@ -1323,7 +1278,6 @@ extern "C" int qk_ep_alloc(qk_prefill *p, int T, int G) {
     p->ep_G = G;
     const size_t d = static_cast<size_t>(L.d), k = static_cast<size_t>(L.k);
     cudaError_t e = cudaMalloc(&p->ep_mask, sizeof(unsigned long long) * T);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_pos, sizeof(int) * rows);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_e, sizeof(int32_t) * rows * k);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_e, sizeof(int32_t) * (rows + T) * k);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_w, sizeof(float) * rows * k);
@@ -1346,44 +1300,37 @@ extern "C" void qk_ep_buffers(qk_prefill *p, qk_ep_bufs *b) {
     b->back = p->ep_back;
 }
 
-extern "C" int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, int *counts, void *stream) {
+extern "C" int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, void *stream) {
     const qk_layout &L = p->L;
-    const int T = f->T, G = p->ep_G;
-    if (T > p->ep_T || L.E % G) return cudaErrorInvalidValue;
+    const int T = f->T, G = p->ep_G, cap = p->ep_T;
+    if (T > cap || L.E % G) return cudaErrorInvalidValue;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int e_per = L.E / G;
-    cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * G, st);
-    if (e != cudaSuccess) return e;
-    if (T > 0) {
-        k_ep_count<<<(T + 255) / 256, 256, 0, st>>>(f->idx, T, L.k, e_per, G, p->ep_mask, counts);
-        k_ep_positions<<<G, 1024, 0, st>>>(p->ep_mask, T, counts, p->ep_pos);
-        k_ep_pack<<<(G * T * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, L.k, e_per, G,
-                                                           f->idx, f->wts, p->ep_pos, p->ep_send_x,
-                                                           p->ep_send_e, p->ep_send_w);
-        // this rank's own tokens lead the receive buffer (shared expert only)
+    if (T > 0)
+        k_ep_mask<<<(T + 255) / 256, 256, 0, st>>>(f->idx, T, L.k, e_per, p->ep_mask);
+    k_ep_pack<<<(G * cap * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, cap, L.k, e_per,
+                                                         G, f->idx, f->wts, p->ep_mask,
+                                                         p->ep_send_x, p->ep_send_e, p->ep_send_w);
+    // this rank's own tokens lead the receive buffer (shared expert only)
+    if (T > 0)
         k_ep_own<<<(T * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, L.k, p->ep_recv_x,
                                                        p->ep_recv_e);
-    }
     return cudaGetLastError();
 }
 
-extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int rows, int shared_slot_index,
-                             void *stream) {
+extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream) {
     const qk_layout &L = p->L;
-    const int T = f->T;
-    if (rows > p->ep_T * p->ep_G) return cudaErrorInvalidValue;
-    if (rows + T == 0) return cudaSuccess;
+    const int T = f->T, rows = p->ep_T * p->ep_G;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // one grouped pass: the own tokens through the shared expert (rows
     // [0, T)), the received rows through this rank's experts
     cudaError_t e = grouped(p, p->ep_recv_x, XK_F16, T + rows, p->ep_recv_e, L.k, T, f->slot_of,
                             shared_slot_index, f->err, st, nullptr);
     if (e != cudaSuccess) return e;
-    if (rows > 0)
-        k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv + static_cast<size_t>(T) * L.k,
-                                           p->ep_recv_e + static_cast<size_t>(T) * L.k,
-                                           p->ep_recv_w + static_cast<size_t>(T) * L.k, L.k, L.d,
-                                           p->ep_ret);
+    k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv + static_cast<size_t>(T) * L.k,
+                                       p->ep_recv_e + static_cast<size_t>(T) * L.k,
+                                       p->ep_recv_w + static_cast<size_t>(T) * L.k, L.k, L.d,
+                                       p->ep_ret);
     return cudaGetLastError();
 }
 
@@ -1393,7 +1340,8 @@ extern "C" int qk_ep_finish(qk_prefill *p, const qk_fwd *f, void *stream) {
     if (T == 0) return cudaSuccess;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // the shared rows are Y[0, T) of the experts pass
-    k_ep_final<<<T, 256, 0, st>>>(p->ep_back, p->ep_pos, T, p->ep_G, p->Y, f->sgate, L.d, f->out);
+    k_ep_final<<<T, 256, 0, st>>>(p->ep_back, p->ep_mask, T, p->ep_T, p->ep_G, p->Y, f->sgate,
+                                  L.d, f->out);
     return cudaGetLastError();
 }
 

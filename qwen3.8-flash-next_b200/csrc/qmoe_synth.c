@@ -20,6 +20,7 @@
 #include <string.h>
 
 #include "../../include/qmoe.h"
+#include "qmoe_internal.h"
 
 #define GOLDEN 0x9E3779B97F4A7C15ull
 
@@ -34,7 +35,7 @@ static inline uint64_t draw(uint64_t key, uint64_t i) {
     return mix64(key + (i + 1) * GOLDEN);
 }
 
-static uint64_t stream_key(uint64_t seed, uint64_t layer, uint64_t tensor) {
+uint64_t qk_stream_key(uint64_t seed, uint64_t layer, uint64_t tensor) {
     return mix64(mix64(seed ^ 0x5851F42D4C957F2Dull) + (layer << 16) + tensor);
 }
 
@@ -60,10 +61,6 @@ static float from_bf16(uint16_t h) {
     return f;
 }
 
-enum {
-    T_ROUTER = 0, T_SHGATE, T_GQ, T_GS, T_UQ, T_US, T_DQ, T_DS,
-    T_SGQ, T_SGS, T_SUQ, T_SUS, T_SDQ, T_SDS, T_PERM = 20
-};
 
 static void fill_words(uint64_t key, uint32_t *q, size_t off, size_t n) {
     for (size_t i = 0; i < n; i++) q[off + i] = (uint32_t)draw(key, off + i);
@@ -107,12 +104,12 @@ int qmoe_synth_layer(const qmoe_config *c, uint64_t seed, int layer,
     if (e0 < 0 || e1 > E) return -1;
     uint64_t L = (uint64_t)layer;
     if (w->router) {
-        uint64_t key = stream_key(seed, L, T_ROUTER);
+        uint64_t key = qk_stream_key(seed, L, QK_T_ROUTER);
         uint16_t *r = (uint16_t *)w->router;
         for (size_t i = 0; i < sz.router; i++) r[i] = to_bf16(normal(key, i) * 0.02f);
     }
     if (w->shared_gate) {
-        uint64_t key = stream_key(seed, L, T_SHGATE);
+        uint64_t key = qk_stream_key(seed, L, QK_T_SHGATE);
         uint16_t *r = (uint16_t *)w->shared_gate;
         for (size_t i = 0; i < sz.shared_gate; i++) r[i] = to_bf16(normal(key, i) * 0.02f);
     }
@@ -120,43 +117,43 @@ int qmoe_synth_layer(const qmoe_config *c, uint64_t seed, int layer,
     size_t gq_pe = I * (d / 8), gs_pe = I * (d / g), dq_pe = d * (I / 8), ds_pe = d * (I / g);
     size_t e0s = (size_t)e0, ne = (size_t)(e1 - e0);
     struct { const qmoe_q4 *t; int tq, ts; size_t q_pe, s_pe; } parts[3] = {
-        {&w->gate, T_GQ, T_GS, gq_pe, gs_pe},
-        {&w->up, T_UQ, T_US, gq_pe, gs_pe},
-        {&w->down, T_DQ, T_DS, dq_pe, ds_pe},
+        {&w->gate, QK_T_GQ, QK_T_GS, gq_pe, gs_pe},
+        {&w->up, QK_T_UQ, QK_T_US, gq_pe, gs_pe},
+        {&w->down, QK_T_DQ, QK_T_DS, dq_pe, ds_pe},
     };
     for (int p = 0; p < 3; p++) {
         const qmoe_q4 *t = parts[p].t;
         if (t->q)
-            fill_words(stream_key(seed, L, parts[p].tq), (uint32_t *)t->q,
+            fill_words(qk_stream_key(seed, L, parts[p].tq), (uint32_t *)t->q,
                        e0s * parts[p].q_pe, ne * parts[p].q_pe);
         if (t->scales || t->biases)
-            fill_scales(stream_key(seed, L, parts[p].ts), (uint16_t *)t->scales,
+            fill_scales(qk_stream_key(seed, L, parts[p].ts), (uint16_t *)t->scales,
                         (uint16_t *)t->biases, e0s * parts[p].s_pe, ne * parts[p].s_pe);
     }
     struct { const qmoe_q4 *t; int tq, ts; size_t nq, ns; } sh[3] = {
-        {&w->sh_gate, T_SGQ, T_SGS, sz.sh_q, sz.sh_sb},
-        {&w->sh_up, T_SUQ, T_SUS, sz.sh_q, sz.sh_sb},
-        {&w->sh_down, T_SDQ, T_SDS, sz.sh_down_q, sz.sh_down_sb},
+        {&w->sh_gate, QK_T_SGQ, QK_T_SGS, sz.sh_q, sz.sh_sb},
+        {&w->sh_up, QK_T_SUQ, QK_T_SUS, sz.sh_q, sz.sh_sb},
+        {&w->sh_down, QK_T_SDQ, QK_T_SDS, sz.sh_down_q, sz.sh_down_sb},
     };
     for (int p = 0; p < 3; p++) {
         const qmoe_q4 *t = sh[p].t;
-        if (t->q) fill_words(stream_key(seed, L, sh[p].tq), (uint32_t *)t->q, 0, sh[p].nq);
+        if (t->q) fill_words(qk_stream_key(seed, L, sh[p].tq), (uint32_t *)t->q, 0, sh[p].nq);
         if (t->scales || t->biases)
-            fill_scales(stream_key(seed, L, sh[p].ts), (uint16_t *)t->scales,
+            fill_scales(qk_stream_key(seed, L, sh[p].ts), (uint16_t *)t->scales,
                         (uint16_t *)t->biases, 0, sh[p].ns);
     }
     return 0;
 }
 
 void qmoe_synth_tokens(uint64_t seed, uint64_t stream, int n, int d, float *x) {
-    uint64_t key = stream_key(seed, 0xFFFF, 0x1000 + stream);
+    uint64_t key = qk_stream_key(seed, 0xFFFF, 0x1000 + stream);
     for (size_t i = 0; i < (size_t)n * (size_t)d; i++)
         x[i] = from_bf16(to_bf16(normal(key, i)));
 }
 
 void qmoe_synth_zipf_bias(uint64_t seed, int layer, int E, double s,
                           float *bias) {
-    uint64_t key = stream_key(seed, (uint64_t)layer, T_PERM);
+    uint64_t key = qk_stream_key(seed, (uint64_t)layer, QK_T_PERM);
     int perm[4096];
     if (E > 4096) return;
     for (int i = 0; i < E; i++) perm[i] = i;

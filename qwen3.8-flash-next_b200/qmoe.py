@@ -99,10 +99,13 @@ SIGNATURES = {
     "qmoe_forward": (C.c_int, [_P, C.c_int, _P, C.c_int, _P, C.POINTER(Err)]),
     "qmoe_forward_dev": (C.c_int, [_P, C.c_int, _P, C.c_int, C.c_int, _P, _P, C.POINTER(Err)]),
     "qmoe_ep_unique_id": (C.c_int, [_P, C.POINTER(Err)]),
-    "qmoe_ep_plan_host": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),
+    "qmoe_ep_plan_host": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),
     "qmoe_ep_connect": (C.c_int, [_P, _P, C.POINTER(Err)]),
     "qmoe_forward_ep": (C.c_int, [_P, C.c_int, _P, C.c_int, C.c_int, _P, _P, C.POINTER(Err)]),
     "qmoe_sync": (C.c_int, [_P, C.POINTER(Err)]),
+    "qmoe_forward_stack": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_int, C.c_float, _P,
+                                     C.POINTER(Err)]),
+    "qmoe_synth_layer_dev": (C.c_int, [_P, C.c_int, C.c_uint64, C.c_double, C.POINTER(Err)]),
     "qmoe_last_routing": (C.c_int, [_P, _P, _P, _P, C.POINTER(Err)]),
     "qmoe_forward_token_noalloc": (C.c_int, [C.POINTER(TokenArgs), _P, C.POINTER(Err)]),
     "qmoe_capture_begin": (C.c_int, [_P, _P, C.POINTER(Err)]),
@@ -282,6 +285,18 @@ class Context:
         err = Err()
         self._chk(lib().qmoe_forward_ep(self.h, layer, x_ptr, x_dtype, n, out_ptr, stream,
                                         C.byref(err)), err)
+
+    def synth_layer_dev(self, layer: int, seed: int, zipf_s: float = 0.0):
+        """The seeded synthetic layer generated on the device (resident contexts)."""
+        err = Err()
+        self._chk(lib().qmoe_synth_layer_dev(self.h, layer, seed, zipf_s, C.byref(err)), err)
+
+    def forward_stack(self, l0: int, l1: int, h_ptr: int, n: int, eps: float = 1e-6,
+                      stream: int | None = None):
+        """h <- h + MoE_l(RMSNorm(h)) for layers [l0, l1); h: device fp32 [n, d]."""
+        err = Err()
+        self._chk(lib().qmoe_forward_stack(self.h, l0, l1, h_ptr, n, eps, stream, C.byref(err)),
+                  err)
 
     def sync(self):
         err = Err()

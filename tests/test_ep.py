@@ -17,13 +17,13 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _plan(idx, E, W):
+def _plan(idx, E, W, cap):
     import qmoe
     idx = np.ascontiguousarray(idx, np.int32)
     n, k = idx.shape
     counts = np.zeros(W, np.int32)
     pos = np.zeros(W * n, np.int32)
-    rc = qmoe.lib().qmoe_ep_plan_host(idx.ctypes.data, n, k, E, W, counts.ctypes.data,
+    rc = qmoe.lib().qmoe_ep_plan_host(idx.ctypes.data, n, k, E, W, cap, counts.ctypes.data,
                                       pos.ctypes.data)
     assert rc == 0
     return counts, pos.reshape(W, n)
@@ -31,19 +31,16 @@ def _plan(idx, E, W):
 
 def test_plan_sends_each_token_once_per_owner_rank(built):
     rng = np.random.default_rng(7)
-    E, W, n, k = 64, 4, 50, 6
+    E, W, n, k, cap = 64, 4, 50, 6, 56
     idx = np.stack([rng.choice(E, k, replace=False) for _ in range(n)]).astype(np.int32)
-    counts, pos = _plan(idx, E, W)
+    counts, pos = _plan(idx, E, W, cap)
     owner = idx // (E // W)
     goes = np.stack([(owner == g).any(1) for g in range(W)])      # [W, n]
     assert counts.tolist() == goes.sum(1).tolist()
-    sent = pos[pos >= 0]
-    assert sorted(sent.tolist()) == list(range(int(counts.sum())))  # rows 0..total-1 once
     assert np.array_equal(pos >= 0, goes)
-    starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
-    for g in range(W):
-        mine = pos[g][goes[g]]                                     # token order
-        assert mine.tolist() == list(range(starts[g], starts[g] + counts[g]))
+    for g in range(W):                                             # row t of block g
+        t = np.nonzero(goes[g])[0]
+        assert pos[g][t].tolist() == (g * cap + t).tolist()
 
 
 def test_plan_rejects_bad_arguments(built):
@@ -51,9 +48,10 @@ def test_plan_rejects_bad_arguments(built):
     idx = np.zeros((2, 2), np.int32)
     counts = np.zeros(4, np.int32)
     f = qmoe.lib().qmoe_ep_plan_host
-    assert f(idx.ctypes.data, 2, 2, 10, 4, counts.ctypes.data, None) == -1   # E % W
+    assert f(idx.ctypes.data, 2, 2, 10, 4, 2, counts.ctypes.data, None) == -1   # E % W
+    assert f(idx.ctypes.data, 2, 2, 16, 4, 1, counts.ctypes.data, None) == -1   # cap < n
     bad = np.array([[0, 99]], np.int32)
-    assert f(bad.ctypes.data, 1, 2, 16, 4, counts.ctypes.data, None) == -1   # expert id
+    assert f(bad.ctypes.data, 1, 2, 16, 4, 1, counts.ctypes.data, None) == -1   # expert id
 
 
 def _free_port():
@@ -82,23 +80,20 @@ def _gloo_rank(rank, world, port, result):
         s = qmoe.SynthLayer(cfg, 20261201)
         x = qmoe.synth_tokens(20261201, 40 + rank, 12 + 5 * rank, d)   # ranks differ in n
         idx, w, _ = oracle.restatement().route(s, x)
-        counts, pos = _plan(idx, E, world)
-        # counts out, counts in
-        rcounts = torch.zeros(world, dtype=torch.int32)
-        dist.all_to_all_single(rcounts, torch.from_numpy(counts))
-        # the slots of each sent row (other ranks' experts as -1), then the
-        # exchange itself
+        cap = 32                                                     # rows per rank pair
+        counts, pos = _plan(idx, E, world, cap)
+        # the fixed-size exchange: cap rows to every rank, each sent row
+        # with the token's slots (other ranks' experts as -1), unused rows
+        # all -1
         n, k = idx.shape
-        send_e = np.full((int(counts.sum()), k), -1, np.int32)
+        send_e = np.full((world * cap, k), -1, np.int32)
         for g in range(world):
             for t in range(n):
                 if pos[g, t] >= 0:
                     own = idx[t] // (E // world) == g
                     send_e[pos[g, t]] = np.where(own, idx[t], -1)
-        recv_e = torch.zeros((int(rcounts.sum()), k), dtype=torch.int32)
-        dist.all_to_all_single(recv_e, torch.from_numpy(send_e),
-                               output_split_sizes=rcounts.tolist(),
-                               input_split_sizes=counts.tolist())
+        recv_e = torch.zeros((world * cap, k), dtype=torch.int32)
+        dist.all_to_all_single(recv_e, torch.from_numpy(send_e))
         # every row received is for one of this rank's experts, and the rows
         # received are exactly every rank's assignments to those experts
         all_idx = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
@@ -124,7 +119,9 @@ def _gloo_rank(rank, world, port, result):
 def test_two_rank_dispatch_over_gloo(built):
     """World size 2 on the CPU (gloo): each rank routes its own tokens with
     the C restatement, plans its dispatch with the library's host plan, and
-    the exchanged rows land exactly on the owners of their experts."""
+    after the fixed-size exchange every expert id received is one of the
+    rank's own and the ids received are exactly every rank's assignments to
+    those experts."""
     import torch.multiprocessing as mp
     world = 2
     with mp.Manager() as m:
@@ -205,4 +202,80 @@ def test_expert_parallel_forward_two_gpus(built):
         assert np.array_equal(idx[sample], ri)
         mab = float(np.abs(out[sample] - ro).max())
         rr = float(np.linalg.norm(out[sample] - ro) / np.linalg.norm(ro))
+        assert mab <= 2e-2 and rr <= 1e-3, (r, mab, rr)
+
+
+def _ep_stack_rank(rank, world, uid_q, out_q, T_per, n_layers):
+    import sys
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "qwen3.8-flash-next_b200"))
+    import torch
+
+    import qmoe
+    torch.cuda.set_device(rank)
+    d, E, k, I = 2048, 512, 10, 512
+    cfg = qmoe.make_config(d, E, k, I, layers=n_layers, max_tokens=T_per, device=rank,
+                           ep_rank=rank, ep_world=world)
+    ctx = qmoe.Context(cfg)
+    for l in range(n_layers):
+        ctx.upload(l, qmoe.SynthLayer(cfg, 20261202, l))
+    if rank == 0:
+        uid = qmoe.ep_unique_id()
+        for _ in range(world - 1):
+            uid_q.put(uid)
+    else:
+        uid = uid_q.get(timeout=120)
+    ctx.ep_connect(uid)
+    h = torch.from_numpy(qmoe.synth_tokens(20261202, 70 + rank, T_per, d)).cuda()
+    # captured as one graph, as the benchmark runs it
+    st = torch.cuda.Stream()
+    ctx.capture_begin(st.cuda_stream)
+    ctx.forward_stack(0, n_layers, h.data_ptr(), T_per, 1e-6, st.cuda_stream)
+    g = ctx.capture_end(st.cuda_stream)
+    g.launch(st.cuda_stream)
+    st.synchronize()
+    ctx.sync()
+    g.close()
+    out_q.put((rank, h.cpu().numpy()))
+    ctx.close()
+
+
+@pytest.mark.gpu
+def test_expert_parallel_stack_two_gpus(built):
+    """Two GPUs: a two-layer MoE-only stack (RMSNorm + MoE + residual), every
+    layer expert-parallel and the whole stack one captured graph per rank,
+    against the restatement composed layer by layer."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    import qmoe
+    from test_stack import compose
+    world, T_per, n_layers = 2, 32, 2
+    ctx = mp.get_context("spawn")
+    uid_q, out_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_ep_stack_rank, args=(r, world, uid_q, out_q, T_per, n_layers))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            r, h = out_q.get(timeout=600)
+            results[r] = h
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    cfg = qmoe.make_config(2048, 512, 10, 512, layers=n_layers, max_tokens=T_per)
+    layers = [qmoe.SynthLayer(cfg, 20261202, l) for l in range(n_layers)]
+    for r in range(world):
+        h0 = qmoe.synth_tokens(20261202, 70 + r, T_per, 2048)
+        ref, _ = compose(layers, h0)
+        delta, rdelta = results[r] - h0, ref - h0
+        mab = float(np.abs(delta - rdelta).max())
+        rr = float(np.linalg.norm(delta - rdelta) / np.linalg.norm(rdelta))
         assert mab <= 2e-2 and rr <= 1e-3, (r, mab, rr)
