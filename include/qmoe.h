@@ -201,7 +201,8 @@ int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream,
  * loaded at run time from libnccl.so.2).
  * qmoe_forward_ep is a collective replacement of qmoe_forward_dev for the
  * rank's own n tokens (device pointers, n may differ between ranks and may
- * be 0): local routing; each token sent once (fp16, with its k slots) to
+ * be 0; x_dtype the same on every rank): local routing; each token sent
+ * once (x as given, bf16 or fp32, with its k slots) to
  * every rank that owns one of its experts; the owners' grouped GEMMs and a
  * weighted combine of each token's local slots; one fp32 partial row per
  * (token, rank) sent back; on the token's rank the partials (in rank order)

@@ -1397,7 +1397,7 @@ int qmoe_ep_connect(qmoe_ctx *c, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_
 
 /* One collective forward: every rank calls it for the same layer with its
  * own n tokens. Route locally; send every rank a block of max_tokens rows in
- * which row t is token t when that rank owns one of its experts (fp16 x,
+ * which row t is token t when that rank owns one of its experts (x as given,
  * slot expert ids and weights) and a row of expert ids -1 otherwise; one
  * grouped pass runs the shared expert on the own tokens and this rank's
  * experts on the rows received, combining each received row's local slots;
@@ -1439,18 +1439,19 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
     qk_ep_buffers(c->prefill, &b);
     if (n > 0 && route(c, layer, &f, st, 0, NULL, err)) return -1;
     if (kerr(qk_ep_dispatch(c->prefill, &f, st), "ep dispatch", err)) return -1;
-    /* token rows with their slots out, and in (after the own n tokens) */
-    const size_t own = (size_t)n;
+    /* token rows with their slots out, and in (after the own n tokens);
+     * x travels as given (bf16 or fp32: every rank passes the same dtype) */
+    const size_t own = (size_t)n, row = (size_t)d * (x_dtype == QMOE_BF16 ? 2 : 4);
     NCK(nc->group_start(), "qmoe_forward_ep");
     for (int p = 0; p < W; p++) {
         const size_t so = (size_t)p * cap, ro = own + (size_t)p * cap;
-        NCK(nc->send((const uint16_t *)b.send_x + so * d, cap * d, ncclFloat16, p, c->ep_comm, st),
+        NCK(nc->send((const uint8_t *)b.send_x + so * row, cap * row, ncclUint8, p, c->ep_comm, st),
             "qmoe_forward_ep dispatch");
         NCK(nc->send(b.send_e + so * k, cap * k, ncclInt32, p, c->ep_comm, st),
             "qmoe_forward_ep dispatch");
         NCK(nc->send(b.send_w + so * k, cap * k, ncclFloat32, p, c->ep_comm, st),
             "qmoe_forward_ep dispatch");
-        NCK(nc->recv((uint16_t *)b.recv_x + ro * d, cap * d, ncclFloat16, p, c->ep_comm, st),
+        NCK(nc->recv((uint8_t *)b.recv_x + ro * row, cap * row, ncclUint8, p, c->ep_comm, st),
             "qmoe_forward_ep dispatch");
         NCK(nc->recv(b.recv_e + ro * k, cap * k, ncclInt32, p, c->ep_comm, st),
             "qmoe_forward_ep dispatch");

@@ -130,7 +130,8 @@ int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream, vo
 
 /* Expert parallelism (qmoe_prefill.cu). Rank g of G owns experts
  * [g E/G, (g+1) E/G). A token travels once to every rank that owns one of
- * its experts (fp16 x plus its k slots, other ranks' slots as expert id -1),
+ * its experts (x as given, bf16 or fp32, plus its k slots, other ranks' slots
+ * as expert id -1),
  * that rank combines its slots' outputs with the routing weights, and one
  * fp32 partial row per (token, rank) comes back. Transfers have a fixed
  * size: cap rows (the plan's tokens per rank) between every pair of ranks,
@@ -149,7 +150,7 @@ int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream, vo
  * The transfers between them are the caller's (NCCL send/recv on the
  * buffers of qk_ep_buffers). */
 typedef struct {
-    void *send_x, *recv_x;       /* fp16 [rows, d] */
+    void *send_x, *recv_x;       /* [rows, d] x as given: bf16 or fp32 (same on every rank) */
     int32_t *send_e, *recv_e;    /* [rows, k] */
     float *send_w, *recv_w;      /* [rows, k] */
     float *ret, *back;           /* fp32 [G cap, d]: partials in received order / send order */

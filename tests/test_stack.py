@@ -46,30 +46,50 @@ def _run_stack(shape, n_layers, n, seed):
         ctx.upload(l, s)
     h0 = qmoe.synth_tokens(seed, 9, n, d)
     h = torch.from_numpy(h0).cuda()
-    # layer by layer, collecting the routing, then the whole stack at once
-    routes = []
+    # layer by layer, keeping h and the routing after each, then the whole
+    # stack in one call
+    hs, routes = [h0], []
     for l in range(n_layers):
         ctx.forward_stack(l, l + 1, h.data_ptr(), n, EPS, None)
         ctx.sync()
+        hs.append(h.cpu().numpy())
         routes.append(ctx.routing(n)[0])
-    h_steps = h.cpu().numpy()
     h.copy_(torch.from_numpy(h0))
     ctx.forward_stack(0, n_layers, h.data_ptr(), n, EPS, None)
     ctx.sync()
     h_all = h.cpu().numpy()
     ctx.close()
-    return layers, h0, h_steps, h_all, routes
+    return layers, hs, h_all, routes
 
 
-def _check(layers, h0, h_steps, h_all, routes):
-    ref, ref_routes = compose(layers, h0)
-    assert np.array_equal(h_steps, h_all), "one call per layer differs from one call per stack"
-    for l, (a, b) in enumerate(zip(routes, ref_routes)):
-        assert np.array_equal(np.sort(a, 1), np.sort(b, 1)), f"layer {l} routing"
-    delta, rdelta = h_all - h0, ref - h0      # the stack's contribution
-    mab = float(np.abs(delta - rdelta).max())
+# RMS of one config-1 layer's output on bf16 N(0, 1) tokens (the scale the
+# layer bars were set at): deeper layers of the stack produce outputs ~10x
+# larger, and their absolute bar scales with them
+CFG1_OUT_RMS = 16.05
+
+
+def _check(layers, hs, h_all, routes):
+    """Per layer, on the device's own input h_l: routing bit-exact and the
+    layer's output y_l = h_{l+1} - h_l within the layer bars: relative RMS
+    1e-3, max-abs 2e-2 scaled by the output's RMS over a config-1 layer's
+    (never below 2e-2). End to end against the oracle's own composition:
+    relative RMS of the stack's contribution within 1e-3 (the stack
+    amplifies a layer's input differences, so an absolute bar is not
+    meaningful there)."""
+    import oracle
+    assert np.array_equal(hs[-1], h_all), "one call per layer differs from one call per stack"
+    for l, s in enumerate(layers):
+        ry, ridx, _ = oracle.restatement().forward(s, rmsnorm(hs[l]))
+        assert np.array_equal(np.sort(routes[l], 1), np.sort(ridx, 1)), f"layer {l} routing"
+        y = hs[l + 1].astype(np.float64) - hs[l].astype(np.float64)
+        mab = float(np.abs(y - ry).max())
+        rr = float(np.linalg.norm(y - ry) / np.linalg.norm(ry))
+        bar = 2e-2 * max(1.0, float(np.sqrt(np.mean(ry.astype(np.float64) ** 2))) / CFG1_OUT_RMS)
+        assert mab <= bar and rr <= 1e-3, (l, mab, bar, rr)
+    ref, _ = compose(layers, hs[0])
+    delta, rdelta = h_all - hs[0], ref - hs[0]
     rr = float(np.linalg.norm(delta - rdelta) / np.linalg.norm(rdelta))
-    assert mab <= 2e-2 and rr <= 1e-3, (mab, rr)
+    assert rr <= 1e-3, rr
 
 
 @pytest.mark.gpu
@@ -81,8 +101,7 @@ def test_stack_small_shape_matches_composition(built):
 @pytest.mark.gpu
 def test_stack_full_shape_matches_composition(built):
     """Two full-size layers (hidden 2048, 512 experts, top-10) at the stack
-    configuration's batch of 64 tokens: routing bit-exact per layer, the
-    stack's contribution to h within the layer tolerance."""
+    configuration's batch of 64 tokens (the bars of _check)."""
     _check(*_run_stack((2048, 512, 10, 512), 2, 64, 33))
 
 
