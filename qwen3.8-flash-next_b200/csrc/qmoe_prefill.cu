@@ -38,6 +38,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "qmoe_dev.cuh"
@@ -434,6 +435,303 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Grouped GEMM for small groups (at most NS = 32 rows per tile): the operands
+// swap roles. A = 128 dequantised weight rows (gate, up or down rows, the B
+// tile of k_gemm), kept in tensor memory; B = the group's token rows (x or
+// H) from shared memory, the hi and lo planes side by side as N = 64 (one
+// plane: N = 32). Per 16-wide K slice and half of the 256-row weight tile
+// one MMA of M=128 x N=64 x K=16; D[weight row][token] sits in TMEM lanes =
+// weight rows and the epilogue writes it transposed (token rows of H or Y),
+// adding the hi and lo columns. Keeping the weights out of shared memory
+// matters here: with them there, the operand reads of these small MMAs and
+// the dequantisers' stores took the shared-memory bandwidth and set the
+// pace. TMEM: accumulators in columns [0, 256) (2 buffers x 2 halves x 64),
+// four dequantised weight buffers in [256, 512) (2 halves x 32 columns).
+// Warp roles and bounded waits as k_gemm; MODE 0 / 3 gate/up (x one plane /
+// hi+lo), 1 down (H hi+lo).
+constexpr int NS = 32;                    // token rows per small tile
+constexpr int kSmallMax = 2 * NS;         // largest group planned as small tiles
+constexpr int kXs = NS * BK * 2;          // 4 KB: one plane of the token tile
+constexpr int kNbT = 4;                   // dequantised weight buffers in TMEM
+template <int MODE>
+struct CfgS {
+    static constexpr bool GU = MODE != 1;
+    static constexpr int X = MODE == 0 ? kXs : 2 * kXs;
+    static constexpr int Raw = 2 * kXs + kBq + kBs;  // 20 KB (1024-aligned) for every mode
+    static constexpr int NR = 8;
+    static constexpr int Smem = NR * Raw + 1024;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_sw(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ,
+              const __grid_constant__ CUtensorMap tmS, GemmArgs g) {
+    constexpr int NR = CfgS<MODE>::NR;
+    constexpr int kRaw = CfgS<MODE>::Raw;
+    constexpr bool kGU = CfgS<MODE>::GU;
+    constexpr bool kLo = MODE != 0;
+    constexpr int kN = kLo ? 2 * NS : NS;  // MMA N: token columns (hi, then lo)
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t raw_full[NR], raw_empty[NR], bf_full[kNbT], bf_empty[kNbT];
+    __shared__ uint64_t acc_full[2], acc_empty[2], drain;
+    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag_;
+    volatile int &abort_flag = abort_flag_;
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < NR; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], 1);
+        }
+        for (int b = 0; b < kNbT; ++b) {
+            mbar_init(&bf_full[b], kDeqWarps);
+            mbar_init(&bf_empty[b], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(&drain, 1);
+        abort_flag = 0;
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    const uint32_t tmem_w = tmem + 256;  // dequantised weight buffers
+    const int ntiles = *g.n_mtiles * g.NT;
+    const int KB = g.KB;
+
+    if (warp == 0) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            int it = 0;
+            int last_it[NR];
+            for (int s = 0; s < NR; ++s) last_it[s] = -1;
+            for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
+                const MTile mt = g.tiles[tile / g.NT];
+                const int nt = tile % g.NT;
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int s = it % NR;
+                    const uint32_t ph = (it / NR) & 1;
+                    if (!mbar_wait(&raw_empty[s], ph ^ 1)) {
+                        atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                        abort_flag = 1;
+                        break;
+                    }
+                    uint8_t *X = smem + s * kRaw;
+                    uint8_t *Bq = X + 2 * kXs, *Bs = Bq + kBq;
+                    mbar_expect_tx(&raw_full[s], CfgS<MODE>::X + kBq + (kGU ? 128 : 256) * 16);
+                    tma_load_2d(X, &tmX, kb * BK, mt.m0, &raw_full[s]);  // (hi)
+                    if (kLo) tma_load_2d(X + kXs, &tmX, kb * BK, g.rows_max + mt.m0, &raw_full[s]);
+                    if (kGU) {
+                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 128, mt.slot, &raw_full[s]);
+                        tma_load_3d(Bq + 128 * 32, &tmQ, g.d / 2 + kb * 32, nt * 128, mt.slot,
+                                    &raw_full[s]);
+                        tma_load_3d(Bs, &tmS, g.d + 16 * (kb >> 1), nt * 128, mt.slot, &raw_full[s]);
+                    } else {
+                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 256, mt.slot, &raw_full[s]);
+                        tma_load_3d(Bs, &tmS, g.I / 2 + 16 * (kb >> 2), nt * 256, mt.slot,
+                                    &raw_full[s]);
+                    }
+                    last_it[s] = it;
+                }
+            }
+            for (int s = 0; s < NR; ++s)
+                if (last_it[s] >= 0) mbar_wait(&raw_full[s], (last_it[s] / NR) & 1);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        const uint32_t idesc = idesc_f16(BM, kN);
+        int it = 0, lt = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
+            const int buf = lt & 1;
+            const uint32_t aph = (lt >> 1) & 1;
+            if (!mbar_wait(&acc_empty[buf], aph ^ 1)) {
+                if (lane == 0) {
+                    atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const uint32_t dt = tmem + buf * 128;
+            bool ok = true;
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                const int s = it % NR, b = it % kNbT;
+                const uint32_t ph = (it / NR) & 1, bph = (it / kNbT) & 1;
+                if (!mbar_wait(&raw_full[s], ph) || !mbar_wait(&bf_full[b], bph)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t x0 = smem_addr(smem + s * kRaw);
+                    const uint32_t w0 = tmem_w + b * 64;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t xd = sdesc_sw128(x0 + kk * 32);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                            umma_f16_ts(dt + h * 64, w0 + h * 32 + kk * 8, xd, idesc, (kb | kk) != 0);
+                    }
+                    umma_commit(&raw_empty[s]);
+                    umma_commit(&bf_empty[b]);
+                }
+                __syncwarp();
+            }
+            if (!ok) {
+                if (lane == 0) {
+                    atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            if (lane == 0) umma_commit(&acc_full[buf]);
+            __syncwarp();
+        }
+        if (lane == 0) {
+            umma_commit(&drain);
+            mbar_wait(&drain, 0);
+        }
+        __syncwarp();
+    } else if (warp < 2 + kDeqWarps) {
+        // ---------------- dequantisers: weight row r of the 256-row tile =
+        // TMEM lane 32 q + lane of half h (warp w reaches lanes 32 (w % 4)..)
+        const int q = warp & 3, h = (warp - 2) >> 2;
+        const int r = h * 128 + 32 * q + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
+            bool ok = true;
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                const int s = it % NR, b = it % kNbT;
+                const uint32_t ph = (it / NR) & 1, bph = (it / kNbT) & 1;
+                if (!mbar_wait(&raw_full[s], ph) || !mbar_wait(&bf_empty[b], bph ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *Bq = smem + s * kRaw + 2 * kXs, *Bs = Bq + kBq;
+                uint32_t sb;
+                if (kGU) {
+                    const uint2 quad = *reinterpret_cast<const uint2 *>(Bs + (r & 127) * 16 + 8 * (kb & 1));
+                    sb = h == 0 ? quad.x : quad.y;
+                } else {
+                    sb = *reinterpret_cast<const uint32_t *>(Bs + r * 16 + 4 * (kb & 3));
+                }
+                const uint4 qa = *reinterpret_cast<const uint4 *>(Bq + r * 32);
+                const uint4 qb = *reinterpret_cast<const uint4 *>(Bq + r * 32 + 16);
+                const __half2 s2 = __float2half2_rn(bf16lo(sb)), b2 = __float2half2_rn(bf16hi(sb));
+                const uint32_t wd[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                uint32_t v[32];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint4 o = dequant_word(wd[c], s2, b2);
+                    v[4 * c] = o.x;
+                    v[4 * c + 1] = o.y;
+                    v[4 * c + 2] = o.z;
+                    v[4 * c + 3] = o.w;
+                }
+                tc_fence_after();  // the MMAs that read this buffer before have completed
+                tmem_st32(tmem_w + lane_off + b * 64 + h * 32, v);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bf_full[b]);
+            }
+            if (!ok) {
+                if (lane == 0) {
+                    atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                    abort_flag = 1;
+                }
+                break;
+            }
+        }
+    } else {
+        // ---------------- epilogue: thread = weight row 32q + lane of each
+        // half; token columns c (hi) and NS + c (lo)
+        const int q = warp & 3;
+        const int wr = 32 * q + lane;
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
+            const MTile mt = g.tiles[tile / g.NT];
+            const int nt = tile % g.NT;
+            const int buf = lt & 1;
+            const uint32_t aph = (lt >> 1) & 1;
+            if (!mbar_wait(&acc_full[buf], aph)) {
+                if (lane == 0) {
+                    atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tb = tmem + (static_cast<uint32_t>(32 * q) << 16) + buf * 128;
+            float v0[NS], v1[NS];
+            tmem_ld16(tb, v0);
+            tmem_ld16(tb + 16, v0 + 16);
+            tmem_ld16(tb + 64, v1);
+            tmem_ld16(tb + 64 + 16, v1 + 16);
+            tmem_wait_ld();
+            if (kLo) {
+                float l0[NS], l1[NS];
+                tmem_ld16(tb + NS, l0);
+                tmem_ld16(tb + NS + 16, l0 + 16);
+                tmem_ld16(tb + 64 + NS, l1);
+                tmem_ld16(tb + 64 + NS + 16, l1 + 16);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < NS; ++c) {
+                    v0[c] += l0[c];
+                    v1[c] += l1[c];
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);  // TMEM free: values are in registers
+            if (kGU) {
+                // H[token][f], f = nt*128 + wr, fp16 hi/lo at the chunk
+                // position of f ([0,4,1,5,2,6,3,7] inside 8-element chunks)
+                const int f = nt * 128 + wr, j = f & 7;
+                const int col = (f & ~7) + (j < 4 ? 2 * j : 2 * (j - 4) + 1);
+#pragma unroll
+                for (int c = 0; c < NS; ++c) {
+                    if (c < mt.rows) {
+                        const float gv = v0[c], uv = v1[c];
+                        const float hv = (gv / (1.0f + expf(-gv))) * uv;
+                        const __half hi = __float2half_rn(hv);
+                        const __half lo = __float2half_rn(hv - __half2float(hi));
+                        __half *orow = g.out + static_cast<size_t>(mt.m0 + c) * g.ld_out + col;
+                        orow[0] = hi;
+                        orow[g.lo_plane] = lo;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < NS; ++c) {
+                    if (c < mt.rows) {
+                        float *orow = g.outf + static_cast<size_t>(mt.m0 + c) * g.ld_out + nt * 256;
+                        orow[wr] = v0[c];
+                        orow[128 + wr] = v1[c];
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // routing -> groups
 
 // Slots with a negative expert id (owned by another rank) are skipped. Lanes
@@ -451,27 +749,35 @@ __global__ void k_count(const int32_t *idx, int nk, int *counts) {
 
 // One CTA (1024 threads, E + 1 <= 1024 groups). Group 0 is the shared expert
 // (rows [0, nsh): every token, or none); group 1 + e is routed expert e.
-// Writes the first row of each routed expert and the M-tile list.
+// Writes the first row of each routed expert and two tile lists: groups of
+// at most small_max rows as NS-row tiles for k_gemm_sw (stiles), larger
+// groups as BM-row tiles for k_gemm (tiles).
 __global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh,
                                                const int32_t *slot_of, int shared_slot,
-                                               int *row0, MTile *tiles, int *n_mtiles,
+                                               int small_max, int *row0, MTile *tiles,
+                                               int *n_mtiles, MTile *stiles, int *n_stiles,
                                                int *n_rows) {
-    __shared__ int s_scan[1024], s_tscan[1024];
+    __shared__ int s_scan[1024], s_tscan[1024], s_sscan[1024];
     const int g = threadIdx.x;
     const int rows = g == 0 ? nsh : (g <= E ? counts[g - 1] : 0);
-    const int mt = (rows + BM - 1) / BM;
+    const bool small = rows <= small_max;
+    const int mt = small ? 0 : (rows + BM - 1) / BM;
+    const int st = small ? (rows + NS - 1) / NS : 0;
     s_scan[g] = rows;
     s_tscan[g] = mt;
+    s_sscan[g] = st;
     __syncthreads();
     for (int off = 1; off < 1024; off <<= 1) {
         const int a = g >= off ? s_scan[g - off] : 0;
         const int b = g >= off ? s_tscan[g - off] : 0;
+        const int c = g >= off ? s_sscan[g - off] : 0;
         __syncthreads();
         s_scan[g] += a;
         s_tscan[g] += b;
+        s_sscan[g] += c;
         __syncthreads();
     }
-    const int r0 = s_scan[g] - rows, t0 = s_tscan[g] - mt;
+    const int r0 = s_scan[g] - rows, t0 = s_tscan[g] - mt, u0 = s_sscan[g] - st;
     if (g >= 1 && g <= E) row0[g - 1] = r0;
     const int slot = g == 0 ? shared_slot : (g <= E ? slot_of[g - 1] : -1);
     for (int i = 0; i < mt; ++i) {
@@ -482,8 +788,17 @@ __global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh
         m.pad = 0;
         tiles[t0 + i] = m;
     }
+    for (int i = 0; i < st; ++i) {
+        MTile m;
+        m.m0 = r0 + NS * i;
+        m.rows = min(NS, rows - NS * i);
+        m.slot = slot;
+        m.pad = 0;
+        stiles[u0 + i] = m;
+    }
     if (g == 1023) {
         *n_mtiles = s_tscan[1023];
+        *n_stiles = s_sscan[1023];
         *n_rows = s_scan[1023];
     }
 }
@@ -1020,11 +1335,13 @@ bool map_3d_u8(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t ro
 struct qk_prefill {
     qk_layout L;
     int max_tokens, num_sms, pool_slots, rows_max, tiles_max;
-    int *counts, *cursor, *row0, *inv, *perm_tok, *n_mtiles, *n_rows;
-    MTile *tiles;
+    int small_max;                  // groups of at most this many rows use k_gemm_sw
+    int *counts, *cursor, *row0, *inv, *perm_tok, *n_mtiles, *n_stiles, *n_rows;
+    MTile *tiles, *stiles;          // BM-row tiles (k_gemm), NS-row tiles (k_gemm_sw)
     __half *xp, *H;
     float *Y;
     CUtensorMap tmX, tmH, tmQgu, tmSgu, tmQdn, tmSdn;
+    CUtensorMap tmXs, tmHs;         // the same planes in NS-row boxes
     // routing: x as a bf16 pair [2 * Tpad, d], token norms, approximate
     // logits [max_tokens, E], the router's M-tile list
     int route_ok, Tpad;
@@ -1050,8 +1367,10 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->inv);
     cudaFree(p->perm_tok);
     cudaFree(p->n_mtiles);
+    cudaFree(p->n_stiles);
     cudaFree(p->n_rows);
     cudaFree(p->tiles);
+    cudaFree(p->stiles);
     cudaFree(p->xp);
     cudaFree(p->H);
     cudaFree(p->Y);
@@ -1090,6 +1409,12 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     p->num_sms = num_sms;
     p->pool_slots = pool_slots;
     p->rows_max = max_tokens * (L->k + 1);
+    // tuning knob: QMOE_GROUP_SMALL_ROWS in [0, 64] (0: k_gemm_sw never used)
+    p->small_max = kSmallMax;
+    if (const char *v = getenv("QMOE_GROUP_SMALL_ROWS")) {
+        const int n = atoi(v);
+        if (n >= 0 && n <= kSmallMax) p->small_max = n;
+    }
     p->tiles_max = p->rows_max / BM + L->E + 2;
     const size_t R = static_cast<size_t>(p->rows_max);
     cudaError_t e = cudaSuccess;
@@ -1099,8 +1424,11 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     if (e == cudaSuccess) e = cudaMalloc(&p->inv, sizeof(int) * static_cast<size_t>(max_tokens) * L->k);
     if (e == cudaSuccess) e = cudaMalloc(&p->perm_tok, sizeof(int) * R);
     if (e == cudaSuccess) e = cudaMalloc(&p->n_mtiles, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&p->n_stiles, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&p->n_rows, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&p->tiles, sizeof(MTile) * p->tiles_max);
+    // groups of at most kSmallMax rows: at most kSmallMax / NS tiles each
+    if (e == cudaSuccess) e = cudaMalloc(&p->stiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
     if (e == cudaSuccess) e = cudaMalloc(&p->xp, 2 * R * L->d * sizeof(__half));  // hi, lo planes
     if (e == cudaSuccess) e = cudaMalloc(&p->H, 2 * R * L->I * sizeof(__half));  // hi, lo planes
     if (e == cudaSuccess) e = cudaMalloc(&p->Y, R * L->d * sizeof(float));
@@ -1111,6 +1439,8 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     }
     bool ok = map_2d_16(&p->tmX, p->xp, L->d, 2 * R, false) &&
               map_2d_16(&p->tmH, p->H, L->I, 2 * R, false) &&
+              map_2d_16(&p->tmXs, p->xp, L->d, 2 * R, false, NS) &&
+              map_2d_16(&p->tmHs, p->H, L->I, 2 * R, false, NS) &&
               map_3d_u8(&p->tmQgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 32, 128) &&
               map_3d_u8(&p->tmSgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 16, 128) &&
               map_3d_u8(&p->tmQdn, pool + L->gu_bytes, L->d_row, L->d, pool_slots, L->slot_bytes, 32,
@@ -1144,14 +1474,17 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
         p->route_ok = map_2d_16(&p->tmXr, p->xr, L->d, 2 * Tp, true) &&
                       map_2d_16(&probe, p->xr, L->d, L->E, true, 256);
     }
-    const void *fns[5] = {reinterpret_cast<const void *>(&k_gemm<0>),
+    const void *fns[8] = {reinterpret_cast<const void *>(&k_gemm<0>),
                           reinterpret_cast<const void *>(&k_gemm<1>),
                           reinterpret_cast<const void *>(&k_gemm<3>),
+                          reinterpret_cast<const void *>(&k_gemm_sw<0>),
+                          reinterpret_cast<const void *>(&k_gemm_sw<1>),
+                          reinterpret_cast<const void *>(&k_gemm_sw<3>),
                           reinterpret_cast<const void *>(&k_gemm<2>),
                           reinterpret_cast<const void *>(&k_route_exact)};
-    const int smem[5] = {Cfg<0>::Smem, Cfg<1>::Smem, Cfg<3>::Smem, Cfg<2>::Smem,
-                         static_cast<int>(p->route_smem)};
-    for (int i = 0; i < (p->route_ok ? 5 : 3); ++i) {
+    const int smem[8] = {Cfg<0>::Smem, Cfg<1>::Smem, Cfg<3>::Smem, CfgS<0>::Smem, CfgS<1>::Smem,
+                         CfgS<3>::Smem, Cfg<2>::Smem, static_cast<int>(p->route_smem)};
+    for (int i = 0; i < (p->route_ok ? 8 : 6); ++i) {
         e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem[i]);
         if (e != cudaSuccess) {
             snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
@@ -1171,8 +1504,8 @@ namespace {
 // (token, slot) in p->inv. events: NULL or 3 events (after grouping+gather,
 // gate/up, down).
 cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32_t *idx, int k,
-                    int nsh, const int32_t *slot_of, int shared_slot_index, int *err,
-                    cudaStream_t st, void **events) {
+                    int nsh, int routed_max, const int32_t *slot_of, int shared_slot_index,
+                    int *err, cudaStream_t st, void **events) {
     const qk_layout &L = p->L;
     const int E = L.E;
     const int nk = T * k;
@@ -1182,12 +1515,18 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         if (events) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), st,
                                              cudaEventRecordExternal);
     };
+    // No group can exceed the small-tile limit (each token is in a group at
+    // most once): every group runs on k_gemm_sw and k_gemm is not launched.
+    // Otherwise every group runs on k_gemm (a second, small-tile launch
+    // beside it measured slower on the prefill workload).
+    const bool all_small = nsh <= p->small_max && routed_max <= p->small_max;
     // counts and cursors in one allocation, cleared together
     cudaError_t e = cudaMemsetAsync(p->counts, 0, sizeof(int) * 2 * (E + 1), st);
     if (e != cudaSuccess) return e;
     if (nk > 0) k_count<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, p->counts);
-    k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index, p->row0, p->tiles,
-                               p->n_mtiles, p->n_rows);
+    k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index,
+                               all_small ? p->small_max : 0, p->row0, p->tiles, p->n_mtiles,
+                               p->stiles, p->n_stiles, p->n_rows);
     if (nk > 0)
         k_place<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, k, p->row0, p->cursor, p->inv,
                                                  p->perm_tok);
@@ -1198,10 +1537,11 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     mark(0);
+    const bool lo = x_kind == XK_F32;  // x as an fp16 hi/lo pair
 
     GemmArgs gu;
     memset(&gu, 0, sizeof(gu));
-    gu.mode = x_kind == XK_F32 ? 3 : 0;
+    gu.mode = lo ? 3 : 0;
     gu.KB = L.d / BK;
     gu.NT = L.I / 128;
     gu.ld_out = L.I;
@@ -1215,13 +1555,27 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     gu.out = p->H;
     gu.outf = nullptr;
     gu.err = err;
-    {
-        void *args[] = {&p->tmX, &p->tmQgu, &p->tmSgu, &gu};
-        e = x_kind == XK_F32
-                ? qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<3>), dim3(p->num_sms),
-                                dim3(kThreads), Cfg<3>::Smem, st, 0, args)
-                : qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<0>), dim3(p->num_sms),
-                                dim3(kThreads), Cfg<0>::Smem, st, 0, args);
+    GemmArgs gus = gu;
+    gus.tiles = p->stiles;
+    gus.n_mtiles = p->n_stiles;
+    auto launch = [&](const void *fn, int smem, const CUtensorMap *a, const CUtensorMap *q,
+                      const CUtensorMap *sc, GemmArgs *ga) {
+        void *args[] = {const_cast<CUtensorMap *>(a), const_cast<CUtensorMap *>(q),
+                        const_cast<CUtensorMap *>(sc), ga};
+        return qk_launch_raw(fn, dim3(p->num_sms), dim3(kThreads), smem, st, 0, args);
+    };
+    if (!all_small) {
+        e = lo ? launch(reinterpret_cast<const void *>(&k_gemm<3>), Cfg<3>::Smem, &p->tmX,
+                        &p->tmQgu, &p->tmSgu, &gu)
+               : launch(reinterpret_cast<const void *>(&k_gemm<0>), Cfg<0>::Smem, &p->tmX,
+                        &p->tmQgu, &p->tmSgu, &gu);
+        if (e != cudaSuccess) return e;
+    }
+    if (all_small) {
+        e = lo ? launch(reinterpret_cast<const void *>(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs,
+                        &p->tmQgu, &p->tmSgu, &gus)
+               : launch(reinterpret_cast<const void *>(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs,
+                        &p->tmQgu, &p->tmSgu, &gus);
         if (e != cudaSuccess) return e;
     }
     mark(1);
@@ -1233,10 +1587,17 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     dn.n_cols = L.d;
     dn.out = nullptr;
     dn.outf = p->Y;
-    {
-        void *args[] = {&p->tmH, &p->tmQdn, &p->tmSdn, &dn};
-        e = qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<1>), dim3(p->num_sms),
-                          dim3(kThreads), Cfg<1>::Smem, st, 0, args);
+    GemmArgs dns = dn;
+    dns.tiles = p->stiles;
+    dns.n_mtiles = p->n_stiles;
+    if (!all_small) {
+        e = launch(reinterpret_cast<const void *>(&k_gemm<1>), Cfg<1>::Smem, &p->tmH, &p->tmQdn,
+                   &p->tmSdn, &dn);
+        if (e != cudaSuccess) return e;
+    }
+    if (all_small) {
+        e = launch(reinterpret_cast<const void *>(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs,
+                   &p->tmQdn, &p->tmSdn, &dns);
         if (e != cudaSuccess) return e;
     }
     mark(2);
@@ -1252,7 +1613,7 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     if (T > p->max_tokens) return cudaErrorInvalidValue;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // diagnostics: events[0..3] bracket grouping+gather, gate/up, down, combine
-    cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, k, T, f->slot_of,
+    cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, k, T, T, f->slot_of,
                             shared_slot_index, f->err, st, events);
     if (e != cudaSuccess) return e;
     k_combine<<<T, 256, 0, st>>>(p->Y, p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
@@ -1318,7 +1679,7 @@ extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int shared_slot_ind
     // one grouped pass: the own tokens through the shared expert (rows
     // [0, T)), the received rows through this rank's experts
     cudaError_t e = grouped(p, p->ep_recv_x, f->x_bf16 ? XK_BF16 : XK_F32, T + rows, p->ep_recv_e,
-                            L.k, T, f->slot_of, shared_slot_index, f->err, st, nullptr);
+                            L.k, T, rows, f->slot_of, shared_slot_index, f->err, st, nullptr);
     if (e != cudaSuccess) return e;
     k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv + static_cast<size_t>(T) * L.k,
                                        p->ep_recv_e + static_cast<size_t>(T) * L.k,
