@@ -93,6 +93,7 @@ struct MTile {
 struct GemmArgs {
     int mode;   // 0: gate/up, 1: down, 2: router
     int KB;     // K / 64
+    int ksplit; // router only: K split over this many tiles (0 or 1: none)
     int NT;     // N-tiles per M-tile
     int ld_out; // output row length (elements)
     int n_cols; // fp32 outputs: columns that exist (a multiple of 16)
@@ -199,8 +200,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base;
-    const int ntiles = *g.n_mtiles * g.NT;
-    const int KB = g.KB;
+    // the router (MODE 2) may split K over KS tiles that add into zeroed outputs
+    const int KS = (MODE == 2 && g.ksplit > 1) ? g.ksplit : 1;
+    const int ntiles = *g.n_mtiles * g.NT * KS;
+    const int KB = g.KB / KS;
 
     if (warp == 0) {
         // ---------------- TMA producer: the raw ring
@@ -209,9 +212,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             int last_it[kMaxNR];
             for (int s = 0; s < NR; ++s) last_it[s] = -1;
             for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
-                const MTile mt = g.tiles[tile / g.NT];
-                const int nt = tile % g.NT;
-                for (int kb = 0; kb < KB; ++kb, ++it) {
+                const MTile mt = g.tiles[tile / (g.NT * KS)];
+                const int nt = (tile / KS) % g.NT;
+                const int kb0 = (tile % KS) * KB;
+                for (int kb = kb0; kb < kb0 + KB; ++kb, ++it) {
                     const int s = it % NR;
                     const uint32_t ph = (it / NR) & 1;
                     if (!mbar_wait(&raw_empty[s], ph ^ 1)) {
@@ -267,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t dt = tmem + buf * BN;
             bool ok = true;
-            for (int kb = 0; kb < KB; ++kb, ++it) {
+            for (int kb = 0; kb < KB; ++kb, ++it) {  // (kb counts from the split's first step)
                 const int s = it % NR, b = it & 1;
                 const uint32_t ph = (it / NR) & 1, bph = (it >> 1) & 1;
                 if (!mbar_wait(&raw_full[s], ph) || (kDeq && !mbar_wait(&bf_full[b], bph))) {
@@ -353,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = 32 * q + lane;
         int lt = 0;
         for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
-            const MTile mt = g.tiles[tile / g.NT];
-            const int nt = tile % g.NT;
+            const MTile mt = g.tiles[tile / (g.NT * KS)];
+            const int nt = (tile / KS) % g.NT;
             const int buf = lt & 1;
             const uint32_t aph = (lt >> 1) & 1;
             if (!mbar_wait(&acc_full[buf], aph)) {
@@ -413,9 +417,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int r = 4 * i + (lane >> 3), j = lane & 7;
                         const int col = nt * 256 + c + 4 * j;
                         const float4 v = stg[r * 8 + (j ^ (r & 7))];
-                        if (32 * q + r < mt.rows && col < g.n_cols)
-                            *reinterpret_cast<float4 *>(
-                                g.outf + static_cast<size_t>(mt.m0 + 32 * q + r) * g.ld_out + col) = v;
+                        if (32 * q + r < mt.rows && col < g.n_cols) {
+                            float *o = g.outf + static_cast<size_t>(mt.m0 + 32 * q + r) * g.ld_out + col;
+                            if (KS > 1) {
+                                atomicAdd(o, v.x);
+                                atomicAdd(o + 1, v.y);
+                                atomicAdd(o + 2, v.z);
+                                atomicAdd(o + 3, v.w);
+                            } else {
+                                *reinterpret_cast<float4 *>(o) = v;
+                            }
+                        }
                     }
                     __syncwarp();
                 }
@@ -803,6 +815,78 @@ __global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh
     }
 }
 
+// Small calls (at most kPlanSmall slots): counting, planning and placing in
+// one CTA, the counters in shared memory (k_count + k_plan + k_place in one
+// launch). Same tile lists and row layout as those three.
+constexpr int kPlanSmall = 4096;
+__global__ void __launch_bounds__(1024) k_plan_small(const int32_t *idx, int nk, int k, int E,
+                                                     int nsh, const int32_t *slot_of,
+                                                     int shared_slot, int small_max, MTile *tiles,
+                                                     int *n_mtiles, MTile *stiles, int *n_stiles,
+                                                     int *n_rows, int *inv, int *perm_tok) {
+    __shared__ int s_cnt[1024], s_scan[1024], s_tscan[1024], s_sscan[1024], s_row0[1024];
+    const int g = threadIdx.x;
+    s_cnt[g] = 0;
+    __syncthreads();
+    for (int a = g; a < nk; a += 1024) {
+        const int e = idx[a];
+        if (e >= 0) atomicAdd(&s_cnt[e], 1);
+    }
+    __syncthreads();
+    const int rows = g == 0 ? nsh : (g <= E ? s_cnt[g - 1] : 0);
+    const bool small = rows <= small_max;
+    const int mt = small ? 0 : (rows + BM - 1) / BM;
+    const int st = small ? (rows + NS - 1) / NS : 0;
+    s_scan[g] = rows;
+    s_tscan[g] = mt;
+    s_sscan[g] = st;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+        const int a = g >= off ? s_scan[g - off] : 0;
+        const int b = g >= off ? s_tscan[g - off] : 0;
+        const int c = g >= off ? s_sscan[g - off] : 0;
+        __syncthreads();
+        s_scan[g] += a;
+        s_tscan[g] += b;
+        s_sscan[g] += c;
+        __syncthreads();
+    }
+    const int r0 = s_scan[g] - rows, t0 = s_tscan[g] - mt, u0 = s_sscan[g] - st;
+    s_row0[g] = r0;
+    const int slot = g == 0 ? shared_slot : (g <= E ? slot_of[g - 1] : -1);
+    for (int i = 0; i < mt; ++i) {
+        MTile m;
+        m.m0 = r0 + BM * i;
+        m.rows = min(BM, rows - BM * i);
+        m.slot = slot;
+        m.pad = 0;
+        tiles[t0 + i] = m;
+    }
+    for (int i = 0; i < st; ++i) {
+        MTile m;
+        m.m0 = r0 + NS * i;
+        m.rows = min(NS, rows - NS * i);
+        m.slot = slot;
+        m.pad = 0;
+        stiles[u0 + i] = m;
+    }
+    if (g == 1023) {
+        *n_mtiles = s_tscan[1023];
+        *n_stiles = s_sscan[1023];
+        *n_rows = s_scan[1023];
+    }
+    s_cnt[g] = 0;  // now the placement cursors
+    __syncthreads();
+    for (int a = g; a < nk; a += 1024) {
+        const int e = idx[a];
+        if (e >= 0) {
+            const int pos = s_row0[e + 1] + atomicAdd(&s_cnt[e], 1);
+            inv[a] = pos;
+            perm_tok[pos] = a / k;
+        }
+    }
+}
+
 // Row of each (token, slot) within its expert's group: row0[e] plus a place
 // taken from the expert's cursor (warp-aggregated atomics). The order of the
 // rows inside a group varies from call to call, the results do not: every
@@ -1046,7 +1130,9 @@ __global__ void k_ep_final(const float *back, const unsigned long long *mask, in
 // whose candidate set exceeds 32, or with a non-finite value, gets every
 // logit exactly instead (the one-warp path of k_topk).
 
-constexpr int kRW = 4;  // warps per token (CTA) of k_route_exact
+// warps per token (CTA) of k_route_exact: 4 at prefill sizes, 16 for small
+// calls (fewer tokens than SMs: the candidates' dots run in parallel)
+constexpr int kRW = 4, kRWsmall = 16;
 
 __global__ void k_route_split(const void *x, int x_bf16, int d, int T, int Tpad,
                               __nv_bfloat16 *xr, float *xnorm, MTile *tiles, int *n_mtiles) {
@@ -1165,6 +1251,7 @@ QK_DEV float exact_logit(const RouteArgs &a, const double2 *xs, int e, int lane)
 // doubles, then E keys. Warp 0 finds the candidate set; the candidates'
 // canonical logits are spread over the warps (each dot is a chain of L2
 // loads, so several in flight per token matter); warp 0 ranks them.
+template <int kRW>
 __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
     extern __shared__ __align__(16) float rsm[];
     __shared__ uint32_t s_key[32];
@@ -1474,17 +1561,19 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
         p->route_ok = map_2d_16(&p->tmXr, p->xr, L->d, 2 * Tp, true) &&
                       map_2d_16(&probe, p->xr, L->d, L->E, true, 256);
     }
-    const void *fns[8] = {reinterpret_cast<const void *>(&k_gemm<0>),
+    const void *fns[9] = {reinterpret_cast<const void *>(&k_gemm<0>),
                           reinterpret_cast<const void *>(&k_gemm<1>),
                           reinterpret_cast<const void *>(&k_gemm<3>),
                           reinterpret_cast<const void *>(&k_gemm_sw<0>),
                           reinterpret_cast<const void *>(&k_gemm_sw<1>),
                           reinterpret_cast<const void *>(&k_gemm_sw<3>),
                           reinterpret_cast<const void *>(&k_gemm<2>),
-                          reinterpret_cast<const void *>(&k_route_exact)};
-    const int smem[8] = {Cfg<0>::Smem, Cfg<1>::Smem, Cfg<3>::Smem, CfgS<0>::Smem, CfgS<1>::Smem,
-                         CfgS<3>::Smem, Cfg<2>::Smem, static_cast<int>(p->route_smem)};
-    for (int i = 0; i < (p->route_ok ? 8 : 6); ++i) {
+                          reinterpret_cast<const void *>(&k_route_exact<kRW>),
+                          reinterpret_cast<const void *>(&k_route_exact<kRWsmall>)};
+    const int smem[9] = {Cfg<0>::Smem, Cfg<1>::Smem, Cfg<3>::Smem, CfgS<0>::Smem, CfgS<1>::Smem,
+                         CfgS<3>::Smem, Cfg<2>::Smem, static_cast<int>(p->route_smem),
+                         static_cast<int>(p->route_smem)};
+    for (int i = 0; i < (p->route_ok ? 9 : 6); ++i) {
         e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem[i]);
         if (e != cudaSuccess) {
             snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
@@ -1520,16 +1609,22 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     // Otherwise every group runs on k_gemm (a second, small-tile launch
     // beside it measured slower on the prefill workload).
     const bool all_small = nsh <= p->small_max && routed_max <= p->small_max;
-    // counts and cursors in one allocation, cleared together
-    cudaError_t e = cudaMemsetAsync(p->counts, 0, sizeof(int) * 2 * (E + 1), st);
-    if (e != cudaSuccess) return e;
-    if (nk > 0) k_count<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, p->counts);
-    k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index,
-                               all_small ? p->small_max : 0, p->row0, p->tiles, p->n_mtiles,
-                               p->stiles, p->n_stiles, p->n_rows);
-    if (nk > 0)
+    cudaError_t e = cudaSuccess;
+    if (nk <= kPlanSmall) {
+        k_plan_small<<<1, 1024, 0, st>>>(idx, nk, k, E, nsh, slot_of, shared_slot_index,
+                                         all_small ? p->small_max : 0, p->tiles, p->n_mtiles,
+                                         p->stiles, p->n_stiles, p->n_rows, p->inv, p->perm_tok);
+    } else {
+        // counts and cursors in one allocation, cleared together
+        e = cudaMemsetAsync(p->counts, 0, sizeof(int) * 2 * (E + 1), st);
+        if (e != cudaSuccess) return e;
+        k_count<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, p->counts);
+        k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index,
+                                   all_small ? p->small_max : 0, p->row0, p->tiles, p->n_mtiles,
+                                   p->stiles, p->n_stiles, p->n_rows);
         k_place<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, k, p->row0, p->cursor, p->inv,
                                                  p->perm_tok);
+    }
     if (rows > 0)
         k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->n_rows,
                                                          p->perm_tok, p->xp,
@@ -1726,7 +1821,18 @@ extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void 
     ra.rows_max = p->Tpad;
     ra.outf = p->lga;
     ra.err = f->err;
-    const int ntiles = (T + BM - 1) / BM * ra.NT;
+    // small calls: split K so that more SMs share the router's 2 MiB (the
+    // approximate logits then add up in a different order, which the bound
+    // below allows: any order of the same fp32 additions stays within it)
+    int ks = 1;
+    if (T <= 512)
+        while (ks * 2 <= ra.KB / 2 && (T + BM - 1) / BM * ra.NT * ks * 2 <= p->num_sms) ks *= 2;
+    ra.ksplit = ks;
+    if (ks > 1) {
+        e = cudaMemsetAsync(p->lga, 0, sizeof(float) * static_cast<size_t>(T) * E, st);
+        if (e != cudaSuccess) return e;
+    }
+    const int ntiles = (T + BM - 1) / BM * ra.NT * ks;
     {
         void *args[] = {&p->tmXr, &tmR, &tmR, &ra};
         e = qk_launch_raw(reinterpret_cast<const void *>(&k_gemm<2>),
@@ -1752,6 +1858,9 @@ extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void 
     a.wts = f->wts;
     a.sgate = f->sgate;
     a.err = f->err;
-    k_route_exact<<<T, kRW * 32, p->route_smem, st>>>(a);
+    if (T < p->num_sms)
+        k_route_exact<kRWsmall><<<T, kRWsmall * 32, p->route_smem, st>>>(a);
+    else
+        k_route_exact<kRW><<<T, kRW * 32, p->route_smem, st>>>(a);
     return cudaGetLastError();
 }
