@@ -575,22 +575,40 @@ def main():
     ref4 = np.concatenate([ctx.forward(0, x_host[t:t + 1]) for t in range(TOKENS - 4, TOKENS)])
     parity_ok = bool(np.array_equal(out_last, ref4))
 
-    # e2e through the host-pointer C ABI: copies in and out on every call
+    # e2e through the host-pointer C ABI (qmoe_forward: x read from host
+    # memory, out written to host memory, on every call), one call per token
+    # made from C as the reference's C caller makes them (qmoe__forward_tokens
+    # loops over qmoe_forward); the same loop from Python beside it
+    import ctypes as C
+    loop = qmoe.lib().qmoe__forward_tokens
+    loop.restype = C.c_int
+    loop.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
     e2e_steps = max(1, min(args.steps, 3))
-    out_h = np.empty((1, D), np.float32)
-    for t in range(16):
-        ctx.forward(0, x_host[t:t + 1])
+    out_all = np.empty((TOKENS, D), np.float32)
+    xh = np.ascontiguousarray(x_host, np.float32)
+    errb = qmoe.Err()
+    if loop(ctx.h, 0, xh.ctypes.data, 16, out_all.ctypes.data, C.byref(errb)) != 0:
+        raise RuntimeError(errb.text())
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        for t in range(TOKENS):
-            out_h[:] = ctx.forward(0, x_host[t:t + 1])
+        if loop(ctx.h, 0, xh.ctypes.data, TOKENS, out_all.ctypes.data, C.byref(errb)) != 0:
+            raise RuntimeError(errb.text())
     e2e_s = time.perf_counter() - t0
+    e2e_parity = bool(np.array_equal(out_all[TOKENS - 4:], out_last))
+    out_h = np.empty((1, D), np.float32)
+    for t in range(16):
+        ctx.forward(0, x_host[t:t + 1])
+    t0 = time.perf_counter()
+    for t in range(TOKENS):
+        out_h[:] = ctx.forward(0, x_host[t:t + 1])
+    py_s = time.perf_counter() - t0
     if world > 1:
-        tt = torch.tensor([e2e_s], device="cuda")
+        tt = torch.tensor([e2e_s, py_s], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_s = float(tt.item())
+        e2e_s, py_s = float(tt[0]), float(tt[1])
     e2e = world * e2e_steps * TOKENS / e2e_s
+    e2e_py = world * TOKENS / py_s
 
     # per-kernel event timing (separate pass, one token replayed as a graph
     # with events between its kernels) -> roofline of the dominant kernel
@@ -647,7 +665,9 @@ def main():
                        "l2": "inputs larger than L2: 906 MB of experts per layer vs 126 MB L2; "
                              "router and shared expert (3.9 MB) stay L2-resident across tokens"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": TOKENS * D * 4,
-                    "d2h_bytes_per_step": TOKENS * (D * 4 + 4)},
+                    "d2h_bytes_per_step": TOKENS * (D * 4 + 8),
+                    "caller": "C loop over qmoe_forward (host buffers), one call per token",
+                    "python_loop_value": e2e_py, "outputs_equal_graph": e2e_parity},
             "gpu_launches": len(names) * TOKENS * args.steps,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,

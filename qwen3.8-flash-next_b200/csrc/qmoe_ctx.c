@@ -53,6 +53,10 @@ struct qmoe_ctx {
     uint8_t *io_dev, *io_pin;
     int *err_dev;
     int *err_host;
+    /* single-token host calls: completions counted by the report kernel at
+     * io + 4 (device counter, pinned mirror); tok_seq = the count expected */
+    unsigned *tok_ctr_dev, *tok_ctr_host;
+    unsigned tok_seq;
     void *dsync;     /* launch counter + exchange area of the single-launch decode kernel */
     layer_dev *layers;
     /* expert pool */
@@ -347,8 +351,11 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
         CK(cudaMalloc((void **)&c->io_dev, io));
         CK(cudaMemset(c->io_dev, 0, 256));
         CK(cudaMallocHost((void **)&c->io_pin, io));
+        memset(c->io_pin, 0, 256);
         c->err_dev = (int *)c->io_dev;
         c->err_host = (int *)c->io_pin;
+        c->tok_ctr_dev = (unsigned *)(c->io_dev + 4);
+        c->tok_ctr_host = (unsigned *)(c->io_pin + 4);
         c->out_dev = (float *)(c->io_dev + 256);
         c->out_pin = (float *)(c->io_pin + 256);
     }
@@ -998,6 +1005,18 @@ void qmoe_graph_free(qmoe_graph *g) {
 /* Diagnostics (not in the public header): one single-token forward through the
  * single-launch kernel with per-CTA phase timestamps; out_ns receives
  * [grid][16] %globaltimer values. Returns the grid size, or -1. */
+/* Diagnostics (not in the public header): n_tokens single-token qmoe_forward
+ * calls made from C, token t from x + t d into out + t d, as the reference's
+ * C caller makes them (one moe_forward per token). */
+int qmoe__forward_tokens(qmoe_ctx *c, int layer, const float *x, int n_tokens, float *out,
+                         qmoe_err *err) {
+    if (!c || n_tokens < 0) return -1;
+    const size_t d = (size_t)c->L.d;
+    for (int t = 0; t < n_tokens; t++)
+        if (qmoe_forward(c, layer, x + (size_t)t * d, 1, out + (size_t)t * d, err)) return -1;
+    return 0;
+}
+
 int qmoe__phase_times(qmoe_ctx *c, int layer, const void *x, int x_dtype, float *out,
                       unsigned long long *out_ns, int max_ctas) {
     if (!c || !c->resident_all || !c->layers[layer].ready) return -1;
@@ -1125,7 +1144,8 @@ int qmoe_forward(qmoe_ctx *c, int layer, const float *x, int n, float *out, qmoe
                 int rc = qk_launch_copy_in(c->x_pin, c->x_dev, bytes, c->stream) ||
                          qmoe_forward_dev(c, layer, c->x_dev, QMOE_F32, n, c->out_pin, c->stream,
                                           err) ||
-                         qk_launch_report(c->err_dev, c->err_host, c->stream);
+                         qk_launch_report(c->err_dev, c->err_host, c->tok_ctr_dev,
+                                          c->tok_ctr_host, c->stream);
                 cudaError_t ee = cudaStreamEndCapture(c->stream, &g);
                 ok = rc == 0 && ee == cudaSuccess && g &&
                      cudaGraphInstantiate(&ld->tok_graph, g, 0) == cudaSuccess;
@@ -1145,10 +1165,31 @@ int qmoe_forward(qmoe_ctx *c, int layer, const float *x, int n, float *out, qmoe
             seterr(err, "qmoe_forward: graph launch failed");
             return -1;
         }
-        cudaError_t se = cudaStreamSynchronize(c->stream);
-        if (se != cudaSuccess) {
-            seterr(err, "qmoe_forward: %s", cudaGetErrorString(se));
-            return -1;
+        /* wait for the report kernel's count in pinned memory (no driver
+         * call on the way); after 2 s, or on a count out of step, the stream
+         * is synchronised, which also surfaces a failed launch */
+        const unsigned want = ++c->tok_seq;
+        volatile const unsigned *done = c->tok_ctr_host;
+        int seen = 0;
+        double tw = 0.0;
+        for (unsigned spin = 0;; spin++) {
+            if (*done == want) {
+                seen = 1;
+                break;
+            }
+            if ((spin & 1023u) == 1023u) {
+                const double tn = now_s();
+                if (tw == 0.0) tw = tn;
+                else if (tn - tw > 2.0) break;
+            }
+        }
+        if (!seen) {
+            cudaError_t se = cudaStreamSynchronize(c->stream);
+            if (se != cudaSuccess) {
+                seterr(err, "qmoe_forward: %s", cudaGetErrorString(se));
+                return -1;
+            }
+            c->tok_seq = *done;
         }
         if (report_dev_err(c, *(volatile int *)c->err_host, c->stream, err)) return -1;
         memcpy(out, c->out_pin, bytes);

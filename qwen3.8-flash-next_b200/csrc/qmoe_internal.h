@@ -87,9 +87,11 @@ int qk_launch_decode_down(const qk_fwd *f, void *stream, int pdl);
 /* Host-pointer single-token calls: copy `bytes` (a multiple of 16) of x from
  * pinned host memory to the device with one CTA that lets its dependents
  * launch at once; after the layer, a dependent launch copies the error word
- * to pinned host memory. */
+ * to pinned host memory and, when ctr is not NULL, increments the device
+ * counter ctr and writes its new value to ctr_host (pinned). */
 int qk_launch_copy_in(const void *src_host, void *dst, size_t bytes, void *stream);
-int qk_launch_report(const int *err, int *err_host, void *stream);
+int qk_launch_report(const int *err, int *err_host, unsigned *ctr, unsigned *ctr_host,
+                     void *stream);
 
 /* Single-launch decode (T == 1): router, top-k, gate/up and down+combine in
  * one persistent kernel with one CTA per SM and grid barriers between the

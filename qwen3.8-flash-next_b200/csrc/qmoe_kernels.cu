@@ -345,9 +345,22 @@ __global__ void k_copy_in(const float4 *src, float4 *dst, int n4) {
     for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = src[i];
 }
 
-__global__ void k_report(const int *err, volatile int *err_host) {
+// After the layer: the error word to pinned memory, then (ctr != NULL) a
+// completion count, so the host can wait by watching pinned memory instead
+// of synchronising the stream. The layer's output writes completed with its
+// grid, before pdl_wait returns here.
+__global__ void k_report(const int *err, volatile int *err_host, unsigned *ctr,
+                         volatile unsigned *ctr_host) {
     pdl_wait();
-    if (threadIdx.x == 0) *err_host = *err;
+    if (threadIdx.x == 0) {
+        *err_host = *err;
+        if (ctr) {
+            const unsigned v = *ctr + 1u;
+            *ctr = v;
+            __threadfence_system();
+            *ctr_host = v;
+        }
+    }
 }
 
 cudaError_t launch(const void *fn, dim3 grid, dim3 block, size_t smem, void *stream, int pdl,
@@ -435,9 +448,11 @@ extern "C" int qk_launch_copy_in(const void *src_host, void *dst, size_t bytes, 
                   args);
 }
 
-extern "C" int qk_launch_report(const int *err, int *err_host, void *stream) {
+extern "C" int qk_launch_report(const int *err, int *err_host, unsigned *ctr, unsigned *ctr_host,
+                                void *stream) {
     volatile int *h = err_host;
-    void *args[] = {&err, &h};
+    volatile unsigned *ch = ctr_host;
+    void *args[] = {&err, &h, &ctr, &ch};
     return launch(reinterpret_cast<const void *>(&k_report), dim3(1), dim3(32), 0, stream, 1, args);
 }
 
