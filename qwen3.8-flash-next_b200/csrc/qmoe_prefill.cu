@@ -465,6 +465,7 @@ constexpr int NS = 32;                    // token rows per small tile
 constexpr int kSmallMax = 2 * NS;         // largest group planned as small tiles
 constexpr int kXs = NS * BK * 2;          // 4 KB: one plane of the token tile
 constexpr int kNbT = 4;                   // dequantised weight buffers in TMEM
+constexpr int kThreadsSw = kThreads + 32; // a second MMA-issuing warp (warp 14)
 template <int MODE>
 struct CfgS {
     static constexpr bool GU = MODE != 1;
@@ -475,7 +476,7 @@ struct CfgS {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsSw, 1)
     k_gemm_sw(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ,
               const __grid_constant__ CUtensorMap tmS, GemmArgs g) {
     constexpr int NR = CfgS<MODE>::NR;
@@ -484,7 +485,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr bool kLo = MODE != 0;
     constexpr int kN = kLo ? 2 * NS : NS;  // MMA N: token columns (hi, then lo)
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t raw_full[NR], raw_empty[NR], bf_full[kNbT], bf_empty[kNbT];
+    // done[s]: the MMAs of the step that used raw stage s (and weight buffer
+    // it % kNbT) completed, one commit from each issuer
+    __shared__ uint64_t raw_full[NR], done[NR], bf_full[kNbT];
     __shared__ uint64_t acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag_;
@@ -495,17 +498,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
         for (int s = 0; s < NR; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], 1);
+            mbar_init(&done[s], 2);
         }
-        for (int b = 0; b < kNbT; ++b) {
-            mbar_init(&bf_full[b], kDeqWarps);
-            mbar_init(&bf_empty[b], 1);
-        }
+        for (int b = 0; b < kNbT; ++b) mbar_init(&bf_full[b], kDeqWarps);
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_full[b], 2);
             mbar_init(&acc_empty[b], 4);
         }
-        mbar_init(&drain, 1);
+        mbar_init(&drain, 2);
         abort_flag = 0;
     }
     if (warp == 1) {
@@ -532,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kb = 0; kb < KB; ++kb, ++it) {
                     const int s = it % NR;
                     const uint32_t ph = (it / NR) & 1;
-                    if (!mbar_wait(&raw_empty[s], ph ^ 1)) {
+                    if (!mbar_wait(&done[s], ph ^ 1)) {
                         atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
                         abort_flag = 1;
                         break;
@@ -558,8 +558,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int s = 0; s < NR; ++s)
                 if (last_it[s] >= 0) mbar_wait(&raw_full[s], (last_it[s] / NR) & 1);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer
+    } else if (warp == 1 || warp == kThreads / 32) {
+        // ---------------- MMA issuers: warp 1 the first 128 weight rows, the
+        // last warp the second (one issuing thread runs small MMAs at about
+        // half the tensor pipe's rate; two keep it busy)
+        const int hh = warp == 1 ? 0 : 1;
         const uint32_t idesc = idesc_f16(BM, kN);
         int it = 0, lt = 0;
         for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
@@ -587,14 +590,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t x0 = smem_addr(smem + s * kRaw);
                     const uint32_t w0 = tmem_w + b * 64;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint64_t xd = sdesc_sw128(x0 + kk * 32);
-#pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            umma_f16_ts(dt + h * 64, w0 + h * 32 + kk * 8, xd, idesc, (kb | kk) != 0);
-                    }
-                    umma_commit(&raw_empty[s]);
-                    umma_commit(&bf_empty[b]);
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_f16_ts(dt + hh * 64, w0 + hh * 32 + kk * 8, sdesc_sw128(x0 + kk * 32), idesc,
+                                    (kb | kk) != 0);
+                    umma_commit(&done[s]);
                 }
                 __syncwarp();
             }
@@ -624,8 +623,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int kb = 0; kb < KB; ++kb, ++it) {
                 const int s = it % NR, b = it % kNbT;
-                const uint32_t ph = (it / NR) & 1, bph = (it / kNbT) & 1;
-                if (!mbar_wait(&raw_full[s], ph) || !mbar_wait(&bf_empty[b], bph ^ 1)) {
+                const uint32_t ph = (it / NR) & 1;
+                // weight buffer b is free once the step kNbT earlier is done;
+                // that barrier cannot be two phases ahead (its next phase needs
+                // this step's dequantised weights)
+                const int pv = it - kNbT;
+                if (!mbar_wait(&raw_full[s], ph) ||
+                    (pv >= 0 && !mbar_wait(&done[pv % NR], (pv / NR) & 1))) {
                     ok = false;
                     break;
                 }
@@ -665,8 +669,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
         }
-    } else {
-        // ---------------- epilogue: thread = weight row 32q + lane of each
+    } else if (warp < kThreads / 32) {
+        // ---------------- epilogue (warps 10-13): thread = weight row 32q + lane of each
         // half; token columns c (hi) and NS + c (lo)
         const int q = warp & 3;
         const int wr = 32 * q + lane;
@@ -761,58 +765,65 @@ __global__ void k_count(const int32_t *idx, int nk, int *counts) {
 
 // One CTA (1024 threads, E + 1 <= 1024 groups). Group 0 is the shared expert
 // (rows [0, nsh): every token, or none); group 1 + e is routed expert e.
-// Writes the first row of each routed expert and two tile lists: groups of
-// at most small_max rows as NS-row tiles for k_gemm_sw (stiles), larger
-// groups as BM-row tiles for k_gemm (tiles).
-__global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh,
-                                               const int32_t *slot_of, int shared_slot,
-                                               int small_max, int *row0, MTile *tiles,
-                                               int *n_mtiles, MTile *stiles, int *n_stiles,
-                                               int *n_rows) {
-    __shared__ int s_scan[1024], s_tscan[1024], s_sscan[1024];
-    const int g = threadIdx.x;
-    const int rows = g == 0 ? nsh : (g <= E ? counts[g - 1] : 0);
-    const bool small = rows <= small_max;
+// Writes the first row of each routed expert and the tile lists: groups of
+// at most small_max rows as NS-row tiles (stiles, k_gemm_sw), larger groups
+// as BM-row tiles (tiles, k_gemm).
+struct PlanOut {
+    int small_max;
+    MTile *tiles, *stiles;
+    int *n_tiles, *n_stiles, *n_rows;
+};
+
+QK_DEV void plan_group(int rows, int slot, int r0, const PlanOut &o, int t0, int u0) {
+    const bool small = rows <= o.small_max;
     const int mt = small ? 0 : (rows + BM - 1) / BM;
     const int st = small ? (rows + NS - 1) / NS : 0;
-    s_scan[g] = rows;
-    s_tscan[g] = mt;
-    s_sscan[g] = st;
+    for (int i = 0; i < mt; ++i) o.tiles[t0 + i] = MTile{r0 + BM * i, min(BM, rows - BM * i), slot, 0};
+    for (int i = 0; i < st; ++i) o.stiles[u0 + i] = MTile{r0 + NS * i, min(NS, rows - NS * i), slot, 0};
+}
+
+// Inclusive block scans (1024 threads) of the rows and the two tile counts
+// of group g; returns the exclusive starts through the pointers.
+QK_DEV void plan_scan(int g, int rows, const PlanOut &o, int *s_a, int *s_b, int *s_c, int *r0,
+                      int *t0, int *u0) {
+    const bool small = rows <= o.small_max;
+    const int mt = small ? 0 : (rows + BM - 1) / BM;
+    const int st = small ? (rows + NS - 1) / NS : 0;
+    s_a[g] = rows;
+    s_b[g] = mt;
+    s_c[g] = st;
     __syncthreads();
     for (int off = 1; off < 1024; off <<= 1) {
-        const int a = g >= off ? s_scan[g - off] : 0;
-        const int b = g >= off ? s_tscan[g - off] : 0;
-        const int c = g >= off ? s_sscan[g - off] : 0;
+        const int a = g >= off ? s_a[g - off] : 0;
+        const int b = g >= off ? s_b[g - off] : 0;
+        const int c = g >= off ? s_c[g - off] : 0;
         __syncthreads();
-        s_scan[g] += a;
-        s_tscan[g] += b;
-        s_sscan[g] += c;
+        s_a[g] += a;
+        s_b[g] += b;
+        s_c[g] += c;
         __syncthreads();
     }
-    const int r0 = s_scan[g] - rows, t0 = s_tscan[g] - mt, u0 = s_sscan[g] - st;
+    *r0 = s_a[g] - rows;
+    *t0 = s_b[g] - mt;
+    *u0 = s_c[g] - st;
+    if (g == 1023) {
+        *o.n_tiles = s_b[1023];
+        *o.n_stiles = s_c[1023];
+        *o.n_rows = s_a[1023];
+    }
+}
+
+__global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh,
+                                               const int32_t *slot_of, int shared_slot, int *row0,
+                                               PlanOut o) {
+    __shared__ int s_a[1024], s_b[1024], s_c[1024];
+    const int g = threadIdx.x;
+    const int rows = g == 0 ? nsh : (g <= E ? counts[g - 1] : 0);
+    int r0, t0, u0;
+    plan_scan(g, rows, o, s_a, s_b, s_c, &r0, &t0, &u0);
     if (g >= 1 && g <= E) row0[g - 1] = r0;
     const int slot = g == 0 ? shared_slot : (g <= E ? slot_of[g - 1] : -1);
-    for (int i = 0; i < mt; ++i) {
-        MTile m;
-        m.m0 = r0 + BM * i;
-        m.rows = min(BM, rows - BM * i);
-        m.slot = slot;
-        m.pad = 0;
-        tiles[t0 + i] = m;
-    }
-    for (int i = 0; i < st; ++i) {
-        MTile m;
-        m.m0 = r0 + NS * i;
-        m.rows = min(NS, rows - NS * i);
-        m.slot = slot;
-        m.pad = 0;
-        stiles[u0 + i] = m;
-    }
-    if (g == 1023) {
-        *n_mtiles = s_tscan[1023];
-        *n_stiles = s_sscan[1023];
-        *n_rows = s_scan[1023];
-    }
+    plan_group(rows, slot, r0, o, t0, u0);
 }
 
 // Small calls (at most kPlanSmall slots): counting, planning and placing in
@@ -821,10 +832,9 @@ __global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh
 constexpr int kPlanSmall = 4096;
 __global__ void __launch_bounds__(1024) k_plan_small(const int32_t *idx, int nk, int k, int E,
                                                      int nsh, const int32_t *slot_of,
-                                                     int shared_slot, int small_max, MTile *tiles,
-                                                     int *n_mtiles, MTile *stiles, int *n_stiles,
-                                                     int *n_rows, int *inv, int *perm_tok) {
-    __shared__ int s_cnt[1024], s_scan[1024], s_tscan[1024], s_sscan[1024], s_row0[1024];
+                                                     int shared_slot, PlanOut o, int *inv,
+                                                     int *perm_tok) {
+    __shared__ int s_cnt[1024], s_a[1024], s_b[1024], s_c[1024], s_row0[1024];
     const int g = threadIdx.x;
     s_cnt[g] = 0;
     __syncthreads();
@@ -834,47 +844,11 @@ __global__ void __launch_bounds__(1024) k_plan_small(const int32_t *idx, int nk,
     }
     __syncthreads();
     const int rows = g == 0 ? nsh : (g <= E ? s_cnt[g - 1] : 0);
-    const bool small = rows <= small_max;
-    const int mt = small ? 0 : (rows + BM - 1) / BM;
-    const int st = small ? (rows + NS - 1) / NS : 0;
-    s_scan[g] = rows;
-    s_tscan[g] = mt;
-    s_sscan[g] = st;
-    __syncthreads();
-    for (int off = 1; off < 1024; off <<= 1) {
-        const int a = g >= off ? s_scan[g - off] : 0;
-        const int b = g >= off ? s_tscan[g - off] : 0;
-        const int c = g >= off ? s_sscan[g - off] : 0;
-        __syncthreads();
-        s_scan[g] += a;
-        s_tscan[g] += b;
-        s_sscan[g] += c;
-        __syncthreads();
-    }
-    const int r0 = s_scan[g] - rows, t0 = s_tscan[g] - mt, u0 = s_sscan[g] - st;
+    int r0, t0, u0;
+    plan_scan(g, rows, o, s_a, s_b, s_c, &r0, &t0, &u0);
     s_row0[g] = r0;
     const int slot = g == 0 ? shared_slot : (g <= E ? slot_of[g - 1] : -1);
-    for (int i = 0; i < mt; ++i) {
-        MTile m;
-        m.m0 = r0 + BM * i;
-        m.rows = min(BM, rows - BM * i);
-        m.slot = slot;
-        m.pad = 0;
-        tiles[t0 + i] = m;
-    }
-    for (int i = 0; i < st; ++i) {
-        MTile m;
-        m.m0 = r0 + NS * i;
-        m.rows = min(NS, rows - NS * i);
-        m.slot = slot;
-        m.pad = 0;
-        stiles[u0 + i] = m;
-    }
-    if (g == 1023) {
-        *n_mtiles = s_tscan[1023];
-        *n_stiles = s_sscan[1023];
-        *n_rows = s_scan[1023];
-    }
+    plan_group(rows, slot, r0, o, t0, u0);
     s_cnt[g] = 0;  // now the placement cursors
     __syncthreads();
     for (int a = g; a < nk; a += 1024) {
@@ -1605,23 +1579,28 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
                                              cudaEventRecordExternal);
     };
     // No group can exceed the small-tile limit (each token is in a group at
-    // most once): every group runs on k_gemm_sw and k_gemm is not launched.
-    // Otherwise every group runs on k_gemm (a second, small-tile launch
-    // beside it measured slower on the prefill workload).
+    // most once): every group runs on k_gemm_sw. Otherwise every group runs
+    // on k_gemm (a second, small-tile launch beside it measured slower on the
+    // prefill workload).
     const bool all_small = nsh <= p->small_max && routed_max <= p->small_max;
+    const bool lo = x_kind == XK_F32;  // x as an fp16 hi/lo pair
+    PlanOut po;
+    po.small_max = all_small ? p->small_max : 0;
+    po.tiles = p->tiles;
+    po.stiles = p->stiles;
+    po.n_tiles = p->n_mtiles;
+    po.n_stiles = p->n_stiles;
+    po.n_rows = p->n_rows;
     cudaError_t e = cudaSuccess;
     if (nk <= kPlanSmall) {
-        k_plan_small<<<1, 1024, 0, st>>>(idx, nk, k, E, nsh, slot_of, shared_slot_index,
-                                         all_small ? p->small_max : 0, p->tiles, p->n_mtiles,
-                                         p->stiles, p->n_stiles, p->n_rows, p->inv, p->perm_tok);
+        k_plan_small<<<1, 1024, 0, st>>>(idx, nk, k, E, nsh, slot_of, shared_slot_index, po, p->inv,
+                                         p->perm_tok);
     } else {
         // counts and cursors in one allocation, cleared together
         e = cudaMemsetAsync(p->counts, 0, sizeof(int) * 2 * (E + 1), st);
         if (e != cudaSuccess) return e;
         k_count<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, p->counts);
-        k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index,
-                                   all_small ? p->small_max : 0, p->row0, p->tiles, p->n_mtiles,
-                                   p->stiles, p->n_stiles, p->n_rows);
+        k_plan<<<1, 1024, 0, st>>>(p->counts, E, nsh, slot_of, shared_slot_index, p->row0, po);
         k_place<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, k, p->row0, p->cursor, p->inv,
                                                  p->perm_tok);
     }
@@ -1632,67 +1611,59 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     mark(0);
-    const bool lo = x_kind == XK_F32;  // x as an fp16 hi/lo pair
 
+    auto launch = [&](const void *fn, int smem, const CUtensorMap *a, const CUtensorMap *q,
+                      const CUtensorMap *sc, GemmArgs *ga, int threads) {
+        void *args[] = {const_cast<CUtensorMap *>(a), const_cast<CUtensorMap *>(q),
+                        const_cast<CUtensorMap *>(sc), ga};
+        return qk_launch_raw(fn, dim3(p->num_sms), dim3(threads), smem, st, 0, args);
+    };
+    auto fn = [](auto f) { return reinterpret_cast<const void *>(f); };
     GemmArgs gu;
     memset(&gu, 0, sizeof(gu));
     gu.mode = lo ? 3 : 0;
     gu.KB = L.d / BK;
-    gu.NT = L.I / 128;
     gu.ld_out = L.I;
     gu.n_cols = L.I;
     gu.d = L.d;
     gu.I = L.I;
-    gu.tiles = p->tiles;
-    gu.n_mtiles = p->n_mtiles;
     gu.rows_max = p->rows_max;
     gu.lo_plane = static_cast<size_t>(p->rows_max) * L.I;
     gu.out = p->H;
     gu.outf = nullptr;
     gu.err = err;
-    GemmArgs gus = gu;
-    gus.tiles = p->stiles;
-    gus.n_mtiles = p->n_stiles;
-    auto launch = [&](const void *fn, int smem, const CUtensorMap *a, const CUtensorMap *q,
-                      const CUtensorMap *sc, GemmArgs *ga) {
-        void *args[] = {const_cast<CUtensorMap *>(a), const_cast<CUtensorMap *>(q),
-                        const_cast<CUtensorMap *>(sc), ga};
-        return qk_launch_raw(fn, dim3(p->num_sms), dim3(kThreads), smem, st, 0, args);
-    };
-    if (!all_small) {
-        e = lo ? launch(reinterpret_cast<const void *>(&k_gemm<3>), Cfg<3>::Smem, &p->tmX,
-                        &p->tmQgu, &p->tmSgu, &gu)
-               : launch(reinterpret_cast<const void *>(&k_gemm<0>), Cfg<0>::Smem, &p->tmX,
-                        &p->tmQgu, &p->tmSgu, &gu);
-        if (e != cudaSuccess) return e;
-    }
-    if (all_small) {
-        e = lo ? launch(reinterpret_cast<const void *>(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs,
-                        &p->tmQgu, &p->tmSgu, &gus)
-               : launch(reinterpret_cast<const void *>(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs,
-                        &p->tmQgu, &p->tmSgu, &gus);
-        if (e != cudaSuccess) return e;
-    }
-    mark(1);
     GemmArgs dn = gu;
     dn.mode = 1;
     dn.KB = L.I / BK;
-    dn.NT = L.d / 256;
     dn.ld_out = L.d;
     dn.n_cols = L.d;
     dn.out = nullptr;
     dn.outf = p->Y;
-    GemmArgs dns = dn;
-    dns.tiles = p->stiles;
-    dns.n_mtiles = p->n_stiles;
-    if (!all_small) {
-        e = launch(reinterpret_cast<const void *>(&k_gemm<1>), Cfg<1>::Smem, &p->tmH, &p->tmQdn,
-                   &p->tmSdn, &dn);
-        if (e != cudaSuccess) return e;
-    }
     if (all_small) {
-        e = launch(reinterpret_cast<const void *>(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs,
-                   &p->tmQdn, &p->tmSdn, &dns);
+        gu.NT = L.I / 128;
+        gu.tiles = p->stiles;
+        gu.n_mtiles = p->n_stiles;
+        e = lo ? launch(fn(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs, &p->tmQgu, &p->tmSgu, &gu, kThreadsSw)
+               : launch(fn(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs, &p->tmQgu, &p->tmSgu, &gu, kThreadsSw);
+        if (e != cudaSuccess) return e;
+        mark(1);
+        dn.NT = L.d / 256;
+        dn.tiles = p->stiles;
+        dn.n_mtiles = p->n_stiles;
+        e = launch(fn(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs, &p->tmQdn, &p->tmSdn, &dn, kThreadsSw);
+        if (e != cudaSuccess) return e;
+    } else {
+        gu.NT = L.I / 128;
+        gu.tiles = p->tiles;
+        gu.n_mtiles = p->n_mtiles;
+        e = lo ? launch(fn(&k_gemm<3>), Cfg<3>::Smem, &p->tmX, &p->tmQgu, &p->tmSgu, &gu, kThreads)
+               : launch(fn(&k_gemm<0>), Cfg<0>::Smem, &p->tmX, &p->tmQgu, &p->tmSgu, &gu, kThreads);
+        if (e != cudaSuccess) return e;
+        mark(1);
+        dn.NT = L.d / 256;
+        dn.tiles = p->tiles;
+        dn.n_mtiles = p->n_mtiles;
+        e = launch(fn(&k_gemm<1>), Cfg<1>::Smem, &p->tmH, &p->tmQdn, &p->tmSdn, &dn, kThreads);
         if (e != cudaSuccess) return e;
     }
     mark(2);
