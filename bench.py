@@ -433,6 +433,24 @@ def measure_stack(rank, world, local, layers=STACK_L, reps=3, warmup=2):
                         if world > 1 else None}
 
 
+def run_stack_eager(layers):
+    """Small case for ncu captures: one eager pass of a `layers`-layer stack
+    (configs[3] shapes, 64 tokens, weights generated on the device)."""
+    import torch
+
+    import qmoe
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, layers=layers, max_tokens=STACK_T)
+    ctx = qmoe.Context(cfg)
+    for l in range(layers):
+        ctx.synth_layer_dev(l, STACK_SEED)
+    h = torch.from_numpy(qmoe.synth_tokens(STACK_SEED, 100, STACK_T, D)).cuda()
+    torch.cuda.synchronize()
+    ctx.forward_stack(0, layers, h.data_ptr(), STACK_T, 1e-6, None)
+    ctx.sync()
+    ctx.close()
+    print(f"stack case: {layers} layers x {STACK_T} tokens ok")
+
+
 def run_eager(n):
     """Small case for ncu captures: n single-token forwards launched eagerly
     on the config-1 layer (906 MB of experts, larger than L2)."""
@@ -467,6 +485,8 @@ def main():
                     help="profiling case: run N eager 4096-token prefill calls and exit")
     ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] leg")
     ap.add_argument("--no-stack", action="store_true", help="skip the configs[3] leg")
+    ap.add_argument("--stack-eager", type=int, default=0,
+                    help="profiling case: one eager pass of an N-layer configs[3] stack and exit")
     ap.add_argument("--stack-only", type=int, default=0,
                     help="run only the configs[3] leg with this many layers and print it")
     args = ap.parse_args()
@@ -478,6 +498,9 @@ def main():
         return
     if args.prefill_eager:
         run_prefill_eager(args.prefill_eager)
+        return
+    if args.stack_eager:
+        run_stack_eager(args.stack_eager)
         return
     if args.stack_only:
         import torch
