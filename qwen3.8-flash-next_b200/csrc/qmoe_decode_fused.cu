@@ -15,8 +15,9 @@
 //             candidates), looks the k experts up in the staged slot table
 //             and issues its share of their gate/up rows (in chunks of <= 8
 //             rows, one mbarrier each) and of their down rows (all k experts
-//             at once). Meanwhile warps 1..15 compute the shared expert's
-//             gate/up rows. Then all warps compute the routed gate/up rows
+//             at once). Meanwhile the warps that do not share warp 0's
+//             scheduler compute the shared expert's gate/up rows. Then all
+//             warps compute the routed gate/up rows
 //             chunk by chunk as they land -> h.              [grid barrier]
 //   phase 3   h -> 24-bit integers in shared memory; this CTA's output rows
 //             for all k+1 experts as (expert, row-pair) tasks, so a warp keeps
@@ -389,11 +390,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
             if (lane == 0) f.sgate[0] = r_w[k];
         }
     } else if (ok0) {
-        // warps 1..15: the shared expert's gate/up rows while warp 0 routes
-        for (int i = warp - 1; i < sr1 - sr0; i += kWarps - 1) {
-            const float hv =
-                gateup_row<UPL>(sm_sgu + static_cast<size_t>(i) * L.gu_row, L, xw, xsc, xsm, lane);
-            if (lane == 0) hf[static_cast<size_t>(k) * I + sr0 + i] = hv;
+        // the shared expert's gate/up rows while warp 0 routes, on the warps
+        // that do not share warp 0's scheduler (warp w issues on scheduler
+        // w % 4): warp 0's top-k is on the critical path
+        if (warp % 4 != 0) {
+            const int helper = warp - 1 - warp / 4, helpers = kWarps - kWarps / 4;
+            for (int i = helper; i < sr1 - sr0; i += helpers) {
+                const float hv =
+                    gateup_row<UPL>(sm_sgu + static_cast<size_t>(i) * L.gu_row, L, xw, xsc, xsm, lane);
+                if (lane == 0) hf[static_cast<size_t>(k) * I + sr0 + i] = hv;
+            }
         }
     }
     __syncthreads();
