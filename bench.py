@@ -433,6 +433,108 @@ def measure_stack(rank, world, local, layers=STACK_L, reps=3, warmup=2):
                         if world > 1 else None}
 
 
+STREAM_LAYERS, STREAM_POOL_76, STREAM_DECODE, STREAM_PREFILL = 76, 8 * 2 ** 30, 16, 512
+
+
+def mem_available():
+    try:
+        for line in open("/proc/meminfo"):
+            if line.startswith("MemAvailable:"):
+                return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
+def measure_stream(layers=STREAM_LAYERS):
+    """configs[4] on one GPU: the MoE-only stack streamed from pinned host
+    memory, Zipf(1.1) routing with a per-layer permutation, an LRU/adaptive
+    HBM pool and route-predicted prefetches of depth 2 (the reference's
+    prefetch_count). The stack has `layers` of the 76 layers (the pinned
+    store is layers x 906 MB, 68.9 GB for all 76; fewer layers when that is
+    more than half the host's available memory), and the pool is config 4's
+    8 GiB pro rata, so it covers the same 11.6% of the stack's experts. Decode: STREAM_DECODE seeded
+    tokens, one at a time through the whole stack; prefill: one
+    STREAM_PREFILL-token call through the stack. CUDA events on the stream
+    (the host's waits for fills show as the stream's idle time)."""
+    import torch
+
+    import qmoe
+    store_per_layer = E * SLOT
+    avail = mem_available()
+    if avail and layers * store_per_layer * 2 > avail:
+        layers = max(2, int(avail // (2 * store_per_layer)))
+    pool = int(STREAM_POOL_76 * layers / STACK_L)
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, layers=layers, max_tokens=STREAM_PREFILL,
+                           pool_bytes=pool, prefetch=2)
+    ctx = qmoe.Context(cfg)
+    t0 = time.perf_counter()
+    for l in range(layers):
+        ctx.synth_layer_dev(l, STACK_SEED + 1, 1.1)
+    ctx.sync()
+    synth_s = time.perf_counter() - t0
+    h0 = torch.from_numpy(qmoe.synth_tokens(STACK_SEED + 1, 200, STREAM_PREFILL, D)).cuda()
+    st = torch.cuda.Stream()
+    cs = st.cuda_stream
+    torch.cuda.synchronize()
+
+    def counters():
+        a, b = ctx.stats(), ctx.cache_stats()
+        return {**a, **{"c_" + k: v for k, v in b.items()}}
+
+    def leg(run, n_tokens):
+        c0 = counters()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        run()
+        e1.record(st)
+        st.synchronize()
+        ctx.sync()
+        ms = e0.elapsed_time(e1)
+        c1 = counters()
+        looks = c1["routed_lookups"] - c0["routed_lookups"]
+        hits = c1["routed_hits"] - c0["routed_hits"]
+        nbytes = c1["expert_bytes"] - c0["expert_bytes"]
+        wait = c1["expert_wait_seconds"] - c0["expert_wait_seconds"]
+        return {"tokens_per_s": n_tokens / (ms / 1e3), "ms": ms,
+                "hit_rate": hits / max(1, looks), "routed_experts": looks, "expert_fills": c1["expert_loads"] - c0["expert_loads"],
+                "h2d_bytes": nbytes, "h2d_gbs_while_filling": nbytes / wait / 1e9 if wait > 0 else None,
+                "h2d_gbs_over_leg": nbytes / (ms / 1e3) / 1e9,
+                "prefetch_issued": c1["prefetch_issued"] - c0["prefetch_issued"],
+                "prefetch_hits": c1["prefetch_hits"] - c0["prefetch_hits"]}
+
+    hd = torch.empty((1, D), dtype=torch.float32, device="cuda")
+
+    def decode(tokens):
+        def run():
+            for t in tokens:
+                with torch.cuda.stream(st):
+                    hd.copy_(h0[t:t + 1])
+                ctx.forward_stack(0, layers, hd.data_ptr(), 1, 1e-6, cs)
+        return run
+
+    decode(range(4))()  # warm-up: the pool and the route statistics start filling
+    st.synchronize()
+    dec = leg(decode(range(4, 4 + STREAM_DECODE)), STREAM_DECODE)
+    hp = torch.empty((STREAM_PREFILL, D), dtype=torch.float32, device="cuda")
+
+    def prefill():
+        with torch.cuda.stream(st):
+            hp.copy_(h0)
+        ctx.forward_stack(0, layers, hp.data_ptr(), STREAM_PREFILL, 1e-6, cs)
+
+    pre = leg(prefill, STREAM_PREFILL)
+    ctx.close()
+    return {"workload": f"config4: {layers} of the 76 stack layers streamed from pinned host memory, "
+                        f"HBM pool {pool / 2 ** 30:.2f} GiB (8 GiB x {layers}/76), Zipf(1.1) with a "
+                        "per-layer permutation, prefetch depth 2",
+            "layers": layers, "pool_bytes": pool, "host_store_bytes": layers * store_per_layer,
+            "host_mem_available": avail, "decode_batch1": dec,
+            "prefill": {**pre, "tokens": STREAM_PREFILL}, "weights_generated_s": synth_s,
+            "timing": "CUDA events on the stream; the host's waits for fills are inside",
+            "note": "fills and prefetches wait for their copies on the host (no overlap with compute)"}
+
+
 def run_stack_eager(layers):
     """Small case for ncu captures: one eager pass of a `layers`-layer stack
     (configs[3] shapes, 64 tokens, weights generated on the device)."""
@@ -485,6 +587,9 @@ def main():
                     help="profiling case: run N eager 4096-token prefill calls and exit")
     ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] leg")
     ap.add_argument("--no-stack", action="store_true", help="skip the configs[3] leg")
+    ap.add_argument("--no-stream", action="store_true", help="skip the configs[4] leg")
+    ap.add_argument("--stream-only", type=int, default=0,
+                    help="run only the configs[4] leg with this many layers and print it")
     ap.add_argument("--stack-eager", type=int, default=0,
                     help="profiling case: one eager pass of an N-layer configs[3] stack and exit")
     ap.add_argument("--stack-only", type=int, default=0,
@@ -501,6 +606,9 @@ def main():
         return
     if args.stack_eager:
         run_stack_eager(args.stack_eager)
+        return
+    if args.stream_only:
+        print(json.dumps(measure_stream(args.stream_only)), flush=True)
         return
     if args.stack_only:
         import torch
@@ -667,6 +775,12 @@ def main():
     if not args.no_stack:
         stack = measure_stack(rank, world, local)
 
+    stream = None
+    if not args.no_stream:
+        stream = (measure_stream() if world == 1 else
+                  {"unavailable": "streaming contexts are single-GPU in this build "
+                                  "(expert parallelism needs every local expert resident)"})
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
@@ -704,6 +818,7 @@ def main():
             "parity_spot_check": parity_ok,
             "prefill": prefill,
             "stack": stack,
+            "stream": stream,
         }
         print(json.dumps(line), flush=True)
     ctx.close()

@@ -99,6 +99,9 @@ typedef struct {
     uint64_t prefill_calls, decode_calls;
     double forward_seconds;                /* host wall time inside qmoe_forward */
     uint64_t prefetch_issued, prefetch_hits;
+    /* streaming: distinct experts a call's routing selected per layer, and
+     * how many of them were already in the pool before its fills */
+    uint64_t routed_lookups, routed_hits;
 } qmoe_stats;
 
 typedef struct qmoe_ctx qmoe_ctx;
@@ -276,8 +279,12 @@ int qmoe_stats_get(qmoe_ctx *ctx, qmoe_stats *out);
 
 /* ---- prefetch hooks (streaming.py:271-284, :400-435) ---- */
 
-/* Queues asynchronous fills of the listed experts on the copy stream; never
- * blocks. Returns the number queued (ExpertStore.request(prefetch=True)). */
+/* Fills the listed experts that are not in the pool, on the copy stream,
+ * once the context's own stream is idle (a fill may evict a slot its
+ * kernels read; a caller that runs forwards on a stream of its own
+ * synchronises that stream first), and waits for the copies. Returns the
+ * number filled (ExpertStore.request(prefetch=True)); 0 on a resident
+ * context. */
 int qmoe_prefetch(qmoe_ctx *ctx, int layer, const int64_t *ids, size_t n);
 /* Records one step's selected experts for the route statistics
  * (ExpertStore.record_route). */

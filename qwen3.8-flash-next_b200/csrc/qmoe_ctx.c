@@ -82,6 +82,7 @@ struct qmoe_ctx {
     qmoe_stats stats;
     /* route statistics (streaming.py:400-413) */
     uint64_t *freq;        /* [num_layers * E] */
+    unsigned char *pf_mark; /* [num_layers * E] filled by a prefetch, not yet routed to */
     uint32_t *trans;       /* [num_layers * E * E], lazily allocated */
     int32_t *recent;       /* [num_layers * k] last selection per layer */
     int *recent_n;
@@ -271,6 +272,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     free(c->slot_owner);
     free(c->free_slots);
     free(c->freq);
+    free(c->pf_mark);
     free(c->trans);
     free(c->recent);
     free(c->recent_n);
@@ -388,10 +390,11 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
         c->slot_owner = malloc((size_t)c->nslots * sizeof(uint64_t));
         c->free_slots = malloc((size_t)c->nslots * sizeof(int));
         c->freq = calloc((size_t)total, sizeof(uint64_t));
+        c->pf_mark = calloc((size_t)total, 1);
         c->recent = calloc((size_t)Lz * cfg->top_k * 4, sizeof(int32_t));
         c->recent_n = calloc((size_t)Lz, sizeof(int));
         if (!c->slot_of_host || !c->slot_owner || !c->free_slots || !c->freq || !c->recent ||
-            !c->recent_n) {
+            !c->recent_n || !c->pf_mark) {
             seterr(err, "qmoe_create: out of host memory");
             goto fail;
         }
@@ -699,18 +702,16 @@ fail:
     return -1;
 }
 
-/* The seeded synthetic layer of qmoe_synth_layer, generated on the device
- * straight into the pool (the local experts), the shared slot, the router
- * and the shared gate; the Zipf bias (zipf_s > 0) is made on the host. */
+/* The seeded synthetic layer of qmoe_synth_layer, generated on the device:
+ * the local experts straight into the pool (resident contexts) or, through a
+ * device staging buffer, into the pinned host store (streaming contexts,
+ * whose cached copies of the layer are dropped); the shared slot, the
+ * router and the shared gate on the device; the Zipf bias (zipf_s > 0) made
+ * on the host. */
 int qmoe_synth_layer_dev(qmoe_ctx *c, int layer, uint64_t seed, double zipf_s, qmoe_err *err) {
     if (err) err->msg[0] = 0;
     if (!c || layer < 0 || layer >= c->cfg.num_layers) {
         seterr(err, "qmoe_synth_layer_dev: bad arguments (layer %d)", layer);
-        return -1;
-    }
-    if (!c->resident_all) {
-        seterr(err, "qmoe_synth_layer_dev: needs every local expert resident (pool_bytes = 0); "
-                    "streaming contexts take host layers (qmoe_upload_layer)");
         return -1;
     }
     const qk_layout *L = &c->L;
@@ -718,6 +719,8 @@ int qmoe_synth_layer_dev(qmoe_ctx *c, int layer, uint64_t seed, double zipf_s, q
     cudaStream_t st = c->copy_stream;
     uint16_t *router_host = NULL;
     float *bias_host = NULL;
+    uint8_t *stage = NULL;            /* streaming: device staging slots */
+    const int stage_slots = 32;
     const uint64_t Ly = (uint64_t)layer;
     const uint64_t rk[6] = {qk_stream_key(seed, Ly, QK_T_GQ), qk_stream_key(seed, Ly, QK_T_GS),
                             qk_stream_key(seed, Ly, QK_T_UQ), qk_stream_key(seed, Ly, QK_T_US),
@@ -739,16 +742,41 @@ int qmoe_synth_layer_dev(qmoe_ctx *c, int layer, uint64_t seed, double zipf_s, q
     CK((cudaError_t)qk_synth_bf16_normal(ld->shgate, (size_t)L->d,
                                          qk_stream_key(seed, Ly, QK_T_SHGATE), st));
     CK((cudaError_t)qk_synth_slot(L, ld->shared_slot, 0, sk, st));
-    for (int e = c->ep_lo; e < c->ep_hi; e++) {
-        pthread_mutex_lock(&c->lock);
-        int slot = c->slot_of_host[(size_t)layer * L->E + e];
-        if (slot < 0) slot = claim_slot(c, layer, e, 0);
-        pthread_mutex_unlock(&c->lock);
-        if (slot < 0) {
-            seterr(err, "qmoe_synth_layer_dev: pool bookkeeping failed");
-            goto fail;
+    if (c->resident_all) {
+        for (int e = c->ep_lo; e < c->ep_hi; e++) {
+            pthread_mutex_lock(&c->lock);
+            int slot = c->slot_of_host[(size_t)layer * L->E + e];
+            if (slot < 0) slot = claim_slot(c, layer, e, 0);
+            pthread_mutex_unlock(&c->lock);
+            if (slot < 0) {
+                seterr(err, "qmoe_synth_layer_dev: pool bookkeeping failed");
+                goto fail;
+            }
+            CK((cudaError_t)qk_synth_slot(L, c->pool + (size_t)slot * L->slot_bytes, e, rk, st));
         }
-        CK((cudaError_t)qk_synth_slot(L, c->pool + (size_t)slot * L->slot_bytes, e, rk, st));
+    } else {
+        /* streaming: the layer's cached copies are stale */
+        pthread_mutex_lock(&c->lock);
+        for (int e = 0; e < L->E; e++) {
+            uint64_t v;
+            if (qmoe_cache_erase(c->cache, ekey(layer, e), &v) && v != NO_OWNER) {
+                c->slot_owner[v] = NO_OWNER;
+                c->free_slots[c->nfree++] = (int)v;
+            }
+            c->slot_of_host[(size_t)layer * L->E + e] = -1;
+        }
+        pthread_mutex_unlock(&c->lock);
+        CK(cudaMalloc((void **)&stage, (size_t)stage_slots * L->slot_bytes));
+        for (int e0 = 0; e0 < L->E; e0 += stage_slots) {
+            const int nb = L->E - e0 < stage_slots ? L->E - e0 : stage_slots;
+            for (int i = 0; i < nb; i++)
+                CK((cudaError_t)qk_synth_slot(L, stage + (size_t)i * L->slot_bytes, e0 + i, rk, st));
+            CK(cudaMemcpyAsync(c->host_store + ((size_t)layer * L->E + e0) * L->slot_bytes, stage,
+                               (size_t)nb * L->slot_bytes, cudaMemcpyDeviceToHost, st));
+            CK(cudaStreamSynchronize(st));
+        }
+        cudaFree(stage);
+        stage = NULL;
     }
     if (zipf_s > 0) {
         bias_host = malloc((size_t)L->E * sizeof(float));
@@ -778,6 +806,7 @@ int qmoe_synth_layer_dev(qmoe_ctx *c, int layer, uint64_t seed, double zipf_s, q
     ld->ready = 1;
     return 0;
 fail:
+    if (stage) cudaFree(stage);
     free(router_host);
     free(bias_host);
     return -1;
@@ -857,6 +886,15 @@ static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, qmoe_er
         if (e >= 0 && e < c->L.E && !seen[e]) {
             seen[e] = 1;
             uniq[nu++] = e;
+            const int resident = qmoe_cache_peek(c->cache, ekey(layer, e), NULL);
+            c->stats.routed_lookups++;
+            c->stats.routed_hits += (uint64_t)resident;
+            /* a prefetched expert routed to while still in the pool */
+            unsigned char *pm = c->pf_mark + (size_t)layer * c->L.E + e;
+            if (*pm) {
+                if (resident) c->stats.prefetch_hits++;
+                *pm = 0;
+            }
         }
     }
     free(seen);
@@ -1298,7 +1336,10 @@ int qmoe_prefetch(qmoe_ctx *c, int layer, const int64_t *ids, size_t n) {
         if (ex < 0 || ex >= c->L.E) continue;
         if (qmoe_cache_peek(c->cache, ekey(layer, ex), NULL)) continue;
         int64_t one = ex;
-        if (fill_experts(c, layer, &one, 1, &e) == 0) queued++;
+        if (fill_experts(c, layer, &one, 1, &e) == 0) {
+            queued++;
+            c->pf_mark[(size_t)layer * c->L.E + ex] = 1;
+        }
     }
     c->stats.prefetch_issued += (uint64_t)queued;
     return queued;
@@ -1519,8 +1560,11 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
 /* MoE-only stack over layers [l0, l1): h_{l+1} = h_l + MoE_l(RMSNorm(h_l)),
  * RMSNorm with unit weight and eps; each layer through qmoe_forward_ep on an
  * expert-parallel context, else qmoe_forward_dev. h: fp32 [n, d] device
- * rows, updated in place. Stream-ordered only (no host synchronisation),
- * so a whole stack can be captured in a graph. */
+ * rows, updated in place. With every expert resident it is stream-ordered
+ * only (no host synchronisation), so a whole stack can be captured in a
+ * graph; a streaming context waits for each layer's routing on the host to
+ * fill its experts, then records the route and queues the predicted
+ * prefetches. */
 int qmoe_forward_stack(qmoe_ctx *c, int l0, int l1, float *h, int n, float eps, void *stream,
                        qmoe_err *err) {
     if (err) err->msg[0] = 0;
@@ -1541,6 +1585,19 @@ int qmoe_forward_stack(qmoe_ctx *c, int l0, int l1, float *h, int n, float eps, 
         if (c->ep_world > 1) rc = qmoe_forward_ep(c, l, c->stk_xn, QMOE_F32, n, c->stk_y, st, err);
         else rc = n > 0 ? qmoe_forward_dev(c, l, c->stk_xn, QMOE_F32, n, c->stk_y, st, err) : 0;
         if (rc) return -1;
+        if (!c->resident_all && n > 0) {
+            /* streaming: the layer's routing is on the host (it chose the
+             * fills); route statistics and predicted prefetches follow it, as
+             * model.py:458-459 calls record_route and prefetch_predictions */
+            const size_t nk = (size_t)n * c->L.k;
+            qmoe_record_route(c, l, c->idx_pin, nk);
+            /* a prefetch may evict a slot this layer's kernels still read */
+            if (cudaStreamSynchronize(st) != cudaSuccess) {
+                seterr(err, "qmoe_forward_stack: layer %d failed on the device", l);
+                return -1;
+            }
+            qmoe_prefetch_predictions(c, l, c->idx_pin, nk);
+        }
     }
     if (l1 > l0 && kerr(qk_launch_residual_norm(h, c->stk_y, NULL, n, d, eps, st), "residual_norm", err))
         return -1;

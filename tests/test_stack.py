@@ -139,3 +139,37 @@ def test_rmsnorm_checker_matches_reference_formula():
         r = np.float32(1.0) / np.sqrt(ss / np.float32(256) + np.float32(EPS))
         want = (h[t] * r).astype(np.float32)
         assert np.allclose(got[t], want, rtol=1e-6, atol=0)
+
+
+@pytest.mark.gpu
+def test_streaming_stack_equals_resident(built):
+    """Layers generated on the device into the pinned host store of a
+    streaming context (a pool of 16 slots for 3 x 16 experts, LRU plus the
+    route-predicted prefetches) run the stack to the same bits as the same
+    layers resident in HBM, for a multi-token call and for single tokens;
+    the fill, prefetch and cache counters move."""
+    import torch
+
+    import qmoe
+    d, E, k, I, L = 256, 16, 4, 128, 3
+    slot = qmoe.lib().qmoe_slot_bytes(qmoe.make_config(d, E, k, I))
+    res = qmoe.Context(qmoe.make_config(d, E, k, I, layers=L, max_tokens=8))
+    stm = qmoe.Context(qmoe.make_config(d, E, k, I, layers=L, max_tokens=8, pool_bytes=16 * slot,
+                                        policy=qmoe.QMOE_POLICY_LRU, prefetch=2))
+    for l in range(L):
+        res.synth_layer_dev(l, 91, 1.1)
+        stm.synth_layer_dev(l, 91, 1.1)
+    h0 = qmoe.synth_tokens(91, 5, 8, d)
+    for n in (8, 1, 1, 1):
+        a = torch.from_numpy(h0[:n]).cuda()
+        b = a.clone()
+        res.forward_stack(0, L, a.data_ptr(), n, EPS, None)
+        stm.forward_stack(0, L, b.data_ptr(), n, EPS, None)
+        res.sync()
+        stm.sync()
+        assert torch.equal(a, b), n
+    st, cs = stm.stats(), stm.cache_stats()
+    assert st["expert_loads"] > 0 and st["prefetch_issued"] > 0
+    assert cs["size"] <= 16 and cs["hits"] + cs["misses"] > 0
+    res.close()
+    stm.close()
