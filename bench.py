@@ -10,8 +10,9 @@ call. A step is those 1000 sequential calls. Synthetic weights and tokens
   value      tokens/s with the inputs already in HBM, timed with CUDA events
              over K steps (a CUDA graph of the 1000 qmoe_forward_dev calls
              per step), max over ranks, summed over ranks.
-  e2e        tokens/s through qmoe_forward with host buffers: every call
-             copies its token host->device and its output device->host.
+  e2e        tokens/s through qmoe_forward with host buffers (x read from and
+             out written to pinned host memory on every call), one call per
+             token from C (qmoe__forward_tokens); the Python loop beside it.
   roofline   the decode kernel's algorithmic bytes per launch / its mean
              duration in the timed region (the step's graph holds only that
              kernel, one launch per token), against MEASURED_PEAKS.json
@@ -20,6 +21,12 @@ call. A step is those 1000 sequential calls. Synthetic weights and tokens
   prefill    configs[2] beside it: one 4096-token call on a Zipf(1.1)-biased
              layer (graph replays, CUDA events), its per-kernel split, and
              the grouped GEMMs' algorithmic FLOP rate against bf16_tflops.
+  stack      configs[3]: the 76-layer MoE-only stack (RMSNorm + MoE +
+             residual) at batch 64, one CUDA graph per step, expert-parallel
+             over the torchrun ranks; HBM roofline of the step's bytes.
+  stream     configs[4] (one GPU): the same stack streamed from pinned host
+             memory into an 8 GiB HBM pool; tokens/s, routed-expert hit rate
+             and host->HBM GB/s for batch-1 decode and a 512-token prefill.
   cpu_baseline  the reference's own moe_forward (oracle/_ref, built from the
              reference sources) on the host cores, over a bounded sample.
 
