@@ -658,7 +658,9 @@ QK_DEV void topk_rank_softmax(int C, int k, uint32_t *s_key, int *s_idx, float *
 // When more than 32 keys qualify the radix path gathers the set instead.
 // keys: (E+31)/32*32 staged keys; s_key/s_idx/s_ev: 32-entry scratch of this
 // warp. Returns false if fewer than k keys exist.
-QK_DEV bool topk_warp(const uint32_t *keys, int E, int k, uint32_t *s_key, int *s_idx,
+// (out of line: the fallback of the decode kernel's top-k, kept apart from
+// its hot code)
+static __device__ __noinline__ bool topk_warp(const uint32_t *keys, int E, int k, uint32_t *s_key, int *s_idx,
                       float *s_ev, int *idx_out, float *w_out) {
     const int lane = threadIdx.x & 31;
     const int nj = (E + 31) / 32;
