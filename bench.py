@@ -24,9 +24,10 @@ call. A step is those 1000 sequential calls. Synthetic weights and tokens
   stack      configs[3]: the 76-layer MoE-only stack (RMSNorm + MoE +
              residual) at batch 64, one CUDA graph per step, expert-parallel
              over the torchrun ranks; HBM roofline of the step's bytes.
-  stream     configs[4] (one GPU): the same stack streamed from pinned host
-             memory into an 8 GiB HBM pool; tokens/s, routed-expert hit rate
-             and host->HBM GB/s for batch-1 decode and a 512-token prefill.
+  stream     configs[4]: the same stack streamed from pinned host memory
+             into an 8 GiB HBM pool per GPU (expert-parallel over the torchrun
+             ranks); tokens/s, routed-expert hit rate and host->HBM GB/s for
+             batch-1 decode and a 512-token prefill.
   cpu_baseline  the reference's own moe_forward (oracle/_ref, built from the
              reference sources) on the host cores, over a bounded sample.
 
@@ -453,41 +454,59 @@ def mem_available():
     return 0
 
 
-def measure_stream(layers=STREAM_LAYERS):
-    """configs[4] on one GPU: the MoE-only stack streamed from pinned host
-    memory, Zipf(1.1) routing with a per-layer permutation, an LRU/adaptive
-    HBM pool and route-predicted prefetches of depth 2 (the reference's
-    prefetch_count). The stack has `layers` of the 76 layers (the pinned
-    store is layers x 906 MB, 68.9 GB for all 76; fewer layers when that is
-    more than half the host's available memory), and the pool is config 4's
-    8 GiB pro rata, so it covers the same 11.6% of the stack's experts. Decode: STREAM_DECODE seeded
-    tokens, one at a time through the whole stack; prefill: one
-    STREAM_PREFILL-token call through the stack. CUDA events on the stream
-    (the host's waits for fills show as the stream's idle time)."""
+def measure_stream(rank=0, world=1, local=0, layers=STREAM_LAYERS):
+    """the MoE-only stack streamed from pinned host memory,
+    Zipf(1.1) routing with a per-layer permutation, an adaptive HBM pool of
+    8 GiB per GPU and route-predicted prefetches of depth 2 (the reference's
+    prefetch_count). With world > 1 the ranks are expert-parallel (rank g
+    streams experts [g E/W, (g+1) E/W) into its own pool; the batch-1 decode
+    token lives on rank 0 and travels to the owners of its experts). The
+    stack has `layers` of the 76 layers (the pinned stores of all ranks hold
+    layers x 906 MB, 68.9 GB for all 76; fewer layers when that is more than
+    half the host's available memory), and the pool is pro rata to 76
+    layers. Decode: STREAM_DECODE seeded tokens, one at a time through the
+    whole stack; prefill: one STREAM_PREFILL-token call through the stack,
+    split over the ranks. CUDA events on the stream (the host's waits for
+    fills show as the stream's idle time), max over ranks."""
     import torch
+    import torch.distributed as dist
 
     import qmoe
-    store_per_layer = E * SLOT
+    store_all = E * SLOT  # per layer, all ranks together
     avail = mem_available()
-    if avail and layers * store_per_layer * 2 > avail:
-        layers = max(2, int(avail // (2 * store_per_layer)))
+    if avail and layers * store_all * 2 > avail:
+        layers = max(2, int(avail // (2 * store_all)))
+    if world > 1:
+        t = torch.tensor([layers], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        layers = int(t.item())
     pool = int(STREAM_POOL_76 * layers / STACK_L)
-    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, layers=layers, max_tokens=STREAM_PREFILL,
-                           pool_bytes=pool, prefetch=2)
+    T_per = STREAM_PREFILL // world
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, layers=layers, max_tokens=T_per, pool_bytes=pool,
+                           prefetch=2, device=local, ep_rank=rank if world > 1 else 0,
+                           ep_world=world if world > 1 else 0)
     ctx = qmoe.Context(cfg)
     t0 = time.perf_counter()
     for l in range(layers):
         ctx.synth_layer_dev(l, STACK_SEED + 1, 1.1)
     ctx.sync()
     synth_s = time.perf_counter() - t0
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(qmoe.ep_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        ctx.ep_connect(bytes(uid.cpu().numpy().tobytes()))
     h0 = torch.from_numpy(qmoe.synth_tokens(STACK_SEED + 1, 200, STREAM_PREFILL, D)).cuda()
     st = torch.cuda.Stream()
     cs = st.cuda_stream
     torch.cuda.synchronize()
+    keys = ("expert_loads", "expert_bytes", "expert_wait_seconds", "prefetch_issued", "prefetch_hits",
+            "routed_lookups", "routed_hits")
 
     def counters():
-        a, b = ctx.stats(), ctx.cache_stats()
-        return {**a, **{"c_" + k: v for k, v in b.items()}}
+        a = ctx.stats()
+        return [float(a[k]) for k in keys]
 
     def leg(run, n_tokens):
         c0 = counters()
@@ -498,47 +517,54 @@ def measure_stream(layers=STREAM_LAYERS):
         st.synchronize()
         ctx.sync()
         ms = e0.elapsed_time(e1)
-        c1 = counters()
-        looks = c1["routed_lookups"] - c0["routed_lookups"]
-        hits = c1["routed_hits"] - c0["routed_hits"]
-        nbytes = c1["expert_bytes"] - c0["expert_bytes"]
-        wait = c1["expert_wait_seconds"] - c0["expert_wait_seconds"]
+        dc = [b - a for a, b in zip(c0, counters())]
+        rate = dc[1] / dc[2] / 1e9 if dc[2] > 0 else 0.0
+        if world > 1:
+            mx = torch.tensor([ms], device="cuda")
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            sm = torch.tensor(dc + [rate], device="cuda", dtype=torch.float64)
+            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+            ms, dc, rate = float(mx.item()), [float(v) for v in sm[:-1]], float(sm[-1]) / world
+        d = dict(zip(keys, dc))
         return {"tokens_per_s": n_tokens / (ms / 1e3), "ms": ms,
-                "hit_rate": hits / max(1, looks), "routed_experts": looks, "expert_fills": c1["expert_loads"] - c0["expert_loads"],
-                "h2d_bytes": nbytes, "h2d_gbs_while_filling": nbytes / wait / 1e9 if wait > 0 else None,
-                "h2d_gbs_over_leg": nbytes / (ms / 1e3) / 1e9,
-                "prefetch_issued": c1["prefetch_issued"] - c0["prefetch_issued"],
-                "prefetch_hits": c1["prefetch_hits"] - c0["prefetch_hits"]}
+                "hit_rate": d["routed_hits"] / max(1.0, d["routed_lookups"]),
+                "routed_experts": int(d["routed_lookups"]), "expert_fills": int(d["expert_loads"]),
+                "h2d_bytes": int(d["expert_bytes"]),
+                "h2d_gbs_while_filling": rate if rate > 0 else None,
+                "h2d_gbs_over_leg": d["expert_bytes"] / (ms / 1e3) / 1e9,
+                "prefetch_issued": int(d["prefetch_issued"]), "prefetch_hits": int(d["prefetch_hits"])}
 
     hd = torch.empty((1, D), dtype=torch.float32, device="cuda")
+    n_dec = 1 if rank == 0 else 0  # one token per step, on rank 0
 
     def decode(tokens):
         def run():
             for t in tokens:
                 with torch.cuda.stream(st):
                     hd.copy_(h0[t:t + 1])
-                ctx.forward_stack(0, layers, hd.data_ptr(), 1, 1e-6, cs)
+                ctx.forward_stack(0, layers, hd.data_ptr(), n_dec, 1e-6, cs)
         return run
 
     decode(range(4))()  # warm-up: the pool and the route statistics start filling
     st.synchronize()
     dec = leg(decode(range(4, 4 + STREAM_DECODE)), STREAM_DECODE)
-    hp = torch.empty((STREAM_PREFILL, D), dtype=torch.float32, device="cuda")
+    hp = torch.empty((T_per, D), dtype=torch.float32, device="cuda")
 
     def prefill():
         with torch.cuda.stream(st):
-            hp.copy_(h0)
-        ctx.forward_stack(0, layers, hp.data_ptr(), STREAM_PREFILL, 1e-6, cs)
+            hp.copy_(h0[rank * T_per:(rank + 1) * T_per])
+        ctx.forward_stack(0, layers, hp.data_ptr(), T_per, 1e-6, cs)
 
     pre = leg(prefill, STREAM_PREFILL)
     ctx.close()
     return {"workload": f"config4: {layers} of the 76 stack layers streamed from pinned host memory, "
-                        f"HBM pool {pool / 2 ** 30:.2f} GiB (8 GiB x {layers}/76), Zipf(1.1) with a "
-                        "per-layer permutation, prefetch depth 2",
-            "layers": layers, "pool_bytes": pool, "host_store_bytes": layers * store_per_layer,
+                        f"HBM pool {pool / 2 ** 30:.2f} GiB per GPU (8 GiB x {layers}/76), Zipf(1.1) "
+                        "with a per-layer permutation, prefetch depth 2",
+            "ranks": world, "parallelism": f"ep{world}" if world > 1 else "single GPU",
+            "layers": layers, "pool_bytes_per_gpu": pool, "host_store_bytes": layers * store_all,
             "host_mem_available": avail, "decode_batch1": dec,
             "prefill": {**pre, "tokens": STREAM_PREFILL}, "weights_generated_s": synth_s,
-            "timing": "CUDA events on the stream; the host's waits for fills are inside",
+            "timing": "CUDA events on the stream, max over ranks; the host's waits for fills are inside",
             "note": "fills and prefetches wait for their copies on the host (no overlap with compute)"}
 
 
@@ -615,7 +641,21 @@ def main():
         run_stack_eager(args.stack_eager)
         return
     if args.stream_only:
-        print(json.dumps(measure_stream(args.stream_only)), flush=True)
+        import torch
+        import torch.distributed as dist
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        if world > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        r = measure_stream(rank, world, local, layers=args.stream_only)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return
     if args.stack_only:
         import torch
@@ -784,9 +824,7 @@ def main():
 
     stream = None
     if not args.no_stream:
-        stream = (measure_stream() if world == 1 else
-                  {"unavailable": "streaming contexts are single-GPU in this build "
-                                  "(expert parallelism needs every local expert resident)"})
+        stream = measure_stream(rank, world, local)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -69,7 +69,7 @@ struct qmoe_ctx {
     int *free_slots;
     int nfree;
     qmoe_cache *cache;
-    uint8_t *host_store;   /* pinned [num_layers * E * slot_bytes] when streaming */
+    uint8_t *host_store;   /* pinned [num_layers][local experts] slots when streaming */
     /* the pool holds nslots routed slots followed by one shared-expert slot
        per layer (slot nslots + layer), so TMA descriptors cover both */
     qk_prefill *prefill;   /* tcgen05 multi-token path, NULL if the shape is not covered */
@@ -94,6 +94,7 @@ struct qmoe_ctx {
     /* expert parallelism */
     int ep_world, ep_rank, ep_lo, ep_hi; /* experts [ep_lo, ep_hi) are local */
     ncclComm_t ep_comm;
+    int32_t *ep_recv_pin;  /* streaming: pinned copy of the received rows' expert ids */
     /* MoE-only stack: the normalised layer input and the layer output */
     float *stk_xn, *stk_y; /* fp32 [max_tokens, d] each */
 };
@@ -279,6 +280,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     if (c->cache) qmoe_cache_free(c->cache);
     qk_prefill_destroy(c->prefill);
     if (c->ep_comm) nccl_api()->comm_destroy(c->ep_comm);
+    cudaFreeHost(c->ep_recv_pin);
     if (c->copy_done) cudaEventDestroy(c->copy_done);
     for (int i = 0; i < 8; i++)
         if (c->pev[i]) cudaEventDestroy(c->pev[i]);
@@ -323,9 +325,9 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     c->ep_world = cfg->ep_world > 1 ? cfg->ep_world : 1;
     c->ep_rank = c->ep_world > 1 ? cfg->ep_rank : 0;
     if (c->ep_world > 1 && (E % c->ep_world || c->ep_rank < 0 || c->ep_rank >= c->ep_world ||
-                            cfg->pool_bytes != 0 || c->ep_world > 64)) {
-        seterr(err, "qmoe_create: expert parallelism needs E %% ep_world == 0, 0 <= ep_rank < "
-                    "ep_world <= 64 and every local expert resident (pool_bytes = 0)");
+                            c->ep_world > 64)) {
+        seterr(err, "qmoe_create: expert parallelism needs E %% ep_world == 0 and "
+                    "0 <= ep_rank < ep_world <= 64");
         free(c);
         return NULL;
     }
@@ -410,8 +412,8 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
             seterr(err, "qmoe_create: out of host memory");
             goto fail;
         }
-        if (!c->resident_all) {
-            size_t hs = (size_t)total * L->slot_bytes;
+        if (!c->resident_all) { /* the local experts only */
+            size_t hs = (size_t)local * L->slot_bytes;
             CK(cudaHostAlloc((void **)&c->host_store, hs, cudaHostAllocPortable));
         }
     }
@@ -437,6 +439,9 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
             goto fail;
         }
         CK((cudaError_t)qk_ep_alloc(c->prefill, T, c->ep_world));
+        if (!c->resident_all)
+            CK(cudaMallocHost((void **)&c->ep_recv_pin,
+                              (size_t)c->ep_world * T * L->k * sizeof(int32_t)));
     } else if (T > 1) {
         char msg[256] = {0};
         c->prefill = qk_prefill_create(L, T, c->pool, c->nslots + Lz, c->num_sms, msg, sizeof(msg));
@@ -451,6 +456,12 @@ fail:
 /* ------------------------------------------------------------- pool fills */
 
 static uint64_t ekey(int layer, int e) { return ((uint64_t)(uint32_t)layer << 32) | (uint32_t)e; }
+
+/* A local expert's slot in the pinned host store (streaming contexts). */
+static uint8_t *store_slot(const qmoe_ctx *c, int layer, int e) {
+    const size_t el = (size_t)(c->ep_hi - c->ep_lo);
+    return c->host_store + ((size_t)layer * el + (size_t)(e - c->ep_lo)) * c->L.slot_bytes;
+}
 
 /* Assigns a slot to (layer, e) in the bookkeeping; evicted owners lose their
  * table entries. Returns the slot or -1 when the cache rejects the entry (all
@@ -516,6 +527,12 @@ static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qm
             rc = -1;
             break;
         }
+        if (e < c->ep_lo || e >= c->ep_hi) {
+            seterr(err, "qmoe_experts_load: expert %d is not one of this rank's [%d, %d)", e,
+                   c->ep_lo, c->ep_hi);
+            rc = -1;
+            break;
+        }
         if (qmoe_cache_peek(c->cache, ekey(layer, e), NULL)) {
             ours[i] = (unsigned char)qmoe_cache_pin(c->cache, ekey(layer, e));
             continue;
@@ -533,7 +550,7 @@ static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qm
             break;
         }
         ours[i] = 1;
-        const uint8_t *src = c->host_store + ((size_t)layer * L->E + e) * L->slot_bytes;
+        const uint8_t *src = store_slot(c, layer, e);
         cudaError_t ce = cudaMemcpyAsync(c->pool + (size_t)slot * L->slot_bytes, src,
                                          L->slot_bytes, cudaMemcpyHostToDevice, c->copy_stream);
         if (ce != cudaSuccess) {
@@ -689,7 +706,7 @@ int qmoe_upload_layer(qmoe_ctx *c, int layer, const qmoe_layer_weights *w, qmoe_
                 c->free_slots[c->nfree++] = (int)v;
             }
             c->slot_of_host[(size_t)layer * L->E + e] = -1;
-            pack_routed(c, w, e, c->host_store + ((size_t)layer * L->E + e) * L->slot_bytes);
+            if (e >= c->ep_lo && e < c->ep_hi) pack_routed(c, w, e, store_slot(c, layer, e));
         }
         pthread_mutex_unlock(&c->lock);
         CK(cudaMemcpy(c->slot_of_dev + (size_t)layer * L->E, c->slot_of_host + (size_t)layer * L->E,
@@ -767,12 +784,12 @@ int qmoe_synth_layer_dev(qmoe_ctx *c, int layer, uint64_t seed, double zipf_s, q
         }
         pthread_mutex_unlock(&c->lock);
         CK(cudaMalloc((void **)&stage, (size_t)stage_slots * L->slot_bytes));
-        for (int e0 = 0; e0 < L->E; e0 += stage_slots) {
-            const int nb = L->E - e0 < stage_slots ? L->E - e0 : stage_slots;
+        for (int e0 = c->ep_lo; e0 < c->ep_hi; e0 += stage_slots) {
+            const int nb = c->ep_hi - e0 < stage_slots ? c->ep_hi - e0 : stage_slots;
             for (int i = 0; i < nb; i++)
                 CK((cudaError_t)qk_synth_slot(L, stage + (size_t)i * L->slot_bytes, e0 + i, rk, st));
-            CK(cudaMemcpyAsync(c->host_store + ((size_t)layer * L->E + e0) * L->slot_bytes, stage,
-                               (size_t)nb * L->slot_bytes, cudaMemcpyDeviceToHost, st));
+            CK(cudaMemcpyAsync(store_slot(c, layer, e0), stage, (size_t)nb * L->slot_bytes,
+                               cudaMemcpyDeviceToHost, st));
             CK(cudaStreamSynchronize(st));
         }
         cudaFree(stage);
@@ -1333,7 +1350,7 @@ int qmoe_prefetch(qmoe_ctx *c, int layer, const int64_t *ids, size_t n) {
     if (cudaStreamSynchronize(c->stream) != cudaSuccess) return 0;
     for (size_t i = 0; i < n; i++) {
         int ex = (int)ids[i];
-        if (ex < 0 || ex >= c->L.E) continue;
+        if (ex < c->ep_lo || ex >= c->ep_hi) continue; /* not this rank's */
         if (qmoe_cache_peek(c->cache, ekey(layer, ex), NULL)) continue;
         int64_t one = ex;
         if (fill_experts(c, layer, &one, 1, &e) == 0) {
@@ -1541,6 +1558,50 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
             "qmoe_forward_ep dispatch");
     }
     NCK(nc->group_end(), "qmoe_forward_ep");
+    if (!c->resident_all) {
+        /* streaming pool: the rows received name this rank's experts; fill
+         * the missing ones before the grouped pass reads the pool */
+        const size_t nr = (size_t)W * cap * k;
+        cudaError_t ce = cudaMemcpyAsync(c->ep_recv_pin, b.recv_e + own * k, nr * sizeof(int32_t),
+                                         cudaMemcpyDeviceToHost, st);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+        if (ce != cudaSuccess) {
+            seterr(err, "qmoe_forward_ep: %s", cudaGetErrorString(ce));
+            return -1;
+        }
+        int64_t *uniq = calloc(nr ? nr : 1, sizeof(int64_t));
+        unsigned char *seen = calloc((size_t)c->L.E, 1);
+        if (!uniq || !seen) {
+            free(uniq);
+            free(seen);
+            seterr(err, "qmoe_forward_ep: out of host memory");
+            return -1;
+        }
+        size_t nu = 0;
+        for (size_t i = 0; i < nr; i++) {
+            const int e = c->ep_recv_pin[i];
+            if (e < 0 || e >= c->L.E || seen[e]) continue;
+            seen[e] = 1;
+            uniq[nu++] = e;
+            const int resident = qmoe_cache_peek(c->cache, ekey(layer, e), NULL);
+            c->stats.routed_lookups++;
+            c->stats.routed_hits += (uint64_t)resident;
+            unsigned char *pm = c->pf_mark + (size_t)layer * c->L.E + e;
+            if (*pm) {
+                if (resident) c->stats.prefetch_hits++;
+                *pm = 0;
+            }
+        }
+        free(seen);
+        int rc = fill_experts(c, layer, uniq, nu, err);
+        if (rc == 0) {
+            pthread_mutex_lock(&c->lock);
+            for (size_t i = 0; i < nu; i++) qmoe_cache_get(c->cache, ekey(layer, (int)uniq[i]), NULL);
+            pthread_mutex_unlock(&c->lock);
+        }
+        free(uniq);
+        if (rc) return -1;
+    }
     /* this rank's experts over the rows it received, combined per row */
     if (kerr(qk_ep_experts(c->prefill, &f, c->nslots + layer, st), "ep experts", err)) return -1;
     /* partial rows back to the ranks that own the tokens */
@@ -1586,16 +1647,21 @@ int qmoe_forward_stack(qmoe_ctx *c, int l0, int l1, float *h, int n, float eps, 
         else rc = n > 0 ? qmoe_forward_dev(c, l, c->stk_xn, QMOE_F32, n, c->stk_y, st, err) : 0;
         if (rc) return -1;
         if (!c->resident_all && n > 0) {
-            /* streaming: the layer's routing is on the host (it chose the
-             * fills); route statistics and predicted prefetches follow it, as
-             * model.py:458-459 calls record_route and prefetch_predictions */
+            /* streaming: route statistics and predicted prefetches follow the
+             * layer's routing (on the host already, or read back here on an
+             * expert-parallel context), as model.py:458-459 calls
+             * record_route and prefetch_predictions */
             const size_t nk = (size_t)n * c->L.k;
-            qmoe_record_route(c, l, c->idx_pin, nk);
-            /* a prefetch may evict a slot this layer's kernels still read */
-            if (cudaStreamSynchronize(st) != cudaSuccess) {
+            cudaError_t ce = cudaSuccess;
+            if (c->ep_world > 1)
+                ce = cudaMemcpyAsync(c->idx_pin, c->idx, nk * sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+            /* (and a prefetch may evict a slot this layer's kernels still read) */
+            if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+            if (ce != cudaSuccess) {
                 seterr(err, "qmoe_forward_stack: layer %d failed on the device", l);
                 return -1;
             }
+            qmoe_record_route(c, l, c->idx_pin, nk);
             qmoe_prefetch_predictions(c, l, c->idx_pin, nk);
         }
     }

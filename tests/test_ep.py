@@ -278,3 +278,81 @@ def test_expert_parallel_stack_two_gpus(built):
         delta, rdelta = results[r] - h0, ref - h0   # relative RMS: see test_stack._check
         rr = float(np.linalg.norm(delta - rdelta) / np.linalg.norm(rdelta))
         assert rr <= 1e-3, (r, rr)
+
+
+def _ep_stream_rank(rank, world, uid_q, out_q, n_layers, pool_slots):
+    import sys
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "qwen3.8-flash-next_b200"))
+    import torch
+
+    import qmoe
+    torch.cuda.set_device(rank)
+    d, E, k, I = 2048, 512, 10, 512
+    T_per = 8
+    slot = qmoe.lib().qmoe_slot_bytes(qmoe.make_config(d, E, k, I))
+    outs = []
+    for pool in (0, pool_slots):   # resident, then streaming from the pinned host store
+        cfg = qmoe.make_config(d, E, k, I, layers=n_layers, max_tokens=T_per, device=rank,
+                               ep_rank=rank, ep_world=world, prefetch=2,
+                               pool_bytes=pool * slot)
+        ctx = qmoe.Context(cfg)
+        for l in range(n_layers):
+            ctx.synth_layer_dev(l, 20261203, 1.1)
+        if rank == 0:
+            uid = qmoe.ep_unique_id()
+            for _ in range(world - 1):
+                uid_q.put(uid)
+        else:
+            uid = uid_q.get(timeout=120)
+        ctx.ep_connect(uid)
+        st = torch.cuda.Stream()
+        res = []
+        # every rank with tokens, then the batch-1 decode form (rank 0 only)
+        for n in (T_per, 1 if rank == 0 else 0):
+            h = torch.from_numpy(qmoe.synth_tokens(20261203, 80 + rank, T_per, d)).cuda()
+            torch.cuda.synchronize()
+            ctx.forward_stack(0, n_layers, h.data_ptr(), n, 1e-6, st.cuda_stream)
+            st.synchronize()
+            res.append(h[:n].cpu().numpy())
+        ctx.sync()
+        s = ctx.stats()
+        outs.append((res, int(s["expert_loads"]), int(s["routed_lookups"])))
+        ctx.close()
+    out_q.put((rank, outs))
+
+
+@pytest.mark.gpu
+def test_expert_parallel_streaming_stack_two_gpus(built):
+    """Two GPUs, expert-parallel, each rank streaming its own experts from a
+    pinned host store into a small pool: the stack's outputs equal the
+    resident expert-parallel stack's bit for bit, for a call with tokens on
+    both ranks and for the batch-1 decode form (the token on rank 0, rank 1
+    serving its experts with no tokens of its own)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    world, n_layers = 2, 3
+    ctx = mp.get_context("spawn")
+    uid_q, out_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_ep_stream_rank, args=(r, world, uid_q, out_q, n_layers, 128))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            r, o = out_q.get(timeout=600)
+            results[r] = o
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for r in range(world):
+        (res_a, loads_a, _), (res_b, loads_b, lookups_b) = results[r]
+        assert loads_a == 0 and loads_b > 0 and lookups_b > 0, (r, loads_a, loads_b, lookups_b)
+        for a, b in zip(res_a, res_b):
+            assert a.shape == b.shape and np.array_equal(a, b), r
