@@ -58,9 +58,11 @@ typedef struct {
     int ep_rank;         /* expert parallelism: this context's rank ... */
     int ep_world;        /* ... of ep_world (0 or 1: no expert parallelism). Rank
                             g holds experts [g E/W, (g+1) E/W) of every layer
-                            (E % W == 0, every expert resident) and serves
-                            qmoe_forward_ep; max_tokens is the per-rank token
-                            count of one call */
+                            (E % W == 0) and serves qmoe_forward_ep;
+                            max_tokens is the per-rank token count of one
+                            call. With pool_bytes below the rank's share the
+                            rank streams its own experts from a pinned host
+                            store of those experts only */
 } qmoe_config;
 
 /* One affine 4-bit tensor in the reference checkpoint layout: `rows` rows of
@@ -351,6 +353,85 @@ void qmoe_synth_zipf_bias(uint64_t seed, int layer, int E, double s,
  * qmoe_synth_layer's by one bf16 unit in rare elements. */
 int qmoe_synth_layer_dev(qmoe_ctx *ctx, int layer, uint64_t seed, double zipf_s,
                          qmoe_err *err);
+
+/* ---- checkpoint reader: safetensors files straight into the pools ----
+ * The reference's storage layer on the MoE path (c/src/safetensors.h:1-76,
+ * c/src/reader.c:11-112, src/colibri_runtime/storage.py:69-291): every
+ * *.safetensors file of a directory is indexed at open, with the same
+ * validation (header length, JSON, dtype, shape, offsets matching the size
+ * and inside the file, no duplicate names, no overlapping ranges) and the
+ * same name normalisation (a leading "language_model." is dropped; a lookup
+ * of "model.x" also tries "language_model.model.x"). Reads are pread(2) on
+ * io_workers threads. The index is read-only after open: reads may run
+ * from several threads at once. */
+typedef struct qmoe_ckpt qmoe_ckpt;
+
+/* safetensors dtypes, in the order of st_dtype (c/src/safetensors.h:10-25) */
+enum {
+    QMOE_ST_BOOL, QMOE_ST_U8, QMOE_ST_I8, QMOE_ST_U16, QMOE_ST_I16, QMOE_ST_U32, QMOE_ST_I32,
+    QMOE_ST_U64, QMOE_ST_I64, QMOE_ST_F16, QMOE_ST_BF16, QMOE_ST_F32, QMOE_ST_F64, QMOE_ST_COUNT
+};
+
+typedef struct {
+    int dtype;         /* QMOE_ST_* */
+    int ndim;
+    int64_t shape[8];
+    uint64_t nbytes;
+    uint64_t row_bytes; /* nbytes / shape[0]; 0 for a scalar or empty tensor */
+    int file;          /* index of its file, files in name order */
+    uint64_t offset;   /* byte offset of its data in that file */
+} qmoe_tensor_info;
+
+/* I/O counters, as IOStats (storage.py:60-66) and st_index's counters
+ * (c/src/safetensors.h:43-48): pread_calls counts system calls; bytes_read
+ * the bytes those reads returned (a row read once however often it was
+ * requested); rows_read the rows requested; tensors_read the whole tensors. */
+typedef struct {
+    uint64_t pread_calls, bytes_read, rows_read, tensors_read;
+    double read_seconds;
+} qmoe_io_stats;
+
+/* st_index_open / st_index_close (c/src/safetensors.h:54-58) */
+qmoe_ckpt *qmoe_ckpt_open(const char *dir, int io_workers, qmoe_err *err);
+void qmoe_ckpt_close(qmoe_ckpt *ck);
+/* tensors in name order (normalised names) */
+size_t qmoe_ckpt_count(const qmoe_ckpt *ck);
+const char *qmoe_ckpt_name(const qmoe_ckpt *ck, size_t i);
+/* st_find (c/src/safetensors.h:60): 0 and *out, or -1 when absent */
+int qmoe_ckpt_find(const qmoe_ckpt *ck, const char *name, qmoe_tensor_info *out);
+/* st_read_tensor (c/src/safetensors.h:63): the whole tensor into out */
+int qmoe_ckpt_read_tensor(qmoe_ckpt *ck, const char *name, void *out, size_t out_bytes,
+                          qmoe_err *err);
+/* st_read_rows (c/src/safetensors.h:67-68): rows of dimension 0 into out in
+ * request order; repeated rows are read once; contiguous rows share a read */
+int qmoe_ckpt_read_rows(qmoe_ckpt *ck, const char *name, const int64_t *rows, size_t n,
+                        void *out, size_t out_bytes, qmoe_err *err);
+int qmoe_ckpt_io_stats(const qmoe_ckpt *ck, qmoe_io_stats *out);
+
+/* Bytes of the host buffer qmoe_ckpt_read_layer fills for one layer. */
+size_t qmoe_ckpt_layer_bytes(const qmoe_config *cfg);
+/* One MoE layer's tensors (model.layers.<layer>.mlp.{gate, shared_expert_gate,
+ * switch_mlp.*, shared_expert.*}, c/src/model.c:1902-1923, :541-585) read
+ * into buf and *w pointed at them, ready for qmoe_upload_layer. The router
+ * and the shared gate must be dense BF16 (model.c:262-265), weights U32 and
+ * scales/biases BF16 of the configured shapes; a missing biases tensor of the
+ * shared expert reads as zeros (model.c:251-257). logit_bias is NULL. */
+int qmoe_ckpt_read_layer(qmoe_ckpt *ck, const qmoe_config *cfg, int layer, void *buf,
+                         size_t buf_bytes, qmoe_layer_weights *w, qmoe_err *err);
+/* The rows of experts ids[0..n) of one layer (the nine rows experts_load
+ * reads, c/src/model.c:603-629) packed into n consecutive slots of
+ * qmoe_slot_bytes each, the layout of the HBM pool. */
+int qmoe_ckpt_pack_experts(qmoe_ckpt *ck, const qmoe_config *cfg, int layer,
+                           const int64_t *ids, size_t n, void *slots, size_t slots_bytes,
+                           qmoe_err *err);
+/* One expert of host weights packed into a slot (expert -1: the shared
+ * expert); the packing qmoe_upload_layer does. */
+int qmoe_pack_expert(const qmoe_config *cfg, const qmoe_layer_weights *w, int expert,
+                     void *slot);
+/* qmoe_ckpt_read_layer of checkpoint layer ckpt_layer, then
+ * qmoe_upload_layer into the context's layer `layer`. */
+int qmoe_upload_layer_ckpt(qmoe_ctx *ctx, int layer, qmoe_ckpt *ck, int ckpt_layer,
+                           qmoe_err *err);
 
 const char *qmoe_version(void);
 

@@ -1446,6 +1446,26 @@ int qmoe_prefetch_predictions(qmoe_ctx *c, int layer, const int32_t *selected, s
     return q;
 }
 
+int qmoe_upload_layer_ckpt(qmoe_ctx *c, int layer, qmoe_ckpt *ck, int ckpt_layer,
+                           qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || !ck) {
+        seterr(err, "qmoe_upload_layer_ckpt: no context or checkpoint");
+        return -1;
+    }
+    const size_t nb = qmoe_ckpt_layer_bytes(&c->cfg);
+    void *buf = nb ? malloc(nb) : NULL;
+    if (!buf) {
+        seterr(err, "qmoe_upload_layer_ckpt: out of host memory (%zu bytes)", nb);
+        return -1;
+    }
+    qmoe_layer_weights w;
+    int rc = qmoe_ckpt_read_layer(ck, &c->cfg, ckpt_layer, buf, nb, &w, err);
+    if (rc == 0) rc = qmoe_upload_layer(c, layer, &w, err);
+    free(buf);
+    return rc;
+}
+
 const char *qmoe_version(void) { return "qmoe-b200 0.1 (sm_100a)"; }
 
 /* ------------------------------------------------- expert parallelism */

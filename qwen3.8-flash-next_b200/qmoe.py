@@ -89,6 +89,27 @@ class TokenArgs(C.Structure):
 
 NOALLOC_SCRATCH_BYTES = 64 * 1024
 
+# safetensors dtypes (QMOE_ST_*): name, numpy type
+ST_DTYPES = [("BOOL", np.bool_), ("U8", np.uint8), ("I8", np.int8), ("U16", np.uint16),
+             ("I16", np.int16), ("U32", np.uint32), ("I32", np.int32), ("U64", np.uint64),
+             ("I64", np.int64), ("F16", np.float16), ("BF16", np.uint16), ("F32", np.float32),
+             ("F64", np.float64)]
+
+
+class TensorInfo(C.Structure):
+    _fields_ = [("dtype", C.c_int), ("ndim", C.c_int), ("shape", C.c_int64 * 8),
+                ("nbytes", C.c_uint64), ("row_bytes", C.c_uint64), ("file", C.c_int),
+                ("offset", C.c_uint64)]
+
+
+class IOStats(C.Structure):
+    _fields_ = [("pread_calls", C.c_uint64), ("bytes_read", C.c_uint64),
+                ("rows_read", C.c_uint64), ("tensors_read", C.c_uint64),
+                ("read_seconds", C.c_double)]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
 
 # every symbol include/qmoe.h declares, with (restype, argtypes)
 _P = C.c_void_p
@@ -143,6 +164,22 @@ SIGNATURES = {
                                    C.POINTER(LayerWeights), C.c_int, C.c_int]),
     "qmoe_synth_tokens": (None, [C.c_uint64, C.c_uint64, C.c_int, C.c_int, _P]),
     "qmoe_synth_zipf_bias": (None, [C.c_uint64, C.c_int, C.c_int, C.c_double, _P]),
+    "qmoe_ckpt_open": (_P, [C.c_char_p, C.c_int, C.POINTER(Err)]),
+    "qmoe_ckpt_close": (None, [_P]),
+    "qmoe_ckpt_count": (C.c_size_t, [_P]),
+    "qmoe_ckpt_name": (C.c_char_p, [_P, C.c_size_t]),
+    "qmoe_ckpt_find": (C.c_int, [_P, C.c_char_p, C.POINTER(TensorInfo)]),
+    "qmoe_ckpt_read_tensor": (C.c_int, [_P, C.c_char_p, _P, C.c_size_t, C.POINTER(Err)]),
+    "qmoe_ckpt_read_rows": (C.c_int, [_P, C.c_char_p, _P, C.c_size_t, _P, C.c_size_t,
+                                      C.POINTER(Err)]),
+    "qmoe_ckpt_io_stats": (C.c_int, [_P, C.POINTER(IOStats)]),
+    "qmoe_ckpt_layer_bytes": (C.c_size_t, [C.POINTER(Config)]),
+    "qmoe_ckpt_read_layer": (C.c_int, [_P, C.POINTER(Config), C.c_int, _P, C.c_size_t,
+                                       C.POINTER(LayerWeights), C.POINTER(Err)]),
+    "qmoe_ckpt_pack_experts": (C.c_int, [_P, C.POINTER(Config), C.c_int, _P, C.c_size_t, _P,
+                                         C.c_size_t, C.POINTER(Err)]),
+    "qmoe_pack_expert": (C.c_int, [C.POINTER(Config), C.POINTER(LayerWeights), C.c_int, _P]),
+    "qmoe_upload_layer_ckpt": (C.c_int, [_P, C.c_int, _P, C.c_int, C.POINTER(Err)]),
     "qmoe_version": (C.c_char_p, []),
 }
 
@@ -230,6 +267,113 @@ class QmoeError(RuntimeError):
     pass
 
 
+def pack_expert(cfg: Config, w: LayerWeights, expert: int) -> np.ndarray:
+    """One expert of host weights in the HBM slot layout (expert -1: the
+    shared expert)."""
+    L = lib()
+    out = np.empty(L.qmoe_slot_bytes(C.byref(cfg)), np.uint8)
+    if L.qmoe_pack_expert(C.byref(cfg), C.byref(w), expert, ptr(out)) != 0:
+        raise QmoeError(f"qmoe_pack_expert failed for expert {expert}")
+    return out
+
+
+class Checkpoint:
+    """A directory of safetensors files (qmoe_ckpt_*): the index, whole-tensor
+    and row reads, and the MoE layer / expert-slot readers."""
+
+    def __init__(self, path, io_workers: int = 4):
+        err = Err()
+        self.h = lib().qmoe_ckpt_open(os.fsencode(path), io_workers, C.byref(err))
+        if not self.h:
+            raise QmoeError(err.text())
+
+    def close(self):
+        if self.h:
+            lib().qmoe_ckpt_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *_):
+        self.close()
+
+    def __getattribute__(self, name):
+        # every reader method needs an open index (storage.py:265-268)
+        if name in ("names", "find", "read_tensor", "read_rows", "stats", "read_layer",
+                    "pack_experts") and object.__getattribute__(self, "h") is None:
+            raise QmoeError("checkpoint index is closed")
+        return object.__getattribute__(self, name)
+
+    def names(self) -> list[str]:
+        L = lib()
+        return [L.qmoe_ckpt_name(self.h, i).decode() for i in range(L.qmoe_ckpt_count(self.h))]
+
+    def find(self, name: str) -> dict | None:
+        t = TensorInfo()
+        if lib().qmoe_ckpt_find(self.h, name.encode(), C.byref(t)) != 0:
+            return None
+        return {"dtype": ST_DTYPES[t.dtype][0], "shape": tuple(t.shape[:t.ndim]),
+                "nbytes": t.nbytes, "row_bytes": t.row_bytes, "file": t.file, "offset": t.offset}
+
+    def _info(self, name):
+        t = TensorInfo()
+        if lib().qmoe_ckpt_find(self.h, name.encode(), C.byref(t)) != 0:
+            raise KeyError(name)
+        return t, ST_DTYPES[t.dtype][1], tuple(t.shape[:t.ndim])
+
+    def read_tensor(self, name: str) -> np.ndarray:
+        t, dt, shape = self._info(name)
+        out = np.empty(t.nbytes, np.uint8)
+        err = Err()
+        if lib().qmoe_ckpt_read_tensor(self.h, name.encode(), ptr(out), out.nbytes, C.byref(err)):
+            raise QmoeError(err.text())
+        return out.view(dt).reshape(shape)
+
+    def read_rows(self, name: str, rows) -> np.ndarray:
+        t, dt, shape = self._info(name)
+        r = np.ascontiguousarray(np.asarray(list(rows), np.int64))
+        out = np.empty(len(r) * t.row_bytes, np.uint8)
+        err = Err()
+        if lib().qmoe_ckpt_read_rows(self.h, name.encode(), ptr(r), len(r), ptr(out), out.nbytes,
+                                     C.byref(err)):
+            raise QmoeError(err.text())
+        return out.view(dt).reshape((len(r),) + shape[1:])
+
+    def stats(self) -> dict:
+        s = IOStats()
+        lib().qmoe_ckpt_io_stats(self.h, C.byref(s))
+        return s.as_dict()
+
+    def read_layer(self, cfg: Config, layer: int):
+        """(buffer, LayerWeights pointing into it) for qmoe_upload_layer."""
+        L = lib()
+        buf = np.empty(L.qmoe_ckpt_layer_bytes(C.byref(cfg)), np.uint8)
+        w = LayerWeights()
+        err = Err()
+        if L.qmoe_ckpt_read_layer(self.h, C.byref(cfg), layer, ptr(buf), buf.nbytes, C.byref(w),
+                                  C.byref(err)):
+            raise QmoeError(err.text())
+        return buf, w
+
+    def pack_experts(self, cfg: Config, layer: int, ids) -> np.ndarray:
+        L = lib()
+        r = np.ascontiguousarray(np.asarray(list(ids), np.int64))
+        sb = L.qmoe_slot_bytes(C.byref(cfg))
+        out = np.empty((len(r), sb), np.uint8)
+        err = Err()
+        if L.qmoe_ckpt_pack_experts(self.h, C.byref(cfg), layer, ptr(r), len(r), ptr(out),
+                                    out.nbytes, C.byref(err)):
+            raise QmoeError(err.text())
+        return out
+
+
 class Context:
     """Owns one qmoe_ctx (one GPU)."""
 
@@ -259,6 +403,13 @@ class Context:
         err = Err()
         w = s.weights()
         self._chk(lib().qmoe_upload_layer(self.h, layer, C.byref(w), C.byref(err)), err)
+
+    def upload_ckpt(self, layer: int, ck: Checkpoint, ckpt_layer: int | None = None):
+        """Checkpoint layer ckpt_layer (default: layer) into this context's layer."""
+        err = Err()
+        rc = lib().qmoe_upload_layer_ckpt(self.h, layer, ck.h, layer if ckpt_layer is None else ckpt_layer,
+                                          C.byref(err))
+        self._chk(rc, err)
 
     def forward(self, layer: int, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32)
