@@ -288,12 +288,16 @@ int qmoe_stats_get(qmoe_ctx *ctx, qmoe_stats *out);
  * number filled (ExpertStore.request(prefetch=True)); 0 on a resident
  * context. */
 int qmoe_prefetch(qmoe_ctx *ctx, int layer, const int64_t *ids, size_t n);
-/* Records one step's selected experts for the route statistics
- * (ExpertStore.record_route). */
+/* Records one step's routing, every token's k experts (ExpertStore.record_route,
+ * streaming.py:400-413, called with idx.reshape(-1) at model.py:458): the
+ * context's predictor (qmoe_predictor_record) with the pool as the cache whose
+ * hot marks it sets. */
 void qmoe_record_route(qmoe_ctx *ctx, int layer, const int32_t *experts,
                        size_t n);
-/* Predicts and queues prefetches for this layer and the next from the route
- * statistics (ExpertStore.prefetch_predictions). Returns the number queued. */
+/* Predicts and fills prefetches for this layer and the next from the route
+ * statistics (ExpertStore.prefetch_predictions, streaming.py:415-435, called
+ * with the step's distinct experts in ascending order at model.py:459).
+ * Returns the number filled. */
 int qmoe_prefetch_predictions(qmoe_ctx *ctx, int layer,
                               const int32_t *selected, size_t n);
 
@@ -319,6 +323,38 @@ int qmoe_cache_mark_hot(qmoe_cache *c, uint64_t key, int hot);
 /* removes the entry; 1 if it existed */
 int qmoe_cache_erase(qmoe_cache *c, uint64_t key, uint64_t *value);
 qmoe_cache_stats qmoe_cache_stats_get(qmoe_cache *c);
+
+/* ---- host-side route predictor (ExpertStore's route statistics,
+ *      streaming.py:400-435 and :445-453), usable without a GPU; a streaming
+ *      context owns one (qmoe_record_route / qmoe_prefetch_predictions).
+ *      Rankings are Counter.most_common's: by count, ties to the key inserted
+ *      first. Not internally locked. ---- */
+typedef struct qmoe_predictor qmoe_predictor;
+qmoe_predictor *qmoe_predictor_new(int num_layers, int num_experts);
+void qmoe_predictor_free(qmoe_predictor *p);
+/* One step's routed experts (all token assignments, duplicates counted):
+ * transitions from the layer's previous selected set to this one, the routed
+ * counts, the new selected set (its distinct experts, ascending, also
+ * written to selected_out when not NULL, capacity num_experts), and, when
+ * cache is not NULL, the hot mark of each selected key ((layer << 32) | e)
+ * set to count >= 4. Returns the number selected, or -1 (nothing changed)
+ * for an expert out of range. */
+int qmoe_predictor_record(qmoe_predictor *p, qmoe_cache *cache, int layer,
+                          const int32_t *experts, size_t n, int32_t *selected_out);
+/* The predicted prefetches after a step of `layer` that selected
+ * selected[0..n): up to depth experts of this layer (pick) and up to depth of
+ * the next layer (next), each in rank order. depth <= 0 predicts nothing. */
+int qmoe_predictor_predict(qmoe_predictor *p, int layer, const int32_t *selected, size_t n,
+                           int depth, int64_t *pick, int *npick, int64_t *next, int *nnext);
+uint64_t qmoe_predictor_count(const qmoe_predictor *p, int layer, int expert);
+/* token assignments recorded (StreamStats.routes) */
+uint64_t qmoe_predictor_routes(const qmoe_predictor *p);
+/* the `want` most routed (layer, expert) pairs (snapshot's frequent_experts);
+ * returns how many were written */
+int qmoe_predictor_frequent(const qmoe_predictor *p, int want, int32_t *layer,
+                            int32_t *expert, uint64_t *count);
+/* The context's predictor (NULL on a resident context), for reading. */
+const qmoe_predictor *qmoe_ctx_predictor(const qmoe_ctx *ctx);
 
 /* ---- seeded synthetic layers (host; benchmark and test inputs) ----
  * Counter-based splitmix64 streams keyed by (seed, layer, tensor). Nibbles

@@ -8,7 +8,8 @@
  *                                             of pread + fp32 dequant)
  *   expert cache  c/src/cache.c            -> qmoe_cache over HBM slot numbers
  *   route stats / prefetch, streaming.py:400-435 -> qmoe_record_route,
- *                                             qmoe_prefetch_predictions
+ *                                             qmoe_prefetch_predictions (the
+ *                                             predictor is qmoe_predict.c)
  *
  * The context owns every device buffer: router, shared gate and shared
  * expert per layer, the expert pool (fixed-size slots), the expert -> slot
@@ -80,12 +81,10 @@ struct qmoe_ctx {
     int32_t *idx_pin;
     int last_T;
     qmoe_stats stats;
-    /* route statistics (streaming.py:400-413) */
-    uint64_t *freq;        /* [num_layers * E] */
+    /* route statistics and prediction (streaming.py:400-435) */
+    qmoe_predictor *pred;
+    int32_t *sel_buf;       /* [E] one step's selected experts */
     unsigned char *pf_mark; /* [num_layers * E] filled by a prefetch, not yet routed to */
-    uint32_t *trans;       /* [num_layers * E * E], lazily allocated */
-    int32_t *recent;       /* [num_layers * k] last selection per layer */
-    int *recent_n;
     /* diagnostics: per-kernel event timing (qmoe_profile_forward) */
     int profile;
     int prof_kernels; /* kernels of the last forward: 1 (single launch) or 4 */
@@ -272,11 +271,9 @@ void qmoe_destroy(qmoe_ctx *c) {
     free(c->slot_of_host);
     free(c->slot_owner);
     free(c->free_slots);
-    free(c->freq);
+    qmoe_predictor_free(c->pred);
+    free(c->sel_buf);
     free(c->pf_mark);
-    free(c->trans);
-    free(c->recent);
-    free(c->recent_n);
     if (c->cache) qmoe_cache_free(c->cache);
     qk_prefill_destroy(c->prefill);
     if (c->ep_comm) nccl_api()->comm_destroy(c->ep_comm);
@@ -391,12 +388,11 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
         c->slot_of_host = malloc((size_t)total * sizeof(int32_t));
         c->slot_owner = malloc((size_t)c->nslots * sizeof(uint64_t));
         c->free_slots = malloc((size_t)c->nslots * sizeof(int));
-        c->freq = calloc((size_t)total, sizeof(uint64_t));
+        c->pred = qmoe_predictor_new(Lz, E);
+        c->sel_buf = malloc((size_t)E * sizeof(int32_t));
         c->pf_mark = calloc((size_t)total, 1);
-        c->recent = calloc((size_t)Lz * cfg->top_k * 4, sizeof(int32_t));
-        c->recent_n = calloc((size_t)Lz, sizeof(int));
-        if (!c->slot_of_host || !c->slot_owner || !c->free_slots || !c->freq || !c->recent ||
-            !c->recent_n || !c->pf_mark) {
+        if (!c->slot_of_host || !c->slot_owner || !c->free_slots || !c->pred || !c->sel_buf ||
+            !c->pf_mark) {
             seterr(err, "qmoe_create: out of host memory");
             goto fail;
         }
@@ -471,8 +467,10 @@ static int claim_slot(qmoe_ctx *c, int layer, int e, int pin) {
     uint64_t ev[64];
     size_t nev = 0;
     int slot = c->nfree > 0 ? c->free_slots[c->nfree - 1] : -1;
+    /* an expert routed at least four times enters hot (streaming.py:396-397) */
+    const int hot = qmoe_predictor_count(c->pred, layer, e) >= 4;
     if (!qmoe_cache_put(c->cache, key, slot >= 0 ? (uint64_t)slot : NO_OWNER, c->L.slot_bytes,
-                        pin, 0, ev, 64, &nev))
+                        pin, hot, ev, 64, &nev))
         return -1;
     if (slot >= 0) c->nfree--;
     for (size_t i = 0; i < nev && i < 64; i++) {
@@ -1363,88 +1361,27 @@ int qmoe_prefetch(qmoe_ctx *c, int layer, const int64_t *ids, size_t n) {
 }
 
 void qmoe_record_route(qmoe_ctx *c, int layer, const int32_t *experts, size_t n) {
-    if (!c || layer < 0 || layer >= c->cfg.num_layers || !experts) return;
-    const int E = c->L.E, K = c->L.k * 4;
+    if (!c || layer < 0 || layer >= c->cfg.num_layers) return;
     pthread_mutex_lock(&c->lock);
-    if (!c->trans) c->trans = calloc((size_t)c->cfg.num_layers * E * E, sizeof(uint32_t));
-    /* selected = sorted distinct experts of this step */
-    unsigned char *mark = calloc((size_t)E, 1);
-    int32_t sel[4096];
-    int ns = 0;
-    for (size_t i = 0; i < n; i++) {
-        int e = experts[i];
-        if (e < 0 || e >= E) continue;
-        c->freq[(size_t)layer * E + e]++;
-        if (mark && !mark[e]) mark[e] = 1;
-    }
-    if (mark)
-        for (int e = 0; e < E && ns < 4096; e++)
-            if (mark[e]) sel[ns++] = e;
-    free(mark);
-    int32_t *prev = c->recent + (size_t)layer * K;
-    if (c->trans)
-        for (int p = 0; p < c->recent_n[layer]; p++)
-            for (int s = 0; s < ns; s++)
-                c->trans[((size_t)layer * E + prev[p]) * E + sel[s]]++;
-    int keep = ns < K ? ns : K;
-    memcpy(prev, sel, (size_t)keep * sizeof(int32_t));
-    c->recent_n[layer] = keep;
-    for (int s = 0; s < ns; s++)
-        qmoe_cache_mark_hot(c->cache, ekey(layer, sel[s]), c->freq[(size_t)layer * E + sel[s]] >= 4);
+    qmoe_predictor_record(c->pred, c->cache, layer, experts, n, NULL);
     pthread_mutex_unlock(&c->lock);
-}
-
-/* the `count` highest scores, ties to the lower expert id */
-static int top_by_score(const uint64_t *score, int E, int count, int64_t *out) {
-    int got = 0;
-    for (int r = 0; r < count; r++) {
-        int best = -1;
-        for (int e = 0; e < E; e++) {
-            if (!score[e]) continue;
-            int taken = 0;
-            for (int i = 0; i < got; i++)
-                if (out[i] == e) { taken = 1; break; }
-            if (taken) continue;
-            if (best < 0 || score[e] > score[best]) best = e;
-        }
-        if (best < 0) break;
-        out[got++] = best;
-    }
-    return got;
 }
 
 int qmoe_prefetch_predictions(qmoe_ctx *c, int layer, const int32_t *selected, size_t n) {
     if (!c || layer < 0 || layer >= c->cfg.num_layers || c->cfg.prefetch_depth <= 0) return 0;
-    const int E = c->L.E, P = c->cfg.prefetch_depth;
-    uint64_t *cand = calloc((size_t)E, sizeof(uint64_t));
-    if (!cand) return 0;
-    int64_t pick[64];
+    const int P = c->cfg.prefetch_depth < 64 ? c->cfg.prefetch_depth : 64;
+    int64_t pick[64], next[64];
     int npick = 0, nnext = 0;
-    int64_t next[64];
     pthread_mutex_lock(&c->lock);
-    int any = 0;
-    if (c->trans)
-        for (size_t i = 0; i < n; i++) {
-            int s = selected[i];
-            if (s < 0 || s >= E) continue;
-            for (int e = 0; e < E; e++) {
-                uint32_t v = c->trans[((size_t)layer * E + s) * E + e];
-                if (v) { cand[e] += v; any = 1; }
-            }
-        }
-    if (!any)
-        for (int e = 0; e < E; e++) cand[e] += c->freq[(size_t)layer * E + e];
-    if (layer + 1 < c->cfg.num_layers)
-        for (int e = 0; e < E; e++) cand[e] += 2 * c->freq[(size_t)(layer + 1) * E + e];
-    npick = top_by_score(cand, E, P < 64 ? P : 64, pick);
-    if (layer + 1 < c->cfg.num_layers)
-        nnext = top_by_score(c->freq + (size_t)(layer + 1) * E, E, P < 64 ? P : 64, next);
+    int rc = qmoe_predictor_predict(c->pred, layer, selected, n, P, pick, &npick, next, &nnext);
     pthread_mutex_unlock(&c->lock);
-    free(cand);
+    if (rc) return 0;
     int q = qmoe_prefetch(c, layer, pick, (size_t)npick);
     if (nnext) q += qmoe_prefetch(c, layer + 1, next, (size_t)nnext);
     return q;
 }
+
+const qmoe_predictor *qmoe_ctx_predictor(const qmoe_ctx *c) { return c ? c->pred : NULL; }
 
 int qmoe_upload_layer_ckpt(qmoe_ctx *c, int layer, qmoe_ckpt *ck, int ckpt_layer,
                            qmoe_err *err) {
@@ -1681,8 +1618,12 @@ int qmoe_forward_stack(qmoe_ctx *c, int l0, int l1, float *h, int n, float eps, 
                 seterr(err, "qmoe_forward_stack: layer %d failed on the device", l);
                 return -1;
             }
-            qmoe_record_route(c, l, c->idx_pin, nk);
-            qmoe_prefetch_predictions(c, l, c->idx_pin, nk);
+            /* record every assignment; predict from the distinct experts in
+             * ascending order (np.unique at model.py:432) */
+            pthread_mutex_lock(&c->lock);
+            const int ns = qmoe_predictor_record(c->pred, c->cache, l, c->idx_pin, nk, c->sel_buf);
+            pthread_mutex_unlock(&c->lock);
+            if (ns > 0) qmoe_prefetch_predictions(c, l, c->sel_buf, (size_t)ns);
         }
     }
     if (l1 > l0 && kerr(qk_launch_residual_norm(h, c->stk_y, NULL, n, d, eps, st), "residual_norm", err))

@@ -180,6 +180,15 @@ SIGNATURES = {
                                          C.c_size_t, C.POINTER(Err)]),
     "qmoe_pack_expert": (C.c_int, [C.POINTER(Config), C.POINTER(LayerWeights), C.c_int, _P]),
     "qmoe_upload_layer_ckpt": (C.c_int, [_P, C.c_int, _P, C.c_int, C.POINTER(Err)]),
+    "qmoe_predictor_new": (_P, [C.c_int, C.c_int]),
+    "qmoe_predictor_free": (None, [_P]),
+    "qmoe_predictor_record": (C.c_int, [_P, _P, C.c_int, _P, C.c_size_t, _P]),
+    "qmoe_predictor_predict": (C.c_int, [_P, C.c_int, _P, C.c_size_t, C.c_int, _P,
+                                         C.POINTER(C.c_int), _P, C.POINTER(C.c_int)]),
+    "qmoe_predictor_count": (C.c_uint64, [_P, C.c_int, C.c_int]),
+    "qmoe_predictor_routes": (C.c_uint64, [_P]),
+    "qmoe_predictor_frequent": (C.c_int, [_P, C.c_int, _P, _P, _P]),
+    "qmoe_ctx_predictor": (_P, [_P]),
     "qmoe_version": (C.c_char_p, []),
 }
 
@@ -275,6 +284,59 @@ def pack_expert(cfg: Config, w: LayerWeights, expert: int) -> np.ndarray:
     if L.qmoe_pack_expert(C.byref(cfg), C.byref(w), expert, ptr(out)) != 0:
         raise QmoeError(f"qmoe_pack_expert failed for expert {expert}")
     return out
+
+
+class Predictor:
+    """A host-side route predictor (qmoe_predictor_*): ExpertStore's route
+    statistics and prefetch prediction. `cache` is an optional qmoe_cache
+    handle whose hot marks record() sets."""
+
+    def __init__(self, num_layers: int, num_experts: int, depth: int = 2):
+        self.h = lib().qmoe_predictor_new(num_layers, num_experts)
+        if not self.h:
+            raise QmoeError("qmoe_predictor_new failed")
+        self.L, self.E, self.depth = num_layers, num_experts, depth
+
+    def close(self):
+        if self.h:
+            lib().qmoe_predictor_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def record(self, layer: int, routed, cache=None) -> list[int]:
+        r = np.ascontiguousarray(np.asarray(list(routed), np.int32))
+        sel = np.empty(self.E, np.int32)
+        ns = lib().qmoe_predictor_record(self.h, cache, layer, ptr(r), len(r), ptr(sel))
+        if ns < 0:
+            raise ValueError("qmoe_predictor_record refused the routing")
+        return sel[:ns].tolist()
+
+    def predict(self, layer: int, selected) -> list[tuple[int, int]]:
+        """The (layer, expert) prefetch requests, in the order issued."""
+        s = np.ascontiguousarray(np.asarray(list(selected), np.int32))
+        pick, nxt = np.empty(64, np.int64), np.empty(64, np.int64)
+        npick, nnext = C.c_int(), C.c_int()
+        if lib().qmoe_predictor_predict(self.h, layer, ptr(s), len(s), self.depth, ptr(pick),
+                                        C.byref(npick), ptr(nxt), C.byref(nnext)):
+            raise ValueError("qmoe_predictor_predict refused the selection")
+        return [(layer, int(e)) for e in pick[:npick.value]] + \
+               [(layer + 1, int(e)) for e in nxt[:nnext.value]]
+
+    def count(self, layer: int, expert: int) -> int:
+        return lib().qmoe_predictor_count(self.h, layer, expert)
+
+    def routes(self) -> int:
+        return lib().qmoe_predictor_routes(self.h)
+
+    def frequent(self, n: int = 20) -> list[tuple[int, int, int]]:
+        lay, ex, cnt = np.empty(n, np.int32), np.empty(n, np.int32), np.empty(n, np.uint64)
+        got = lib().qmoe_predictor_frequent(self.h, n, ptr(lay), ptr(ex), ptr(cnt))
+        return [(int(lay[i]), int(ex[i]), int(cnt[i])) for i in range(got)]
 
 
 class Checkpoint:
