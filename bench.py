@@ -502,7 +502,7 @@ def measure_stream(rank=0, world=1, local=0, layers=STREAM_LAYERS):
     cs = st.cuda_stream
     torch.cuda.synchronize()
     keys = ("expert_loads", "expert_bytes", "expert_wait_seconds", "prefetch_issued", "prefetch_hits",
-            "routed_lookups", "routed_hits")
+            "routed_lookups", "routed_hits", "prefetch_wasted")
 
     def counters():
         a = ctx.stats()
@@ -532,7 +532,8 @@ def measure_stream(rank=0, world=1, local=0, layers=STREAM_LAYERS):
                 "h2d_bytes": int(d["expert_bytes"]),
                 "h2d_gbs_while_filling": rate if rate > 0 else None,
                 "h2d_gbs_over_leg": d["expert_bytes"] / (ms / 1e3) / 1e9,
-                "prefetch_issued": int(d["prefetch_issued"]), "prefetch_hits": int(d["prefetch_hits"])}
+                "prefetch_issued": int(d["prefetch_issued"]), "prefetch_hits": int(d["prefetch_hits"]),
+                "prefetch_wasted": int(d["prefetch_wasted"])}
 
     hd = torch.empty((1, D), dtype=torch.float32, device="cuda")
     n_dec = 1 if rank == 0 else 0  # one token per step, on rank 0

@@ -104,6 +104,9 @@ typedef struct {
     /* streaming: distinct experts a call's routing selected per layer, and
      * how many of them were already in the pool before its fills */
     uint64_t routed_lookups, routed_hits;
+    /* prefetched experts evicted before any routing reached them
+     * (StreamStats.prefetch_wasted, streaming.py:346-349) */
+    uint64_t prefetch_wasted;
 } qmoe_stats;
 
 typedef struct qmoe_ctx qmoe_ctx;

@@ -478,8 +478,13 @@ static int claim_slot(qmoe_ctx *c, int layer, int e, int pin) {
         int s = (int)ev[i];
         uint64_t owner = c->slot_owner[s];
         if (owner != NO_OWNER) {
-            c->slot_of_host[(owner >> 32) * (uint64_t)c->L.E + (uint32_t)owner] = -1;
+            const size_t m = (size_t)(owner >> 32) * (size_t)c->L.E + (uint32_t)owner;
+            c->slot_of_host[m] = -1;
             c->slot_owner[s] = NO_OWNER;
+            if (c->pf_mark[m]) { /* prefetched, never routed to */
+                c->pf_mark[m] = 0;
+                c->stats.prefetch_wasted++;
+            }
         }
         c->free_slots[c->nfree++] = s;
     }
