@@ -32,6 +32,49 @@ class OracleLayer(C.Structure):
                                           "sdb")]
 
 
+class OracleHC(C.Structure):
+    """oracle_hc: one layer's MoE-side hyper connection."""
+    _fields_ = [("d", C.c_int), ("hc", C.c_int), ("lowrank", C.c_int), ("norm", C.c_void_p),
+                ("down_q", C.c_void_p), ("down_s", C.c_void_p), ("down_b", C.c_void_p),
+                ("down_bf16", C.c_void_p), ("up_q", C.c_void_p), ("up_s", C.c_void_p),
+                ("up_b", C.c_void_p), ("up_bf16", C.c_void_p), ("inject", C.c_void_p)]
+
+
+def _bf16(a: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bits, round to nearest even (c/src/util.h:63-71)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+class SynthHC:
+    """Seeded hyper-connection weights of one layer (test inputs): hc_norm
+    near 1, the two mixer weights q4 (nibbles uniform, scales |N(0, 0.02)|,
+    biases -8 scales; `biases=False` leaves them absent) or dense bf16
+    N(0, 0.02), block_inject bf16 N(0, 0.02)."""
+
+    def __init__(self, d: int, hc: int, lowrank: int, seed: int, q4: bool = True, biases: bool = True):
+        rng = np.random.default_rng(seed)
+        self.d, self.hc, self.lowrank, hd = d, hc, lowrank, hc * d
+        self.norm = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+        self.norm = (_bf16(self.norm).astype(np.uint32) << 16).view(np.float32)   # bf16 on disk
+        self.inject = _bf16(0.02 * rng.standard_normal((hc, hd)))
+        self.parts = {}
+        for name, rows, cols in (("down", lowrank, hd), ("up", hd, lowrank)):
+            if q4:
+                q = rng.integers(0, 2 ** 32, size=(rows, cols // 8), dtype=np.uint32)
+                sc = _bf16(np.abs(0.02 * rng.standard_normal((rows, cols // 64))))
+                bi = _bf16(-8.0 * (sc.astype(np.uint32) << 16).view(np.float32)) if biases else None
+                self.parts[name] = (q, sc, bi, None)
+            else:
+                self.parts[name] = (None, None, None, _bf16(0.02 * rng.standard_normal((rows, cols))))
+
+    def struct(self) -> OracleHC:
+        dq, ds, db, dbf = self.parts["down"]
+        uq, us, ub, ubf = self.parts["up"]
+        return OracleHC(self.d, self.hc, self.lowrank, _p(self.norm), _p(dq), _p(ds), _p(db), _p(dbf),
+                        _p(uq), _p(us), _p(ub), _p(ubf), _p(self.inject))
+
+
 def build(ref: bool = True) -> None:
     """Builds the restatement, and the reference harness when its sources exist."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
@@ -63,6 +106,10 @@ _SIGS = {
     "oracle_router_dot": (C.c_float, [_V, _V, _I]),
     "oracle_dequant_q4": (None, [_V, _V, _V, _I, _I, _I, _V]),
     "ref_moe_forward": (_I, [C.POINTER(OracleLayer), _V, _I, _V, _V, _V]),
+    "oracle_gated_residual": (_I, [C.POINTER(OracleHC), _V, _I, _V, _V]),
+    "oracle_hc_moe_step": (_I, [C.POINTER(OracleHC), C.POINTER(OracleLayer), _V, _I]),
+    "ref_gated_residual": (_I, [C.POINTER(OracleHC), _V, _I, _V, _V]),
+    "ref_hc_moe_step": (_I, [C.POINTER(OracleHC), C.POINTER(OracleLayer), _V, _I]),
     "ref_set_threads": (None, [_I]),
     "ref_reset_cache": (None, []),
     "ref_blas_available": (_I, []),
@@ -107,6 +154,29 @@ class _Impl:
         if self.lib.oracle_route(C.byref(L), _p(x), n, _p(idx), _p(w), _p(lg)) != 0:
             raise RuntimeError("oracle_route failed")
         return idx, w, lg
+
+    def _hc(self, name):
+        prefix = "oracle_" if self.kind == "oracle_moe_forward" else "ref_"
+        return getattr(self.lib, prefix + name)
+
+    def gated_residual(self, H: "SynthHC", h: np.ndarray):
+        """(mixed [n, d], inject [n, hc]) of hyper states h [n, hc*d]."""
+        h = np.ascontiguousarray(h, np.float32)
+        n = h.shape[0]
+        mixed = np.empty((n, H.d), np.float32)
+        inj = np.empty((n, H.hc), np.float32)
+        st = H.struct()
+        if self._hc("gated_residual")(C.byref(st), _p(h), n, _p(mixed), _p(inj)) != 0:
+            raise RuntimeError("gated_residual failed")
+        return mixed, inj
+
+    def hc_moe_step(self, H: "SynthHC", s, h: np.ndarray) -> np.ndarray:
+        """h after one layer's gated_residual -> MoE -> inject-add."""
+        h = np.array(h, np.float32, order="C", copy=True)
+        st, L = H.struct(), layer_struct(s)
+        if self._hc("hc_moe_step")(C.byref(st), C.byref(L), _p(h), h.shape[0]) != 0:
+            raise RuntimeError("hc_moe_step failed")
+        return h
 
     def router_dot(self, x: np.ndarray, w: np.ndarray) -> float:
         x = np.ascontiguousarray(x, np.float32)

@@ -142,7 +142,7 @@ static void gemm_q4_f(int M, int N, int K, const float *A, const uint32_t *W,
                         xq += ag[wd * 8 + i] * (float)((v >> (4 * i)) & 0xF);
                 }
                 float s = bf16f(S[(size_t)n * groups + g]);
-                float b = bf16f(B[(size_t)n * groups + g]);
+                float b = B ? bf16f(B[(size_t)n * groups + g]) : 0.0f; /* absent: zeros */
                 acc += s * xq + b * xsum[g];
             }
             C[(size_t)m * N + n] = acc;
@@ -276,4 +276,105 @@ int oracle_moe_forward(const oracle_layer *L, const float *x, int n,
     free(idx);
     free(wts);
     return 0;
+}
+
+/* ------------------------------------------------ hyper connections */
+
+/* kernel_rmsnorm_grouped, c/src/kernel.c:22-36: groups of `group` values,
+ * weight row (g % groups_per_row) */
+static void rmsnorm_grouped(const float *x, const float *w, size_t n, size_t group, size_t rows,
+                            float eps, float *y) {
+    size_t groups = n / group, per_row = rows ? groups / rows : groups;
+    for (size_t g = 0; g < groups; g++) {
+        const float *xg = x + g * group;
+        float ss = 0;
+        for (size_t i = 0; i < group; i++) ss += xg[i] * xg[i];
+        float r = 1.0f / sqrtf(ss / (float)group + eps);
+        const float *wg = w ? w + (g % per_row) * group : NULL;
+        for (size_t i = 0; i < group; i++) y[g * group + i] = xg[i] * r * (wg ? wg[i] : 1.0f);
+    }
+}
+
+static float sigmoid1(float v) { return 1.0f / (1.0f + expf(-v)); } /* kernel.c:45-47 */
+
+/* linear_forward (model.c:194-202) with group 64, as gated_residual calls it
+ * (model.c:753, :757): q4 through gemm_q4, else bf16 through gemm_bf16 */
+static void hc_linear(const uint32_t *q, const uint16_t *s, const uint16_t *b, const uint16_t *bf,
+                      int M, int N, int K, const float *A, float *C) {
+    if (q) {
+        gemm_q4_f(M, N, K, A, q, s, b, 64, C);
+        return;
+    }
+    for (int m = 0; m < M; m++)
+        for (int nn = 0; nn < N; nn++)
+            C[(size_t)m * N + nn] = oracle_router_dot(A + (size_t)m * K, bf + (size_t)nn * K, K);
+}
+
+int oracle_gated_residual(const oracle_hc *H, const float *h, int n, float *mixed,
+                          float *inject) {
+    const int hc = H->hc, d = H->d, lr = H->lowrank, hd = hc * d;
+    if (n < 0 || hc < 1 || d < 1 || lr < 1 || (!H->down_q && !H->down_bf16) ||
+        (!H->up_q && !H->up_bf16) || (inject && !H->inject))
+        return -1;
+    if (!n) return 0;
+    float *normed = malloc((size_t)n * hd * sizeof(float));
+    float *w = malloc((size_t)n * lr * sizeof(float));
+    float *tmp = malloc((size_t)n * hd * sizeof(float));
+    if (!normed || !w || !tmp) {
+        free(normed);
+        free(w);
+        free(tmp);
+        return -1;
+    }
+    /* normed = rmsnorm over each stream's d values (model.c:733) */
+    rmsnorm_grouped(h, H->norm, (size_t)n * hd, (size_t)d, (size_t)n, 1e-6f, normed);
+    /* w = silu(down(normed) / hc) (model.c:752-755) */
+    hc_linear(H->down_q, H->down_s, H->down_b, H->down_bf16, n, lr, hd, normed, w);
+    for (size_t i = 0; i < (size_t)n * lr; i++) w[i] = silu1(w[i] * (1.0f / hc));
+    /* tmp = sigmoid(up(w)) (model.c:756-758) */
+    hc_linear(H->up_q, H->up_s, H->up_b, H->up_bf16, n, hd, lr, w, tmp);
+    for (size_t i = 0; i < (size_t)n * hd; i++) tmp[i] = sigmoid1(tmp[i]);
+    /* mixed = mean over the streams of tmp * normed (model.c:773-783) */
+    for (int t = 0; t < n; t++)
+        for (int i = 0; i < d; i++) {
+            float acc = 0;
+            for (int c = 0; c < hc; c++)
+                acc += tmp[(size_t)t * hd + (size_t)c * d + i] * normed[(size_t)t * hd + (size_t)c * d + i];
+            mixed[(size_t)t * d + i] = acc / hc;
+        }
+    /* inject = 2 * sigmoid(block_inject(normed) / hc) (model.c:784-791) */
+    if (inject)
+        for (int t = 0; t < n; t++)
+            for (int c = 0; c < hc; c++) {
+                float v = oracle_router_dot(normed + (size_t)t * hd, H->inject + (size_t)c * hd, hd);
+                inject[(size_t)t * hc + c] = sigmoid1(v * (1.0f / hc)) * 2.0f;
+            }
+    free(normed);
+    free(w);
+    free(tmp);
+    return 0;
+}
+
+int oracle_hc_moe_step(const oracle_hc *H, const oracle_layer *L, float *h, int n) {
+    const int hc = H->hc, d = H->d;
+    if (d != L->d) return -1;
+    if (!n) return 0;
+    float *mixed = malloc((size_t)n * d * sizeof(float));
+    float *inj = malloc((size_t)n * hc * sizeof(float));
+    float *y = malloc((size_t)n * d * sizeof(float));
+    int rc = -1;
+    if (mixed && inj && y && !oracle_gated_residual(H, h, n, mixed, inj) &&
+        !oracle_moe_forward(L, mixed, n, y, NULL, NULL, NULL)) {
+        /* the inject-add after the block (model.c:1723-1731) */
+        for (int t = 0; t < n; t++)
+            for (int c = 0; c < hc; c++) {
+                const float a = inj[(size_t)t * hc + c];
+                for (int j = 0; j < d; j++) h[((size_t)t * hc + c) * d + j] += a * y[(size_t)t * d + j];
+            }
+        rc = 0;
+    }
+    free(mixed);
+    free(inj);
+    free(y);
+    return rc;
 }

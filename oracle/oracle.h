@@ -51,6 +51,33 @@ int oracle_route(const oracle_layer *L, const float *x, int n, int32_t *idx,
 /* Canonical router dot product: see moe_oracle.c. */
 float oracle_router_dot(const float *x, const uint16_t *w, int K);
 
+/* The MoE side's hyper connection of one layer (mlp_hyper_connection.*,
+ * c/src/model.c:1945-1964; the checkpoint's hc_count streams of d values).
+ * The two mixer weights are q4 when their words are given (u32 [rows,
+ * cols/8], bf16 scales/biases [rows, cols/64], biases may be NULL = zeros),
+ * else dense bf16 [rows, cols] (mw_load, model.c:215-266). */
+typedef struct {
+    int d, hc, lowrank;
+    const float *norm;           /* fp32 [hc*d]   hc_norm.weight (model.c:1946) */
+    const uint32_t *down_q;      /* input_mix_weight_down [lowrank, hc*d] */
+    const uint16_t *down_s, *down_b, *down_bf16;
+    const uint32_t *up_q;        /* input_mix_weight_up   [hc*d, lowrank] */
+    const uint16_t *up_s, *up_b, *up_bf16;
+    const uint16_t *inject;      /* bf16 [hc, hc*d] block_inject_weight */
+} oracle_hc;
+
+/* gated_residual restated (model.c:728-796): h fp32 [n, hc*d] -> mixed
+ * [n, d] and, when inject is not NULL, inject [n, hc]. */
+int oracle_gated_residual(const oracle_hc *H, const float *h, int n, float *mixed,
+                          float *inject);
+/* One layer's MoE step with its hyper connection (model.c:1708-1731):
+ * gated_residual, moe_forward of the mixed rows, then
+ * h[t, c, :] += inject[t, c] * moe[t, :]. h is updated in place. */
+int oracle_hc_moe_step(const oracle_hc *H, const oracle_layer *L, float *h, int n);
+/* The same two through the reference's own code (ref_harness.c). */
+int ref_gated_residual(const oracle_hc *H, const float *h, int n, float *mixed, float *inject);
+int ref_hc_moe_step(const oracle_hc *H, const oracle_layer *L, float *h, int n);
+
 /* Known-answer helper: kernel_dequant_q4 restated (c/src/kernel.c:152-173). */
 void oracle_dequant_q4(const uint32_t *q, const float *scales,
                        const float *biases, int rows, int cols, int group,

@@ -209,3 +209,65 @@ int ref_moe_forward(const oracle_layer *L, const float *x, int n, float *out,
     free(scratch);
     return rc;
 }
+
+/* ---------------------------------------------- hyper connections */
+
+/* an mweight over caller memory, as mw_load builds it (model.c:215-266):
+ * q4 with fp32 scales/biases (absent biases: zeros), else bf16 */
+static void hc_weight(mweight *w, const uint32_t *q, const uint16_t *s, const uint16_t *b,
+                      const uint16_t *bf, int rows, int cols) {
+    memset(w, 0, sizeof(*w));
+    w->rows = rows;
+    if (q) {
+        w->is_q4 = 1;
+        w->q = q;
+        w->cols = cols / 8;
+        size_t ng = (size_t)rows * (cols / 64);
+        w->scales = widen(s, ng);
+        float *fb = xcalloc(ng, sizeof(float));
+        if (b)
+            for (size_t i = 0; i < ng; i++) fb[i] = bf16_to_f32(b[i]);
+        w->biases = fb;
+    } else {
+        w->cols = cols;
+        w->bf16 = bf;
+    }
+}
+
+int ref_gated_residual(const oracle_hc *H, const float *h, int n, float *mixed, float *inject) {
+    const int hc = H->hc, d = H->d, lr = H->lowrank, hd = hc * d;
+    if (n <= 0) return n < 0 ? -1 : 0;
+    mweight down, up, inj;
+    hc_weight(&down, H->down_q, H->down_s, H->down_b, H->down_bf16, lr, hd);
+    hc_weight(&up, H->up_q, H->up_s, H->up_b, H->up_bf16, hd, lr);
+    hc_weight(&inj, NULL, NULL, NULL, H->inject, hc, hd);
+    float *scratch = xcalloc((size_t)n * (2 * (size_t)hd + lr) + 1024, sizeof(float));
+    gated_residual(h, H->norm, &down, &up, &inj, hc, d, lr, n, mixed, inject, scratch);
+    free(scratch);
+    free(down.scales);
+    free(down.biases);
+    free(up.scales);
+    free(up.biases);
+    return 0;
+}
+
+int ref_hc_moe_step(const oracle_hc *H, const oracle_layer *L, float *h, int n) {
+    const int hc = H->hc, d = H->d;
+    if (n <= 0) return n < 0 ? -1 : 0;
+    float *mixed = xmalloc((size_t)n * d * sizeof(float));
+    float *inj = xmalloc((size_t)n * hc * sizeof(float));
+    float *y = xmalloc((size_t)n * d * sizeof(float));
+    int rc = ref_gated_residual(H, h, n, mixed, inj);
+    if (rc == 0) rc = ref_moe_forward(L, mixed, n, y, NULL, NULL);
+    if (rc == 0)
+        /* model_forward's inject-add after the block (model.c:1723-1731) */
+        for (int t = 0; t < n; t++)
+            for (int hh = 0; hh < hc; hh++) {
+                float a = inj[(size_t)t * hc + hh];
+                for (int j = 0; j < d; j++) h[((size_t)t * hc + hh) * d + j] += a * y[(size_t)t * d + j];
+            }
+    free(mixed);
+    free(inj);
+    free(y);
+    return rc;
+}
