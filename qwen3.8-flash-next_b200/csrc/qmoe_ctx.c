@@ -469,10 +469,11 @@ static int claim_slot(qmoe_ctx *c, int layer, int e, int pin) {
     int slot = c->nfree > 0 ? c->free_slots[c->nfree - 1] : -1;
     /* an expert routed at least four times enters hot (streaming.py:396-397) */
     const int hot = qmoe_predictor_count(c->pred, layer, e) >= 4;
-    if (!qmoe_cache_put(c->cache, key, slot >= 0 ? (uint64_t)slot : NO_OWNER, c->L.slot_bytes,
-                        pin, hot, ev, 64, &nev))
-        return -1;
-    if (slot >= 0) c->nfree--;
+    const int ok = qmoe_cache_put(c->cache, key, slot >= 0 ? (uint64_t)slot : NO_OWNER,
+                                  c->L.slot_bytes, pin, hot, ev, 64, &nev);
+    if (ok && slot >= 0) c->nfree--;
+    /* victims leave the pool even when the put is then rejected (the cache
+     * does not restore them, as cache.c:236-242): their slots are free */
     for (size_t i = 0; i < nev && i < 64; i++) {
         if (ev[i] == NO_OWNER) continue;
         int s = (int)ev[i];
@@ -488,6 +489,7 @@ static int claim_slot(qmoe_ctx *c, int layer, int e, int pin) {
         }
         c->free_slots[c->nfree++] = s;
     }
+    if (!ok) return -1;
     if (slot < 0) {
         if (c->nfree == 0) {
             uint64_t dummy;

@@ -190,3 +190,30 @@ def test_concurrent_bytes_within_budget(L):
     assert not errors
     assert s["bytes"] <= 64 * 100 and s["peak_bytes"] <= 64 * 100
     c.close()
+
+
+def test_rejected_put_reports_the_victims_it_dropped(L):
+    """cache.c:236-242: a put that runs out of unpinned victims is rejected,
+    and the victims it had already dropped stay out (no rollback); it reports
+    them, so the pool can free their slots."""
+    c = Cache(L, 300, LRU)
+    assert c.put(1, 11, 100) and c.put(2, 22, 100, pin=1) and c.put(3, 33, 100, pin=1)
+    assert c.put(4, 44, 200) == 0
+    assert c.last_evicted == [11]
+    assert c.peek(1) is None and c.peek(2) == 22 and c.peek(3) == 33 and c.peek(4) is None
+    s = c.stats()
+    assert s["rejected"] == 1 and s["evictions"] == 0 and s["bytes"] == 200 and s["size"] == 2
+    assert c.put(4, 44, 100) == 1          # the freed room is usable
+    c.close()
+
+
+def test_rejected_replacement_preserves_existing_value(L):
+    """tests/test_cache.py:32-41 of the reference: an oversized replacement is
+    refused before the old entry is touched."""
+    c = Cache(L, 2, LRU)
+    assert c.put(7, 1, 2)
+    assert c.put(7, 2, 3) == 0
+    assert c.get(7) == 1
+    s = c.stats()
+    assert s["rejected"] == 1 and s["evictions"] == 0 and s["bytes"] == 2
+    c.close()
