@@ -51,7 +51,12 @@ typedef struct {
     int num_layers;      /* layers this context serves */
     int max_tokens;      /* largest n of one forward call (sizes workspaces) */
     uint64_t pool_bytes; /* HBM expert pool budget in bytes; 0 = room for every
-                            expert of every layer (all resident) */
+                            expert of every layer (all resident). A streaming
+                            pool must hold at least top_k slots, and one call's
+                            distinct routed experts of a layer must fit in it
+                            at once (the call fails otherwise; the reference
+                            reloads evicted experts one by one instead,
+                            model.c:1341-1349) */
     int policy;          /* QMOE_POLICY_* for the pool (reference: ADAPTIVE) */
     int prefetch_depth;  /* prefetch_count of streaming.py (2) */
     int device;          /* CUDA device ordinal */
