@@ -1348,7 +1348,7 @@ int qmoe_stats_get(qmoe_ctx *c, qmoe_stats *out) {
 /* ------------------------------------------------------ prefetch hooks */
 
 int qmoe_prefetch(qmoe_ctx *c, int layer, const int64_t *ids, size_t n) {
-    if (!c || layer < 0 || layer >= c->cfg.num_layers || c->resident_all) return 0;
+    if (!c || layer < 0 || layer >= c->cfg.num_layers || c->resident_all || (n && !ids)) return 0;
     qmoe_err e;
     int queued = 0;
     /* a fill may evict a slot that queued kernels still read */
