@@ -137,8 +137,32 @@ static size_t put_utf8(char *o, unsigned cp) {
     return 4;
 }
 
+/* length of the UTF-8 sequence at p (at most `left` bytes), 0 if invalid.
+ * Encoded surrogates (ED A0-BF ..) pass, as Python's json.loads decodes a
+ * header with 'surrogatepass'; overlong forms and code points above
+ * U+10FFFF do not. */
+static int utf8_len(const unsigned char *p, ptrdiff_t left) {
+    const unsigned char b = p[0];
+    int n;
+    unsigned char lo = 0x80, hi = 0xBF;
+    if (b >= 0xC2 && b <= 0xDF) n = 2;
+    else if (b >= 0xE0 && b <= 0xEF) {
+        n = 3;
+        if (b == 0xE0) lo = 0xA0;
+    } else if (b >= 0xF0 && b <= 0xF4) {
+        n = 4;
+        if (b == 0xF0) lo = 0x90;
+        if (b == 0xF4) hi = 0x8F;
+    } else
+        return 0;
+    if (left < n || p[1] < lo || p[1] > hi) return 0;
+    for (int i = 2; i < n; i++)
+        if (p[i] < 0x80 || p[i] > 0xBF) return 0;
+    return n;
+}
+
 /* a JSON string at c->p; *out (malloc'd, NUL-terminated, escapes decoded)
- * when out is not NULL */
+ * when out is not NULL. The text must be UTF-8. */
 static int jstr(jcur *c, char **out) {
     if (c->p >= c->end || *c->p != '"') return -1;
     c->p++;
@@ -146,8 +170,17 @@ static int jstr(jcur *c, char **out) {
     if (out && !buf) return -1;
     size_t n = 0;
     while (c->p < c->end && *c->p != '"') {
-        unsigned char ch = (unsigned char)*c->p++;
+        unsigned char ch = (unsigned char)*c->p;
         if (ch < 0x20) goto bad;
+        if (ch >= 0x80) {
+            const int u = utf8_len((const unsigned char *)c->p, c->end - c->p);
+            if (!u) goto bad;
+            if (buf) memcpy(buf + n, c->p, (size_t)u);
+            n += buf ? (size_t)u : 0;
+            c->p += u;
+            continue;
+        }
+        c->p++;
         if (ch != '\\') {
             if (buf) buf[n++] = (char)ch;
             continue;
@@ -342,6 +375,7 @@ typedef struct {
     int is_obj;
     int has_dtype;
     char *dtype;
+    char dtype_repr[32]; /* a non-string dtype as Python prints it ("" = None) */
     int offs_is_arr, offs_n, offs_int;
     int64_t offs[2];
     int shape_is_arr, shape_n, shape_int;
@@ -376,11 +410,26 @@ static int jentry_parse(jcur *c, jentry *e) {
             free(e->dtype);
             e->dtype = NULL;
             e->has_dtype = 0;
+            e->dtype_repr[0] = 0;
             if (c->p < c->end && *c->p == '"') {
                 rc = jstr(c, &e->dtype);
                 e->has_dtype = rc == 0;
             } else {
+                /* how Python prints a non-string dtype in the error message */
+                const char *t0 = c->p;
                 rc = jskip(c);
+                const size_t tl = (size_t)(c->p - t0);
+                if (!rc && tl == 4 && !memcmp(t0, "true", 4)) snprintf(e->dtype_repr, 32, "True");
+                else if (!rc && tl == 5 && !memcmp(t0, "false", 5)) snprintf(e->dtype_repr, 32, "False");
+                else if (!rc && (*t0 == '-' || (*t0 >= '0' && *t0 <= '9'))) {
+                    jcur nc = {t0, c->p, 0};
+                    int kind, ovf;
+                    int64_t v;
+                    if (!jnum(&nc, &kind, &v, &ovf) && kind == J_INT && !ovf)
+                        snprintf(e->dtype_repr, 32, "%lld", (long long)v);
+                    else
+                        snprintf(e->dtype_repr, 32, "%.*s", (int)(tl < 31 ? tl : 31), t0);
+                }
             }
         } else if (!strcmp(key, "data_offsets") || !strcmp(key, "shape")) {
             const int offs = key[0] == 'd';
@@ -498,6 +547,9 @@ static int parse_file(qmoe_ckpt *ck, const char *path, int fi, qmoe_err *err) {
     size_t nr = 0, rcap = 0;
     int failed = 1;
     jcur c = {hdr, hdr + hlen, 0};
+    /* a leading UTF-8 byte-order mark is dropped, as json.loads does for a
+     * header given as bytes */
+    if (hlen >= 3 && !memcmp(hdr, "\xEF\xBB\xBF", 3)) c.p += 3;
     jws(&c);
     if (c.p >= c.end || *c.p != '{') {
         /* valid JSON of another kind, or not JSON at all */
@@ -549,8 +601,8 @@ static int parse_file(qmoe_ckpt *ck, const char *path, int fi, qmoe_err *err) {
                 ck_err(err, "invalid safetensors entry in %s", path);
                 bad = 1;
             } else if (!e.has_dtype || find_dtype(e.dtype) < 0) {
-                ck_err(err, "unsupported safetensors dtype %s for %s", e.has_dtype ? e.dtype : "None",
-                       name);
+                ck_err(err, "unsupported safetensors dtype %s for %s",
+                       e.has_dtype ? e.dtype : e.dtype_repr[0] ? e.dtype_repr : "None", name);
                 bad = 1;
             } else if (!e.offs_is_arr || e.offs_n != 2 || !e.shape_is_arr) {
                 ck_err(err, "invalid safetensors metadata for %s", name);

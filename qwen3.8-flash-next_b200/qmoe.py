@@ -376,11 +376,12 @@ class Checkpoint:
 
     def names(self) -> list[str]:
         L = lib()
-        return [L.qmoe_ckpt_name(self.h, i).decode() for i in range(L.qmoe_ckpt_count(self.h))]
+        return [L.qmoe_ckpt_name(self.h, i).decode("utf-8", "surrogatepass")
+                for i in range(L.qmoe_ckpt_count(self.h))]
 
     def find(self, name: str) -> dict | None:
         t = TensorInfo()
-        if lib().qmoe_ckpt_find(self.h, name.encode(), C.byref(t)) != 0:
+        if lib().qmoe_ckpt_find(self.h, name.encode("utf-8", "surrogatepass"), C.byref(t)) != 0:
             return None
         return {"dtype": ST_DTYPES[t.dtype][0], "shape": tuple(t.shape[:t.ndim]),
                 "nbytes": t.nbytes, "row_bytes": t.row_bytes, "file": t.file, "offset": t.offset}
