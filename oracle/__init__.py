@@ -111,6 +111,14 @@ _SIGS = {
     "ref_gated_residual": (_I, [C.POINTER(OracleHC), _V, _I, _V, _V]),
     "ref_hc_moe_step": (_I, [C.POINTER(OracleHC), C.POINTER(OracleLayer), _V, _I]),
     "ref_set_threads": (None, [_I]),
+    "ref_st_open": (_V, [C.c_char_p, _I, C.c_char_p, _I]),
+    "ref_st_close": (None, [_V]),
+    "ref_st_count": (_I, [_V]),
+    "ref_st_name": (C.c_char_p, [_V, _I]),
+    "ref_st_info": (_I, [_V, C.c_char_p, C.POINTER(_I), C.POINTER(_I), _V, C.POINTER(C.c_uint64),
+                         C.POINTER(C.c_uint64)]),
+    "ref_st_read_rows": (_I, [_V, C.c_char_p, _V, C.c_size_t, _V]),
+    "ref_st_rows_read": (C.c_uint64, [_V]),
     "ref_reset_cache": (None, []),
     "ref_blas_available": (_I, []),
 }
@@ -190,6 +198,46 @@ class _Impl:
         biases = np.ascontiguousarray(biases, np.float32)
         self.lib.oracle_dequant_q4(_p(q), _p(scales), _p(biases), rows, cols, group, _p(out))
         return out
+
+
+class RefIndex:
+    """The reference's own safetensors index (c/src/safetensors.c) over a
+    directory, through the harness; raises ValueError with its message."""
+    DT = ["BOOL", "U8", "I8", "U16", "I16", "U32", "I32", "U64", "I64", "F16", "BF16", "F32", "F64"]
+
+    def __init__(self, lib, path: str, workers: int = 2):
+        self.lib = lib
+        msg = C.create_string_buffer(512)
+        self.h = lib.ref_st_open(os.fsencode(path), workers, msg, 512)
+        if not self.h:
+            raise ValueError(msg.value.decode("utf-8", "surrogateescape"))
+
+    def close(self):
+        if self.h:
+            self.lib.ref_st_close(self.h)
+            self.h = None
+
+    def table(self):
+        out = []
+        for i in range(self.lib.ref_st_count(self.h)):
+            raw = self.lib.ref_st_name(self.h, i)
+            dt, nd = C.c_int(), C.c_int()
+            shape = (C.c_int64 * 8)()
+            off, nb = C.c_uint64(), C.c_uint64()
+            self.lib.ref_st_info(self.h, raw, C.byref(dt), C.byref(nd), shape, C.byref(off), C.byref(nb))
+            out.append([raw.decode("utf-8", "surrogatepass"), self.DT[dt.value], list(shape[:nd.value]),
+                        off.value, nb.value])
+        return sorted(out)
+
+    def read_rows(self, name: str, rows, row_bytes: int) -> np.ndarray:
+        r = np.ascontiguousarray(np.asarray(list(rows), np.int64))
+        out = np.empty(len(r) * row_bytes + 1, np.uint8)
+        if self.lib.ref_st_read_rows(self.h, name.encode(), _p(r), len(r), _p(out)) != 0:
+            raise ValueError(f"row read refused for {name}")
+        return out[:len(r) * row_bytes]
+
+    def rows_read(self) -> int:
+        return self.lib.ref_st_rows_read(self.h)
 
 
 _cache = {}

@@ -18,6 +18,7 @@
 #ifndef QMOE_ORACLE_H
 #define QMOE_ORACLE_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 typedef struct {
@@ -77,6 +78,17 @@ int oracle_hc_moe_step(const oracle_hc *H, const oracle_layer *L, float *h, int 
 /* The same two through the reference's own code (ref_harness.c). */
 int ref_gated_residual(const oracle_hc *H, const float *h, int n, float *mixed, float *inject);
 int ref_hc_moe_step(const oracle_hc *H, const oracle_layer *L, float *h, int n);
+
+/* The reference's safetensors index and row reader (ref_harness.c, oracle/_ref
+ * only): st_index_open / st_find / st_read_rows behind opaque handles. */
+void *ref_st_open(const char *dir, int workers, char *msg, int msgcap);
+void ref_st_close(void *h);
+int ref_st_count(void *h);
+const char *ref_st_name(void *h, int i);
+int ref_st_info(void *h, const char *name, int *dtype, int *ndim, int64_t *shape,
+                uint64_t *offset, uint64_t *nbytes);
+int ref_st_read_rows(void *h, const char *name, const int64_t *rows, size_t n, void *out);
+uint64_t ref_st_rows_read(void *h);
 
 /* Known-answer helper: kernel_dequant_q4 restated (c/src/kernel.c:152-173). */
 void oracle_dequant_q4(const uint32_t *q, const float *scales,

@@ -271,3 +271,52 @@ int ref_hc_moe_step(const oracle_hc *H, const oracle_layer *L, float *h, int n) 
     free(y);
     return rc;
 }
+
+/* ------------------------------------ the reference's safetensors index */
+
+/* st_index_open / st_find / st_read_rows (c/src/safetensors.c), compiled
+ * unmodified, for differential tests of the library's checkpoint reader */
+void *ref_st_open(const char *dir, int workers, char *msg, int msgcap) {
+    st_index *ix = xcalloc(1, sizeof(st_index));
+    err_t err = {{0}};
+    if (st_index_open(ix, dir, workers, &err) != 0) {
+        if (msg && msgcap > 0) snprintf(msg, (size_t)msgcap, "%s", err.msg);
+        free(ix);
+        return NULL;
+    }
+    return ix;
+}
+
+void ref_st_close(void *h) {
+    if (!h) return;
+    st_index_close((st_index *)h);
+    free(h);
+}
+
+int ref_st_count(void *h) { return h ? (int)((st_index *)h)->ntensors : 0; }
+
+const char *ref_st_name(void *h, int i) {
+    st_index *ix = h;
+    return ix && i >= 0 && (size_t)i < ix->ntensors ? ix->tensors[i].name : NULL;
+}
+
+int ref_st_info(void *h, const char *name, int *dtype, int *ndim, int64_t *shape,
+                uint64_t *offset, uint64_t *nbytes) {
+    st_tensor *t = h ? st_find((st_index *)h, name) : NULL;
+    if (!t) return -1;
+    *dtype = (int)t->dtype;
+    *ndim = (int)t->ndim;
+    for (size_t i = 0; i < t->ndim && i < 8; i++) shape[i] = t->shape[i];
+    *offset = t->offset;
+    *nbytes = t->nbytes;
+    return 0;
+}
+
+int ref_st_read_rows(void *h, const char *name, const int64_t *rows, size_t n, void *out) {
+    st_tensor *t = h ? st_find((st_index *)h, name) : NULL;
+    err_t err = {{0}};
+    if (!t) return -1;
+    return st_read_rows((st_index *)h, t, rows, n, out, &err);
+}
+
+uint64_t ref_st_rows_read(void *h) { return h ? ((st_index *)h)->rows_read : 0; }
