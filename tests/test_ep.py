@@ -124,7 +124,9 @@ def test_two_rank_dispatch_over_gloo(built):
     those experts."""
     import torch.multiprocessing as mp
     world = 2
-    with mp.Manager() as m:
+    # the manager's server process is spawned, not forked from this
+    # (multi-threaded) test process
+    with mp.get_context("spawn").Manager() as m:
         result = m.dict()
         mp.spawn(_gloo_rank, args=(world, _free_port(), result), nprocs=world, join=True)
         assert dict(result) == {0: True, 1: True}
