@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""MoE-layer throughput on B200 (BASELINE metric: MoE-layer tokens/s).
+"""MoE-layer throughput on B200 (the headline metric: MoE-layer tokens/s).
 
 Workload: one full-size MoE layer (hidden 2048, 512 routed
 experts, top-10, one shared expert, intermediate 512, affine q4 with group
