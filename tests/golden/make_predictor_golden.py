@@ -65,13 +65,16 @@ def main():
     cases = []
     for ci, (L, E, k, depth, steps, skew, max_tok) in enumerate(
             [(3, 8, 2, 2, 24, 0.0, 3), (4, 16, 4, 2, 40, 1.1, 4), (2, 32, 4, 3, 30, 0.6, 8),
-             (5, 64, 8, 2, 50, 1.1, 2), (3, 12, 3, 0, 10, 0.5, 2), (1, 16, 2, 4, 12, 1.0, 3)]):
+             (5, 64, 8, 2, 50, 1.1, 2), (3, 12, 3, 0, 10, 0.5, 2), (1, 16, 2, 4, 12, 1.0, 3),
+             # the workload's shape: 512 experts, top-10, Zipf(1.1); max_tok -1 = one token a step
+             (4, 512, 10, 2, 160, 1.1, -1), (2, 512, 10, 2, 12, 1.1, 48)]):
         rng = np.random.default_rng(20261206 + ci)
         store, calls = make_store(streaming, L, E, depth)
         rec = []
         for s in range(steps):
             layer = s % L
-            routed = routed_step(rng, E, k, int(rng.integers(0, max_tok + 1)), skew)
+            ntok = 1 if max_tok < 0 else int(rng.integers(0, max_tok + 1))
+            routed = routed_step(rng, E, k, ntok, skew)
             selected = sorted(set(routed))
             store.record_route(layer, routed)
             del calls[:]

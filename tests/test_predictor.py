@@ -34,7 +34,7 @@ def _run(make, case):
     return p, reqs
 
 
-@pytest.mark.parametrize("ci", range(6))
+@pytest.mark.parametrize("ci", range(8))
 def test_restatement_matches_reference_vectors(ci):
     from oracle.predictor import RoutePredictor
     case = _cases()[ci]
@@ -44,7 +44,7 @@ def test_restatement_matches_reference_vectors(ci):
     assert [list(f) for f in p.frequent(20)] == case["frequent"]
 
 
-@pytest.mark.parametrize("ci", range(6))
+@pytest.mark.parametrize("ci", range(8))
 def test_library_predictor_matches_reference_vectors(built, ci):
     import qmoe
     case = _cases()[ci]
