@@ -1,5 +1,5 @@
 """include/qmoe.h from C: tests/c/host_abi.c compiled as C11 and as C++17
-(warnings as errors), linked against libqmoe.so and run; it exercises the
+(pedantic, warnings as errors), linked against libqmoe.so and run; it exercises the
 host-only objects (expert cache, route predictor, checkpoint index) through the
 C ABI without a GPU."""
 import os
@@ -16,7 +16,7 @@ def test_host_abi_from_c(built, tmp_path, lang):
     exe = tmp_path / f"host_abi_{lang}"
     cc = ["gcc", "-std=c11"] if lang == "c" else ["g++", "-std=c++17", "-x", "c++"]
     src = os.path.join(ROOT, "tests", "c", "host_abi.c")
-    cmd = cc + ["-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"), src]
+    cmd = cc + ["-Wall", "-Wextra", "-Wpedantic", "-Werror", "-I", os.path.join(ROOT, "include"), src]
     if lang == "c++":
         cmd += ["-x", "none"]
     cmd += ["-L", PKG, "-lqmoe", f"-Wl,-rpath,{PKG}", "-o", str(exe)]
