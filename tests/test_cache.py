@@ -217,3 +217,29 @@ def test_rejected_replacement_preserves_existing_value(L):
     s = c.stats()
     assert s["rejected"] == 1 and s["evictions"] == 0 and s["bytes"] == 2
     c.close()
+
+
+def test_eviction_and_pinning_of_the_python_runtime(L):
+    """tests/test_cache.py:6-16 of the reference (ExpertCache(max_items=2));
+    the item limit is a byte budget here, one byte per item."""
+    c = Cache(L, 2, LRU)
+    assert c.put(1, 1, 1) and c.put(2, 2, 1, pin=1) and c.put(3, 3, 1)
+    assert c.get(1) is None and c.get(2) == 2 and c.get(3) == 3
+    s = c.stats()
+    assert s["evictions"] >= 1 and s["pinned"] == 1
+    c.close()
+
+
+def test_partition_over_its_share_of_the_python_runtime(L):
+    """tests/test_cache.py:19-29 of the reference: with two layer partitions,
+    the layer over its fair share gives up its oldest entry."""
+    c = Cache(L, 4, ADAPTIVE, parts=2)
+    k = lambda layer, e: (layer << 32) | e
+    for key in (k(0, 0), k(0, 1), k(0, 2), k(1, 0), k(1, 1)):
+        assert c.put(key, key + 1, 1)
+    assert c.peek(k(0, 0)) is None
+    assert c.peek(k(1, 0)) == k(1, 0) + 1 and c.peek(k(1, 1)) == k(1, 1) + 1
+    # partition bytes {0: 2, 1: 2}
+    assert c.peek(k(0, 1)) is not None and c.peek(k(0, 2)) is not None
+    assert c.stats()["bytes"] == 4
+    c.close()
