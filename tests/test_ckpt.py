@@ -1,4 +1,5 @@
-"""The safetensors checkpoint reader (qmoe_ckpt_*), on the CPU.
+"""The safetensors checkpoint reader (qmoe_ckpt_*), on the CPU, and one GPU
+test of a context uploaded from checkpoint files.
 
 Index validation follows c/tests/test_safetensors.c:63-166 and the storage
 cases of tests/test_streaming.py:43-127 (the reference's own tests); row reads
@@ -309,3 +310,25 @@ def test_layer_reader_checks_names_types_and_shapes(built, tmp_path):
             ck.pack_experts(cfg, 0, [16])
         with pytest.raises(qmoe.QmoeError, match="missing expert tensor"):
             ck.pack_experts(cfg, 3, [0])
+
+
+@pytest.mark.gpu
+@pytest.mark.xfail(reason="first run of the checkpoint upload on a GPU; the marker goes once it has passed",
+                   strict=False)
+def test_upload_from_checkpoint_equals_upload_from_memory(tiny_ckpt):
+    """qmoe_upload_layer_ckpt (a layer read from the files, then uploaded)
+    gives the same outputs, bit for bit, as qmoe_upload_layer of the arrays
+    the files were written from; two layers, one per file."""
+    import qmoe
+    cfg, layers, path = tiny_ckpt
+    a, b = qmoe.Context(cfg), qmoe.Context(cfg)
+    with qmoe.Checkpoint(str(path), 2) as ck:
+        for l, s in enumerate(layers):
+            a.upload(l, s)
+            b.upload_ckpt(l, ck, l)
+    x = qmoe.synth_tokens(20261204, 3, 32, D)
+    for l in range(2):
+        for n in (1, 32):
+            assert np.array_equal(a.forward(l, x[:n]), b.forward(l, x[:n])), (l, n)
+    a.close()
+    b.close()
