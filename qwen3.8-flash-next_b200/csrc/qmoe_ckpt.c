@@ -276,8 +276,12 @@ static int jnum(jcur *c, int *kind, int64_t *v, int *ovf) {
 
 static int jskip(jcur *c);
 
+/* nesting deeper than this is refused (json.loads accepts several hundred
+ * levels; the bound keeps the recursion's stack use small) */
+#define QK_JSON_DEPTH 512
+
 static int jskip_container(jcur *c, char open, char close) {
-    if (++c->depth > 64) return -1;
+    if (++c->depth > QK_JSON_DEPTH) return -1;
     c->p++; /* open */
     jws(c);
     if (c->p < c->end && *c->p == close) {

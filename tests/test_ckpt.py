@@ -129,6 +129,22 @@ def test_metadata_escapes_and_zero_length_tensors(built, tmp_path):
         assert ck.find("empty")["shape"] == (0, 3) and ck.find("empty")["row_bytes"] == 0
 
 
+def test_deeply_nested_metadata(built, tmp_path):
+    """json.loads takes a few hundred levels of nesting in __metadata__, and so
+    does the index; far deeper nesting is refused, not a crash."""
+    import qmoe
+    t = '"t":{"dtype":"F32","shape":[4],"data_offsets":[0,16]}'
+    for depth, ok in ((300, True), (100000, False)):
+        write_st(tmp_path / "m.safetensors", {"t": ("F32", np.zeros(4, np.float32))},
+                 header='{"__metadata__":' + "[" * depth + "]" * depth + "," + t + "}")
+        if ok:
+            with _open(tmp_path) as ck:
+                assert ck.names() == ["t"]
+        else:
+            with pytest.raises(qmoe.QmoeError, match="invalid safetensors JSON"):
+                _open(tmp_path)
+
+
 def test_row_reads_restore_order_and_deduplicate(built, tmp_path):
     """tests/test_streaming.py:113-126 and :85-93: rows [3, 1, 3, 2] come
     back in request order from one pread of rows 1..3."""
