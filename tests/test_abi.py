@@ -98,3 +98,31 @@ def test_zipf_bias(built):
     b = s.logit_bias
     ranks = np.rint(np.exp(-b.astype(np.float64) / 1.1)).astype(int)
     assert sorted(ranks.tolist()) == list(range(1, 513))
+
+
+def _arity():
+    """{name: number of parameters} of every function declared in qmoe.h."""
+    txt = open(os.path.join(ROOT, "include", "qmoe.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    txt = re.sub(r"#[^\n]*", "", txt)
+    out = {}
+    for m in re.finditer(r"\b(qmoe_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", txt, flags=re.S):
+        params, depth, n = m.group(2).strip(), 0, 1
+        if params in ("", "void"):
+            out[m.group(1)] = 0
+            continue
+        for ch in params:
+            depth += ch in "([" and 1 or ch in ")]" and -1 or 0
+            n += ch == "," and depth == 0
+        out[m.group(1)] = n
+    return out
+
+
+def test_binding_arity_matches_the_header(built):
+    """Every ctypes signature in qmoe.py takes as many arguments as the C
+    declaration it binds."""
+    import qmoe
+    ar = _arity()
+    assert set(ar) == set(qmoe.SIGNATURES), set(ar) ^ set(qmoe.SIGNATURES)
+    bad = {n: (len(qmoe.SIGNATURES[n][1]), k) for n, k in ar.items() if len(qmoe.SIGNATURES[n][1]) != k}
+    assert not bad, bad
