@@ -122,3 +122,35 @@ def test_out_of_range_experts_change_nothing(built):
     p.record(0, [])
     p.record(0, [5])
     assert p.predict(0, [5]) == [(0, 1), (0, 2)]   # falls back to the layer's counts
+
+
+hypothesis = pytest.importorskip("hypothesis")
+from hypothesis import HealthCheck, given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+
+@st.composite
+def step_sequences(draw):
+    L = draw(st.integers(1, 4))
+    E = draw(st.integers(1, 6))
+    depth = draw(st.integers(0, 4))
+    steps = draw(st.lists(st.tuples(st.integers(0, L - 1),
+                                    st.lists(st.integers(0, E - 1), max_size=12)), max_size=30))
+    return L, E, depth, steps
+
+
+@settings(max_examples=300, deadline=None, suppress_health_check=list(HealthCheck))
+@given(seq=step_sequences())
+def test_library_predictor_matches_restatement_on_random_steps(built, seq):
+    """Few experts, so nearly every ranking has ties; layers in any order;
+    empty steps included."""
+    import qmoe
+    from oracle.predictor import RoutePredictor
+    L, E, depth, steps = seq
+    a, b = RoutePredictor(L, E, depth), qmoe.Predictor(L, E, depth)
+    for layer, routed in steps:
+        sel = a.record_route(layer, routed)
+        assert b.record(layer, routed) == list(sel)
+        assert b.predict(layer, sel) == a.prefetch_predictions(layer, sel)
+    assert b.frequent(20) == a.frequent(20) and b.routes() == a.routes
+    b.close()
