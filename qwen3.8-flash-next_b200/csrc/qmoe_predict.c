@@ -91,11 +91,15 @@ static void touch(qmoe_predictor *p, int layer) {
     if (p->layer_seq[layer] < 0) p->layer_seq[layer] = p->next_seq++;
 }
 
+/* A layer's transition tables, allocated on first use and written through at
+ * once: a sequential fill maps every page now, where the lazily mapped zero
+ * pages of calloc would fault one row at a time on the streaming path (tens of
+ * microseconds a decode step until every row was touched). */
 static trans_layer *trans_of(qmoe_predictor *p, int layer) {
     trans_layer *t = &p->trans[layer];
     if (!t->count) {
         const size_t EE = (size_t)p->E * (size_t)p->E;
-        t->count = calloc(EE, sizeof(uint32_t));
+        t->count = malloc(EE * sizeof(uint32_t));
         t->order = malloc(EE * sizeof(uint16_t));
         t->n = calloc((size_t)p->E, sizeof(uint16_t));
         if (!t->count || !t->order || !t->n) {
@@ -105,6 +109,8 @@ static trans_layer *trans_of(qmoe_predictor *p, int layer) {
             memset(t, 0, sizeof(*t));
             return NULL;
         }
+        memset(t->count, 0, EE * sizeof(uint32_t));
+        memset(t->order, 0, EE * sizeof(uint16_t));
     }
     return t;
 }
@@ -136,11 +142,15 @@ int qmoe_predictor_record(qmoe_predictor *p, qmoe_cache *cache, int layer, const
         free(sel);
         return -1;
     }
-    for (int a = 0; a < np; a++) {
-        const size_t row = (size_t)prev[a] * E;
+    for (int a = 0; t && a < np; a++) { /* t is NULL when either set is empty */
+        uint32_t *crow = t->count + (size_t)prev[a] * E;
+        uint16_t *orow = t->order + (size_t)prev[a] * E;
+        unsigned keys = t->n[prev[a]];
         for (int s = 0; s < ns; s++) {
-            if (!t->count[row + sel[s]]++) t->order[row + t->n[prev[a]]++] = (uint16_t)sel[s];
+            const int e = sel[s];
+            if (!crow[e]++) orow[keys++] = (uint16_t)e;
         }
+        t->n[prev[a]] = (uint16_t)keys;
     }
     touch(p, layer);
     uint64_t *f = p->freq + (size_t)layer * E;
@@ -199,11 +209,13 @@ int qmoe_predictor_predict(qmoe_predictor *p, int layer, const int32_t *selected
     const trans_layer *t = &p->trans[layer];
     if (t->count)
         for (size_t i = 0; i < n; i++) { /* :423-424 */
-            const size_t row = (size_t)selected[i] * E;
-            for (int j = 0; j < t->n[selected[i]]; j++) {
-                const uint16_t e = t->order[row + j];
+            const uint32_t *crow = t->count + (size_t)selected[i] * E;
+            const uint16_t *orow = t->order + (size_t)selected[i] * E;
+            const int keys = t->n[selected[i]];
+            for (int j = 0; j < keys; j++) {
+                const uint16_t e = orow[j];
                 if (!cand[e]) order[nc++] = e;
-                cand[e] += t->count[row + e];
+                cand[e] += crow[e];
             }
         }
     if (!nc) { /* :425-426 */
