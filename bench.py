@@ -138,21 +138,42 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def cpu_reference_rate(x, budget_s=12.0, max_tokens=1000, threads=None):
-    """Times the reference's moe_forward (oracle/_ref) per token on the host
-    cores, experts already dequantised in its cache (steady state). Falls back
-    to the C restatement when the reference build is absent."""
-    import qmoe
+def bench_config(world=1):
+    """The `config` block of the headline line, shared by both arms."""
+    return {"workload": "config1: one MoE layer, decode batch 1, 1000 tokens/step",
+            "hidden": D, "experts": E, "top_k": K_TOP, "shared_experts": 1,
+            "moe_inter": I_DIM, "quant": "affine q4 g64 (bf16 scale/bias)",
+            "tokens_per_step": TOKENS, "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2: 906 MB of experts per layer vs 126 MB L2; "
+                  "router and shared expert (3.9 MB) stay L2-resident across tokens",
+            "activations": "decode: x as 16-bit and h as 24-bit block fixed point (one power-of-two "
+                           "scale per 32 values) in integer dot products with the q4 weights; "
+                           "prefill: fp16 tensor-core operands (h as an fp16 hi/lo pair), fp32 "
+                           "accumulation; router fp64 in a fixed order; outputs fp32"}
+
+
+def _cpu_impl():
+    """The timed CPU path: the reference's own moe_forward (oracle/_ref) with
+    every host thread for its BLAS calls, or the C restatement (one thread)
+    when the reference build is absent. Inputs come from the checkers' own
+    generator (oracle.SynthLayer / oracle.synth_tokens): nothing of the
+    product library is loaded on this path."""
     import oracle
-    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=1)
-    s = qmoe.SynthLayer(cfg, SEED)
-    ref = oracle.reference()
-    kind = "reference"
+    ref, kind = oracle.reference(), "reference"
     if ref is None:
         ref, kind = oracle.restatement(), "port"
-    threads = threads or os.cpu_count()
+    threads = os.cpu_count() or 1
     if kind == "reference":
         ref.lib.ref_set_threads(threads)
+    return oracle, ref, kind, (threads if kind == "reference" else 1)
+
+
+def cpu_reference_rate(budget_s=12.0, max_tokens=1000):
+    """configs[1] on the host cores: the reference's moe_forward per token,
+    experts already dequantised in its cache (steady state)."""
+    oracle, ref, kind, cores = _cpu_impl()
+    s = oracle.SynthLayer(D, E, K_TOP, I_DIM, G, SEED)
+    x = oracle.synth_tokens(SEED, 0, max_tokens, D)
     # size the sample from one warm token
     ref.forward(s, x[:1])
     t0 = time.perf_counter()
@@ -168,28 +189,80 @@ def cpu_reference_rate(x, budget_s=12.0, max_tokens=1000, threads=None):
     dt = time.perf_counter() - t0
     if kind == "reference":
         ref.lib.ref_reset_cache()
-    return {"value": n / dt, "unit": UNIT, "cores": threads if kind == "reference" else 1,
-            "kind": kind,
+    return {"value": n / dt, "unit": UNIT, "cores": cores, "kind": kind,
             "sample": f"{n} config-1 decode tokens, one moe_forward call each, experts "
                       f"pre-dequantised in the reference cache; {dt:.1f} s"}
 
 
+def cpu_prefill_rate():
+    """configs[2] on the host cores: the whole 4096-token call, one
+    moe_forward(n = 4096) on the Zipf(1.1)-biased layer the GPU leg runs,
+    after a first call that dequantised the touched experts into the
+    reference's cache (steady state)."""
+    oracle, ref, kind, cores = _cpu_impl()
+    s = oracle.SynthLayer(D, E, K_TOP, I_DIM, G, SEED, 1, zipf_s=1.1)
+    x = oracle.synth_tokens(SEED, 3, PREFILL_T, D)
+    t0 = time.perf_counter()
+    ref.forward(s, x)
+    fill = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    ref.forward(s, x)
+    dt = time.perf_counter() - t0
+    if kind == "reference":
+        ref.lib.ref_reset_cache()
+    return {"value": PREFILL_T / dt, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "ms_per_call": 1e3 * dt,
+            "sample": f"the full config-2 call: one moe_forward of {PREFILL_T} tokens, experts "
+                      f"pre-dequantised (the first call, {fill:.1f} s, filled the cache); {dt:.1f} s"}
+
+
+def cpu_stack_rate(seed, stream, n_tokens, zipf, sample_layers, per_call, label):
+    """configs[3]/[4] on the host cores: the stack h <- h + MoE_l(RMSNorm(h))
+    over its first `sample_layers` layers (the reference's kernel_rmsnorm,
+    c/src/kernel.c:10-20, and moe_forward), each layer timed after a warm
+    pass that dequantised its touched experts into the reference's cache;
+    the step time is the mean layer time x 76 (extrapolated). per_call
+    tokens go through moe_forward at once (1: batch-1 decode, one token per
+    call)."""
+    oracle, ref, kind, cores = _cpu_impl()
+    h = oracle.synth_tokens(seed, stream, n_tokens, D)
+    times = []
+    for l in range(sample_layers):
+        s = oracle.SynthLayer(D, E, K_TOP, I_DIM, G, seed, l, zipf_s=zipf)
+
+        def layer(h):
+            out = np.empty_like(h)
+            for a in range(0, n_tokens, per_call):
+                y, _, _ = ref.forward(s, oracle.rmsnorm(h[a:a + per_call], 1e-6))
+                out[a:a + per_call] = h[a:a + per_call] + y
+            return out
+
+        layer(h)  # warm: the touched experts into the cache
+        t0 = time.perf_counter()
+        h = layer(h)
+        times.append(time.perf_counter() - t0)
+        if kind == "reference":
+            ref.lib.ref_reset_cache()
+    step = statistics.mean(times) * STACK_L
+    return {"value": n_tokens / step, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "ms_per_step": 1e3 * step, "extrapolated": True,
+            "sample": f"{label}: layers 0-{sample_layers - 1} of the 76 timed ({n_tokens} tokens, "
+                      f"{per_call} per moe_forward call, RMSNorm + moe_forward + residual, experts "
+                      f"pre-dequantised), mean layer time x 76; {sum(times):.1f} s timed"}
+
+
 def run_reference(args):
+    """--impl reference: the reference's own CPU moe_forward on the host
+    cores, on the GPU arm's metric and config, one bounded sample per step
+    (8 decode tokens, one call each; the per-token rate is the metric).
+    Rank 0 only; inputs from the checkers' generator, so the product library
+    is never loaded here."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import qmoe
-    x = qmoe.synth_tokens(SEED, 0, 64, D)
-    import oracle
-    ref = oracle.reference()
-    kind = "reference"
-    if ref is None:
-        ref, kind = oracle.restatement(), "port"
-    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=1)
-    s = qmoe.SynthLayer(cfg, SEED)
-    threads = os.cpu_count()
-    if kind == "reference":
-        ref.lib.ref_set_threads(threads)
+    oracle, ref, kind, cores = _cpu_impl()
+    x = oracle.synth_tokens(SEED, 0, 64, D)
+    s = oracle.SynthLayer(D, E, K_TOP, I_DIM, G, SEED)
     per_step = 8
     sample = x[:per_step]
     for _ in range(max(args.warmup, 1)):
@@ -206,13 +279,12 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "config1: MoE layer decode, batch 1 (bounded CPU sample)",
-                   "hidden": D, "experts": E, "top_k": K_TOP, "moe_inter": I_DIM, "group": G,
-                   "tokens_per_step": per_step},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads if kind == "reference" else 1,
-                         "kind": kind,
-                         "sample": f"{per_step} tokens per step, one moe_forward call each, "
-                                   "experts pre-dequantised (steady state)"},
+        "config": bench_config(args.gpus),
+        "sample_tokens_per_step": per_step,
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": f"{per_step} of the step's {TOKENS} config-1 tokens per timed "
+                                   "step (a bounded sample: tokens/s is a per-token rate), one "
+                                   "moe_forward call each, experts pre-dequantised (steady state)"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -830,10 +902,29 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
-            cpu = cpu_reference_rate(x_host)
+            cpu = cpu_reference_rate()
         except Exception as e:  # reported, never silently replaced
             cpu = {"value": None, "unit": UNIT, "cores": 0, "kind": "unavailable",
                    "sample": f"failed: {e}"}
+        legs = []
+        if prefill is not None:
+            legs.append((prefill, cpu_prefill_rate))
+        if stack is not None:
+            legs.append((stack, lambda: cpu_stack_rate(STACK_SEED, 100, STACK_T, None, 3, STACK_T,
+                                                       "config 3, decode batch 64")))
+        if stream is not None:
+            legs.append((stream["decode_batch1"],
+                         lambda: cpu_stack_rate(STACK_SEED + 1, 200, 4, 1.1, 2, 1,
+                                                "config 4 batch-1 decode, 4 tokens one at a time")))
+            legs.append((stream["prefill"],
+                         lambda: cpu_stack_rate(STACK_SEED + 1, 200, STREAM_PREFILL, 1.1, 2,
+                                                STREAM_PREFILL, "config 4 prefill, 512 tokens")))
+        for where, fn in legs:
+            try:
+                where["cpu_baseline"] = fn()
+            except Exception as e:  # reported, never silently replaced
+                where["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": 0,
+                                         "kind": "unavailable", "sample": f"failed: {e}"}
 
     if rank == 0:
         line = {
@@ -841,12 +932,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config1: one MoE layer, decode batch 1, 1000 tokens/step",
-                       "hidden": D, "experts": E, "top_k": K_TOP, "shared_experts": 1,
-                       "moe_inter": I_DIM, "quant": "affine q4 g64 (bf16 scale/bias)",
-                       "tokens_per_step": TOKENS, "parallelism": f"replicas x{world}",
-                       "l2": "inputs larger than L2: 906 MB of experts per layer vs 126 MB L2; "
-                             "router and shared expert (3.9 MB) stay L2-resident across tokens"},
+            "config": bench_config(world),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": TOKENS * D * 4,
                     "d2h_bytes_per_step": TOKENS * (D * 4 + 8),
                     "caller": "C loop over qmoe_forward (host buffers), one call per token",

@@ -104,4 +104,14 @@ void ref_set_threads(int threads);
 /* Drops the harness's dequantised expert cache (fp32, 12*d*I bytes each). */
 void ref_reset_cache(void);
 
+/* The seeded synthetic workload (synth_oracle.c): writes the tensors L points
+ * at (the pointers are written through although declared const), for experts
+ * [e0, e1) of the routed tensors (e1 <= e0: all), the router, shared gate and
+ * shared expert. Buffers hold all E experts. Returns 0, or -1 on a bad shape. */
+int oracle_synth_layer(oracle_layer *L, uint64_t seed, int layer, int e0, int e1);
+void oracle_synth_tokens(uint64_t seed, uint64_t stream, int n, int d, float *x);
+int oracle_synth_zipf_bias(uint64_t seed, int layer, int E, double s, float *bias);
+/* Unit-weight RMSNorm of n rows of d (sum of squares in fp64). */
+void oracle_rmsnorm_rows(const float *x, int n, int d, float eps, float *y);
+
 #endif
