@@ -168,9 +168,20 @@ def _cpu_impl():
     return oracle, ref, kind, (threads if kind == "reference" else 1)
 
 
-def cpu_reference_rate(budget_s=12.0, max_tokens=1000):
+def _margin(out, ref, what):
+    out = np.asarray(out, np.float64)
+    ref = np.asarray(ref, np.float64)
+    mab = float(np.abs(out - ref).max())
+    rr = float(np.linalg.norm(out - ref) / np.linalg.norm(ref))
+    return {"max_abs": mab, "rel_rms": rr, "bars": [2e-2, 1e-3], "ok": mab <= 2e-2 and rr <= 1e-3,
+            "against": what}
+
+
+def cpu_reference_rate(budget_s=12.0, max_tokens=1000, gpu_out=None):
     """configs[1] on the host cores: the reference's moe_forward per token,
-    experts already dequantised in its cache (steady state)."""
+    experts already dequantised in its cache (steady state). With gpu_out
+    (the GPU arm's outputs for the same tokens), also the parity margin of
+    the sampled tokens against the reference's outputs."""
     oracle, ref, kind, cores = _cpu_impl()
     s = oracle.SynthLayer(D, E, K_TOP, I_DIM, G, SEED)
     x = oracle.synth_tokens(SEED, 0, max_tokens, D)
@@ -183,22 +194,27 @@ def cpu_reference_rate(budget_s=12.0, max_tokens=1000):
     sample = x[:n]
     for t in range(n):  # warm: fills the reference's expert cache for the sample
         ref.forward(s, sample[t:t + 1])
+    outs = np.empty((n, D), np.float32)
     t0 = time.perf_counter()
     for t in range(n):
-        ref.forward(s, sample[t:t + 1])
+        outs[t] = ref.forward(s, sample[t:t + 1])[0][0]
     dt = time.perf_counter() - t0
     if kind == "reference":
         ref.lib.ref_reset_cache()
-    return {"value": n / dt, "unit": UNIT, "cores": cores, "kind": kind,
-            "sample": f"{n} config-1 decode tokens, one moe_forward call each, experts "
-                      f"pre-dequantised in the reference cache; {dt:.1f} s"}
+    r = {"value": n / dt, "unit": UNIT, "cores": cores, "kind": kind,
+         "sample": f"{n} config-1 decode tokens, one moe_forward call each, experts "
+                   f"pre-dequantised in the reference cache; {dt:.1f} s"}
+    if gpu_out is not None:
+        r["parity_margin"] = _margin(gpu_out[:n], outs, f"{kind} moe_forward, the {n} sampled tokens")
+    return r
 
 
-def cpu_prefill_rate():
+def cpu_prefill_rate(gpu_out=None):
     """configs[2] on the host cores: the whole 4096-token call, one
     moe_forward(n = 4096) on the Zipf(1.1)-biased layer the GPU leg runs,
     after a first call that dequantised the touched experts into the
-    reference's cache (steady state)."""
+    reference's cache (steady state). With gpu_out, the parity margin of all
+    4096 GPU output rows against the reference's."""
     oracle, ref, kind, cores = _cpu_impl()
     s = oracle.SynthLayer(D, E, K_TOP, I_DIM, G, SEED, 1, zipf_s=1.1)
     x = oracle.synth_tokens(SEED, 3, PREFILL_T, D)
@@ -206,14 +222,17 @@ def cpu_prefill_rate():
     ref.forward(s, x)
     fill = time.perf_counter() - t0
     t0 = time.perf_counter()
-    ref.forward(s, x)
+    out = ref.forward(s, x)[0]
     dt = time.perf_counter() - t0
     if kind == "reference":
         ref.lib.ref_reset_cache()
-    return {"value": PREFILL_T / dt, "unit": "tokens/s", "cores": cores, "kind": kind,
-            "ms_per_call": 1e3 * dt,
-            "sample": f"the full config-2 call: one moe_forward of {PREFILL_T} tokens, experts "
-                      f"pre-dequantised (the first call, {fill:.1f} s, filled the cache); {dt:.1f} s"}
+    r = {"value": PREFILL_T / dt, "unit": "tokens/s", "cores": cores, "kind": kind,
+         "ms_per_call": 1e3 * dt,
+         "sample": f"the full config-2 call: one moe_forward of {PREFILL_T} tokens, experts "
+                   f"pre-dequantised (the first call, {fill:.1f} s, filled the cache); {dt:.1f} s"}
+    if gpu_out is not None:
+        r["parity_margin"] = _margin(gpu_out, out, f"{kind} moe_forward, all {PREFILL_T} rows")
+    return r
 
 
 def cpu_stack_rate(seed, stream, n_tokens, zipf, sample_layers, per_call, label):
@@ -342,6 +361,7 @@ def measure_prefill(ctx, layer_index, rank, reps=5, warmup=3):
     st.synchronize()
     ctx.sync()
     ms = e0.elapsed_time(e1) / reps
+    out_host = out.cpu().numpy()
     us = ctx.profile_forward(layer_index, x.data_ptr(), qmoe.QMOE_BF16, PREFILL_T, out.data_ptr(), reps)
     names = ["route_tc", "route_exact", "group_gather", "gemm_gateup", "gemm_down", "combine"]
     split = {n: float(u) for n, u in zip(names, us)}
@@ -350,6 +370,7 @@ def measure_prefill(ctx, layer_index, rank, reps=5, warmup=3):
     tf = PREFILL_FLOP / (gemm_us * 1e-6) / 1e12 if gemm_us > 0 else None
     del g
     return {"workload": "config2: one MoE layer, prefill 4096 tokens, Zipf(1.1) router bias",
+            "_out": out_host,
             "tokens_per_s": PREFILL_T / (ms / 1e3), "ms_per_call": ms, "kernel_us": split,
             "gpu_launches_per_call": 10,
             "gemm": {"bound": "tensor", "achieved": tf, "peak": bf16, "unit": "TFLOP/s",
@@ -359,11 +380,14 @@ def measure_prefill(ctx, layer_index, rank, reps=5, warmup=3):
                      "(h as a hi/lo pair) per algorithmic one"}}
 
 
-def measure_prefill_ep(rank, world, local, reps=5, warmup=2):
+def measure_prefill_ep(rank, world, local, local_ctx=None, local_layer=1, reps=5, warmup=2):
     """configs[2] expert-parallel over the torchrun ranks: the 4096 tokens
     split evenly, rank g owning experts [g E/W, (g+1) E/W), qmoe_forward_ep
     on each rank (NCCL through the library). Whole-call time = max over
-    ranks of the CUDA-event time per call."""
+    ranks of the CUDA-event time per call. ep_parity: every rank's output
+    rows against the single-GPU path (local_ctx, the same layer with all
+    experts, itself parity-tested against the reference) on the same tokens,
+    worst margins over the ranks."""
     import torch
     import torch.distributed as dist
 
@@ -400,10 +424,23 @@ def measure_prefill_ep(rank, world, local, reps=5, warmup=2):
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms = float(tt.item())
     ctx.close()
+    ep_parity = None
+    if local_ctx is not None:
+        ref = torch.empty_like(out)
+        local_ctx.forward_dev(local_layer, x.data_ptr(), qmoe.QMOE_BF16, T_per, ref.data_ptr(), cs)
+        st.synchronize()
+        local_ctx.sync()
+        a, b = out.double(), ref.double()
+        m = torch.tensor([float((a - b).abs().max()), float((a - b).norm() / b.norm())], device="cuda")
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ep_parity = {"max_abs": float(m[0]), "rel_rms": float(m[1]), "bars": [2e-2, 1e-3],
+                     "ok": float(m[0]) <= 2e-2 and float(m[1]) <= 1e-3,
+                     "against": "the single-GPU path on the same tokens, every rank's rows, worst rank"}
     return {"workload": "config2 expert-parallel: 4096 tokens split over the ranks, Zipf(1.1)",
             "ranks": world, "tokens_per_s": PREFILL_T / (ms / 1e3), "ms_per_call": ms,
             "scaling": "strong", "timing": "CUDA events per rank, max over ranks",
-            "exchange": "NCCL send/recv all-to-all of fp16 rows and fp32 outputs"}
+            "exchange": "NCCL send/recv all-to-all of fp16 rows and fp32 outputs",
+            "ep_parity": ep_parity}
 
 
 STACK_L, STACK_T, STACK_SEED = 76, 64, 20261203
@@ -443,6 +480,28 @@ def measure_stack(rank, world, local, layers=STACK_L, reps=3, warmup=2):
     st = torch.cuda.Stream()
     cs = st.cuda_stream
     torch.cuda.synchronize()
+    ep_parity = None
+    if world > 1:
+        # layer 0 expert-parallel against the single-GPU path on this rank's
+        # tokens (a local context holding all of layer 0's experts)
+        hc = h0.clone()
+        ctx.forward_stack(0, 1, hc.data_ptr(), T_per, 1e-6, cs)
+        st.synchronize()
+        ctx.sync()
+        lc = qmoe.Context(qmoe.make_config(D, E, K_TOP, I_DIM, G, layers=1, max_tokens=T_per,
+                                           device=local))
+        lc.synth_layer_dev(0, STACK_SEED)
+        hl = h0.clone()
+        lc.forward_stack(0, 1, hl.data_ptr(), T_per, 1e-6, cs)
+        st.synchronize()
+        lc.sync()
+        lc.close()
+        a, b = (hc - h0).double(), (hl - h0).double()
+        m = torch.tensor([float((a - b).abs().max()), float((a - b).norm() / b.norm())], device="cuda")
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ep_parity = {"max_abs": float(m[0]), "rel_rms": float(m[1]), "bars": [2e-2, 1e-3],
+                     "ok": float(m[0]) <= 2e-2 and float(m[1]) <= 1e-3,
+                     "against": "layer 0 on the single-GPU path, same tokens, every rank, worst rank"}
     # census pass, layer by layer: the distinct experts each layer touches
     # (over all ranks' tokens), for the algorithmic bytes of a step
     lo, hi = rank * E // world, (rank + 1) * E // world
@@ -510,7 +569,8 @@ def measure_stack(rank, world, local, layers=STACK_L, reps=3, warmup=2):
             "graph_equals_eager": bad == 0.0, "weights_generated_s": synth_s,
             "timing": "one CUDA graph per rank per step, CUDA events, max over ranks",
             "exchange": "NCCL send/recv, fixed-size blocks of fp16 rows and fp32 partials"
-                        if world > 1 else None}
+                        if world > 1 else None,
+            "ep_parity": ep_parity}
 
 
 STREAM_LAYERS, STREAM_POOL_76, STREAM_DECODE, STREAM_PREFILL = 76, 8 * 2 ** 30, 16, 512
@@ -821,7 +881,8 @@ def main():
 
     # parity spot check of the timed outputs (tokens 996..999 of the last
     # replay; out_dev was zeroed before capture, so these come from the graph)
-    out_last = out_dev[TOKENS - 4:].cpu().numpy()
+    gpu_out = out_dev.cpu().numpy()  # every token of the last replay
+    out_last = gpu_out[TOKENS - 4:]
     # (one eager single-token call each: the same kernel, so the same bits)
     ref4 = np.concatenate([ctx.forward(0, x_host[t:t + 1]) for t in range(TOKENS - 4, TOKENS)])
     parity_ok = bool(np.array_equal(out_last, ref4))
@@ -885,11 +946,12 @@ def main():
     traffic = NCU_TRAFFIC.get(dom)
     layer_gbs = layer_bytes_per_token() * (value / world) / 1e9
 
-    prefill = None
+    prefill, prefill_out = None, None
     if not args.no_prefill:
         prefill = measure_prefill(ctx, 1, rank)
+        prefill_out = prefill.pop("_out")
         if world > 1:
-            prefill["expert_parallel"] = measure_prefill_ep(rank, world, local)
+            prefill["expert_parallel"] = measure_prefill_ep(rank, world, local, ctx, 1)
 
     stack = None
     if not args.no_stack:
@@ -902,13 +964,13 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
-            cpu = cpu_reference_rate()
+            cpu = cpu_reference_rate(gpu_out=gpu_out)
         except Exception as e:  # reported, never silently replaced
             cpu = {"value": None, "unit": UNIT, "cores": 0, "kind": "unavailable",
                    "sample": f"failed: {e}"}
         legs = []
         if prefill is not None:
-            legs.append((prefill, cpu_prefill_rate))
+            legs.append((prefill, lambda: cpu_prefill_rate(prefill_out)))
         if stack is not None:
             legs.append((stack, lambda: cpu_stack_rate(STACK_SEED, 100, STACK_T, None, 3, STACK_T,
                                                        "config 3, decode batch 64")))
@@ -948,6 +1010,7 @@ def main():
             "cpu_baseline": cpu,
             "clocks": clk,
             "parity_spot_check": parity_ok,
+            "parity_margin": (cpu or {}).get("parity_margin"),
             "prefill": prefill,
             "stack": stack,
             "stream": stream,

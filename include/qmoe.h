@@ -187,8 +187,13 @@ int qmoe_forward_stack(qmoe_ctx *ctx, int l0, int l1, float *h, int n, float eps
  * kernel attributes, with that device current; make that first call before
  * any stream capture. All calls share the array and each call starts by
  * clearing its error word, barrier counter and exchange area, so calls that
- * overlap on the GPU race; serialise them. The call waits for its work on `stream` (NULL =
- * the legacy default stream) and returns 0, or -1 with a message. */
+ * overlap on the GPU race; serialise them. x, out, router, shared_gate, pool,
+ * slot_of and shared_slot must be 16-byte aligned (the kernel moves them with
+ * 16-byte vector loads and bulk copies; slots are multiples of 16 bytes), and
+ * logit_bias 4-byte aligned: other addresses are refused before any launch.
+ * Before returning, the call synchronises `stream` (NULL = the legacy default
+ * stream) and reads the error word back with a blocking copy; it returns 0,
+ * or -1 with a message. */
 #define QMOE_NOALLOC_SCRATCH_BYTES (64u * 1024u)
 typedef struct {
     int hidden, num_experts, top_k, moe_inter, group_size;

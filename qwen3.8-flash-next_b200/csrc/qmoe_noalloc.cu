@@ -18,6 +18,7 @@
 
 #include <cuda_runtime.h>
 #include <pthread.h>
+#include <stdint.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -39,6 +40,8 @@ void seterr(qmoe_err *err, const char *msg) {
 }
 
 size_t up16(size_t v) { return (v + 15) / 16 * 16; }
+
+bool misaligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
 
 // Per-device set-up on the first call: device address of the array, kernel
 // attributes, SM count. Runs with `dev` current.
@@ -78,6 +81,26 @@ extern "C" int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream
     if (a->x_dtype != QMOE_F32 && a->x_dtype != QMOE_BF16) {
         seterr(err, "qmoe_forward_token_noalloc: unknown x dtype");
         return -1;
+    }
+    // the kernel reads x, the router rows, the shared gate, the slot table and
+    // the slots with 16-byte vector loads and bulk copies, which need 16-byte
+    // aligned addresses: refuse others here rather than fault on the GPU
+    {
+        const struct { const void *p; const char *name; } ptrs[] = {
+            {a->x, "x"}, {a->out, "out"}, {a->router, "router"}, {a->shared_gate, "shared_gate"},
+            {a->pool, "pool"}, {a->slot_of, "slot_of"}, {a->shared_slot, "shared_slot"}};
+        for (const auto &q : ptrs)
+            if (misaligned(q.p, 16)) {
+                char m[160];
+                snprintf(m, sizeof(m),
+                         "qmoe_forward_token_noalloc: %s (%p) is not 16-byte aligned", q.name, q.p);
+                seterr(err, m);
+                return -1;
+            }
+        if (a->logit_bias && misaligned(a->logit_bias, 4)) {
+            seterr(err, "qmoe_forward_token_noalloc: logit_bias is not 4-byte aligned");
+            return -1;
+        }
     }
     qk_layout L;
     if (qk_layout_init(&L, a->hidden, a->num_experts, a->top_k, a->moe_inter, a->group_size)) {

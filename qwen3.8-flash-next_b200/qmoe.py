@@ -2,7 +2,7 @@
 
 The product is the C library; this module only marshals arguments. It is what
 the tests and bench.py use to reach the C ABI, and it is the binding a Python
-host of the reference runtime would add (see INTEGRATION.md). Loading fails
+host of the reference runtime would add. Loading fails
 loudly when libqmoe.so has not been built; there is no fallback path.
 """
 from __future__ import annotations

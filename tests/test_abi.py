@@ -126,3 +126,31 @@ def test_binding_arity_matches_the_header(built):
     assert set(ar) == set(qmoe.SIGNATURES), set(ar) ^ set(qmoe.SIGNATURES)
     bad = {n: (len(qmoe.SIGNATURES[n][1]), k) for n, k in ar.items() if len(qmoe.SIGNATURES[n][1]) != k}
     assert not bad, bad
+
+
+def test_noalloc_refuses_bad_arguments_before_any_launch(built):
+    """qmoe_forward_token_noalloc checks its arguments on the host before any
+    CUDA call: a misaligned pointer (the kernel moves its inputs with 16-byte
+    vector loads and bulk copies) and a shape beyond the library's scratch
+    array are refused with a message. No GPU is needed for either."""
+    import ctypes as C
+
+    import qmoe
+    lib = qmoe.lib()
+    base = dict(x=16, out=16, router=16, shared_gate=16, pool=16, slot_of=16, shared_slot=16)
+    for name in base:
+        p = dict(base, **{name: base[name] + 4})
+        a = qmoe.TokenArgs(2048, 512, 10, 512, 64, p["x"], qmoe.QMOE_F32, p["out"], p["router"],
+                           p["shared_gate"], None, p["pool"], p["slot_of"], p["shared_slot"])
+        err = qmoe.Err()
+        assert lib.qmoe_forward_token_noalloc(C.byref(a), None, C.byref(err)) == -1
+        assert f"{name} (" in err.text() and "16-byte aligned" in err.text(), err.text()
+    a = qmoe.TokenArgs(2048, 512, 10, 512, 64, 16, qmoe.QMOE_F32, 16, 16, 16, 18, 16, 16, 16)
+    err = qmoe.Err()
+    assert lib.qmoe_forward_token_noalloc(C.byref(a), None, C.byref(err)) == -1
+    assert "logit_bias" in err.text()
+    # k=32, I=1024 needs ~135 KB of scratch, more than the library's 64 KB
+    a = qmoe.TokenArgs(2048, 64, 32, 1024, 64, 16, qmoe.QMOE_F32, 16, 16, 16, None, 16, 16, 16)
+    err = qmoe.Err()
+    assert lib.qmoe_forward_token_noalloc(C.byref(a), None, C.byref(err)) == -1
+    assert "QMOE_NOALLOC_SCRATCH_BYTES" in err.text()

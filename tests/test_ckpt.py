@@ -329,8 +329,6 @@ def test_layer_reader_checks_names_types_and_shapes(built, tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.xfail(reason="first run of the checkpoint upload on a GPU; the marker goes once it has passed",
-                   strict=False)
 def test_upload_from_checkpoint_equals_upload_from_memory(tiny_ckpt):
     """qmoe_upload_layer_ckpt (a layer read from the files, then uploaded)
     gives the same outputs, bit for bit, as qmoe_upload_layer of the arrays

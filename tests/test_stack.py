@@ -77,6 +77,7 @@ def _check(layers, hs, h_all, routes):
     amplifies a layer's input differences, so an absolute bar is not
     meaningful there)."""
     import oracle
+    from conftest import record_margin
     assert np.array_equal(hs[-1], h_all), "one call per layer differs from one call per stack"
     for l, s in enumerate(layers):
         ry, ridx, _ = oracle.restatement().forward(s, rmsnorm(hs[l]))
@@ -85,10 +86,13 @@ def _check(layers, hs, h_all, routes):
         mab = float(np.abs(y - ry).max())
         rr = float(np.linalg.norm(y - ry) / np.linalg.norm(ry))
         bar = 2e-2 * max(1.0, float(np.sqrt(np.mean(ry.astype(np.float64) ** 2))) / CFG1_OUT_RMS)
+        record_margin(f"layer {l} output vs restatement", mab, rr, {"max_abs": bar, "rel_rms": 1e-3})
         assert mab <= bar and rr <= 1e-3, (l, mab, bar, rr)
     ref, _ = compose(layers, hs[0])
     delta, rdelta = h_all - hs[0], ref - hs[0]
     rr = float(np.linalg.norm(delta - rdelta) / np.linalg.norm(rdelta))
+    record_margin("whole stack vs composition", float(np.abs(delta - rdelta).max()), rr,
+                  {"rel_rms": 1e-3})
     assert rr <= 1e-3, rr
 
 
