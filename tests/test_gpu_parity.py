@@ -13,6 +13,11 @@ pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 MAX_ABS = 2e-2
 REL_RMS = 1e-3
+# measured precision of the paths on B200 (worst seen: decode 1.0e-3 /
+# 7.3e-6, grouped tensor-core path 1.0e-3 / 8.2e-6, configs[0] 6.7e-6 /
+# 7.2e-7), with headroom: a regression toward the north-star bars fails here
+TIGHT = (3e-3, 3e-5)
+TIGHT_CFG0 = (1e-4, 1e-5)
 
 
 def _sorted(idx, w):
@@ -72,10 +77,10 @@ def test_cfg0_matches_reference_golden(built):
     si, sw = _sorted(idx, w)
     assert np.array_equal(si, g["idx_sorted"])
     np.testing.assert_allclose(sw, g["w_sorted"], rtol=1e-5, atol=1e-6)
-    _close(out, g["out"], "cfg0 vs reference golden")
+    _close(out, g["out"], "cfg0 vs reference golden", TIGHT_CFG0)
     ro, ri, rw = oracle.restatement().forward(s, x)
     assert np.array_equal(idx, ri)  # same (value desc, index asc) order
-    _close(out, ro, "cfg0 vs restatement")
+    _close(out, ro, "cfg0 vs restatement", TIGHT_CFG0)
     ctx.close()
 
 
@@ -90,7 +95,7 @@ def test_cfg1_decode_matches_reference_golden(cfg1_layer, cfg1_ctx):
         si, sw = _sorted(idx, w)
         assert np.array_equal(si[0], g["idx_sorted"][t])
         np.testing.assert_allclose(sw[0], g["w_sorted"][t], rtol=1e-5, atol=1e-6)
-        _close(out, g["out"][t:t + 1], f"cfg1 decode token {t} vs reference golden")
+        _close(out, g["out"][t:t + 1], f"cfg1 decode token {t} vs reference golden", TIGHT)
 
 
 def test_cfg1_decode_matches_restatement(cfg1_layer, cfg1_ctx):
@@ -104,7 +109,7 @@ def test_cfg1_decode_matches_restatement(cfg1_layer, cfg1_ctx):
         idx, w, _ = cfg1_ctx.routing(1)
         assert np.array_equal(idx[0], ri[t])
         np.testing.assert_allclose(w[0], rw[t], rtol=1e-5, atol=1e-6)
-        _close(out, ro[t:t + 1], f"cfg1 decode token {t} vs restatement")
+        _close(out, ro[t:t + 1], f"cfg1 decode token {t} vs restatement", TIGHT)
 
 
 def test_batch_equals_token_by_token(cfg1_layer, cfg1_ctx):
@@ -121,7 +126,7 @@ def test_batch_equals_token_by_token(cfg1_layer, cfg1_ctx):
         one = cfg1_ctx.forward(0, x[t:t + 1])
         idx1, w1, _ = cfg1_ctx.routing(1)
         assert np.array_equal(idx1[0], idx_full[t])
-        _close(full[t:t + 1], one, f"batch row {t} vs single-token call")
+        _close(full[t:t + 1], one, f"batch row {t} vs single-token call", TIGHT)
 
 
 def test_prefill_cfg1_shapes_matches_restatement(cfg1_layer, cfg1_ctx):
@@ -135,7 +140,7 @@ def test_prefill_cfg1_shapes_matches_restatement(cfg1_layer, cfg1_ctx):
     ro, ri, rw = oracle.restatement().forward(s, x)
     assert np.array_equal(idx, ri)
     np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-6)
-    _close(out, ro, "64-token grouped path vs restatement")
+    _close(out, ro, "64-token grouped path vs restatement", TIGHT)
 
 
 def test_prefill_routing_ties_take_exact_path(cfg1_layer, cfg1_ctx):
@@ -156,7 +161,7 @@ def test_prefill_routing_ties_take_exact_path(cfg1_layer, cfg1_ctx):
     assert np.array_equal(idx, ri)
     np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-6)
     assert idx[3].tolist() == list(range(10))
-    _close(out[[0, 1, 2, 3, 4, 6, 7]], ro[[0, 1, 2, 3, 4, 6, 7]], "tie tokens vs restatement")
+    _close(out[[0, 1, 2, 3, 4, 6, 7]], ro[[0, 1, 2, 3, 4, 6, 7]], "tie tokens vs restatement", TIGHT)
 
 
 def test_prefill_cfg2_full_zipf(built):
@@ -186,12 +191,12 @@ def test_prefill_cfg2_full_zipf(built):
         rsi, rsw = _sorted(ri, rw)
         assert np.array_equal(si, rsi)
         np.testing.assert_allclose(sw, rsw, rtol=1e-5, atol=1e-6)
-        _close(out, ro, "cfg2 all 4096 rows vs reference build")
+        _close(out, ro, "cfg2 all 4096 rows vs reference build", TIGHT)
     else:
         sample = np.linspace(0, n - 1, 512).astype(int)
         ro, ri, rw = oracle.restatement().forward(s, x[sample])
         assert np.array_equal(idx[sample], ri)
-        _close(out[sample], ro, "cfg2 512 sampled rows vs restatement")
+        _close(out[sample], ro, "cfg2 512 sampled rows vs restatement", TIGHT)
 
 
 def test_cfg2_zipf_routing_bit_exact(built):

@@ -62,20 +62,13 @@ def _run_stack(shape, n_layers, n, seed):
     return layers, hs, h_all, routes
 
 
-# RMS of one config-1 layer's output on bf16 N(0, 1) tokens (the scale the
-# layer bars were set at): deeper layers of the stack produce outputs ~10x
-# larger, and their absolute bar scales with them
-CFG1_OUT_RMS = 16.05
-
-
 def _check(layers, hs, h_all, routes):
     """Per layer, on the device's own input h_l: routing bit-exact and the
-    layer's output y_l = h_{l+1} - h_l within the layer bars: relative RMS
-    1e-3, max-abs 2e-2 scaled by the output's RMS over a config-1 layer's
-    (never below 2e-2). End to end against the oracle's own composition:
-    relative RMS of the stack's contribution within 1e-3 (the stack
-    amplifies a layer's input differences, so an absolute bar is not
-    meaningful there)."""
+    layer's output y_l = h_{l+1} - h_l within the north-star bars (max-abs
+    2e-2, relative RMS 1e-3). End to end against the oracle's own
+    composition: relative RMS of the stack's contribution within 1e-3 (the
+    stack amplifies a layer's input differences, so the absolute bar is
+    reported there but not imposed)."""
     import oracle
     from conftest import record_margin
     assert np.array_equal(hs[-1], h_all), "one call per layer differs from one call per stack"
@@ -85,9 +78,8 @@ def _check(layers, hs, h_all, routes):
         y = hs[l + 1].astype(np.float64) - hs[l].astype(np.float64)
         mab = float(np.abs(y - ry).max())
         rr = float(np.linalg.norm(y - ry) / np.linalg.norm(ry))
-        bar = 2e-2 * max(1.0, float(np.sqrt(np.mean(ry.astype(np.float64) ** 2))) / CFG1_OUT_RMS)
-        record_margin(f"layer {l} output vs restatement", mab, rr, {"max_abs": bar, "rel_rms": 1e-3})
-        assert mab <= bar and rr <= 1e-3, (l, mab, bar, rr)
+        record_margin(f"layer {l} output vs restatement", mab, rr, {"max_abs": 2e-2, "rel_rms": 1e-3})
+        assert mab <= 2e-2 and rr <= 1e-3, (l, mab, rr)
     ref, _ = compose(layers, hs[0])
     delta, rdelta = h_all - hs[0], ref - hs[0]
     rr = float(np.linalg.norm(delta - rdelta) / np.linalg.norm(rdelta))
