@@ -1098,6 +1098,37 @@ int qmoe__phase_times(qmoe_ctx *c, int layer, const void *x, int x_dtype, float 
     return rc == 0 ? c->num_sms : -1;
 }
 
+/* Diagnostics (not in the public header): n_tokens single-token launches of
+ * the single-launch kernel back to back on the context's stream with
+ * programmatic dependent launch, as a captured decode step runs them, token t
+ * from x + t d (x_dtype) into out + t d, each with per-CTA phase timestamps:
+ * out_ns receives [n_tokens][max_ctas][32] values. Returns the grid size, or
+ * -1. */
+int qmoe__phase_times_seq(qmoe_ctx *c, int layer, const void *x, int x_dtype, float *out,
+                          int n_tokens, unsigned long long *out_ns, int max_ctas) {
+    if (!c || !c->resident_all || !c->layers[layer].ready || n_tokens < 1) return -1;
+    const size_t per = (size_t)c->num_sms * 32;
+    unsigned long long *buf = NULL;
+    if (cudaMalloc((void **)&buf, per * n_tokens * sizeof(unsigned long long)) != cudaSuccess)
+        return -1;
+    int rc = cudaMemset(buf, 0, per * n_tokens * sizeof(unsigned long long));
+    const size_t xb = (size_t)c->L.d * (x_dtype == QMOE_BF16 ? 2 : 4);
+    for (int t = 0; rc == 0 && t < n_tokens; t++) {
+        qk_fwd f;
+        fill_fwd(c, layer, (const char *)x + t * xb, x_dtype == QMOE_BF16, 1,
+                 out + (size_t)t * c->L.d, &f);
+        f.ptimes = buf + per * t;
+        rc = qk_launch_decode_fused(&f, c->dsync, c->stream, t > 0);
+    }
+    if (rc == 0) rc = cudaStreamSynchronize(c->stream);
+    const int n = max_ctas < c->num_sms ? max_ctas : c->num_sms;
+    for (int t = 0; rc == 0 && t < n_tokens; t++)
+        rc = cudaMemcpy(out_ns + (size_t)t * max_ctas * 32, buf + per * t,
+                        (size_t)n * 32 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(buf);
+    return rc == 0 ? c->num_sms : -1;
+}
+
 int qmoe_profile_forward(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, float *out,
                          int reps, double *kernel_us, int max_kernels, int *kernels,
                          qmoe_err *err) {

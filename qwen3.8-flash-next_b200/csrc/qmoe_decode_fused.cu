@@ -13,17 +13,20 @@
 //   phase 2   every CTA takes all logits as order keys and computes the same
 //             exact top-k (block-wide threshold, then one warp ranks the
 //             candidates), looks the k experts up in the staged slot table
-//             and issues its share of their gate/up rows (in chunks of <= 8
+//             and issues its share of their gate/up rows (in chunks of <= 16
 //             rows, one mbarrier each) and of their down rows (all k experts
 //             at once). Meanwhile the warps that do not share warp 0's
 //             scheduler compute the shared expert's gate/up rows. Then all
 //             warps compute the routed gate/up rows
 //             chunk by chunk as they land -> h.              [grid barrier]
-//   phase 3   h -> 24-bit integers in shared memory; this CTA's output rows
-//             for all k+1 experts as (expert, row-pair) tasks, so a warp keeps
-//             one expert's h slice in registers across rows; per-expert
-//             partials are combined in a fixed expert order with the routing
-//             weights and the shared gate; each output written once.
+//   phase 3   h -> 24-bit integers in shared memory (every h load of a
+//             thread issued before it quantizes); this CTA's output rows with
+//             one warp per expert: the expert's h units stay in registers
+//             while the warp walks the rows, one partial per row step in
+//             registers, the row reductions (shuffles) batched at the end;
+//             per-expert partials are combined in a fixed expert order with
+//             the routing weights and the shared gate; each output written
+//             once.
 //
 // The q4 products are the integer dot products of qmoe_dev.cuh (quant_word,
 // dot_unit_q): four dp4a per q4 word for x, six for h. The router dot keeps
@@ -46,11 +49,13 @@ namespace {
 
 constexpr int kThreads = 512;   // 16 warps, one CTA per SM
 constexpr int kWarps = kThreads / 32;
-constexpr int kChunkRows = 8;   // routed gate/up rows per bulk copy / mbarrier
+constexpr int kChunkRows = 16;  // routed gate/up rows per bulk copy / mbarrier (one per warp)
 constexpr int kMaxChunks = 12;  // chunks per CTA (checked by make_plan)
 constexpr int kXB = 2;          // byte planes of x
 constexpr int kHB = 3;          // byte planes of h
 constexpr int kSyncWords = 32;  // 64-bit words before the exchange area
+constexpr int kHW = 2;          // h words (8 values) quantized per thread in phase 3
+constexpr int kRowSteps = 8;    // phase 3: output row steps per expert warp (checked by make_plan)
 
 struct Plan {
     int G;       // CTAs, one per SM
@@ -145,48 +150,62 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     float *xusm = xusc + d / 32;                              // [d / 32] unit sums
     double2 *rx = reinterpret_cast<double2 *>(smem + p.off_x);  // x staged for the router
 
-    // diagnostics: phase timestamps of this CTA (thread 0)
-#define STAMP(i)                                                                         \
-    do {                                                                                 \
-        if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 32 + (i)] = gtimer(); \
+    // diagnostics: phase timestamps of this CTA (thread 0, %globaltimer),
+    // kept in shared memory and written out when the CTA ends, so the probe
+    // adds no global stores along the way
+    __shared__ unsigned long long s_stamp[32];
+#define STAMP(i)                                   \
+    do {                                           \
+        if (f.ptimes && tid == 0) s_stamp[(i)] = gtimer(); \
     } while (0)
+    if (f.ptimes && tid < 32) s_stamp[tid] = 0ull;
     STAMP(0);
-    if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 32 + 30] = clock64();
+    if (f.ptimes && tid == 0) s_stamp[30] = clock64();
+    const uint32_t b_router = static_cast<uint32_t>((rr1 - rr0) * d * 2);
+    const uint32_t b_sgu = static_cast<uint32_t>((sr1 - sr0) * L.gu_row);
+    const uint32_t b_sdown = static_cast<uint32_t>((or1 - or0) * L.d_row);
+    const uint32_t b_slots = static_cast<uint32_t>(E * 4);
     if (tid < 2 + kMaxChunks) mbar_init(&bar[tid], 1);
+    // the prologue barrier's byte count before any of its copies is issued
+    if (tid == 0) mbar_expect_tx(&bar[0], b_router + b_sgu + b_sdown + b_slots);
     __syncthreads();
 
-    // ---- prologue: what does not depend on routing
-    if (tid == 0) {
-        const uint32_t b_router = static_cast<uint32_t>((rr1 - rr0) * d * 2);
-        const uint32_t b_sgu = static_cast<uint32_t>((sr1 - sr0) * L.gu_row);
-        const uint32_t b_sdown = static_cast<uint32_t>((or1 - or0) * L.d_row);
-        const uint32_t b_slots = static_cast<uint32_t>(E * 4);
-        mbar_expect_tx(&bar[0], b_router + b_sgu + b_sdown + b_slots);
-        STAMP(18);
+    // ---- prologue: what does not depend on routing. Five bulk copies, each
+    // issued by lane 0 of its own warp among the last six (a TMA issue costs
+    // ~0.1 us; the warps issue in parallel), while the sixth plans the routed
+    // gate/up chunks; the first warps, which stage x, go straight on to it.
+    {
         const int re = min(rr1, E);
-        if (re > rr0)
-            bulk_load(sm_router, f.router + static_cast<size_t>(rr0) * d,
-                      static_cast<uint32_t>((re - rr0) * d * 2), &bar[0]);
-        if (rr1 > E)
-            bulk_load(sm_router + static_cast<size_t>(E - rr0) * d * 2, f.shared_gate,
-                      static_cast<uint32_t>(d * 2), &bar[0]);
-        bulk_load(s_slots, f.slot_of, b_slots, &bar[0]);
-        if (sr1 > sr0)
-            bulk_load(sm_sgu, f.shared_slot + static_cast<size_t>(sr0) * L.gu_row, b_sgu, &bar[0]);
-        if (or1 > or0)
-            bulk_load(sm_down + static_cast<size_t>(k) * p.or_max * L.d_row,
-                      f.shared_slot + L.gu_bytes + static_cast<size_t>(or0) * L.d_row, b_sdown,
-                      &bar[0]);
-        STAMP(19);
-        // routed gate/up chunk boundaries: runs within one expert, <= 8 rows
-        int n = 0, r = gr0;
-        while (r < gr1 && n < kMaxChunks) {
-            const int end = min(min(gr1, (r / I + 1) * I), r + kChunkRows);
-            s_chunk0[n++] = r - gr0;
-            r = end;
+        const int q = warp - (kWarps - 6);  // 0..5 for the last six warps
+        if (q == 0 && lane == 0) {
+            if (re > rr0)
+                bulk_load(sm_router, f.router + static_cast<size_t>(rr0) * d,
+                          static_cast<uint32_t>((re - rr0) * d * 2), &bar[0]);
+        } else if (q == 1 && lane == 0) {
+            if (rr1 > E)
+                bulk_load(sm_router + static_cast<size_t>(E - rr0) * d * 2, f.shared_gate,
+                          static_cast<uint32_t>(d * 2), &bar[0]);
+        } else if (q == 2 && lane == 0) {
+            bulk_load(s_slots, f.slot_of, b_slots, &bar[0]);
+        } else if (q == 3 && lane == 0) {
+            if (sr1 > sr0)
+                bulk_load(sm_sgu, f.shared_slot + static_cast<size_t>(sr0) * L.gu_row, b_sgu, &bar[0]);
+        } else if (q == 4 && lane == 0) {
+            if (or1 > or0)
+                bulk_load(sm_down + static_cast<size_t>(k) * p.or_max * L.d_row,
+                          f.shared_slot + L.gu_bytes + static_cast<size_t>(or0) * L.d_row, b_sdown,
+                          &bar[0]);
+        } else if (q == 5 && lane == 0) {
+            // routed gate/up chunk boundaries: runs within one expert, <= 16 rows
+            int n = 0, r = gr0;
+            while (r < gr1 && n < kMaxChunks) {
+                const int end = min(min(gr1, (r / I + 1) * I), r + kChunkRows);
+                s_chunk0[n++] = r - gr0;
+                r = end;
+            }
+            s_chunk0[n] = gr1 - gr0;
+            s_nchunks = n;
         }
-        s_chunk0[n] = gr1 - gr0;
-        s_nchunks = n;
     }
     STAMP(24);
     pdl_wait();
@@ -194,7 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     // twice), so it starts at a multiple of 2G; when this CTA reads it, at
     // most G - 1 arrivals of this launch can have happened (the first
     // barrier needs this CTA), so rounding down gives the launch's base.
-    if (tid == 0) s_base = ld_acquire64(sync) / (2ull * G) * (2ull * G);
+    // (Read by the last thread, which stages no x: x's loads go out at once.)
+    if (tid == kThreads - 1) s_base = ld_acquire64(sync) / (2ull * G) * (2ull * G);
     float *lg = reinterpret_cast<float *>(sync + kSyncWords);  // [E + 1] logits
     float *hf = lg + ((E + 1 + 3) & ~3);                       // [S * I] h
     STAMP(1);
@@ -361,27 +381,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
             mbar_expect_tx(&bar[2 + lane],
                            static_cast<uint32_t>((s_chunk0[lane + 1] - s_chunk0[lane]) * L.gu_row));
         if (lane < k) s_slotp[lane] = sp;
-        __syncwarp();
-        STAMP(26);
-        // the routed gate/up rows: one bulk copy per chunk (nch <= 12); the
-        // down rows follow below as 16-byte asynchronous copies by every
-        // thread (a bulk copy costs tens of ns to issue)
-        const int s = lane < nch ? (gr0 + s_chunk0[lane]) / I : 0;
-        const uint8_t *src =
-            reinterpret_cast<const uint8_t *>(__shfl_sync(QK_FULL, reinterpret_cast<uintptr_t>(sp), s & 31));
-        if (good && lane < nch) {
-            const int lo = gr0 + s_chunk0[lane], hi = gr0 + s_chunk0[lane + 1];
-            bulk_load(sm_rgu + static_cast<size_t>(lo - gr0) * L.gu_row,
-                      src + static_cast<size_t>(lo - s * I) * L.gu_row,
-                      static_cast<uint32_t>((hi - lo) * L.gu_row), &bar[2 + lane]);
-        }
-        STAMP(14);
         if (lane == 0) {
             r_w[k] = 1.0f / (1.0f + expf(-s_gl));
             if (!okk) atomicOr(f.err, QK_ERR_BAD_ROUTE);
             else if (!resident) atomicOr(f.err, QK_ERR_NOT_RESIDENT);
             s_ok = good ? 1 : 0;
         }
+        STAMP(26);
+        __syncwarp();
+        // the routed gate/up rows: one bulk copy per chunk (nch <= 12), from
+        // the chunk's lane; the down rows follow below as 16-byte
+        // asynchronous copies by every thread
+        if (good) {
+            if (lane < nch) {
+                const int lo = gr0 + s_chunk0[lane], hi = gr0 + s_chunk0[lane + 1];
+                const int sx = lo / I;
+                bulk_load(sm_rgu + static_cast<size_t>(lo - gr0) * L.gu_row,
+                          s_slotp[sx] + static_cast<size_t>(lo - sx * I) * L.gu_row,
+                          static_cast<uint32_t>((hi - lo) * L.gu_row), &bar[2 + lane]);
+            }
+        }
+        STAMP(14);
         if (c == 0 && okk) {
             if (lane < k) {
                 f.idx[lane] = r_idx[lane];
@@ -389,17 +409,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
             }
             if (lane == 0) f.sgate[0] = r_w[k];
         }
-    } else if (ok0) {
+    } else if (ok0 && warp % 4 != 0) {
         // the shared expert's gate/up rows while warp 0 routes, on the warps
         // that do not share warp 0's scheduler (warp w issues on scheduler
         // w % 4): warp 0's top-k is on the critical path
-        if (warp % 4 != 0) {
-            const int helper = warp - 1 - warp / 4, helpers = kWarps - kWarps / 4;
-            for (int i = helper; i < sr1 - sr0; i += helpers) {
-                const float hv =
-                    gateup_row<UPL>(sm_sgu + static_cast<size_t>(i) * L.gu_row, L, xw, xsc, xsm, lane);
-                if (lane == 0) hf[static_cast<size_t>(k) * I + sr0 + i] = hv;
-            }
+        const int helper = warp - 1 - warp / 4, helpers = kWarps - kWarps / 4;
+        for (int i = helper; i < sr1 - sr0; i += helpers) {
+            const float hv =
+                gateup_row<UPL>(sm_sgu + static_cast<size_t>(i) * L.gu_row, L, xw, xsc, xsm, lane);
+            if (lane == 0) hf[static_cast<size_t>(k) * I + sr0 + i] = hv;
         }
     }
     __syncthreads();
@@ -410,9 +428,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         // at s * or_max rows), 16 bytes per copy, spread over every thread
         const int per = (or1 - or0) * (L.d_row / 16);
         for (int i = tid; i < k * per; i += kThreads) {
-            const int s = i / per, rem = i - s * per;
-            cp_async16(sm_down + static_cast<size_t>(s) * p.or_max * L.d_row + 16 * static_cast<size_t>(rem),
-                       s_slotp[s] + L.gu_bytes + static_cast<size_t>(or0) * L.d_row + 16 * static_cast<size_t>(rem));
+            const int sx = i / per, rem = i - sx * per;
+            cp_async16(sm_down + static_cast<size_t>(sx) * p.or_max * L.d_row + 16 * static_cast<size_t>(rem),
+                       s_slotp[sx] + L.gu_bytes + static_cast<size_t>(or0) * L.d_row + 16 * static_cast<size_t>(rem));
         }
         cp_async_commit();
     }
@@ -446,31 +464,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     if (!live) return;
 
     // ---- phase 3: h -> 24-bit integers (kHB planes of S * I / 8 words, one
-    // scale and sum per 32-element unit), down rows + weighted combine
+    // scale and sum per 32-element unit); a thread's kHW words are all loaded
+    // before it quantizes, so the L2 round trip is paid once
     const int hwn = S * (I / 8), upe = I / 32;
     uint2 *hq = reinterpret_cast<uint2 *>(sm_rgu);
     float *husc = reinterpret_cast<float *>(hq + kHB * hwn);
     float *husm = husc + S * upe;
-    float *partial = husm + S * upe;  // [S][or_max]
-    for (int w0 = 0; w0 < hwn; w0 += kThreads) {
-        const int w = w0 + tid;
-        float v[8];
-        if (w < hwn) {
-            const float4 *hp = reinterpret_cast<const float4 *>(hf) + 2 * w;
-            const float4 a = __ldcg(hp), b = __ldcg(hp + 1);
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-        } else {
+    {
+        float4 hl[kHW][2];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        for (int r = 0; r < kHW; ++r) {
+            const int w = tid + r * kThreads;
+            if (w < hwn) {
+                const float4 *hp = reinterpret_cast<const float4 *>(hf) + 2 * w;
+                hl[r][0] = __ldcg(hp);
+                hl[r][1] = __ldcg(hp + 1);
+            } else {
+                hl[r][0] = make_float4(0.f, 0.f, 0.f, 0.f);
+                hl[r][1] = hl[r][0];
+            }
         }
-        uint2 pl[kHB];
-        float usum;
-        const float sc = quant_word<kHB>(v, pl, &usum);
-        if (w < hwn) {
-            store_word<kHB>(hq, hwn, w, pl);
-            if ((w & 3) == 0) {
-                husc[w >> 2] = sc;
-                husm[w >> 2] = usum;
+#pragma unroll
+        for (int r = 0; r < kHW; ++r) {
+            if (r * kThreads >= hwn) break;  // CTA-uniform
+            const int w = tid + r * kThreads;
+            const float v[8] = {hl[r][0].x, hl[r][0].y, hl[r][0].z, hl[r][0].w,
+                                hl[r][1].x, hl[r][1].y, hl[r][1].z, hl[r][1].w};
+            uint2 pl[kHB];
+            float usum;
+            const float sc = quant_word<kHB>(v, pl, &usum);
+            if (w < hwn) {
+                store_word<kHB>(hq, hwn, w, pl);
+                if ((w & 3) == 0) {
+                    husc[w >> 2] = sc;
+                    husm[w >> 2] = usum;
+                }
             }
         }
     }
@@ -479,39 +507,47 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     STAMP(10);
     if (!ok1) return;
     STAMP(11);
-    // tasks (expert s, row group) in expert-major order; warp w owns a
-    // contiguous task range, so it reloads its h slice only when s changes
+    // down: warp w takes expert s = w (and w + 16, ...): its h units stay in
+    // registers (lane j holds unit j % LPR) while it walks the CTA's output
+    // rows, RPW rows per step, keeping one partial per row step in registers;
+    // each row's LPR lanes then reduce by shuffles (all row steps at once) into
+    // partial[s][row]. The combine sums the partials in expert order with the
+    // routing weights (the shared gate last); each output is written once.
     constexpr int RPW = 32 / LPR;
     const int nrows = or1 - or0;
-    const int ngrp = (nrows + RPW - 1) / RPW;
-    const int ntask = S * ngrp;
-    const int t0 = warp * ntask / kWarps, t1 = (warp + 1) * ntask / kWarps;
+    const int nsteps = (nrows + RPW - 1) / RPW;  // <= kRowSteps (make_plan)
     const int j = lane % LPR;
     const int grp = (32 * j) / L.g;
-    int cur = -1;
-    uint2 hv[kHB][4];
-    float hsc = 0.f, hsm = 0.f;
-    for (int t = t0; t < t1; ++t) {
-        const int s = t / ngrp, rg = t % ngrp;
-        if (s != cur) {
-            load_unit<kHB>(hq, hwn, s * upe + j, hv);
-            hsc = husc[s * upe + j];
-            hsm = husm[s * upe + j];
-            cur = s;
-        }
-        const int rl = rg * RPW + lane / LPR;
-        const int rlc = rl < nrows ? rl : 0;
-        const uint8_t *row = sm_down + (static_cast<size_t>(s) * p.or_max + rlc) * L.d_row;
-        const uint4 w = *reinterpret_cast<const uint4 *>(row + 16 * j);
-        const uint32_t sb = *reinterpret_cast<const uint32_t *>(row + I / 2 + 4 * grp);
-        float part_ = fmaf(bf16lo(sb), dot_unit_q<kHB>(w, hv) * hsc, bf16hi(sb) * hsm);
+    float *partial = husm + S * upe;  // [S][or_max]
+    for (int s = warp; s < S; s += kWarps) {
+        uint2 hv[kHB][4];
+        load_unit<kHB>(hq, hwn, s * upe + j, hv);
+        const float hsc = husc[s * upe + j], hsm = husm[s * upe + j];
+        const uint8_t *rows = sm_down + static_cast<size_t>(s) * p.or_max * L.d_row;
+        float part[kRowSteps];
 #pragma unroll
-        for (int off = LPR / 2; off >= 1; off >>= 1) part_ += __shfl_xor_sync(QK_FULL, part_, off);
-        if (j == 0 && rl < nrows) partial[s * p.or_max + rl] = part_;
+        for (int q = 0; q < kRowSteps; ++q) {
+            part[q] = 0.f;
+            const int rl = q * RPW + lane / LPR;
+            if (q < nsteps && rl < nrows) {
+                const uint8_t *row = rows + static_cast<size_t>(rl) * L.d_row;
+                const uint4 w = *reinterpret_cast<const uint4 *>(row + 16 * j);
+                const uint32_t sb = *reinterpret_cast<const uint32_t *>(row + I / 2 + 4 * grp);
+                part[q] = fmaf(bf16lo(sb), dot_unit_q<kHB>(w, hv) * hsc, bf16hi(sb) * hsm);
+            }
+        }
+#pragma unroll
+        for (int off = LPR / 2; off >= 1; off >>= 1)
+#pragma unroll
+            for (int q = 0; q < kRowSteps; ++q) part[q] += __shfl_xor_sync(QK_FULL, part[q], off);
+#pragma unroll
+        for (int q = 0; q < kRowSteps; ++q) {
+            const int rl = q * RPW + lane / LPR;
+            if (j == 0 && q < nsteps && rl < nrows) partial[s * p.or_max + rl] = part[q];
+        }
     }
-    STAMP(16);
     __syncthreads();
-    STAMP(17);
+    STAMP(16);
     // combine in expert order: out = sum_s w_s * partial_s (shared gate last)
     for (int rl = tid; rl < nrows; rl += kThreads) {
         float acc = 0.f;
@@ -519,7 +555,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         f.out[or0 + rl] = acc;
     }
     STAMP(12);
-    if (f.ptimes && tid == 0) f.ptimes[static_cast<size_t>(c) * 32 + 31] = clock64();
+    if (f.ptimes && tid == 0) {
+        s_stamp[31] = clock64();
+        for (int i = 0; i < 32; ++i) f.ptimes[static_cast<size_t>(c) * 32 + i] = s_stamp[i];
+    }
 #undef STAMP
 }
 
@@ -548,6 +587,8 @@ bool make_plan(const qk_fwd *f, Plan *p) {
     // after phase 2 the routed gate/up area holds h (planes, unit scales and
     // sums) and the per-expert partial outputs
     const int h_bytes = kHB * S * (L.I / 8) * 8 + 2 * S * (L.I / 32) * 4 + S * p->or_max * 4;
+    if (S * (L.I / 8) > kHW * kThreads) return false;  // phase 3's h words per thread
+    if ((p->or_max + 32 / (L.I / 32) - 1) / (32 / (L.I / 32)) > kRowSteps) return false;
     off = align128(off + (p->gr_max * L.gu_row > h_bytes ? p->gr_max * L.gu_row : h_bytes));
     p->off_down = off;
     off = align128(off + S * p->or_max * L.d_row);
