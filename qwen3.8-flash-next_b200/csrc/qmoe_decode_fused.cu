@@ -8,8 +8,9 @@
 //             this CTA's router rows (mlp.gate plus the shared-gate row), its
 //             rows of the shared expert (gate/up and down) and the layer's
 //             expert -> slot table. Issued before griddepcontrol.wait.
-//   phase 1   x -> fp64 in shared memory (router) and as 16-bit integers
-//             (quant_word); router rows -> logits.           [grid barrier]
+//   phase 1   x -> fp64 in shared memory; router rows -> logits; while the
+//             grid barrier is pending, x -> 16-bit integers (quant_word) for
+//             the experts.                                     [grid barrier]
 //   phase 2   every CTA takes all logits as order keys and computes the same
 //             exact top-k (block-wide threshold, then one warp ranks the
 //             candidates), looks the k experts up in the staged slot table
@@ -219,48 +220,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     float *hf = lg + ((E + 1 + 3) & ~3);                       // [S * I] h
     STAMP(1);
 
-    // ---- phase 1: x -> fp32 (router) and 16-bit integers; thread t owns
-    // the q4 word position t (elements 8t .. 8t + 7)
-    for (int t0 = 0; t0 < xwn; t0 += kThreads) {
-        const int t = t0 + tid;
-        float v[8];
+    // ---- phase 1: x -> fp64 in shared memory for the router; thread t owns
+    // the q4 word position t (elements 8t .. 8t + 7) and keeps its 8 values
+    // in registers for the integer planes, which are made after the router
+    // while the first grid barrier is pending (make_plan: d / 8 <= threads)
+    float xv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
-        if (t < xwn) load_x_word(f, t, v);
-        uint2 pl[kXB];
-        float usum;
-        const float sc = quant_word<kXB>(v, pl, &usum);
-        if (t < xwn) {
-            rx_store(rx, t, v);
-            store_word<kXB>(xq, xwn, t, pl);
-            if ((t & 3) == 0) {
-                xusc[t >> 2] = sc;
-                xusm[t >> 2] = usum;
-            }
-        }
+    for (int i = 0; i < 8; ++i) xv[i] = 0.f;
+    if (tid < xwn) {
+        load_x_word(f, tid, xv);
+        rx_store(rx, tid, xv);
     }
     __syncthreads();
     const unsigned long long base = s_base;
-    // every lane: its x units in registers
-    uint2 xw[UPL][kXB][4];
-    float xsc[UPL], xsm[UPL];
-#pragma unroll
-    for (int i = 0; i < UPL; ++i) {
-        const int u = lane + 32 * i;
-        if (u < d / 32) {
-            load_unit<kXB>(xq, xwn, u, xw[i]);
-            xsc[i] = xusc[u];
-            xsm[i] = xusm[u];
-        } else {
-#pragma unroll
-            for (int pp = 0; pp < kXB; ++pp)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) xw[i][pp][q] = make_uint2(0u, 0u);
-            xsc[i] = 0.f;
-            xsm[i] = 0.f;
-        }
-    }
-    STAMP(13);
+    STAMP(21);
     const bool ok0 = __syncthreads_and(mbar_wait(&bar[0], 0)) != 0;  // CTA-uniform
     STAMP(2);
     if (!ok0 && tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
@@ -303,7 +276,42 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         }
     }
     STAMP(3);
-    grid_arrive_wait(sync, base + G, f.err);
+    grid_arrive(sync);
+    // the experts' x: 16-bit integer planes, unit scales and sums
+    {
+        uint2 pl[kXB];
+        float usum;
+        const float sc = quant_word<kXB>(xv, pl, &usum);
+        if (tid < xwn) {
+            store_word<kXB>(xq, xwn, tid, pl);
+            if ((tid & 3) == 0) {
+                xusc[tid >> 2] = sc;
+                xusm[tid >> 2] = usum;
+            }
+        }
+    }
+    __syncthreads();
+    // every lane: its x units in registers
+    uint2 xw[UPL][kXB][4];
+    float xsc[UPL], xsm[UPL];
+#pragma unroll
+    for (int i = 0; i < UPL; ++i) {
+        const int u = lane + 32 * i;
+        if (u < d / 32) {
+            load_unit<kXB>(xq, xwn, u, xw[i]);
+            xsc[i] = xusc[u];
+            xsm[i] = xusm[u];
+        } else {
+#pragma unroll
+            for (int pp = 0; pp < kXB; ++pp)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) xw[i][pp][q] = make_uint2(0u, 0u);
+            xsc[i] = 0.f;
+            xsm[i] = 0.f;
+        }
+    }
+    STAMP(13);
+    grid_wait(sync, base + G, f.err);
     STAMP(4);
 
     // ---- phase 2: top-k over the whole CTA. Every warp's largest key goes to
@@ -588,6 +596,7 @@ bool make_plan(const qk_fwd *f, Plan *p) {
     // sums) and the per-expert partial outputs
     const int h_bytes = kHB * S * (L.I / 8) * 8 + 2 * S * (L.I / 32) * 4 + S * p->or_max * 4;
     if (S * (L.I / 8) > kHW * kThreads) return false;  // phase 3's h words per thread
+    if (L.d / 8 > kThreads) return false;              // phase 1: one x word per thread
     if ((p->or_max + 32 / (L.I / 32) - 1) / (32 / (L.I / 32)) > kRowSteps) return false;
     off = align128(off + (p->gr_max * L.gu_row > h_bytes ? p->gr_max * L.gu_row : h_bytes));
     p->off_down = off;
