@@ -52,11 +52,15 @@ typedef struct {
     int max_tokens;      /* largest n of one forward call (sizes workspaces) */
     uint64_t pool_bytes; /* HBM expert pool budget in bytes; 0 = room for every
                             expert of every layer (all resident). A streaming
-                            pool must hold at least top_k slots, and one call's
-                            distinct routed experts of a layer must fit in it
-                            at once (the call fails otherwise; the reference
-                            reloads evicted experts one by one instead,
-                            model.c:1341-1349) */
+                            pool must hold at least top_k slots. A multi-token
+                            call whose distinct routed experts of a layer do
+                            not fit runs them in waves of at most a pool each
+                            (filled, then computed; one combine at the end),
+                            with the result of a pool that holds them all, as
+                            the reference reloads evicted experts inside its
+                            expert loop (model.c:1341-1349). Expert-parallel
+                            streaming calls need a rank's experts of a call to
+                            fit at once. */
     int policy;          /* QMOE_POLICY_* for the pool (reference: ADAPTIVE) */
     int prefetch_depth;  /* prefetch_count of streaming.py (2) */
     int device;          /* CUDA device ordinal */
@@ -112,6 +116,9 @@ typedef struct {
     /* prefetched experts evicted before any routing reached them
      * (StreamStats.prefetch_wasted, streaming.py:346-349) */
     uint64_t prefetch_wasted;
+    /* streaming: waves run by calls that routed to more distinct experts of
+     * a layer than the pool has slots (each wave fills at most a pool) */
+    uint64_t expert_waves;
 } qmoe_stats;
 
 typedef struct qmoe_ctx qmoe_ctx;

@@ -79,6 +79,7 @@ struct qmoe_ctx {
     int32_t *idx;
     float *x_pin, *out_pin;
     int32_t *idx_pin;
+    uint8_t *wave_pin;      /* streaming: [E + 1] expert mask of one wave */
     int last_T;
     qmoe_stats stats;
     /* route statistics and prediction (streaming.py:400-435) */
@@ -266,6 +267,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     cudaFree(c->stk_y);
     cudaFreeHost(c->x_pin);
     cudaFreeHost(c->idx_pin);
+    cudaFreeHost(c->wave_pin);
     cudaFreeHost(c->io_pin);
     cudaFreeHost(c->host_store);
     free(c->slot_of_host);
@@ -424,6 +426,7 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaMalloc((void **)&c->stk_y, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->x_pin, (size_t)T * L->d * sizeof(float)));
     CK(cudaMallocHost((void **)&c->idx_pin, (size_t)T * L->k * sizeof(int32_t)));
+    CK(cudaMallocHost((void **)&c->wave_pin, (size_t)L->E + 1));
     if (c->ep_world > 1) {
         /* the experts pass holds the own T tokens and at most T tokens from
          * every rank */
@@ -883,8 +886,14 @@ static int route(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, int pdl, cu
     return kerr(qk_launch_topk(f, st, pdl), "topk", err);
 }
 
-/* streaming mode: route first, make the selected experts resident */
-static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, qmoe_err *err) {
+/* streaming mode: route first, make the selected experts resident. When the
+ * call routes to more distinct experts than the pool has slots, nothing is
+ * filled: *over receives the distinct experts (first-appearance order, the
+ * caller frees it) and *n_over their count, for a pass in waves. */
+static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, int64_t **over,
+                     size_t *n_over, qmoe_err *err) {
+    *over = NULL;
+    *n_over = 0;
     int n = f->T, k = c->L.k;
     if (route(c, layer, f, st, 0, NULL, err)) return -1;
     cudaError_t ce = cudaMemcpyAsync(c->idx_pin, c->idx, (size_t)n * k * sizeof(int32_t),
@@ -920,6 +929,11 @@ static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, qmoe_er
         }
     }
     free(seen);
+    if (nu > (size_t)c->nslots) {
+        *over = uniq;
+        *n_over = nu;
+        return 0;
+    }
     int rc = fill_experts(c, layer, uniq, nu, err);
     if (rc == 0) {
         pthread_mutex_lock(&c->lock);
@@ -928,6 +942,49 @@ static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, qmoe_er
     }
     free(uniq);
     return rc;
+}
+
+/* A streaming call whose distinct experts exceed the pool (the reference
+ * reloads evicted experts inside its expert loop, model.c:1341-1349): rows
+ * grouped once, then the experts in waves of at most the pool's slots, each
+ * wave filled and run through the grouped GEMMs over its own tiles, then one
+ * combine. Each output row is computed by exactly one wave and combined in
+ * the one-pass order, so the result equals a pool that holds them all. */
+static int forward_waves(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, const int64_t *ids,
+                         size_t nu, qmoe_err *err) {
+    if (!c->prefill || f->T < 2) {
+        seterr(err, "qmoe_forward: %zu distinct experts routed, the pool has %d slots (a "
+                    "single-token call needs them at once)", nu, c->nslots);
+        return -1;
+    }
+    const int E = c->L.E, shared = c->nslots + layer;
+    if (kerr(qk_prefill_plan(c->prefill, f, shared, st), "prefill plan", err)) return -1;
+    uint8_t *mask_dev = qk_prefill_wave_mask(c->prefill);
+    for (size_t w0 = 0; w0 < nu; w0 += (size_t)c->nslots) {
+        const size_t nw = nu - w0 < (size_t)c->nslots ? nu - w0 : (size_t)c->nslots;
+        /* the previous wave's GEMMs read slots this wave's fills may evict,
+         * and its mask copy reads wave_pin */
+        cudaError_t ce = cudaStreamSynchronize(st);
+        if (ce != cudaSuccess) {
+            seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
+            return -1;
+        }
+        if (fill_experts(c, layer, ids + w0, nw, err)) return -1;
+        pthread_mutex_lock(&c->lock);
+        for (size_t i = 0; i < nw; i++) qmoe_cache_get(c->cache, ekey(layer, (int)ids[w0 + i]), NULL);
+        pthread_mutex_unlock(&c->lock);
+        memset(c->wave_pin, 0, (size_t)E + 1);
+        c->wave_pin[0] = w0 == 0; /* the shared expert runs with the first wave */
+        for (size_t i = 0; i < nw; i++) c->wave_pin[ids[w0 + i] + 1] = 1;
+        ce = cudaMemcpyAsync(mask_dev, c->wave_pin, (size_t)E + 1, cudaMemcpyHostToDevice, st);
+        if (ce != cudaSuccess) {
+            seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
+            return -1;
+        }
+        if (kerr(qk_prefill_wave(c->prefill, f, shared, st), "prefill wave", err)) return -1;
+        c->stats.expert_waves++;
+    }
+    return kerr(qk_prefill_combine(c->prefill, f, st), "combine", err);
 }
 
 int qmoe_forward_dev(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, float *out,
@@ -974,7 +1031,15 @@ int qmoe_forward_dev(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, 
     }
     c->prof_kernels = 4;
     if (!c->resident_all) {
-        if (stream_in(c, layer, &f, st, err)) return -1;
+        int64_t *over = NULL;
+        size_t n_over = 0;
+        if (stream_in(c, layer, &f, st, &over, &n_over, err)) return -1;
+        if (over) {
+            const int rc = forward_waves(c, layer, &f, st, over, n_over, err);
+            free(over);
+            c->prof_kernels = 6;
+            return rc;
+        }
     } else {
         PEV(0);
         if (route(c, layer, &f, st, !prof, prof ? c->pev[1] : NULL, err)) return -1;

@@ -121,6 +121,20 @@ void qk_prefill_destroy(qk_prefill *p);
  * gate/up GEMM, down GEMM and combine (diagnostics). */
 int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream,
                       void **events);
+/* The same pass in waves, for a call whose distinct experts exceed the pool:
+ * qk_prefill_plan groups and gathers every row once (as qk_launch_prefill);
+ * then per wave the caller fills the wave's experts, writes the wave's
+ * expert mask (qk_prefill_wave_mask: [E + 1] bytes on the device, index 0
+ * the shared expert, e + 1 expert e) and calls qk_prefill_wave, which runs
+ * the two GEMMs over that wave's tiles only (each output row is written by
+ * exactly one wave, at the row the plan gave it); qk_prefill_combine then
+ * combines every row once, in the fixed order of qk_launch_prefill, so the
+ * result is the one-pass result bit for bit. */
+int qk_prefill_plan(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream);
+uint8_t *qk_prefill_wave_mask(qk_prefill *p);
+int qk_prefill_wave(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream);
+int qk_prefill_combine(qk_prefill *p, const qk_fwd *f, void *stream);
+
 /* Routing of a multi-token call on the tensor cores (approximate logits)
  * with an exact re-ranking of each token's candidates: writes f->idx, f->wts
  * and f->sgate, identical to qk_launch_router + qk_launch_topk (f->logits is

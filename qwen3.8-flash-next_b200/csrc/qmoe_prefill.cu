@@ -87,7 +87,7 @@ struct MTile {
     int m0;    // first row in the grouped buffers
     int rows;  // valid rows (<= 128)
     int slot;  // pool slot of the expert
-    int pad;
+    int ex;    // the expert (-1: the shared expert)
 };
 
 struct GemmArgs {
@@ -774,12 +774,12 @@ struct PlanOut {
     int *n_tiles, *n_stiles, *n_rows;
 };
 
-QK_DEV void plan_group(int rows, int slot, int r0, const PlanOut &o, int t0, int u0) {
+QK_DEV void plan_group(int rows, int slot, int ex, int r0, const PlanOut &o, int t0, int u0) {
     const bool small = rows <= o.small_max;
     const int mt = small ? 0 : (rows + BM - 1) / BM;
     const int st = small ? (rows + NS - 1) / NS : 0;
-    for (int i = 0; i < mt; ++i) o.tiles[t0 + i] = MTile{r0 + BM * i, min(BM, rows - BM * i), slot, 0};
-    for (int i = 0; i < st; ++i) o.stiles[u0 + i] = MTile{r0 + NS * i, min(NS, rows - NS * i), slot, 0};
+    for (int i = 0; i < mt; ++i) o.tiles[t0 + i] = MTile{r0 + BM * i, min(BM, rows - BM * i), slot, ex};
+    for (int i = 0; i < st; ++i) o.stiles[u0 + i] = MTile{r0 + NS * i, min(NS, rows - NS * i), slot, ex};
 }
 
 // Inclusive block scans (1024 threads) of the rows and the two tile counts
@@ -823,7 +823,7 @@ __global__ void __launch_bounds__(1024) k_plan(const int *counts, int E, int nsh
     plan_scan(g, rows, o, s_a, s_b, s_c, &r0, &t0, &u0);
     if (g >= 1 && g <= E) row0[g - 1] = r0;
     const int slot = g == 0 ? shared_slot : (g <= E ? slot_of[g - 1] : -1);
-    plan_group(rows, slot, r0, o, t0, u0);
+    plan_group(rows, slot, g - 1, r0, o, t0, u0);
 }
 
 // Small calls (at most kPlanSmall slots): counting, planning and placing in
@@ -848,7 +848,7 @@ __global__ void __launch_bounds__(1024) k_plan_small(const int32_t *idx, int nk,
     plan_scan(g, rows, o, s_a, s_b, s_c, &r0, &t0, &u0);
     s_row0[g] = r0;
     const int slot = g == 0 ? shared_slot : (g <= E ? slot_of[g - 1] : -1);
-    plan_group(rows, slot, r0, o, t0, u0);
+    plan_group(rows, slot, g - 1, r0, o, t0, u0);
     s_cnt[g] = 0;  // now the placement cursors
     __syncthreads();
     for (int a = g; a < nk; a += 1024) {
@@ -881,6 +881,38 @@ __global__ void k_place(const int32_t *idx, int nk, int k, const int *row0, int 
             inv[a] = pos;
             perm_tok[pos] = a / k;
         }
+    }
+}
+
+// The tiles of one wave of a call whose experts exceed the pool (the
+// experts of wave[ex + 1] != 0, the shared expert at wave[0]): copies of the
+// plan's tiles with the slots the experts hold now. The order of the copies
+// varies from call to call, the results do not (every tile is independent).
+__global__ void __launch_bounds__(1024) k_wave_tiles(const MTile *tiles, const int *n_tiles,
+                                                     const MTile *stiles, const int *n_stiles,
+                                                     const uint8_t *wave, const int32_t *slot_of,
+                                                     MTile *wt, int *n_wt, MTile *wst, int *n_wst) {
+    __shared__ int c0, c1;
+    if (threadIdx.x == 0) c0 = c1 = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < *n_tiles; i += blockDim.x) {
+        MTile m = tiles[i];
+        if (wave[m.ex + 1]) {
+            if (m.ex >= 0) m.slot = slot_of[m.ex];
+            wt[atomicAdd(&c0, 1)] = m;
+        }
+    }
+    for (int i = threadIdx.x; i < *n_stiles; i += blockDim.x) {
+        MTile m = stiles[i];
+        if (wave[m.ex + 1]) {
+            if (m.ex >= 0) m.slot = slot_of[m.ex];
+            wst[atomicAdd(&c1, 1)] = m;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *n_wt = c0;
+        *n_wst = c1;
     }
 }
 
@@ -1118,7 +1150,7 @@ __global__ void k_route_split(const void *x, int x_bf16, int d, int T, int Tpad,
             m.m0 = BM * i;
             m.rows = min(BM, T - BM * i);
             m.slot = 0;
-            m.pad = 0;
+            m.ex = 0;
             tiles[i] = m;
         }
         if (threadIdx.x == 0) *n_mtiles = nm;
@@ -1399,6 +1431,13 @@ struct qk_prefill {
     int small_max;                  // groups of at most this many rows use k_gemm_sw
     int *counts, *cursor, *row0, *inv, *perm_tok, *n_mtiles, *n_stiles, *n_rows;
     MTile *tiles, *stiles;          // BM-row tiles (k_gemm), NS-row tiles (k_gemm_sw)
+    // waves of a call whose experts exceed the pool: the wave's tiles, the
+    // expert mask ([E + 1], shared expert first) and the plan's small/large
+    // choice of the call
+    MTile *wtiles, *wstiles;
+    int *n_wtiles;                  // [2]: tiles, small tiles
+    uint8_t *wave;
+    int wave_all_small;
     __half *xp, *H;
     float *Y;
     CUtensorMap tmX, tmH, tmQgu, tmSgu, tmQdn, tmSdn;
@@ -1449,6 +1488,10 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->ep_recv_x);
     cudaFree(p->ep_ret);
     cudaFree(p->ep_back);
+    cudaFree(p->wtiles);
+    cudaFree(p->wstiles);
+    cudaFree(p->n_wtiles);
+    cudaFree(p->wave);
     delete p;
 }
 
@@ -1490,6 +1533,10 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     if (e == cudaSuccess) e = cudaMalloc(&p->tiles, sizeof(MTile) * p->tiles_max);
     // groups of at most kSmallMax rows: at most kSmallMax / NS tiles each
     if (e == cudaSuccess) e = cudaMalloc(&p->stiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
+    if (e == cudaSuccess) e = cudaMalloc(&p->wtiles, sizeof(MTile) * p->tiles_max);
+    if (e == cudaSuccess) e = cudaMalloc(&p->wstiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
+    if (e == cudaSuccess) e = cudaMalloc(&p->n_wtiles, 2 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&p->wave, L->E + 1);
     if (e == cudaSuccess) e = cudaMalloc(&p->xp, 2 * R * L->d * sizeof(__half));  // hi, lo planes
     if (e == cudaSuccess) e = cudaMalloc(&p->H, 2 * R * L->I * sizeof(__half));  // hi, lo planes
     if (e == cudaSuccess) e = cudaMalloc(&p->Y, R * L->d * sizeof(float));
@@ -1566,9 +1613,11 @@ namespace {
 // Leaves the down outputs in p->Y (shared rows first) and the row of each
 // (token, slot) in p->inv. events: NULL or 3 events (after grouping+gather,
 // gate/up, down).
+// phases: 1 = grouping and gather, 2 = the two GEMMs (both by default).
+// wave != 0: the GEMMs take the wave tile lists (p->wtiles, p->wstiles).
 cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32_t *idx, int k,
                     int nsh, int routed_max, const int32_t *slot_of, int shared_slot_index,
-                    int *err, cudaStream_t st, void **events) {
+                    int *err, cudaStream_t st, void **events, int phases = 3, int wave = 0) {
     const qk_layout &L = p->L;
     const int E = L.E;
     const int nk = T * k;
@@ -1592,7 +1641,9 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     po.n_stiles = p->n_stiles;
     po.n_rows = p->n_rows;
     cudaError_t e = cudaSuccess;
-    if (nk <= kPlanSmall) {
+    if (!(phases & 1)) {
+        // GEMMs only (a wave of an earlier plan)
+    } else if (nk <= kPlanSmall) {
         k_plan_small<<<1, 1024, 0, st>>>(idx, nk, k, E, nsh, slot_of, shared_slot_index, po, p->inv,
                                          p->perm_tok);
     } else {
@@ -1604,13 +1655,16 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         k_place<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, k, p->row0, p->cursor, p->inv,
                                                  p->perm_tok);
     }
-    if (rows > 0)
+    if ((phases & 1) && rows > 0)
         k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->n_rows,
                                                          p->perm_tok, p->xp,
                                                          static_cast<size_t>(p->rows_max) * L.d);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     mark(0);
+    if (!(phases & 2)) return cudaSuccess;
+    MTile *tl = wave ? p->wtiles : p->tiles, *stl = wave ? p->wstiles : p->stiles;
+    int *ntl = wave ? p->n_wtiles : p->n_mtiles, *nstl = wave ? p->n_wtiles + 1 : p->n_stiles;
 
     auto launch = [&](const void *fn, int smem, const CUtensorMap *a, const CUtensorMap *q,
                       const CUtensorMap *sc, GemmArgs *ga, int threads) {
@@ -1641,28 +1695,28 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     dn.outf = p->Y;
     if (all_small) {
         gu.NT = L.I / 128;
-        gu.tiles = p->stiles;
-        gu.n_mtiles = p->n_stiles;
+        gu.tiles = stl;
+        gu.n_mtiles = nstl;
         e = lo ? launch(fn(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs, &p->tmQgu, &p->tmSgu, &gu, kThreadsSw)
                : launch(fn(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs, &p->tmQgu, &p->tmSgu, &gu, kThreadsSw);
         if (e != cudaSuccess) return e;
         mark(1);
         dn.NT = L.d / 256;
-        dn.tiles = p->stiles;
-        dn.n_mtiles = p->n_stiles;
+        dn.tiles = stl;
+        dn.n_mtiles = nstl;
         e = launch(fn(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs, &p->tmQdn, &p->tmSdn, &dn, kThreadsSw);
         if (e != cudaSuccess) return e;
     } else {
         gu.NT = L.I / 128;
-        gu.tiles = p->tiles;
-        gu.n_mtiles = p->n_mtiles;
+        gu.tiles = tl;
+        gu.n_mtiles = ntl;
         e = lo ? launch(fn(&k_gemm<3>), Cfg<3>::Smem, &p->tmX, &p->tmQgu, &p->tmSgu, &gu, kThreads)
                : launch(fn(&k_gemm<0>), Cfg<0>::Smem, &p->tmX, &p->tmQgu, &p->tmSgu, &gu, kThreads);
         if (e != cudaSuccess) return e;
         mark(1);
         dn.NT = L.d / 256;
-        dn.tiles = p->tiles;
-        dn.n_mtiles = p->n_mtiles;
+        dn.tiles = tl;
+        dn.n_mtiles = ntl;
         e = launch(fn(&k_gemm<1>), Cfg<1>::Smem, &p->tmH, &p->tmQdn, &p->tmSdn, &dn, kThreads);
         if (e != cudaSuccess) return e;
     }
@@ -1684,6 +1738,33 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     if (e != cudaSuccess) return e;
     k_combine<<<T, 256, 0, st>>>(p->Y, p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
     if (events) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[3]), st, cudaEventRecordExternal);
+    return cudaGetLastError();
+}
+
+extern "C" uint8_t *qk_prefill_wave_mask(qk_prefill *p) { return p->wave; }
+
+extern "C" int qk_prefill_plan(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream) {
+    const int T = f->T;
+    if (T > p->max_tokens) return cudaErrorInvalidValue;
+    return grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, p->L.k, T, T, f->slot_of,
+                   shared_slot_index, f->err, static_cast<cudaStream_t>(stream), nullptr, 1);
+}
+
+extern "C" int qk_prefill_wave(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream) {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    k_wave_tiles<<<1, 1024, 0, st>>>(p->tiles, p->n_mtiles, p->stiles, p->n_stiles, p->wave,
+                                     f->slot_of, p->wtiles, p->n_wtiles, p->wstiles, p->n_wtiles + 1);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int T = f->T;
+    return grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, p->L.k, T, T, f->slot_of,
+                   shared_slot_index, f->err, st, nullptr, 2, 1);
+}
+
+extern "C" int qk_prefill_combine(qk_prefill *p, const qk_fwd *f, void *stream) {
+    const int T = f->T;
+    k_combine<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(p->Y, p->Y, p->inv, f->wts, f->sgate,
+                                                               p->L.k, p->L.d, f->out);
     return cudaGetLastError();
 }
 

@@ -64,7 +64,7 @@ class Stats(C.Structure):
         ("decode_calls", C.c_uint64), ("forward_seconds", C.c_double),
         ("prefetch_issued", C.c_uint64), ("prefetch_hits", C.c_uint64),
         ("routed_lookups", C.c_uint64), ("routed_hits", C.c_uint64),
-        ("prefetch_wasted", C.c_uint64),
+        ("prefetch_wasted", C.c_uint64), ("expert_waves", C.c_uint64),
     ]
 
     def as_dict(self):

@@ -19,7 +19,7 @@ int main(void) {
     F(qmoe_cache_stats, hot);
     S(qmoe_stats);
     F(qmoe_stats, expert_wait_seconds); F(qmoe_stats, forward_seconds); F(qmoe_stats, routed_hits);
-    F(qmoe_stats, prefetch_wasted);
+    F(qmoe_stats, prefetch_wasted); F(qmoe_stats, expert_waves);
     S(qmoe_token_args);
     F(qmoe_token_args, x); F(qmoe_token_args, x_dtype); F(qmoe_token_args, out);
     F(qmoe_token_args, shared_slot);

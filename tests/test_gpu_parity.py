@@ -279,3 +279,30 @@ def test_streaming_pool_equals_resident(cfg1_layer, cfg1_ctx):
         ctx.experts_load(0, list(range(300, 365)))  # more than the pool holds
     assert qmoe.lib().qmoe_expert_unpin(ctx.h, 0, e) == 1
     ctx.close()
+
+
+def test_pool_smaller_than_a_call_runs_in_waves(cfg1_layer, cfg1_ctx):
+    """A streaming pool of 16 slots under 64 tokens that route to a few hundred
+    distinct experts: the call runs in waves of at most 16 experts (fill, then
+    the grouped GEMMs over that wave's tiles) and one combine, and its output
+    equals the all-resident pool bit for bit (each row computed by one wave,
+    combined in the one-pass order). The reference reloads evicted experts
+    inside its expert loop instead of failing (c/src/model.c:1341-1349)."""
+    import qmoe
+    s, seed = cfg1_layer
+    slot = qmoe.lib().qmoe_slot_bytes(qmoe.make_config(2048, 512, 10, 512))
+    ctx = qmoe.Context(qmoe.make_config(2048, 512, 10, 512, max_tokens=64,
+                                        pool_bytes=16 * slot, policy=qmoe.QMOE_POLICY_LRU))
+    ctx.upload(0, s)
+    x = qmoe.synth_tokens(seed, 17, 64, 2048)
+    for n in (64, 24):
+        a = ctx.forward(0, x[:n])
+        ia = ctx.routing(n)[0]
+        b = cfg1_ctx.forward(0, x[:n])
+        ib = cfg1_ctx.routing(n)[0]
+        assert np.array_equal(ia, ib), n
+        assert np.array_equal(a, b), n
+    st = ctx.stats()
+    assert st["expert_waves"] >= 2 * 16  # both calls ran in many waves
+    assert ctx.cache_stats()["size"] <= 16
+    ctx.close()
