@@ -650,20 +650,19 @@ def measure_stream(rank=0, world=1, local=0, layers=STREAM_LAYERS):
         ctx.sync()
         ms = e0.elapsed_time(e1)
         dc = [b - a for a, b in zip(c0, counters())]
-        rate = dc[1] / dc[2] / 1e9 if dc[2] > 0 else 0.0
         if world > 1:
             mx = torch.tensor([ms], device="cuda")
             dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            sm = torch.tensor(dc + [rate], device="cuda", dtype=torch.float64)
+            sm = torch.tensor(dc, device="cuda", dtype=torch.float64)
             dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-            ms, dc, rate = float(mx.item()), [float(v) for v in sm[:-1]], float(sm[-1]) / world
+            ms, dc = float(mx.item()), [float(v) for v in sm]
         d = dict(zip(keys, dc))
         return {"tokens_per_s": n_tokens / (ms / 1e3), "ms": ms,
                 "hit_rate": d["routed_hits"] / max(1.0, d["routed_lookups"]),
                 "routed_experts": int(d["routed_lookups"]), "expert_fills": int(d["expert_loads"]),
                 "h2d_bytes": int(d["expert_bytes"]),
-                "h2d_gbs_while_filling": rate if rate > 0 else None,
                 "h2d_gbs_over_leg": d["expert_bytes"] / (ms / 1e3) / 1e9,
+                "host_blocked_s_in_fills": d["expert_wait_seconds"],
                 "prefetch_issued": int(d["prefetch_issued"]), "prefetch_hits": int(d["prefetch_hits"]),
                 "prefetch_wasted": int(d["prefetch_wasted"])}
 
@@ -697,8 +696,11 @@ def measure_stream(rank=0, world=1, local=0, layers=STREAM_LAYERS):
             "layers": layers, "pool_bytes_per_gpu": pool, "host_store_bytes": layers * store_all,
             "host_mem_available": avail, "decode_batch1": dec,
             "prefill": {**pre, "tokens": STREAM_PREFILL}, "weights_generated_s": synth_s,
-            "timing": "CUDA events on the stream, max over ranks; the host's waits for fills are inside",
-            "note": "fills and prefetches wait for their copies on the host (no overlap with compute)"}
+            "timing": "CUDA events on the stream, max over ranks; the host's wait for each layer's "
+                      "routing is inside",
+            "note": "fills and prefetches are queued on a copy stream behind the work they may "
+                    "evict from; each layer's kernels wait for them on the device, the host only "
+                    "for the layer's routing"}
 
 
 def run_stack_eager(layers):

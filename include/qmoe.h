@@ -301,12 +301,16 @@ int qmoe_stats_get(qmoe_ctx *ctx, qmoe_stats *out);
 
 /* ---- prefetch hooks (streaming.py:271-284, :400-435) ---- */
 
-/* Fills the listed experts that are not in the pool, on the copy stream,
- * once the context's own stream is idle (a fill may evict a slot its
- * kernels read; a caller that runs forwards on a stream of its own
- * synchronises that stream first), and waits for the copies. Returns the
- * number filled (ExpertStore.request(prefetch=True)); 0 on a resident
- * context. */
+/* Queues fills of the listed experts that are not in the pool on the copy
+ * stream and returns at once (ExpertStore.request(prefetch=True) futures):
+ * the copies wait, on the device, for the work already queued on the
+ * context's own stream (a fill may evict a slot its kernels read; a caller
+ * that runs forwards on a stream of its own synchronises that stream first,
+ * or prefetches through qmoe_forward_stack, which orders them after its
+ * stream), and the next forward's kernels wait for them. Prefetched experts
+ * neither routed to nor evicted yet are capped at min(pool slots,
+ * max(2, prefetch_depth x layers)) (ExpertStore._max_speculative,
+ * streaming.py:115). Returns the number queued; 0 on a resident context. */
 int qmoe_prefetch(qmoe_ctx *ctx, int layer, const int64_t *ids, size_t n);
 /* Records one step's routing, every token's k experts (ExpertStore.record_route,
  * streaming.py:400-413, called with idx.reshape(-1) at model.py:458): the
@@ -314,10 +318,10 @@ int qmoe_prefetch(qmoe_ctx *ctx, int layer, const int64_t *ids, size_t n);
  * hot marks it sets. */
 void qmoe_record_route(qmoe_ctx *ctx, int layer, const int32_t *experts,
                        size_t n);
-/* Predicts and fills prefetches for this layer and the next from the route
- * statistics (ExpertStore.prefetch_predictions, streaming.py:415-435, called
- * with the step's distinct experts in ascending order at model.py:459).
- * Returns the number filled. */
+/* Predicts and queues prefetches (as qmoe_prefetch) for this layer and the
+ * next from the route statistics (ExpertStore.prefetch_predictions,
+ * streaming.py:415-435, called with the step's distinct experts in ascending
+ * order at model.py:459). Returns the number queued. */
 int qmoe_prefetch_predictions(qmoe_ctx *ctx, int layer,
                               const int32_t *selected, size_t n);
 

@@ -48,6 +48,9 @@ struct qmoe_ctx {
     int num_sms;
     cudaStream_t stream, copy_stream;
     cudaEvent_t copy_done;
+    cudaEvent_t compute_mark; /* streaming: recorded on the compute stream before a fill */
+    int pf_outstanding;       /* prefetched experts neither routed to nor evicted yet */
+    int max_speculative;      /* their cap (ExpertStore._max_speculative) */
     /* device error word and output share one allocation (err at 0, out at
        256) so a host-pointer forward reads both back with one copy; the
        pinned mirror has the same layout */
@@ -281,6 +284,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     if (c->ep_comm) nccl_api()->comm_destroy(c->ep_comm);
     cudaFreeHost(c->ep_recv_pin);
     if (c->copy_done) cudaEventDestroy(c->copy_done);
+    if (c->compute_mark) cudaEventDestroy(c->compute_mark);
     for (int i = 0; i < 8; i++)
         if (c->pev[i]) cudaEventDestroy(c->pev[i]);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -349,6 +353,7 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&c->copy_done, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&c->compute_mark, cudaEventDisableTiming));
     {
         const size_t io = 256 + (size_t)T * L->d * sizeof(float);
         CK(cudaMalloc((void **)&c->io_dev, io));
@@ -382,6 +387,14 @@ qmoe_ctx *qmoe_create(const qmoe_config *cfg, qmoe_err *err) {
         }
         c->nslots = (int)want;
         c->resident_all = want == local;
+        /* prefetches in flight: min(cache slots, max(2 workers, prefetch_count
+         * x layers)) as ExpertStore sizes it (streaming.py:115), with the
+         * copy stream as the one I/O worker */
+        {
+            const long spec = (long)(cfg->prefetch_depth > 0 ? cfg->prefetch_depth : 0) * Lz;
+            c->max_speculative = (int)(spec > 2 ? (spec < c->nslots ? spec : c->nslots)
+                                               : (2 < c->nslots ? 2 : c->nslots));
+        }
         CK(cudaMalloc((void **)&c->pool, ((size_t)c->nslots + Lz) * L->slot_bytes));
         for (int l = 0; l < Lz; l++)
             c->layers[l].shared_slot = c->pool + ((size_t)c->nslots + l) * L->slot_bytes;
@@ -487,6 +500,7 @@ static int claim_slot(qmoe_ctx *c, int layer, int e, int pin) {
             c->slot_owner[s] = NO_OWNER;
             if (c->pf_mark[m]) { /* prefetched, never routed to */
                 c->pf_mark[m] = 0;
+                c->pf_outstanding--;
                 c->stats.prefetch_wasted++;
             }
         }
@@ -507,13 +521,20 @@ static int claim_slot(qmoe_ctx *c, int layer, int e, int pin) {
     return slot;
 }
 
-/* Synchronous fill of the uncached experts in ids (experts_load semantics:
- * present entries are skipped without touching their stats). While the call
- * runs, every listed expert is pinned so that filling one cannot evict
- * another the same call needs; pins the call added are dropped at the end.
- * The caller makes sure no queued kernel still reads a slot that may be
- * evicted (the compute stream is idle). */
-static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qmoe_err *err) {
+/* Fill of the uncached experts in ids (experts_load semantics: present
+ * entries are skipped without touching their stats). While the call runs,
+ * every listed expert is pinned so that filling one cannot evict another the
+ * same call needs; pins the call added are dropped at the end.
+ *   st == NULL  synchronous: the host waits for the copies; the caller makes
+ *               sure no queued kernel still reads a slot that may be evicted
+ *               (the compute stream is idle).
+ *   st != NULL  asynchronous: the copy stream first waits for everything
+ *               already queued on st (a victim slot may still be read there),
+ *               then copies; nothing waits on the host. The copies complete
+ *               before whatever the caller queues on st after a later
+ *               mark_fills_ready(c, st). */
+static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, cudaStream_t st,
+                        qmoe_err *err) {
     const qk_layout *L = &c->L;
     double t0 = now_s();
     int loaded = 0, rc = 0;
@@ -526,6 +547,15 @@ static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qm
     if (!ours) {
         seterr(err, "qmoe_experts_load: out of host memory");
         return -1;
+    }
+    if (st) {
+        cudaError_t ce = cudaEventRecord(c->compute_mark, st);
+        if (ce == cudaSuccess) ce = cudaStreamWaitEvent(c->copy_stream, c->compute_mark, 0);
+        if (ce != cudaSuccess) {
+            free(ours);
+            seterr(err, "qmoe_experts_load: %s", cudaGetErrorString(ce));
+            return -1;
+        }
     }
     pthread_mutex_lock(&c->lock);
     for (size_t i = 0; i < n; i++) {
@@ -571,11 +601,13 @@ static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qm
     for (size_t i = 0; i < n; i++)
         if (ours[i]) qmoe_cache_unpin(c->cache, ekey(layer, (int)ids[i]));
     free(ours);
-    cudaError_t ce = cudaMemcpyAsync(c->slot_of_dev + (size_t)layer * L->E,
-                                     c->slot_of_host + (size_t)layer * L->E,
-                                     (size_t)L->E * sizeof(int32_t), cudaMemcpyHostToDevice,
-                                     c->copy_stream);
-    if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->copy_stream);
+    /* the layer's slot table (from pageable memory: staged by the call, so
+     * the host may change it again at once) */
+    cudaError_t ce = cudaSuccess;
+    if (loaded || !st)
+        ce = cudaMemcpyAsync(c->slot_of_dev + (size_t)layer * L->E, c->slot_of_host + (size_t)layer * L->E,
+                             (size_t)L->E * sizeof(int32_t), cudaMemcpyHostToDevice, c->copy_stream);
+    if (ce == cudaSuccess && !st) ce = cudaStreamSynchronize(c->copy_stream);
     pthread_mutex_unlock(&c->lock);
     if (rc) return rc;
     if (ce != cudaSuccess) {
@@ -585,6 +617,18 @@ static int fill_experts(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qm
     c->stats.expert_loads += (uint64_t)loaded;
     c->stats.expert_bytes += (uint64_t)loaded * L->slot_bytes;
     c->stats.expert_wait_seconds += now_s() - t0;
+    return 0;
+}
+
+/* Whatever the caller queues on st after this waits for every copy queued
+ * so far on the copy stream (the layer's fills and earlier prefetches). */
+static int mark_fills_ready(qmoe_ctx *c, cudaStream_t st, qmoe_err *err) {
+    cudaError_t ce = cudaEventRecord(c->copy_done, c->copy_stream);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(st, c->copy_done, 0);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
+        return -1;
+    }
     return 0;
 }
 
@@ -925,6 +969,7 @@ static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, int64_t
             if (*pm) {
                 if (resident) c->stats.prefetch_hits++;
                 *pm = 0;
+                c->pf_outstanding--;
             }
         }
     }
@@ -934,7 +979,11 @@ static int stream_in(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, int64_t
         *n_over = nu;
         return 0;
     }
-    int rc = fill_experts(c, layer, uniq, nu, err);
+    /* the misses are copied behind the routing on the copy stream; the
+     * layer's kernels, queued next on st, wait for them (and for any
+     * prefetch still in flight) */
+    int rc = fill_experts(c, layer, uniq, nu, st, err);
+    if (rc == 0) rc = mark_fills_ready(c, st, err);
     if (rc == 0) {
         pthread_mutex_lock(&c->lock);
         for (size_t i = 0; i < nu; i++) qmoe_cache_get(c->cache, ekey(layer, (int)uniq[i]), NULL);
@@ -969,7 +1018,7 @@ static int forward_waves(qmoe_ctx *c, int layer, qk_fwd *f, cudaStream_t st, con
             seterr(err, "qmoe_forward: %s", cudaGetErrorString(ce));
             return -1;
         }
-        if (fill_experts(c, layer, ids + w0, nw, err)) return -1;
+        if (fill_experts(c, layer, ids + w0, nw, NULL, err)) return -1;
         pthread_mutex_lock(&c->lock);
         for (size_t i = 0; i < nw; i++) qmoe_cache_get(c->cache, ekey(layer, (int)ids[w0 + i]), NULL);
         pthread_mutex_unlock(&c->lock);
@@ -1416,7 +1465,7 @@ int qmoe_experts_load(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, qmoe
         seterr(err, "qmoe_experts_load: %s", cudaGetErrorString(ce));
         return -1;
     }
-    return fill_experts(c, layer, ids, n, err);
+    return fill_experts(c, layer, ids, n, NULL, err);
 }
 
 int qmoe_expert_pin(qmoe_ctx *c, int layer, int e) {
@@ -1443,24 +1492,33 @@ int qmoe_stats_get(qmoe_ctx *c, qmoe_stats *out) {
 
 /* ------------------------------------------------------ prefetch hooks */
 
-int qmoe_prefetch(qmoe_ctx *c, int layer, const int64_t *ids, size_t n) {
+/* Prefetch fills ordered after the work queued on st (see qmoe_prefetch). */
+static int prefetch_on(qmoe_ctx *c, int layer, const int64_t *ids, size_t n, cudaStream_t st) {
     if (!c || layer < 0 || layer >= c->cfg.num_layers || c->resident_all || (n && !ids)) return 0;
     qmoe_err e;
     int queued = 0;
-    /* a fill may evict a slot that queued kernels still read */
-    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return 0;
     for (size_t i = 0; i < n; i++) {
         int ex = (int)ids[i];
         if (ex < c->ep_lo || ex >= c->ep_hi) continue; /* not this rank's */
         if (qmoe_cache_peek(c->cache, ekey(layer, ex), NULL)) continue;
+        /* speculative fills in flight are capped (streaming.py:115, :235-241) */
+        if (c->pf_outstanding >= c->max_speculative) break;
         int64_t one = ex;
-        if (fill_experts(c, layer, &one, 1, &e) == 0) {
+        /* asynchronous: the copy waits, on the device, for the kernels
+         * already queued on the compute stream (a victim slot may still be
+         * read there) and never blocks the host */
+        if (fill_experts(c, layer, &one, 1, st, &e) == 0) {
             queued++;
             c->pf_mark[(size_t)layer * c->L.E + ex] = 1;
+            c->pf_outstanding++;
         }
     }
     c->stats.prefetch_issued += (uint64_t)queued;
     return queued;
+}
+
+int qmoe_prefetch(qmoe_ctx *c, int layer, const int64_t *ids, size_t n) {
+    return c ? prefetch_on(c, layer, ids, n, c->stream) : 0;
 }
 
 void qmoe_record_route(qmoe_ctx *c, int layer, const int32_t *experts, size_t n) {
@@ -1470,7 +1528,8 @@ void qmoe_record_route(qmoe_ctx *c, int layer, const int32_t *experts, size_t n)
     pthread_mutex_unlock(&c->lock);
 }
 
-int qmoe_prefetch_predictions(qmoe_ctx *c, int layer, const int32_t *selected, size_t n) {
+static int prefetch_predictions_on(qmoe_ctx *c, int layer, const int32_t *selected, size_t n,
+                                   cudaStream_t st) {
     if (!c || layer < 0 || layer >= c->cfg.num_layers || c->cfg.prefetch_depth <= 0) return 0;
     const int P = c->cfg.prefetch_depth < 64 ? c->cfg.prefetch_depth : 64;
     int64_t pick[64], next[64];
@@ -1479,9 +1538,13 @@ int qmoe_prefetch_predictions(qmoe_ctx *c, int layer, const int32_t *selected, s
     int rc = qmoe_predictor_predict(c->pred, layer, selected, n, P, pick, &npick, next, &nnext);
     pthread_mutex_unlock(&c->lock);
     if (rc) return 0;
-    int q = qmoe_prefetch(c, layer, pick, (size_t)npick);
-    if (nnext) q += qmoe_prefetch(c, layer + 1, next, (size_t)nnext);
+    int q = prefetch_on(c, layer, pick, (size_t)npick, st);
+    if (nnext) q += prefetch_on(c, layer + 1, next, (size_t)nnext, st);
     return q;
+}
+
+int qmoe_prefetch_predictions(qmoe_ctx *c, int layer, const int32_t *selected, size_t n) {
+    return c ? prefetch_predictions_on(c, layer, selected, n, c->stream) : 0;
 }
 
 const qmoe_predictor *qmoe_ctx_predictor(const qmoe_ctx *c) { return c ? c->pred : NULL; }
@@ -1650,10 +1713,12 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
             if (*pm) {
                 if (resident) c->stats.prefetch_hits++;
                 *pm = 0;
+                c->pf_outstanding--;
             }
         }
         free(seen);
-        int rc = fill_experts(c, layer, uniq, nu, err);
+        int rc = fill_experts(c, layer, uniq, nu, st, err);
+        if (rc == 0) rc = mark_fills_ready(c, st, err);
         if (rc == 0) {
             pthread_mutex_lock(&c->lock);
             for (size_t i = 0; i < nu; i++) qmoe_cache_get(c->cache, ekey(layer, (int)uniq[i]), NULL);
@@ -1712,21 +1777,24 @@ int qmoe_forward_stack(qmoe_ctx *c, int l0, int l1, float *h, int n, float eps, 
              * expert-parallel context), as model.py:458-459 calls
              * record_route and prefetch_predictions */
             const size_t nk = (size_t)n * c->L.k;
-            cudaError_t ce = cudaSuccess;
-            if (c->ep_world > 1)
-                ce = cudaMemcpyAsync(c->idx_pin, c->idx, nk * sizeof(int32_t), cudaMemcpyDeviceToHost, st);
-            /* (and a prefetch may evict a slot this layer's kernels still read) */
-            if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
-            if (ce != cudaSuccess) {
-                seterr(err, "qmoe_forward_stack: layer %d failed on the device", l);
-                return -1;
+            if (c->ep_world > 1) {
+                cudaError_t ce = cudaMemcpyAsync(c->idx_pin, c->idx, nk * sizeof(int32_t),
+                                                 cudaMemcpyDeviceToHost, st);
+                if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+                if (ce != cudaSuccess) {
+                    seterr(err, "qmoe_forward_stack: layer %d failed on the device", l);
+                    return -1;
+                }
             }
+            /* (single GPU: idx_pin already holds the layer's routing, read
+             * before its fills; no wait for the layer's kernels here, since a
+             * prefetch's copies wait for them on the device) */
             /* record every assignment; predict from the distinct experts in
              * ascending order (np.unique at model.py:432) */
             pthread_mutex_lock(&c->lock);
             const int ns = qmoe_predictor_record(c->pred, c->cache, l, c->idx_pin, nk, c->sel_buf);
             pthread_mutex_unlock(&c->lock);
-            if (ns > 0) qmoe_prefetch_predictions(c, l, c->sel_buf, (size_t)ns);
+            if (ns > 0) prefetch_predictions_on(c, l, c->sel_buf, (size_t)ns, st);
         }
     }
     if (l1 > l0 && kerr(qk_launch_residual_norm(h, c->stk_y, NULL, n, d, eps, st), "residual_norm", err))
