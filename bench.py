@@ -61,8 +61,9 @@ UNIT = "tokens/s"
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
 # one ncu --set full capture of the kernel on this workload
-# (`ncu ... -k regex:k_decode_fused -s 8 -c 1 python bench.py --eager-tokens 20`)
-NCU_TRAFFIC = {"decode_fused": 21659136}
+# (`ncu --set full --clock-control none -k regex:k_decode_fused -s 8 -c 1
+#  python bench.py --eager-tokens 20`)
+NCU_TRAFFIC = {"decode_fused": 21658368}
 
 
 def peaks():
