@@ -21,6 +21,9 @@ call. A step is those 1000 sequential calls. Synthetic weights and tokens
   prefill    configs[2] beside it: one 4096-token call on a Zipf(1.1)-biased
              layer (graph replays, CUDA events), its per-kernel split, and
              the grouped GEMMs' algorithmic FLOP rate against bf16_tflops.
+  hyper_connection  the config-1 layer inside its hyper connection (4
+             residual streams, low-rank 64 q4 mixers): qmoe_forward_hc per
+             token, graph replays, CUDA events.
   stack      configs[3]: the 76-layer MoE-only stack (RMSNorm + MoE +
              residual) at batch 64, one CUDA graph per step, expert-parallel
              over the torchrun ranks; HBM roofline of the step's bytes.
@@ -379,6 +382,94 @@ def measure_prefill(ctx, layer_index, rank, reps=5, warmup=3):
                      "peak_source": src, "note": "algorithmic FLOPs of the two grouped GEMMs "
                      "over their event-timed durations; the down GEMM issues two fp16 MMAs "
                      "(h as a hi/lo pair) per algorithmic one"}}
+
+
+HC_N, HC_LR, HC_SEED = 4, 64, 20261213
+
+
+def measure_hc(ctx, rank, reps=5, warmup=3):
+    """The config-1 layer inside its hyper connection (hc 4 residual streams,
+    low-rank 64 q4 mixers), decode at batch 1: TOKENS sequential
+    qmoe_forward_hc calls (gated_residual, the MoE block, the inject-add) on
+    h [TOKENS, hc*d] fp32, captured as one CUDA graph and replayed. The first
+    replay's rows are the parity sample (each row depends only on its own
+    input); later replays keep updating h in place."""
+    import torch
+
+    import qmoe
+    H = qmoe.SynthHC(D, HC_N, HC_LR, HC_SEED)
+    ctx.upload_hc(0, H)
+    h0 = np.ascontiguousarray(np.concatenate(
+        [qmoe.synth_tokens(SEED, 40 + rank * HC_N + j, TOKENS, D) for j in range(HC_N)], axis=1))
+    h = torch.from_numpy(h0).cuda()
+    st = torch.cuda.Stream()
+    cs = st.cuda_stream
+    row = HC_N * D * 4
+    torch.cuda.synchronize()
+    for t in range(4):  # eager warm-up on scratch rows (restored below)
+        ctx.forward_hc(0, h.data_ptr() + t * row, 1, cs)
+    st.synchronize()
+    ctx.sync()
+    h.copy_(torch.from_numpy(h0))
+    torch.cuda.synchronize()
+    ctx.capture_begin(cs)
+    for t in range(TOKENS):
+        ctx.forward_hc(0, h.data_ptr() + t * row, 1, cs)
+    g = ctx.capture_end(cs)
+    g.launch(cs)
+    st.synchronize()
+    first = h.cpu().numpy()
+    for _ in range(warmup):
+        g.launch(cs)
+    st.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        g.launch(cs)
+    e1.record(st)
+    st.synchronize()
+    ctx.sync()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    return {"workload": f"config1 layer inside a hyper connection (hc {HC_N}, lowrank {HC_LR}, "
+                        f"q4 mixers), decode batch 1, {TOKENS} tokens/step",
+            "_h0": h0, "_out": first,
+            "tokens_per_s": TOKENS / (ms / 1e3), "us_per_token": 1e3 * ms / TOKENS,
+            "gpu_launches_per_token": 2,
+            "note": "per token: k_hc_pre1 (one CTA per SM, one grid barrier: RMSNorm of the "
+                    "hc streams, the low-rank down mixer and the inject weights, then the up "
+                    "mixer and the stream mean, the block's input) and the decode kernel, whose "
+                    "combine also adds inject x its output to the hc streams; h fp32 in HBM"}
+
+
+def cpu_hc_rate(h0, gpu_out, budget_s=10.0):
+    """The hyper-connection leg on the host cores: the reference's own
+    gated_residual + moe_forward + inject-add (ref_hc_moe_step, built from
+    its sources) per token, experts pre-dequantised (steady state); the
+    parity margin of the sampled rows' contribution h' - h0 against the GPU's."""
+    oracle, ref, kind, cores = _cpu_impl()
+    s = oracle.SynthLayer(D, E, K_TOP, I_DIM, G, SEED)
+    H = oracle.SynthHC(D, HC_N, HC_LR, HC_SEED)
+    ref.hc_moe_step(H, s, h0[:1])
+    t0 = time.perf_counter()
+    ref.hc_moe_step(H, s, h0[:1])
+    per = max(time.perf_counter() - t0, 1e-4)
+    n = int(min(len(h0), max(4, budget_s / per / 2)))
+    for t in range(n):  # warm: the sample's experts into the reference cache
+        ref.hc_moe_step(H, s, h0[t:t + 1])
+    outs = np.empty((n, h0.shape[1]), np.float32)
+    t0 = time.perf_counter()
+    for t in range(n):
+        outs[t] = ref.hc_moe_step(H, s, h0[t:t + 1])[0]
+    dt = time.perf_counter() - t0
+    if kind == "reference":
+        ref.lib.ref_reset_cache()
+    r = {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": kind,
+         "sample": f"{n} tokens of the hyper-connection leg, one hc step each "
+                   f"(gated_residual, moe_forward, inject-add), experts pre-dequantised; {dt:.1f} s"}
+    r["parity_margin"] = _margin(gpu_out[:n] - h0[:n], outs - h0[:n],
+                                 f"{kind} hc step, the {n} sampled tokens (h' - h)")
+    return r
 
 
 def measure_prefill_ep(rank, world, local, local_ctx=None, local_layer=1, reps=5, warmup=2):
@@ -757,6 +848,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] leg")
     ap.add_argument("--no-stack", action="store_true", help="skip the configs[3] leg")
     ap.add_argument("--no-stream", action="store_true", help="skip the configs[4] leg")
+    ap.add_argument("--no-hc", action="store_true", help="skip the hyper-connection leg")
     ap.add_argument("--stream-only", type=int, default=0,
                     help="run only the configs[4] leg with this many layers and print it")
     ap.add_argument("--stack-eager", type=int, default=0,
@@ -956,6 +1048,11 @@ def main():
         if world > 1:
             prefill["expert_parallel"] = measure_prefill_ep(rank, world, local, ctx, 1)
 
+    hc, hc_h0, hc_out = None, None, None
+    if not args.no_hc:
+        hc = measure_hc(ctx, rank)
+        hc_h0, hc_out = hc.pop("_h0"), hc.pop("_out")
+
     stack = None
     if not args.no_stack:
         stack = measure_stack(rank, world, local)
@@ -974,6 +1071,8 @@ def main():
         legs = []
         if prefill is not None:
             legs.append((prefill, lambda: cpu_prefill_rate(prefill_out)))
+        if hc is not None:
+            legs.append((hc, lambda: cpu_hc_rate(hc_h0, hc_out)))
         if stack is not None:
             legs.append((stack, lambda: cpu_stack_rate(STACK_SEED, 100, STACK_T, None, 3, STACK_T,
                                                        "config 3, decode batch 64")))
@@ -1015,6 +1114,7 @@ def main():
             "parity_spot_check": parity_ok,
             "parity_margin": (cpu or {}).get("parity_margin"),
             "prefill": prefill,
+            "hyper_connection": hc,
             "stack": stack,
             "stream": stream,
         }

@@ -217,6 +217,36 @@ typedef struct {
 int qmoe_forward_token_noalloc(const qmoe_token_args *a, void *stream,
                                qmoe_err *err);
 
+/* ---- the MoE side's hyper connection around the block ----
+ * The C port's layer wraps the MoE block in a hyper connection
+ * (mlp_hyper_connection.*, c/src/model.c:1945-1964): the residual state of a
+ * token is hc streams of d values, h [n, hc*d]. qmoe_forward_hc runs, on the
+ * device, gated_residual (c/src/model.c:728-796: each stream RMS-normalised
+ * with eps 1e-6 and scaled by norm; w = silu(down(normed) / hc);
+ * tmp = sigmoid(up(w)); mixed = the streams' mean of tmp * normed;
+ * inject = 2 sigmoid(inject(normed) / hc)), the MoE block of `layer` on
+ * mixed (as qmoe_forward_dev), and the inject-add after it
+ * (c/src/model.c:1723-1731: h[t, c, :] += inject[t, c] * moe[t, :]), in
+ * stream order, without host waits on a resident context. The mixers are q4
+ * with group 64 (absent biases read as zeros; up needs lowrank % 64 == 0) or
+ * dense bf16 (q NULL); dense bf16 products and inject use the canonical dot
+ * of the router. */
+typedef struct {
+    int hc;                      /* hc_count: streams (1..8) */
+    int lowrank;                 /* hc_lowrank */
+    const float *norm;           /* [hc*d] hc_norm.weight, widened to fp32 */
+    qmoe_q4 down;                /* input_mix_weight_down [lowrank, hc*d] */
+    const uint16_t *down_bf16;   /* or dense bf16 [lowrank, hc*d] when down.q is NULL */
+    qmoe_q4 up;                  /* input_mix_weight_up [hc*d, lowrank] */
+    const uint16_t *up_bf16;     /* or dense bf16 [hc*d, lowrank] when up.q is NULL */
+    const uint16_t *inject;      /* block_inject_weight bf16 [hc, hc*d] */
+} qmoe_hc_weights;
+/* Copies one layer's hyper-connection weights to the device (host pointers).
+ * Returns 0, or -1 with a message (shapes the kernels do not cover included). */
+int qmoe_upload_hc(qmoe_ctx *ctx, int layer, const qmoe_hc_weights *w, qmoe_err *err);
+/* h: device fp32 [n, hc*d], updated in place; n <= max_tokens. */
+int qmoe_forward_hc(qmoe_ctx *ctx, int layer, float *h, int n, void *stream, qmoe_err *err);
+
 /* Expert parallelism over ep_world GPUs, one context (and one process or
  * thread) per GPU, created with qmoe_config.ep_rank / ep_world. Experts are
  * partitioned as in a config-2/3 expert-parallel run: rank g owns experts

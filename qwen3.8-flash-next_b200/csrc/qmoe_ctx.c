@@ -40,6 +40,7 @@ typedef struct {
     uint8_t *shared_slot; /* slot layout */
     float router_wmax;    /* max_e |router row e|_2, rounded up */
     int ready;
+    qk_hc_dev hc;         /* the hyper connection around the block (hc.hc == 0: none) */
 } layer_dev;
 
 struct qmoe_ctx {
@@ -50,6 +51,10 @@ struct qmoe_ctx {
     cudaEvent_t copy_done;
     cudaEvent_t compute_mark; /* streaming: recorded on the compute stream before a fill */
     int pf_outstanding;       /* prefetched experts neither routed to nor evicted yet */
+    /* hyper-connection workspaces, [max_tokens] rows of hc_lr / hc_n / d values */
+    float *hc_W, *hc_R, *hc_INJ, *hc_mixed, *hc_y;
+    unsigned long long *hc_sync; /* the one-token pre-pass's grid-barrier counter */
+    int hc_lr, hc_n;
     int max_speculative;      /* their cap (ExpertStore._max_speculative) */
     /* device error word and output share one allocation (err at 0, out at
        256) so a host-pointer forward reads both back with one copy; the
@@ -242,6 +247,20 @@ static const nccl_fns *nccl_api(void) {
 
 /* ----------------------------------------------------------------- create */
 
+static void hc_free(qk_hc_dev *w) {
+    cudaFree(w->norm);
+    cudaFree(w->down_q);
+    cudaFree(w->down_s);
+    cudaFree(w->down_b);
+    cudaFree(w->down_bf);
+    cudaFree(w->up_q);
+    cudaFree(w->up_s);
+    cudaFree(w->up_b);
+    cudaFree(w->up_bf);
+    cudaFree(w->inject);
+    memset(w, 0, sizeof(*w));
+}
+
 void qmoe_destroy(qmoe_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->cfg.device);
@@ -253,6 +272,7 @@ void qmoe_destroy(qmoe_ctx *c) {
             cudaFree(c->layers[l].router);
             cudaFree(c->layers[l].shgate);
             cudaFree(c->layers[l].bias);
+            hc_free(&c->layers[l].hc);
         }
         free(c->layers);
     }
@@ -268,6 +288,12 @@ void qmoe_destroy(qmoe_ctx *c) {
     cudaFree(c->h);
     cudaFree(c->stk_xn);
     cudaFree(c->stk_y);
+    cudaFree(c->hc_W);
+    cudaFree(c->hc_R);
+    cudaFree(c->hc_INJ);
+    cudaFree(c->hc_mixed);
+    cudaFree(c->hc_y);
+    cudaFree(c->hc_sync);
     cudaFreeHost(c->x_pin);
     cudaFreeHost(c->idx_pin);
     cudaFreeHost(c->wave_pin);
@@ -1570,6 +1596,155 @@ int qmoe_upload_layer_ckpt(qmoe_ctx *c, int layer, qmoe_ckpt *ck, int ckpt_layer
 }
 
 const char *qmoe_version(void) { return "qmoe-b200 0.1 (sm_100a)"; }
+
+/* ------------------------------------------------- hyper connection */
+
+static int dev_copy(void **dst, const void *src, size_t bytes, qmoe_err *err) {
+    *dst = NULL;
+    if (!src) return 0;
+    cudaError_t ce = cudaMalloc(dst, bytes);
+    if (ce == cudaSuccess) ce = cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        seterr(err, "qmoe_upload_hc: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    return 0;
+}
+
+int qmoe_upload_hc(qmoe_ctx *c, int layer, const qmoe_hc_weights *w, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || !w || layer < 0 || layer >= c->cfg.num_layers) {
+        seterr(err, "qmoe_upload_hc: bad arguments (layer %d)", layer);
+        return -1;
+    }
+    const int d = c->L.d, hc = w->hc, lr = w->lowrank;
+    const size_t hd = (size_t)hc * d;
+    if (hc < 1 || hc > 8 || lr < 1 || !w->norm || !w->inject) {
+        seterr(err, "qmoe_upload_hc: need 1 <= hc <= 8, lowrank >= 1, norm and inject (hc=%d lowrank=%d)",
+               hc, lr);
+        return -1;
+    }
+    if (w->down.q ? (!w->down.scales || hd % 64) : !w->down_bf16) {
+        seterr(err, "qmoe_upload_hc: down mixer: q4 needs scales and hc*d %% 64 == 0, else dense bf16");
+        return -1;
+    }
+    if (w->up.q ? (!w->up.scales || lr % 64) : !w->up_bf16) {
+        seterr(err, "qmoe_upload_hc: up mixer: q4 needs scales and lowrank %% 64 == 0 (lowrank=%d), else "
+                    "dense bf16", lr);
+        return -1;
+    }
+    if (!qk_hc_smem_ok(d, hc)) {
+        seterr(err, "qmoe_upload_hc: hc*d = %zu values do not fit the kernel's shared memory", hd);
+        return -1;
+    }
+    if (cudaSetDevice(c->cfg.device) != cudaSuccess || cudaStreamSynchronize(c->stream) != cudaSuccess ||
+        qk_hc_prepare(d, hc) != 0) {
+        seterr(err, "qmoe_upload_hc: device set-up failed");
+        return -1;
+    }
+    qk_hc_dev *h = &c->layers[layer].hc;
+    hc_free(h);
+    const size_t ngd = hd / 64, ngu = (size_t)lr / 64;
+    int rc = dev_copy((void **)&h->norm, w->norm, hd * sizeof(float), err);
+    if (!rc && w->down.q) {
+        rc = dev_copy((void **)&h->down_q, w->down.q, (size_t)lr * hd / 2, err);
+        if (!rc) rc = dev_copy((void **)&h->down_s, w->down.scales, (size_t)lr * ngd * 2, err);
+        if (!rc) rc = dev_copy((void **)&h->down_b, w->down.biases, (size_t)lr * ngd * 2, err);
+    } else if (!rc) {
+        rc = dev_copy((void **)&h->down_bf, w->down_bf16, (size_t)lr * hd * 2, err);
+    }
+    if (!rc && w->up.q) {
+        rc = dev_copy((void **)&h->up_q, w->up.q, hd * (size_t)lr / 2, err);
+        if (!rc) rc = dev_copy((void **)&h->up_s, w->up.scales, hd * ngu * 2, err);
+        if (!rc) rc = dev_copy((void **)&h->up_b, w->up.biases, hd * ngu * 2, err);
+    } else if (!rc) {
+        rc = dev_copy((void **)&h->up_bf, w->up_bf16, hd * (size_t)lr * 2, err);
+    }
+    if (!rc) rc = dev_copy((void **)&h->inject, w->inject, (size_t)hc * hd * 2, err);
+    if (rc) {
+        hc_free(h);
+        return -1;
+    }
+    h->d = d;
+    h->hc = hc;
+    h->lowrank = lr;
+    /* workspaces for max_tokens rows, grown to the widest layer */
+    const size_t T = (size_t)c->cfg.max_tokens;
+    if (!c->hc_mixed) {
+        if (cudaMalloc((void **)&c->hc_mixed, T * d * sizeof(float)) != cudaSuccess ||
+            cudaMalloc((void **)&c->hc_y, T * d * sizeof(float)) != cudaSuccess ||
+            cudaMalloc((void **)&c->hc_sync, sizeof(unsigned long long)) != cudaSuccess ||
+            cudaMemset(c->hc_sync, 0, sizeof(unsigned long long)) != cudaSuccess) {
+            seterr(err, "qmoe_upload_hc: out of device memory");
+            return -1;
+        }
+    }
+    if (lr > c->hc_lr) {
+        cudaFree(c->hc_W);
+        c->hc_W = NULL;
+        if (cudaMalloc((void **)&c->hc_W, T * lr * sizeof(float)) != cudaSuccess) {
+            seterr(err, "qmoe_upload_hc: out of device memory");
+            return -1;
+        }
+        c->hc_lr = lr;
+    }
+    if (hc > c->hc_n) {
+        cudaFree(c->hc_R);
+        cudaFree(c->hc_INJ);
+        c->hc_R = c->hc_INJ = NULL;
+        if (cudaMalloc((void **)&c->hc_R, T * hc * sizeof(float)) != cudaSuccess ||
+            cudaMalloc((void **)&c->hc_INJ, T * hc * sizeof(float)) != cudaSuccess) {
+            seterr(err, "qmoe_upload_hc: out of device memory");
+            return -1;
+        }
+        c->hc_n = hc;
+    }
+    return 0;
+}
+
+int qmoe_forward_hc(qmoe_ctx *c, int layer, float *h, int n, void *stream, qmoe_err *err) {
+    if (err) err->msg[0] = 0;
+    if (!c || !h || layer < 0 || layer >= c->cfg.num_layers) {
+        seterr(err, "qmoe_forward_hc: bad arguments (layer %d)", layer);
+        return -1;
+    }
+    const qk_hc_dev *w = &c->layers[layer].hc;
+    if (!w->hc) {
+        seterr(err, "qmoe_forward_hc: layer %d has no hyper connection (qmoe_upload_hc)", layer);
+        return -1;
+    }
+    if (n < 0 || n > c->cfg.max_tokens) {
+        seterr(err, "qmoe_forward_hc: n=%d outside [0, max_tokens=%d]", n, c->cfg.max_tokens);
+        return -1;
+    }
+    if (!c->layers[layer].ready) {
+        seterr(err, "qmoe_forward_hc: layer %d was not uploaded", layer);
+        return -1;
+    }
+    if (n == 0) return 0;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    if (kerr(qk_launch_hc_pre(w, h, n, c->hc_W, c->hc_R, c->hc_INJ, c->hc_mixed, c->hc_sync, c->err_dev,
+                              c->num_sms, st),
+             "hc pre", err))
+        return -1;
+    if (n == 1 && c->resident_all && c->layers[layer].ready) {
+        /* one token: the decode kernel adds inject x its output to h itself */
+        qk_fwd f;
+        fill_fwd(c, layer, c->hc_mixed, 0, 1, c->hc_y, &f);
+        f.hc_h = h;
+        f.hc_inj = c->hc_INJ;
+        f.hc_n = w->hc;
+        const int rc = qk_launch_decode_fused(&f, c->dsync, st, 1);
+        if (rc == 0) {
+            c->last_T = 1;
+            c->stats.decode_calls++;
+            return 0;
+        }
+        if (rc != QK_FUSED_UNFIT) return kerr(rc, "decode_fused", err);
+    }
+    if (qmoe_forward_dev(c, layer, c->hc_mixed, QMOE_F32, n, c->hc_y, st, err)) return -1;
+    return kerr(qk_launch_hc_inject(h, c->hc_INJ, c->hc_y, n, w->hc, w->d, st), "hc inject", err);
+}
 
 /* ------------------------------------------------- expert parallelism */
 

@@ -561,6 +561,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         float acc = 0.f;
         for (int s = 0; s < S; ++s) acc = fmaf(r_w[s], partial[s * p.or_max + rl], acc);
         f.out[or0 + rl] = acc;
+        if (f.hc_h) {  // the hyper connection's inject-add (k_hc_inject's arithmetic)
+            for (int sc = 0; sc < f.hc_n; ++sc) {
+                float *hp = f.hc_h + static_cast<size_t>(sc) * L.d + or0 + rl;
+                *hp = fmaf(f.hc_inj[sc], acc, *hp);
+            }
+        }
     }
     STAMP(12);
     if (f.ptimes && tid == 0) {

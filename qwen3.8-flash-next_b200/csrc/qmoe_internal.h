@@ -71,6 +71,11 @@ typedef struct {
     int num_sms;
     unsigned long long *ptimes;  /* diagnostics: per-CTA phase timestamps
                                     [grid][32] (%globaltimer ns), or NULL */
+    /* the hyper connection's inject-add in the decode kernel's combine
+     * (T = 1): hc_h[c, :] += hc_inj[c] * out for c < hc_n; hc_h NULL: none */
+    float *hc_h;
+    const float *hc_inj;
+    int hc_n;
 } qk_fwd;
 
 /* Kernel launchers (qmoe_kernels.cu). Each returns a cudaError_t as int.
@@ -143,6 +148,30 @@ int qk_prefill_combine(qk_prefill *p, const qk_fwd *f, void *stream);
  * Returns QK_ROUTE_UNFIT (no launch) when the plan does not cover the shape. */
 #define QK_ROUTE_UNFIT (-8)
 int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream, void *mid_event);
+
+/* The MoE side's hyper connection (qmoe_hc.cu), device copies of one layer's
+ * weights: gated_residual before the block, the inject-add after it. */
+typedef struct {
+    int d, hc, lowrank;
+    float *norm;                          /* [hc*d] */
+    uint32_t *down_q;                     /* [lowrank, hc*d/8] or NULL: down_bf */
+    uint16_t *down_s, *down_b, *down_bf;  /* [lowrank, hc*d/64] (b may be NULL), [lowrank, hc*d] */
+    uint32_t *up_q;                       /* [hc*d, lowrank/8] or NULL: up_bf */
+    uint16_t *up_s, *up_b, *up_bf;        /* [hc*d, lowrank/64] (b may be NULL), [hc*d, lowrank] */
+    uint16_t *inject;                     /* [hc, hc*d] */
+} qk_hc_dev;
+int qk_hc_smem_ok(int d, int hc);
+int qk_hc_prepare(int d, int hc);
+/* gated_residual of n tokens h [n, hc*d]: mixed [n, d] (the block's input),
+ * INJ [n, hc]; W [n, lowrank] and R [n, hc] are its workspaces. One token
+ * takes a single launch of num_sms CTAs with a grid barrier on the zeroed,
+ * only-growing counter ctr (timeouts set QK_ERR_TIMEOUT_GRID in err); more
+ * tokens take two launches. */
+int qk_launch_hc_pre(const qk_hc_dev *w, const float *h, int n, float *W, float *R, float *INJ,
+                     float *mixed, unsigned long long *ctr, int *err, int num_sms, void *stream);
+/* h[t, c, :] += INJ[t, c] * y[t, :] */
+int qk_launch_hc_inject(float *h, const float *INJ, const float *y, int n, int hc, int d,
+                        void *stream);
 
 /* Expert parallelism (qmoe_prefill.cu). Rank g of G owns experts
  * [g E/G, (g+1) E/G). A token travels once to every rank that owns one of

@@ -77,6 +77,15 @@ class SynthSize(C.Structure):
                  "sh_q", "sh_sb", "sh_down_q", "sh_down_sb")]
 
 
+class HCWeights(C.Structure):
+    """qmoe_hc_weights: one layer's hyper connection around the MoE block."""
+    _fields_ = [
+        ("hc", C.c_int), ("lowrank", C.c_int), ("norm", C.c_void_p),
+        ("down", Q4), ("down_bf16", C.c_void_p), ("up", Q4), ("up_bf16", C.c_void_p),
+        ("inject", C.c_void_p),
+    ]
+
+
 class TokenArgs(C.Structure):
     """qmoe_token_args: one decode token for qmoe_forward_token_noalloc."""
     _fields_ = [
@@ -131,6 +140,8 @@ SIGNATURES = {
     "qmoe_synth_layer_dev": (C.c_int, [_P, C.c_int, C.c_uint64, C.c_double, C.POINTER(Err)]),
     "qmoe_last_routing": (C.c_int, [_P, _P, _P, _P, C.POINTER(Err)]),
     "qmoe_forward_token_noalloc": (C.c_int, [C.POINTER(TokenArgs), _P, C.POINTER(Err)]),
+    "qmoe_upload_hc": (C.c_int, [_P, C.c_int, C.POINTER(HCWeights), C.POINTER(Err)]),
+    "qmoe_forward_hc": (C.c_int, [_P, C.c_int, _P, C.c_int, _P, C.POINTER(Err)]),
     "qmoe_capture_begin": (C.c_int, [_P, _P, C.POINTER(Err)]),
     "qmoe_capture_end": (_P, [_P, _P, C.POINTER(Err)]),
     "qmoe_graph_launch": (C.c_int, [_P, _P, C.POINTER(Err)]),
@@ -265,6 +276,39 @@ class SynthLayer:
         return LayerWeights(ptr(self.router), ptr(self.shared_gate), ptr(self.logit_bias),
                             q4("gate"), q4("up"), q4("down"), q4("sh_gate"), q4("sh_up"),
                             q4("sh_down"))
+
+
+def _bf16_bits(a) -> np.ndarray:
+    """fp32 -> bf16 bits, round to nearest even."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+class SynthHC:
+    """Seeded synthetic hyper-connection weights of one layer (numpy, in the
+    layout qmoe_upload_hc takes): hc_norm near 1 (bf16-valued fp32), the two
+    low-rank mixers q4 (nibbles uniform, scales |N(0, 0.02)|, biases -8 x
+    scale; biases=False leaves them absent) or dense bf16 N(0, 0.02), and
+    block_inject bf16 N(0, 0.02) [hc, hc*d]. Draws come from numpy's
+    default_rng(seed) in that order."""
+
+    def __init__(self, d: int, hc: int, lowrank: int, seed: int, q4: bool = True, biases: bool = True):
+        rng = np.random.default_rng(seed)
+        self.d, self.hc, self.lowrank, hd = d, hc, lowrank, hc * d
+        norm = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+        self.norm = (_bf16_bits(norm).astype(np.uint32) << 16).view(np.float32)
+        self.inject = _bf16_bits(0.02 * rng.standard_normal((hc, hd)))
+        self.parts = {}
+        for name, rows, cols in (("down", lowrank, hd), ("up", hd, lowrank)):
+            if q4:
+                q = rng.integers(0, 2 ** 32, size=(rows, cols // 8), dtype=np.uint32)
+                sc = _bf16_bits(np.abs(0.02 * rng.standard_normal((rows, cols // 64))))
+                bi = (_bf16_bits(-8.0 * (sc.astype(np.uint32) << 16).view(np.float32))
+                      if biases else None)
+                self.parts[name] = (q, sc, bi, None)
+            else:
+                self.parts[name] = (None, None, None,
+                                    _bf16_bits(0.02 * rng.standard_normal((rows, cols))))
 
 
 def synth_tokens(seed: int, stream: int, n: int, d: int) -> np.ndarray:
@@ -501,6 +545,25 @@ class Context:
         err = Err()
         self._chk(lib().qmoe_forward_ep(self.h, layer, x_ptr, x_dtype, n, out_ptr, stream,
                                         C.byref(err)), err)
+
+    def upload_hc(self, layer: int, hcw):
+        """A layer's hyper-connection weights: an object with hc, lowrank, norm
+        (fp32 [hc*d]), inject (bf16 bits [hc, hc*d]) and parts["down"] /
+        parts["up"] = (q, scales, biases, dense_bf16), q4 or dense."""
+        def ptr_(a):
+            return None if a is None else a.ctypes.data
+        dq, ds, db, dbf = hcw.parts["down"]
+        uq, us, ub, ubf = hcw.parts["up"]
+        w = HCWeights(hcw.hc, hcw.lowrank, ptr_(hcw.norm), Q4(ptr_(dq), ptr_(ds), ptr_(db)), ptr_(dbf),
+                      Q4(ptr_(uq), ptr_(us), ptr_(ub)), ptr_(ubf), ptr_(hcw.inject))
+        err = Err()
+        self._chk(lib().qmoe_upload_hc(self.h, layer, C.byref(w), C.byref(err)), err)
+
+    def forward_hc(self, layer: int, h_ptr: int, n: int, stream: int | None = None):
+        """gated_residual, the MoE block and the inject-add; h: device fp32
+        [n, hc*d], updated in place."""
+        err = Err()
+        self._chk(lib().qmoe_forward_hc(self.h, layer, h_ptr, n, stream, C.byref(err)), err)
 
     def synth_layer_dev(self, layer: int, seed: int, zipf_s: float = 0.0):
         """The seeded synthetic layer generated on the device (resident contexts)."""

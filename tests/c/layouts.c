@@ -20,6 +20,8 @@ int main(void) {
     S(qmoe_stats);
     F(qmoe_stats, expert_wait_seconds); F(qmoe_stats, forward_seconds); F(qmoe_stats, routed_hits);
     F(qmoe_stats, prefetch_wasted); F(qmoe_stats, expert_waves);
+    S(qmoe_hc_weights);
+    F(qmoe_hc_weights, norm); F(qmoe_hc_weights, down_bf16); F(qmoe_hc_weights, up); F(qmoe_hc_weights, inject);
     S(qmoe_token_args);
     F(qmoe_token_args, x); F(qmoe_token_args, x_dtype); F(qmoe_token_args, out);
     F(qmoe_token_args, shared_slot);

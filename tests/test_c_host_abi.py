@@ -42,7 +42,7 @@ def test_struct_layouts_match_the_bindings(built, tmp_path):
               "qmoe_layer_weights": qmoe.LayerWeights, "qmoe_cache_stats": qmoe.CacheStats,
               "qmoe_stats": qmoe.Stats, "qmoe_token_args": qmoe.TokenArgs,
               "qmoe_synth_size": qmoe.SynthSize, "qmoe_tensor_info": qmoe.TensorInfo,
-              "qmoe_io_stats": qmoe.IOStats}
+              "qmoe_io_stats": qmoe.IOStats, "qmoe_hc_weights": qmoe.HCWeights}
     n = 0
     for line in out.splitlines():
         name, field, value = line.split()

@@ -85,3 +85,21 @@ def test_checker_rmsnorm_matches_reference_kernel(built):
     y = oracle.rmsnorm(x, 1e-6)
     r = 1.0 / np.sqrt((x.astype(np.float64) ** 2).mean(1) + 1e-6)
     np.testing.assert_allclose(y, x * r[:, None], rtol=2e-6, atol=0)
+
+
+@pytest.mark.parametrize("q4,biases", [(True, True), (True, False), (False, True)])
+def test_checker_hc_weights_equal_library_hc_weights(built, q4, biases):
+    """The bench's hyper-connection leg builds its GPU weights with
+    qmoe.SynthHC and its CPU baseline with oracle.SynthHC: both are the same
+    bytes for the same seed."""
+    import oracle
+    import qmoe
+    a = oracle.SynthHC(256, 4, 64, 20261213, q4=q4, biases=biases)
+    b = qmoe.SynthHC(256, 4, 64, 20261213, q4=q4, biases=biases)
+    assert np.array_equal(a.norm.view(np.uint32), b.norm.view(np.uint32))
+    assert np.array_equal(a.inject, b.inject)
+    for part in ("down", "up"):
+        for x, y in zip(a.parts[part], b.parts[part]):
+            assert (x is None) == (y is None)
+            if x is not None:
+                assert x.dtype == y.dtype and np.array_equal(x, y), part
