@@ -813,6 +813,51 @@ def run_stack_eager(layers):
     print(f"stack case: {layers} layers x {STACK_T} tokens ok")
 
 
+def run_stream_eager(n):
+    """Small case for ncu captures of the per-token kernels: n single-token
+    forwards of one streamed config-1 layer (Zipf(1.1) routing, a pool of 64
+    expert slots): routing on the device (k_router, k_topk), misses filled
+    from pinned host memory, then k_decode_gateup and k_decode_down."""
+    import torch
+
+    import qmoe
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=1, pool_bytes=64 * SLOT, prefetch=0)
+    ctx = qmoe.Context(cfg)
+    ctx.synth_layer_dev(0, STACK_SEED + 1, 1.1)
+    x = torch.from_numpy(qmoe.synth_tokens(SEED, 0, n, D)).cuda()
+    out = torch.empty((n, D), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    for t in range(n):
+        ctx.forward_dev(0, x.data_ptr() + t * D * 4, qmoe.QMOE_F32, 1, out.data_ptr() + t * D * 4, None)
+    ctx.sync()
+    ctx.close()
+    print(f"stream case: {n} tokens ok")
+
+
+def run_hc_eager(n):
+    """Small case for ncu captures of the hyper-connection kernels: n eager
+    qmoe_forward_hc calls of one token (k_hc_pre1 and the decode kernel with
+    the inject-add), then one call of 8 tokens (k_hc_down, k_hc_up, the
+    grouped path, k_hc_inject), on the config-1 layer."""
+    import torch
+
+    import qmoe
+    cfg = qmoe.make_config(D, E, K_TOP, I_DIM, G, max_tokens=8)
+    ctx = qmoe.Context(cfg)
+    ctx.upload(0, qmoe.SynthLayer(cfg, SEED))
+    ctx.upload_hc(0, qmoe.SynthHC(D, HC_N, HC_LR, HC_SEED))
+    h = torch.from_numpy(np.concatenate(
+        [qmoe.synth_tokens(SEED, 40 + j, n + 8, D) for j in range(HC_N)], axis=1)).cuda()
+    torch.cuda.synchronize()
+    row = HC_N * D * 4
+    for t in range(n):
+        ctx.forward_hc(0, h.data_ptr() + t * row, 1, None)
+    ctx.forward_hc(0, h.data_ptr() + n * row, 8, None)
+    ctx.sync()
+    ctx.close()
+    print(f"hc case: {n} single-token calls and one 8-token call ok")
+
+
 def run_eager(n):
     """Small case for ncu captures: n single-token forwards launched eagerly
     on the config-1 layer (906 MB of experts, larger than L2)."""
@@ -853,6 +898,10 @@ def main():
                     help="run only the configs[4] leg with this many layers and print it")
     ap.add_argument("--stack-eager", type=int, default=0,
                     help="profiling case: one eager pass of an N-layer configs[3] stack and exit")
+    ap.add_argument("--stream-eager", type=int, default=0,
+                    help="profiling case: N single-token forwards of one streamed layer and exit")
+    ap.add_argument("--hc-eager", type=int, default=0,
+                    help="profiling case: N single-token hyper-connection steps (and one of 8) and exit")
     ap.add_argument("--stack-only", type=int, default=0,
                     help="run only the configs[3] leg with this many layers and print it")
     args = ap.parse_args()
@@ -867,6 +916,12 @@ def main():
         return
     if args.stack_eager:
         run_stack_eager(args.stack_eager)
+        return
+    if args.stream_eager:
+        run_stream_eager(args.stream_eager)
+        return
+    if args.hc_eager:
+        run_hc_eager(args.hc_eager)
         return
     if args.stream_only:
         import torch
