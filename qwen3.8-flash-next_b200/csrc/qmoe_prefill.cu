@@ -450,44 +450,60 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Grouped GEMM for small groups (at most NS = 32 rows per tile): the operands
 // swap roles. A = 128 dequantised weight rows (gate, up or down rows, the B
 // tile of k_gemm), kept in tensor memory; B = the group's token rows (x or
-// H) from shared memory, the hi and lo planes side by side as N = 64 (one
-// plane: N = 32). Per 16-wide K slice and half of the 256-row weight tile
-// one MMA of M=128 x N=64 x K=16; D[weight row][token] sits in TMEM lanes =
+// H) from shared memory, the hi and lo planes side by side in N (one plane:
+// N = the rows). Per 16-wide K slice and half of the 256-row weight tile
+// one MMA of M=128 x N x K=16; D[weight row][token] sits in TMEM lanes =
 // weight rows and the epilogue writes it transposed (token rows of H or Y),
 // adding the hi and lo columns. Keeping the weights out of shared memory
 // matters here: with them there, the operand reads of these small MMAs and
 // the dequantisers' stores took the shared-memory bandwidth and set the
 // pace. TMEM: accumulators in columns [0, 256) (2 buffers x 2 halves x 64),
 // four dequantised weight buffers in [256, 512) (2 halves x 32 columns).
+//
+// A raw stage holds KS = 4 K steps. The packed q4 words of its 256 weight
+// rows arrive as one 128-byte-wide box per 128 rows (128-byte swizzle, so
+// the dequantisers' reads of 32 bytes per row and step spread over the
+// banks) and the scales as one 32-byte box: 2 + 1 loads for 4 steps,
+// where one box per step and per row block cost a TMA row request for
+// every 32 (or 16) bytes. Tiles of at most 8 rows (most groups at batch
+// decode sizes) load 8-row token boxes and run N = 16 (8 hi + 8 lo
+// columns), so their token traffic is a quarter of a 32-row tile's.
 // Warp roles and bounded waits as k_gemm; MODE 0 / 3 gate/up (x one plane /
 // hi+lo), 1 down (H hi+lo).
 constexpr int NS = 32;                    // token rows per small tile
+constexpr int NS8 = 8;                    // rows of a narrow tile (8-row token boxes)
 constexpr int kSmallMax = 2 * NS;         // largest group planned as small tiles
-constexpr int kXs = NS * BK * 2;          // 4 KB: one plane of the token tile
+constexpr int kXs = NS * BK * 2;          // 4 KB: one plane of the token tile, one K step
 constexpr int kNbT = 4;                   // dequantised weight buffers in TMEM
 constexpr int kThreadsSw = kThreads + 32; // a second MMA-issuing warp (warp 14)
+constexpr int KS = 4;                     // K steps per raw stage
 template <int MODE>
 struct CfgS {
     static constexpr bool GU = MODE != 1;
-    static constexpr int X = MODE == 0 ? kXs : 2 * kXs;
-    static constexpr int Raw = 2 * kXs + kBq + kBs;  // 20 KB (1024-aligned) for every mode
-    static constexpr int NR = 8;
+    static constexpr int Xr = KS * 2 * kXs;  // 32 KB: KS steps x (hi, lo) planes x 32 rows
+    static constexpr int Qr = 256 * 128;     // 32 KB: 256 weight rows x 128 bytes (KS steps of q4)
+    static constexpr int Sr = 256 * 32;      // 8 KB: scales of KS steps (GU: 128 rows x 32 B)
+    static constexpr int Raw = Xr + Qr + Sr; // 72 KB (1024-aligned)
+    static constexpr int NR = 3;
     static constexpr int Smem = NR * Raw + 1024;
 };
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreadsSw, 1)
-    k_gemm_sw(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ,
-              const __grid_constant__ CUtensorMap tmS, GemmArgs g) {
+    k_gemm_sw(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX8,
+              const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmS,
+              GemmArgs g) {
     constexpr int NR = CfgS<MODE>::NR;
     constexpr int kRaw = CfgS<MODE>::Raw;
+    constexpr int kXr = CfgS<MODE>::Xr, kQr = CfgS<MODE>::Qr;
     constexpr bool kGU = CfgS<MODE>::GU;
     constexpr bool kLo = MODE != 0;
-    constexpr int kN = kLo ? 2 * NS : NS;  // MMA N: token columns (hi, then lo)
     extern __shared__ uint8_t smem_raw[];
-    // done[s]: the MMAs of the step that used raw stage s (and weight buffer
-    // it % kNbT) completed, one commit from each issuer
-    __shared__ uint64_t raw_full[NR], done[NR], bf_full[kNbT];
+    // raw_full[s] / raw_free[s]: stage s loaded / its last step's MMAs done
+    // (one commit from each issuer); wfree[b]: the MMAs that read weight
+    // buffer b completed (one commit from each issuer); bf_full[b]: weight
+    // buffer b written by the eight dequantising warps
+    __shared__ uint64_t raw_full[NR], raw_free[NR], wfree[kNbT], bf_full[kNbT];
     __shared__ uint64_t acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag_;
@@ -498,9 +514,12 @@ __global__ void __launch_bounds__(kThreadsSw, 1)
     if (tid == 0) {
         for (int s = 0; s < NR; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&done[s], 2);
+            mbar_init(&raw_free[s], 2);
         }
-        for (int b = 0; b < kNbT; ++b) mbar_init(&bf_full[b], kDeqWarps);
+        for (int b = 0; b < kNbT; ++b) {
+            mbar_init(&bf_full[b], kDeqWarps);
+            mbar_init(&wfree[b], 2);
+        }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 2);
             mbar_init(&acc_empty[b], 4);
@@ -519,53 +538,64 @@ __global__ void __launch_bounds__(kThreadsSw, 1)
     const uint32_t tmem_w = tmem + 256;  // dequantised weight buffers
     const int ntiles = *g.n_mtiles * g.NT;
     const int KB = g.KB;
+    const int nst = (KB + KS - 1) / KS;  // stages per tile
 
     if (warp == 0) {
-        // ---------------- TMA producer
+        // ---------------- TMA producer: one raw stage per KS K steps
         if (lane == 0) {
-            int it = 0;
-            int last_it[NR];
-            for (int s = 0; s < NR; ++s) last_it[s] = -1;
+            int sg = 0;
+            int last_sg[NR];
+            for (int s = 0; s < NR; ++s) last_sg[s] = -1;
             for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
                 const MTile mt = g.tiles[tile / g.NT];
                 const int nt = tile % g.NT;
-                for (int kb = 0; kb < KB; ++kb, ++it) {
-                    const int s = it % NR;
-                    const uint32_t ph = (it / NR) & 1;
-                    if (!mbar_wait(&done[s], ph ^ 1)) {
+                const bool narrow = mt.rows <= NS8;
+                const uint32_t xbox = (narrow ? NS8 : NS) * BK * 2;
+                const int lo_off = narrow ? NS8 * 128 : kXs;  // lo plane right after the hi rows
+                for (int st = 0; st < nst; ++st, ++sg) {
+                    const int s = sg % NR;
+                    if (!mbar_wait(&raw_free[s], ((sg / NR) & 1) ^ 1)) {
                         atomicOr(g.err, QK_ERR_TIMEOUT_COPY);
                         abort_flag = 1;
                         break;
                     }
-                    uint8_t *X = smem + s * kRaw;
-                    uint8_t *Bq = X + 2 * kXs, *Bs = Bq + kBq;
-                    mbar_expect_tx(&raw_full[s], CfgS<MODE>::X + kBq + (kGU ? 128 : 256) * 16);
-                    tma_load_2d(X, &tmX, kb * BK, mt.m0, &raw_full[s]);  // (hi)
-                    if (kLo) tma_load_2d(X + kXs, &tmX, kb * BK, g.rows_max + mt.m0, &raw_full[s]);
-                    if (kGU) {
-                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 128, mt.slot, &raw_full[s]);
-                        tma_load_3d(Bq + 128 * 32, &tmQ, g.d / 2 + kb * 32, nt * 128, mt.slot,
-                                    &raw_full[s]);
-                        tma_load_3d(Bs, &tmS, g.d + 16 * (kb >> 1), nt * 128, mt.slot, &raw_full[s]);
-                    } else {
-                        tma_load_3d(Bq, &tmQ, kb * 32, nt * 256, mt.slot, &raw_full[s]);
-                        tma_load_3d(Bs, &tmS, g.I / 2 + 16 * (kb >> 2), nt * 256, mt.slot,
-                                    &raw_full[s]);
+                    const int kb0 = st * KS, nk = min(KS, KB - kb0);
+                    uint8_t *X = smem + s * kRaw, *Q = X + kXr, *S = Q + kQr;
+                    mbar_expect_tx(&raw_full[s], nk * xbox * (kLo ? 2 : 1) + 256 * 128 + (kGU ? 128 : 256) * 32);
+                    for (int kk = 0; kk < nk; ++kk) {
+                        uint8_t *Xk = X + kk * 2 * kXs;
+                        const int kb = kb0 + kk;
+                        tma_load_2d(Xk, narrow ? &tmX8 : &tmX, kb * BK, mt.m0, &raw_full[s]);  // (hi)
+                        if (kLo)
+                            tma_load_2d(Xk + lo_off, narrow ? &tmX8 : &tmX, kb * BK, g.rows_max + mt.m0,
+                                        &raw_full[s]);
                     }
-                    last_it[s] = it;
+                    if (kGU) {
+                        tma_load_3d(Q, &tmQ, kb0 * 32, nt * 128, mt.slot, &raw_full[s]);                    // gate
+                        tma_load_3d(Q + 128 * 128, &tmQ, g.d / 2 + kb0 * 32, nt * 128, mt.slot, &raw_full[s]);  // up
+                        tma_load_3d(S, &tmS, g.d + 8 * kb0, nt * 128, mt.slot, &raw_full[s]);
+                    } else {
+                        tma_load_3d(Q, &tmQ, kb0 * 32, nt * 256, mt.slot, &raw_full[s]);
+                        tma_load_3d(Q + 128 * 128, &tmQ, kb0 * 32, nt * 256 + 128, mt.slot, &raw_full[s]);
+                        tma_load_3d(S, &tmS, g.I / 2, nt * 256, mt.slot, &raw_full[s]);
+                    }
+                    last_sg[s] = sg;
                 }
             }
             for (int s = 0; s < NR; ++s)
-                if (last_it[s] >= 0) mbar_wait(&raw_full[s], (last_it[s] / NR) & 1);
+                if (last_sg[s] >= 0) mbar_wait(&raw_full[s], (last_sg[s] / NR) & 1);
         }
     } else if (warp == 1 || warp == kThreads / 32) {
         // ---------------- MMA issuers: warp 1 the first 128 weight rows, the
         // last warp the second (one issuing thread runs small MMAs at about
         // half the tensor pipe's rate; two keep it busy)
         const int hh = warp == 1 ? 0 : 1;
-        const uint32_t idesc = idesc_f16(BM, kN);
-        int it = 0, lt = 0;
+        int it = 0, sg = 0, lt = 0;
         for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
+            const MTile mt = g.tiles[tile / g.NT];
+            const bool narrow = mt.rows <= NS8;
+            const int ns = narrow ? NS8 : NS;
+            const uint32_t idesc = idesc_f16(BM, kLo ? 2 * ns : (narrow ? 16 : NS));
             const int buf = lt & 1;
             const uint32_t aph = (lt >> 1) & 1;
             if (!mbar_wait(&acc_empty[buf], aph ^ 1)) {
@@ -578,24 +608,32 @@ __global__ void __launch_bounds__(kThreadsSw, 1)
             tc_fence_after();
             const uint32_t dt = tmem + buf * 128;
             bool ok = true;
-            for (int kb = 0; kb < KB; ++kb, ++it) {
-                const int s = it % NR, b = it % kNbT;
-                const uint32_t ph = (it / NR) & 1, bph = (it / kNbT) & 1;
-                if (!mbar_wait(&raw_full[s], ph) || !mbar_wait(&bf_full[b], bph)) {
+            for (int st = 0; st < nst && ok; ++st, ++sg) {
+                const int s = sg % NR;
+                const int nk = min(KS, KB - st * KS);
+                if (!mbar_wait(&raw_full[s], (sg / NR) & 1)) {
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t x0 = smem_addr(smem + s * kRaw);
-                    const uint32_t w0 = tmem_w + b * 64;
+                for (int kk = 0; kk < nk; ++kk, ++it) {
+                    const int b = it % kNbT;
+                    if (!mbar_wait(&bf_full[b], (it / kNbT) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t x0 = smem_addr(smem + s * kRaw + kk * 2 * kXs);
+                        const uint32_t w0 = tmem_w + b * 64;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        umma_f16_ts(dt + hh * 64, w0 + hh * 32 + kk * 8, sdesc_sw128(x0 + kk * 32), idesc,
-                                    (kb | kk) != 0);
-                    umma_commit(&done[s]);
+                        for (int kq = 0; kq < BK / 16; ++kq)
+                            umma_f16_ts(dt + hh * 64, w0 + hh * 32 + kq * 8, sdesc_sw128(x0 + kq * 32), idesc,
+                                        (st | kk | kq) != 0);
+                        umma_commit(&wfree[b]);
+                        if (kk == nk - 1) umma_commit(&raw_free[s]);
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
             if (!ok) {
                 if (lane == 0) {
@@ -617,49 +655,55 @@ __global__ void __launch_bounds__(kThreadsSw, 1)
         // TMEM lane 32 q + lane of half h (warp w reaches lanes 32 (w % 4)..)
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int r = h * 128 + 32 * q + lane;
+        const int rr = r & 127;
         const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
-        int it = 0;
+        int it = 0, sg = 0;
         for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x) {
             bool ok = true;
-            for (int kb = 0; kb < KB; ++kb, ++it) {
-                const int s = it % NR, b = it % kNbT;
-                const uint32_t ph = (it / NR) & 1;
-                // weight buffer b is free once the step kNbT earlier is done;
-                // that barrier cannot be two phases ahead (its next phase needs
-                // this step's dequantised weights)
-                const int pv = it - kNbT;
-                if (!mbar_wait(&raw_full[s], ph) ||
-                    (pv >= 0 && !mbar_wait(&done[pv % NR], (pv / NR) & 1))) {
+            for (int st = 0; st < nst && ok; ++st, ++sg) {
+                const int s = sg % NR;
+                const int nk = min(KS, KB - st * KS);
+                if (!mbar_wait(&raw_full[s], (sg / NR) & 1)) {
                     ok = false;
                     break;
                 }
-                const uint8_t *Bq = smem + s * kRaw + 2 * kXs, *Bs = Bq + kBq;
-                uint32_t sb;
-                if (kGU) {
-                    const uint2 quad = *reinterpret_cast<const uint2 *>(Bs + (r & 127) * 16 + 8 * (kb & 1));
-                    sb = h == 0 ? quad.x : quad.y;
-                } else {
-                    sb = *reinterpret_cast<const uint32_t *>(Bs + r * 16 + 4 * (kb & 3));
-                }
-                const uint4 qa = *reinterpret_cast<const uint4 *>(Bq + r * 32);
-                const uint4 qb = *reinterpret_cast<const uint4 *>(Bq + r * 32 + 16);
-                const __half2 s2 = __float2half2_rn(bf16lo(sb)), b2 = __float2half2_rn(bf16hi(sb));
-                const uint32_t wd[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                uint32_t v[32];
+                const uint8_t *Qrow = smem + s * kRaw + kXr + r * 128;  // 128-byte swizzled row
+                const uint8_t *S = smem + s * kRaw + kXr + kQr;
+                for (int kk = 0; kk < nk; ++kk, ++it) {
+                    const int b = it % kNbT;
+                    // weight buffer b is free once the MMAs of step it - kNbT are done
+                    const int pv = it - kNbT;
+                    if (pv >= 0 && !mbar_wait(&wfree[b], (pv / kNbT) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    uint32_t sb;
+                    if (kGU) {
+                        const uint2 quad = *reinterpret_cast<const uint2 *>(S + rr * 32 + 8 * kk);
+                        sb = h == 0 ? quad.x : quad.y;
+                    } else {
+                        sb = *reinterpret_cast<const uint32_t *>(S + r * 32 + 4 * (st * KS + kk));
+                    }
+                    const uint4 qa = *reinterpret_cast<const uint4 *>(Qrow + (((2 * kk) ^ (r & 7)) << 4));
+                    const uint4 qb = *reinterpret_cast<const uint4 *>(Qrow + (((2 * kk + 1) ^ (r & 7)) << 4));
+                    const __half2 s2 = __float2half2_rn(bf16lo(sb)), b2 = __float2half2_rn(bf16hi(sb));
+                    const uint32_t wd[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                    uint32_t v[32];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 o = dequant_word(wd[c], s2, b2);
-                    v[4 * c] = o.x;
-                    v[4 * c + 1] = o.y;
-                    v[4 * c + 2] = o.z;
-                    v[4 * c + 3] = o.w;
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 o = dequant_word(wd[c], s2, b2);
+                        v[4 * c] = o.x;
+                        v[4 * c + 1] = o.y;
+                        v[4 * c + 2] = o.z;
+                        v[4 * c + 3] = o.w;
+                    }
+                    tc_fence_after();  // the MMAs that read this buffer before have completed
+                    tmem_st32(tmem_w + lane_off + b * 64 + h * 32, v);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bf_full[b]);
                 }
-                tc_fence_after();  // the MMAs that read this buffer before have completed
-                tmem_st32(tmem_w + lane_off + b * 64 + h * 32, v);
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bf_full[b]);
             }
             if (!ok) {
                 if (lane == 0) {
@@ -671,13 +715,14 @@ __global__ void __launch_bounds__(kThreadsSw, 1)
         }
     } else if (warp < kThreads / 32) {
         // ---------------- epilogue (warps 10-13): thread = weight row 32q + lane of each
-        // half; token columns c (hi) and NS + c (lo)
+        // half; token columns c (hi) and ns + c (lo)
         const int q = warp & 3;
         const int wr = 32 * q + lane;
         int lt = 0;
         for (int tile = blockIdx.x; tile < ntiles && !abort_flag; tile += gridDim.x, ++lt) {
             const MTile mt = g.tiles[tile / g.NT];
             const int nt = tile % g.NT;
+            const bool narrow = mt.rows <= NS8;
             const int buf = lt & 1;
             const uint32_t aph = (lt >> 1) & 1;
             if (!mbar_wait(&acc_full[buf], aph)) {
@@ -690,22 +735,37 @@ __global__ void __launch_bounds__(kThreadsSw, 1)
             tc_fence_after();
             const uint32_t tb = tmem + (static_cast<uint32_t>(32 * q) << 16) + buf * 128;
             float v0[NS], v1[NS];
-            tmem_ld16(tb, v0);
-            tmem_ld16(tb + 16, v0 + 16);
-            tmem_ld16(tb + 64, v1);
-            tmem_ld16(tb + 64 + 16, v1 + 16);
-            tmem_wait_ld();
-            if (kLo) {
-                float l0[NS], l1[NS];
-                tmem_ld16(tb + NS, l0);
-                tmem_ld16(tb + NS + 16, l0 + 16);
-                tmem_ld16(tb + 64 + NS, l1);
-                tmem_ld16(tb + 64 + NS + 16, l1 + 16);
+            if (narrow) {
+                // columns [0, 8) hi and [8, 16) lo (one plane: [0, 8))
+                float a0[16], a1[16];
+                tmem_ld16(tb, a0);
+                tmem_ld16(tb + 64, a1);
                 tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < NS; ++c) {
-                    v0[c] += l0[c];
-                    v1[c] += l1[c];
+                for (int c = 0; c < NS8; ++c) {
+                    v0[c] = kLo ? a0[c] + a0[NS8 + c] : a0[c];
+                    v1[c] = kLo ? a1[c] + a1[NS8 + c] : a1[c];
+                }
+#pragma unroll
+                for (int c = NS8; c < NS; ++c) v0[c] = v1[c] = 0.f;
+            } else {
+                tmem_ld16(tb, v0);
+                tmem_ld16(tb + 16, v0 + 16);
+                tmem_ld16(tb + 64, v1);
+                tmem_ld16(tb + 64 + 16, v1 + 16);
+                tmem_wait_ld();
+                if (kLo) {
+                    float l0[NS], l1[NS];
+                    tmem_ld16(tb + NS, l0);
+                    tmem_ld16(tb + NS + 16, l0 + 16);
+                    tmem_ld16(tb + 64 + NS, l1);
+                    tmem_ld16(tb + 64 + NS + 16, l1 + 16);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < NS; ++c) {
+                        v0[c] += l0[c];
+                        v1[c] += l1[c];
+                    }
                 }
             }
             tc_fence_before();
@@ -1412,13 +1472,15 @@ bool map_2d_16(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, b
 }
 
 bool map_3d_u8(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t rows,
-               uint64_t slots, uint64_t slot_stride, uint32_t box_x, uint32_t box_y) {
+               uint64_t slots, uint64_t slot_stride, uint32_t box_x, uint32_t box_y,
+               bool swizzle128 = false) {
     const cuuint64_t dims[3] = {row_bytes, rows, slots};
     const cuuint64_t strides[2] = {row_bytes, slot_stride};
     const cuuint32_t box[3] = {box_x, box_y, 1};
     const cuuint32_t es[3] = {1, 1, 1};
     return get_encode()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims,
-                        strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1442,6 +1504,10 @@ struct qk_prefill {
     float *Y;
     CUtensorMap tmX, tmH, tmQgu, tmSgu, tmQdn, tmSdn;
     CUtensorMap tmXs, tmHs;         // the same planes in NS-row boxes
+    CUtensorMap tmXs8, tmHs8;       // and in NS8-row boxes (narrow small tiles)
+    // k_gemm_sw's weight boxes: q4 words of KS K steps (128 bytes, swizzled)
+    // per row, the scales of KS steps (GU) or of the whole row (down)
+    CUtensorMap tmQgu4, tmSgu4, tmQdn4, tmSdn4;
     // routing: x as a bf16 pair [2 * Tpad, d], token norms, approximate
     // logits [max_tokens, E], the router's M-tile list
     int route_ok, Tpad;
@@ -1549,6 +1615,13 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
               map_2d_16(&p->tmH, p->H, L->I, 2 * R, false) &&
               map_2d_16(&p->tmXs, p->xp, L->d, 2 * R, false, NS) &&
               map_2d_16(&p->tmHs, p->H, L->I, 2 * R, false, NS) &&
+              map_2d_16(&p->tmXs8, p->xp, L->d, 2 * R, false, NS8) &&
+              map_2d_16(&p->tmHs8, p->H, L->I, 2 * R, false, NS8) &&
+              map_3d_u8(&p->tmQgu4, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 128, 128, true) &&
+              map_3d_u8(&p->tmSgu4, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 32, 128) &&
+              map_3d_u8(&p->tmQdn4, pool + L->gu_bytes, L->d_row, L->d, pool_slots, L->slot_bytes, 128, 128,
+                        true) &&
+              map_3d_u8(&p->tmSdn4, pool + L->gu_bytes, L->d_row, L->d, pool_slots, L->slot_bytes, 32, 256) &&
               map_3d_u8(&p->tmQgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 32, 128) &&
               map_3d_u8(&p->tmSgu, pool, L->gu_row, L->I, pool_slots, L->slot_bytes, 16, 128) &&
               map_3d_u8(&p->tmQdn, pool + L->gu_bytes, L->d_row, L->d, pool_slots, L->slot_bytes, 32,
@@ -1673,6 +1746,12 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         return qk_launch_raw(fn, dim3(p->num_sms), dim3(threads), smem, st, 0, args);
     };
     auto fn = [](auto f) { return reinterpret_cast<const void *>(f); };
+    auto launch_sw = [&](const void *f, int smem, const CUtensorMap *a, const CUtensorMap *a8,
+                         const CUtensorMap *q, const CUtensorMap *sc, GemmArgs *ga) {
+        void *args[] = {const_cast<CUtensorMap *>(a), const_cast<CUtensorMap *>(a8),
+                        const_cast<CUtensorMap *>(q), const_cast<CUtensorMap *>(sc), ga};
+        return qk_launch_raw(f, dim3(p->num_sms), dim3(kThreadsSw), smem, st, 0, args);
+    };
     GemmArgs gu;
     memset(&gu, 0, sizeof(gu));
     gu.mode = lo ? 3 : 0;
@@ -1697,14 +1776,14 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         gu.NT = L.I / 128;
         gu.tiles = stl;
         gu.n_mtiles = nstl;
-        e = lo ? launch(fn(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs, &p->tmQgu, &p->tmSgu, &gu, kThreadsSw)
-               : launch(fn(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs, &p->tmQgu, &p->tmSgu, &gu, kThreadsSw);
+        e = lo ? launch_sw(fn(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs, &p->tmXs8, &p->tmQgu4, &p->tmSgu4, &gu)
+               : launch_sw(fn(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs, &p->tmXs8, &p->tmQgu4, &p->tmSgu4, &gu);
         if (e != cudaSuccess) return e;
         mark(1);
         dn.NT = L.d / 256;
         dn.tiles = stl;
         dn.n_mtiles = nstl;
-        e = launch(fn(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs, &p->tmQdn, &p->tmSdn, &dn, kThreadsSw);
+        e = launch_sw(fn(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs, &p->tmHs8, &p->tmQdn4, &p->tmSdn4, &dn);
         if (e != cudaSuccess) return e;
     } else {
         gu.NT = L.I / 128;
