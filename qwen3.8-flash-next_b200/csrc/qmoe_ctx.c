@@ -54,6 +54,7 @@ struct qmoe_ctx {
     /* hyper-connection workspaces, [max_tokens] rows of hc_lr / hc_n / d values */
     float *hc_W, *hc_R, *hc_INJ, *hc_mixed, *hc_y;
     unsigned long long *hc_sync; /* the one-token pre-pass's grid-barrier counter */
+    void *hc_dsync;              /* the decode kernel's counter and exchange area in hc_pre launches */
     int hc_lr, hc_n;
     int max_speculative;      /* their cap (ExpertStore._max_speculative) */
     /* device error word and output share one allocation (err at 0, out at
@@ -294,6 +295,7 @@ void qmoe_destroy(qmoe_ctx *c) {
     cudaFree(c->hc_mixed);
     cudaFree(c->hc_y);
     cudaFree(c->hc_sync);
+    cudaFree(c->hc_dsync);
     cudaFreeHost(c->x_pin);
     cudaFreeHost(c->idx_pin);
     cudaFreeHost(c->wave_pin);
@@ -1674,7 +1676,9 @@ int qmoe_upload_hc(qmoe_ctx *c, int layer, const qmoe_hc_weights *w, qmoe_err *e
         if (cudaMalloc((void **)&c->hc_mixed, T * d * sizeof(float)) != cudaSuccess ||
             cudaMalloc((void **)&c->hc_y, T * d * sizeof(float)) != cudaSuccess ||
             cudaMalloc((void **)&c->hc_sync, sizeof(unsigned long long)) != cudaSuccess ||
-            cudaMemset(c->hc_sync, 0, sizeof(unsigned long long)) != cudaSuccess) {
+            cudaMemset(c->hc_sync, 0, sizeof(unsigned long long)) != cudaSuccess ||
+            cudaMalloc(&c->hc_dsync, qk_decode_sync_bytes(&c->L)) != cudaSuccess ||
+            cudaMemset(c->hc_dsync, 0, qk_decode_sync_bytes(&c->L)) != cudaSuccess) {
             seterr(err, "qmoe_upload_hc: out of device memory");
             return -1;
         }
@@ -1723,6 +1727,36 @@ int qmoe_forward_hc(qmoe_ctx *c, int layer, float *h, int n, void *stream, qmoe_
     }
     if (n == 0) return 0;
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    if (n == 1 && c->resident_all) {
+        /* one token: gated_residual in the decode kernel's prologue and the
+         * inject-add in its combine, one launch */
+        qk_fwd f;
+        fill_fwd(c, layer, c->hc_mixed, 0, 1, c->hc_y, &f);
+        f.hc_h = h;
+        f.hc_inj = c->hc_INJ;
+        f.hc_n = w->hc;
+        f.hc_pre = 1;
+        f.hc_lr = w->lowrank;
+        f.hc_norm = w->norm;
+        f.hc_down_q = w->down_q;
+        f.hc_down_s = w->down_s;
+        f.hc_down_b = w->down_b;
+        f.hc_down_bf = w->down_bf;
+        f.hc_up_q = w->up_q;
+        f.hc_up_s = w->up_s;
+        f.hc_up_b = w->up_b;
+        f.hc_up_bf = w->up_bf;
+        f.hc_inject = w->inject;
+        f.hc_w = c->hc_W;
+        f.hc_mixed = c->hc_mixed;
+        const int rc = qk_launch_decode_fused(&f, c->hc_dsync, st, 1);
+        if (rc == 0) {
+            c->last_T = 1;
+            c->stats.decode_calls++;
+            return 0;
+        }
+        if (rc != QK_FUSED_UNFIT) return kerr(rc, "decode_fused", err);
+    }
     if (kerr(qk_launch_hc_pre(w, h, n, c->hc_W, c->hc_R, c->hc_INJ, c->hc_mixed, c->hc_sync, c->err_dev,
                               c->num_sms, st),
              "hc pre", err))

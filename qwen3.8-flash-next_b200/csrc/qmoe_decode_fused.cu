@@ -29,6 +29,17 @@
 //             the routing weights and the shared gate; each output written
 //             once.
 //
+// With f.hc_pre (the hyper connection around the block, one token) the
+// kernel first computes gated_residual: every CTA stages the normed hc
+// streams (each stream's RMS in fp64) in its routed gate/up area, which is
+// idle until phase 2; CTA r < lowrank computes down-mixer row r (16 warps
+// over word ranges for q4, the canonical order's eight per-lane sums for
+// bf16), the next hc CTAs the inject weights; [grid barrier] every CTA then
+// computes the up-mixer rows and the stream mean of its d / G columns into
+// f.x; [grid barrier] phase 1 reads x from there. The combine adds inject x
+// output to every stream. These launches count four barriers and use a
+// counter of their own.
+//
 // The q4 products are the integer dot products of qmoe_dev.cuh (quant_word,
 // dot_unit_q): four dp4a per q4 word for x, six for h. The router dot keeps
 // the canonical fp64 order (router_lane) with x staged once as doubles.
@@ -70,6 +81,7 @@ struct Plan {
 __device__ __forceinline__ int part(int c, int n, int G) { return (c * n) / G; }
 
 // x (bf16 or fp32) word t: elements 8t .. 8t + 7
+template <bool HC>
 __device__ __forceinline__ void load_x_word(const qk_fwd &f, int t, float (&v)[8]) {
     if (f.x_bf16) {
         const uint4 w = reinterpret_cast<const uint4 *>(f.x)[t];
@@ -77,9 +89,29 @@ __device__ __forceinline__ void load_x_word(const qk_fwd &f, int t, float (&v)[8
         v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
     } else {
         const float4 *p = reinterpret_cast<const float4 *>(f.x) + 2 * t;
-        const float4 a = p[0], b = p[1];
+        // written by this launch's CTAs (hc_pre): past L1
+        const float4 a = HC ? __ldcg(p) : p[0], b = HC ? __ldcg(p + 1) : p[1];
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     }
+}
+
+constexpr int kHcVals = 16;  // hc_pre: h values per thread (hc*d <= 16 * kThreads, d % kThreads == 0)
+
+// Up-mixer row `row` (lowrank 64, one q4 group: the words and the group's
+// scale and bias already in registers) times w: the arithmetic of
+// qmoe_hc.cu's up_row for one group.
+__device__ __forceinline__ float hc_up1(const uint32_t (&uw)[8], float sg, float bg, bool has_b,
+                                        const float *s_w) {
+    float xq = 0.f, xs = 0.f;
+    for (int i2 = 0; i2 < 64; ++i2) xs += s_w[i2];
+#pragma unroll
+    for (int wd = 0; wd < 8; ++wd)
+#pragma unroll
+        for (int bb = 0; bb < 8; ++bb)
+            xq = fmaf(s_w[8 * wd + bb], static_cast<float>((uw[wd] >> (4 * bb)) & 0xFu), xq);
+    float u = fmaf(sg, xq, 0.f);
+    if (has_b) u = fmaf(bg, xs, u);
+    return u;
 }
 
 // One h-row of gate/up from a staged slot row: h = SiLU(gate . x) * (up . x).
@@ -111,11 +143,12 @@ __device__ __forceinline__ float gateup_row(const uint8_t *row, const qk_layout 
     return (pg / (1.0f + expf(-pg))) * pu;
 }
 
-template <int UPL, int LPR>
+template <int UPL, int LPR, bool HC>
 __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
                                                               unsigned long long *sync) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bar[2 + kMaxChunks];  // 0: prologue, 1: down rows, 2..: chunks
+    __shared__ uint64_t s_hcbar;              // hc_pre: the down-mixer row or inject stream
     __shared__ int s_ok;
     __shared__ int s_chunk0[kMaxChunks + 1];  // first routed row (CTA-local) of each chunk
     __shared__ int s_nchunks;
@@ -167,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     const uint32_t b_sdown = static_cast<uint32_t>((or1 - or0) * L.d_row);
     const uint32_t b_slots = static_cast<uint32_t>(E * 4);
     if (tid < 2 + kMaxChunks) mbar_init(&bar[tid], 1);
+    if (tid == kThreads - 1) mbar_init(&s_hcbar, 1);
     // the prologue barrier's byte count before any of its copies is issued
     if (tid == 0) mbar_expect_tx(&bar[0], b_router + b_sgu + b_sdown + b_slots);
     __syncthreads();
@@ -208,17 +242,190 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
             s_nchunks = n;
         }
     }
+    // hc_pre: this CTA's down-mixer row or inject stream into shared memory
+    // (after the normed streams), and the up-mixer words of its columns into
+    // registers, before waiting for the previous kernel
+    const int hd = HC ? f.hc_n * d : 0;
+    float *hc_x = reinterpret_cast<float *>(sm_rgu);  // [hd] normed streams
+    uint8_t *hc_row = sm_rgu + static_cast<size_t>(hd) * 4;
+    const bool hc_q4 = HC && c < f.hc_lr && f.hc_down_q;
+    const bool hc_canon = HC && !hc_q4 && c < f.hc_lr + f.hc_n;
+    const int hc_i0 = part(c, d, G), hc_nc = part(c + 1, d, G) - hc_i0;
+    const bool hc_urow = HC && tid < f.hc_n * hc_nc;
+    const int hc_uc = hc_urow ? tid / hc_nc : 0;
+    const size_t hc_ui = static_cast<size_t>(hc_uc) * d + hc_i0 + (hc_urow ? tid - hc_uc * hc_nc : 0);
+    uint32_t hc_uw[8];
+    float hc_usg = 0.f, hc_ubg = 0.f;
+    float hc_nv[kHcVals];
+    if constexpr (HC) {
+        if (tid == 0 && (hc_q4 || hc_canon)) {
+            uint32_t bytes;
+            if (hc_q4) {
+                const uint32_t qb = static_cast<uint32_t>(hd / 2), sb = static_cast<uint32_t>(hd / 32);
+                bytes = qb + sb + (f.hc_down_b ? sb : 0u);
+                mbar_expect_tx(&s_hcbar, bytes);
+                bulk_load(hc_row, f.hc_down_q + static_cast<size_t>(c) * (hd / 8), qb, &s_hcbar);
+                bulk_load(hc_row + qb, f.hc_down_s + static_cast<size_t>(c) * (hd / 64), sb, &s_hcbar);
+                if (f.hc_down_b)
+                    bulk_load(hc_row + qb + sb, f.hc_down_b + static_cast<size_t>(c) * (hd / 64), sb, &s_hcbar);
+            } else {
+                const uint16_t *src = c >= f.hc_lr ? f.hc_inject + static_cast<size_t>(c - f.hc_lr) * hd
+                                                   : f.hc_down_bf + static_cast<size_t>(c) * hd;
+                bytes = static_cast<uint32_t>(hd * 2);
+                mbar_expect_tx(&s_hcbar, bytes);
+                bulk_load(hc_row, src, bytes, &s_hcbar);
+            }
+        }
+        if (hc_urow && f.hc_up_q) {
+            const uint4 qa = *reinterpret_cast<const uint4 *>(f.hc_up_q + hc_ui * 8);
+            const uint4 qb = *reinterpret_cast<const uint4 *>(f.hc_up_q + hc_ui * 8 + 4);
+            hc_uw[0] = qa.x, hc_uw[1] = qa.y, hc_uw[2] = qa.z, hc_uw[3] = qa.w;
+            hc_uw[4] = qb.x, hc_uw[5] = qb.y, hc_uw[6] = qb.z, hc_uw[7] = qb.w;
+            hc_usg = bf16lo(static_cast<uint32_t>(f.hc_up_s[hc_ui]));
+            hc_ubg = f.hc_up_b ? bf16lo(static_cast<uint32_t>(f.hc_up_b[hc_ui])) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kHcVals; ++u) {
+            const int kk = u * kThreads + tid;
+            hc_nv[u] = kk < hd ? f.hc_norm[kk] : 0.f;
+        }
+    }
     STAMP(24);
     pdl_wait();
-    // Grid barriers: every launch adds 2G to the counter (each CTA arrives
-    // twice), so it starts at a multiple of 2G; when this CTA reads it, at
+    // Grid barriers: every launch adds nb G to the counter (each CTA arrives
+    // nb times: 2, or 4 with hc_pre, whose launches use a counter of their
+    // own), so it starts at a multiple of nb G; when this CTA reads it, at
     // most G - 1 arrivals of this launch can have happened (the first
     // barrier needs this CTA), so rounding down gives the launch's base.
     // (Read by the last thread, which stages no x: x's loads go out at once.)
-    if (tid == kThreads - 1) s_base = ld_acquire64(sync) / (2ull * G) * (2ull * G);
+    const unsigned long long nbG = (HC ? 4ull : 2ull) * G;
+    const unsigned long long boff = HC ? 2ull * G : 0ull;  // the decode barriers' offset
+    if (tid == kThreads - 1) s_base = ld_acquire64(sync) / nbG * nbG;
     float *lg = reinterpret_cast<float *>(sync + kSyncWords);  // [E + 1] logits
     float *hf = lg + ((E + 1 + 3) & ~3);                       // [S * I] h
     STAMP(1);
+
+    if constexpr (HC) {
+        // ---- gated_residual: h -> each stream's 1/rms (fp64 sum of squares,
+        // the thread's values in ascending order, then the warps in order)
+        double *s_ss = reinterpret_cast<double *>(hc_row + 16384 + 1024);  // [kWarps][8]
+        double *s_acc = s_ss + kWarps * 8;                                  // [8][32]
+        float *s_part = reinterpret_cast<float *>(s_acc + 8 * 32);          // [kWarps]
+        float *s_r = s_part + kWarps;                                       // [8]
+        float *s_w = s_r + 8;                                               // [lowrank]
+        float *s_m = s_w + f.hc_lr;                                         // [8][32]
+        const int upc = d / kThreads;  // h values of a stream per thread
+        float hv[kHcVals];
+#pragma unroll
+        for (int u = 0; u < kHcVals; ++u) {
+            const int kk = u * kThreads + tid;
+            hv[u] = kk < hd ? f.hc_h[kk] : 0.f;
+        }
+        for (int sc = 0; sc < f.hc_n; ++sc) {
+            double ss = 0.0;
+#pragma unroll
+            for (int u = 0; u < kHcVals; ++u)
+                if (u >= sc * upc && u < (sc + 1) * upc)
+                    ss = fma(static_cast<double>(hv[u]), static_cast<double>(hv[u]), ss);
+            ss = warp_sum_butterfly(ss);
+            if (lane == 0) s_ss[warp * 8 + sc] = ss;
+        }
+        __syncthreads();
+        if (tid < f.hc_n) {
+            double tot = 0.0;
+            for (int w = 0; w < kWarps; w += 2) tot += s_ss[w * 8 + tid] + s_ss[(w + 1) * 8 + tid];
+            s_r[tid] = 1.0f / sqrtf(static_cast<float>(tot) / static_cast<float>(d) + 1e-6f);
+        }
+        __syncthreads();
+        for (int sc = 0; sc < f.hc_n; ++sc) {
+            const float rc = s_r[sc];
+#pragma unroll
+            for (int u = 0; u < kHcVals; ++u)
+                if (u >= sc * upc && u < (sc + 1) * upc) hc_x[u * kThreads + tid] = hv[u] * rc * hc_nv[u];
+        }
+        bool okh = true;
+        if ((hc_q4 || hc_canon) && !mbar_wait(&s_hcbar, 0)) okh = false;
+        okh = __syncthreads_and(okh) != 0;
+        if (!okh && tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
+        const float inv_hc = 1.0f / static_cast<float>(f.hc_n);
+        if (okh && hc_q4) {
+            // down-mixer row c: warp w takes words [w nw / 16, (w + 1) nw / 16)
+            const int nw = hd / 8;
+            const uint32_t *q = reinterpret_cast<const uint32_t *>(hc_row);
+            const uint16_t *scl = reinterpret_cast<const uint16_t *>(hc_row + hd / 2);
+            const uint16_t *bia = f.hc_down_b ? scl + hd / 64 : nullptr;
+            float acc = 0.f;
+            for (int wi = warp * nw / kWarps + lane; wi < (warp + 1) * nw / kWarps; wi += 32) {
+                const uint32_t v = q[wi];
+                const float4 x0 = *reinterpret_cast<const float4 *>(hc_x + 8 * wi);
+                const float4 x1 = *reinterpret_cast<const float4 *>(hc_x + 8 * wi + 4);
+                const float xs8[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                float xq = 0.f, xs = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    xq = fmaf(xs8[i], static_cast<float>((v >> (4 * i)) & 0xFu), xq);
+                    xs += xs8[i];
+                }
+                acc = fmaf(bf16lo(static_cast<uint32_t>(scl[wi / 8])), xq, acc);
+                if (bia) acc = fmaf(bf16lo(static_cast<uint32_t>(bia[wi / 8])), xs, acc);
+            }
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(QK_FULL, acc, off);
+            if (lane == 0) s_part[warp] = acc;
+            __syncthreads();
+            if (tid == 0) {
+                float v = 0.f;
+                for (int w = 0; w < kWarps; ++w) v += s_part[w];
+                v *= inv_hc;
+                f.hc_w[c] = v / (1.0f + expf(-v));
+            }
+        } else if (okh && hc_canon) {
+            // the canonical order: warp j < 8 forms every lane's sum number j
+            const uint16_t *wr = reinterpret_cast<const uint16_t *>(hc_row);
+            if (warp < 8) {
+                double acc = 0.0;
+                for (int base = 0; base < hd; base += 256) {
+                    const int kk = base + 8 * lane + warp;
+                    if (kk < hd) acc = fma(static_cast<double>(hc_x[kk]), bf16_to_f64(wr[kk]), acc);
+                }
+                s_acc[warp * 32 + lane] = acc;
+            }
+            __syncthreads();
+            if (warp == 0) {
+                const double* a = s_acc + lane;
+                const double fo = ((a[0] + a[32]) + (a[64] + a[96])) + ((a[128] + a[160]) + (a[192] + a[224]));
+                const float v = static_cast<float>(warp_sum_butterfly(fo));
+                if (lane == 0) {
+                    if (c >= f.hc_lr) {
+                        f.hc_inj[c - f.hc_lr] = 2.0f / (1.0f + expf(-(v * inv_hc)));
+                    } else {
+                        const float u = v * inv_hc;
+                        f.hc_w[c] = u / (1.0f + expf(-u));
+                    }
+                }
+            }
+        }
+        const unsigned long long hbase = s_base;  // (read after the CTA barriers above)
+        grid_arrive(sync);
+        grid_wait(sync, hbase + G, f.err);
+        // ---- the up-mixer rows and the stream mean of columns [i0, i0 + nc)
+        for (int j = tid; j < f.hc_lr; j += kThreads) s_w[j] = __ldcg(f.hc_w + j);
+        __syncthreads();
+        if (hc_urow) {
+            // (make_plan: a q4 up mixer with lowrank 64)
+            const float u = hc_up1(hc_uw, hc_usg, hc_ubg, f.hc_up_b != nullptr, s_w);
+            const float tmp = 1.0f / (1.0f + expf(-u));
+            s_m[hc_uc * 32 + (tid - hc_uc * hc_nc)] = tmp * hc_x[hc_ui];
+        }
+        __syncthreads();
+        if (tid < hc_nc) {
+            float acc = 0.f;
+            for (int sc = 0; sc < f.hc_n; ++sc) acc += s_m[sc * 32 + tid];
+            f.hc_mixed[hc_i0 + tid] = acc / static_cast<float>(f.hc_n);
+        }
+        grid_arrive(sync);
+        grid_wait(sync, hbase + 2ull * G, f.err);
+    }
 
     // ---- phase 1: x -> fp64 in shared memory for the router; thread t owns
     // the q4 word position t (elements 8t .. 8t + 7) and keeps its 8 values
@@ -228,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
 #pragma unroll
     for (int i = 0; i < 8; ++i) xv[i] = 0.f;
     if (tid < xwn) {
-        load_x_word(f, tid, xv);
+        load_x_word<HC>(f, tid, xv);
         rx_store(rx, tid, xv);
     }
     __syncthreads();
@@ -311,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         }
     }
     STAMP(13);
-    grid_wait(sync, base + G, f.err);
+    grid_wait(sync, base + boff + G, f.err);
     STAMP(4);
 
     // ---- phase 2: top-k over the whole CTA. Every warp's largest key goes to
@@ -464,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     }
     ok1 = __syncthreads_and(ok1) != 0;  // CTA-uniform from here on
     STAMP(8);
-    grid_arrive_wait(sync, base + 2ull * G, f.err);  // every CTA, on every path
+    grid_arrive_wait(sync, base + boff + 2ull * G, f.err);  // every CTA, on every path
     STAMP(9);
     // every CTA of this grid has arrived, so all of them are resident: a
     // dependent launch may take SMs as they free up
@@ -564,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         if (f.hc_h) {  // the hyper connection's inject-add (k_hc_inject's arithmetic)
             for (int sc = 0; sc < f.hc_n; ++sc) {
                 float *hp = f.hc_h + static_cast<size_t>(sc) * L.d + or0 + rl;
-                *hp = fmaf(f.hc_inj[sc], acc, *hp);
+                *hp = fmaf(__ldcg(f.hc_inj + sc), acc, *hp);
             }
         }
     }
@@ -592,6 +799,17 @@ bool make_plan(const qk_fwd *f, Plan *p) {
     // chunk count bound: every expert boundary inside the range adds one
     const int chunks = (p->gr_max + kChunkRows - 1) / kChunkRows + (p->gr_max + L.I - 1) / L.I + 1;
     if (chunks > kMaxChunks) return false;
+    if (f->hc_pre) {
+        // gated_residual in the prologue: h values per thread, one item per
+        // CTA, columns per CTA, a q4 up mixer of one group, the staging in
+        // the routed gate/up area (normed streams, the item's row, scratch)
+        const int hd = f->hc_n * L.d;
+        if (f->hc_n < 1 || f->hc_n > 8 || L.d % kThreads || hd > kHcVals * kThreads) return false;
+        if (G < f->hc_lr + f->hc_n || L.d > 32 * G || !f->hc_up_q || f->hc_lr != 64) return false;
+        const int need = hd * 4 + 16384 + 1024 + kWarps * 8 * 8 + 8 * 32 * 8 + kWarps * 4 + 8 * 4 +
+                         f->hc_lr * 4 + 8 * 32 * 4;
+        if (hd * 2 > 16384 || need > ((L.k * L.I + G - 1) / G) * L.gu_row) return false;
+    }
     int off = 0;
     p->off_router = off;
     off = align128(off + p->rr_max * L.d * 2);
@@ -615,25 +833,26 @@ bool make_plan(const qk_fwd *f, Plan *p) {
     return off <= kFusedSmemMax;
 }
 
-template <int UPL, int LPR>
+template <int UPL, int LPR, bool HC = false>
 const void *fused_fn() {
-    return reinterpret_cast<const void *>(&k_decode_fused<UPL, LPR>);
+    return reinterpret_cast<const void *>(&k_decode_fused<UPL, LPR, HC>);
 }
 
 // instantiated shapes: d in (1024, 2048] with I = 512, and d <= 1024 with
 // I = 128 (E <= 1024, group 64 for both)
-const void *pick(const qk_layout &L) {
+// (the gated_residual prologue, hc_pre, is instantiated for the first shape)
+const void *pick(const qk_layout &L, bool hc) {
     const int nunits = L.d / 32, lpr = L.I / 32;
     if (L.E > 1024 || L.g != 64) return nullptr;
-    if (nunits <= 64 && nunits > 32 && lpr == 16) return fused_fn<2, 16>();
-    if (nunits <= 32 && lpr == 4) return fused_fn<1, 4>();
+    if (nunits <= 64 && nunits > 32 && lpr == 16) return hc ? fused_fn<2, 16, true>() : fused_fn<2, 16>();
+    if (nunits <= 32 && lpr == 4 && !hc) return fused_fn<1, 4>();
     return nullptr;
 }
 
 }  // namespace
 
 int qk_prepare_fused() {
-    const void *fns[] = {fused_fn<2, 16>(), fused_fn<1, 4>()};
+    const void *fns[] = {fused_fn<2, 16>(), fused_fn<1, 4>(), fused_fn<2, 16, true>()};
     for (const void *fn : fns) {
         cudaError_t e =
             cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kFusedSmemMax);
@@ -650,7 +869,7 @@ extern "C" size_t qk_decode_sync_bytes(const qk_layout *L) {
 extern "C" int qk_launch_decode_fused(const qk_fwd *f, void *sync, void *stream, int pdl) {
     if (f->T != 1) return QK_FUSED_UNFIT;
     Plan p;
-    const void *fn = pick(f->L);
+    const void *fn = pick(f->L, f->hc_pre != 0);
     if (!fn || !make_plan(f, &p) || (f->L.E & 3)) return QK_FUSED_UNFIT;
     qk_fwd a = *f;
     unsigned long long *ctr = static_cast<unsigned long long *>(sync);

@@ -74,8 +74,17 @@ typedef struct {
     /* the hyper connection's inject-add in the decode kernel's combine
      * (T = 1): hc_h[c, :] += hc_inj[c] * out for c < hc_n; hc_h NULL: none */
     float *hc_h;
-    const float *hc_inj;
+    float *hc_inj;
     int hc_n;
+    /* hc_pre: the decode kernel also computes gated_residual from hc_h
+     * first (its prologue, two more grid barriers, a counter of its own):
+     * the inject weights into hc_inj, the low-rank w into hc_w and the block
+     * input into x (= hc_mixed, fp32). The layer's device weights: */
+    int hc_pre, hc_lr;
+    const float *hc_norm;
+    const uint32_t *hc_down_q, *hc_up_q;
+    const uint16_t *hc_down_s, *hc_down_b, *hc_down_bf, *hc_up_s, *hc_up_b, *hc_up_bf, *hc_inject;
+    float *hc_w, *hc_mixed;
 } qk_fwd;
 
 /* Kernel launchers (qmoe_kernels.cu). Each returns a cudaError_t as int.
