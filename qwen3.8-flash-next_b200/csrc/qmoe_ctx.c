@@ -1706,6 +1706,57 @@ int qmoe_upload_hc(qmoe_ctx *c, int layer, const qmoe_hc_weights *w, qmoe_err *e
     return 0;
 }
 
+/* The one-token hyper-connection step as one decode-kernel launch
+ * (QK_FUSED_UNFIT when the kernel's plan does not cover the shape). */
+static int launch_hc_fused(qmoe_ctx *c, int layer, float *h, cudaStream_t st, unsigned long long *ptimes,
+                           int pdl) {
+    const qk_hc_dev *w = &c->layers[layer].hc;
+    qk_fwd f;
+    fill_fwd(c, layer, c->hc_mixed, 0, 1, c->hc_y, &f);
+    f.ptimes = ptimes;
+    f.hc_h = h;
+    f.hc_inj = c->hc_INJ;
+    f.hc_n = w->hc;
+    f.hc_pre = 1;
+    f.hc_lr = w->lowrank;
+    f.hc_norm = w->norm;
+    f.hc_down_q = w->down_q;
+    f.hc_down_s = w->down_s;
+    f.hc_down_b = w->down_b;
+    f.hc_down_bf = w->down_bf;
+    f.hc_up_q = w->up_q;
+    f.hc_up_s = w->up_s;
+    f.hc_up_b = w->up_b;
+    f.hc_up_bf = w->up_bf;
+    f.hc_inject = w->inject;
+    f.hc_w = c->hc_W;
+    f.hc_mixed = c->hc_mixed;
+    return qk_launch_decode_fused(&f, c->hc_dsync, st, pdl);
+}
+
+/* Diagnostics: the phase timestamps of n_tokens back-to-back one-token
+ * hyper-connection steps on h [n_tokens, hc*d] (as qmoe__phase_times_seq). */
+int qmoe__phase_times_hc(qmoe_ctx *c, int layer, float *h, int n_tokens, unsigned long long *out_ns,
+                         int max_ctas) {
+    if (!c || !c->resident_all || layer < 0 || layer >= c->cfg.num_layers || !c->layers[layer].ready ||
+        !c->layers[layer].hc.hc || n_tokens < 1)
+        return -1;
+    const size_t per = (size_t)c->num_sms * 32;
+    const size_t row = (size_t)c->layers[layer].hc.hc * c->L.d;
+    unsigned long long *buf = NULL;
+    if (cudaMalloc((void **)&buf, per * n_tokens * sizeof(unsigned long long)) != cudaSuccess) return -1;
+    int rc = cudaMemset(buf, 0, per * n_tokens * sizeof(unsigned long long));
+    for (int t = 0; rc == 0 && t < n_tokens; t++)
+        rc = launch_hc_fused(c, layer, h + row * t, c->stream, buf + per * t, t > 0);
+    if (rc == 0) rc = cudaStreamSynchronize(c->stream);
+    const int n = max_ctas < c->num_sms ? max_ctas : c->num_sms;
+    for (int t = 0; rc == 0 && t < n_tokens; t++)
+        rc = cudaMemcpy(out_ns + (size_t)t * max_ctas * 32, buf + per * t,
+                        (size_t)n * 32 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(buf);
+    return rc == 0 ? c->num_sms : -1;
+}
+
 int qmoe_forward_hc(qmoe_ctx *c, int layer, float *h, int n, void *stream, qmoe_err *err) {
     if (err) err->msg[0] = 0;
     if (!c || !h || layer < 0 || layer >= c->cfg.num_layers) {
@@ -1730,26 +1781,7 @@ int qmoe_forward_hc(qmoe_ctx *c, int layer, float *h, int n, void *stream, qmoe_
     if (n == 1 && c->resident_all) {
         /* one token: gated_residual in the decode kernel's prologue and the
          * inject-add in its combine, one launch */
-        qk_fwd f;
-        fill_fwd(c, layer, c->hc_mixed, 0, 1, c->hc_y, &f);
-        f.hc_h = h;
-        f.hc_inj = c->hc_INJ;
-        f.hc_n = w->hc;
-        f.hc_pre = 1;
-        f.hc_lr = w->lowrank;
-        f.hc_norm = w->norm;
-        f.hc_down_q = w->down_q;
-        f.hc_down_s = w->down_s;
-        f.hc_down_b = w->down_b;
-        f.hc_down_bf = w->down_bf;
-        f.hc_up_q = w->up_q;
-        f.hc_up_s = w->up_s;
-        f.hc_up_b = w->up_b;
-        f.hc_up_bf = w->up_bf;
-        f.hc_inject = w->inject;
-        f.hc_w = c->hc_W;
-        f.hc_mixed = c->hc_mixed;
-        const int rc = qk_launch_decode_fused(&f, c->hc_dsync, st, 1);
+        const int rc = launch_hc_fused(c, layer, h, st, NULL, 1);
         if (rc == 0) {
             c->last_T = 1;
             c->stats.decode_calls++;

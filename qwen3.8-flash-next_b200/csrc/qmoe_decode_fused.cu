@@ -100,8 +100,9 @@ constexpr int kHcVals = 16;  // hc_pre: h values per thread (hc*d <= 16 * kThrea
 // Up-mixer row `row` (lowrank 64, one q4 group: the words and the group's
 // scale and bias already in registers) times w: the arithmetic of
 // qmoe_hc.cu's up_row for one group.
-__device__ __forceinline__ float hc_up1(const uint32_t (&uw)[8], float sg, float bg, bool has_b,
+__device__ __forceinline__ float hc_up1(uint4 qa, uint4 qb, float sg, float bg, bool has_b,
                                         const float *s_w) {
+    const uint32_t uw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     float xq = 0.f, xs = 0.f;
     for (int i2 = 0; i2 < 64; ++i2) xs += s_w[i2];
 #pragma unroll
@@ -254,10 +255,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
     const bool hc_urow = HC && tid < f.hc_n * hc_nc;
     const int hc_uc = hc_urow ? tid / hc_nc : 0;
     const size_t hc_ui = static_cast<size_t>(hc_uc) * d + hc_i0 + (hc_urow ? tid - hc_uc * hc_nc : 0);
-    uint32_t hc_uw[8];
-    float hc_usg = 0.f, hc_ubg = 0.f;
+    uint4 hc_ua = make_uint4(0u, 0u, 0u, 0u), hc_ub = hc_ua;
+    uint16_t hc_usb = 0, hc_ubb = 0;
     float hc_nv[kHcVals];
     if constexpr (HC) {
+        STAMP(18);
         if (tid == 0 && (hc_q4 || hc_canon)) {
             uint32_t bytes;
             if (hc_q4) {
@@ -277,12 +279,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
             }
         }
         if (hc_urow && f.hc_up_q) {
-            const uint4 qa = *reinterpret_cast<const uint4 *>(f.hc_up_q + hc_ui * 8);
-            const uint4 qb = *reinterpret_cast<const uint4 *>(f.hc_up_q + hc_ui * 8 + 4);
-            hc_uw[0] = qa.x, hc_uw[1] = qa.y, hc_uw[2] = qa.z, hc_uw[3] = qa.w;
-            hc_uw[4] = qb.x, hc_uw[5] = qb.y, hc_uw[6] = qb.z, hc_uw[7] = qb.w;
-            hc_usg = bf16lo(static_cast<uint32_t>(f.hc_up_s[hc_ui]));
-            hc_ubg = f.hc_up_b ? bf16lo(static_cast<uint32_t>(f.hc_up_b[hc_ui])) : 0.f;
+            hc_ua = *reinterpret_cast<const uint4 *>(f.hc_up_q + hc_ui * 8);
+            hc_ub = *reinterpret_cast<const uint4 *>(f.hc_up_q + hc_ui * 8 + 4);
+            hc_usb = f.hc_up_s[hc_ui];  // converted after the wait: no use of a load before it
+            hc_ubb = f.hc_up_b ? f.hc_up_b[hc_ui] : 0;
         }
 #pragma unroll
         for (int u = 0; u < kHcVals; ++u) {
@@ -314,39 +314,55 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         float *s_r = s_part + kWarps;                                       // [8]
         float *s_w = s_r + 8;                                               // [lowrank]
         float *s_m = s_w + f.hc_lr;                                         // [8][32]
-        const int upc = d / kThreads;  // h values of a stream per thread
+        // d = 4 kThreads (make_plan): values u = 4 sc .. 4 sc + 3 of a thread
+        // belong to stream sc (hc <= 4)
         float hv[kHcVals];
 #pragma unroll
         for (int u = 0; u < kHcVals; ++u) {
             const int kk = u * kThreads + tid;
             hv[u] = kk < hd ? f.hc_h[kk] : 0.f;
         }
-        for (int sc = 0; sc < f.hc_n; ++sc) {
-            double ss = 0.0;
+        double ss[4];
 #pragma unroll
-            for (int u = 0; u < kHcVals; ++u)
-                if (u >= sc * upc && u < (sc + 1) * upc)
-                    ss = fma(static_cast<double>(hv[u]), static_cast<double>(hv[u]), ss);
-            ss = warp_sum_butterfly(ss);
-            if (lane == 0) s_ss[warp * 8 + sc] = ss;
+        for (int sc = 0; sc < 4; ++sc) {
+            ss[sc] = 0.0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const double v = f32_to_f64(hv[4 * sc + j]);
+                ss[sc] = fma(v, v, ss[sc]);
+            }
         }
+        STAMP(19);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+            for (int sc = 0; sc < 4; ++sc) ss[sc] += __shfl_xor_sync(QK_FULL, ss[sc], off);
+        if (lane == 0)
+#pragma unroll
+            for (int sc = 0; sc < 4; ++sc) s_ss[warp * 8 + sc] = ss[sc];
         __syncthreads();
+        STAMP(22);
         if (tid < f.hc_n) {
             double tot = 0.0;
             for (int w = 0; w < kWarps; w += 2) tot += s_ss[w * 8 + tid] + s_ss[(w + 1) * 8 + tid];
             s_r[tid] = 1.0f / sqrtf(static_cast<float>(tot) / static_cast<float>(d) + 1e-6f);
         }
         __syncthreads();
-        for (int sc = 0; sc < f.hc_n; ++sc) {
-            const float rc = s_r[sc];
 #pragma unroll
-            for (int u = 0; u < kHcVals; ++u)
-                if (u >= sc * upc && u < (sc + 1) * upc) hc_x[u * kThreads + tid] = hv[u] * rc * hc_nv[u];
+        for (int sc = 0; sc < 4; ++sc) {
+            if (sc < f.hc_n) {
+                const float rc = s_r[sc];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    hc_x[(4 * sc + j) * kThreads + tid] = hv[4 * sc + j] * rc * hc_nv[4 * sc + j];
+            }
         }
+        STAMP(27);
         bool okh = true;
         if ((hc_q4 || hc_canon) && !mbar_wait(&s_hcbar, 0)) okh = false;
         okh = __syncthreads_and(okh) != 0;
         if (!okh && tid == 0) atomicOr(f.err, QK_ERR_TIMEOUT_COPY);
+        STAMP(23);
         const float inv_hc = 1.0f / static_cast<float>(f.hc_n);
         if (okh && hc_q4) {
             // down-mixer row c: warp w takes words [w nw / 16, (w + 1) nw / 16)
@@ -380,21 +396,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
                 f.hc_w[c] = v / (1.0f + expf(-v));
             }
         } else if (okh && hc_canon) {
-            // the canonical order: warp j < 8 forms every lane's sum number j
+            // inject weights (or a dense bf16 down row): fp32 products, each
+            // thread's over k = tid + 512 m in order, then the lanes' tree
+            // and the warps in order (within the tolerance of the oracle's
+            // canonical fp64 dot, which took about 3 us on eight warps here)
             const uint16_t *wr = reinterpret_cast<const uint16_t *>(hc_row);
-            if (warp < 8) {
-                double acc = 0.0;
-                for (int base = 0; base < hd; base += 256) {
-                    const int kk = base + 8 * lane + warp;
-                    if (kk < hd) acc = fma(static_cast<double>(hc_x[kk]), bf16_to_f64(wr[kk]), acc);
-                }
-                s_acc[warp * 32 + lane] = acc;
-            }
+            float acc = 0.f;
+            for (int kk = tid; kk < hd; kk += kThreads) acc = fmaf(hc_x[kk], bf16lo(wr[kk]), acc);
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(QK_FULL, acc, off);
+            if (lane == 0) s_part[warp] = acc;
             __syncthreads();
             if (warp == 0) {
-                const double* a = s_acc + lane;
-                const double fo = ((a[0] + a[32]) + (a[64] + a[96])) + ((a[128] + a[160]) + (a[192] + a[224]));
-                const float v = static_cast<float>(warp_sum_butterfly(fo));
+                float v = 0.f;
+                for (int w = 0; w < kWarps; ++w) v += s_part[w];
                 if (lane == 0) {
                     if (c >= f.hc_lr) {
                         f.hc_inj[c - f.hc_lr] = 2.0f / (1.0f + expf(-(v * inv_hc)));
@@ -405,15 +420,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
                 }
             }
         }
+        STAMP(17);
         const unsigned long long hbase = s_base;  // (read after the CTA barriers above)
         grid_arrive(sync);
         grid_wait(sync, hbase + G, f.err);
+        STAMP(28);
         // ---- the up-mixer rows and the stream mean of columns [i0, i0 + nc)
         for (int j = tid; j < f.hc_lr; j += kThreads) s_w[j] = __ldcg(f.hc_w + j);
         __syncthreads();
         if (hc_urow) {
             // (make_plan: a q4 up mixer with lowrank 64)
-            const float u = hc_up1(hc_uw, hc_usg, hc_ubg, f.hc_up_b != nullptr, s_w);
+            const float u = hc_up1(hc_ua, hc_ub, bf16lo(hc_usb), bf16lo(hc_ubb), f.hc_up_b != nullptr, s_w);
             const float tmp = 1.0f / (1.0f + expf(-u));
             s_m[hc_uc * 32 + (tid - hc_uc * hc_nc)] = tmp * hc_x[hc_ui];
         }
@@ -425,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_fused(qk_fwd f, Plan p,
         }
         grid_arrive(sync);
         grid_wait(sync, hbase + 2ull * G, f.err);
+        STAMP(29);
     }
 
     // ---- phase 1: x -> fp64 in shared memory for the router; thread t owns
@@ -804,7 +822,7 @@ bool make_plan(const qk_fwd *f, Plan *p) {
         // CTA, columns per CTA, a q4 up mixer of one group, the staging in
         // the routed gate/up area (normed streams, the item's row, scratch)
         const int hd = f->hc_n * L.d;
-        if (f->hc_n < 1 || f->hc_n > 8 || L.d % kThreads || hd > kHcVals * kThreads) return false;
+        if (f->hc_n < 1 || f->hc_n > 4 || L.d != 4 * kThreads) return false;
         if (G < f->hc_lr + f->hc_n || L.d > 32 * G || !f->hc_up_q || f->hc_lr != 64) return false;
         const int need = hd * 4 + 16384 + 1024 + kWarps * 8 * 8 + 8 * 32 * 8 + kWarps * 4 + 8 * 4 +
                          f->hc_lr * 4 + 8 * 32 * 4;

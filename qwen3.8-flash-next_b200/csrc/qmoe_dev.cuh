@@ -441,6 +441,17 @@ QK_DEV double bf16_to_f64(uint32_t b) {
     return __hiloint2double(static_cast<int>(hi), 0);
 }
 
+// fp32 -> fp64 by rebuilding the IEEE fields with integer operations
+// (exponent + 1023 - 127, fraction shifted up by 29) for normal numbers;
+// zero, subnormals, infinities and NaN take the conversion instruction.
+QK_DEV double f32_to_f64(float x) {
+    const uint32_t u = __float_as_uint(x);
+    const uint32_t e = (u >> 23) & 0xFFu;
+    if (e - 1u >= 254u) return static_cast<double>(x);
+    const uint32_t hi = (u & 0x80000000u) | (((u & 0x7FFFFFFFu) >> 3) + (896u << 20));
+    return __hiloint2double(static_cast<int>(hi), static_cast<int>(u << 29));
+}
+
 // Staged x for the canonical router dot: element k = 256 i + 8 l + j (lane
 // l, j < 8) sits in double2 slot (4 i + j / 2) * 32 + l, so each lane's
 // 128-bit reads are consecutive across the warp. rx_slot gives the slot of
