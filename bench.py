@@ -390,7 +390,8 @@ HC_N, HC_LR, HC_SEED = 4, 64, 20261213
 def measure_hc(ctx, rank, reps=5, warmup=3):
     """The config-1 layer inside its hyper connection (hc 4 residual streams,
     low-rank 64 q4 mixers), decode at batch 1: TOKENS sequential
-    qmoe_forward_hc calls (gated_residual, the MoE block, the inject-add) on
+    qmoe_forward_hc calls (gated_residual, the MoE block, the inject-add: one
+    decode-kernel launch each) on
     h [TOKENS, hc*d] fp32, captured as one CUDA graph and replayed. The first
     replay's rows are the parity sample (each row depends only on its own
     input); later replays keep updating h in place."""
@@ -435,11 +436,12 @@ def measure_hc(ctx, rank, reps=5, warmup=3):
                         f"q4 mixers), decode batch 1, {TOKENS} tokens/step",
             "_h0": h0, "_out": first,
             "tokens_per_s": TOKENS / (ms / 1e3), "us_per_token": 1e3 * ms / TOKENS,
-            "gpu_launches_per_token": 2,
-            "note": "per token: k_hc_pre1 (one CTA per SM, one grid barrier: RMSNorm of the "
-                    "hc streams, the low-rank down mixer and the inject weights, then the up "
-                    "mixer and the stream mean, the block's input) and the decode kernel, whose "
-                    "combine also adds inject x its output to the hc streams; h fp32 in HBM"}
+            "gpu_launches_per_token": 1,
+            "note": "per token one decode-kernel launch: its prologue computes gated_residual "
+                    "(RMSNorm of the hc streams, the low-rank down mixer and the inject weights; "
+                    "grid barrier; the up mixer and the stream mean, the block's input; grid "
+                    "barrier), then the MoE block, whose combine also adds inject x output to "
+                    "the hc streams; h fp32 in HBM"}
 
 
 def cpu_hc_rate(h0, gpu_out, budget_s=10.0):
