@@ -474,6 +474,20 @@ def cpu_hc_rate(h0, gpu_out, budget_s=10.0):
     return r
 
 
+def exchange_label(ctx):
+    """How a connected expert-parallel context moves its rows."""
+    import ctypes
+
+    import qmoe
+    f = qmoe.lib().qmoe__ep_p2p
+    f.restype, f.argtypes = ctypes.c_int, [ctypes.c_void_p]
+    if f(ctx.h):
+        return ("peer memory over NVLink: each rank writes its rows into the owners' receive rows and "
+                "the partial rows into the token owners' return rows (CUDA IPC mappings), flags "
+                "released and acquired at system scope")
+    return "NCCL send/recv, fixed-size blocks of rows and fp32 partials"
+
+
 def measure_prefill_ep(rank, world, local, local_ctx=None, local_layer=1, reps=5, warmup=2):
     """configs[2] expert-parallel over the torchrun ranks: the 4096 tokens
     split evenly, rank g owning experts [g E/W, (g+1) E/W), qmoe_forward_ep
@@ -517,6 +531,7 @@ def measure_prefill_ep(rank, world, local, local_ctx=None, local_layer=1, reps=5
     tt = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda")
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms = float(tt.item())
+    xchg = exchange_label(ctx)
     ctx.close()
     ep_parity = None
     if local_ctx is not None:
@@ -533,7 +548,7 @@ def measure_prefill_ep(rank, world, local, local_ctx=None, local_layer=1, reps=5
     return {"workload": "config2 expert-parallel: 4096 tokens split over the ranks, Zipf(1.1)",
             "ranks": world, "tokens_per_s": PREFILL_T / (ms / 1e3), "ms_per_call": ms,
             "scaling": "strong", "timing": "CUDA events per rank, max over ranks",
-            "exchange": "NCCL send/recv all-to-all of fp16 rows and fp32 outputs",
+            "exchange": xchg,
             "ep_parity": ep_parity}
 
 
@@ -642,6 +657,7 @@ def measure_stack(rank, world, local, layers=STACK_L, reps=3, warmup=2):
     else:
         all_touched, bad = float(stats[1]), float(stats[2])
     g.close()
+    xchg = exchange_label(ctx) if world > 1 else None
     ctx.close()
     # algorithmic bytes of one step, all ranks: every rank reads the router,
     # shared gate and shared expert of every layer, and its own touched experts
@@ -662,8 +678,7 @@ def measure_stack(rank, world, local, layers=STACK_L, reps=3, warmup=2):
                                  "plus the distinct routed experts the step touches"},
             "graph_equals_eager": bad == 0.0, "weights_generated_s": synth_s,
             "timing": "one CUDA graph per rank per step, CUDA events, max over ranks",
-            "exchange": "NCCL send/recv, fixed-size blocks of fp16 rows and fp32 partials"
-                        if world > 1 else None,
+            "exchange": xchg,
             "ep_parity": ep_parity}
 
 

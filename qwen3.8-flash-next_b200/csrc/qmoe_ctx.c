@@ -103,6 +103,7 @@ struct qmoe_ctx {
     /* expert parallelism */
     int ep_world, ep_rank, ep_lo, ep_hi; /* experts [ep_lo, ep_hi) are local */
     ncclComm_t ep_comm;
+    int ep_p2p; /* the exchanges go through peer memory (qk_ep_*_p2p) */
     int32_t *ep_recv_pin;  /* streaming: pinned copy of the received rows' expert ids */
     /* MoE-only stack: the normalised layer input and the layer output */
     float *stk_xn, *stk_y; /* fp32 [max_tokens, d] each */
@@ -1836,6 +1837,115 @@ int qmoe_ep_unique_id(unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err) {
     return 0;
 }
 
+/* Every rank's bytes [len] at slot rank of all [W][len] (device), over the
+ * communicator. */
+static int ep_allgather(qmoe_ctx *c, const unsigned char *mine, unsigned char *all, size_t len, qmoe_err *err) {
+    const nccl_fns *n = nccl_api();
+    const int W = c->ep_world, me = c->ep_rank;
+    unsigned char *dev = NULL;
+    cudaError_t ce = cudaMalloc((void **)&dev, (size_t)W * len);
+    if (ce == cudaSuccess) ce = cudaMemcpy(dev + (size_t)me * len, mine, len, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        cudaFree(dev);
+        seterr(err, "qmoe_ep_connect: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    ncclResult_t r = n->group_start();
+    for (int p = 0; p < W && r == ncclSuccess; p++) {
+        if (p == me) continue;
+        r = n->send(dev + (size_t)me * len, len, ncclUint8, p, c->ep_comm, c->stream);
+        if (r == ncclSuccess) r = n->recv(dev + (size_t)p * len, len, ncclUint8, p, c->ep_comm, c->stream);
+    }
+    const ncclResult_t r2 = n->group_end();
+    if (r == ncclSuccess) r = r2;
+    ce = cudaStreamSynchronize(c->stream);
+    if (r == ncclSuccess && ce == cudaSuccess) ce = cudaMemcpy(all, dev, (size_t)W * len, cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    if (r != ncclSuccess || ce != cudaSuccess) {
+        seterr(err, "qmoe_ep_connect: exchange failed (%s)",
+               r != ncclSuccess ? n->error_string(r) : cudaGetErrorString(ce));
+        return -1;
+    }
+    return 0;
+}
+
+/* The peer-memory exchange when every rank can map every other rank's
+ * buffers (another GPU with peer access; QMOE_EP_P2P=0 keeps NCCL): the IPC
+ * handles and device ordinals travel over the communicator, then every
+ * rank reports whether it mapped all of them, and the ranks use peer memory
+ * only if all did (they must take the same path). Collective. */
+static int ep_try_p2p(qmoe_ctx *c, qmoe_err *err) {
+    enum { LEN = 5 * 64 + 8 };
+    const int W = c->ep_world, me = c->ep_rank;
+    const char *pv = getenv("QMOE_EP_P2P");
+    unsigned char mine[LEN];
+    memset(mine, 0, sizeof(mine));
+    int want = !(pv && strcmp(pv, "0") == 0) && c->prefill != NULL;
+    if (want && qk_ep_ipc_handles(c->prefill, mine) != 0) {
+        cudaGetLastError();
+        want = 0;
+    }
+    memcpy(mine + 320, &c->cfg.device, 4);
+    memcpy(mine + 324, &want, 4);
+    unsigned char *all = calloc((size_t)W, LEN);
+    if (!all) {
+        seterr(err, "qmoe_ep_connect: out of host memory");
+        return -1;
+    }
+    if (ep_allgather(c, mine, all, LEN, err)) {
+        free(all);
+        return -1;
+    }
+    int ok = 1;
+    for (int p = 0; p < W; p++) {
+        int dev, w;
+        memcpy(&dev, all + (size_t)p * LEN + 320, 4);
+        memcpy(&w, all + (size_t)p * LEN + 324, 4);
+        if (!w) ok = 0;
+        if (p == me) continue;
+        int can = 0;
+        if (dev == c->cfg.device || cudaDeviceCanAccessPeer(&can, c->cfg.device, dev) != cudaSuccess || !can)
+            ok = 0;
+    }
+    cudaGetLastError();
+    if (ok) {
+        unsigned char *h = calloc((size_t)W, 5 * 64);
+        if (!h) ok = 0;
+        for (int p = 0; h && p < W; p++) memcpy(h + (size_t)p * 5 * 64, all + (size_t)p * LEN, 5 * 64);
+        if (ok && qk_ep_p2p_open(c->prefill, h, me) != 0) {
+            cudaGetLastError();
+            ok = 0;
+        }
+        free(h);
+    }
+    free(all);
+    /* every rank's outcome: peer memory only if all mapped everything */
+    unsigned char okb[8] = {0};
+    memcpy(okb, &ok, 4);
+    unsigned char *oks = calloc((size_t)W, 8);
+    if (!oks) {
+        seterr(err, "qmoe_ep_connect: out of host memory");
+        return -1;
+    }
+    if (ep_allgather(c, okb, oks, 8, err)) {
+        free(oks);
+        return -1;
+    }
+    int all_ok = 1;
+    for (int p = 0; p < W; p++) {
+        int v;
+        memcpy(&v, oks + (size_t)p * 8, 4);
+        if (!v) all_ok = 0;
+    }
+    free(oks);
+    if (!all_ok) qk_ep_p2p_close(c->prefill);
+    c->ep_p2p = all_ok;
+    return 0;
+}
+
+/* Diagnostics: 1 when this context's exchanges go through peer memory. */
+int qmoe__ep_p2p(const qmoe_ctx *c) { return c ? c->ep_p2p : 0; }
+
 int qmoe_ep_connect(qmoe_ctx *c, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_err *err) {
     if (err) err->msg[0] = 0;
     if (!c || c->ep_world < 2) {
@@ -1855,7 +1965,7 @@ int qmoe_ep_connect(qmoe_ctx *c, const unsigned char id[QMOE_EP_ID_BYTES], qmoe_
         return -1;
     }
     NCK(n->comm_init_rank(&c->ep_comm, c->ep_world, u, c->ep_rank), "qmoe_ep_connect");
-    return 0;
+    return ep_try_p2p(c, err);
 }
 
 /* One collective forward: every rank calls it for the same layer with its
@@ -1901,10 +2011,17 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
     qk_ep_bufs b;
     qk_ep_buffers(c->prefill, &b);
     if (n > 0 && route(c, layer, &f, st, 0, NULL, err)) return -1;
+    /* the receive buffer: the own tokens in rows [0, cap), rank p's rows
+     * from cap + p cap on; x travels as given (bf16 or fp32: every rank
+     * passes the same dtype) */
+    const size_t own = cap, row = (size_t)d * (x_dtype == QMOE_BF16 ? 2 : 4);
+    if (c->ep_p2p) {
+        /* peer memory: rows written straight into their destinations */
+        if (kerr(qk_ep_dispatch_p2p(c->prefill, &f, c->ep_rank, st), "ep dispatch", err) ||
+            kerr(qk_ep_wait(c->prefill, 0, c->err_dev, st), "ep wait", err))
+            return -1;
+    } else {
     if (kerr(qk_ep_dispatch(c->prefill, &f, st), "ep dispatch", err)) return -1;
-    /* token rows with their slots out, and in (after the own n tokens);
-     * x travels as given (bf16 or fp32: every rank passes the same dtype) */
-    const size_t own = (size_t)n, row = (size_t)d * (x_dtype == QMOE_BF16 ? 2 : 4);
     NCK(nc->group_start(), "qmoe_forward_ep");
     for (int p = 0; p < W; p++) {
         const size_t so = (size_t)p * cap, ro = own + (size_t)p * cap;
@@ -1922,6 +2039,7 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
             "qmoe_forward_ep dispatch");
     }
     NCK(nc->group_end(), "qmoe_forward_ep");
+    }
     if (!c->resident_all) {
         /* streaming pool: the rows received name this rank's experts; fill
          * the missing ones before the grouped pass reads the pool */
@@ -1969,6 +2087,14 @@ int qmoe_forward_ep(qmoe_ctx *c, int layer, const void *x, int x_dtype, int n, f
         if (rc) return -1;
     }
     /* this rank's experts over the rows it received, combined per row */
+    if (c->ep_p2p) {
+        /* partial rows written straight into their owners' return rows */
+        if (kerr(qk_ep_experts_p2p(c->prefill, &f, c->nslots + layer, c->ep_rank, st), "ep experts", err) ||
+            kerr(qk_ep_wait(c->prefill, 1, c->err_dev, st), "ep wait", err))
+            return -1;
+        if (n > 0 && kerr(qk_ep_finish(c->prefill, &f, st), "ep finish", err)) return -1;
+        return 0;
+    }
     if (kerr(qk_ep_experts(c->prefill, &f, c->nslots + layer, st), "ep experts", err)) return -1;
     /* partial rows back to the ranks that own the tokens */
     NCK(nc->group_start(), "qmoe_forward_ep");

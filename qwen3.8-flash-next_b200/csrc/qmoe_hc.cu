@@ -248,27 +248,6 @@ constexpr int kPreCols = 32;      // k_hc_pre1: most d columns per CTA
 constexpr int kPreWords = 4;      // k_hc_pre1: most q4 words of a down row per lane
 constexpr int kPreH = 32;         // k_hc_pre1: h values per thread (hc*d <= 8192)
 
-// Lane `lane`'s fp64 sum number j of canon_dot (k = 256 i + 8 lane + j, i
-// ascending): the same additions in the same order as there. The weights of
-// 16 steps are loaded before their products (one memory latency per 16).
-QK_DEV double canon_part(const float *x, const uint16_t *w, int K, int lane, int j) {
-    double acc = 0.0;
-    for (int base = 0; base < K; base += 16 * 256) {
-        uint16_t wv[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            const int k = base + 256 * u + 8 * lane + j;
-            wv[u] = k < K ? w[k] : 0;
-        }
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            const int k = base + 256 * u + 8 * lane + j;
-            if (k < K) acc = fma(static_cast<double>(x[k]), bf16_to_f64(wv[u]), acc);
-        }
-    }
-    return acc;
-}
-
 __global__ void __launch_bounds__(kPreThreads) k_hc_pre1(HcArgs a, unsigned long long *ctr, int *err) {
     extern __shared__ float s_x[];  // [hc*d] normed, then [lr] w
     __shared__ double s_ss[8][8];   // [warp][stream]

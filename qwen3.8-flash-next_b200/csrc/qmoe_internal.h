@@ -202,7 +202,9 @@ int qk_launch_hc_inject(float *h, const float *INJ, const float *y, int n, int h
  *   qk_ep_finish    the sum of the returned partials (rank order) and the
  *                   shared expert into out
  * The transfers between them are the caller's (NCCL send/recv on the
- * buffers of qk_ep_buffers). */
+ * buffers of qk_ep_buffers), or the peer-memory path below. The receive
+ * buffer holds the own tokens in rows [0, cap) and rank g's rows from
+ * cap + g cap on. */
 typedef struct {
     void *send_x, *recv_x;       /* [rows, d] x as given: bf16 or fp32 (same on every rank) */
     int32_t *send_e, *recv_e;    /* [rows, k] */
@@ -210,6 +212,23 @@ typedef struct {
     float *ret, *back;           /* fp32 [G cap, d]: partials in received order / send order */
 } qk_ep_bufs;
 int qk_ep_alloc(qk_prefill *p, int cap, int G);
+/* Peer-memory exchange instead of the caller's transfers (every pair of
+ * ranks with peer access, one process per GPU): each rank's receive rows,
+ * return rows and flags mapped into every rank through CUDA IPC.
+ *   qk_ep_ipc_handles   the 5 handles of this rank (5 x 64 bytes)
+ *   qk_ep_p2p_open      maps every rank's handles (all: G x 5 x 64 bytes)
+ *   qk_ep_dispatch_p2p  the dispatch written into the destinations' receive
+ *                       rows, then the destinations' flags raised
+ *   qk_ep_wait          waits (bounded) for every rank's flag `which`
+ *                       (0: dispatch, 1: return; the return wait ends the call)
+ *   qk_ep_experts_p2p   qk_ep_experts with each partial row written into its
+ *                       owner's return row, then the owners' flags raised */
+int qk_ep_ipc_handles(qk_prefill *p, unsigned char *out);
+int qk_ep_p2p_open(qk_prefill *p, const unsigned char *all, int rank);
+void qk_ep_p2p_close(qk_prefill *p);
+int qk_ep_dispatch_p2p(qk_prefill *p, const qk_fwd *f, int rank, void *stream);
+int qk_ep_wait(qk_prefill *p, int which, int *err, void *stream);
+int qk_ep_experts_p2p(qk_prefill *p, const qk_fwd *f, int shared_slot_index, int rank, void *stream);
 void qk_ep_buffers(qk_prefill *p, qk_ep_bufs *b);
 int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, void *stream);
 int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream);

@@ -1110,13 +1110,14 @@ __global__ void k_ep_pack(const uint8_t *x, int row_bytes, int T, int cap, int k
 }
 
 // The rank's own tokens as the leading rows of the receive buffer (x as
-// given), no routed slots (the experts pass gives them only the shared
-// expert).
-__global__ void k_ep_own(const uint8_t *x, int row_bytes, int T, int k, uint8_t *recv_x,
+// given; rows [T, cap) carry only ids), no routed slots (the experts pass
+// gives them only the shared expert).
+__global__ void k_ep_own(const uint8_t *x, int row_bytes, int T, int cap, int k, uint8_t *recv_x,
                          int32_t *recv_e) {
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (t >= T) return;
+    if (t >= cap) return;
     if (lane < k) recv_e[static_cast<size_t>(t) * k + lane] = -1;
+    if (t >= T) return;
     const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t) * row_bytes);
     uint4 *dst = reinterpret_cast<uint4 *>(recv_x + static_cast<size_t>(t) * row_bytes);
     for (int c = lane; c < row_bytes / 16; c += 32) dst[c] = src[c];
@@ -1487,6 +1488,16 @@ bool map_3d_u8(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t ro
 
 }  // namespace
 
+// Every rank's receive-side buffers as mapped in this process (peer
+// exchange).
+struct EpPeers {
+    uint8_t *recv_x[64];
+    int32_t *recv_e[64];
+    float *recv_w[64];
+    float *back[64];
+    unsigned long long *flags[64];
+};
+
 struct qk_prefill {
     qk_layout L;
     int max_tokens, num_sms, pool_slots, rows_max, tiles_max;
@@ -1524,6 +1535,12 @@ struct qk_prefill {
     float *ep_send_w, *ep_recv_w;   // [rows * k] slot weights
     uint8_t *ep_send_x, *ep_recv_x; // [rows, d] x as given (bf16 or fp32)
     float *ep_ret, *ep_back;        // [rows, d] fp32 partial outputs: received / send order
+    unsigned long long *ep_flags;   // [2][64] peer-exchange flags (written by the peers)
+    unsigned long long *ep_epoch;   // calls completed (peer exchange)
+    unsigned *ep_done;              // [2] CTAs done, dispatch / return grids
+    EpPeers ep_peers;               // every rank's buffers as mapped here
+    EpPeers *ep_peers_dev;
+    int ep_p2p;                     // the peer table is open
 };
 
 extern "C" void qk_prefill_destroy(qk_prefill *p) {
@@ -1553,6 +1570,11 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->ep_send_x);
     cudaFree(p->ep_recv_x);
     cudaFree(p->ep_ret);
+    qk_ep_p2p_close(p);
+    cudaFree(p->ep_flags);
+    cudaFree(p->ep_epoch);
+    cudaFree(p->ep_done);
+    cudaFree(p->ep_peers_dev);
     cudaFree(p->ep_back);
     cudaFree(p->wtiles);
     cudaFree(p->wstiles);
@@ -1847,6 +1869,111 @@ extern "C" int qk_prefill_combine(qk_prefill *p, const qk_fwd *f, void *stream) 
     return cudaGetLastError();
 }
 
+// ---- peer-memory exchange: every rank's receive-side buffers mapped into
+// every rank (CUDA IPC), so rows go straight into their destination's
+// buffers over NVLink; per-rank flags [2][64] (dispatch, return; indexed by
+// the writing rank) carry the call's epoch (this rank's counter + 1: every
+// rank runs the same calls, so the counters advance in step).
+
+QK_DEV void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+QK_DEV unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// After a CTA's peer writes: every thread fences them at system scope, the
+// CTA counts itself done, and the last CTA of the grid raises flag slot
+// `which` of this rank on every destination (dst_mask bit g: rank g).
+QK_DEV void ep_signal(const EpPeers *peers, int which, int me, int G, unsigned long long e, unsigned *done) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(done, 1u) == gridDim.x - 1) {
+        *done = 0;  // the next call's count (stream-ordered after this grid)
+        __threadfence_system();
+        for (int g = 0; g < G; ++g) st_release_sys(peers->flags[g] + which * 64 + me, e);
+    }
+}
+
+// The dispatch of k_ep_pack, written into rank g's receive rows
+// cap + me * cap + t (its rows [0, cap) are its own tokens).
+__global__ void k_ep_pack_p2p(const uint8_t *x, int row_bytes, int T, int cap, int k, int e_per, int G, int me,
+                              const int32_t *idx, const float *wts, const unsigned long long *mask,
+                              const EpPeers *peers, const unsigned long long *epoch, unsigned *done) {
+    const int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (wi < G * cap) {
+        const int g = wi / cap, t = wi % cap;
+        const size_t row = static_cast<size_t>(cap) * (1 + me) + t;
+        const bool live = t < T && ((mask[t] >> g) & 1ull);
+        if (lane < k) {
+            const int e = live ? idx[t * k + lane] : -1;
+            const bool own = live && e / e_per == g;
+            peers->recv_e[g][row * k + lane] = own ? e : -1;
+            peers->recv_w[g][row * k + lane] = own ? wts[t * k + lane] : 0.f;
+        }
+        if (live) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t) * row_bytes);
+            uint4 *dst = reinterpret_cast<uint4 *>(peers->recv_x[g] + row * row_bytes);
+            for (int c = lane; c < row_bytes / 16; c += 32) dst[c] = src[c];
+        }
+    }
+    ep_signal(peers, 0, me, G, *epoch + 1, done);
+}
+
+// Waits (one thread per source rank, bounded) until every rank's flag
+// `which` carries this call's epoch; the return wait then advances the
+// epoch for the next call.
+__global__ void k_ep_wait(const unsigned long long *flags, int which, int G, unsigned long long *epoch, int *err) {
+    const unsigned long long e = *epoch + 1;
+    const int g = threadIdx.x;
+    if (g < G) {
+        const unsigned long long *fl = flags + which * 64 + g;
+        if (ld_acquire_sys(fl) < e) {
+            const uint64_t t0 = gtimer();
+            while (ld_acquire_sys(fl) < e) {
+                if (gtimer() - t0 > kWaitNs) {
+                    atomicOr(err, QK_ERR_TIMEOUT_GRID);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (which == 1 && threadIdx.x == 0) *epoch = e;
+}
+
+// The expert-side combine of k_ep_partial for received row j (source rank
+// j / cap, its token j % cap), written into the source's return row
+// me * cap + t; rows that carry none of this rank's experts are not sent
+// (their owner does not read them).
+__global__ void k_ep_partial_p2p(const float *Y, const int *inv, const int32_t *e_of, const float *w, int k,
+                                 int d, int cap, int G, int me, const EpPeers *peers,
+                                 const unsigned long long *epoch, unsigned *done) {
+    const int r = blockIdx.x;
+    bool live = false;
+    for (int s = 0; s < k; ++s) live |= e_of[static_cast<size_t>(r) * k + s] >= 0;
+    if (live) {
+        float *dst = peers->back[r / cap] + (static_cast<size_t>(me) * cap + r % cap) * d;
+        for (int c = threadIdx.x; c < d / 4; c += blockDim.x) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < k; ++s) {
+                const size_t a = static_cast<size_t>(r) * k + s;
+                if (e_of[a] < 0) continue;
+                const float4 v = reinterpret_cast<const float4 *>(Y + static_cast<size_t>(inv[a]) * d)[c];
+                const float ws = w[a];
+                acc.x = fmaf(ws, v.x, acc.x);
+                acc.y = fmaf(ws, v.y, acc.y);
+                acc.z = fmaf(ws, v.z, acc.z);
+                acc.w = fmaf(ws, v.w, acc.w);
+            }
+            reinterpret_cast<float4 *>(dst)[c] = acc;
+        }
+    }
+    ep_signal(peers, 1, me, G, *epoch + 1, done);
+}
+
 extern "C" int qk_ep_alloc(qk_prefill *p, int T, int G) {
     const qk_layout &L = p->L;
     const size_t rows = static_cast<size_t>(T) * G;  // both directions: at most T per pair
@@ -1864,7 +1991,87 @@ extern "C" int qk_ep_alloc(qk_prefill *p, int T, int G) {
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_recv_x, sizeof(float) * (rows + T) * d);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_ret, sizeof(float) * rows * d);
     if (e == cudaSuccess) e = cudaMalloc(&p->ep_back, sizeof(float) * rows * d);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_flags, sizeof(unsigned long long) * 2 * 64);
+    if (e == cudaSuccess) e = cudaMemset(p->ep_flags, 0, sizeof(unsigned long long) * 2 * 64);
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_epoch, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(p->ep_epoch, 0, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_done, 2 * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(p->ep_done, 0, 2 * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMalloc(&p->ep_peers_dev, sizeof(EpPeers));
     return e;
+}
+
+extern "C" int qk_ep_ipc_handles(qk_prefill *p, unsigned char *out) {
+    void *bufs[5] = {p->ep_recv_x, p->ep_recv_e, p->ep_recv_w, p->ep_back, p->ep_flags};
+    for (int i = 0; i < 5; ++i) {
+        cudaIpcMemHandle_t h;
+        const cudaError_t e = cudaIpcGetMemHandle(&h, bufs[i]);
+        if (e != cudaSuccess) return e;
+        memcpy(out + 64 * i, &h, 64);
+    }
+    return cudaSuccess;
+}
+
+extern "C" void qk_ep_p2p_close(qk_prefill *p) {
+    if (!p->ep_p2p) return;
+    for (int g = 0; g < p->ep_G; ++g)
+        if (p->ep_peers.back[g] != p->ep_back) {
+            cudaIpcCloseMemHandle(p->ep_peers.recv_x[g]);
+            cudaIpcCloseMemHandle(p->ep_peers.recv_e[g]);
+            cudaIpcCloseMemHandle(p->ep_peers.recv_w[g]);
+            cudaIpcCloseMemHandle(p->ep_peers.back[g]);
+            cudaIpcCloseMemHandle(p->ep_peers.flags[g]);
+        }
+    p->ep_p2p = 0;
+}
+
+extern "C" int qk_ep_p2p_open(qk_prefill *p, const unsigned char *all, int rank) {
+    EpPeers pe;
+    memset(&pe, 0, sizeof(pe));
+    cudaError_t e = cudaSuccess;
+    for (int g = 0; g < p->ep_G && e == cudaSuccess; ++g) {
+        if (g == rank) {
+            pe.recv_x[g] = p->ep_recv_x;
+            pe.recv_e[g] = p->ep_recv_e;
+            pe.recv_w[g] = p->ep_recv_w;
+            pe.back[g] = p->ep_back;
+            pe.flags[g] = p->ep_flags;
+            continue;
+        }
+        void *ptr[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+        for (int i = 0; i < 5 && e == cudaSuccess; ++i) {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, all + (static_cast<size_t>(g) * 5 + i) * 64, 64);
+            e = cudaIpcOpenMemHandle(&ptr[i], h, cudaIpcMemLazyEnablePeerAccess);
+        }
+        if (e != cudaSuccess) {
+            for (int i = 0; i < 5; ++i)
+                if (ptr[i]) cudaIpcCloseMemHandle(ptr[i]);
+            break;
+        }
+        pe.recv_x[g] = static_cast<uint8_t *>(ptr[0]);
+        pe.recv_e[g] = static_cast<int32_t *>(ptr[1]);
+        pe.recv_w[g] = static_cast<float *>(ptr[2]);
+        pe.back[g] = static_cast<float *>(ptr[3]);
+        pe.flags[g] = static_cast<unsigned long long *>(ptr[4]);
+    }
+    if (e != cudaSuccess) {
+        for (int g = 0; g < p->ep_G; ++g)
+            if (g != rank && pe.back[g]) {
+                cudaIpcCloseMemHandle(pe.recv_x[g]);
+                cudaIpcCloseMemHandle(pe.recv_e[g]);
+                cudaIpcCloseMemHandle(pe.recv_w[g]);
+                cudaIpcCloseMemHandle(pe.back[g]);
+                cudaIpcCloseMemHandle(pe.flags[g]);
+            }
+        cudaGetLastError();
+        return e;
+    }
+    e = cudaMemcpy(p->ep_peers_dev, &pe, sizeof(pe), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return e;
+    p->ep_peers = pe;
+    p->ep_p2p = 1;
+    return cudaSuccess;
 }
 
 extern "C" void qk_ep_buffers(qk_prefill *p, qk_ep_bufs *b) {
@@ -1891,27 +2098,65 @@ extern "C" int qk_ep_dispatch(qk_prefill *p, const qk_fwd *f, void *stream) {
     k_ep_pack<<<(G * cap * 32 + 255) / 256, 256, 0, st>>>(x, row_bytes, T, cap, L.k, e_per, G,
                                                          f->idx, f->wts, p->ep_mask, p->ep_send_x,
                                                          p->ep_send_e, p->ep_send_w);
-    // this rank's own tokens lead the receive buffer (shared expert only)
+    // this rank's own tokens lead the receive buffer (rows [0, cap): shared
+    // expert only)
+    k_ep_own<<<(cap * 32 + 255) / 256, 256, 0, st>>>(x, row_bytes, T, cap, L.k, p->ep_recv_x, p->ep_recv_e);
+    return cudaGetLastError();
+}
+
+extern "C" int qk_ep_dispatch_p2p(qk_prefill *p, const qk_fwd *f, int rank, void *stream) {
+    const qk_layout &L = p->L;
+    const int T = f->T, G = p->ep_G, cap = p->ep_T;
+    if (!p->ep_p2p || T > cap || L.E % G) return cudaErrorInvalidValue;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int e_per = L.E / G;
     if (T > 0)
-        k_ep_own<<<(T * 32 + 255) / 256, 256, 0, st>>>(x, row_bytes, T, L.k, p->ep_recv_x,
-                                                       p->ep_recv_e);
+        k_ep_mask<<<(T + 255) / 256, 256, 0, st>>>(f->idx, T, L.k, e_per, p->ep_mask);
+    const int row_bytes = L.d * (f->x_bf16 ? 2 : 4);
+    const uint8_t *x = static_cast<const uint8_t *>(f->x);
+    k_ep_own<<<(cap * 32 + 255) / 256, 256, 0, st>>>(x, row_bytes, T, cap, L.k, p->ep_recv_x, p->ep_recv_e);
+    k_ep_pack_p2p<<<(G * cap * 32 + 255) / 256, 256, 0, st>>>(x, row_bytes, T, cap, L.k, e_per, G, rank,
+                                                             f->idx, f->wts, p->ep_mask, p->ep_peers_dev,
+                                                             p->ep_epoch, p->ep_done);
+    return cudaGetLastError();
+}
+
+extern "C" int qk_ep_wait(qk_prefill *p, int which, int *err, void *stream) {
+    k_ep_wait<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(p->ep_flags, which, p->ep_G, p->ep_epoch, err);
+    return cudaGetLastError();
+}
+
+// The experts pass over rows [0, cap + rows): the own tokens (rows [0, T))
+// through the shared expert, the received rows (from cap on) through this
+// rank's experts; then each received row's partial, kept here (the caller
+// returns it) or, with the peer table, written into its owner's return row.
+static int ep_experts(qk_prefill *p, const qk_fwd *f, int shared_slot_index, int rank, bool p2p,
+                      void *stream) {
+    const qk_layout &L = p->L;
+    const int T = f->T, cap = p->ep_T, rows = cap * p->ep_G;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = grouped(p, p->ep_recv_x, f->x_bf16 ? XK_BF16 : XK_F32, cap + rows, p->ep_recv_e,
+                            L.k, T, rows, f->slot_of, shared_slot_index, f->err, st, nullptr);
+    if (e != cudaSuccess) return e;
+    const size_t o = static_cast<size_t>(cap) * L.k;
+    if (p2p)
+        k_ep_partial_p2p<<<rows, 256, 0, st>>>(p->Y, p->inv + o, p->ep_recv_e + o, p->ep_recv_w + o, L.k,
+                                               L.d, cap, p->ep_G, rank, p->ep_peers_dev, p->ep_epoch,
+                                               p->ep_done + 1);
+    else
+        k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv + o, p->ep_recv_e + o, p->ep_recv_w + o, L.k, L.d,
+                                           p->ep_ret);
     return cudaGetLastError();
 }
 
 extern "C" int qk_ep_experts(qk_prefill *p, const qk_fwd *f, int shared_slot_index, void *stream) {
-    const qk_layout &L = p->L;
-    const int T = f->T, rows = p->ep_T * p->ep_G;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // one grouped pass: the own tokens through the shared expert (rows
-    // [0, T)), the received rows through this rank's experts
-    cudaError_t e = grouped(p, p->ep_recv_x, f->x_bf16 ? XK_BF16 : XK_F32, T + rows, p->ep_recv_e,
-                            L.k, T, rows, f->slot_of, shared_slot_index, f->err, st, nullptr);
-    if (e != cudaSuccess) return e;
-    k_ep_partial<<<rows, 256, 0, st>>>(p->Y, p->inv + static_cast<size_t>(T) * L.k,
-                                       p->ep_recv_e + static_cast<size_t>(T) * L.k,
-                                       p->ep_recv_w + static_cast<size_t>(T) * L.k, L.k, L.d,
-                                       p->ep_ret);
-    return cudaGetLastError();
+    return ep_experts(p, f, shared_slot_index, 0, false, stream);
+}
+
+extern "C" int qk_ep_experts_p2p(qk_prefill *p, const qk_fwd *f, int shared_slot_index, int rank,
+                                 void *stream) {
+    if (!p->ep_p2p) return cudaErrorInvalidValue;
+    return ep_experts(p, f, shared_slot_index, rank, true, stream);
 }
 
 extern "C" int qk_ep_finish(qk_prefill *p, const qk_fwd *f, void *stream) {

@@ -132,8 +132,10 @@ def test_two_rank_dispatch_over_gloo(built):
         assert dict(result) == {0: True, 1: True}
 
 
-def _ep_rank(rank, world, uid_q, out_q, T_per):
+def _ep_rank(rank, world, uid_q, out_q, T_per, exchange="p2p"):
     import sys
+    if exchange == "nccl":
+        os.environ["QMOE_EP_P2P"] = "0"
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "qwen3.8-flash-next_b200"))
     import torch
@@ -160,15 +162,20 @@ def _ep_rank(rank, world, uid_q, out_q, T_per):
         ctx.forward_ep(0, xd.data_ptr(), qmoe.QMOE_BF16, T_per, out.data_ptr(), None)
         ctx.sync()
     idx, _, _ = ctx.routing(T_per)
-    out_q.put((rank, out.cpu().numpy(), idx))
+    import ctypes
+    p2p = qmoe.lib().qmoe__ep_p2p
+    p2p.restype, p2p.argtypes = ctypes.c_int, [ctypes.c_void_p]
+    out_q.put((rank, out.cpu().numpy(), idx, int(p2p(ctx.h))))
     ctx.close()
 
 
 @pytest.mark.gpu
-def test_expert_parallel_forward_two_gpus(built):
-    """Two GPUs, one process each, NCCL through the library: every token's
-    routing equals the restatement's and a spread sample of outputs is within
-    the parity tolerance (the same bars as the one-GPU path)."""
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_expert_parallel_forward_two_gpus(built, exchange):
+    """Two GPUs, one process each, the exchanges through peer memory (the
+    default where the GPUs have peer access) or NCCL (QMOE_EP_P2P=0): every
+    token's routing equals the restatement's and a spread sample of outputs
+    is within the parity tolerance (the same bars as the one-GPU path)."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -179,21 +186,27 @@ def test_expert_parallel_forward_two_gpus(built):
     world, T_per = 2, 256
     ctx = mp.get_context("spawn")
     uid_q, out_q = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_ep_rank, args=(r, world, uid_q, out_q, T_per))
+    procs = [ctx.Process(target=_ep_rank, args=(r, world, uid_q, out_q, T_per, exchange))
              for r in range(world)]
     for p in procs:
         p.start()
     results = {}
+    modes = set()
     try:
         for _ in range(world):
-            r, out, idx = out_q.get(timeout=600)
+            r, out, idx, p2p = out_q.get(timeout=600)
             results[r] = (out, idx)
+            modes.add(p2p)
     finally:
         for p in procs:
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    if exchange == "nccl":
+        assert modes == {0}
+    elif torch.cuda.can_device_access_peer(0, 1):
+        assert modes == {1}
     cfg = qmoe.make_config(2048, 512, 10, 512, max_tokens=T_per)
     s = qmoe.SynthLayer(cfg, 20261201, zipf_s=1.1)
     for r in range(world):
