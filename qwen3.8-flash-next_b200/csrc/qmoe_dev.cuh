@@ -340,7 +340,8 @@ QK_DEV float pow2i(int e) { return __int_as_float((127 + e) << 23); }
 // (4 words, 32 elements) sum of the quantised values, scaled back. A group
 // with a non-finite value gets a NaN scale, so its dot products come out NaN
 // as the float ones would.
-template <int NB>
+// GL = 4 makes the scale per 32-element unit (four lanes) instead.
+template <int NB, int GL = 8>
 QK_DEV float quant_word(const float (&v)[8], uint2 (&pl)[NB], float *usum) {
     constexpr int kBits = NB == 2 ? 15 : 22;  // largest |v| 2^e in [2^(kBits-1), 2^kBits)
     constexpr int kMax = (1 << (8 * NB - 1)) - 1;
@@ -352,10 +353,10 @@ QK_DEV float quant_word(const float (&v)[8], uint2 (&pl)[NB], float *usum) {
         fin = fin && isfinite(v[i]);
     }
 #pragma unroll
-    for (int off = 1; off < 8; off <<= 1) m = fmaxf(m, __shfl_xor_sync(QK_FULL, m, off));
+    for (int off = 1; off < GL; off <<= 1) m = fmaxf(m, __shfl_xor_sync(QK_FULL, m, off));
     const unsigned bad = __ballot_sync(QK_FULL, !fin);
     const int lane = threadIdx.x & 31;
-    const bool gfin = ((bad >> (lane & ~7)) & 0xFFu) == 0u;
+    const bool gfin = ((bad >> (lane & ~(GL - 1))) & ((1u << GL) - 1u)) == 0u;
     int ex = 0;
     frexpf(m, &ex);  // m = f 2^ex, f in [0.5, 1)
     int e = m > 0.f ? kBits - ex : 0;

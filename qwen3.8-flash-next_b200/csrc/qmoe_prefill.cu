@@ -807,6 +807,423 @@ __global__ void __launch_bounds__(kThreadsSw, 1)
     }
 }
 
+constexpr int kSbThreads = 512;
+constexpr int kSbBatch = 8;     // most rows (tokens) of a tile on the CUDA cores
+constexpr int kSbGuRows = 32;   // gate/up rows per unit (one 32-element unit of h)
+constexpr int kSbDnRows = 128;  // down rows per unit
+constexpr int kSbMaxRows = 4;   // default: tiles of more rows stay on the tensor cores
+
+__host__ __device__ constexpr int sb_xrow(int d) { return (d / 8) * 16 + (d / 32) * 8; }
+__host__ __device__ constexpr int sb_hrow(int I) { return (I / 8) * 24 + (I / 32) * 8; }
+
+struct SbArgs {
+    const MTile *tiles;       // small tiles (<= 32 rows of one group)
+    const int *n_tiles;
+    int nsh;                  // rows [0, nsh) are tokens [0, nsh) (the shared expert)
+    const int *perm_tok;      // row -> token for the other rows
+    const uint8_t *pool;
+    qk_layout L;
+    const uint8_t *xq;        // [tokens][sb_xrow(d)]
+    uint8_t *hq;              // [rows][sb_hrow(I)]
+    float *Y;                 // [rows][d]
+    int max_rows;             // tiles of more rows are left to the tensor cores
+    int *err;
+};
+
+// The staged x and h vectors interleave each plane's words by unit: the 16
+// bytes of words 4u, 4u + 1 of every unit u first, then those of words
+// 4u + 2, 4u + 3, so that lanes reading consecutive units read consecutive
+// 16-byte pieces (no shared-memory bank conflicts). n words a plane.
+template <int NB>
+QK_DEV void store_word_il(uint2 *planes, int n, int w, const uint2 (&pl)[NB]) {
+    const int q = w & 3;
+    const size_t pos = static_cast<size_t>(q >> 1) * (n / 2) + 2 * (w >> 2) + (q & 1);
+#pragma unroll
+    for (int p = 0; p < NB; ++p) planes[static_cast<size_t>(p) * n + pos] = pl[p];
+}
+
+template <int NB>
+QK_DEV void load_unit_il(const uint2 *planes, int n, int u, uint2 (&v)[NB][4]) {
+#pragma unroll
+    for (int p = 0; p < NB; ++p) {
+        const uint2 *base = planes + static_cast<size_t>(p) * n;
+        const uint4 a = reinterpret_cast<const uint4 *>(base)[u];
+        const uint4 b = reinterpret_cast<const uint4 *>(base + n / 2)[u];
+        v[p][0] = make_uint2(a.x, a.y);
+        v[p][1] = make_uint2(a.z, a.w);
+        v[p][2] = make_uint2(b.x, b.y);
+        v[p][3] = make_uint2(b.z, b.w);
+    }
+}
+
+// Sums each of v[0 .. N) over an aligned group of W lanes, halving the
+// values at each of the first log2 N levels (a lane keeps one half and
+// sends the other): log2 N + ... shuffles in all instead of N log2 W. On
+// return lane l holds the sum of value (l % W) / (W / N).
+template <int N, int W>
+QK_DEV float group_sum_tr(float (&v)[N], int lane) {
+    constexpr int kLevels = N >= 16 ? 4 : N >= 8 ? 3 : N >= 4 ? 2 : N >= 2 ? 1 : 0;
+    static_assert((1 << kLevels) == N && N <= W, "N a power of two, at most W");
+#pragma unroll
+    for (int lv = 0; lv < kLevels; ++lv) {
+        const int c = N >> lv, off = W >> (lv + 1);
+        const bool hi = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < c / 2; ++i) {
+            const float send = hi ? v[i] : v[i + c / 2];
+            const float keep = hi ? v[i + c / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(QK_FULL, send, off);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int off = W / N / 2; off >= 1; off >>= 1) r += __shfl_xor_sync(QK_FULL, r, off);
+    return r;
+}
+
+// NT tokens (jj0 .. jj0 + NT of the staged batch) of the warp's two gate/up
+// rows il and il + 16: each token's x is read once for both rows; the 4 NT
+// sums (token, row, gate/up) reduced together.
+template <int NT, int UPL>
+QK_DEV void sb_gu_tokens(const uint8_t *xs, int xrow, int n, int nunits, int lane, int jj0,
+                         const uint4 (&gw)[2][UPL], const uint4 (&uw)[2][UPL],
+                         const uint2 (&sb)[2][UPL], float *hbuf, int il) {
+    constexpr int N = 4 * NT;
+    float v[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = 0.f;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const uint8_t *xr = xs + (jj0 + t) * xrow;
+        const uint2 *xp = reinterpret_cast<const uint2 *>(xr);
+        const float *us = reinterpret_cast<const float *>(xr + n * 16);
+#pragma unroll
+        for (int i = 0; i < UPL; ++i) {
+            const int uu = lane + 32 * i;
+            if (uu < nunits) {
+                uint2 xw[2][4];
+                load_unit_il<2>(xp, n, uu, xw);
+                const float xsc = us[uu], xsm = us[nunits + uu];
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    v[(t * 2 + rr) * 2] += fmaf(bf16lo(sb[rr][i].x), dot_unit_q<2>(gw[rr][i], xw) * xsc,
+                                                bf16hi(sb[rr][i].x) * xsm);
+                    v[(t * 2 + rr) * 2 + 1] += fmaf(bf16lo(sb[rr][i].y), dot_unit_q<2>(uw[rr][i], xw) * xsc,
+                                                    bf16hi(sb[rr][i].y) * xsm);
+                }
+            }
+        }
+    }
+    // value k = (t * 2 + row) * 2 + gate/up sits on lanes k (32 / N) ..
+    constexpr int kSpan = 32 / N;
+    const float r = group_sum_tr<N, 32>(v, lane);
+    const float up = __shfl_down_sync(QK_FULL, r, kSpan);
+    const int k = lane / kSpan;
+    if (lane % kSpan == 0 && (k & 1) == 0) {
+        const int t = k >> 2, rr = (k >> 1) & 1;
+        hbuf[(jj0 + t) * 32 + il + 16 * rr] = (r / (1.0f + expf(-r))) * up;
+    }
+}
+
+// NT tile rows of the lane group's P down rows (LPR lanes, lane j on h unit
+// j): each row of h read once for the P rows, the P NT sums reduced together.
+template <int NT, int P, int LPR>
+QK_DEV void sb_dn_tokens(const uint8_t *hs, int hrow, int hn, int upe, int j, int lane, int jj0,
+                         const uint4 (&w)[P], const uint32_t (&sb)[P], float *ys, const int (&r)[P]) {
+    constexpr int N = NT * P;
+    float v[N];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const uint8_t *hr = hs + (jj0 + t) * hrow;
+        uint2 hv[3][4];
+        load_unit_il<3>(reinterpret_cast<const uint2 *>(hr), hn, j, hv);
+        const float *hsf = reinterpret_cast<const float *>(hr + hn * 24);
+        const float hsc = hsf[j], hsm = hsf[upe + j];
+#pragma unroll
+        for (int p = 0; p < P; ++p)
+            v[t * P + p] = fmaf(bf16lo(sb[p]), dot_unit_q<3>(w[p], hv) * hsc, bf16hi(sb[p]) * hsm);
+    }
+    constexpr int kSpan = LPR / N;
+    const float s = group_sum_tr<N, LPR>(v, lane);
+    if (j % kSpan == 0) {
+        const int k = j / kSpan, t = k / P, p = k % P;
+        int rp = r[0];
+#pragma unroll
+        for (int q = 1; q < P; ++q)
+            if (p == q) rp = r[q];
+        if (rp < kSbDnRows) ys[(jj0 + t) * kSbDnRows + rp] = s;
+    }
+}
+
+// Gate/up: unit = (small tile of at most kSbBatch rows, 32 gate/up rows). A
+// stage holds the unit's weight rows and the x of the tile's tokens, both by
+// bulk copies on one barrier, the next unit's stage in flight while this one
+// computes. Tile descriptors are read two units ahead and the tokens one
+// unit ahead, so a unit's copies are issued without a dependent global load.
+// Warp w takes rows w and w + 16 (weights in registers), lane l its UPL
+// 32-element units of x (l, l + 32); each token's x is read once for both
+// rows (the arithmetic of the decode kernel's gateup_row). h goes through one
+// of two buffers, so warp 0 quantises it while the others go on.
+__host__ __device__ int sb_gu_stage(const qk_layout &L) { return kSbGuRows * L.gu_row + kSbBatch * sb_xrow(L.d); }
+int sb_gu_smem(const qk_layout &L) { return 2 * sb_gu_stage(L) + 2 * kSbBatch * 32 * 4; }
+
+template <int UPL>
+__global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t sbar[2];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const qk_layout &L = a.L;
+    const int d = L.d, n = d / 8, nunits = d / 32, xrow = sb_xrow(d), hrow = sb_hrow(L.I);
+    const uint32_t wbytes = static_cast<uint32_t>(kSbGuRows * L.gu_row);
+    const size_t stage = static_cast<size_t>(sb_gu_stage(L));
+    float *hbuf0 = reinterpret_cast<float *>(smem + 2 * stage);  // 2 x [kSbBatch][32]
+    if (tid == 0) {
+        mbar_init(&sbar[0], 1);
+        mbar_init(&sbar[1], 1);
+    }
+    __syncthreads();
+    const int rb_n = L.I / kSbGuRows;
+    const int nu = *a.n_tiles * rb_n;
+    const int step = gridDim.x;
+    // a tile of more than max_rows rows becomes a unit of no rows: its stage
+    // barrier completes on the plain arrive, and it computes nothing
+    auto tile_of = [&](int u) {
+        MTile m = {0, 0, 0, 0};
+        if (u < nu) m = a.tiles[u / rb_n];
+        if (m.rows > a.max_rows) m.rows = 0;
+        return m;
+    };
+    // warp 0 lane l: the token of the tile's row l
+    auto tok_of = [&](const MTile &m) {
+        int t = 0;
+        if (warp == 0 && lane < m.rows) {
+            const int r = m.m0 + lane;
+            t = r < a.nsh ? r : a.perm_tok[r];
+        }
+        return t;
+    };
+    // warp 0: the unit's weights and its tokens' x into stage s
+    auto issue = [&](int u, int s, const MTile &mt, int tok) {
+        uint8_t *dst = smem + s * stage;
+        if (lane == 0) {
+            mbar_expect_tx(&sbar[s], mt.rows > 0 ? wbytes + static_cast<uint32_t>(mt.rows * xrow) : 0u);
+            if (mt.rows > 0)
+                bulk_load(dst, a.pool + static_cast<size_t>(mt.slot) * L.slot_bytes +
+                                   static_cast<size_t>(u % rb_n) * kSbGuRows * L.gu_row,
+                          wbytes, &sbar[s]);
+        }
+        __syncwarp();
+        if (lane < mt.rows)
+            bulk_load(dst + wbytes + lane * xrow, a.xq + static_cast<size_t>(tok) * xrow,
+                      static_cast<uint32_t>(xrow), &sbar[s]);
+    };
+    const int u0 = blockIdx.x;
+    MTile m0 = tile_of(u0), m1 = tile_of(u0 + step), m2 = tile_of(u0 + 2 * step);
+    int t1 = tok_of(m1);
+    if (warp == 0 && u0 < nu) issue(u0, 0, m0, tok_of(m0));
+    bool ok = true;
+    int it = 0, hb = 0;  // hb: the h buffer, switched per unit with rows
+    for (int u = u0; u < nu; u += step, ++it) {
+        const int s = it & 1;
+        const MTile mt = m0;
+        const int rb = u % rb_n;
+        if (warp == 0 && u + step < nu) issue(u + step, s ^ 1, m1, t1);
+        {
+            const MTile m3 = tile_of(u + 3 * step);
+            t1 = tok_of(m2);
+            m0 = m1;
+            m1 = m2;
+            m2 = m3;
+        }
+        if (!mbar_wait(&sbar[s], (it >> 1) & 1)) ok = false;
+        if (mt.rows == 0) continue;
+        const uint8_t *W = smem + s * stage;
+        const uint8_t *xs = W + wbytes;
+        const int nb = mt.rows;
+        float *hbuf = hbuf0 + hb * kSbBatch * 32;
+        hb ^= 1;
+        {
+            // warp w: rows w and w + 16, weights in registers (scale group
+            // of unit u: u / 2, the prefill path's groups being 64 wide)
+            uint4 gw[2][UPL], uw[2][UPL];
+            uint2 sb[2][UPL];
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const uint8_t *row = W + static_cast<size_t>(warp + 16 * rr) * L.gu_row;
+#pragma unroll
+                for (int i = 0; i < UPL; ++i) {
+                    const int uu = lane + 32 * i, uc = uu < nunits ? uu : 0;
+                    gw[rr][i] = *reinterpret_cast<const uint4 *>(row + 16 * uc);
+                    uw[rr][i] = *reinterpret_cast<const uint4 *>(row + d / 2 + 16 * uc);
+                    sb[rr][i] = *reinterpret_cast<const uint2 *>(row + d + 8 * (uc >> 1));
+                }
+            }
+            // the tokens in blocks of 2, 1 (an unrolled loop predicated on nb
+            // would issue all kSbBatch tokens' work)
+            int jj = 0;
+            for (; jj + 2 <= nb; jj += 2)
+                sb_gu_tokens<2, UPL>(xs, xrow, n, nunits, lane, jj, gw, uw, sb, hbuf, warp);
+            if (jj < nb) sb_gu_tokens<1, UPL>(xs, xrow, n, nunits, lane, jj, gw, uw, sb, hbuf, warp);
+        }
+        // the stage is refilled two units on, after the next unit's barrier
+        __syncthreads();
+        // h of the tile's rows over this unit's 32 rows -> 24-bit planes with
+        // their own scale (lanes 4 jj .. 4 jj + 3: token jj's words); the
+        // next unit writes the other buffer
+        if (warp == 0) {
+            const int jj = lane >> 2, w = lane & 3;
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = jj < nb ? hbuf[jj * 32 + 8 * w + i] : 0.f;
+            uint2 pl[3];
+            float usum;
+            const float sc = quant_word<3, 4>(v, pl, &usum);
+            if (jj < nb) {
+                uint8_t *hr = a.hq + static_cast<size_t>(mt.m0 + jj) * hrow;
+                store_word_il<3>(reinterpret_cast<uint2 *>(hr), L.I / 8, rb * 4 + w, pl);
+                if (w == 0) {
+                    float *hs = reinterpret_cast<float *>(hr + (L.I / 8) * 24);
+                    hs[rb] = sc;
+                    hs[L.I / 32 + rb] = usum;
+                }
+            }
+        }
+    }
+    if (!ok && tid == 0) atomicOr(a.err, QK_ERR_TIMEOUT_COPY);
+}
+
+// Down: unit = (small tile of at most kSbBatch rows, 128 down rows). A stage
+// holds the unit's weight rows and the h of the tile's rows (one bulk copy
+// each, one barrier); three stages, two units in flight while one computes,
+// the descriptors read a unit before their copies are issued. LPR lanes per
+// down row (one 32-element unit of h each); a lane group holds P rows'
+// weights in registers and reads each row of h once for them. Y is staged in
+// one of two shared buffers and written a row piece at a time while the next
+// unit computes into the other.
+__host__ __device__ int sb_dn_stage(const qk_layout &L) { return kSbDnRows * L.d_row + kSbBatch * sb_hrow(L.I); }
+int sb_dn_smem(const qk_layout &L) { return 3 * sb_dn_stage(L) + 2 * kSbBatch * kSbDnRows * 4; }
+
+template <int LPR>
+__global__ void __launch_bounds__(kSbThreads, 1) k_sb_dn(SbArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t sbar[3];
+    constexpr int RPW = 32 / LPR;                                  // rows a warp holds at once
+    constexpr int P = kSbDnRows / ((kSbThreads / 32) * RPW) > 0    // rows a lane group holds
+                          ? kSbDnRows / ((kSbThreads / 32) * RPW) : 1;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const qk_layout &L = a.L;
+    const int d = L.d, hn = L.I / 8, upe = L.I / 32, hrow = sb_hrow(L.I);
+    const uint32_t wbytes = static_cast<uint32_t>(kSbDnRows * L.d_row);
+    const size_t stage = static_cast<size_t>(sb_dn_stage(L));
+    float *ys0 = reinterpret_cast<float *>(smem + 3 * stage);  // 2 x [kSbBatch][kSbDnRows]
+    if (tid == 0) {
+        mbar_init(&sbar[0], 1);
+        mbar_init(&sbar[1], 1);
+        mbar_init(&sbar[2], 1);
+    }
+    __syncthreads();
+    const int db_n = d / kSbDnRows;
+    const int nu = *a.n_tiles * db_n;
+    const int step = gridDim.x;
+    auto tile_of = [&](int u) {
+        MTile m = {0, 0, 0, 0};
+        if (u < nu) m = a.tiles[u / db_n];
+        if (m.rows > a.max_rows) m.rows = 0;  // left to the tensor cores
+        return m;
+    };
+    auto issue = [&](int u, int s, const MTile &mt) {
+        uint8_t *dst = smem + s * stage;
+        if (mt.rows == 0) {
+            mbar_expect_tx(&sbar[s], 0u);
+            return;
+        }
+        mbar_expect_tx(&sbar[s], wbytes + static_cast<uint32_t>(mt.rows * hrow));
+        bulk_load(dst, a.pool + static_cast<size_t>(mt.slot) * L.slot_bytes + L.gu_bytes +
+                           static_cast<size_t>(u % db_n) * kSbDnRows * L.d_row,
+                  wbytes, &sbar[s]);
+        bulk_load(dst + wbytes, a.hq + static_cast<size_t>(mt.m0) * hrow,
+                  static_cast<uint32_t>(mt.rows * hrow), &sbar[s]);
+    };
+    const int u0 = blockIdx.x;
+    MTile m0 = tile_of(u0), m1 = tile_of(u0 + step), m2 = tile_of(u0 + 2 * step);
+    if (tid == 0) {
+        if (u0 < nu) issue(u0, 0, m0);
+        if (u0 + step < nu) issue(u0 + step, 1, m1);
+    }
+    bool ok = true;
+    int it = 0, yb = 0;  // yb: the Y buffer, switched per unit with rows
+    for (int u = u0; u < nu; u += step, ++it) {
+        const int s = it % 3;
+        const MTile mt = m0;
+        const int db = u % db_n;
+        if (tid == 0 && u + 2 * step < nu) issue(u + 2 * step, (it + 2) % 3, m2);
+        {
+            const MTile m3 = tile_of(u + 3 * step);
+            m0 = m1;
+            m1 = m2;
+            m2 = m3;
+        }
+        if (!mbar_wait(&sbar[s], (it / 3) & 1)) ok = false;
+        if (mt.rows == 0) continue;
+        const uint8_t *W = smem + s * stage;
+        const uint8_t *hs = W + wbytes;
+        float *ys = ys0 + yb * kSbBatch * kSbDnRows;
+        yb ^= 1;
+        const int j = lane % LPR;
+        if (warp * RPW < kSbDnRows) {
+            // the lane group's P rows, weights in registers (scale group of
+            // unit j: j / 2, the prefill path's groups being 64 wide)
+            int r[P];
+            uint4 w[P];
+            uint32_t sb[P];
+#pragma unroll
+            for (int q = 0; q < P; ++q) {
+                r[q] = warp * RPW + lane / LPR + q * (kSbThreads / 32) * RPW;
+                const uint8_t *row = W + static_cast<size_t>(r[q] < kSbDnRows ? r[q] : 0) * L.d_row;
+                w[q] = *reinterpret_cast<const uint4 *>(row + 16 * j);
+                sb[q] = *reinterpret_cast<const uint32_t *>(row + L.I / 2 + 4 * (j >> 1));
+            }
+            int jj = 0;
+            for (; jj + 2 <= mt.rows; jj += 2) sb_dn_tokens<2, P, LPR>(hs, hrow, hn, upe, j, lane, jj, w, sb, ys, r);
+            if (jj < mt.rows) sb_dn_tokens<1, P, LPR>(hs, hrow, hn, upe, j, lane, jj, w, sb, ys, r);
+        }
+        // one barrier a unit: the stage and this ys buffer are reused only
+        // after later barriers
+        __syncthreads();
+        for (int i = tid; i < mt.rows * kSbDnRows; i += kSbThreads)
+            a.Y[static_cast<size_t>(mt.m0 + i / kSbDnRows) * d + db * kSbDnRows + i % kSbDnRows] = ys[i];
+    }
+    if (!ok && tid == 0) atomicOr(a.err, QK_ERR_TIMEOUT_COPY);
+}
+
+// The tiles of more than max_rows rows, in list order (one CTA of 1024
+// threads): the tensor-core kernels take these, k_sb_* the rest.
+__global__ void k_heavy_tiles(const MTile *tiles, const int *n_tiles, int max_rows, MTile *out,
+                              int *n_out) {
+    __shared__ int s_cnt[32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = *n_tiles;
+    int base = 0;
+    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+        const int i = i0 + tid;
+        MTile m = {0, 0, 0, 0};
+        if (i < n) m = tiles[i];
+        const bool heavy = i < n && m.rows > max_rows;
+        const unsigned b = __ballot_sync(QK_FULL, heavy);
+        if (lane == 0) s_cnt[warp] = __popc(b);
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int w = 0; w < static_cast<int>(blockDim.x) / 32; ++w) {
+            before += w < warp ? s_cnt[w] : 0;
+            total += s_cnt[w];
+        }
+        if (heavy) out[base + before + __popc(b & ((1u << lane) - 1u))] = m;
+        base += total;
+        __syncthreads();
+    }
+    if (tid == 0) *n_out = base;
+}
+
 // ---------------------------------------------------------------------------
 // routing -> groups
 
@@ -978,6 +1395,62 @@ __global__ void __launch_bounds__(1024) k_wave_tiles(const MTile *tiles, const i
 
 // x element types of the grouped path
 enum { XK_F32 = 0, XK_BF16 = 1, XK_F16 = 2 };
+
+// ---------------------------------------------------------------------------
+// Small groups on the CUDA cores (calls whose groups all have at most 64
+// rows: batched decode and the stack): the integer dot products of the
+// single-launch decode kernel, each expert's weight rows streamed once for
+// all of its rows (tokens). The tensor-core path dequantises a 256-row weight
+// tile per K step whatever the group's few tokens; here every q4 word is
+// multiplied with each token's 16-bit x (four dp4a a token).
+//   k_sb_xq   every token's x -> 16-bit planes, one scale and sum per
+//             32-element unit (XROW bytes a token)
+//   k_sb_gu   unit = (small tile, 32 gate/up rows): the rows by one bulk copy
+//             (two-unit ring), the tile's tokens' x in batches of 8; h of the
+//             32 rows per token -> 24-bit planes with its own unit scale
+//             (HROW bytes a grouped row)
+//   k_sb_dn   unit = (small tile, 64 down rows): Y[row][d0 .. d0 + 64) fp32
+// k_combine then runs as on the tensor-core path.
+// One CTA per token, one thread per q4 word position (d / 8 <= 1024).
+__global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq) {
+    const int t = blockIdx.x, w = threadIdx.x, n = d / 8;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    if (w < n) {
+        if (x_kind == XK_BF16) {
+            const uint4 q = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) + static_cast<size_t>(t) * d)[w];
+            v[0] = bf16lo(q.x); v[1] = bf16hi(q.x); v[2] = bf16lo(q.y); v[3] = bf16hi(q.y);
+            v[4] = bf16lo(q.z); v[5] = bf16hi(q.z); v[6] = bf16lo(q.w); v[7] = bf16hi(q.w);
+        } else if (x_kind == XK_F16) {
+            const uint4 q = reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) + static_cast<size_t>(t) * d)[w];
+            const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f2 = __half22float2(u2h(qq[i]));
+                v[2 * i] = f2.x;
+                v[2 * i + 1] = f2.y;
+            }
+        } else {
+            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(x) + static_cast<size_t>(t) * d) + 2 * w;
+            const float4 a = p[0], b = p[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+    }
+    uint2 pl[2];
+    float usum;
+    const float sc = quant_word<2, 4>(v, pl, &usum);
+    uint8_t *row = xq + static_cast<size_t>(t) * sb_xrow(d);
+    if (w < n) {
+        store_word_il<2>(reinterpret_cast<uint2 *>(row), n, w, pl);
+        if ((w & 3) == 0) {
+            float *us = reinterpret_cast<float *>(row + n * 16);
+            us[w >> 2] = sc;
+            us[n / 4 + (w >> 2)] = usum;
+        }
+    }
+}
+
 
 // Grouped fp16 A operand: row r holds token r (r < nsh, the shared group) or
 // perm_tok[r]; each 8-element chunk in the order [0,4,1,5,2,6,3,7].
@@ -1502,15 +1975,19 @@ struct qk_prefill {
     qk_layout L;
     int max_tokens, num_sms, pool_slots, rows_max, tiles_max;
     int small_max;                  // groups of at most this many rows use k_gemm_sw
+    int sb;                         // small tiles on the CUDA cores (k_sb_*) instead of k_gemm_sw
+    int sb_max_rows;                // ... those of at most this many rows; k_gemm_sw the others
+    uint8_t *sb_xq, *sb_hq;         // their quantised x per token, h per grouped row
+    MTile *htiles;                  // the small tiles of more than sb_max_rows rows
+    int *n_htiles;
+    const uint8_t *pool;            // the weight pool the expert slots index
     int *counts, *cursor, *row0, *inv, *perm_tok, *n_mtiles, *n_stiles, *n_rows;
     MTile *tiles, *stiles;          // BM-row tiles (k_gemm), NS-row tiles (k_gemm_sw)
-    // waves of a call whose experts exceed the pool: the wave's tiles, the
-    // expert mask ([E + 1], shared expert first) and the plan's small/large
-    // choice of the call
+    // waves of a call whose experts exceed the pool: the wave's tiles and the
+    // expert mask ([E + 1], shared expert first)
     MTile *wtiles, *wstiles;
     int *n_wtiles;                  // [2]: tiles, small tiles
     uint8_t *wave;
-    int wave_all_small;
     __half *xp, *H;
     float *Y;
     CUtensorMap tmX, tmH, tmQgu, tmSgu, tmQdn, tmSdn;
@@ -1554,6 +2031,10 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->n_rows);
     cudaFree(p->tiles);
     cudaFree(p->stiles);
+    cudaFree(p->sb_xq);
+    cudaFree(p->sb_hq);
+    cudaFree(p->htiles);
+    cudaFree(p->n_htiles);
     cudaFree(p->xp);
     cudaFree(p->H);
     cudaFree(p->Y);
@@ -1600,12 +2081,25 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     p->max_tokens = max_tokens;
     p->num_sms = num_sms;
     p->pool_slots = pool_slots;
+    p->pool = pool;
     p->rows_max = max_tokens * (L->k + 1);
     // tuning knob: QMOE_GROUP_SMALL_ROWS in [0, 64] (0: k_gemm_sw never used)
     p->small_max = kSmallMax;
     if (const char *v = getenv("QMOE_GROUP_SMALL_ROWS")) {
         const int n = atoi(v);
         if (n >= 0 && n <= kSmallMax) p->small_max = n;
+    }
+    // tuning knob: QMOE_SMALL_PATH=tc keeps small groups on the tensor cores
+    // (k_gemm_sw); the CUDA-core path covers d <= 2048 and I / 32 in {4, 16}
+    p->sb = L->d <= 2048 && L->d % 256 == 0 && (L->I == 128 || L->I == 512) && L->g % 32 == 0;
+    if (const char *v = getenv("QMOE_SMALL_PATH")) p->sb = p->sb && strcmp(v, "tc") != 0;
+    // tuning knob: QMOE_SB_MAX_ROWS in [1, 8], the largest tile on the CUDA
+    // cores (a token more costs them a pass over the unit; k_gemm_sw's cost
+    // hardly depends on the rows)
+    p->sb_max_rows = kSbMaxRows;
+    if (const char *v = getenv("QMOE_SB_MAX_ROWS")) {
+        const int m = atoi(v);
+        if (m >= 1 && m <= kSbBatch) p->sb_max_rows = m;
     }
     p->tiles_max = p->rows_max / BM + L->E + 2;
     const size_t R = static_cast<size_t>(p->rows_max);
@@ -1621,6 +2115,10 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     if (e == cudaSuccess) e = cudaMalloc(&p->tiles, sizeof(MTile) * p->tiles_max);
     // groups of at most kSmallMax rows: at most kSmallMax / NS tiles each
     if (e == cudaSuccess) e = cudaMalloc(&p->stiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
+    if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->sb_xq, static_cast<size_t>(max_tokens) * sb_xrow(L->d));
+    if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->sb_hq, R * sb_hrow(L->I));
+    if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->htiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
+    if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->n_htiles, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&p->wtiles, sizeof(MTile) * p->tiles_max);
     if (e == cudaSuccess) e = cudaMalloc(&p->wstiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
     if (e == cudaSuccess) e = cudaMalloc(&p->n_wtiles, 2 * sizeof(int));
@@ -1697,6 +2195,19 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
             return nullptr;
         }
     }
+    if (p->sb) {
+        const void *sfn[4] = {reinterpret_cast<const void *>(&k_sb_gu<1>), reinterpret_cast<const void *>(&k_sb_gu<2>),
+                              reinterpret_cast<const void *>(&k_sb_dn<4>), reinterpret_cast<const void *>(&k_sb_dn<16>)};
+        const int ssm[4] = {sb_gu_smem(*L), sb_gu_smem(*L), sb_dn_smem(*L), sb_dn_smem(*L)};
+        for (int i = 0; i < 4; ++i) {
+            e = cudaFuncSetAttribute(sfn[i], cudaFuncAttributeMaxDynamicSharedMemorySize, ssm[i]);
+            if (e != cudaSuccess) {
+                snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
+                qk_prefill_destroy(p);
+                return nullptr;
+            }
+        }
+    }
     return p;
 }
 
@@ -1750,6 +2261,11 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         k_place<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, k, p->row0, p->cursor, p->inv,
                                                  p->perm_tok);
     }
+    // small groups on the CUDA cores: x quantised per token (by the plan
+    // phase; the waves of a call read it) instead of the grouped fp16 rows
+    const bool sb = all_small && p->sb;
+    if (sb && (phases & 1) && T > 0)
+        k_sb_xq<<<T, (L.d / 8 + 31) / 32 * 32, 0, st>>>(x, x_kind, L.d, T, p->sb_xq);
     if ((phases & 1) && rows > 0)
         k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->n_rows,
                                                          p->perm_tok, p->xp,
@@ -1794,7 +2310,45 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     dn.n_cols = L.d;
     dn.out = nullptr;
     dn.outf = p->Y;
-    if (all_small) {
+    if (sb) {
+        SbArgs sa;
+        sa.tiles = stl;
+        sa.n_tiles = nstl;
+        sa.nsh = nsh;
+        sa.perm_tok = p->perm_tok;
+        sa.pool = p->pool;
+        sa.L = L;
+        sa.xq = p->sb_xq;
+        sa.hq = p->sb_hq;
+        sa.Y = p->Y;
+        sa.max_rows = p->sb_max_rows;
+        sa.err = err;
+        void *args[] = {&sa};
+        // the tiles of more rows: k_gemm_sw, on its own list
+        k_heavy_tiles<<<1, 1024, 0, st>>>(stl, nstl, p->sb_max_rows, p->htiles, p->n_htiles);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        const void *gfn = L.d <= 1024 ? reinterpret_cast<const void *>(&k_sb_gu<1>)
+                                      : reinterpret_cast<const void *>(&k_sb_gu<2>);
+        e = qk_launch_raw(gfn, dim3(p->num_sms), dim3(kSbThreads), sb_gu_smem(L), st, 0, args);
+        if (e != cudaSuccess) return e;
+        gu.NT = L.I / 128;
+        gu.tiles = p->htiles;
+        gu.n_mtiles = p->n_htiles;
+        e = lo ? launch_sw(fn(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs, &p->tmXs8, &p->tmQgu4, &p->tmSgu4, &gu)
+               : launch_sw(fn(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs, &p->tmXs8, &p->tmQgu4, &p->tmSgu4, &gu);
+        if (e != cudaSuccess) return e;
+        mark(1);
+        const void *dfn = L.I == 128 ? reinterpret_cast<const void *>(&k_sb_dn<4>)
+                                     : reinterpret_cast<const void *>(&k_sb_dn<16>);
+        e = qk_launch_raw(dfn, dim3(p->num_sms), dim3(kSbThreads), sb_dn_smem(L), st, 0, args);
+        if (e != cudaSuccess) return e;
+        dn.NT = L.d / 256;
+        dn.tiles = p->htiles;
+        dn.n_mtiles = p->n_htiles;
+        e = launch_sw(fn(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs, &p->tmHs8, &p->tmQdn4, &p->tmSdn4, &dn);
+        if (e != cudaSuccess) return e;
+    } else if (all_small) {
         gu.NT = L.I / 128;
         gu.tiles = stl;
         gu.n_mtiles = nstl;
