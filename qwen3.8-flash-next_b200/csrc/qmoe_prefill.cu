@@ -813,7 +813,9 @@ constexpr int kSbGuRows = 32;   // gate/up rows per unit (one 32-element unit of
 constexpr int kSbDnRows = 128;  // down rows per unit
 constexpr int kSbMaxRows = 4;   // default: tiles of more rows stay on the tensor cores
 
-__host__ __device__ constexpr int sb_xrow(int d) { return (d / 8) * 16 + (d / 32) * 8; }
+// x of a token: two 8-bit planes of d / 8 words in group-major 16-byte
+// chunks (store_word_gx), then {scale, sum} per 64-element group
+__host__ __device__ constexpr int sb_xrow(int d) { return (d / 8) * 16 + (d / 64) * 8; }
 __host__ __device__ constexpr int sb_hrow(int I) { return (I / 8) * 24 + (I / 32) * 8; }
 
 struct SbArgs {
@@ -827,6 +829,8 @@ struct SbArgs {
     uint8_t *hq;              // [rows][sb_hrow(I)]
     float *Y;                 // [rows][d]
     int max_rows;             // tiles of more rows are left to the tensor cores
+    MTile *heavy;             // k_sb_gu's first CTA lists those tiles here (in order)
+    int *n_heavy;
     int *err;
 };
 
@@ -856,6 +860,70 @@ QK_DEV void load_unit_il(const uint2 *planes, int n, int u, uint2 (&v)[NB][4]) {
     }
 }
 
+// Group-major chunks of a plane of n words (gate/up's x): chunk (q, g), 16
+// bytes at (q * n / 8 + g) * 16, holds words 8 g + 2 q and 8 g + 2 q + 1, so
+// the lane of group g reads its 8 words as 4 chunks, consecutive lanes
+// consecutive chunks.
+template <int NB>
+QK_DEV void store_word_gx(uint2 *planes, int n, int w, const uint2 (&pl)[NB]) {
+    const int g = w >> 3, q = (w & 7) >> 1;
+    const size_t pos = (static_cast<size_t>(q) * (n / 8) + g) * 2 + (w & 1);
+#pragma unroll
+    for (int p = 0; p < NB; ++p) planes[static_cast<size_t>(p) * n + pos] = pl[p];
+}
+
+// a (4 unsigned bytes) . b (4 signed bytes) + c
+QK_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// sum(q_k x_k) over one 64-element group: q the 8 q4 words w0 (words 0-3),
+// w1 (4-7); x 16-bit as a signed hi and an unsigned lo plane, chunk q of each
+// holding words 2q, 2q + 1 as {even bytes, odd bytes}. The odd nibbles are
+// used in place (w & 0xF0F0F0F0, 16 q) and their sums shifted back once.
+// Exact in 32 bits (|sum| < 64 * 15 * 2^15).
+QK_DEV int dot_group_x16(const uint4 &w0, const uint4 &w1, const uint4 (&xh)[4], const uint4 (&xl)[4]) {
+    const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    int he = 0, ho = 0;
+    unsigned le = 0, lo = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t ev = wd[i] & 0x0F0F0F0Fu, oh = wd[i] & 0xF0F0F0F0u;
+        const uint4 &ch = xh[i >> 1], &cl = xl[i >> 1];
+        const uint32_t hev = (i & 1) ? ch.z : ch.x, hod = (i & 1) ? ch.w : ch.y;
+        const uint32_t lev = (i & 1) ? cl.z : cl.x, lod = (i & 1) ? cl.w : cl.y;
+        he = __dp4a(static_cast<int>(ev), static_cast<int>(hev), he);
+        ho = dp4a_us(oh, hod, ho);
+        le = __dp4a(ev, lev, le);
+        lo = __dp4a(oh, lod, lo);
+    }
+    return (he + (ho >> 4)) * 256 + static_cast<int>(le + (lo >> 4));
+}
+
+// sum(q_k h_k) over one 16-byte unit (32 nibbles) for 24-bit h (signed hi,
+// unsigned mid and lo planes), in units of the scale; the odd nibbles used in
+// place as in dot_group_x16. The same value as dot_unit_q<3>.
+QK_DEV float dot_unit_h24(const uint4 &w, const uint2 (&v)[3][4]) {
+    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+    int he = 0, ho = 0;
+    unsigned me = 0, mo = 0, le = 0, lo = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t ev = wd[i] & 0x0F0F0F0Fu, oh = wd[i] & 0xF0F0F0F0u;
+        he = __dp4a(static_cast<int>(ev), static_cast<int>(v[0][i].x), he);
+        ho = dp4a_us(oh, v[0][i].y, ho);
+        me = __dp4a(ev, v[1][i].x, me);
+        mo = __dp4a(oh, v[1][i].y, mo);
+        le = __dp4a(ev, v[2][i].x, le);
+        lo = __dp4a(oh, v[2][i].y, lo);
+    }
+    const int hi = he + (ho >> 4);
+    const unsigned mid = me + (mo >> 4), low = le + (lo >> 4);
+    return fmaf(static_cast<float>(hi), 65536.f, static_cast<float>(mid * 256u + low));
+}
+
 // Sums each of v[0 .. N) over an aligned group of W lanes, halving the
 // values at each of the first log2 N levels (a lane keeps one half and
 // sends the other): log2 N + ... shuffles in all instead of N log2 W. On
@@ -882,35 +950,37 @@ QK_DEV float group_sum_tr(float (&v)[N], int lane) {
 }
 
 // NT tokens (jj0 .. jj0 + NT of the staged batch) of the warp's two gate/up
-// rows il and il + 16: each token's x is read once for both rows; the 4 NT
+// rows il and il + 16; lane l on the 64-element group l (lanes past the
+// groups contribute 0): each token's x is read once for both rows; the 4 NT
 // sums (token, row, gate/up) reduced together.
-template <int NT, int UPL>
-QK_DEV void sb_gu_tokens(const uint8_t *xs, int xrow, int n, int nunits, int lane, int jj0,
-                         const uint4 (&gw)[2][UPL], const uint4 (&uw)[2][UPL],
-                         const uint2 (&sb)[2][UPL], float *hbuf, int il) {
+template <int NT>
+QK_DEV void sb_gu_tokens(const uint8_t *xs, int xrow, int n, bool act, int lane, int jj0,
+                         const uint4 (&gw)[2][2], const uint4 (&uw)[2][2], const uint2 (&sb)[2],
+                         float *hbuf, int il) {
     constexpr int N = 4 * NT;
     float v[N];
 #pragma unroll
     for (int i = 0; i < N; ++i) v[i] = 0.f;
+    if (act) {
+        const int ng = n / 8;
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        const uint8_t *xr = xs + (jj0 + t) * xrow;
-        const uint2 *xp = reinterpret_cast<const uint2 *>(xr);
-        const float *us = reinterpret_cast<const float *>(xr + n * 16);
+        for (int t = 0; t < NT; ++t) {
+            const uint8_t *xr = xs + (jj0 + t) * xrow;
+            const uint4 *ph = reinterpret_cast<const uint4 *>(xr);
+            const uint4 *pl = reinterpret_cast<const uint4 *>(xr + n * 8);
+            uint4 xh[4], xl[4];
 #pragma unroll
-        for (int i = 0; i < UPL; ++i) {
-            const int uu = lane + 32 * i;
-            if (uu < nunits) {
-                uint2 xw[2][4];
-                load_unit_il<2>(xp, n, uu, xw);
-                const float xsc = us[uu], xsm = us[nunits + uu];
+            for (int q = 0; q < 4; ++q) {
+                xh[q] = ph[q * ng + lane];
+                xl[q] = pl[q * ng + lane];
+            }
+            const float2 xs2 = reinterpret_cast<const float2 *>(xr + n * 16)[lane];
 #pragma unroll
-                for (int rr = 0; rr < 2; ++rr) {
-                    v[(t * 2 + rr) * 2] += fmaf(bf16lo(sb[rr][i].x), dot_unit_q<2>(gw[rr][i], xw) * xsc,
-                                                bf16hi(sb[rr][i].x) * xsm);
-                    v[(t * 2 + rr) * 2 + 1] += fmaf(bf16lo(sb[rr][i].y), dot_unit_q<2>(uw[rr][i], xw) * xsc,
-                                                    bf16hi(sb[rr][i].y) * xsm);
-                }
+            for (int rr = 0; rr < 2; ++rr) {
+                const float dg = static_cast<float>(dot_group_x16(gw[rr][0], gw[rr][1], xh, xl));
+                const float du = static_cast<float>(dot_group_x16(uw[rr][0], uw[rr][1], xh, xl));
+                v[(t * 2 + rr) * 2] = fmaf(bf16lo(sb[rr].x), dg * xs2.x, bf16hi(sb[rr].x) * xs2.y);
+                v[(t * 2 + rr) * 2 + 1] = fmaf(bf16lo(sb[rr].y), du * xs2.x, bf16hi(sb[rr].y) * xs2.y);
             }
         }
     }
@@ -941,7 +1011,7 @@ QK_DEV void sb_dn_tokens(const uint8_t *hs, int hrow, int hn, int upe, int j, in
         const float hsc = hsf[j], hsm = hsf[upe + j];
 #pragma unroll
         for (int p = 0; p < P; ++p)
-            v[t * P + p] = fmaf(bf16lo(sb[p]), dot_unit_q<3>(w[p], hv) * hsc, bf16hi(sb[p]) * hsm);
+            v[t * P + p] = fmaf(bf16lo(sb[p]), dot_unit_h24(w[p], hv) * hsc, bf16hi(sb[p]) * hsm);
     }
     constexpr int kSpan = LPR / N;
     const float s = group_sum_tr<N, LPR>(v, lane);
@@ -960,20 +1030,25 @@ QK_DEV void sb_dn_tokens(const uint8_t *hs, int hrow, int hn, int upe, int j, in
 // bulk copies on one barrier, the next unit's stage in flight while this one
 // computes. Tile descriptors are read two units ahead and the tokens one
 // unit ahead, so a unit's copies are issued without a dependent global load.
-// Warp w takes rows w and w + 16 (weights in registers), lane l its UPL
-// 32-element units of x (l, l + 32); each token's x is read once for both
-// rows (the arithmetic of the decode kernel's gateup_row). h goes through one
-// of two buffers, so warp 0 quantises it while the others go on.
+// Warp w takes rows w and w + 16 (weights in registers), lane l the
+// 64-element scale group l (d <= 2048); each token's x is read once for both
+// rows (integer dots on 16-bit block fixed point x, as in the decode kernel's
+// gateup_row). h goes through one of two buffers, so warp 0 quantises it
+// while the others go on.
 __host__ __device__ int sb_gu_stage(const qk_layout &L) { return kSbGuRows * L.gu_row + kSbBatch * sb_xrow(L.d); }
 int sb_gu_smem(const qk_layout &L) { return 2 * sb_gu_stage(L) + 2 * kSbBatch * 32 * 4; }
 
-template <int UPL>
+QK_DEV void list_heavy_tiles(const MTile *tiles, int n, int max_rows, MTile *out, int *n_out,
+                             int *s_cnt);
+
 __global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t sbar[2];
+    __shared__ int s_cnt[kSbThreads / 32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const qk_layout &L = a.L;
-    const int d = L.d, n = d / 8, nunits = d / 32, xrow = sb_xrow(d), hrow = sb_hrow(L.I);
+    const int d = L.d, n = d / 8, xrow = sb_xrow(d), hrow = sb_hrow(L.I);
+    const bool act = lane < d / 64;  // lane l: 64-element group l
     const uint32_t wbytes = static_cast<uint32_t>(kSbGuRows * L.gu_row);
     const size_t stage = static_cast<size_t>(sb_gu_stage(L));
     float *hbuf0 = reinterpret_cast<float *>(smem + 2 * stage);  // 2 x [kSbBatch][32]
@@ -985,6 +1060,7 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
     const int rb_n = L.I / kSbGuRows;
     const int nu = *a.n_tiles * rb_n;
     const int step = gridDim.x;
+    if (blockIdx.x == 0) list_heavy_tiles(a.tiles, *a.n_tiles, a.max_rows, a.heavy, a.n_heavy, s_cnt);
     // a tile of more than max_rows rows becomes a unit of no rows: its stage
     // barrier completes on the plain arrive, and it computes nothing
     auto tile_of = [&](int u) {
@@ -1043,27 +1119,26 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
         float *hbuf = hbuf0 + hb * kSbBatch * 32;
         hb ^= 1;
         {
-            // warp w: rows w and w + 16, weights in registers (scale group
-            // of unit u: u / 2, the prefill path's groups being 64 wide)
-            uint4 gw[2][UPL], uw[2][UPL];
-            uint2 sb[2][UPL];
+            // warp w: rows w and w + 16, the lane's group of each in registers
+            // (the prefill path's scale groups are 64 wide)
+            uint4 gw[2][2], uw[2][2];
+            uint2 sb[2];
+            const int gc = act ? lane : 0;
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
                 const uint8_t *row = W + static_cast<size_t>(warp + 16 * rr) * L.gu_row;
-#pragma unroll
-                for (int i = 0; i < UPL; ++i) {
-                    const int uu = lane + 32 * i, uc = uu < nunits ? uu : 0;
-                    gw[rr][i] = *reinterpret_cast<const uint4 *>(row + 16 * uc);
-                    uw[rr][i] = *reinterpret_cast<const uint4 *>(row + d / 2 + 16 * uc);
-                    sb[rr][i] = *reinterpret_cast<const uint2 *>(row + d + 8 * (uc >> 1));
-                }
+                const uint4 *gq = reinterpret_cast<const uint4 *>(row + 32 * gc);
+                const uint4 *uq = reinterpret_cast<const uint4 *>(row + d / 2 + 32 * gc);
+                gw[rr][0] = gq[0];
+                gw[rr][1] = gq[1];
+                uw[rr][0] = uq[0];
+                uw[rr][1] = uq[1];
+                sb[rr] = *reinterpret_cast<const uint2 *>(row + d + 8 * gc);
             }
-            // the tokens in blocks of 2, 1 (an unrolled loop predicated on nb
-            // would issue all kSbBatch tokens' work)
-            int jj = 0;
-            for (; jj + 2 <= nb; jj += 2)
-                sb_gu_tokens<2, UPL>(xs, xrow, n, nunits, lane, jj, gw, uw, sb, hbuf, warp);
-            if (jj < nb) sb_gu_tokens<1, UPL>(xs, xrow, n, nunits, lane, jj, gw, uw, sb, hbuf, warp);
+            // one token at a time (two would hold 64 registers of x; an
+            // unrolled loop predicated on nb would issue all kSbBatch tokens'
+            // work)
+            for (int jj = 0; jj < nb; ++jj) sb_gu_tokens<1>(xs, xrow, n, act, lane, jj, gw, uw, sb, hbuf, warp);
         }
         // the stage is refilled two units on, after the next unit's barrier
         __syncthreads();
@@ -1196,13 +1271,11 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_dn(SbArgs a) {
     if (!ok && tid == 0) atomicOr(a.err, QK_ERR_TIMEOUT_COPY);
 }
 
-// The tiles of more than max_rows rows, in list order (one CTA of 1024
-// threads): the tensor-core kernels take these, k_sb_* the rest.
-__global__ void k_heavy_tiles(const MTile *tiles, const int *n_tiles, int max_rows, MTile *out,
-                              int *n_out) {
-    __shared__ int s_cnt[32];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n = *n_tiles;
+// The tiles of more than max_rows rows, in list order, by one CTA: the
+// tensor-core kernels launched after k_sb_gu take these.
+QK_DEV void list_heavy_tiles(const MTile *tiles, int n, int max_rows, MTile *out, int *n_out,
+                             int *s_cnt) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     int base = 0;
     for (int i0 = 0; i0 < n; i0 += blockDim.x) {
         const int i = i0 + tid;
@@ -1213,7 +1286,7 @@ __global__ void k_heavy_tiles(const MTile *tiles, const int *n_tiles, int max_ro
         if (lane == 0) s_cnt[warp] = __popc(b);
         __syncthreads();
         int before = 0, total = 0;
-        for (int w = 0; w < static_cast<int>(blockDim.x) / 32; ++w) {
+        for (int w = 0; w < nw; ++w) {
             before += w < warp ? s_cnt[w] : 0;
             total += s_cnt[w];
         }
@@ -1439,15 +1512,12 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq) {
     }
     uint2 pl[2];
     float usum;
-    const float sc = quant_word<2, 4>(v, pl, &usum);
+    const float sc = quant_word<2>(v, pl, &usum);  // one scale per 64-element group
+    const float gsum = usum + __shfl_xor_sync(QK_FULL, usum, 4);
     uint8_t *row = xq + static_cast<size_t>(t) * sb_xrow(d);
     if (w < n) {
-        store_word_il<2>(reinterpret_cast<uint2 *>(row), n, w, pl);
-        if ((w & 3) == 0) {
-            float *us = reinterpret_cast<float *>(row + n * 16);
-            us[w >> 2] = sc;
-            us[n / 4 + (w >> 2)] = usum;
-        }
+        store_word_gx<2>(reinterpret_cast<uint2 *>(row), n, w, pl);
+        if ((w & 7) == 0) reinterpret_cast<float2 *>(row + n * 16)[w >> 3] = make_float2(sc, gsum);
     }
 }
 
@@ -2196,10 +2266,10 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
         }
     }
     if (p->sb) {
-        const void *sfn[4] = {reinterpret_cast<const void *>(&k_sb_gu<1>), reinterpret_cast<const void *>(&k_sb_gu<2>),
-                              reinterpret_cast<const void *>(&k_sb_dn<4>), reinterpret_cast<const void *>(&k_sb_dn<16>)};
-        const int ssm[4] = {sb_gu_smem(*L), sb_gu_smem(*L), sb_dn_smem(*L), sb_dn_smem(*L)};
-        for (int i = 0; i < 4; ++i) {
+        const void *sfn[3] = {reinterpret_cast<const void *>(&k_sb_gu), reinterpret_cast<const void *>(&k_sb_dn<4>),
+                              reinterpret_cast<const void *>(&k_sb_dn<16>)};
+        const int ssm[3] = {sb_gu_smem(*L), sb_dn_smem(*L), sb_dn_smem(*L)};
+        for (int i = 0; i < 3; ++i) {
             e = cudaFuncSetAttribute(sfn[i], cudaFuncAttributeMaxDynamicSharedMemorySize, ssm[i]);
             if (e != cudaSuccess) {
                 snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
@@ -2322,15 +2392,12 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         sa.hq = p->sb_hq;
         sa.Y = p->Y;
         sa.max_rows = p->sb_max_rows;
+        sa.heavy = p->htiles;      // the tiles of more rows: k_gemm_sw, on this list
+        sa.n_heavy = p->n_htiles;
         sa.err = err;
         void *args[] = {&sa};
-        // the tiles of more rows: k_gemm_sw, on its own list
-        k_heavy_tiles<<<1, 1024, 0, st>>>(stl, nstl, p->sb_max_rows, p->htiles, p->n_htiles);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
-        const void *gfn = L.d <= 1024 ? reinterpret_cast<const void *>(&k_sb_gu<1>)
-                                      : reinterpret_cast<const void *>(&k_sb_gu<2>);
-        e = qk_launch_raw(gfn, dim3(p->num_sms), dim3(kSbThreads), sb_gu_smem(L), st, 0, args);
+        e = qk_launch_raw(reinterpret_cast<const void *>(&k_sb_gu), dim3(p->num_sms), dim3(kSbThreads),
+                          sb_gu_smem(L), st, 0, args);
         if (e != cudaSuccess) return e;
         gu.NT = L.I / 128;
         gu.tiles = p->htiles;
