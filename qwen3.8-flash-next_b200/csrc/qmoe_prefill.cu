@@ -819,7 +819,7 @@ __host__ __device__ constexpr int sb_xrow(int d) { return (d / 8) * 16 + (d / 64
 __host__ __device__ constexpr int sb_hrow(int I) { return (I / 8) * 24 + (I / 32) * 8; }
 
 struct SbArgs {
-    const MTile *tiles;       // small tiles (<= 32 rows of one group)
+    const MTile *tiles;       // the light tiles (at most kSbBatch rows of one group)
     const int *n_tiles;
     int nsh;                  // rows [0, nsh) are tokens [0, nsh) (the shared expert)
     const int *perm_tok;      // row -> token for the other rows
@@ -828,9 +828,7 @@ struct SbArgs {
     const uint8_t *xq;        // [tokens][sb_xrow(d)]
     uint8_t *hq;              // [rows][sb_hrow(I)]
     float *Y;                 // [rows][d]
-    int max_rows;             // tiles of more rows are left to the tensor cores
-    MTile *heavy;             // k_sb_gu's first CTA lists those tiles here (in order)
-    int *n_heavy;
+    int *ctr;                 // [2]: next unit to take, CTAs done (both 0 between launches)
     int *err;
 };
 
@@ -1038,13 +1036,28 @@ QK_DEV void sb_dn_tokens(const uint8_t *hs, int hrow, int hn, int upe, int j, in
 __host__ __device__ int sb_gu_stage(const qk_layout &L) { return kSbGuRows * L.gu_row + kSbBatch * sb_xrow(L.d); }
 int sb_gu_smem(const qk_layout &L) { return 2 * sb_gu_stage(L) + 2 * kSbBatch * 32 * 4; }
 
-QK_DEV void list_heavy_tiles(const MTile *tiles, int n, int max_rows, MTile *out, int *n_out,
-                             int *s_cnt);
+// Units are taken in request order from a counter (a.ctr[0]), four ahead of
+// the one computing, so CTAs that start late (the SMs of a tensor-core
+// kernel running beside this one) take fewer. Unit k's index is requested at
+// the top of iteration k - 4 and published in s_u before that iteration's
+// block barrier. The last CTA to finish zeroes the counters.
+QK_DEV void sb_take_first(int *ctr, int *s_u) {
+    if (threadIdx.x == 0)
+        for (int i = 0; i < 4; ++i) s_u[i] = atomicAdd(ctr, 1);
+    __syncthreads();
+}
+
+QK_DEV void sb_finish(int *ctr) {
+    if (threadIdx.x == 0 && atomicAdd(ctr + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+        atomicExch(ctr, 0);
+        atomicExch(ctr + 1, 0);
+    }
+}
 
 __global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t sbar[2];
-    __shared__ int s_cnt[kSbThreads / 32];
+    __shared__ int s_u[4];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const qk_layout &L = a.L;
     const int d = L.d, n = d / 8, xrow = sb_xrow(d), hrow = sb_hrow(L.I);
@@ -1056,17 +1069,12 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
         mbar_init(&sbar[0], 1);
         mbar_init(&sbar[1], 1);
     }
-    __syncthreads();
     const int rb_n = L.I / kSbGuRows;
     const int nu = *a.n_tiles * rb_n;
-    const int step = gridDim.x;
-    if (blockIdx.x == 0) list_heavy_tiles(a.tiles, *a.n_tiles, a.max_rows, a.heavy, a.n_heavy, s_cnt);
-    // a tile of more than max_rows rows becomes a unit of no rows: its stage
-    // barrier completes on the plain arrive, and it computes nothing
+    sb_take_first(a.ctr, s_u);  // (its barrier also publishes the barrier inits)
     auto tile_of = [&](int u) {
         MTile m = {0, 0, 0, 0};
         if (u < nu) m = a.tiles[u / rb_n];
-        if (m.rows > a.max_rows) m.rows = 0;
         return m;
     };
     // warp 0 lane l: the token of the tile's row l
@@ -1082,42 +1090,42 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
     auto issue = [&](int u, int s, const MTile &mt, int tok) {
         uint8_t *dst = smem + s * stage;
         if (lane == 0) {
-            mbar_expect_tx(&sbar[s], mt.rows > 0 ? wbytes + static_cast<uint32_t>(mt.rows * xrow) : 0u);
-            if (mt.rows > 0)
-                bulk_load(dst, a.pool + static_cast<size_t>(mt.slot) * L.slot_bytes +
-                                   static_cast<size_t>(u % rb_n) * kSbGuRows * L.gu_row,
-                          wbytes, &sbar[s]);
+            mbar_expect_tx(&sbar[s], wbytes + static_cast<uint32_t>(mt.rows * xrow));
+            bulk_load(dst, a.pool + static_cast<size_t>(mt.slot) * L.slot_bytes +
+                               static_cast<size_t>(u % rb_n) * kSbGuRows * L.gu_row,
+                      wbytes, &sbar[s]);
         }
         __syncwarp();
         if (lane < mt.rows)
             bulk_load(dst + wbytes + lane * xrow, a.xq + static_cast<size_t>(tok) * xrow,
                       static_cast<uint32_t>(xrow), &sbar[s]);
     };
-    const int u0 = blockIdx.x;
-    MTile m0 = tile_of(u0), m1 = tile_of(u0 + step), m2 = tile_of(u0 + 2 * step);
+    // units u0 (computing), u1 (its stage in flight), u2 (descriptor and
+    // tokens read), u3 (descriptor read)
+    int u0 = s_u[0], u1 = s_u[1], u2 = s_u[2], u3 = s_u[3];
+    MTile m0 = tile_of(u0), m1 = tile_of(u1), m2 = tile_of(u2);
     int t1 = tok_of(m1);
     if (warp == 0 && u0 < nu) issue(u0, 0, m0, tok_of(m0));
     bool ok = true;
-    int it = 0, hb = 0;  // hb: the h buffer, switched per unit with rows
-    for (int u = u0; u < nu; u += step, ++it) {
+    for (int it = 0; u0 < nu; ++it) {
         const int s = it & 1;
         const MTile mt = m0;
-        const int rb = u % rb_n;
-        if (warp == 0 && u + step < nu) issue(u + step, s ^ 1, m1, t1);
+        const int rb = u0 % rb_n;
+        if (warp == 0 && u1 < nu) issue(u1, s ^ 1, m1, t1);
+        int grab = 0;
+        if (tid == 0) grab = atomicAdd(a.ctr, 1);  // unit it + 4
         {
-            const MTile m3 = tile_of(u + 3 * step);
+            const MTile m3 = tile_of(u3);
             t1 = tok_of(m2);
             m0 = m1;
             m1 = m2;
             m2 = m3;
         }
         if (!mbar_wait(&sbar[s], (it >> 1) & 1)) ok = false;
-        if (mt.rows == 0) continue;
         const uint8_t *W = smem + s * stage;
         const uint8_t *xs = W + wbytes;
         const int nb = mt.rows;
-        float *hbuf = hbuf0 + hb * kSbBatch * 32;
-        hb ^= 1;
+        float *hbuf = hbuf0 + (it & 1) * kSbBatch * 32;
         {
             // warp w: rows w and w + 16, the lane's group of each in registers
             // (the prefill path's scale groups are 64 wide)
@@ -1141,7 +1149,12 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
             for (int jj = 0; jj < nb; ++jj) sb_gu_tokens<1>(xs, xrow, n, act, lane, jj, gw, uw, sb, hbuf, warp);
         }
         // the stage is refilled two units on, after the next unit's barrier
+        if (tid == 0) s_u[it & 3] = grab;
         __syncthreads();
+        u0 = u1;
+        u1 = u2;
+        u2 = u3;
+        u3 = s_u[it & 3];
         // h of the tile's rows over this unit's 32 rows -> 24-bit planes with
         // their own scale (lanes 4 jj .. 4 jj + 3: token jj's words); the
         // next unit writes the other buffer
@@ -1165,6 +1178,7 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_gu(SbArgs a) {
         }
     }
     if (!ok && tid == 0) atomicOr(a.err, QK_ERR_TIMEOUT_COPY);
+    sb_finish(a.ctr);
 }
 
 // Down: unit = (small tile of at most kSbBatch rows, 128 down rows). A stage
@@ -1182,6 +1196,7 @@ template <int LPR>
 __global__ void __launch_bounds__(kSbThreads, 1) k_sb_dn(SbArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t sbar[3];
+    __shared__ int s_u[4];
     constexpr int RPW = 32 / LPR;                                  // rows a warp holds at once
     constexpr int P = kSbDnRows / ((kSbThreads / 32) * RPW) > 0    // rows a lane group holds
                           ? kSbDnRows / ((kSbThreads / 32) * RPW) : 1;
@@ -1196,22 +1211,16 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_dn(SbArgs a) {
         mbar_init(&sbar[1], 1);
         mbar_init(&sbar[2], 1);
     }
-    __syncthreads();
     const int db_n = d / kSbDnRows;
     const int nu = *a.n_tiles * db_n;
-    const int step = gridDim.x;
+    sb_take_first(a.ctr, s_u);  // (its barrier also publishes the barrier inits)
     auto tile_of = [&](int u) {
         MTile m = {0, 0, 0, 0};
         if (u < nu) m = a.tiles[u / db_n];
-        if (m.rows > a.max_rows) m.rows = 0;  // left to the tensor cores
         return m;
     };
     auto issue = [&](int u, int s, const MTile &mt) {
         uint8_t *dst = smem + s * stage;
-        if (mt.rows == 0) {
-            mbar_expect_tx(&sbar[s], 0u);
-            return;
-        }
         mbar_expect_tx(&sbar[s], wbytes + static_cast<uint32_t>(mt.rows * hrow));
         bulk_load(dst, a.pool + static_cast<size_t>(mt.slot) * L.slot_bytes + L.gu_bytes +
                            static_cast<size_t>(u % db_n) * kSbDnRows * L.d_row,
@@ -1219,31 +1228,33 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_dn(SbArgs a) {
         bulk_load(dst + wbytes, a.hq + static_cast<size_t>(mt.m0) * hrow,
                   static_cast<uint32_t>(mt.rows * hrow), &sbar[s]);
     };
-    const int u0 = blockIdx.x;
-    MTile m0 = tile_of(u0), m1 = tile_of(u0 + step), m2 = tile_of(u0 + 2 * step);
+    // units u0 (computing), u1 and u2 (stages in flight), u3 (descriptor read)
+    int u0 = s_u[0], u1 = s_u[1], u2 = s_u[2], u3 = s_u[3];
+    MTile m0 = tile_of(u0), m1 = tile_of(u1), m2 = tile_of(u2);
     if (tid == 0) {
         if (u0 < nu) issue(u0, 0, m0);
-        if (u0 + step < nu) issue(u0 + step, 1, m1);
+        if (u1 < nu) issue(u1, 1, m1);
     }
     bool ok = true;
-    int it = 0, yb = 0;  // yb: the Y buffer, switched per unit with rows
-    for (int u = u0; u < nu; u += step, ++it) {
+    for (int it = 0; u0 < nu; ++it) {
         const int s = it % 3;
         const MTile mt = m0;
-        const int db = u % db_n;
-        if (tid == 0 && u + 2 * step < nu) issue(u + 2 * step, (it + 2) % 3, m2);
+        const int db = u0 % db_n;
+        int grab = 0;
+        if (tid == 0) {
+            if (u2 < nu) issue(u2, (it + 2) % 3, m2);
+            grab = atomicAdd(a.ctr, 1);  // unit it + 4
+        }
         {
-            const MTile m3 = tile_of(u + 3 * step);
+            const MTile m3 = tile_of(u3);
             m0 = m1;
             m1 = m2;
             m2 = m3;
         }
         if (!mbar_wait(&sbar[s], (it / 3) & 1)) ok = false;
-        if (mt.rows == 0) continue;
         const uint8_t *W = smem + s * stage;
         const uint8_t *hs = W + wbytes;
-        float *ys = ys0 + yb * kSbBatch * kSbDnRows;
-        yb ^= 1;
+        float *ys = ys0 + (it & 1) * kSbBatch * kSbDnRows;
         const int j = lane % LPR;
         if (warp * RPW < kSbDnRows) {
             // the lane group's P rows, weights in registers (scale group of
@@ -1264,37 +1275,61 @@ __global__ void __launch_bounds__(kSbThreads, 1) k_sb_dn(SbArgs a) {
         }
         // one barrier a unit: the stage and this ys buffer are reused only
         // after later barriers
+        if (tid == 0) s_u[it & 3] = grab;
         __syncthreads();
+        u0 = u1;
+        u1 = u2;
+        u2 = u3;
+        u3 = s_u[it & 3];
         for (int i = tid; i < mt.rows * kSbDnRows; i += kSbThreads)
             a.Y[static_cast<size_t>(mt.m0 + i / kSbDnRows) * d + db * kSbDnRows + i % kSbDnRows] = ys[i];
     }
     if (!ok && tid == 0) atomicOr(a.err, QK_ERR_TIMEOUT_COPY);
+    sb_finish(a.ctr);
 }
 
-// The tiles of more than max_rows rows, in list order, by one CTA: the
-// tensor-core kernels launched after k_sb_gu take these.
-QK_DEV void list_heavy_tiles(const MTile *tiles, int n, int max_rows, MTile *out, int *n_out,
-                             int *s_cnt) {
+// The small tiles split in list order by one CTA: those of at most max_rows
+// rows (k_sb_*) and the others (k_gemm_sw). s_cnt: 2 x 32 ints of shared
+// memory.
+QK_DEV void split_tiles(const MTile *tiles, int n, int max_rows, MTile *light, int *n_light,
+                        MTile *heavy, int *n_heavy, int *s_cnt) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
-    int base = 0;
+    int base_l = 0, base_h = 0;
     for (int i0 = 0; i0 < n; i0 += blockDim.x) {
         const int i = i0 + tid;
         MTile m = {0, 0, 0, 0};
         if (i < n) m = tiles[i];
-        const bool heavy = i < n && m.rows > max_rows;
-        const unsigned b = __ballot_sync(QK_FULL, heavy);
-        if (lane == 0) s_cnt[warp] = __popc(b);
-        __syncthreads();
-        int before = 0, total = 0;
-        for (int w = 0; w < nw; ++w) {
-            before += w < warp ? s_cnt[w] : 0;
-            total += s_cnt[w];
+        const bool hv = i < n && m.rows > max_rows, lt = i < n && !hv;
+        const unsigned bh = __ballot_sync(QK_FULL, hv), bl = __ballot_sync(QK_FULL, lt);
+        if (lane == 0) {
+            s_cnt[warp] = __popc(bl);
+            s_cnt[32 + warp] = __popc(bh);
         }
-        if (heavy) out[base + before + __popc(b & ((1u << lane) - 1u))] = m;
-        base += total;
+        __syncthreads();
+        int before_l = 0, before_h = 0, total_l = 0, total_h = 0;
+        for (int w = 0; w < nw; ++w) {
+            before_l += w < warp ? s_cnt[w] : 0;
+            before_h += w < warp ? s_cnt[32 + w] : 0;
+            total_l += s_cnt[w];
+            total_h += s_cnt[32 + w];
+        }
+        const unsigned below = (1u << lane) - 1u;
+        if (lt) light[base_l + before_l + __popc(bl & below)] = m;
+        if (hv) heavy[base_h + before_h + __popc(bh & below)] = m;
+        base_l += total_l;
+        base_h += total_h;
         __syncthreads();
     }
-    if (tid == 0) *n_out = base;
+    if (tid == 0) {
+        *n_light = base_l;
+        *n_heavy = base_h;
+    }
+}
+
+__global__ void k_split_tiles(const MTile *tiles, const int *n_tiles, int max_rows, MTile *light,
+                              int *n_light, MTile *heavy, int *n_heavy) {
+    __shared__ int s_cnt[64];
+    split_tiles(tiles, *n_tiles, max_rows, light, n_light, heavy, n_heavy, s_cnt);
 }
 
 // ---------------------------------------------------------------------------
@@ -1485,7 +1520,12 @@ enum { XK_F32 = 0, XK_BF16 = 1, XK_F16 = 2 };
 //   k_sb_dn   unit = (small tile, 64 down rows): Y[row][d0 .. d0 + 64) fp32
 // k_combine then runs as on the tensor-core path.
 // One CTA per token, one thread per q4 word position (d / 8 <= 1024).
-__global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq) {
+// Block 0 also splits the call's small tiles (tiles != nullptr) into the
+// light and heavy lists.
+__global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, const MTile *tiles,
+                        const int *n_tiles, int max_rows, MTile *light, int *n_light, MTile *heavy,
+                        int *n_heavy) {
+    __shared__ int s_cnt[64];
     const int t = blockIdx.x, w = threadIdx.x, n = d / 8;
     float v[8];
 #pragma unroll
@@ -1519,6 +1559,7 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq) {
         store_word_gx<2>(reinterpret_cast<uint2 *>(row), n, w, pl);
         if ((w & 7) == 0) reinterpret_cast<float2 *>(row + n * 16)[w >> 3] = make_float2(sc, gsum);
     }
+    if (t == 0 && tiles != nullptr) split_tiles(tiles, *n_tiles, max_rows, light, n_light, heavy, n_heavy, s_cnt);
 }
 
 
@@ -2048,8 +2089,11 @@ struct qk_prefill {
     int sb;                         // small tiles on the CUDA cores (k_sb_*) instead of k_gemm_sw
     int sb_max_rows;                // ... those of at most this many rows; k_gemm_sw the others
     uint8_t *sb_xq, *sb_hq;         // their quantised x per token, h per grouped row
-    MTile *htiles;                  // the small tiles of more than sb_max_rows rows
-    int *n_htiles;
+    MTile *ltiles, *htiles;         // the small tiles of at most / more than sb_max_rows rows
+    int *n_ltiles, *n_htiles;
+    int *sb_ctr;                    // [4]: k_sb_gu's and k_sb_dn's unit counters (0 between launches)
+    cudaStream_t st2;               // k_gemm_sw on the heavy tiles, beside k_sb_* ...
+    cudaEvent_t ev_fork, ev_join;   // ... forked from and joined back into the call's stream
     const uint8_t *pool;            // the weight pool the expert slots index
     int *counts, *cursor, *row0, *inv, *perm_tok, *n_mtiles, *n_stiles, *n_rows;
     MTile *tiles, *stiles;          // BM-row tiles (k_gemm), NS-row tiles (k_gemm_sw)
@@ -2105,6 +2149,12 @@ extern "C" void qk_prefill_destroy(qk_prefill *p) {
     cudaFree(p->sb_hq);
     cudaFree(p->htiles);
     cudaFree(p->n_htiles);
+    cudaFree(p->ltiles);
+    cudaFree(p->n_ltiles);
+    cudaFree(p->sb_ctr);
+    if (p->st2) cudaStreamDestroy(p->st2);
+    if (p->ev_fork) cudaEventDestroy(p->ev_fork);
+    if (p->ev_join) cudaEventDestroy(p->ev_join);
     cudaFree(p->xp);
     cudaFree(p->H);
     cudaFree(p->Y);
@@ -2189,6 +2239,13 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
     if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->sb_hq, R * sb_hrow(L->I));
     if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->htiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
     if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->n_htiles, sizeof(int));
+    if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->ltiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
+    if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->n_ltiles, sizeof(int));
+    if (e == cudaSuccess && p->sb) e = cudaMalloc(&p->sb_ctr, 4 * sizeof(int));
+    if (e == cudaSuccess && p->sb) e = cudaMemset(p->sb_ctr, 0, 4 * sizeof(int));
+    if (e == cudaSuccess && p->sb) e = cudaStreamCreateWithFlags(&p->st2, cudaStreamNonBlocking);
+    if (e == cudaSuccess && p->sb) e = cudaEventCreateWithFlags(&p->ev_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess && p->sb) e = cudaEventCreateWithFlags(&p->ev_join, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc(&p->wtiles, sizeof(MTile) * p->tiles_max);
     if (e == cudaSuccess) e = cudaMalloc(&p->wstiles, sizeof(MTile) * (L->E + 1) * (kSmallMax / NS));
     if (e == cudaSuccess) e = cudaMalloc(&p->n_wtiles, 2 * sizeof(int));
@@ -2334,8 +2391,12 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     // small groups on the CUDA cores: x quantised per token (by the plan
     // phase; the waves of a call read it) instead of the grouped fp16 rows
     const bool sb = all_small && p->sb;
+    const bool xq_split = sb && (phases & 1) && !wave && T > 0;  // xq's block 0 splits the tiles
     if (sb && (phases & 1) && T > 0)
-        k_sb_xq<<<T, (L.d / 8 + 31) / 32 * 32, 0, st>>>(x, x_kind, L.d, T, p->sb_xq);
+        k_sb_xq<<<T, (L.d / 8 + 31) / 32 * 32, 0, st>>>(x, x_kind, L.d, T, p->sb_xq,
+                                                       xq_split ? p->stiles : nullptr, p->n_stiles,
+                                                       p->sb_max_rows, p->ltiles, p->n_ltiles,
+                                                       p->htiles, p->n_htiles);
     if ((phases & 1) && rows > 0)
         k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->n_rows,
                                                          p->perm_tok, p->xp,
@@ -2355,10 +2416,11 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     };
     auto fn = [](auto f) { return reinterpret_cast<const void *>(f); };
     auto launch_sw = [&](const void *f, int smem, const CUtensorMap *a, const CUtensorMap *a8,
-                         const CUtensorMap *q, const CUtensorMap *sc, GemmArgs *ga) {
+                         const CUtensorMap *q, const CUtensorMap *sc, GemmArgs *ga,
+                         cudaStream_t on = nullptr) {
         void *args[] = {const_cast<CUtensorMap *>(a), const_cast<CUtensorMap *>(a8),
                         const_cast<CUtensorMap *>(q), const_cast<CUtensorMap *>(sc), ga};
-        return qk_launch_raw(f, dim3(p->num_sms), dim3(kThreadsSw), smem, st, 0, args);
+        return qk_launch_raw(f, dim3(p->num_sms), dim3(kThreadsSw), smem, on ? on : st, 0, args);
     };
     GemmArgs gu;
     memset(&gu, 0, sizeof(gu));
@@ -2381,9 +2443,33 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     dn.out = nullptr;
     dn.outf = p->Y;
     if (sb) {
+        if (!xq_split) {
+            k_split_tiles<<<1, 1024, 0, st>>>(stl, nstl, p->sb_max_rows, p->ltiles, p->n_ltiles, p->htiles,
+                                              p->n_htiles);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+        }
+        // the heavy tiles on the tensor cores, on the second stream beside
+        // k_sb_* (which take their units from a counter, so they fill the
+        // SMs k_gemm_sw leaves)
+        e = cudaEventRecord(p->ev_fork, st);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->st2, p->ev_fork, 0);
+        if (e != cudaSuccess) return e;
+        gu.NT = L.I / 128;
+        gu.tiles = p->htiles;
+        gu.n_mtiles = p->n_htiles;
+        e = lo ? launch_sw(fn(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs, &p->tmXs8, &p->tmQgu4, &p->tmSgu4, &gu, p->st2)
+               : launch_sw(fn(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs, &p->tmXs8, &p->tmQgu4, &p->tmSgu4, &gu, p->st2);
+        if (e != cudaSuccess) return e;
+        dn.NT = L.d / 256;
+        dn.tiles = p->htiles;
+        dn.n_mtiles = p->n_htiles;
+        e = launch_sw(fn(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs, &p->tmHs8, &p->tmQdn4, &p->tmSdn4, &dn, p->st2);
+        if (e == cudaSuccess) e = cudaEventRecord(p->ev_join, p->st2);
+        if (e != cudaSuccess) return e;
         SbArgs sa;
-        sa.tiles = stl;
-        sa.n_tiles = nstl;
+        sa.tiles = p->ltiles;
+        sa.n_tiles = p->n_ltiles;
         sa.nsh = nsh;
         sa.perm_tok = p->perm_tok;
         sa.pool = p->pool;
@@ -2391,29 +2477,18 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         sa.xq = p->sb_xq;
         sa.hq = p->sb_hq;
         sa.Y = p->Y;
-        sa.max_rows = p->sb_max_rows;
-        sa.heavy = p->htiles;      // the tiles of more rows: k_gemm_sw, on this list
-        sa.n_heavy = p->n_htiles;
+        sa.ctr = p->sb_ctr;
         sa.err = err;
         void *args[] = {&sa};
         e = qk_launch_raw(reinterpret_cast<const void *>(&k_sb_gu), dim3(p->num_sms), dim3(kSbThreads),
                           sb_gu_smem(L), st, 0, args);
         if (e != cudaSuccess) return e;
-        gu.NT = L.I / 128;
-        gu.tiles = p->htiles;
-        gu.n_mtiles = p->n_htiles;
-        e = lo ? launch_sw(fn(&k_gemm_sw<3>), CfgS<3>::Smem, &p->tmXs, &p->tmXs8, &p->tmQgu4, &p->tmSgu4, &gu)
-               : launch_sw(fn(&k_gemm_sw<0>), CfgS<0>::Smem, &p->tmXs, &p->tmXs8, &p->tmQgu4, &p->tmSgu4, &gu);
-        if (e != cudaSuccess) return e;
         mark(1);
+        sa.ctr = p->sb_ctr + 2;
         const void *dfn = L.I == 128 ? reinterpret_cast<const void *>(&k_sb_dn<4>)
                                      : reinterpret_cast<const void *>(&k_sb_dn<16>);
         e = qk_launch_raw(dfn, dim3(p->num_sms), dim3(kSbThreads), sb_dn_smem(L), st, 0, args);
-        if (e != cudaSuccess) return e;
-        dn.NT = L.d / 256;
-        dn.tiles = p->htiles;
-        dn.n_mtiles = p->n_htiles;
-        e = launch_sw(fn(&k_gemm_sw<1>), CfgS<1>::Smem, &p->tmHs, &p->tmHs8, &p->tmQdn4, &p->tmSdn4, &dn);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, p->ev_join, 0);
         if (e != cudaSuccess) return e;
     } else if (all_small) {
         gu.NT = L.I / 128;
