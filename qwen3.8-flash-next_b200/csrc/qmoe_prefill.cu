@@ -1522,9 +1522,13 @@ enum { XK_F32 = 0, XK_BF16 = 1, XK_F16 = 2 };
 // One CTA per token, one thread per q4 word position (d / 8 <= 1024).
 // Block 0 also splits the call's small tiles (tiles != nullptr) into the
 // light and heavy lists.
+// It also writes the token's rows of the grouped fp16 A operand of the
+// tensor-core kernels (as k_gather: row t for t < nsh, the row inv[t, s] of
+// each slot with an expert id >= 0; the lo plane for fp32 x).
 __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, const MTile *tiles,
                         const int *n_tiles, int max_rows, MTile *light, int *n_light, MTile *heavy,
-                        int *n_heavy) {
+                        int *n_heavy, const int32_t *idx, int k, int nsh, const int *inv, __half *xp,
+                        size_t lo_plane) {
     __shared__ int s_cnt[64];
     const int t = blockIdx.x, w = threadIdx.x, n = d / 8;
     float v[8];
@@ -1558,6 +1562,33 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, co
     if (w < n) {
         store_word_gx<2>(reinterpret_cast<uint2 *>(row), n, w, pl);
         if ((w & 7) == 0) reinterpret_cast<float2 *>(row + n * 16)[w >> 3] = make_float2(sc, gsum);
+    }
+    if (w < n) {
+        uint4 o;
+        o.x = h2u(__floats2half2_rn(v[0], v[4]));
+        o.y = h2u(__floats2half2_rn(v[1], v[5]));
+        o.z = h2u(__floats2half2_rn(v[2], v[6]));
+        o.w = h2u(__floats2half2_rn(v[3], v[7]));
+        uint4 ol = make_uint4(0u, 0u, 0u, 0u);
+        if (x_kind == XK_F32) {
+            // lo = fp16(x - hi): the pair carries x to about 22 bits
+            const float2 h0 = __half22float2(u2h(o.x)), h1 = __half22float2(u2h(o.y)),
+                         h2 = __half22float2(u2h(o.z)), h3 = __half22float2(u2h(o.w));
+            ol.x = h2u(__floats2half2_rn(v[0] - h0.x, v[4] - h0.y));
+            ol.y = h2u(__floats2half2_rn(v[1] - h1.x, v[5] - h1.y));
+            ol.z = h2u(__floats2half2_rn(v[2] - h2.x, v[6] - h2.y));
+            ol.w = h2u(__floats2half2_rn(v[3] - h3.x, v[7] - h3.y));
+        }
+        for (int sl = t < nsh ? -1 : 0; sl < k; ++sl) {
+            int r = t;
+            if (sl >= 0) {
+                if (idx[static_cast<size_t>(t) * k + sl] < 0) continue;
+                r = inv[static_cast<size_t>(t) * k + sl];
+            }
+            __half *dst = xp + static_cast<size_t>(r) * d;
+            reinterpret_cast<uint4 *>(dst)[w] = o;
+            if (x_kind == XK_F32) reinterpret_cast<uint4 *>(dst + lo_plane)[w] = ol;
+        }
     }
     if (t == 0 && tiles != nullptr) split_tiles(tiles, *n_tiles, max_rows, light, n_light, heavy, n_heavy, s_cnt);
 }
@@ -2396,8 +2427,9 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
         k_sb_xq<<<T, (L.d / 8 + 31) / 32 * 32, 0, st>>>(x, x_kind, L.d, T, p->sb_xq,
                                                        xq_split ? p->stiles : nullptr, p->n_stiles,
                                                        p->sb_max_rows, p->ltiles, p->n_ltiles,
-                                                       p->htiles, p->n_htiles);
-    if ((phases & 1) && rows > 0)
+                                                       p->htiles, p->n_htiles, idx, k, nsh, p->inv,
+                                                       p->xp, static_cast<size_t>(p->rows_max) * L.d);
+    else if ((phases & 1) && rows > 0)
         k_gather<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, x_kind, L.d, nsh, rows, p->n_rows,
                                                          p->perm_tok, p->xp,
                                                          static_cast<size_t>(p->rows_max) * L.d);
