@@ -151,9 +151,11 @@ def bench_config(world=1):
             "l2": "inputs larger than L2: 906 MB of experts per layer vs 126 MB L2; "
                   "router and shared expert (3.9 MB) stay L2-resident across tokens",
             "activations": "decode: x as 16-bit and h as 24-bit block fixed point (one power-of-two "
-                           "scale per 32 values) in integer dot products with the q4 weights; "
-                           "prefill: fp16 tensor-core operands (h as an fp16 hi/lo pair), fp32 "
-                           "accumulation; router fp64 in a fixed order; outputs fp32"}
+                           "scale per 64 values) in integer dot products with the q4 weights; "
+                           "multi-token calls: expert groups of at most 4 tokens the same way "
+                           "(h scaled per 32 values), larger ones on fp16 tensor-core operands "
+                           "(h as an fp16 hi/lo pair), fp32 accumulation; router fp64 in a fixed "
+                           "order; outputs fp32"}
 
 
 def _cpu_impl():
