@@ -1866,6 +1866,88 @@ __global__ void k_route_split(const void *x, int x_bf16, int d, int T, int Tpad,
     if (lane == 0) xnorm[warp] = __double2float_ru(sqrt(ss));
 }
 
+// Small calls (T <= kRouteSmallT): the approximate logits on the CUDA cores
+// in fp32, in place of k_route_split + k_gemm<2>. CTA (32 experts, 8 tokens),
+// 16 warps; warp w takes experts e0 + 2w and e0 + 2w + 1 for the 8 tokens,
+// lane l the elements 8l + 256i + (0..7) of each, the 16 sums reduced by a
+// halving butterfly. Along any path an fp32 sum here meets at most 69
+// roundings, far inside the bound k_route_exact allows for (2^-10 |x| max|w|),
+// so its candidate sets still hold the exact top-k. The first expert block
+// also writes the tokens' 2-norms exactly as k_route_split does.
+constexpr int kRouteSmallT = 64, kRaTok = 8, kRaExp = 32;
+
+__global__ void __launch_bounds__(512) k_route_approx(const void *x, int x_bf16, int d, int T, int E,
+                                                       const uint16_t *router, float *lga, float *xnorm) {
+    extern __shared__ __align__(16) float xsa[];  // [kRaTok][d] fp32
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e0 = blockIdx.x * kRaExp, t0 = blockIdx.y * kRaTok;
+    const int nt = min(kRaTok, T - t0);
+    auto load8 = [&](int t, int c, float (&v)[8]) {
+        if (x_bf16) {
+            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
+                                                            static_cast<size_t>(t) * d)[c];
+            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
+            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
+        } else {
+            const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
+                                                               static_cast<size_t>(t) * d) + 2 * c;
+            const float4 a = q[0], b = q[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+    };
+    for (int i = threadIdx.x; i < kRaTok * (d / 8); i += blockDim.x) {
+        const int tt = i / (d / 8), c = i % (d / 8);
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (tt < nt) load8(t0 + tt, c, v);
+        float4 *dst = reinterpret_cast<float4 *>(xsa + static_cast<size_t>(tt) * d) + 2 * c;
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    if (blockIdx.x == 0 && warp < nt) {
+        double ss = 0.0;
+        for (int c = lane; c < d / 8; c += 32) {
+            float v[8];
+            load8(t0 + warp, c, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+        }
+        ss = warp_sum_butterfly(ss);
+        if (lane == 0) xnorm[t0 + warp] = __double2float_ru(sqrt(ss));
+    }
+    __syncthreads();
+    const int ea = e0 + 2 * warp;
+    float acc[2 * kRaTok];
+#pragma unroll
+    for (int i = 0; i < 2 * kRaTok; ++i) acc[i] = 0.f;
+    for (int k0 = 8 * lane; k0 < d; k0 += 256) {
+        uint4 q[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+            q[j] = ea + j < E ? *reinterpret_cast<const uint4 *>(router + static_cast<size_t>(ea + j) * d + k0)
+                              : make_uint4(0u, 0u, 0u, 0u);
+        float w[2][8];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            w[j][0] = bf16lo(q[j].x); w[j][1] = bf16hi(q[j].x); w[j][2] = bf16lo(q[j].y); w[j][3] = bf16hi(q[j].y);
+            w[j][4] = bf16lo(q[j].z); w[j][5] = bf16hi(q[j].z); w[j][6] = bf16lo(q[j].w); w[j][7] = bf16hi(q[j].w);
+        }
+#pragma unroll
+        for (int tt = 0; tt < kRaTok; ++tt) {
+            const float4 *xp = reinterpret_cast<const float4 *>(xsa + static_cast<size_t>(tt) * d + k0);
+            const float4 a = xp[0], b = xp[1];
+            const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[j * kRaTok + tt] = fmaf(xv[i], w[j][i], acc[j * kRaTok + tt]);
+        }
+    }
+    // lane l: the sum of value l / 2 = (expert ea + (l / 2) / 8, token (l / 2) % 8)
+    const float sum = group_sum_tr<2 * kRaTok, 32>(acc, lane);
+    const int v = lane >> 1, ee = ea + v / kRaTok, tt = v % kRaTok;
+    if ((lane & 1) == 0 && tt < nt && ee < E) lga[static_cast<size_t>(t0 + tt) * E + ee] = sum;
+}
+
 struct RouteArgs {
     const void *x;
     int x_bf16, d, E, k, T;
@@ -2347,6 +2429,15 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
                          static_cast<int>(p->route_smem)};
     for (int i = 0; i < (p->route_ok ? 9 : 6); ++i) {
         e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem[i]);
+        if (e != cudaSuccess) {
+            snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
+            qk_prefill_destroy(p);
+            return nullptr;
+        }
+    }
+    if (p->route_ok) {
+        e = cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_route_approx),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kRaTok * L->d * 4);
         if (e != cudaSuccess) {
             snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
             qk_prefill_destroy(p);
@@ -2898,6 +2989,8 @@ extern "C" int qk_ep_finish(qk_prefill *p, const qk_fwd *f, void *stream) {
     return cudaGetLastError();
 }
 
+static int route_exact(qk_prefill *p, const qk_fwd *f, float wmax, cudaStream_t st, void *mid_event);
+
 extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void *stream,
                                void *mid_event) {
     if (!p->route_ok) return QK_ROUTE_UNFIT;
@@ -2905,9 +2998,18 @@ extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void 
     const int T = f->T, E = L.E;
     if (T > p->max_tokens) return cudaErrorInvalidValue;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (T <= kRouteSmallT) {
+        k_route_approx<<<dim3((E + kRaExp - 1) / kRaExp, (T + kRaTok - 1) / kRaTok), 512,
+                         kRaTok * L.d * sizeof(float), st>>>(f->x, f->x_bf16, L.d, T, E, f->router,
+                                                             p->lga, p->xnorm);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        return route_exact(p, f, wmax, st, mid_event);
+    }
     k_route_split<<<(T * 32 + 255) / 256, 256, 0, st>>>(f->x, f->x_bf16, L.d, T, p->Tpad, p->xr,
                                                        p->xnorm, p->rtiles, p->rn);
-    cudaError_t e = cudaGetLastError();
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     CUtensorMap tmR;
     if (!map_2d_16(&tmR, f->router, L.d, E, true, 256)) return cudaErrorInvalidValue;
@@ -2944,6 +3046,14 @@ extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void 
                           Cfg<2>::Smem, stream, 0, args);
         if (e != cudaSuccess) return e;
     }
+    return route_exact(p, f, wmax, st, mid_event);
+}
+
+// The exact re-ranking of the approximate logits in p->lga (after either
+// approximate pass).
+static int route_exact(qk_prefill *p, const qk_fwd *f, float wmax, cudaStream_t st, void *mid_event) {
+    const qk_layout &L = p->L;
+    const int T = f->T, E = L.E;
     if (mid_event) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(mid_event), st, cudaEventRecordExternal);
     RouteArgs a;
     a.x = f->x;

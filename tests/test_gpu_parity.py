@@ -306,3 +306,47 @@ def test_pool_smaller_than_a_call_runs_in_waves(cfg1_layer, cfg1_ctx):
     assert st["expert_waves"] >= 2 * 16  # both calls ran in many waves
     assert ctx.cache_stats()["size"] <= 16
     ctx.close()
+
+
+def test_small_tile_splits_match_restatement(built):
+    """A 64-token call with a Zipf(1.1) router bias touches 51 experts with
+    groups of 1 to 63 tokens. Groups of at most QMOE_SB_MAX_ROWS tokens run on
+    the CUDA cores (integer dot products, k_sb_gu / k_sb_dn), the others on the
+    tensor cores (k_gemm_sw) on a second stream beside them; QMOE_SMALL_PATH=tc
+    keeps every group on the tensor cores. Every split (1, the default 4, 8,
+    tensor cores only) gives the restatement's routing, and outputs within the
+    tight bars, and the splits agree with each other."""
+    import oracle
+    import qmoe
+    cfg = qmoe.make_config(2048, 512, 10, 512, max_tokens=64)
+    s = qmoe.SynthLayer(cfg, 20261207, zipf_s=1.1)
+    x = qmoe.synth_tokens(20261207, 1, 64, 2048)
+    ro, ri, rw = oracle.restatement().forward(s, x)
+    sizes = np.bincount(ri.ravel(), minlength=512)
+    # the group sizes fall on both sides of every split below
+    for m in (1, 4, 8):
+        assert ((sizes >= 1) & (sizes <= m)).any() and (sizes > m).any(), m
+    keys = ("QMOE_SB_MAX_ROWS", "QMOE_SMALL_PATH")
+    outs = {}
+    for name, env in (("max_rows 1", {"QMOE_SB_MAX_ROWS": "1"}), ("default", {}),
+                      ("max_rows 8", {"QMOE_SB_MAX_ROWS": "8"}), ("tensor cores", {"QMOE_SMALL_PATH": "tc"})):
+        saved = {k: os.environ.pop(k, None) for k in keys}
+        os.environ.update(env)
+        try:
+            ctx = qmoe.Context(cfg)  # the switches are read when the context is made
+            ctx.upload(0, s)
+            out = ctx.forward(0, x)
+            idx, w, _ = ctx.routing(64)
+            ctx.close()
+        finally:
+            for k in keys:
+                os.environ.pop(k, None)
+                if saved[k] is not None:
+                    os.environ[k] = saved[k]
+        assert np.array_equal(idx, ri), name
+        np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-6)
+        _close(out, ro, f"64-token Zipf call, small tiles: {name}", TIGHT)
+        outs[name] = out
+    base = outs["tensor cores"]
+    for name, out in outs.items():
+        _close(out, base, f"64-token Zipf call, {name} vs tensor cores", TIGHT)
