@@ -1530,7 +1530,14 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, co
                         int *n_heavy, const int32_t *idx, int k, int nsh, const int *inv, __half *xp,
                         size_t lo_plane) {
     __shared__ int s_cnt[64];
+    __shared__ int s_row[33];  // the token's rows of the grouped operand (-1: none)
     const int t = blockIdx.x, w = threadIdx.x, n = d / 8;
+    for (int i = w; i <= k; i += blockDim.x) {
+        int r = -1;
+        if (i == k) r = t < nsh ? t : -1;
+        else if (idx[static_cast<size_t>(t) * k + i] >= 0) r = inv[static_cast<size_t>(t) * k + i];
+        s_row[i] = r;
+    }
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.f;
@@ -1563,13 +1570,12 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, co
         store_word_gx<2>(reinterpret_cast<uint2 *>(row), n, w, pl);
         if ((w & 7) == 0) reinterpret_cast<float2 *>(row + n * 16)[w >> 3] = make_float2(sc, gsum);
     }
+    uint4 o = make_uint4(0u, 0u, 0u, 0u), ol = make_uint4(0u, 0u, 0u, 0u);
     if (w < n) {
-        uint4 o;
         o.x = h2u(__floats2half2_rn(v[0], v[4]));
         o.y = h2u(__floats2half2_rn(v[1], v[5]));
         o.z = h2u(__floats2half2_rn(v[2], v[6]));
         o.w = h2u(__floats2half2_rn(v[3], v[7]));
-        uint4 ol = make_uint4(0u, 0u, 0u, 0u);
         if (x_kind == XK_F32) {
             // lo = fp16(x - hi): the pair carries x to about 22 bits
             const float2 h0 = __half22float2(u2h(o.x)), h1 = __half22float2(u2h(o.y)),
@@ -1579,12 +1585,12 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, co
             ol.z = h2u(__floats2half2_rn(v[2] - h2.x, v[6] - h2.y));
             ol.w = h2u(__floats2half2_rn(v[3] - h3.x, v[7] - h3.y));
         }
-        for (int sl = t < nsh ? -1 : 0; sl < k; ++sl) {
-            int r = t;
-            if (sl >= 0) {
-                if (idx[static_cast<size_t>(t) * k + sl] < 0) continue;
-                r = inv[static_cast<size_t>(t) * k + sl];
-            }
+    }
+    __syncthreads();
+    if (w < n) {
+        for (int sl = 0; sl <= k; ++sl) {
+            const int r = s_row[sl];
+            if (r < 0) continue;
             __half *dst = xp + static_cast<size_t>(r) * d;
             reinterpret_cast<uint4 *>(dst)[w] = o;
             if (x_kind == XK_F32) reinterpret_cast<uint4 *>(dst + lo_plane)[w] = ol;
@@ -1653,29 +1659,31 @@ __global__ void k_gather(const void *x, int x_kind, int d, int nsh, int rows, co
 // issued before the sums.
 __global__ void k_combine(const float *Yr, const float *Ysh, const int *inv, const float *wts,
                           const float *sgate, int k, int d, float *out) {
+    // the token's k + 1 row pointers and weights first, so that a thread's
+    // row loads go out together (8 at a time), summed in slot order
+    __shared__ const float *s_y[33];
+    __shared__ float s_w[33];
     const int t = blockIdx.x;
+    for (int s = threadIdx.x; s <= k; s += blockDim.x) {
+        s_y[s] = s < k ? Yr + static_cast<size_t>(inv[t * k + s]) * d : Ysh + static_cast<size_t>(t) * d;
+        s_w[s] = s < k ? wts[t * k + s] : sgate[t];
+    }
+    __syncthreads();
     for (int c = threadIdx.x; c < d / 4; c += blockDim.x) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s0 = 0; s0 <= k; s0 += 4) {
-            float4 v[4];
-            float w[4];
+        for (int s0 = 0; s0 <= k; s0 += 8) {
+            float4 v[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int s = s0 + u;
-                if (s <= k) {
-                    const float *Y = s < k ? Yr + static_cast<size_t>(inv[t * k + s]) * d
-                                           : Ysh + static_cast<size_t>(t) * d;
-                    w[u] = s < k ? wts[t * k + s] : sgate[t];
-                    v[u] = reinterpret_cast<const float4 *>(Y)[c];
-                }
-            }
+            for (int u = 0; u < 8; ++u)
+                if (s0 + u <= k) v[u] = reinterpret_cast<const float4 *>(s_y[s0 + u])[c];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 8; ++u) {
                 if (s0 + u <= k) {
-                    acc.x = fmaf(w[u], v[u].x, acc.x);
-                    acc.y = fmaf(w[u], v[u].y, acc.y);
-                    acc.z = fmaf(w[u], v[u].z, acc.z);
-                    acc.w = fmaf(w[u], v[u].w, acc.w);
+                    const float w = s_w[s0 + u];
+                    acc.x = fmaf(w, v[u].x, acc.x);
+                    acc.y = fmaf(w, v[u].y, acc.y);
+                    acc.z = fmaf(w, v[u].z, acc.z);
+                    acc.w = fmaf(w, v[u].w, acc.w);
                 }
             }
         }
@@ -1875,61 +1883,85 @@ __global__ void k_route_split(const void *x, int x_bf16, int d, int T, int Tpad,
 // so its candidate sets still hold the exact top-k. The first expert block
 // also writes the tokens' 2-norms exactly as k_route_split does.
 constexpr int kRouteSmallT = 64, kRaTok = 8, kRaExp = 32;
+int route_approx_smem(int d) { return kRaExp * d * 2 + kRaTok * d * 4; }
+constexpr int kRaSmemMax = 200 * 1024;  // larger d: k_route_split + k_gemm<2>
 
 __global__ void __launch_bounds__(512) k_route_approx(const void *x, int x_bf16, int d, int T, int E,
                                                        const uint16_t *router, float *lga, float *xnorm) {
-    extern __shared__ __align__(16) float xsa[];  // [kRaTok][d] fp32
+    // dynamic shared memory: the CTA's 32 router rows (bf16, one bulk copy),
+    // then x of its 8 tokens as fp32
+    extern __shared__ __align__(128) uint8_t rsa[];
+    __shared__ uint64_t rbar;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e0 = blockIdx.x * kRaExp, t0 = blockIdx.y * kRaTok;
-    const int nt = min(kRaTok, T - t0);
-    auto load8 = [&](int t, int c, float (&v)[8]) {
-        if (x_bf16) {
-            const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
-                                                            static_cast<size_t>(t) * d)[c];
-            v[0] = bf16lo(w.x); v[1] = bf16hi(w.x); v[2] = bf16lo(w.y); v[3] = bf16hi(w.y);
-            v[4] = bf16lo(w.z); v[5] = bf16hi(w.z); v[6] = bf16lo(w.w); v[7] = bf16hi(w.w);
-        } else {
-            const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
-                                                               static_cast<size_t>(t) * d) + 2 * c;
-            const float4 a = q[0], b = q[1];
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-        }
-    };
-    for (int i = threadIdx.x; i < kRaTok * (d / 8); i += blockDim.x) {
-        const int tt = i / (d / 8), c = i % (d / 8);
-        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (tt < nt) load8(t0 + tt, c, v);
-        float4 *dst = reinterpret_cast<float4 *>(xsa + static_cast<size_t>(tt) * d) + 2 * c;
-        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    const int nt = min(kRaTok, T - t0), ne = min(kRaExp, E - e0);
+    const uint16_t *wr = reinterpret_cast<const uint16_t *>(rsa);
+    float *xsa = reinterpret_cast<float *>(rsa + static_cast<size_t>(kRaExp) * d * 2);
+    const uint32_t rbytes = static_cast<uint32_t>(ne) * d * 2;
+    if (threadIdx.x == 0) {
+        mbar_init(&rbar, 1);
+        mbar_expect_tx(&rbar, rbytes);
+        bulk_load(rsa, router + static_cast<size_t>(e0) * d, rbytes, &rbar);
     }
+    // x of the 8 tokens: every load of a thread issued before its stores
+    constexpr int kMaxPer = 8;  // chunks per thread (d <= 4096 at 512 threads)
+    const int per = (kRaTok * (d / 8) + blockDim.x - 1) / blockDim.x;
+    float4 va[kMaxPer], vb[kMaxPer];
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+        va[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        vb[j] = va[j];
+        const int i = threadIdx.x + j * blockDim.x;
+        const int tt = i / (d / 8), c = i % (d / 8);
+        if (j < per && tt < nt) {
+            if (x_bf16) {
+                const uint4 w = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) +
+                                                                static_cast<size_t>(t0 + tt) * d)[c];
+                va[j] = make_float4(bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y));
+                vb[j] = make_float4(bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w));
+            } else {
+                const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(x) +
+                                                                   static_cast<size_t>(t0 + tt) * d) + 2 * c;
+                va[j] = q[0];
+                vb[j] = q[1];
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (j < per && i < kRaTok * (d / 8)) {
+            float4 *dst = reinterpret_cast<float4 *>(xsa + static_cast<size_t>(i / (d / 8)) * d) + 2 * (i % (d / 8));
+            dst[0] = va[j];
+            dst[1] = vb[j];
+        }
+    }
+    __syncthreads();
+    // the tokens' 2-norms (first expert block), from the staged values in
+    // k_route_split's order
     if (blockIdx.x == 0 && warp < nt) {
         double ss = 0.0;
-        for (int c = lane; c < d / 8; c += 32) {
-            float v[8];
-            load8(t0 + warp, c, v);
+        const float *xr = xsa + static_cast<size_t>(warp) * d;
+        for (int c = lane; c < d / 8; c += 32)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
-        }
+            for (int i = 0; i < 8; ++i)
+                ss = fma(static_cast<double>(xr[8 * c + i]), static_cast<double>(xr[8 * c + i]), ss);
         ss = warp_sum_butterfly(ss);
         if (lane == 0) xnorm[t0 + warp] = __double2float_ru(sqrt(ss));
     }
-    __syncthreads();
-    const int ea = e0 + 2 * warp;
+    const bool ok = mbar_wait(&rbar, 0);
+    const int el = 2 * warp;  // experts e0 + el, e0 + el + 1
     float acc[2 * kRaTok];
 #pragma unroll
     for (int i = 0; i < 2 * kRaTok; ++i) acc[i] = 0.f;
     for (int k0 = 8 * lane; k0 < d; k0 += 256) {
-        uint4 q[2];
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-            q[j] = ea + j < E ? *reinterpret_cast<const uint4 *>(router + static_cast<size_t>(ea + j) * d + k0)
-                              : make_uint4(0u, 0u, 0u, 0u);
         float w[2][8];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            w[j][0] = bf16lo(q[j].x); w[j][1] = bf16hi(q[j].x); w[j][2] = bf16lo(q[j].y); w[j][3] = bf16hi(q[j].y);
-            w[j][4] = bf16lo(q[j].z); w[j][5] = bf16hi(q[j].z); w[j][6] = bf16lo(q[j].w); w[j][7] = bf16hi(q[j].w);
+            const uint4 q = el + j < ne ? *reinterpret_cast<const uint4 *>(wr + static_cast<size_t>(el + j) * d + k0)
+                                        : make_uint4(0u, 0u, 0u, 0u);
+            w[j][0] = bf16lo(q.x); w[j][1] = bf16hi(q.x); w[j][2] = bf16lo(q.y); w[j][3] = bf16hi(q.y);
+            w[j][4] = bf16lo(q.z); w[j][5] = bf16hi(q.z); w[j][6] = bf16lo(q.w); w[j][7] = bf16hi(q.w);
         }
 #pragma unroll
         for (int tt = 0; tt < kRaTok; ++tt) {
@@ -1942,10 +1974,10 @@ __global__ void __launch_bounds__(512) k_route_approx(const void *x, int x_bf16,
                 for (int i = 0; i < 8; ++i) acc[j * kRaTok + tt] = fmaf(xv[i], w[j][i], acc[j * kRaTok + tt]);
         }
     }
-    // lane l: the sum of value l / 2 = (expert ea + (l / 2) / 8, token (l / 2) % 8)
+    // lane l: the sum of value l / 2 = (expert e0 + el + (l / 2) / 8, token (l / 2) % 8)
     const float sum = group_sum_tr<2 * kRaTok, 32>(acc, lane);
-    const int v = lane >> 1, ee = ea + v / kRaTok, tt = v % kRaTok;
-    if ((lane & 1) == 0 && tt < nt && ee < E) lga[static_cast<size_t>(t0 + tt) * E + ee] = sum;
+    const int v = lane >> 1, ee = el + v / kRaTok, tt = v % kRaTok;
+    if ((lane & 1) == 0 && tt < nt && ee < ne) lga[static_cast<size_t>(t0 + tt) * E + e0 + ee] = ok ? sum : NAN;
 }
 
 struct RouteArgs {
@@ -2435,9 +2467,9 @@ extern "C" qk_prefill *qk_prefill_create(const qk_layout *L, int max_tokens, con
             return nullptr;
         }
     }
-    if (p->route_ok) {
+    if (p->route_ok && route_approx_smem(L->d) <= kRaSmemMax) {
         e = cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_route_approx),
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kRaTok * L->d * 4);
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, route_approx_smem(L->d));
         if (e != cudaSuccess) {
             snprintf(msg, msg_len, "prefill: %s", cudaGetErrorString(e));
             qk_prefill_destroy(p);
@@ -2999,10 +3031,10 @@ extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void 
     if (T > p->max_tokens) return cudaErrorInvalidValue;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
-    if (T <= kRouteSmallT) {
+    if (T <= kRouteSmallT && route_approx_smem(L.d) <= kRaSmemMax) {
         k_route_approx<<<dim3((E + kRaExp - 1) / kRaExp, (T + kRaTok - 1) / kRaTok), 512,
-                         kRaTok * L.d * sizeof(float), st>>>(f->x, f->x_bf16, L.d, T, E, f->router,
-                                                             p->lga, p->xnorm);
+                         route_approx_smem(L.d), st>>>(f->x, f->x_bf16, L.d, T, E, f->router, p->lga,
+                                                       p->xnorm);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         return route_exact(p, f, wmax, st, mid_event);
