@@ -928,7 +928,7 @@ QK_DEV float dot_unit_h24(const uint4 &w, const uint2 (&v)[3][4]) {
 // return lane l holds the sum of value (l % W) / (W / N).
 template <int N, int W>
 QK_DEV float group_sum_tr(float (&v)[N], int lane) {
-    constexpr int kLevels = N >= 16 ? 4 : N >= 8 ? 3 : N >= 4 ? 2 : N >= 2 ? 1 : 0;
+    constexpr int kLevels = N >= 32 ? 5 : N >= 16 ? 4 : N >= 8 ? 3 : N >= 4 ? 2 : N >= 2 ? 1 : 0;
     static_assert((1 << kLevels) == N && N <= W, "N a power of two, at most W");
 #pragma unroll
     for (int lv = 0; lv < kLevels; ++lv) {
@@ -1876,17 +1876,19 @@ __global__ void k_route_split(const void *x, int x_bf16, int d, int T, int Tpad,
 
 // Small calls (T <= kRouteSmallT): the approximate logits on the CUDA cores
 // in fp32, in place of k_route_split + k_gemm<2>. CTA (32 experts, 8 tokens),
-// 16 warps; warp w takes experts e0 + 2w and e0 + 2w + 1 for the 8 tokens,
-// lane l the elements 8l + 256i + (0..7) of each, the 16 sums reduced by a
-// halving butterfly. Along any path an fp32 sum here meets at most 69
-// roundings, far inside the bound k_route_exact allows for (2^-10 |x| max|w|),
-// so its candidate sets still hold the exact top-k. The first expert block
-// also writes the tokens' 2-norms exactly as k_route_split does.
-constexpr int kRouteSmallT = 64, kRaTok = 8, kRaExp = 32;
+// 8 warps; the CTA's router rows come in by one bulk copy, x of its tokens is
+// staged as fp32. Warp w takes experts e0 + 4w .. e0 + 4w + 3 for the 8
+// tokens, lane l the elements 4l + 128i + (0..3) (consecutive lanes read
+// consecutive 16-byte pieces), the 32 sums reduced by a halving butterfly.
+// Along any path an fp32 sum here meets at most 69 roundings, far inside the
+// bound k_route_exact allows for (2^-10 |x| max|w|), so its candidate sets
+// still hold the exact top-k. The first expert block also writes the tokens'
+// 2-norms exactly as k_route_split does.
+constexpr int kRouteSmallT = 64, kRaTok = 8, kRaExp = 32, kRaEw = 4, kRaThreads = kRaExp / kRaEw * 32;
 int route_approx_smem(int d) { return kRaExp * d * 2 + kRaTok * d * 4; }
 constexpr int kRaSmemMax = 200 * 1024;  // larger d: k_route_split + k_gemm<2>
 
-__global__ void __launch_bounds__(512) k_route_approx(const void *x, int x_bf16, int d, int T, int E,
+__global__ void __launch_bounds__(kRaThreads) k_route_approx(const void *x, int x_bf16, int d, int T, int E,
                                                        const uint16_t *router, float *lga, float *xnorm) {
     // dynamic shared memory: the CTA's 32 router rows (bf16, one bulk copy),
     // then x of its 8 tokens as fp32
@@ -1904,7 +1906,7 @@ __global__ void __launch_bounds__(512) k_route_approx(const void *x, int x_bf16,
         bulk_load(rsa, router + static_cast<size_t>(e0) * d, rbytes, &rbar);
     }
     // x of the 8 tokens: every load of a thread issued before its stores
-    constexpr int kMaxPer = 8;  // chunks per thread (d <= 4096 at 512 threads)
+    constexpr int kMaxPer = 8;  // chunks per thread (d <= 2048 at 256 threads)
     const int per = (kRaTok * (d / 8) + blockDim.x - 1) / blockDim.x;
     float4 va[kMaxPer], vb[kMaxPer];
 #pragma unroll
@@ -1950,34 +1952,35 @@ __global__ void __launch_bounds__(512) k_route_approx(const void *x, int x_bf16,
         if (lane == 0) xnorm[t0 + warp] = __double2float_ru(sqrt(ss));
     }
     const bool ok = mbar_wait(&rbar, 0);
-    const int el = 2 * warp;  // experts e0 + el, e0 + el + 1
-    float acc[2 * kRaTok];
+    const int el = kRaEw * warp;  // experts e0 + el .. e0 + el + 3
+    float acc[kRaEw * kRaTok];
 #pragma unroll
-    for (int i = 0; i < 2 * kRaTok; ++i) acc[i] = 0.f;
-    for (int k0 = 8 * lane; k0 < d; k0 += 256) {
-        float w[2][8];
+    for (int i = 0; i < kRaEw * kRaTok; ++i) acc[i] = 0.f;
+    for (int k0 = 4 * lane; k0 < d; k0 += 128) {
+        float w[kRaEw][4];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const uint4 q = el + j < ne ? *reinterpret_cast<const uint4 *>(wr + static_cast<size_t>(el + j) * d + k0)
-                                        : make_uint4(0u, 0u, 0u, 0u);
+        for (int j = 0; j < kRaEw; ++j) {
+            const uint2 q = el + j < ne ? *reinterpret_cast<const uint2 *>(wr + static_cast<size_t>(el + j) * d + k0)
+                                        : make_uint2(0u, 0u);
             w[j][0] = bf16lo(q.x); w[j][1] = bf16hi(q.x); w[j][2] = bf16lo(q.y); w[j][3] = bf16hi(q.y);
-            w[j][4] = bf16lo(q.z); w[j][5] = bf16hi(q.z); w[j][6] = bf16lo(q.w); w[j][7] = bf16hi(q.w);
         }
 #pragma unroll
         for (int tt = 0; tt < kRaTok; ++tt) {
-            const float4 *xp = reinterpret_cast<const float4 *>(xsa + static_cast<size_t>(tt) * d + k0);
-            const float4 a = xp[0], b = xp[1];
-            const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            const float4 a = *reinterpret_cast<const float4 *>(xsa + static_cast<size_t>(tt) * d + k0);
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[j * kRaTok + tt] = fmaf(xv[i], w[j][i], acc[j * kRaTok + tt]);
+            for (int j = 0; j < kRaEw; ++j) {
+                float &c = acc[j * kRaTok + tt];
+                c = fmaf(a.x, w[j][0], c);
+                c = fmaf(a.y, w[j][1], c);
+                c = fmaf(a.z, w[j][2], c);
+                c = fmaf(a.w, w[j][3], c);
+            }
         }
     }
-    // lane l: the sum of value l / 2 = (expert e0 + el + (l / 2) / 8, token (l / 2) % 8)
-    const float sum = group_sum_tr<2 * kRaTok, 32>(acc, lane);
-    const int v = lane >> 1, ee = el + v / kRaTok, tt = v % kRaTok;
-    if ((lane & 1) == 0 && tt < nt && ee < ne) lga[static_cast<size_t>(t0 + tt) * E + e0 + ee] = ok ? sum : NAN;
+    // lane l: the sum of value l = (expert e0 + el + l / 8, token l % 8)
+    const float sum = group_sum_tr<kRaEw * kRaTok, 32>(acc, lane);
+    const int ee = el + lane / kRaTok, tt = lane % kRaTok;
+    if (tt < nt && ee < ne) lga[static_cast<size_t>(t0 + tt) * E + e0 + ee] = ok ? sum : NAN;
 }
 
 struct RouteArgs {
@@ -3032,7 +3035,7 @@ extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
     if (T <= kRouteSmallT && route_approx_smem(L.d) <= kRaSmemMax) {
-        k_route_approx<<<dim3((E + kRaExp - 1) / kRaExp, (T + kRaTok - 1) / kRaTok), 512,
+        k_route_approx<<<dim3((E + kRaExp - 1) / kRaExp, (T + kRaTok - 1) / kRaTok), kRaThreads,
                          route_approx_smem(L.d), st>>>(f->x, f->x_bf16, L.d, T, E, f->router, p->lga,
                                                        p->xnorm);
         e = cudaGetLastError();
