@@ -2129,6 +2129,9 @@ __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
             s_fast = fast ? 1 : 0;
             s_fin = 1;
         }
+    } else if (warp == kRW - 1) {  // the shared gate, canonical order, beside warp 0's selection
+        const double sg = warp_sum_butterfly(router_lane(a.shared_gate, xs, d, lane));
+        if (lane == 0) s_sg = 1.0f / (1.0f + expf(-static_cast<float>(sg)));
     }
     __syncthreads();
     const bool fast = s_fast != 0;
@@ -2142,10 +2145,6 @@ __global__ void __launch_bounds__(kRW * 32) k_route_exact(RouteArgs a) {
                 if (!isfinite(v)) s_fin = 0;
             }
         }
-    }
-    if (warp == kRW - 1) {  // the shared gate, canonical order
-        const double sg = warp_sum_butterfly(router_lane(a.shared_gate, xs, d, lane));
-        if (lane == 0) s_sg = 1.0f / (1.0f + expf(-static_cast<float>(sg)));
     }
     __syncthreads();
     if (fast && s_fin) {
@@ -2691,7 +2690,8 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, k, T, T, f->slot_of,
                             shared_slot_index, f->err, st, events);
     if (e != cudaSuccess) return e;
-    k_combine<<<T, 256, 0, st>>>(p->Y, p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
+    k_combine<<<T, min(512, (L.d / 4 + 31) / 32 * 32), 0, st>>>(p->Y, p->Y, p->inv, f->wts, f->sgate, k, L.d,
+                                                               f->out);
     if (events) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[3]), st, cudaEventRecordExternal);
     return cudaGetLastError();
 }
@@ -2718,8 +2718,8 @@ extern "C" int qk_prefill_wave(qk_prefill *p, const qk_fwd *f, int shared_slot_i
 
 extern "C" int qk_prefill_combine(qk_prefill *p, const qk_fwd *f, void *stream) {
     const int T = f->T;
-    k_combine<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(p->Y, p->Y, p->inv, f->wts, f->sgate,
-                                                               p->L.k, p->L.d, f->out);
+    k_combine<<<T, min(512, (p->L.d / 4 + 31) / 32 * 32), 0, static_cast<cudaStream_t>(stream)>>>(
+        p->Y, p->Y, p->inv, f->wts, f->sgate, p->L.k, p->L.d, f->out);
     return cudaGetLastError();
 }
 
