@@ -1520,11 +1520,11 @@ enum { XK_F32 = 0, XK_BF16 = 1, XK_F16 = 2 };
 //   k_sb_dn   unit = (small tile, 64 down rows): Y[row][d0 .. d0 + 64) fp32
 // k_combine then runs as on the tensor-core path.
 // One CTA per token, one thread per q4 word position (d / 8 <= 1024).
-// Block 0 also splits the call's small tiles (tiles != nullptr) into the
-// light and heavy lists.
 // It also writes the token's rows of the grouped fp16 A operand of the
 // tensor-core kernels (as k_gather: row t for t < nsh, the row inv[t, s] of
-// each slot with an expert id >= 0; the lo plane for fp32 x).
+// each slot with an expert id >= 0; the lo plane for fp32 x). With
+// tiles != nullptr the grid has one block more, block T, which splits the
+// call's small tiles into the light and heavy lists.
 __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, const MTile *tiles,
                         const int *n_tiles, int max_rows, MTile *light, int *n_light, MTile *heavy,
                         int *n_heavy, const int32_t *idx, int k, int nsh, const int *inv, __half *xp,
@@ -1532,11 +1532,9 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, co
     __shared__ int s_cnt[64];
     __shared__ int s_row[33];  // the token's rows of the grouped operand (-1: none)
     const int t = blockIdx.x, w = threadIdx.x, n = d / 8;
-    for (int i = w; i <= k; i += blockDim.x) {
-        int r = -1;
-        if (i == k) r = t < nsh ? t : -1;
-        else if (idx[static_cast<size_t>(t) * k + i] >= 0) r = inv[static_cast<size_t>(t) * k + i];
-        s_row[i] = r;
+    if (t == T) {
+        split_tiles(tiles, *n_tiles, max_rows, light, n_light, heavy, n_heavy, s_cnt);
+        return;
     }
     float v[8];
 #pragma unroll
@@ -1560,6 +1558,12 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, co
             const float4 a = p[0], b = p[1];
             v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
         }
+    }
+    for (int i = w; i <= k; i += blockDim.x) {
+        int r = -1;
+        if (i == k) r = t < nsh ? t : -1;
+        else if (idx[static_cast<size_t>(t) * k + i] >= 0) r = inv[static_cast<size_t>(t) * k + i];
+        s_row[i] = r;
     }
     uint2 pl[2];
     float usum;
@@ -1596,7 +1600,6 @@ __global__ void k_sb_xq(const void *x, int x_kind, int d, int T, uint8_t *xq, co
             if (x_kind == XK_F32) reinterpret_cast<uint4 *>(dst + lo_plane)[w] = ol;
         }
     }
-    if (t == 0 && tiles != nullptr) split_tiles(tiles, *n_tiles, max_rows, light, n_light, heavy, n_heavy, s_cnt);
 }
 
 
@@ -1657,6 +1660,11 @@ __global__ void k_gather(const void *x, int x_kind, int d, int nsh, int rows, co
 // out[t] = sum_s w[t,s] * Yr[inv[t,s]] + sigmoid(g_t) * Ysh[t], fixed
 // order; one CTA per token, 4 columns per thread, all row loads of a thread
 // issued before the sums.
+// Threads per token: a small call (fewer tokens than about two per SM) gets
+// one thread per 4 columns, up to 512, so each thread's loads are one group;
+// a large call 256 (measured faster at 4096 tokens).
+int combine_threads(int T, int d) { return T <= 256 ? min(512, (d / 4 + 31) / 32 * 32) : 256; }
+
 __global__ void k_combine(const float *Yr, const float *Ysh, const int *inv, const float *wts,
                           const float *sgate, int k, int d, float *out) {
     // the token's k + 1 row pointers and weights first, so that a thread's
@@ -2549,7 +2557,7 @@ cudaError_t grouped(qk_prefill *p, const void *x, int x_kind, int T, const int32
     const bool sb = all_small && p->sb;
     const bool xq_split = sb && (phases & 1) && !wave && T > 0;  // xq's block 0 splits the tiles
     if (sb && (phases & 1) && T > 0)
-        k_sb_xq<<<T, (L.d / 8 + 31) / 32 * 32, 0, st>>>(x, x_kind, L.d, T, p->sb_xq,
+        k_sb_xq<<<T + (xq_split ? 1 : 0), (L.d / 8 + 31) / 32 * 32, 0, st>>>(x, x_kind, L.d, T, p->sb_xq,
                                                        xq_split ? p->stiles : nullptr, p->n_stiles,
                                                        p->sb_max_rows, p->ltiles, p->n_ltiles,
                                                        p->htiles, p->n_htiles, idx, k, nsh, p->inv,
@@ -2690,8 +2698,7 @@ extern "C" int qk_launch_prefill(qk_prefill *p, const qk_fwd *f, int shared_slot
     cudaError_t e = grouped(p, f->x, f->x_bf16 ? XK_BF16 : XK_F32, T, f->idx, k, T, T, f->slot_of,
                             shared_slot_index, f->err, st, events);
     if (e != cudaSuccess) return e;
-    k_combine<<<T, min(512, (L.d / 4 + 31) / 32 * 32), 0, st>>>(p->Y, p->Y, p->inv, f->wts, f->sgate, k, L.d,
-                                                               f->out);
+    k_combine<<<T, combine_threads(T, L.d), 0, st>>>(p->Y, p->Y, p->inv, f->wts, f->sgate, k, L.d, f->out);
     if (events) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[3]), st, cudaEventRecordExternal);
     return cudaGetLastError();
 }
@@ -2718,7 +2725,7 @@ extern "C" int qk_prefill_wave(qk_prefill *p, const qk_fwd *f, int shared_slot_i
 
 extern "C" int qk_prefill_combine(qk_prefill *p, const qk_fwd *f, void *stream) {
     const int T = f->T;
-    k_combine<<<T, min(512, (p->L.d / 4 + 31) / 32 * 32), 0, static_cast<cudaStream_t>(stream)>>>(
+    k_combine<<<T, combine_threads(T, p->L.d), 0, static_cast<cudaStream_t>(stream)>>>(
         p->Y, p->Y, p->inv, f->wts, f->sgate, p->L.k, p->L.d, f->out);
     return cudaGetLastError();
 }
