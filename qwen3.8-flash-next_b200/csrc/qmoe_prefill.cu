@@ -1897,7 +1897,8 @@ int route_approx_smem(int d) { return kRaExp * d * 2 + kRaTok * d * 4; }
 constexpr int kRaSmemMax = 200 * 1024;  // larger d: k_route_split + k_gemm<2>
 
 __global__ void __launch_bounds__(kRaThreads) k_route_approx(const void *x, int x_bf16, int d, int T, int E,
-                                                       const uint16_t *router, float *lga, float *xnorm) {
+                                                       const uint16_t *router, float *lga, float *xnorm,
+                                                       int *err) {
     // dynamic shared memory: the CTA's 32 router rows (bf16, one bulk copy),
     // then x of its 8 tokens as fp32
     extern __shared__ __align__(128) uint8_t rsa[];
@@ -1959,7 +1960,10 @@ __global__ void __launch_bounds__(kRaThreads) k_route_approx(const void *x, int 
         ss = warp_sum_butterfly(ss);
         if (lane == 0) xnorm[t0 + warp] = __double2float_ru(sqrt(ss));
     }
+    // (a copy that never lands: NaN logits, which send the tokens to the
+    // all-exact ranking, and the error word)
     const bool ok = mbar_wait(&rbar, 0);
+    if (!ok && threadIdx.x == 0) atomicOr(err, QK_ERR_TIMEOUT_COPY);
     const int el = kRaEw * warp;  // experts e0 + el .. e0 + el + 3
     float acc[kRaEw * kRaTok];
 #pragma unroll
@@ -3044,7 +3048,7 @@ extern "C" int qk_launch_route(qk_prefill *p, const qk_fwd *f, float wmax, void 
     if (T <= kRouteSmallT && route_approx_smem(L.d) <= kRaSmemMax) {
         k_route_approx<<<dim3((E + kRaExp - 1) / kRaExp, (T + kRaTok - 1) / kRaTok), kRaThreads,
                          route_approx_smem(L.d), st>>>(f->x, f->x_bf16, L.d, T, E, f->router, p->lga,
-                                                       p->xnorm);
+                                                       p->xnorm, f->err);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         return route_exact(p, f, wmax, st, mid_event);
